@@ -1,0 +1,395 @@
+#!/usr/bin/env python
+"""Throughput of the Lizard GLA forward on B200.
+
+One step = one gla(fq, fk, v, log_gamma) forward over B=8, H=32, L=2048,
+F=D=128 bf16 with a per-head gate [B, H, L] (the reference's Table-3 shape
+family, src/benchmark.py:28-41). Inputs (386 MB) exceed the 126 MB L2, so no
+flush is needed between steps. With N GPUs every rank runs its own config-2
+batch (batch x head shards, weak scaling, no collective on the data path);
+value = all ranks' tokens / max-over-ranks device time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Rank 0 prints one JSON line. `--impl reference` times the CPU oracle (the
+restatement of the reference's torch backend, oracle/lizard_oracle.py) on the
+host cores for the same metric.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "lizard-reproduction_b200"))
+
+B, H, L, FD, D = 8, 32, 2048, 128, 128
+METRIC = "gla_fwd_tokens_per_s"
+UNIT = "tokens/s"
+BYTES_PER_TOKEN_HEAD = 2 * (2 * FD + 2 * D) + 4         # fq, fk, v, y bf16 + G fp32
+FLOPS_PER_TOKEN_HEAD = 2 * (2 * FD * D + 64 * FD + 64 * D)  # state, inter, intra s, intra av
+CONFIG = {
+    "workload": "gla_fwd config 2: B=8 H=32 L=2048 F=D=128 bf16, per-head gate [B,H,L]",
+    "B": B, "H": H, "L": L, "F": FD, "D": D, "gate": "per-head",
+    "global_batch_per_gpu": B,
+    "l2": "inputs 386 MB > 126 MB L2 (no flush)",
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the config-3 fwd+bwd side measurements")
+    return ap.parse_args()
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
+            int(os.environ.get("WORLD_SIZE", "1")))
+
+
+def make_inputs(torch, device, seed):
+    import torch.nn.functional as F
+    g = torch.Generator(device=device).manual_seed(seed)
+    fq = (F.softplus(torch.randn(B, H, L, FD, generator=g, device=device)) / math.sqrt(D)).bfloat16()
+    fk = (F.softplus(torch.randn(B, H, L, FD, generator=g, device=device)) / math.sqrt(D)).bfloat16()
+    v = torch.randn(B, H, L, D, generator=g, device=device).bfloat16()
+    lg = F.logsigmoid(3 + 1.5 * torch.randn(B, H, L, generator=g, device=device))
+    return fq, fk, v, lg
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
+        sm, mx, reasons = [], 0.0, set()
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+            except ValueError:
+                continue
+            for name, val in zip(self.NAMES, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def physical_gpu(local_rank):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per launch of the forward kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "gla_fwd_kernel_cfg2.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+# -------------------------------------------------------------- CPU baseline
+def cpu_oracle_rate(torch, fq, fk, v, lg, heads, budget_s, min_runs=1):
+    """tokens/s of the dense CPU oracle on `heads` heads of batch row 0."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import lizard_oracle as orc
+    a, b_, c, d = (t[0:1, :heads].float().cpu() for t in (fq, fk, v, lg))
+    runs, t0 = 0, time.perf_counter()
+    with torch.no_grad():
+        while runs < min_runs or time.perf_counter() - t0 < budget_s:
+            orc.gla(a, b_, c, d)
+            runs += 1
+    dt = time.perf_counter() - t0
+    tokens = runs * L * heads / H  # a token is one position of one batch row, all H heads
+    return tokens / dt, runs, dt
+
+
+def run_reference(args, torch):
+    rank, _, world = env_rank()
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    fq, fk, v, lg = make_cpu_inputs(torch)
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import lizard_oracle as orc
+    # size one step so the whole run stays within about two minutes
+    probe, _, _ = cpu_oracle_rate(torch, fq, fk, v, lg, 1, 0.0)
+    per_head_s = (L / H) / probe
+    total = max(1, args.steps + args.warmup)
+    heads = int(max(1, min(H, 120.0 / total / per_head_s)))
+    a, b_, c, d = (t[0:1, :heads].float() for t in (fq, fk, v, lg))
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            orc.gla(a, b_, c, d)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            orc.gla(a, b_, c, d)
+        dt = time.perf_counter() - t0
+    tokens = args.steps * L * heads / H
+    value = tokens / dt
+    sample = (f"each step: dense fp32 torch oracle on {heads} of {B * H} heads "
+              f"(batch row 0) of the config-2 workload, L={L}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3 / max(1, args.steps), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": CONFIG,
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def make_cpu_inputs(torch):
+    """The config-2 distributions for one batch row, generated on the CPU."""
+    import torch.nn.functional as F
+    g = torch.Generator().manual_seed(0)
+    fq = (F.softplus(torch.randn(1, H, L, FD, generator=g)) / math.sqrt(D)).bfloat16()
+    fk = (F.softplus(torch.randn(1, H, L, FD, generator=g)) / math.sqrt(D)).bfloat16()
+    v = torch.randn(1, H, L, D, generator=g).bfloat16()
+    lg = F.logsigmoid(3 + 1.5 * torch.randn(1, H, L, generator=g))
+    return fq, fk, v, lg
+
+
+# ---------------------------------------------------------------- ours
+def secondary(torch, lizard_cuda, device, steps=50, warmup=5):
+    """Config 3 (B=1, L=2048, H=32, F=D=64): GLA fwd+bwd with a per-token gate
+    and SWA fwd+bwd (window 64, 4 sinks); device ms per step."""
+    import torch.nn.functional as F
+    g = torch.Generator(device=device).manual_seed(7)
+    Bs, Hs, Ls, Ds = 1, 32, 2048, 64
+
+    def leaf(t):
+        return t.detach().requires_grad_()
+    fq = leaf((F.softplus(torch.randn(Bs, Hs, Ls, Ds, generator=g, device=device)) / 8).bfloat16())
+    fk = leaf((F.softplus(torch.randn(Bs, Hs, Ls, Ds, generator=g, device=device)) / 8).bfloat16())
+    v = leaf(torch.randn(Bs, Hs, Ls, Ds, generator=g, device=device).bfloat16())
+    lg = leaf(F.logsigmoid(3 + 1.5 * torch.randn(Bs, Ls, generator=g, device=device)))
+    q = leaf(torch.randn(Bs, Hs, Ls, Ds, generator=g, device=device).bfloat16())
+    k = leaf(torch.randn(Bs, Hs, Ls, Ds, generator=g, device=device).bfloat16())
+    meta = leaf(torch.randn(4, generator=g, device=device))
+    dy = torch.randn(Bs, Hs, Ls, Ds, generator=g, device=device).bfloat16()
+    out = {}
+
+    def timed(name, fn, leaves):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0 = lizard_cuda.launch_count()
+        s.record()
+        for _ in range(steps):
+            for t in leaves:
+                t.grad = None
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / steps
+        out[name] = {"ms": ms, "tokens_per_s": Bs * Ls / (ms / 1e3),
+                     "launches_per_step": (lizard_cuda.launch_count() - n0) / steps}
+
+    timed("gla_fwd_bwd_cfg3", lambda: lizard_cuda.gla(fq, fk, v, lg).backward(dy),
+          (fq, fk, v, lg))
+    timed("swa_fwd_bwd_cfg3", lambda: lizard_cuda.swa(q, k, v, meta, 64).backward(dy),
+          (q, k, v, meta))
+    with torch.no_grad():
+        timed("gla_fwd_cfg3", lambda: lizard_cuda.gla(fq, fk, v, lg), ())
+        timed("swa_fwd_cfg3", lambda: lizard_cuda.swa(q, k, v, meta, 64), ())
+    return out
+
+
+def run_ours(args, torch):
+    import lizard_cuda
+    rank, local, world = env_rank()
+    if args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=device)
+    lizard_cuda.load()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    fq, fk, v, lg = make_inputs(torch, device, seed=1234 + rank)
+    stream = torch.cuda.current_stream(device)
+    sampler = ClockSampler(physical_gpu(local)) if rank == 0 else None
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            lizard_cuda.gla(fq, fk, v, lg)
+        # untimed soak of about one second so the clock sampler sees the load
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < 1.0:
+            for _ in range(20):
+                lizard_cuda.gla(fq, fk, v, lg)
+            torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0 = lizard_cuda.launch_count()
+        start.record(stream)
+        for _ in range(args.steps):
+            y = lizard_cuda.gla(fq, fk, v, lg)
+        end.record(stream)
+        torch.cuda.synchronize()
+        launches = lizard_cuda.launch_count() - n0
+        barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], device=device, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    del y
+
+    # end to end through the public API: pinned host inputs, H2D + compute + D2H
+    host = [x.cpu().pin_memory() for x in (fq, fk, v, lg)]
+    y_host = torch.empty(B, H, L, D, dtype=torch.bfloat16).pin_memory()
+    dev_in = [torch.empty_like(x) for x in (fq, fk, v, lg)]
+    h2d = sum(x.numel() * x.element_size() for x in host)
+    d2h = y_host.numel() * y_host.element_size()
+    e2e_steps = max(3, min(args.steps, 50))
+    with torch.no_grad():
+        for _ in range(2):
+            for dst, src in zip(dev_in, host):
+                dst.copy_(src, non_blocking=True)
+            y_host.copy_(lizard_cuda.gla(*dev_in), non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(stream)
+        for _ in range(e2e_steps):
+            for dst, src in zip(dev_in, host):
+                dst.copy_(src, non_blocking=True)
+            y_host.copy_(lizard_cuda.gla(*dev_in), non_blocking=True)
+        e2.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    t2 = torch.tensor([s2.elapsed_time(e2)], device=device, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t2.item())
+
+    side = None
+    if rank == 0 and not args.no_secondary:
+        side = secondary(torch, lizard_cuda, device)
+
+    cpu = None
+    if rank == 0 and world == 1:
+        rate, runs, dt = cpu_oracle_rate(torch, fq, fk, v, lg, H, 10.0)
+        cpu = {"value": rate, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"dense fp32 torch oracle, batch row 0 (32 heads x {L} tokens) of the "
+                         f"config-2 workload, {runs} runs in {dt:.1f} s"}
+
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    hbm_peak, tc_peak, src = measured_peaks()
+    tokens_per_step = B * L * world
+    ms_step = ms_max / args.steps
+    kernel_ms = ms / max(1, launches)  # rank 0: one forward launch per step
+    alg_bytes = B * H * L * BYTES_PER_TOKEN_HEAD
+    alg_flops = B * H * L * FLOPS_PER_TOKEN_HEAD
+    achieved = alg_bytes / (kernel_ms / 1e3) / 1e9
+    traffic = profiled_traffic()
+    line = {
+        "metric": METRIC,
+        "value": tokens_per_step * args.steps / (ms_max / 1e3),
+        "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": dict(CONFIG, parallelism=f"dp{world} (batch*head shards, no collective)"),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "traffic": traffic,
+                     "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured"
+                     else "fallback 6.65 TB/s",
+                     "alg_bytes_per_launch": alg_bytes,
+                     "tensor_tflops": alg_flops / (kernel_ms / 1e3) / 1e12,
+                     "tensor_frac": alg_flops / (kernel_ms / 1e3) / 1e12 / tc_peak},
+        "e2e": {"value": tokens_per_step * e2e_steps / (e2e_ms / 1e3), "unit": UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    if side:
+        line["secondary"] = side
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    import torch
+    if args.impl == "reference":
+        run_reference(args, torch)
+    else:
+        run_ours(args, torch)
+
+
+if __name__ == "__main__":
+    main()

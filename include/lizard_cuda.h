@@ -1,0 +1,127 @@
+/*
+ * lizard_cuda.h — C ABI of the B200 (sm_100a) backend for Lizard's two
+ * attention branches: chunked gated linear attention (GLA) and sliding-window
+ * softmax attention with sink logits (SWA).
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * passed as void*. The library never allocates or frees device memory: the
+ * caller owns every buffer, including the opaque "saved" buffer that carries
+ * forward state into the backward pass and the backward workspace. Sizes of
+ * those two buffers come from the *_bytes queries below. All work is enqueued
+ * on the given stream; no call synchronises the host.
+ *
+ * Return value: LZ_OK (0) or an LZ_ERR_* code; lz_last_error_string() then
+ * holds a message for the calling thread. Bad shapes, null or misaligned
+ * pointers are reported as errors, never by aborting or trapping.
+ *
+ * Tensor layouts (row-major, contiguous, "BH" = batch*heads, b-major):
+ *   fq, fk     bf16 [BH, L, F]      feature-mapped queries / keys (F = NF)
+ *   v, y, dy   bf16 [BH, L, D]      values / output / output grad (D = ND)
+ *   log_gamma  fp32 [B, L] when gate_per_head == 0 (one gate shared by the H
+ *              heads of a batch row), fp32 [BH, L] when gate_per_head == 1
+ *   q, k       bf16 [BH, L, D]      already-rotated queries / keys for SWA
+ *   meta       fp32 [n_meta]        sink logits (n_meta may be 0)
+ */
+#ifndef LIZARD_CUDA_H_
+#define LIZARD_CUDA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LZ_ABI_VERSION 1
+
+enum {
+  LZ_OK = 0,
+  LZ_ERR_INVALID_ARGUMENT = 1, /* bad shape, null pointer, bad alignment */
+  LZ_ERR_UNSUPPORTED = 2,      /* valid but outside this build's limits  */
+  LZ_ERR_CUDA = 3,             /* a CUDA launch or runtime call failed   */
+  LZ_ERR_WORKSPACE = 4         /* workspace / saved buffer too small     */
+};
+
+/* Output dtype selector for gradient buffers. */
+enum { LZ_DTYPE_F32 = 0, LZ_DTYPE_BF16 = 1 };
+
+/* ABI revision of the loaded library; equals LZ_ABI_VERSION it was built with. */
+int lz_abi_version(void);
+
+/* Message for the last failing call on this host thread ("" if none). */
+const char* lz_last_error_string(void);
+
+/* Number of kernels this library has launched in this process (all devices).
+ * Lets a caller count device launches inside a timed region. */
+uint64_t lz_launch_count(void);
+
+/* ------------------------------------------------------------------------ */
+/* GLA                                                                      */
+/* ------------------------------------------------------------------------ */
+
+/* Bytes of the opaque buffer lz_gla_fwd fills for lz_gla_bwd.
+ * Replaces the tensors _GLA.forward keeps with ctx.save_for_backward
+ * (src/kernels/gla.py:220-232 of the reference): fp32 y and den, the
+ * cumulative log gate G, the per-chunk states S (bf16) and z (fp32). */
+size_t lz_gla_saved_bytes(int B, int H, int L, int F, int D, int chunk);
+
+/* Bytes of scratch lz_gla_bwd needs (delta, dS, dz, dG). */
+size_t lz_gla_bwd_workspace_bytes(int B, int H, int L, int F, int D, int chunk);
+
+/* Forward of gla(fq, fk, v, log_gamma, chunk).
+ * Replaces gla() + _GLA.forward of the reference (src/kernels/gla.py:259-263
+ * and 213-234): G = cumsum(log_gamma) is computed inside the kernel, so one
+ * launch covers the whole forward. y is bf16. When saved is non-null the
+ * forward also fills it for the backward; y is bit-identical either way.
+ * chunk is the reference's chunk length argument; the kernels use 64-token
+ * chunks and accept any chunk >= 1 (results agree within bf16 tolerance). */
+int lz_gla_fwd(const void* fq, const void* fk, const void* v,
+               const float* log_gamma, int gate_per_head,
+               void* y, void* saved, size_t saved_bytes,
+               int B, int H, int L, int F, int D, int chunk, void* stream);
+
+/* Backward of gla(). Replaces _GLA.backward (src/kernels/gla.py:236-256)
+ * including the torch-side delta, dg and the cumsum/expand backward of
+ * gla.py:260-262: it writes dfq, dfk [BH,L,F], dv [BH,L,D] in grad_dtype and
+ * dlog_gamma (fp32, same shape as log_gamma). */
+int lz_gla_bwd(const void* fq, const void* fk, const void* v,
+               const float* log_gamma, int gate_per_head,
+               const void* saved, size_t saved_bytes, const void* dy,
+               void* dfq, void* dfk, void* dv, int grad_dtype,
+               float* dlog_gamma, void* workspace, size_t workspace_bytes,
+               int B, int H, int L, int F, int D, int chunk, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* SWA                                                                      */
+/* ------------------------------------------------------------------------ */
+
+/* Bytes of the opaque buffer lz_swa_fwd fills (log-sum-exp per row). */
+size_t lz_swa_saved_bytes(int B, int H, int L, int D);
+
+/* Bytes of scratch lz_swa_bwd needs (delta per row, sink-grad partials). */
+size_t lz_swa_bwd_workspace_bytes(int B, int H, int L, int D, int n_meta);
+
+/* Forward of swa(q, k, v, meta, window). Replaces _SWA.forward
+ * (src/kernels/swa.py:136-156): y = softmax over [i-window+1, i] with the
+ * sink logits in the denominator, scale 1/sqrt(D). y is bf16. saved may be
+ * null when no backward follows. */
+int lz_swa_fwd(const void* q, const void* k, const void* v,
+               const float* meta, int n_meta, int window,
+               void* y, void* saved, size_t saved_bytes,
+               int B, int H, int L, int D, void* stream);
+
+/* Backward of swa(). Replaces _SWA.backward (src/kernels/swa.py:158-179)
+ * including the torch-side delta and dmeta: writes dq, dk, dv [BH,L,D] in
+ * grad_dtype and dmeta (fp32 [n_meta]). */
+int lz_swa_bwd(const void* q, const void* k, const void* v,
+               const float* meta, int n_meta, int window,
+               const void* y, const void* saved, size_t saved_bytes,
+               const void* dy, void* dq, void* dk, void* dv, int grad_dtype,
+               float* dmeta, void* workspace, size_t workspace_bytes,
+               int B, int H, int L, int D, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LIZARD_CUDA_H_ */

@@ -1,0 +1,149 @@
+// extern "C" entry points declared in include/lizard_cuda.h: argument
+// validation, carving of caller-owned buffers, dispatch to the kernels.
+#include "common.cuh"
+#include "gla_layout.h"
+#include "swa_layout.h"
+
+namespace {
+
+int check_sizes(int B, int H, int L, int F, int D) {
+  LZ_REQUIRE(B >= 1 && H >= 1 && L >= 1, LZ_ERR_INVALID_ARGUMENT,
+             "B, H and L must be positive");
+  LZ_REQUIRE(F >= 1 && D >= 1, LZ_ERR_INVALID_ARGUMENT, "feature and value dims must be positive");
+  LZ_REQUIRE((long long)B * H * L < (1ll << 31), LZ_ERR_UNSUPPORTED, "B*H*L must fit in int32");
+  return LZ_OK;
+}
+
+}  // namespace
+
+extern "C" size_t lz_gla_saved_bytes(int B, int H, int L, int F, int D, int chunk) {
+  (void)chunk;
+  if (B < 1 || H < 1 || L < 1 || F < 1 || D < 1) return 0;
+  return lz::gla_saved_layout(B, H, L, F, D, nullptr, nullptr);
+}
+
+extern "C" size_t lz_gla_bwd_workspace_bytes(int B, int H, int L, int F, int D, int chunk) {
+  (void)chunk;
+  if (B < 1 || H < 1 || L < 1 || F < 1 || D < 1) return 0;
+  return lz::gla_work_layout(B, H, L, F, D, nullptr, nullptr);
+}
+
+extern "C" int lz_gla_fwd(const void* fq, const void* fk, const void* v, const float* log_gamma,
+                          int gate_per_head, void* y, void* saved, size_t saved_bytes, int B,
+                          int H, int L, int F, int D, int chunk, void* stream) {
+  lz::clear_error();
+  int rc = check_sizes(B, H, L, F, D);
+  if (rc) return rc;
+  LZ_REQUIRE(fq && fk && v && log_gamma && y, LZ_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  LZ_REQUIRE(chunk >= 1, LZ_ERR_INVALID_ARGUMENT, "chunk must be >= 1");
+  LZ_REQUIRE(F <= 256, LZ_ERR_UNSUPPORTED, "feature dim above 256 is not supported");
+  LZ_REQUIRE(D <= 256, LZ_ERR_UNSUPPORTED, "value dim above 256 is not supported");
+  lz::GlaSaved sv;
+  if (saved) {
+    const size_t need = lz::gla_saved_layout(B, H, L, F, D, nullptr, nullptr);
+    LZ_REQUIRE(saved_bytes >= need, LZ_ERR_WORKSPACE, "saved buffer too small");
+    LZ_REQUIRE(lz::aligned16(saved), LZ_ERR_INVALID_ARGUMENT, "saved buffer must be 16-byte aligned");
+    lz::gla_saved_layout(B, H, L, F, D, static_cast<unsigned char*>(saved), &sv);
+  }
+  return lz::gla_fwd(static_cast<const bf16*>(fq), static_cast<const bf16*>(fk),
+                     static_cast<const bf16*>(v), log_gamma, gate_per_head ? 1 : 0,
+                     static_cast<bf16*>(y), sv, B, H, L, F, D,
+                     static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lz_gla_bwd(const void* fq, const void* fk, const void* v, const float* log_gamma,
+                          int gate_per_head, const void* saved, size_t saved_bytes,
+                          const void* dy, void* dfq, void* dfk, void* dv, int grad_dtype,
+                          float* dlog_gamma, void* workspace, size_t workspace_bytes, int B,
+                          int H, int L, int F, int D, int chunk, void* stream) {
+  lz::clear_error();
+  int rc = check_sizes(B, H, L, F, D);
+  if (rc) return rc;
+  LZ_REQUIRE(fq && fk && v && log_gamma && saved && dy && dfq && dfk && dv && dlog_gamma &&
+                 workspace,
+             LZ_ERR_INVALID_ARGUMENT, "null pointer");
+  LZ_REQUIRE(chunk >= 1, LZ_ERR_INVALID_ARGUMENT, "chunk must be >= 1");
+  LZ_REQUIRE(grad_dtype == LZ_DTYPE_F32 || grad_dtype == LZ_DTYPE_BF16, LZ_ERR_INVALID_ARGUMENT,
+             "grad_dtype must be LZ_DTYPE_F32 or LZ_DTYPE_BF16");
+  LZ_REQUIRE(F <= 256, LZ_ERR_UNSUPPORTED, "feature dim above 256 is not supported");
+  LZ_REQUIRE(D <= 128, LZ_ERR_UNSUPPORTED, "value dim above 128 is not supported in the backward");
+  const size_t need_s = lz::gla_saved_layout(B, H, L, F, D, nullptr, nullptr);
+  const size_t need_w = lz::gla_work_layout(B, H, L, F, D, nullptr, nullptr);
+  LZ_REQUIRE(saved_bytes >= need_s, LZ_ERR_WORKSPACE, "saved buffer too small");
+  LZ_REQUIRE(workspace_bytes >= need_w, LZ_ERR_WORKSPACE, "workspace too small");
+  LZ_REQUIRE(lz::aligned16(saved) && lz::aligned16(workspace), LZ_ERR_INVALID_ARGUMENT,
+             "saved buffer and workspace must be 16-byte aligned");
+  lz::GlaSaved sv;
+  lz::GlaWork wk;
+  lz::gla_saved_layout(B, H, L, F, D, (unsigned char*)const_cast<void*>(saved), &sv);
+  lz::gla_work_layout(B, H, L, F, D, static_cast<unsigned char*>(workspace), &wk);
+  return lz::gla_bwd(static_cast<const bf16*>(fq), static_cast<const bf16*>(fk),
+                     static_cast<const bf16*>(v), log_gamma, gate_per_head ? 1 : 0, sv,
+                     static_cast<const bf16*>(dy), dfq, dfk, dv, grad_dtype, dlog_gamma, wk, B,
+                     H, L, F, D, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t lz_swa_saved_bytes(int B, int H, int L, int D) {
+  (void)D;
+  if (B < 1 || H < 1 || L < 1) return 0;
+  return lz::swa_saved_bytes(B, H, L);
+}
+
+extern "C" size_t lz_swa_bwd_workspace_bytes(int B, int H, int L, int D, int n_meta) {
+  (void)D;
+  if (B < 1 || H < 1 || L < 1 || n_meta < 0) return 0;
+  return lz::swa_work_layout(B, H, L, n_meta, nullptr, nullptr);
+}
+
+extern "C" int lz_swa_fwd(const void* q, const void* k, const void* v, const float* meta,
+                          int n_meta, int window, void* y, void* saved, size_t saved_bytes,
+                          int B, int H, int L, int D, void* stream) {
+  lz::clear_error();
+  int rc = check_sizes(B, H, L, 1, D);
+  if (rc) return rc;
+  LZ_REQUIRE(q && k && v && y, LZ_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  LZ_REQUIRE(n_meta >= 0 && (n_meta == 0 || meta), LZ_ERR_INVALID_ARGUMENT,
+             "meta must be non-null when n_meta > 0");
+  LZ_REQUIRE(n_meta <= lz::kMaxMeta, LZ_ERR_UNSUPPORTED, "more than 32 sink logits");
+  LZ_REQUIRE(window >= 1, LZ_ERR_INVALID_ARGUMENT, "window must be >= 1");
+  LZ_REQUIRE(D <= 128, LZ_ERR_UNSUPPORTED, "head dim above 128 is not supported");
+  float* lse = nullptr;
+  if (saved) {
+    LZ_REQUIRE(saved_bytes >= lz::swa_saved_bytes(B, H, L), LZ_ERR_WORKSPACE,
+               "saved buffer too small");
+    lse = static_cast<float*>(saved);
+  }
+  return lz::swa_fwd(static_cast<const bf16*>(q), static_cast<const bf16*>(k),
+                     static_cast<const bf16*>(v), meta, n_meta, window, static_cast<bf16*>(y),
+                     lse, B, H, L, D, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lz_swa_bwd(const void* q, const void* k, const void* v, const float* meta,
+                          int n_meta, int window, const void* y, const void* saved,
+                          size_t saved_bytes, const void* dy, void* dq, void* dk, void* dv,
+                          int grad_dtype, float* dmeta, void* workspace, size_t workspace_bytes,
+                          int B, int H, int L, int D, void* stream) {
+  lz::clear_error();
+  int rc = check_sizes(B, H, L, 1, D);
+  if (rc) return rc;
+  LZ_REQUIRE(q && k && v && y && saved && dy && dq && dk && dv && workspace,
+             LZ_ERR_INVALID_ARGUMENT, "null pointer");
+  LZ_REQUIRE(n_meta >= 0 && (n_meta == 0 || (meta && dmeta)), LZ_ERR_INVALID_ARGUMENT,
+             "meta and dmeta must be non-null when n_meta > 0");
+  LZ_REQUIRE(n_meta <= lz::kMaxMeta, LZ_ERR_UNSUPPORTED, "more than 32 sink logits");
+  LZ_REQUIRE(window >= 1, LZ_ERR_INVALID_ARGUMENT, "window must be >= 1");
+  LZ_REQUIRE(grad_dtype == LZ_DTYPE_F32 || grad_dtype == LZ_DTYPE_BF16, LZ_ERR_INVALID_ARGUMENT,
+             "grad_dtype must be LZ_DTYPE_F32 or LZ_DTYPE_BF16");
+  LZ_REQUIRE(D <= 128, LZ_ERR_UNSUPPORTED, "head dim above 128 is not supported");
+  LZ_REQUIRE(saved_bytes >= lz::swa_saved_bytes(B, H, L), LZ_ERR_WORKSPACE,
+             "saved buffer too small");
+  LZ_REQUIRE(workspace_bytes >= lz::swa_work_layout(B, H, L, n_meta, nullptr, nullptr),
+             LZ_ERR_WORKSPACE, "workspace too small");
+  lz::SwaWork wk;
+  lz::swa_work_layout(B, H, L, n_meta, static_cast<unsigned char*>(workspace), &wk);
+  return lz::swa_bwd(static_cast<const bf16*>(q), static_cast<const bf16*>(k),
+                     static_cast<const bf16*>(v), meta, n_meta, window,
+                     static_cast<const bf16*>(y), static_cast<const float*>(saved),
+                     static_cast<const bf16*>(dy), dq, dk, dv, grad_dtype, dmeta, wk, B, H, L,
+                     D, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,91 @@
+"""ctypes binding of liblizard_cuda.so (the C ABI in include/lizard_cuda.h).
+
+The shared library is built in-tree by lizard-reproduction_b200/csrc/build.py.
+There is no fallback: if the library is missing or its ABI revision differs,
+every call raises.
+"""
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+ABI_VERSION = 1
+LIB_PATH = Path(__file__).resolve().with_name("liblizard_cuda.so")
+HEADER = Path(__file__).resolve().parents[2] / "include" / "lizard_cuda.h"
+
+LZ_DTYPE_F32 = 0
+LZ_DTYPE_BF16 = 1
+
+_c_int, _c_size, _vp = ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p
+_SIGNATURES = {
+    "lz_abi_version": (_c_int, []),
+    "lz_last_error_string": (ctypes.c_char_p, []),
+    "lz_launch_count": (ctypes.c_uint64, []),
+    "lz_gla_saved_bytes": (_c_size, [_c_int] * 6),
+    "lz_gla_bwd_workspace_bytes": (_c_size, [_c_int] * 6),
+    "lz_gla_fwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_size] + [_c_int] * 6 + [_vp]),
+    "lz_gla_bwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _c_size, _vp, _vp, _vp, _vp, _c_int,
+                            _vp, _vp, _c_size] + [_c_int] * 6 + [_vp]),
+    "lz_swa_saved_bytes": (_c_size, [_c_int] * 4),
+    "lz_swa_bwd_workspace_bytes": (_c_size, [_c_int] * 5),
+    "lz_swa_fwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _c_size] + [_c_int] * 4
+                   + [_vp]),
+    "lz_swa_bwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _c_size, _vp, _vp, _vp,
+                            _vp, _c_int, _vp, _vp, _c_size] + [_c_int] * 4 + [_vp]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load():
+    """Load and type the library once per process."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{LIB_PATH.name} is not built; run "
+                    "`python lizard-reproduction_b200/csrc/build.py` first")
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in _SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype, fn.argtypes = res, args
+            if lib.lz_abi_version() != ABI_VERSION:
+                raise RuntimeError(f"{LIB_PATH.name} has ABI {lib.lz_abi_version()}, "
+                                   f"this module expects {ABI_VERSION}")
+            _lib = lib
+    return _lib
+
+
+def check(rc, what):
+    if rc != 0:
+        msg = load().lz_last_error_string().decode(errors="replace")
+        raise RuntimeError(f"lizard_cuda {what} failed (code {rc}): {msg}")
+
+
+def launch_count():
+    return int(load().lz_launch_count())
+
+
+def ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def require_cuda(*tensors):
+    for t in tensors:
+        if not (isinstance(t, torch.Tensor) and t.is_cuda):
+            raise RuntimeError("lizard_cuda runs on CUDA tensors only (no CPU path); "
+                               f"got {type(t).__name__} on "
+                               f"{getattr(t, 'device', 'n/a')}")
+    dev = tensors[0].device
+    for t in tensors[1:]:
+        if t.device != dev:
+            raise RuntimeError(f"lizard_cuda: tensors on different devices ({dev}, {t.device})")

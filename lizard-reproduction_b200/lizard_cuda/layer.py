@@ -1,0 +1,96 @@
+"""LizardAttention with the `cuda` backend.
+
+Mirror of the reference layer (src/lizard_attention.py:47-107): same
+constructor arguments, parameter names and forward contract
+(forward(hidden_states, position_embeddings) -> (out, None)), with the two
+attention branches running on this package's gla / swa kernels exactly where
+the reference's `triton` backend calls kernels.gla / kernels.swa
+(src/lizard_attention.py:90-93). The projections, feature map, gate and RoPE
+are the same torch operations as the reference.
+"""
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .gla import gla
+from .swa import swa
+
+BACKENDS = ("cuda",)
+
+
+def hedgehog(x, weight):
+    """[softmax(x W^T), softmax(-x W^T)] (src/lizard_attention.py:9-11)."""
+    xw = x @ weight.T
+    return torch.cat([xw.softmax(-1), (-xw).softmax(-1)], dim=-1)
+
+
+def _rotate_half(x):
+    half = x.shape[-1] // 2
+    return torch.cat([-x[..., half:], x[..., :half]], dim=-1)
+
+
+def apply_rotary(q, k, cos, sin):
+    """Llama rotate-half RoPE with cos/sin [B, L, Dh] broadcast over heads."""
+    cos, sin = cos[:, None], sin[:, None]
+    return q * cos + _rotate_half(q) * sin, k * cos + _rotate_half(k) * sin
+
+
+class LizardAttention(nn.Module):
+    def __init__(self, config, layer_idx, window=128, num_meta=4, feature_dim=128,
+                 backend="cuda"):
+        super().__init__()
+        if backend not in BACKENDS:
+            raise ValueError(f"this layer runs the cuda backend only, got {backend!r}; the "
+                             "torch and triton backends live in the reference package")
+        self.backend = backend
+        hidden = config.hidden_size
+        self.layer_idx = layer_idx
+        self.heads = config.num_attention_heads
+        self.kv_heads = config.num_key_value_heads
+        self.head_dim = hidden // self.heads
+        self.window = window
+        kv_dim = self.kv_heads * self.head_dim
+        self.q_proj = nn.Linear(hidden, hidden, bias=False)
+        self.k_proj = nn.Linear(hidden, kv_dim, bias=False)
+        self.v_proj = nn.Linear(hidden, kv_dim, bias=False)
+        self.o_proj = nn.Linear(hidden, hidden, bias=False)
+        self.phi_q = nn.Linear(self.head_dim, feature_dim, bias=False)
+        self.phi_k = nn.Linear(self.head_dim, feature_dim, bias=False)
+        self.W_gamma = nn.Linear(hidden, 1, bias=False)
+        self.meta_tokens = nn.Parameter(torch.zeros(num_meta))
+        self.alpha_blend = nn.Parameter(torch.ones(()))
+        nn.init.normal_(self.phi_q.weight, std=0.02)
+        nn.init.normal_(self.phi_k.weight, std=0.02)
+        nn.init.zeros_(self.W_gamma.weight)
+
+    def split(self, x, heads):
+        b, n, _ = x.shape
+        x = x.view(b, n, heads, self.head_dim).transpose(1, 2)
+        return x.repeat_interleave(self.heads // heads, dim=1)
+
+    def forward(self, hidden_states, position_embeddings, **kwargs):
+        x = hidden_states
+        dtype = torch.promote_types(x.dtype, torch.float32)
+        q = self.split(self.q_proj(x), self.heads).to(dtype)
+        k = self.split(self.k_proj(x), self.kv_heads).to(dtype)
+        v = self.split(self.v_proj(x), self.kv_heads).to(dtype)
+        z = self.W_gamma(x).to(dtype).squeeze(-1)
+        fq = hedgehog(q, self.phi_q.weight.to(dtype))
+        fk = hedgehog(k, self.phi_k.weight.to(dtype))
+        cos, sin = (t.to(dtype) for t in position_embeddings)
+        qr, kr = apply_rotary(q, k, cos, sin)
+        alpha, meta = self.alpha_blend.to(dtype), self.meta_tokens.to(dtype)
+        y = gla(fq, fk, v, F.logsigmoid(z)).to(dtype)
+        y = y + alpha * swa(qr, kr, v, meta, self.window).to(dtype)
+        return self.o_proj(y.to(x.dtype).transpose(1, 2).flatten(2)), None
+
+
+def from_llama(attention, config, **options):
+    """Build a LizardAttention from a Llama attention layer, copying q/k/v/o
+    (src/lizard_attention.py:100-107)."""
+    weight = attention.q_proj.weight
+    layer = LizardAttention(config, attention.layer_idx, **options)
+    layer = layer.to(weight.device, weight.dtype)
+    for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
+        getattr(layer, name).load_state_dict(getattr(attention, name).state_dict())
+    return layer

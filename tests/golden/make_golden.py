@@ -1,0 +1,103 @@
+"""Generate the golden fixtures in this directory from the reference itself.
+
+Runs the reference's own torch backend (src/lizard_attention.py of
+mahdikhashan/lizard-reproduction: gla, awa, LizardAttention) in fp32 on the
+seeded inputs of cases.py and stores outputs and gradients. This is exactly
+how the reference checks its kernels (tests/test_kernels.py:32-42, 61-70,
+121-122, 137-156). Needs a checkout of the reference; the path comes from
+LIZARD_REFERENCE_SRC (default: the reference's src/ directory mounted beside
+this repository). The fixtures are committed; the tests never need the
+reference.
+
+    python tests/golden/make_golden.py
+"""
+import os
+import sys
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+import cases  # noqa: E402
+
+REF_SRC = os.environ.get("LIZARD_REFERENCE_SRC", "/root/reference/src")
+
+
+def reference():
+    sys.path.insert(0, REF_SRC)
+    import lizard_attention as lz  # the reference module
+    return lz
+
+
+def gla_golden(lz, name, kw):
+    inp = cases.gla_case(**kw)
+    fq, fk, v = (inp[n].float().requires_grad_() for n in ("fq", "fk", "v"))
+    lg = inp["log_gamma"].clone().requires_grad_()
+    gamma = lg.exp()
+    if lg.dim() == 2:
+        y = lz.gla(fq, fk, v, gamma)
+    else:  # per-head gate: fold batch*heads (tests/test_kernels.py:66-70)
+        b, h, n, _ = fq.shape
+
+        def fold(t):
+            return t.reshape(b * h, 1, n, -1)
+        y = lz.gla(fold(fq), fold(fk), fold(v), gamma.reshape(b * h, n)).reshape(b, h, n, -1)
+    y.backward(inp["dy"])
+    return dict(kind="gla", kw=kw, inputs=inp, y=y.detach(), dfq=fq.grad, dfk=fk.grad,
+                dv=v.grad, dlog_gamma=lg.grad)
+
+
+def swa_golden(lz, name, kw, window):
+    inp = cases.swa_case(**kw)
+    q, k, v = (inp[n].float().requires_grad_() for n in ("q", "k", "v"))
+    meta = inp["meta"].clone().requires_grad_()
+    if meta.numel() == 0:  # no sinks: the reference evaluates it with a -1e4 sink
+        ref_meta = torch.full((1,), -1e4)  # (tests/test_kernels.py:127-134)
+    else:
+        ref_meta = meta
+    y = lz.awa(q, k, v, ref_meta, window)
+    y.backward(inp["dy"])
+    out = dict(kind="swa", kw=kw, window=window, inputs=inp, y=y.detach(), dq=q.grad,
+               dk=k.grad, dv=v.grad)
+    out["dmeta"] = meta.grad if meta.numel() else torch.zeros(0)
+    return out
+
+
+def layer_golden(lz, name, case):
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding
+    config = LlamaConfig(hidden_size=case["hidden"], intermediate_size=2 * case["hidden"],
+                         num_hidden_layers=1, num_attention_heads=case["heads"],
+                         num_key_value_heads=case["kv_heads"], vocab_size=100,
+                         rope_theta=case["theta"], attn_implementation="eager")
+    layer = lz.LizardAttention(config, 0, window=case["window"], num_meta=case["num_meta"],
+                               feature_dim=case["feature_dim"], backend="torch")
+    cases.init_layer_params(layer, case["init"])
+    x, grad = cases.layer_inputs(case)
+    positions = torch.arange(case["length"])[None]
+    cos, sin = LlamaRotaryEmbedding(config)(x, positions)
+    y = layer(x, (cos, sin))[0]
+    y.backward(grad)
+    grads = {n: p.grad.detach().clone() for n, p in layer.named_parameters()}
+    params = {n: cases.checksum(p) for n, p in layer.named_parameters()}
+    return dict(kind="layer", case=case, x_sum=cases.checksum(x), grad_sum=cases.checksum(grad),
+                param_sums=params, cos=cos.float(), sin=sin.float(), y=y.detach(), grads=grads)
+
+
+def main():
+    lz = reference()
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    for name, kw in cases.GLA_CASES.items():
+        torch.save(gla_golden(lz, name, kw), HERE / f"{name}.pt")
+        print("wrote", name)
+    for name, (kw, window) in cases.SWA_CASES.items():
+        torch.save(swa_golden(lz, name, kw, window), HERE / f"{name}.pt")
+        print("wrote", name)
+    for name, case in cases.LAYER_CASES.items():
+        torch.save(layer_golden(lz, name, case), HERE / f"{name}.pt")
+        print("wrote", name)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,135 @@
+"""The C-ABI library loads, exports every symbol include/lizard_cuda.h declares,
+and rejects bad arguments with an error code and message. No GPU needed: every
+call here fails validation before any CUDA call."""
+import ctypes
+import inspect
+import re
+
+import pytest
+import torch
+
+from conftest import ROOT
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "lizard_cuda.h").read_text()
+    return sorted(set(re.findall(r"\b(lz_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib(built_lib):
+    from lizard_cuda import _lib
+    return _lib.load()
+
+
+def test_header_declares_the_expected_entry_points():
+    syms = declared_symbols()
+    for name in ("lz_gla_fwd", "lz_gla_bwd", "lz_swa_fwd", "lz_swa_bwd", "lz_abi_version",
+                 "lz_last_error_string", "lz_gla_saved_bytes", "lz_swa_bwd_workspace_bytes"):
+        assert name in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_abi_version(lib):
+    from lizard_cuda import _lib
+    assert lib.lz_abi_version() == _lib.ABI_VERSION == 1
+
+
+def test_buffer_size_queries(lib):
+    B, H, L, F, D = 2, 3, 150, 24, 20
+    nt = -(-L // 64)
+    saved = lib.lz_gla_saved_bytes(B, H, L, F, D, 64)
+    assert saved >= B * H * L * D * 4 + 2 * B * H * L * 4 + B * H * nt * F * (2 * D + 4)
+    assert lib.lz_gla_bwd_workspace_bytes(B, H, L, F, D, 64) >= B * H * nt * F * D * 2
+    assert lib.lz_swa_saved_bytes(B, H, L, D) >= B * H * L * 4
+    assert lib.lz_swa_bwd_workspace_bytes(B, H, L, D, 4) >= B * H * L * 4
+    assert lib.lz_gla_saved_bytes(0, H, L, F, D, 64) == 0
+
+
+def _fake(n=1):
+    # never dereferenced: validation rejects the calls first
+    return [ctypes.c_void_p(0x1000 * (i + 1)) for i in range(n)]
+
+
+def test_gla_fwd_rejects_null_pointers(lib):
+    rc = lib.lz_gla_fwd(None, None, None, None, 0, None, None, 0, 1, 1, 8, 8, 8, 64, None)
+    assert rc == 1
+    assert b"null" in lib.lz_last_error_string()
+
+
+def test_gla_fwd_rejects_bad_sizes(lib):
+    p = _fake(5)
+    assert lib.lz_gla_fwd(*p[:4], 0, p[4], None, 0, 0, 1, 8, 8, 8, 64, None) == 1
+    assert lib.lz_gla_fwd(*p[:4], 0, p[4], None, 0, 1, 1, 8, 8, 8, 0, None) == 1
+    assert lib.lz_gla_fwd(*p[:4], 0, p[4], None, 0, 1, 1, 8, 300, 8, 64, None) == 2
+    assert b"feature dim" in lib.lz_last_error_string()
+
+
+def test_gla_fwd_rejects_small_saved_buffer(lib):
+    p = _fake(6)
+    rc = lib.lz_gla_fwd(*p[:4], 0, p[4], p[5], 16, 1, 1, 8, 8, 8, 64, None)
+    assert rc == 4
+    assert b"saved" in lib.lz_last_error_string()
+
+
+def test_gla_bwd_rejects_bad_grad_dtype(lib):
+    p = _fake(12)
+    rc = lib.lz_gla_bwd(*p[:4], 0, p[4], 1 << 30, p[5], p[6], p[7], p[8], 7, p[9], p[10],
+                        1 << 30, 1, 1, 8, 8, 8, 64, None)
+    assert rc == 1
+    assert b"grad_dtype" in lib.lz_last_error_string()
+
+
+def test_swa_rejects_bad_window_and_sinks(lib):
+    p = _fake(5)
+    assert lib.lz_swa_fwd(*p[:3], None, 0, 0, p[4], None, 0, 1, 1, 8, 8, None) == 1
+    assert b"window" in lib.lz_last_error_string()
+    assert lib.lz_swa_fwd(*p[:3], None, 2, 4, p[4], None, 0, 1, 1, 8, 8, None) == 1
+    assert lib.lz_swa_fwd(*p[:3], p[3], 33, 4, p[4], None, 0, 1, 1, 8, 8, None) == 2
+    assert lib.lz_swa_fwd(*p[:3], p[3], 1, 4, p[4], None, 0, 1, 1, 8, 256, None) == 2
+
+
+def test_error_string_is_cleared_by_a_new_call(lib):
+    lib.lz_gla_fwd(None, None, None, None, 0, None, None, 0, 1, 1, 8, 8, 8, 64, None)
+    assert lib.lz_last_error_string() != b""
+    lib.lz_abi_version()
+    p = _fake(5)
+    lib.lz_swa_fwd(*p[:3], None, 0, 0, p[4], None, 0, 1, 1, 8, 8, None)
+    assert b"window" in lib.lz_last_error_string()
+
+
+def test_python_signatures_match_the_reference(built_lib):
+    import lizard_cuda
+    sig = inspect.signature(lizard_cuda.gla)
+    assert list(sig.parameters) == ["fq", "fk", "v", "log_gamma", "chunk"]
+    assert sig.parameters["chunk"].default == 64
+    sig = inspect.signature(lizard_cuda.swa)
+    assert list(sig.parameters) == ["q", "k", "v", "meta", "window", "fwd_blocks", "bwd_blocks"]
+    assert lizard_cuda.swa.__defaults__ == ((64, 64), (64, 64))
+
+
+def test_cpu_tensors_are_rejected_not_computed(built_lib):
+    import lizard_cuda
+    x = torch.rand(1, 1, 4, 8)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        lizard_cuda.gla(x, x, x, torch.zeros(1, 4))
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        lizard_cuda.swa(x, x, x, torch.zeros(4), 4)
+
+
+def test_layer_accepts_only_the_cuda_backend(built_lib):
+    from types import SimpleNamespace
+
+    from lizard_cuda.layer import LizardAttention
+    cfg = SimpleNamespace(hidden_size=32, num_attention_heads=2, num_key_value_heads=1)
+    layer = LizardAttention(cfg, 0, window=8, num_meta=2, feature_dim=4)
+    names = sorted(n for n, _ in layer.named_parameters())
+    assert names == sorted(["q_proj.weight", "k_proj.weight", "v_proj.weight", "o_proj.weight",
+                            "phi_q.weight", "phi_k.weight", "W_gamma.weight", "meta_tokens",
+                            "alpha_blend"])
+    with pytest.raises(ValueError, match="cuda backend only"):
+        LizardAttention(cfg, 0, backend="torch")

@@ -1,0 +1,190 @@
+"""GLA kernels on the GPU against the reference fixtures and the CPU oracle."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+import cases
+import lizard_oracle as orc
+from conftest import load_golden
+from parity import assert_grad, assert_output
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib(built_lib):
+    import lizard_cuda
+    lizard_cuda.load()
+
+
+def cuda_gla(fq, fk, v, lg, dy=None, chunk=64):
+    import lizard_cuda
+    leaves = [t.detach().to(DEV).clone().requires_grad_() for t in (fq, fk, v, lg)]
+    y = lizard_cuda.gla(*leaves, chunk)
+    if dy is not None:
+        y.backward(dy.to(DEV).to(y.dtype))
+    return y, [t.grad for t in leaves]
+
+
+def oracle_gla(fq, fk, v, lg, dy=None):
+    leaves = [t.detach().float().cpu().clone().requires_grad_() for t in (fq, fk, v, lg)]
+    y = orc.gla(*leaves)
+    if dy is not None:
+        y.backward(dy.float().cpu())
+    return y.detach(), [t.grad for t in leaves]
+
+
+GRAD_NAMES = ("dfq", "dfk", "dv", "dlog_gamma")
+
+
+@pytest.mark.parametrize("name", list(cases.GLA_CASES))
+def test_gla_matches_reference_fixture(name):
+    fx = load_golden(name)
+    inp = fx["inputs"]
+    y, grads = cuda_gla(inp["fq"], inp["fk"], inp["v"], inp["log_gamma"], inp["dy"])
+    assert y.dtype == torch.bfloat16
+    assert_output(y, fx["y"], f"{name} y")
+    for g, key in zip(grads, GRAD_NAMES):
+        assert g.dtype == fx["inputs"][{"dfq": "fq", "dfk": "fk", "dv": "v",
+                                        "dlog_gamma": "log_gamma"}[key]].dtype
+        assert_grad(g, fx[key], f"{name} {key}")
+
+
+def baseline_inputs(B, H, L, Fd, D, per_head, seed=0, device=DEV):
+    """fq, fk = softplus(N(0,1))/sqrt(D), v ~ N(0,1),
+    log_gamma = logsigmoid(N(3, 1.5)), dO ~ N(0,1); seeded on the device."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    fq = (F.softplus(torch.randn(B, H, L, Fd, generator=g, device=device)) / math.sqrt(D)).bfloat16()
+    fk = (F.softplus(torch.randn(B, H, L, Fd, generator=g, device=device)) / math.sqrt(D)).bfloat16()
+    v = torch.randn(B, H, L, D, generator=g, device=device).bfloat16()
+    shape = (B, H, L) if per_head else (B, L)
+    lg = F.logsigmoid(3 + 1.5 * torch.randn(shape, generator=g, device=device))
+    dy = torch.randn(B, H, L, D, generator=g, device=device)
+    return fq, fk, v, lg, dy
+
+
+def test_gla_config2_forward_sampled_heads():
+    """B=8, L=2048, H=32, F=D=128, per-head gate; 4 (b, h) slices checked."""
+    import lizard_cuda
+    fq, fk, v, lg, _ = baseline_inputs(8, 32, 2048, 128, 128, per_head=True)
+    with torch.no_grad():
+        y = lizard_cuda.gla(fq, fk, v, lg)
+    torch.cuda.synchronize()
+    for b, h in ((0, 0), (3, 17), (5, 31), (7, 8)):
+        sl = (slice(b, b + 1), slice(h, h + 1))
+        ref, _ = oracle_gla(fq[sl], fk[sl], v[sl], lg[sl])
+        assert_output(y[sl], ref, f"cfg2 y[{b},{h}]")
+
+
+def test_gla_config3_forward_backward_all_heads():
+    """B=1, L=2048, H=32, F=D=64, per-token gate shared by the heads."""
+    fq, fk, v, lg, dy = baseline_inputs(1, 32, 2048, 64, 64, per_head=False)
+    y, grads = cuda_gla(fq, fk, v, lg, dy)
+    torch.cuda.synchronize()
+    ys, dfq, dfk, dv, dlg = [], [], [], [], torch.zeros(1, 2048, dtype=torch.float32)
+    for h0 in range(0, 32, 8):
+        sl = (slice(None), slice(h0, h0 + 8))
+        r, (a, b_, c, d) = oracle_gla(fq[sl], fk[sl], v[sl], lg, dy[sl])
+        ys.append(r), dfq.append(a), dfk.append(b_), dv.append(c)
+        dlg += d
+    assert_output(y, torch.cat(ys, 1), "cfg3 y")
+    for got, ref, n in zip(grads, (torch.cat(dfq, 1), torch.cat(dfk, 1), torch.cat(dv, 1), dlg),
+                           GRAD_NAMES):
+        assert_grad(got, ref, f"cfg3 {n}")
+
+
+def test_gla_long_sequence_against_recurrent_float64():
+    """64 chunks, F=D=128, per-head gate: the O(L F D) float64 recurrence."""
+    import lizard_cuda
+    fq, fk, v, lg, _ = baseline_inputs(1, 2, 4096, 128, 128, per_head=True, seed=3)
+    with torch.no_grad():
+        y = lizard_cuda.gla(fq, fk, v, lg)
+    ref = orc.gla_recurrent(fq.double().cpu(), fk.double().cpu(), v.double().cpu(),
+                            lg.double().cpu())
+    assert_output(y, ref, "L=4096 y")
+
+
+def test_gla_model_feature_dim_256():
+    """F = 2 * feature_dim = 256 (the 1B model), D = 64, fwd + bwd."""
+    fq, fk, v, lg, dy = baseline_inputs(1, 4, 300, 256, 64, per_head=False, seed=5)
+    y, grads = cuda_gla(fq, fk, v, lg, dy)
+    ref, rgrads = oracle_gla(fq, fk, v, lg, dy)
+    assert_output(y, ref, "F=256 y")
+    for got, r, n in zip(grads, rgrads, GRAD_NAMES):
+        assert_grad(got, r, f"F=256 {n}")
+
+
+def test_gla_without_grad_gives_the_same_output():
+    """tests/test_kernels.py:102-107: bit-identical with and without autograd."""
+    import lizard_cuda
+    inp = cases.gla_case(70)
+    fq, fk, v, lg = (inp[n].to(DEV) for n in ("fq", "fk", "v", "log_gamma"))
+    y = lizard_cuda.gla(fq, fk, v.clone().requires_grad_(), lg)
+    with torch.no_grad():
+        assert torch.equal(lizard_cuda.gla(fq, fk, v, lg), y)
+
+
+def test_gla_chunk_argument_does_not_change_the_result():
+    import lizard_cuda
+    inp = cases.gla_case(150)
+    args = [inp[n].to(DEV) for n in ("fq", "fk", "v", "log_gamma")]
+    with torch.no_grad():
+        assert torch.equal(lizard_cuda.gla(*args, 16), lizard_cuda.gla(*args))
+
+
+def test_gla_single_token_returns_v():
+    """One token: the row sum uses the same rounded weight, so y = v exactly."""
+    import lizard_cuda
+    inp = cases.gla_case(1)
+    fq, fk, v, lg = (inp[n].to(DEV) for n in ("fq", "fk", "v", "log_gamma"))
+    with torch.no_grad():
+        assert torch.equal(lizard_cuda.gla(fq, fk, v, lg), v)
+
+
+def test_gla_very_strong_gate_keeps_only_the_current_token():
+    import lizard_cuda
+    inp = cases.gla_case(130)
+    fq, fk, v = (inp[n].to(DEV) for n in ("fq", "fk", "v"))
+    lg = torch.full(inp["log_gamma"].shape, -90.0, device=DEV)
+    with torch.no_grad():
+        y = lizard_cuda.gla(fq, fk, v, lg)
+    assert orc.max_rel(y.cpu(), v.cpu()) < 4e-3
+
+
+def test_gla_fp32_strided_inputs_give_fp32_grads():
+    """The layer feeds fp32, non-contiguous tensors (src/lizard_attention.py:80-86)."""
+    inp = cases.gla_case(90)
+    fq, fk, v = (inp[n].float().transpose(1, 2).contiguous().transpose(1, 2)
+                 for n in ("fq", "fk", "v"))
+    assert not fq.is_contiguous()
+    y, grads = cuda_gla(fq, fk, v, inp["log_gamma"], inp["dy"])
+    assert all(g.dtype == torch.float32 for g in grads)
+    ref, rgrads = oracle_gla(fq, fk, v, inp["log_gamma"], inp["dy"])
+    assert_output(y, ref, "fp32 y")
+    for got, r, n in zip(grads, rgrads, GRAD_NAMES):
+        assert_grad(got, r, f"fp32 {n}")
+
+
+def test_gla_poisoned_outputs_are_fully_written():
+    """Direct C-ABI call into NaN-filled y and saved buffers: every element of
+    y and of the saved rows is overwritten (no unwritten padding leaks)."""
+    from lizard_cuda import _lib
+    lib = _lib.load()
+    inp = cases.gla_case(77, gates=(3,))
+    fq, fk, v, lg = (inp[n].to(DEV).contiguous() for n in ("fq", "fk", "v", "log_gamma"))
+    B, H, L, Fd = fq.shape
+    D = v.shape[-1]
+    y = torch.full((B, H, L, D), float("nan"), device=DEV, dtype=torch.bfloat16)
+    nbytes = lib.lz_gla_saved_bytes(B, H, L, Fd, D, 64)
+    saved = torch.full((nbytes // 4,), float("nan"), device=DEV, dtype=torch.float32)
+    rc = lib.lz_gla_fwd(_lib.ptr(fq), _lib.ptr(fk), _lib.ptr(v), _lib.ptr(lg), 1, _lib.ptr(y),
+                        _lib.ptr(saved), nbytes, B, H, L, Fd, D, 64, _lib.stream_of(fq))
+    _lib.check(rc, "gla forward")
+    torch.cuda.synchronize()
+    assert torch.isfinite(y).all()
+    y32 = saved[: B * H * L * D].view(B, H, L, D)
+    assert torch.isfinite(y32).all()
+    assert torch.equal(y32.bfloat16(), y)
