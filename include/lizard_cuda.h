@@ -55,6 +55,12 @@ const char* lz_last_error_string(void);
  * Lets a caller count device launches inside a timed region. */
 uint64_t lz_launch_count(void);
 
+/* Every wait inside the tensor-core kernels is bounded (about 2 s); a wait
+ * that gives up records where in this per-device flag and the kernel unwinds
+ * instead of hanging. Reads the flag of the current device into *site
+ * (0 = no wait ever timed out). Synchronous. */
+int lz_device_timeout_flag(unsigned int* site);
+
 /* ------------------------------------------------------------------------ */
 /* GLA                                                                      */
 /* ------------------------------------------------------------------------ */

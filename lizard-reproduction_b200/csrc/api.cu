@@ -16,6 +16,16 @@ int check_sizes(int B, int H, int L, int F, int D) {
 
 }  // namespace
 
+namespace lz {
+int gla_tc_timeout_flag(unsigned int* out);
+}
+
+extern "C" int lz_device_timeout_flag(unsigned int* site) {
+  lz::clear_error();
+  LZ_REQUIRE(site, LZ_ERR_INVALID_ARGUMENT, "null pointer");
+  return lz::gla_tc_timeout_flag(site);
+}
+
 extern "C" size_t lz_gla_saved_bytes(int B, int H, int L, int F, int D, int chunk) {
   (void)chunk;
   if (B < 1 || H < 1 || L < 1 || F < 1 || D < 1) return 0;

@@ -22,6 +22,7 @@ _SIGNATURES = {
     "lz_abi_version": (_c_int, []),
     "lz_last_error_string": (ctypes.c_char_p, []),
     "lz_launch_count": (ctypes.c_uint64, []),
+    "lz_device_timeout_flag": (_c_int, [ctypes.POINTER(ctypes.c_uint)]),
     "lz_gla_saved_bytes": (_c_size, [_c_int] * 6),
     "lz_gla_bwd_workspace_bytes": (_c_size, [_c_int] * 6),
     "lz_gla_fwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_size] + [_c_int] * 6 + [_vp]),
@@ -69,6 +70,13 @@ def check(rc, what):
 
 def launch_count():
     return int(load().lz_launch_count())
+
+
+def device_timeout_flag():
+    """Site of the first bounded wait that gave up on the current device (0 = none)."""
+    out = ctypes.c_uint(0)
+    check(load().lz_device_timeout_flag(ctypes.byref(out)), "timeout flag query")
+    return int(out.value)
 
 
 def ptr(t):

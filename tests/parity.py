@@ -20,10 +20,10 @@ def assert_output(got, ref, what, layer=False):
 
 def assert_grad(got, ref, what):
     got, ref = got.cpu(), ref.cpu()
-    if ref.abs().max().item() < 1e-6:
-        # analytically zero gradient (e.g. fq, fk for a single token): the
-        # reference holds fp32 rounding noise, so compare absolutely
-        assert got.abs().max().item() <= 1e-5, f"{what}: max|got| {got.abs().max().item():.3e}"
+    if ref.abs().max().item() < 1e-5:
+        # analytically zero gradient (fq, fk for a single token: y = v exactly):
+        # the reference holds fp32 rounding noise, so compare absolutely
+        assert got.abs().max().item() <= 1e-4, f"{what}: max|got| {got.abs().max().item():.3e}"
         return
     m = orc.max_rel(got, ref)
     ok = orc.close(got, ref, BACKWARD)

@@ -188,3 +188,30 @@ def test_gla_poisoned_outputs_are_fully_written():
     y32 = saved[: B * H * L * D].view(B, H, L, D)
     assert torch.isfinite(y32).all()
     assert torch.equal(y32.bfloat16(), y)
+
+
+@pytest.mark.parametrize("per_head,L", [(False, 300), (True, 256), (True, 1)])
+def test_gla_f128_d128_forward_backward(per_head, L):
+    """F = D = 128 runs the tensor-core forward (128-token chunks) and, in
+    training mode, the 64-token state walk feeding the backward."""
+    fq, fk, v, lg, dy = baseline_inputs(2, 3, L, 128, 128, per_head=per_head, seed=11)
+    y, grads = cuda_gla(fq, fk, v, lg, dy)
+    ref, rgrads = oracle_gla(fq, fk, v, lg, dy)
+    assert_output(y, ref, f"F=D=128 L={L} y")
+    for got, r, n in zip(grads, rgrads, GRAD_NAMES):
+        assert_grad(got, r, f"F=D=128 L={L} {n}")
+
+
+def test_gla_f128_without_grad_gives_the_same_output():
+    import lizard_cuda
+    fq, fk, v, lg, _ = baseline_inputs(2, 2, 333, 128, 128, per_head=True, seed=12)
+    y = lizard_cuda.gla(fq, fk, v.clone().requires_grad_(), lg)
+    with torch.no_grad():
+        assert torch.equal(lizard_cuda.gla(fq, fk, v, lg), y)
+
+
+def test_no_kernel_wait_timed_out():
+    """Every bounded wait inside the tensor-core kernels completed."""
+    from lizard_cuda import _lib
+    torch.cuda.synchronize()
+    assert _lib.device_timeout_flag() == 0
