@@ -33,32 +33,59 @@ constexpr int kC = 128;                     // tokens per chunk
 constexpr int kStageBytes = 6 * 16384;      // fq, fk, v: two 64-column blocks each
 constexpr int kOffQ = 0, kOffK = 32768, kOffV = 65536;
 constexpr int kOffS = 2 * kStageBytes;      // bf16 state S [F x D], MN-major
-constexpr int kOffMisc = kOffS + 32768;     // ones row + barriers + gates (2 KB)
-constexpr int kSmemBytes = kOffMisc + 2048 + 1024;  // + alignment slack
-// misc block (the first 128 B are the "ones" B-operand row of dz = K~^T 1;
-// the MMA also reads rows 1..15 of this 2 KB block, whose products land in
-// accumulator columns that are never read)
-constexpr int kMiscBars = 128, kMiscG = 256, kMiscZ = 768, kMiscScan = 1280, kMiscTmem = 1296;
-// TMEM columns
-constexpr uint32_t kTS = 0, kTA = 128, kTO = 192, kTDS = 320, kTDZ = 448, kTCols = 512;
+constexpr int kOffMisc = kOffS + 32768;     // ones row + barriers + per-chunk scalars
+constexpr int kMiscBytes = 3072;
+constexpr int kSmemBytes = kOffMisc + kMiscBytes;  // = 232448, the sm_100 maximum
+// misc block layout. Bytes [0, 128) are the "ones" row of the B operand of
+// z += K~^T 1 (a K-major [16 x 64] tile); the MMA also reads bytes
+// [128, 2048) as rows 1..15 of that tile, whose products land in TMEM columns
+// that are never read, so small scalars live there.
+constexpr int kMiscBars = 128;    // 12 mbarriers
+constexpr int kMiscG = 256;       // g2 of the current chunk, 128 floats
+constexpr int kMiscB = 768;       // column decay factors 2^(g2_ref - g2_t), 128 floats
+constexpr int kMiscGS = 1792;     // (start2, end2) per chunk parity
+constexpr int kMiscScan = 1824;   // 4 warp totals
+constexpr int kMiscTmem = 1840;   // TMEM base address
+constexpr int kMiscZ = 2048;      // z_n for den = Q~ . z, 2 x 128 floats (by parity)
+// TMEM columns: scores s, output o, running state S (fp32), normaliser z
+// (col 0; cols 1..15 unused), bf16 intra weights a (the A operand of a V),
+// intra-chunk row sums (one column per chunk parity)
+constexpr uint32_t kTSA = 0, kTO = 128, kTSF = 256, kTZ = 384, kTA = 400, kTDEN = 464,
+                   kTCols = 512;
 
 enum { BAR_FULL0 = 0, BAR_FULL1, BAR_EMPTY0, BAR_EMPTY1, BAR_SFULL, BAR_AREADY, BAR_OFULL,
-       BAR_SREADY, BAR_COUNT };
+       BAR_SREADY, BAR_GATE, BAR_DEN0, BAR_DEN1, BAR_COUNT };
 
-__global__ void __launch_bounds__(192, 1)
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 decay, warps 6-9 output
+
+__device__ __forceinline__ uint4 scale8(uint4 w, float sc) {
+  w.x = pack_bf16(bf16_lo(w.x) * sc, bf16_hi(w.x) * sc);
+  w.y = pack_bf16(bf16_lo(w.y) * sc, bf16_hi(w.y) * sc);
+  w.z = pack_bf16(bf16_lo(w.z) * sc, bf16_hi(w.z) * sc);
+  w.w = pack_bf16(bf16_lo(w.w) * sc, bf16_hi(w.w) * sc);
+  return w;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
 gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                  const __grid_constant__ CUtensorMap tv, const float* __restrict__ lg,
+                  const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap ty,
+                  const float* __restrict__ lg,
                   int gate_per_head, int H, int L, int NT, bf16* __restrict__ y,
                   float* __restrict__ y32, float* __restrict__ den_out,
                   float* __restrict__ g_out) {
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* base = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  if (smem_u32(smem_raw) & 1023) {  // the tile swizzle needs a 1024-byte aligned window
+    if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 99u);
+    return;
+  }
+  unsigned char* base = smem_raw;
   unsigned char* misc = base + kOffMisc;
   uint64_t* bars = reinterpret_cast<uint64_t*>(misc + kMiscBars);
   float* sG = reinterpret_cast<float*>(misc + kMiscG);
-  float* sZ = reinterpret_cast<float*>(misc + kMiscZ);
+  float* sB = reinterpret_cast<float*>(misc + kMiscB);
+  float* sGS = reinterpret_cast<float*>(misc + kMiscGS);
   float* sScan = reinterpret_cast<float*>(misc + kMiscScan);
+  float* sZ = reinterpret_cast<float*>(misc + kMiscZ);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + kMiscTmem);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -68,27 +95,34 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   if (tid == 0) {
     tc::mbar_init(&bars[BAR_FULL0], 1);
     tc::mbar_init(&bars[BAR_FULL1], 1);
-    tc::mbar_init(&bars[BAR_EMPTY0], 1);
-    tc::mbar_init(&bars[BAR_EMPTY1], 1);
+    // a stage is free once its MMAs are done and its fq block, reused as the
+    // y staging tile, has been read by the output store
+    tc::mbar_init(&bars[BAR_EMPTY0], 2);
+    tc::mbar_init(&bars[BAR_EMPTY1], 2);
     tc::mbar_init(&bars[BAR_SFULL], 1);
     tc::mbar_init(&bars[BAR_AREADY], 128);
     tc::mbar_init(&bars[BAR_OFULL], 1);
     tc::mbar_init(&bars[BAR_SREADY], 128);
+    tc::mbar_init(&bars[BAR_GATE], 128);
+    tc::mbar_init(&bars[BAR_DEN0], 128);
+    tc::mbar_init(&bars[BAR_DEN1], 128);
     tc::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     tc::prefetch_tmap(&tq);
     tc::prefetch_tmap(&tk);
     tc::prefetch_tmap(&tv);
+    tc::prefetch_tmap(&ty);
   }
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, kTCols);
     tc::tmem_relinquish();
   }
-  if (warp >= 2) {
+  if (warp >= 2 && warp < 6) {
     const int e = tid - 64;  // 0..127
     if (e < 64) reinterpret_cast<bf16*>(misc)[e] = __float2bfloat16_rn(1.f);
     sZ[e] = 0.f;
+    sZ[128 + e] = 0.f;
     tc::fence_proxy_async_smem();
   }
   tc::tc_fence_before();
@@ -114,15 +148,14 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         tc::tma_load_3d(stage + kOffV + 16384, &tv, 64, n * kC, bh, full);
         ++issued[st];
       }
-      // let every issued copy land before the CTA can exit
-      for (int st = 0; st < 2; ++st)
+      for (int st = 0; st < 2; ++st)  // every issued copy lands before exit
         if (issued[st]) tc::mbar_wait(&bars[BAR_FULL0 + st], (issued[st] - 1) & 1, 9);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
       constexpr uint32_t id_s = tc::idesc_bf16(128, 128, 0, 0);   // fq (K) x fk (K)
-      constexpr uint32_t id_o = tc::idesc_bf16(128, 128, 0, 1);   // Q~ (K) x S (MN)
+      constexpr uint32_t id_o = tc::idesc_bf16(128, 128, 0, 1);   // Q~|a (K) x S|V (MN)
       constexpr uint32_t id_ds = tc::idesc_bf16(128, 128, 1, 1);  // K~ (MN) x V (MN)
       constexpr uint32_t id_dz = tc::idesc_bf16(128, 16, 1, 0);   // K~ (MN) x ones (K)
       const uint32_t s_addr = smem_u32(base + kOffS);
@@ -136,8 +169,8 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t ko = (j >> 2) * 16384 + (j & 3) * 32;
-          tc::mma_ss(tmem + kTS, tc::sdesc(qa + ko, 16, 1024), tc::sdesc(ka + ko, 16, 1024), id_s,
-                     j > 0);
+          tc::mma_ss(tmem + kTSA, tc::sdesc(qa + ko, 16, 1024), tc::sdesc(ka + ko, 16, 1024),
+                     id_s, j > 0);
         }
         tc::mma_commit(&bars[BAR_SFULL]);
         if (!tc::mbar_wait(&bars[BAR_AREADY], n & 1, 3)) break;
@@ -155,172 +188,260 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         for (int j = 0; j < 8; ++j)
           tc::mma_ts(tmem + kTO, tmem + kTA + 8 * j, tc::sdesc(va + 2048 * j, 16384, 1024), id_o,
                      (n > 0 || j > 0) ? 1u : 0u);
+        // running state: the output warps pre-scaled S and z by this chunk's decay
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          tc::mma_ss(tmem + kTDS, tc::sdesc(ka + 2048 * j, 16384, 1024),
-                     tc::sdesc(va + 2048 * j, 16384, 1024), id_ds, j > 0);
+          tc::mma_ss(tmem + kTSF, tc::sdesc(ka + 2048 * j, 16384, 1024),
+                     tc::sdesc(va + 2048 * j, 16384, 1024), id_ds, (n > 0 || j > 0) ? 1u : 0u);
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          tc::mma_ss(tmem + kTDZ, tc::sdesc(ka + 2048 * j, 16384, 1024),
-                     tc::sdesc(ones + 32 * (j & 3), 16, 1024), id_dz, j > 0);
+          tc::mma_ss(tmem + kTZ, tc::sdesc(ka + 2048 * j, 16384, 1024),
+                     tc::sdesc(ones + 32 * (j & 3), 16, 1024), id_dz, (n > 0 || j > 0) ? 1u : 0u);
         tc::mma_commit(&bars[BAR_OFULL]);
         tc::mma_commit(&bars[BAR_EMPTY0 + st]);
       }
     }
-  } else {
-    // ------------------------------------------------------------ epilogue
+  } else if (warp < 6) {
+    // ------------------------------- decay warps: gates, s -> a, K~ in place
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // chunk row == TMEM lane == state row f
+    const int r = quad * 32 + lane;  // chunk row == TMEM lane
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
     const float* LG = lg + (size_t)(gate_per_head ? bh : b) * L;
-    float S[128];
-#pragma unroll
-    for (int i = 0; i < 128; ++i) S[i] = 0.f;
-    float z = 0.f, carry = 0.f;
-    unsigned char* srow_base = base + kOffS + r * 128;
+    float carry = 0.f;
+    float lg_next = (r < L) ? LG[r] : 0.f;
     for (int n = 0; n < NT; ++n) {
       const int r0 = n * kC;
       const int nvalid = min(kC, L - r0);
       const bool valid = r < nvalid;
+      float x = valid ? lg_next * kLog2e : 0.f;
+      if (r0 + kC + r < L) lg_next = LG[r0 + kC + r];  // prefetch the next chunk's gate
+      if (!__all_sync(0xffffffffu, tc::mbar_wait(&bars[BAR_SFULL], n & 1, 5))) break;
+      tc::tc_fence_after();
       // running log2 gate: inclusive scan over the chunk's 128 rows
-      float x = valid ? LG[r0 + r] * kLog2e : 0.f;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const float u = __shfl_up_sync(0xffffffffu, x, o);
         if (lane >= o) x += u;
       }
       if (lane == 31) sScan[quad] = x;
-      tc::named_bar_sync(1, 128);  // also orders last chunk's sZ writes
+      tc::named_bar_sync(1, 128);
       float pre = 0.f;
 #pragma unroll
       for (int qq = 0; qq < 4; ++qq)
         if (qq < quad) pre += sScan[qq];
       const float g2 = carry + pre + x;
       sG[r] = g2;
+      // column factor relative to the last row of this row's 32-block (= lane 31)
+      sB[r] = tc::ex2(__shfl_sync(0xffffffffu, g2, 31) - g2);
+      const float start2 = carry;
+      if (r == 0) sGS[(n & 1) * 2] = start2;
+      if (r == nvalid - 1) sGS[(n & 1) * 2 + 1] = g2;
       tc::named_bar_sync(1, 128);
-      const float start2 = carry, end2 = sG[nvalid - 1];
+      const float end2 = sGS[(n & 1) * 2 + 1];
       carry = end2;
+      tc::mbar_arrive(&bars[BAR_GATE]);
       if (save && valid) g_out[(size_t)bh * L + r0 + r] = g2 * 0.6931471805599453f;
-
-      if (!__all_sync(0xffffffffu, tc::mbar_wait(&bars[BAR_SFULL], n & 1, 5))) break;
-      tc::tc_fence_after();
-      // a = bf16(s * decay) for t <= r, row sum of the rounded weights
+      // a = bf16(s 2^(g2_r - g2_t)) for t <= r. Blocks left of the diagonal use
+      // 2^(g2_r - g2_ref) 2^(g2_ref - g2_t) with ref the block's last row (both
+      // factors <= 1); the diagonal block takes one ex2 per element; blocks to
+      // its right are zero.
       float den = 0.f;
-#pragma unroll
+#pragma unroll 1
       for (int cb = 0; cb < 4; ++cb) {
-        float s[32];
-        tc::tmem_ld32(trow + kTS + 32 * cb, s);
-        tc::tmem_wait_ld();
         uint32_t pk[16];
+        if (cb < quad) {
+          float s[32];
+          tc::tmem_ld32(trow + kTSA + 32 * cb, s);
+          const float ar = valid ? tc::ex2(g2 - sG[32 * cb + 31]) : 0.f;
+          const float4* bt = reinterpret_cast<const float4*>(sB + 32 * cb);
+          tc::tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int t0 = 32 * cb + 2 * j;
-          const float w0 = (t0 <= r && valid) ? s[2 * j] * exp2f(g2 - sG[t0]) : 0.f;
-          const float w1 = (t0 + 1 <= r && valid) ? s[2 * j + 1] * exp2f(g2 - sG[t0 + 1]) : 0.f;
-          pk[j] = pack_bf16(w0, w1);
-          den += bf16_lo(pk[j]) + bf16_hi(pk[j]);
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 f = bt[j4];
+            const uint32_t p0 = pack_bf16(s[4 * j4] * f.x * ar, s[4 * j4 + 1] * f.y * ar);
+            const uint32_t p1 = pack_bf16(s[4 * j4 + 2] * f.z * ar, s[4 * j4 + 3] * f.w * ar);
+            pk[2 * j4] = p0;
+            pk[2 * j4 + 1] = p1;
+            den += (bf16_lo(p0) + bf16_hi(p0)) + (bf16_lo(p1) + bf16_hi(p1));
+          }
+        } else if (cb == quad) {
+          float s[32];
+          tc::tmem_ld32(trow + kTSA + 32 * cb, s);
+          const float4* gt = reinterpret_cast<const float4*>(sG + 32 * cb);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 f = gt[j4];
+            const int t = 32 * cb + 4 * j4;
+            float w0 = s[4 * j4] * tc::ex2(g2 - f.x);
+            float w1 = s[4 * j4 + 1] * tc::ex2(g2 - f.y);
+            float w2 = s[4 * j4 + 2] * tc::ex2(g2 - f.z);
+            float w3 = s[4 * j4 + 3] * tc::ex2(g2 - f.w);
+            w0 = (t <= r && valid) ? w0 : 0.f;
+            w1 = (t + 1 <= r && valid) ? w1 : 0.f;
+            w2 = (t + 2 <= r && valid) ? w2 : 0.f;
+            w3 = (t + 3 <= r && valid) ? w3 : 0.f;
+            const uint32_t p0 = pack_bf16(w0, w1), p1 = pack_bf16(w2, w3);
+            pk[2 * j4] = p0;
+            pk[2 * j4 + 1] = p1;
+            den += (bf16_lo(p0) + bf16_hi(p0)) + (bf16_lo(p1) + bf16_hi(p1));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) pk[j] = 0u;
         }
         tc::tmem_st16(trow + kTA + 16 * cb, pk);
       }
-      // Q~ and K~ rows in place (row r of each swizzled 64-column block);
-      // den += Q~_r . z
+      tc::tmem_st1(trow + kTDEN + (n & 1), __float_as_uint(den));
+      // K~ = fk 2^(end - g2) in place (row r of both 64-column blocks)
       {
         unsigned char* stage = base + (n & 1) * kStageBytes;
-        const float qs = valid ? exp2f(g2 - start2) : 0.f;
-        const float ks = valid ? exp2f(end2 - g2) : 0.f;
-        float dz = 0.f;
+        const float ks = valid ? tc::ex2(end2 - g2) : 0.f;
+        uint4 w[16];
 #pragma unroll
-        for (int blk = 0; blk < 2; ++blk) {
-          unsigned char* rq = stage + kOffQ + blk * 16384 + r * 128;
-          unsigned char* rk = stage + kOffK + blk * 16384 + r * 128;
+        for (int i = 0; i < 16; ++i)
+          w[i] = *reinterpret_cast<const uint4*>(stage + kOffK + (i >> 3) * 16384 + r * 128 +
+                                                 (((i & 7) ^ (r & 7)) * 16));
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const int p = (c ^ (r & 7)) * 16;
-            uint4 w = *reinterpret_cast<uint4*>(rq + p);
-            w.x = pack_bf16(bf16_lo(w.x) * qs, bf16_hi(w.x) * qs);
-            w.y = pack_bf16(bf16_lo(w.y) * qs, bf16_hi(w.y) * qs);
-            w.z = pack_bf16(bf16_lo(w.z) * qs, bf16_hi(w.z) * qs);
-            w.w = pack_bf16(bf16_lo(w.w) * qs, bf16_hi(w.w) * qs);
-            *reinterpret_cast<uint4*>(rq + p) = w;
-            const float* zz = sZ + blk * 64 + c * 8;
-            dz += bf16_lo(w.x) * zz[0] + bf16_hi(w.x) * zz[1] + bf16_lo(w.y) * zz[2] +
-                  bf16_hi(w.y) * zz[3] + bf16_lo(w.z) * zz[4] + bf16_hi(w.z) * zz[5] +
-                  bf16_lo(w.w) * zz[6] + bf16_hi(w.w) * zz[7];
-            uint4 u = *reinterpret_cast<uint4*>(rk + p);
-            u.x = pack_bf16(bf16_lo(u.x) * ks, bf16_hi(u.x) * ks);
-            u.y = pack_bf16(bf16_lo(u.y) * ks, bf16_hi(u.y) * ks);
-            u.z = pack_bf16(bf16_lo(u.z) * ks, bf16_hi(u.z) * ks);
-            u.w = pack_bf16(bf16_lo(u.w) * ks, bf16_hi(u.w) * ks);
-            *reinterpret_cast<uint4*>(rk + p) = u;
-          }
-        }
-        den += dz;
+        for (int i = 0; i < 16; ++i)
+          *reinterpret_cast<uint4*>(stage + kOffK + (i >> 3) * 16384 + r * 128 +
+                                    (((i & 7) ^ (r & 7)) * 16)) = scale8(w[i], ks);
       }
       tc::fence_proxy_async_smem();
       tc::tmem_wait_st();
       tc::tc_fence_before();
       tc::mbar_arrive(&bars[BAR_AREADY]);
-
+      tc::mbar_arrive(&bars[BAR_DEN0 + (n & 1)]);
+    }
+  } else {
+    // ---------- output warps: y; S, z for the next chunk; Q~ in place, Q~ . z
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // chunk row for o; state row f for S, z
+    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+    unsigned char* srow_base = base + kOffS + r * 128;
+    float den_inter = 0.f;  // Q~_r . z_n of the chunk about to be output
+    for (int n = 0; n < NT; ++n) {
+      const int r0 = n * kC;
+      const int nvalid = min(kC, L - r0);
+      const bool valid = r < nvalid;
       if (!__all_sync(0xffffffffu, tc::mbar_wait(&bars[BAR_OFULL], n & 1, 6))) break;
+      if (!__all_sync(0xffffffffu,
+                      tc::mbar_wait(&bars[BAR_DEN0 + (n & 1)], (n >> 1) & 1, 8)))
+        break;
       tc::tc_fence_after();
-      const float inv = 1.f / fmaxf(den, kTiny);
+      // y = o / max(den, FLT_MIN)
+      const float den = tc::tmem_ld1(trow + kTDEN + (n & 1));
+      tc::tmem_wait_ld();
+      const float dtot = den + den_inter;
+      const float inv = 1.f / fmaxf(dtot, kTiny);
       const size_t row = (size_t)bh * L + r0 + r;
-#pragma unroll
+      // y rows go to the stage's fq block (free now: every MMA of this chunk is
+      // done) in the 128-byte swizzled box layout, then out with one TMA store
+      unsigned char* ystage = base + (n & 1) * kStageBytes + kOffQ;
+#pragma unroll 1
       for (int cb = 0; cb < 4; ++cb) {
         float o[32];
         tc::tmem_ld32(trow + kTO + 32 * cb, o);
         tc::tmem_wait_ld();
-        if (valid) {
-          uint4* dst = reinterpret_cast<uint4*>(y + row * 128 + 32 * cb);
+        unsigned char* yrow = ystage + (cb >> 1) * 16384 + r * 128;
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            uint4 w;
-            w.x = pack_bf16(o[8 * q4 + 0] * inv, o[8 * q4 + 1] * inv);
-            w.y = pack_bf16(o[8 * q4 + 2] * inv, o[8 * q4 + 3] * inv);
-            w.z = pack_bf16(o[8 * q4 + 4] * inv, o[8 * q4 + 5] * inv);
-            w.w = pack_bf16(o[8 * q4 + 6] * inv, o[8 * q4 + 7] * inv);
-            dst[q4] = w;
-          }
-          if (save) {
-            float4* d32 = reinterpret_cast<float4*>(y32 + row * 128 + 32 * cb);
-#pragma unroll
-            for (int q4 = 0; q4 < 8; ++q4)
-              d32[q4] = make_float4(o[4 * q4] * inv, o[4 * q4 + 1] * inv, o[4 * q4 + 2] * inv,
-                                    o[4 * q4 + 3] * inv);
-          }
-        }
-      }
-      if (save && valid) den_out[row] = den;
-      // S <- 2^(end-start) S + dS ; publish bf16 S for the next chunk
-      const float decay = exp2f(end2 - start2);
-#pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        float d[32];
-        tc::tmem_ld32(trow + kTDS + 32 * cb, d);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) S[32 * cb + j] = S[32 * cb + j] * decay + d[j];
-        unsigned char* srow = srow_base + (cb >> 1) * 16384;
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int c = (cb & 1) * 4 + cc;
-          const float* v8 = &S[32 * cb + 8 * cc];
+        for (int q4 = 0; q4 < 4; ++q4) {
           uint4 w;
-          w.x = pack_bf16(v8[0], v8[1]);
-          w.y = pack_bf16(v8[2], v8[3]);
-          w.z = pack_bf16(v8[4], v8[5]);
-          w.w = pack_bf16(v8[6], v8[7]);
-          *reinterpret_cast<uint4*>(srow + ((c ^ (r & 7)) * 16)) = w;
+          w.x = pack_bf16(o[8 * q4 + 0] * inv, o[8 * q4 + 1] * inv);
+          w.y = pack_bf16(o[8 * q4 + 2] * inv, o[8 * q4 + 3] * inv);
+          w.z = pack_bf16(o[8 * q4 + 4] * inv, o[8 * q4 + 5] * inv);
+          w.w = pack_bf16(o[8 * q4 + 6] * inv, o[8 * q4 + 7] * inv);
+          const int c = (cb & 1) * 4 + q4;
+          *reinterpret_cast<uint4*>(yrow + ((c ^ (r & 7)) * 16)) = w;
+        }
+        if (save && valid) {
+          float4* d32 = reinterpret_cast<float4*>(y32 + row * 128 + 32 * cb);
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4)
+            d32[q4] = make_float4(o[4 * q4] * inv, o[4 * q4 + 1] * inv, o[4 * q4 + 2] * inv,
+                                  o[4 * q4 + 3] * inv);
         }
       }
-      const float dzn = tc::tmem_ld1(trow + kTDZ);
-      tc::tmem_wait_ld();
-      z = z * decay + dzn;
-      sZ[r] = z;
       tc::fence_proxy_async_smem();
+      tc::named_bar_sync(2, 128);
+      if (r == 0) {
+        tc::tma_store_3d(&ty, ystage, 0, r0, bh);
+        tc::tma_store_3d(&ty, ystage + 16384, 64, r0, bh);
+        tc::bulk_commit();
+        tc::bulk_wait_read0();
+        tc::mbar_arrive(&bars[BAR_EMPTY0 + (n & 1)]);
+      }
+      __syncwarp();
+      if (save && valid) den_out[row] = dtot;
+      if (n + 1 < NT) {
+        // prepare chunk n+1: bf16 S_{n+1}; S and z pre-scaled by its decay;
+        // Q~_{n+1} in place and its row sums against z_{n+1}
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&bars[BAR_GATE], (n + 1) & 1, 10))) break;
+        const float start2 = sGS[((n + 1) & 1) * 2], end2 = sGS[((n + 1) & 1) * 2 + 1];
+        const float decay = tc::ex2(end2 - start2);
+        const float g2r = sG[r];
+        const float zn = tc::tmem_ld1(trow + kTZ);
+        tc::tmem_wait_ld();
+        float* zbuf = sZ + ((n + 1) & 1) * 128;
+        zbuf[r] = zn;
+        tc::tmem_st1(trow + kTZ, __float_as_uint(zn * decay));
+#pragma unroll 1
+        for (int cb = 0; cb < 4; ++cb) {
+          float sv[32];
+          tc::tmem_ld32(trow + kTSF + 32 * cb, sv);
+          tc::tmem_wait_ld();
+          unsigned char* srow = srow_base + (cb >> 1) * 16384;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const int c = (cb & 1) * 4 + cc;
+            const float* v8 = &sv[8 * cc];
+            uint4 w;
+            w.x = pack_bf16(v8[0], v8[1]);
+            w.y = pack_bf16(v8[2], v8[3]);
+            w.z = pack_bf16(v8[4], v8[5]);
+            w.w = pack_bf16(v8[6], v8[7]);
+            *reinterpret_cast<uint4*>(srow + ((c ^ (r & 7)) * 16)) = w;
+          }
+          uint32_t lo[16], hi[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            lo[j] = __float_as_uint(sv[j] * decay);
+            hi[j] = __float_as_uint(sv[16 + j] * decay);
+          }
+          tc::tmem_st16(trow + kTSF + 32 * cb, lo);
+          tc::tmem_st16(trow + kTSF + 32 * cb + 16, hi);
+        }
+        tc::named_bar_sync(2, 128);  // all of z_{n+1} is in zbuf
+        {
+          const bool nvld = r < min(kC, L - r0 - kC);
+          const float qs = nvld ? tc::ex2(g2r - start2) : 0.f;
+          unsigned char* stage = base + ((n + 1) & 1) * kStageBytes;
+          uint4 w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            w[i] = *reinterpret_cast<const uint4*>(stage + kOffQ + (i >> 3) * 16384 + r * 128 +
+                                                   (((i & 7) ^ (r & 7)) * 16));
+          float dz = 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const uint4 q = scale8(w[i], qs);
+            *reinterpret_cast<uint4*>(stage + kOffQ + (i >> 3) * 16384 + r * 128 +
+                                      (((i & 7) ^ (r & 7)) * 16)) = q;
+            const float4 z0 = *reinterpret_cast<const float4*>(zbuf + (i >> 3) * 64 + (i & 7) * 8);
+            const float4 z1 = *reinterpret_cast<const float4*>(zbuf + (i >> 3) * 64 + (i & 7) * 8 + 4);
+            dz += bf16_lo(q.x) * z0.x + bf16_hi(q.x) * z0.y + bf16_lo(q.y) * z0.z +
+                  bf16_hi(q.y) * z0.w + bf16_lo(q.z) * z1.x + bf16_hi(q.z) * z1.y +
+                  bf16_lo(q.w) * z1.z + bf16_hi(q.w) * z1.w;
+          }
+          den_inter = dz;
+        }
+      }
+      tc::fence_proxy_async_smem();
+      tc::tmem_wait_st();
       tc::tc_fence_before();
       tc::mbar_arrive(&bars[BAR_SREADY]);
     }
+    if (r == 0) tc::bulk_wait0();  // output stores complete before the CTA exits
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -374,8 +495,9 @@ int gla_fwd_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
   if (!aligned16(fq) || !aligned16(fk) || !aligned16(v) || !aligned16(y)) return LZ_ERR_UNSUPPORTED;
   if (sv.y32 && !aligned16(sv.y32)) return LZ_ERR_UNSUPPORTED;
   const int BH = B * H;
-  CUtensorMap mq, mk, mv;
-  if (!make_map(&mq, fq, BH, L, F) || !make_map(&mk, fk, BH, L, F) || !make_map(&mv, v, BH, L, D))
+  CUtensorMap mq, mk, mv, my;
+  if (!make_map(&mq, fq, BH, L, F) || !make_map(&mk, fk, BH, L, F) || !make_map(&mv, v, BH, L, D) ||
+      !make_map(&my, y, BH, L, D))
     return LZ_ERR_UNSUPPORTED;
   static std::mutex mu;
   static bool attr_done[64] = {false};
@@ -395,7 +517,7 @@ int gla_fwd_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
     }
   }
   const int NT = (L + kC - 1) / kC;
-  gla_fwd_tc_kernel<<<BH, 192, kSmemBytes, stream>>>(mq, mk, mv, lg, gph, H, L, NT, y, sv.y32,
+  gla_fwd_tc_kernel<<<BH, kThreads, kSmemBytes, stream>>>(mq, mk, mv, my, lg, gph, H, L, NT, y, sv.y32,
                                                      sv.den, sv.g);
   count_launches(1);
   return check_launch("gla_fwd_tc_kernel");
