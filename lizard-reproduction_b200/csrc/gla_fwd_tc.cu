@@ -36,25 +36,28 @@ constexpr int kOffS = 2 * kStageBytes;      // bf16 state S [F x D], MN-major
 constexpr int kOffMisc = kOffS + 32768;     // ones row + barriers + per-chunk scalars
 constexpr int kMiscBytes = 3072;
 constexpr int kSmemBytes = kOffMisc + kMiscBytes;  // = 232448, the sm_100 maximum
-// misc block layout. Bytes [0, 128) are the "ones" row of the B operand of
-// z += K~^T 1 (a K-major [16 x 64] tile); the MMA also reads bytes
-// [128, 2048) as rows 1..15 of that tile, whose products land in TMEM columns
-// that are never read, so small scalars live there.
-constexpr int kMiscBars = 128;    // 12 mbarriers
-constexpr int kMiscG = 256;       // g2 of the current chunk, 128 floats
-constexpr int kMiscB = 768;       // column decay factors 2^(g2_ref - g2_t), 128 floats
-constexpr int kMiscGS = 1792;     // (start2, end2) per chunk parity
-constexpr int kMiscScan = 1824;   // 4 warp totals
-constexpr int kMiscTmem = 1840;   // TMEM base address
-constexpr int kMiscZ = 2048;      // z_n for den = Q~ . z, 2 x 128 floats (by parity)
+// misc block layout. It doubles as the 16-row K-major B operand of the
+// row-sum MMAs:
+//   block A = bytes [0, 2048): row 0 ones, row 1 z_hi[0:64], row 2 z_lo[0:64]
+//   block B = bytes [1024, 3072): row 0 ones, row 1 z_hi[64:128], row 2 z_lo[64:128]
+// (block B's rows 0-7 are block A's rows 8-15). den_intra = a . (row 0) and
+// den_inter = Q~ . (row 1 + row 2) land in TMEM columns; the products of the
+// other rows land in columns that are never read, so the remaining bytes hold
+// barriers and per-chunk scalars.
+constexpr int kMiscBars = 384;    // 12 mbarriers (rows 3..)
+constexpr int kMiscGS = 512;      // (start2, end2) per chunk parity
+constexpr int kMiscScan = 544;    // 4 warp totals
+constexpr int kMiscTmem = 560;    // TMEM base address
+constexpr int kMiscG = 1408;      // g2 of the current chunk, 128 floats
+constexpr int kMiscB = 2048;      // column decay factors 2^(g2_ref - g2_t), 128 floats
 // TMEM columns: scores s, output o, running state S (fp32), normaliser z
-// (col 0; cols 1..15 unused), bf16 intra weights a (the A operand of a V),
-// intra-chunk row sums (one column per chunk parity)
-constexpr uint32_t kTSA = 0, kTO = 128, kTSF = 256, kTZ = 384, kTA = 400, kTDEN = 464,
-                   kTCols = 512;
+// (col 0), bf16 intra weights a (the A operand of a V), row sums: a . 1 at
+// kTDI, Q~ . z_hi and Q~ . z_lo at kTDQ + 1, + 2
+constexpr uint32_t kTSA = 0, kTO = 128, kTSF = 256, kTZ = 384, kTA = 400, kTDI = 464,
+                   kTDQ = 480, kTCols = 512;
 
 enum { BAR_FULL0 = 0, BAR_FULL1, BAR_EMPTY0, BAR_EMPTY1, BAR_SFULL, BAR_AREADY, BAR_OFULL,
-       BAR_SREADY, BAR_GATE, BAR_DEN0, BAR_DEN1, BAR_COUNT };
+       BAR_SREADY, BAR_GATE, BAR_SFDONE, BAR_COUNT };
 
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 decay, warps 6-9 output
 
@@ -85,7 +88,6 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   float* sB = reinterpret_cast<float*>(misc + kMiscB);
   float* sGS = reinterpret_cast<float*>(misc + kMiscGS);
   float* sScan = reinterpret_cast<float*>(misc + kMiscScan);
-  float* sZ = reinterpret_cast<float*>(misc + kMiscZ);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + kMiscTmem);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -104,8 +106,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     tc::mbar_init(&bars[BAR_OFULL], 1);
     tc::mbar_init(&bars[BAR_SREADY], 128);
     tc::mbar_init(&bars[BAR_GATE], 128);
-    tc::mbar_init(&bars[BAR_DEN0], 128);
-    tc::mbar_init(&bars[BAR_DEN1], 128);
+    tc::mbar_init(&bars[BAR_SFDONE], 1);
     tc::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -120,9 +121,17 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   }
   if (warp >= 2 && warp < 6) {
     const int e = tid - 64;  // 0..127
-    if (e < 64) reinterpret_cast<bf16*>(misc)[e] = __float2bfloat16_rn(1.f);
-    sZ[e] = 0.f;
-    sZ[128 + e] = 0.f;
+    // ones in row 0 of both operand blocks, z = 0 in rows 1 and 2
+    if (e < 64) {
+      reinterpret_cast<bf16*>(misc)[e] = __float2bfloat16_rn(1.f);
+      reinterpret_cast<bf16*>(misc + 1024)[e] = __float2bfloat16_rn(1.f);
+    } else {
+      const int i = e - 64;
+      reinterpret_cast<bf16*>(misc + 128)[i] = __float2bfloat16_rn(0.f);
+      reinterpret_cast<bf16*>(misc + 256)[i] = __float2bfloat16_rn(0.f);
+      reinterpret_cast<bf16*>(misc + 1024 + 128)[i] = __float2bfloat16_rn(0.f);
+      reinterpret_cast<bf16*>(misc + 1024 + 256)[i] = __float2bfloat16_rn(0.f);
+    }
     tc::fence_proxy_async_smem();
   }
   tc::tc_fence_before();
@@ -158,47 +167,73 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       constexpr uint32_t id_o = tc::idesc_bf16(128, 128, 0, 1);   // Q~|a (K) x S|V (MN)
       constexpr uint32_t id_ds = tc::idesc_bf16(128, 128, 1, 1);  // K~ (MN) x V (MN)
       constexpr uint32_t id_dz = tc::idesc_bf16(128, 16, 1, 0);   // K~ (MN) x ones (K)
+      constexpr uint32_t id_n16 = tc::idesc_bf16(128, 16, 0, 0);  // Q~|a (K) x ones|z (K)
       const uint32_t s_addr = smem_u32(base + kOffS);
       const uint32_t ones = smem_u32(misc);
-      for (int n = 0; n < NT; ++n) {
-        const int st = n & 1;
-        if (!tc::mbar_wait(&bars[BAR_FULL0 + st], (n >> 1) & 1, 2)) break;
+      // s = fq fk^T of chunk m into TMEM, signalled on BAR_SFULL
+      auto issue_scores = [&](int m) -> bool {
+        const int st = m & 1;
+        if (!tc::mbar_wait(&bars[BAR_FULL0 + st], (m >> 1) & 1, 2)) return false;
         tc::tc_fence_after();
         const uint32_t stage = smem_u32(base + st * kStageBytes);
-        const uint32_t qa = stage + kOffQ, ka = stage + kOffK, va = stage + kOffV;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t ko = (j >> 2) * 16384 + (j & 3) * 32;
-          tc::mma_ss(tmem + kTSA, tc::sdesc(qa + ko, 16, 1024), tc::sdesc(ka + ko, 16, 1024),
-                     id_s, j > 0);
+          tc::mma_ss(tmem + kTSA, tc::sdesc(stage + kOffQ + ko, 16, 1024),
+                     tc::sdesc(stage + kOffK + ko, 16, 1024), id_s, j > 0);
         }
         tc::mma_commit(&bars[BAR_SFULL]);
-        if (!tc::mbar_wait(&bars[BAR_AREADY], n & 1, 3)) break;
-        if (n > 0 && !tc::mbar_wait(&bars[BAR_SREADY], (n - 1) & 1, 4)) break;
-        tc::tc_fence_after();
-        if (n > 0) {
+        return true;
+      };
+      if (issue_scores(0)) {
+        for (int n = 0; n < NT; ++n) {
+          const int st = n & 1;
+          const uint32_t stage = smem_u32(base + st * kStageBytes);
+          const uint32_t qa = stage + kOffQ, ka = stage + kOffK, va = stage + kOffV;
+          if (!tc::mbar_wait(&bars[BAR_AREADY], n & 1, 3)) break;
+          if (n > 0 && !tc::mbar_wait(&bars[BAR_SREADY], (n - 1) & 1, 4)) break;
+          tc::tc_fence_after();
+          // o = Q~ S_n + a V; row sums Q~ . z_n and a . 1
+          if (n > 0) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint32_t ko = (j >> 2) * 16384 + (j & 3) * 32;
-            tc::mma_ss(tmem + kTO, tc::sdesc(qa + ko, 16, 1024),
-                       tc::sdesc(s_addr + 2048 * j, 16384, 1024), id_o, j > 0);
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t ko = (j >> 2) * 16384 + (j & 3) * 32;
+              tc::mma_ss(tmem + kTO, tc::sdesc(qa + ko, 16, 1024),
+                         tc::sdesc(s_addr + 2048 * j, 16384, 1024), id_o, j > 0);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t ko = (j >> 2) * 16384 + (j & 3) * 32;
+              tc::mma_ss(tmem + kTDQ, tc::sdesc(qa + ko, 16, 1024),
+                         tc::sdesc(ones + (j >> 2) * 1024 + (j & 3) * 32, 16, 1024), id_n16,
+                         j > 0);
+            }
           }
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            tc::mma_ts(tmem + kTO, tmem + kTA + 8 * j, tc::sdesc(va + 2048 * j, 16384, 1024),
+                       id_o, (n > 0 || j > 0) ? 1u : 0u);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            tc::mma_ts(tmem + kTDI, tmem + kTA + 8 * j, tc::sdesc(ones + 32 * (j & 3), 16, 1024),
+                       id_n16, j > 0);
+          tc::mma_commit(&bars[BAR_OFULL]);
+          // next chunk's scores go ahead of this chunk's state update, so the
+          // decay warps can start on them while the state MMAs run
+          if (n + 1 < NT && !issue_scores(n + 1)) break;
+          // running state: the output warps pre-scaled S and z by this chunk's decay
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            tc::mma_ss(tmem + kTSF, tc::sdesc(ka + 2048 * j, 16384, 1024),
+                       tc::sdesc(va + 2048 * j, 16384, 1024), id_ds, (n > 0 || j > 0) ? 1u : 0u);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            tc::mma_ss(tmem + kTZ, tc::sdesc(ka + 2048 * j, 16384, 1024),
+                       tc::sdesc(ones + 32 * (j & 3), 16, 1024), id_dz,
+                       (n > 0 || j > 0) ? 1u : 0u);
+          tc::mma_commit(&bars[BAR_SFDONE]);
+          tc::mma_commit(&bars[BAR_EMPTY0 + st]);
         }
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          tc::mma_ts(tmem + kTO, tmem + kTA + 8 * j, tc::sdesc(va + 2048 * j, 16384, 1024), id_o,
-                     (n > 0 || j > 0) ? 1u : 0u);
-        // running state: the output warps pre-scaled S and z by this chunk's decay
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          tc::mma_ss(tmem + kTSF, tc::sdesc(ka + 2048 * j, 16384, 1024),
-                     tc::sdesc(va + 2048 * j, 16384, 1024), id_ds, (n > 0 || j > 0) ? 1u : 0u);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          tc::mma_ss(tmem + kTZ, tc::sdesc(ka + 2048 * j, 16384, 1024),
-                     tc::sdesc(ones + 32 * (j & 3), 16, 1024), id_dz, (n > 0 || j > 0) ? 1u : 0u);
-        tc::mma_commit(&bars[BAR_OFULL]);
-        tc::mma_commit(&bars[BAR_EMPTY0 + st]);
       }
     }
   } else if (warp < 6) {
@@ -244,8 +279,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       // a = bf16(s 2^(g2_r - g2_t)) for t <= r. Blocks left of the diagonal use
       // 2^(g2_r - g2_ref) 2^(g2_ref - g2_t) with ref the block's last row (both
       // factors <= 1); the diagonal block takes one ex2 per element; blocks to
-      // its right are zero.
-      float den = 0.f;
+      // its right are zero. The row sums come from the MMA (a . 1).
 #pragma unroll 1
       for (int cb = 0; cb < 4; ++cb) {
         uint32_t pk[16];
@@ -262,7 +296,6 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
             const uint32_t p1 = pack_bf16(s[4 * j4 + 2] * f.z * ar, s[4 * j4 + 3] * f.w * ar);
             pk[2 * j4] = p0;
             pk[2 * j4 + 1] = p1;
-            den += (bf16_lo(p0) + bf16_hi(p0)) + (bf16_lo(p1) + bf16_hi(p1));
           }
         } else if (cb == quad) {
           float s[32];
@@ -284,7 +317,6 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
             const uint32_t p0 = pack_bf16(w0, w1), p1 = pack_bf16(w2, w3);
             pk[2 * j4] = p0;
             pk[2 * j4 + 1] = p1;
-            den += (bf16_lo(p0) + bf16_hi(p0)) + (bf16_lo(p1) + bf16_hi(p1));
           }
         } else {
 #pragma unroll
@@ -292,72 +324,79 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         }
         tc::tmem_st16(trow + kTA + 16 * cb, pk);
       }
-      tc::tmem_st1(trow + kTDEN + (n & 1), __float_as_uint(den));
-      // K~ = fk 2^(end - g2) in place (row r of both 64-column blocks)
+      // K~ = fk 2^(end - g2) in place. The causal mask gives the warp of rows
+      // 32q..32q+31 q+1 score blocks, so the K~ rows go to the lighter warps:
+      // quad 0 scales rows 0..63, quad 1 rows 64..95, quad 2 rows 96..127.
       {
         unsigned char* stage = base + (n & 1) * kStageBytes;
-        const float ks = valid ? tc::ex2(end2 - g2) : 0.f;
-        uint4 w[16];
+        const int npass = quad == 0 ? 2 : (quad == 3 ? 0 : 1);
+        const int row0 = quad == 0 ? 0 : 32 + 32 * quad;
+#pragma unroll 1
+        for (int ps = 0; ps < npass; ++ps) {
+          const int t = row0 + 32 * ps + lane;
+          const float ks = t < nvalid ? tc::ex2(end2 - sG[t]) : 0.f;
+          uint4 w[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          w[i] = *reinterpret_cast<const uint4*>(stage + kOffK + (i >> 3) * 16384 + r * 128 +
-                                                 (((i & 7) ^ (r & 7)) * 16));
+          for (int i = 0; i < 16; ++i)
+            w[i] = *reinterpret_cast<const uint4*>(stage + kOffK + (i >> 3) * 16384 + t * 128 +
+                                                   (((i & 7) ^ (t & 7)) * 16));
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          *reinterpret_cast<uint4*>(stage + kOffK + (i >> 3) * 16384 + r * 128 +
-                                    (((i & 7) ^ (r & 7)) * 16)) = scale8(w[i], ks);
+          for (int i = 0; i < 16; ++i)
+            *reinterpret_cast<uint4*>(stage + kOffK + (i >> 3) * 16384 + t * 128 +
+                                      (((i & 7) ^ (t & 7)) * 16)) = scale8(w[i], ks);
+        }
       }
       tc::fence_proxy_async_smem();
       tc::tmem_wait_st();
       tc::tc_fence_before();
       tc::mbar_arrive(&bars[BAR_AREADY]);
-      tc::mbar_arrive(&bars[BAR_DEN0 + (n & 1)]);
     }
   } else {
-    // ---------- output warps: y; S, z for the next chunk; Q~ in place, Q~ . z
+    // ------------- output warps: y; S, z for the next chunk; Q~ in place
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // chunk row for o; state row f for S, z
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
     unsigned char* srow_base = base + kOffS + r * 128;
-    float den_inter = 0.f;  // Q~_r . z_n of the chunk about to be output
+    // z_hi / z_lo of state row r: row 1 / row 2 of operand block r / 64, column
+    // r % 64, in the 128-byte swizzled layout
+    unsigned char* zblk = misc + (r >> 6) * 1024;
+    const int zcol = ((((r & 63) >> 3) ^ 1) << 4) + (r & 7) * 2;
+    const int zcol2 = ((((r & 63) >> 3) ^ 2) << 4) + (r & 7) * 2;
     for (int n = 0; n < NT; ++n) {
       const int r0 = n * kC;
       const int nvalid = min(kC, L - r0);
       const bool valid = r < nvalid;
       if (!__all_sync(0xffffffffu, tc::mbar_wait(&bars[BAR_OFULL], n & 1, 6))) break;
-      if (!__all_sync(0xffffffffu,
-                      tc::mbar_wait(&bars[BAR_DEN0 + (n & 1)], (n >> 1) & 1, 8)))
-        break;
       tc::tc_fence_after();
-      // y = o / max(den, FLT_MIN)
-      const float den = tc::tmem_ld1(trow + kTDEN + (n & 1));
+      // y = o / max(den, FLT_MIN), den = a . 1 + Q~ . z_hi + Q~ . z_lo
+      float dv[32];
+      tc::tmem_ld32(trow + kTDI, dv);
       tc::tmem_wait_ld();
-      const float dtot = den + den_inter;
+      const float dtot = dv[0] + (n > 0 ? dv[17] + dv[18] : 0.f);
       const float inv = 1.f / fmaxf(dtot, kTiny);
       const size_t row = (size_t)bh * L + r0 + r;
       // y rows go to the stage's fq block (free now: every MMA of this chunk is
       // done) in the 128-byte swizzled box layout, then out with one TMA store
       unsigned char* ystage = base + (n & 1) * kStageBytes + kOffQ;
 #pragma unroll 1
-      for (int cb = 0; cb < 4; ++cb) {
-        float o[32];
-        tc::tmem_ld32(trow + kTO + 32 * cb, o);
+      for (int hb = 0; hb < 2; ++hb) {
+        float o[64];
+        tc::tmem_ld64(trow + kTO + 64 * hb, o);
         tc::tmem_wait_ld();
-        unsigned char* yrow = ystage + (cb >> 1) * 16384 + r * 128;
+        unsigned char* yrow = ystage + hb * 16384 + r * 128;
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
+        for (int c = 0; c < 8; ++c) {
           uint4 w;
-          w.x = pack_bf16(o[8 * q4 + 0] * inv, o[8 * q4 + 1] * inv);
-          w.y = pack_bf16(o[8 * q4 + 2] * inv, o[8 * q4 + 3] * inv);
-          w.z = pack_bf16(o[8 * q4 + 4] * inv, o[8 * q4 + 5] * inv);
-          w.w = pack_bf16(o[8 * q4 + 6] * inv, o[8 * q4 + 7] * inv);
-          const int c = (cb & 1) * 4 + q4;
+          w.x = pack_bf16(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
+          w.y = pack_bf16(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+          w.z = pack_bf16(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+          w.w = pack_bf16(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
           *reinterpret_cast<uint4*>(yrow + ((c ^ (r & 7)) * 16)) = w;
         }
         if (save && valid) {
-          float4* d32 = reinterpret_cast<float4*>(y32 + row * 128 + 32 * cb);
+          float4* d32 = reinterpret_cast<float4*>(y32 + row * 128 + 64 * hb);
 #pragma unroll
-          for (int q4 = 0; q4 < 8; ++q4)
+          for (int q4 = 0; q4 < 16; ++q4)
             d32[q4] = make_float4(o[4 * q4] * inv, o[4 * q4 + 1] * inv, o[4 * q4 + 2] * inv,
                                   o[4 * q4 + 3] * inv);
         }
@@ -368,33 +407,35 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         tc::tma_store_3d(&ty, ystage, 0, r0, bh);
         tc::tma_store_3d(&ty, ystage + 16384, 64, r0, bh);
         tc::bulk_commit();
-        tc::bulk_wait_read0();
-        tc::mbar_arrive(&bars[BAR_EMPTY0 + (n & 1)]);
       }
-      __syncwarp();
       if (save && valid) den_out[row] = dtot;
       if (n + 1 < NT) {
         // prepare chunk n+1: bf16 S_{n+1}; S and z pre-scaled by its decay;
         // Q~_{n+1} in place and its row sums against z_{n+1}
         if (!__all_sync(0xffffffffu, tc::mbar_wait(&bars[BAR_GATE], (n + 1) & 1, 10))) break;
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&bars[BAR_SFDONE], n & 1, 11))) break;
+        tc::tc_fence_after();
         const float start2 = sGS[((n + 1) & 1) * 2], end2 = sGS[((n + 1) & 1) * 2 + 1];
         const float decay = tc::ex2(end2 - start2);
         const float g2r = sG[r];
         const float zn = tc::tmem_ld1(trow + kTZ);
         tc::tmem_wait_ld();
-        float* zbuf = sZ + ((n + 1) & 1) * 128;
-        zbuf[r] = zn;
+        {
+          const bf16 zh = __float2bfloat16_rn(zn);
+          *reinterpret_cast<bf16*>(zblk + 128 + zcol) = zh;
+          *reinterpret_cast<bf16*>(zblk + 256 + zcol2) =
+              __float2bfloat16_rn(zn - __bfloat162float(zh));
+        }
         tc::tmem_st1(trow + kTZ, __float_as_uint(zn * decay));
 #pragma unroll 1
-        for (int cb = 0; cb < 4; ++cb) {
-          float sv[32];
-          tc::tmem_ld32(trow + kTSF + 32 * cb, sv);
+        for (int hb = 0; hb < 2; ++hb) {
+          float sv[64];
+          tc::tmem_ld64(trow + kTSF + 64 * hb, sv);
           tc::tmem_wait_ld();
-          unsigned char* srow = srow_base + (cb >> 1) * 16384;
+          unsigned char* srow = srow_base + hb * 16384;
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            const int c = (cb & 1) * 4 + cc;
-            const float* v8 = &sv[8 * cc];
+          for (int c = 0; c < 8; ++c) {
+            const float* v8 = &sv[8 * c];
             uint4 w;
             w.x = pack_bf16(v8[0], v8[1]);
             w.y = pack_bf16(v8[2], v8[3]);
@@ -402,16 +443,14 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
             w.w = pack_bf16(v8[6], v8[7]);
             *reinterpret_cast<uint4*>(srow + ((c ^ (r & 7)) * 16)) = w;
           }
-          uint32_t lo[16], hi[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            lo[j] = __float_as_uint(sv[j] * decay);
-            hi[j] = __float_as_uint(sv[16 + j] * decay);
+          for (int q = 0; q < 4; ++q) {
+            uint32_t sc[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) sc[j] = __float_as_uint(sv[16 * q + j] * decay);
+            tc::tmem_st16(trow + kTSF + 64 * hb + 16 * q, sc);
           }
-          tc::tmem_st16(trow + kTSF + 32 * cb, lo);
-          tc::tmem_st16(trow + kTSF + 32 * cb + 16, hi);
         }
-        tc::named_bar_sync(2, 128);  // all of z_{n+1} is in zbuf
         {
           const bool nvld = r < min(kC, L - r0 - kC);
           const float qs = nvld ? tc::ex2(g2r - start2) : 0.f;
@@ -421,25 +460,21 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
           for (int i = 0; i < 16; ++i)
             w[i] = *reinterpret_cast<const uint4*>(stage + kOffQ + (i >> 3) * 16384 + r * 128 +
                                                    (((i & 7) ^ (r & 7)) * 16));
-          float dz = 0.f;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const uint4 q = scale8(w[i], qs);
+          for (int i = 0; i < 16; ++i)
             *reinterpret_cast<uint4*>(stage + kOffQ + (i >> 3) * 16384 + r * 128 +
-                                      (((i & 7) ^ (r & 7)) * 16)) = q;
-            const float4 z0 = *reinterpret_cast<const float4*>(zbuf + (i >> 3) * 64 + (i & 7) * 8);
-            const float4 z1 = *reinterpret_cast<const float4*>(zbuf + (i >> 3) * 64 + (i & 7) * 8 + 4);
-            dz += bf16_lo(q.x) * z0.x + bf16_hi(q.x) * z0.y + bf16_lo(q.y) * z0.z +
-                  bf16_hi(q.y) * z0.w + bf16_lo(q.z) * z1.x + bf16_hi(q.z) * z1.y +
-                  bf16_lo(q.w) * z1.z + bf16_hi(q.w) * z1.w;
-          }
-          den_inter = dz;
+                                      (((i & 7) ^ (r & 7)) * 16)) = scale8(w[i], qs);
         }
       }
       tc::fence_proxy_async_smem();
       tc::tmem_wait_st();
       tc::tc_fence_before();
       tc::mbar_arrive(&bars[BAR_SREADY]);
+      if (r == 0) {  // the y staging block is read: hand the stage back to TMA
+        tc::bulk_wait_read0();
+        tc::mbar_arrive(&bars[BAR_EMPTY0 + (n & 1)]);
+      }
+      __syncwarp();
     }
     if (r == 0) tc::bulk_wait0();  // output stores complete before the CTA exits
   }
