@@ -20,6 +20,8 @@
  *   log_gamma  fp32 [B, L] when gate_per_head == 0 (one gate shared by the H
  *              heads of a batch row), fp32 [BH, L] when gate_per_head == 1
  *   q, k       bf16 [BH, L, D]      already-rotated queries / keys for SWA
+ *   q_lo, k_lo bf16 [BH, L, D]      optional residuals: q = q + q_lo, k = k + k_lo
+ *              (pass null for both when the caller's data is bf16)
  *   meta       fp32 [n_meta]        sink logits (n_meta may be 0)
  */
 #ifndef LIZARD_CUDA_H_
@@ -104,24 +106,29 @@ int lz_gla_bwd(const void* fq, const void* fk, const void* v,
 /* Bytes of the opaque buffer lz_swa_fwd fills (log-sum-exp per row). */
 size_t lz_swa_saved_bytes(int B, int H, int L, int D);
 
-/* Bytes of scratch lz_swa_bwd needs (delta per row, sink-grad partials). */
+/* Bytes of scratch lz_swa_bwd needs (delta per row, per-block sink partials). */
 size_t lz_swa_bwd_workspace_bytes(int B, int H, int L, int D, int n_meta);
 
 /* Forward of swa(q, k, v, meta, window). Replaces _SWA.forward
  * (src/kernels/swa.py:136-156): y = softmax over [i-window+1, i] with the
  * sink logits in the denominator, scale 1/sqrt(D). y is bf16. saved may be
- * null when no backward follows. */
+ * null when no backward follows. With q_lo and k_lo the logits are
+ * q.k + q.k_lo + q_lo.k (about 16 mantissa bits), for fp32 callers. */
 int lz_swa_fwd(const void* q, const void* k, const void* v,
+               const void* q_lo, const void* k_lo,
                const float* meta, int n_meta, int window,
                void* y, void* saved, size_t saved_bytes,
                int B, int H, int L, int D, void* stream);
 
 /* Backward of swa(). Replaces _SWA.backward (src/kernels/swa.py:158-179)
  * including the torch-side delta and dmeta: writes dq, dk, dv [BH,L,D] in
- * grad_dtype and dmeta (fp32 [n_meta]). */
+ * grad_dtype and dmeta (fp32 [n_meta]). delta_i = sum_t P_it (dy_i . v_t) is
+ * formed in fp32 inside the kernels, so y is not needed. q_lo / k_lo as in
+ * the forward (both null or both set, the same as the forward call). */
 int lz_swa_bwd(const void* q, const void* k, const void* v,
+               const void* q_lo, const void* k_lo,
                const float* meta, int n_meta, int window,
-               const void* y, const void* saved, size_t saved_bytes,
+               const void* saved, size_t saved_bytes,
                const void* dy, void* dq, void* dk, void* dv, int grad_dtype,
                float* dmeta, void* workspace, size_t workspace_bytes,
                int B, int H, int L, int D, void* stream);

@@ -105,13 +105,16 @@ extern "C" size_t lz_swa_bwd_workspace_bytes(int B, int H, int L, int D, int n_m
   return lz::swa_work_layout(B, H, L, n_meta, nullptr, nullptr);
 }
 
-extern "C" int lz_swa_fwd(const void* q, const void* k, const void* v, const float* meta,
-                          int n_meta, int window, void* y, void* saved, size_t saved_bytes,
-                          int B, int H, int L, int D, void* stream) {
+extern "C" int lz_swa_fwd(const void* q, const void* k, const void* v, const void* q_lo,
+                          const void* k_lo, const float* meta, int n_meta, int window, void* y,
+                          void* saved, size_t saved_bytes, int B, int H, int L, int D,
+                          void* stream) {
   lz::clear_error();
   int rc = check_sizes(B, H, L, 1, D);
   if (rc) return rc;
   LZ_REQUIRE(q && k && v && y, LZ_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  LZ_REQUIRE((q_lo == nullptr) == (k_lo == nullptr), LZ_ERR_INVALID_ARGUMENT,
+             "q_lo and k_lo must be both null or both set");
   LZ_REQUIRE(n_meta >= 0 && (n_meta == 0 || meta), LZ_ERR_INVALID_ARGUMENT,
              "meta must be non-null when n_meta > 0");
   LZ_REQUIRE(n_meta <= lz::kMaxMeta, LZ_ERR_UNSUPPORTED, "more than 32 sink logits");
@@ -124,20 +127,23 @@ extern "C" int lz_swa_fwd(const void* q, const void* k, const void* v, const flo
     lse = static_cast<float*>(saved);
   }
   return lz::swa_fwd(static_cast<const bf16*>(q), static_cast<const bf16*>(k),
-                     static_cast<const bf16*>(v), meta, n_meta, window, static_cast<bf16*>(y),
-                     lse, B, H, L, D, static_cast<cudaStream_t>(stream));
+                     static_cast<const bf16*>(v), static_cast<const bf16*>(q_lo),
+                     static_cast<const bf16*>(k_lo), meta, n_meta, window,
+                     static_cast<bf16*>(y), lse, B, H, L, D, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int lz_swa_bwd(const void* q, const void* k, const void* v, const float* meta,
-                          int n_meta, int window, const void* y, const void* saved,
-                          size_t saved_bytes, const void* dy, void* dq, void* dk, void* dv,
-                          int grad_dtype, float* dmeta, void* workspace, size_t workspace_bytes,
-                          int B, int H, int L, int D, void* stream) {
+extern "C" int lz_swa_bwd(const void* q, const void* k, const void* v, const void* q_lo,
+                          const void* k_lo, const float* meta, int n_meta, int window,
+                          const void* saved, size_t saved_bytes, const void* dy, void* dq,
+                          void* dk, void* dv, int grad_dtype, float* dmeta, void* workspace,
+                          size_t workspace_bytes, int B, int H, int L, int D, void* stream) {
   lz::clear_error();
   int rc = check_sizes(B, H, L, 1, D);
   if (rc) return rc;
-  LZ_REQUIRE(q && k && v && y && saved && dy && dq && dk && dv && workspace,
+  LZ_REQUIRE(q && k && v && saved && dy && dq && dk && dv && workspace,
              LZ_ERR_INVALID_ARGUMENT, "null pointer");
+  LZ_REQUIRE((q_lo == nullptr) == (k_lo == nullptr), LZ_ERR_INVALID_ARGUMENT,
+             "q_lo and k_lo must be both null or both set");
   LZ_REQUIRE(n_meta >= 0 && (n_meta == 0 || (meta && dmeta)), LZ_ERR_INVALID_ARGUMENT,
              "meta and dmeta must be non-null when n_meta > 0");
   LZ_REQUIRE(n_meta <= lz::kMaxMeta, LZ_ERR_UNSUPPORTED, "more than 32 sink logits");
@@ -152,8 +158,8 @@ extern "C" int lz_swa_bwd(const void* q, const void* k, const void* v, const flo
   lz::SwaWork wk;
   lz::swa_work_layout(B, H, L, n_meta, static_cast<unsigned char*>(workspace), &wk);
   return lz::swa_bwd(static_cast<const bf16*>(q), static_cast<const bf16*>(k),
-                     static_cast<const bf16*>(v), meta, n_meta, window,
-                     static_cast<const bf16*>(y), static_cast<const float*>(saved),
-                     static_cast<const bf16*>(dy), dq, dk, dv, grad_dtype, dmeta, wk, B, H, L,
-                     D, static_cast<cudaStream_t>(stream));
+                     static_cast<const bf16*>(v), static_cast<const bf16*>(q_lo),
+                     static_cast<const bf16*>(k_lo), meta, n_meta, window,
+                     static_cast<const float*>(saved), static_cast<const bf16*>(dy), dq, dk, dv,
+                     grad_dtype, dmeta, wk, B, H, L, D, static_cast<cudaStream_t>(stream));
 }

@@ -5,9 +5,18 @@
 //
 // Forward: flash-style online softmax whose running max / sum start from the
 // sinks (src/kernels/swa.py:34-38), so the sinks add to the denominator only.
-// Backward: delta_i = dy_i . y_i (bf16 y, swa.py:164), dq per query block,
-// dk/dv per key block, dmeta_j = -sum_i exp(meta_j - lse_i) delta_i
-// (swa.py:175-176) reduced in a fixed order.
+// Backward (src/kernels/swa.py:62-133, 158-179), three launches:
+//   dq kernel  : per query block, pass 1 forms delta_i = sum_t P_it (dy_i . v_t)
+//                in fp32 (the reference uses dy . bf16(y), swa.py:164, which
+//                loses the small 1 - P differences); pass 2 accumulates dq.
+//                It also writes delta and per-block sink-gradient partials.
+//   dkv kernel : per key block, dk and dv over the query blocks in its window.
+//   dmeta      : dmeta_j = -sum_i exp(meta_j - lse_i) delta_i (swa.py:175-176),
+//                reduced over the per-block partials in a fixed order.
+// Optional bf16 residuals q_lo, k_lo (q = q_hi + q_lo) make the logits
+// q_hi.k_hi + q_hi.k_lo + q_lo.k_hi, about 16 mantissa bits, for callers whose
+// queries and keys are fp32: softmax turns logit rounding into relative
+// weight errors, which the sink gradient accumulates.
 #include <mutex>
 
 #include "common.cuh"
@@ -41,17 +50,66 @@ __device__ __forceinline__ bool in_window(int i, int t, int L, int W) {
   return t <= i && i - t < W && i < L;
 }
 
-// ---------------------------------------------------------------- forward
 template <int DP>
+struct Tile {
+  static constexpr int LD = DP + 8;
+  static constexpr size_t bytes = (size_t)kB * LD * 2;
+};
+
+// Scores of this warp's 16 query rows against the 64 rows of tK (keys):
+// s = qa . k_hi (+ qa . k_lo + qla . k_hi).
+template <int DP, bool SPLIT>
+__device__ __forceinline__ void scores(float (&s)[8][4], const uint32_t (&qa)[DP / 16][4],
+                                       const uint32_t (&qla)[DP / 16][4], const bf16* tK,
+                                       const bf16* tKl) {
+  constexpr int LD = Tile<DP>::LD;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[c][e] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < DP / 16; ++kk) {
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t bk[4];
+      ldb_nk(bk, tK, LD, 16 * np, 16 * kk);
+      mma16816(s[2 * np], qa[kk], bk[0], bk[1]);
+      mma16816(s[2 * np + 1], qa[kk], bk[2], bk[3]);
+      if constexpr (SPLIT) {
+        uint32_t bl[4];
+        ldb_nk(bl, tKl, LD, 16 * np, 16 * kk);
+        mma16816(s[2 * np], qa[kk], bl[0], bl[1]);
+        mma16816(s[2 * np + 1], qa[kk], bl[2], bl[3]);
+        mma16816(s[2 * np], qla[kk], bk[0], bk[1]);
+        mma16816(s[2 * np + 1], qla[kk], bk[2], bk[3]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- forward
+template <int DP, bool SPLIT>
+struct FwdSmem {
+  static constexpr size_t T = Tile<DP>::bytes;
+  static constexpr size_t q = 0, ql = q + T, k = ql + (SPLIT ? T : 0), kl = k + 2 * T,
+                          v = kl + (SPLIT ? 2 * T : 0), bytes = v + 2 * T;
+};
+
+template <int DP, bool SPLIT>
 __global__ void __launch_bounds__(128)
 swa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
+               const bf16* __restrict__ ql, const bf16* __restrict__ kl,
                const float* __restrict__ meta, int n_meta, int W, float scale_log2, int L, int D,
                int nqb, int vec, bf16* __restrict__ y, float* __restrict__ lse) {
-  constexpr int LD = DP + 8, NTD = DP / 8;
+  using SM = FwdSmem<DP, SPLIT>;
+  constexpr int LD = Tile<DP>::LD, NTD = DP / 8;
+  constexpr size_t T = Tile<DP>::bytes;
   extern __shared__ __align__(128) unsigned char smem[];
-  bf16* sQ = reinterpret_cast<bf16*>(smem);
-  bf16* sK = sQ + kB * LD;  // 2 stages
-  bf16* sV = sK + 2 * kB * LD;
+  bf16* sQ = reinterpret_cast<bf16*>(smem + SM::q);
+  bf16* sQl = reinterpret_cast<bf16*>(smem + SM::ql);
+  auto sK = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::k + s * T); };
+  auto sKl = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::kl + s * T); };
+  auto sV = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::v + s * T); };
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, cq = lane & 3;
   const int qb = blockIdx.x % nqb, bh = blockIdx.x / nqb;
@@ -66,9 +124,14 @@ swa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
 
   const int lo = max(q0 - W + 1, 0) / kB * kB;
   const int hi = min(q0 + kB, L);
+  auto issue = [&](int kb, int s) {
+    stage_tile<kB, DP, 128>(sK(s), LD, k + base, D, kb, L, 0, D, vec);
+    if (SPLIT) stage_tile<kB, DP, 128>(sKl(s), LD, kl + base, D, kb, L, 0, D, vec);
+    stage_tile<kB, DP, 128>(sV(s), LD, v + base, D, kb, L, 0, D, vec);
+  };
   stage_tile<kB, DP, 128>(sQ, LD, q + base, D, q0, L, 0, D, vec);
-  stage_tile<kB, DP, 128>(sK, LD, k + base, D, lo, L, 0, D, vec);
-  stage_tile<kB, DP, 128>(sV, LD, v + base, D, lo, L, 0, D, vec);
+  if (SPLIT) stage_tile<kB, DP, 128>(sQl, LD, ql + base, D, q0, L, 0, D, vec);
+  issue(lo, 0);
   cp_async_commit();
 
   const int i0 = q0 + 16 * warp + gq, i1 = i0 + 8;
@@ -78,13 +141,12 @@ swa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   for (int c = 0; c < NTD; ++c)
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[c][e] = 0.f;
-  uint32_t qa[DP / 16][4];
+  uint32_t qa[DP / 16][4], qla[DP / 16][4];
 
   int stage = 0;
   for (int kb = lo; kb < hi; kb += kB, stage ^= 1) {
     if (kb + kB < hi) {
-      stage_tile<kB, DP, 128>(sK + (stage ^ 1) * kB * LD, LD, k + base, D, kb + kB, L, 0, D, vec);
-      stage_tile<kB, DP, 128>(sV + (stage ^ 1) * kB * LD, LD, v + base, D, kb + kB, L, 0, D, vec);
+      issue(kb + kB, stage ^ 1);
       cp_async_commit();
       asm volatile("cp.async.wait_group 1;\n" ::);
     } else {
@@ -93,25 +155,13 @@ swa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     __syncthreads();
     if (kb == lo) {
 #pragma unroll
-      for (int kk = 0; kk < DP / 16; ++kk) lda_rm(qa[kk], sQ, LD, 16 * warp, 16 * kk);
-    }
-    const bf16* tK = sK + stage * kB * LD;
-    const bf16* tV = sV + stage * kB * LD;
-    float s[8][4];
-#pragma unroll
-    for (int c = 0; c < 8; ++c)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) s[c][e] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < DP / 16; ++kk) {
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        uint32_t bb[4];
-        ldb_nk(bb, tK, LD, 16 * np, 16 * kk);
-        mma16816(s[2 * np], qa[kk], bb[0], bb[1]);
-        mma16816(s[2 * np + 1], qa[kk], bb[2], bb[3]);
+      for (int kk = 0; kk < DP / 16; ++kk) {
+        lda_rm(qa[kk], sQ, LD, 16 * warp, 16 * kk);
+        if (SPLIT) lda_rm(qla[kk], sQl, LD, 16 * warp, 16 * kk);
       }
     }
+    float s[8][4];
+    scores<DP, SPLIT>(s, qa, qla, sK(stage), sKl(stage));
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
@@ -154,6 +204,7 @@ swa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       o[c][2] *= al1;
       o[c][3] *= al1;
     }
+    const bf16* tV = sV(stage);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
 #pragma unroll
@@ -185,68 +236,34 @@ swa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   }
 }
 
-// ------------------------------------------------------- backward: prep
-// delta_i = dy_i . y_i; per-block partials of sum_i exp(meta_j - lse_i) delta_i.
-constexpr int kPrepRows = 64;
-__global__ void __launch_bounds__(256)
-swa_bwd_prep_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ y,
-                    const float* __restrict__ lse, const float* __restrict__ meta, int n_meta,
-                    long long rows, int D, float* __restrict__ delta,
-                    float* __restrict__ partial) {
-  __shared__ float wpart[8][kMaxMeta];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float acc[kMaxMeta];
-#pragma unroll
-  for (int j = 0; j < kMaxMeta; ++j) acc[j] = 0.f;
-  for (int r = warp; r < kPrepRows; r += 8) {
-    const long long row = (long long)blockIdx.x * kPrepRows + r;
-    if (row >= rows) break;
-    float x = 0.f;
-    for (int d = lane; d < D; d += 32)
-      x += __bfloat162float(dy[row * D + d]) * __bfloat162float(y[row * D + d]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-    if (lane == 0) {
-      delta[row] = x;
-      const float l = lse[row];
-#pragma unroll
-      for (int j = 0; j < kMaxMeta; ++j)
-        if (j < n_meta) acc[j] += __expf(meta[j] - l) * x;
-    }
-  }
-  if (lane == 0)
-#pragma unroll
-    for (int j = 0; j < kMaxMeta; ++j) wpart[warp][j] = acc[j];
-  __syncthreads();
-  if (threadIdx.x < n_meta) {
-    float s = 0.f;
-    for (int w = 0; w < 8; ++w) s += wpart[w][threadIdx.x];
-    partial[(size_t)blockIdx.x * n_meta + threadIdx.x] = s;
-  }
-}
-
-__global__ void swa_dmeta_kernel(const float* __restrict__ partial, int nblocks, int n_meta,
-                                 float* __restrict__ dmeta) {
-  const int j = threadIdx.x;
-  if (j >= n_meta) return;
-  float s = 0.f;
-  for (int b = 0; b < nblocks; ++b) s += partial[(size_t)b * n_meta + j];
-  dmeta[j] = -s;
-}
-
 // ------------------------------------------------------- backward: dq
-template <int DP>
+template <int DP, bool SPLIT>
+struct DqSmem {
+  static constexpr size_t T = Tile<DP>::bytes;
+  static constexpr size_t q = 0, ql = q + T, dy = ql + (SPLIT ? T : 0), k = dy + T,
+                          kl = k + 2 * T, v = kl + (SPLIT ? 2 * T : 0), red = v + 2 * T,
+                          bytes = red + 4 * kMaxMeta * 4;
+};
+
+template <int DP, bool SPLIT>
 __global__ void __launch_bounds__(128)
 swa_bwd_dq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
-                  const bf16* __restrict__ v, const bf16* __restrict__ dy,
-                  const float* __restrict__ lse, const float* __restrict__ delta, int W,
-                  float scale, int L, int D, int nqb, int vec, void* __restrict__ dq, int gdt) {
-  constexpr int LD = DP + 8, NTD = DP / 8;
+                  const bf16* __restrict__ v, const bf16* __restrict__ ql,
+                  const bf16* __restrict__ kl, const bf16* __restrict__ dy,
+                  const float* __restrict__ meta, int n_meta, const float* __restrict__ lse,
+                  int W, float scale, int L, int D, int nqb, int vec, void* __restrict__ dq,
+                  int gdt, float* __restrict__ delta_out, float* __restrict__ partial) {
+  using SM = DqSmem<DP, SPLIT>;
+  constexpr int LD = Tile<DP>::LD, NTD = DP / 8;
+  constexpr size_t T = Tile<DP>::bytes;
   extern __shared__ __align__(128) unsigned char smem[];
-  bf16* sQ = reinterpret_cast<bf16*>(smem);
-  bf16* sDy = sQ + kB * LD;
-  bf16* sK = sDy + kB * LD;  // 2 stages
-  bf16* sV = sK + 2 * kB * LD;
+  bf16* sQ = reinterpret_cast<bf16*>(smem + SM::q);
+  bf16* sQl = reinterpret_cast<bf16*>(smem + SM::ql);
+  bf16* sDy = reinterpret_cast<bf16*>(smem + SM::dy);
+  float* sRed = reinterpret_cast<float*>(smem + SM::red);
+  auto sK = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::k + s * T); };
+  auto sKl = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::kl + s * T); };
+  auto sV = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::v + s * T); };
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, cq = lane & 3;
   const int qb = blockIdx.x % nqb, bh = blockIdx.x / nqb;
@@ -254,77 +271,110 @@ swa_bwd_dq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
   const size_t base = (size_t)bh * L * D;
   const int lo = max(q0 - W + 1, 0) / kB * kB;
   const int hi = min(q0 + kB, L);
+  const int nkb = (hi - lo + kB - 1) / kB;
+  auto issue = [&](int step, int s) {
+    const int kb = lo + (step % nkb) * kB;
+    stage_tile<kB, DP, 128>(sK(s), LD, k + base, D, kb, L, 0, D, vec);
+    if (SPLIT) stage_tile<kB, DP, 128>(sKl(s), LD, kl + base, D, kb, L, 0, D, vec);
+    stage_tile<kB, DP, 128>(sV(s), LD, v + base, D, kb, L, 0, D, vec);
+  };
   stage_tile<kB, DP, 128>(sQ, LD, q + base, D, q0, L, 0, D, vec);
+  if (SPLIT) stage_tile<kB, DP, 128>(sQl, LD, ql + base, D, q0, L, 0, D, vec);
   stage_tile<kB, DP, 128>(sDy, LD, dy + base, D, q0, L, 0, D, vec);
-  stage_tile<kB, DP, 128>(sK, LD, k + base, D, lo, L, 0, D, vec);
-  stage_tile<kB, DP, 128>(sV, LD, v + base, D, lo, L, 0, D, vec);
+  issue(0, 0);
   cp_async_commit();
   const int i0 = q0 + 16 * warp + gq, i1 = i0 + 8;
   const float lse0 = i0 < L ? lse[(size_t)bh * L + i0] : 0.f;
   const float lse1 = i1 < L ? lse[(size_t)bh * L + i1] : 0.f;
-  const float dl0 = i0 < L ? delta[(size_t)bh * L + i0] : 0.f;
-  const float dl1 = i1 < L ? delta[(size_t)bh * L + i1] : 0.f;
   float acc[NTD][4];
 #pragma unroll
   for (int c = 0; c < NTD; ++c)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[c][e] = 0.f;
+  uint32_t qa[DP / 16][4], qla[DP / 16][4], ga[DP / 16][4];
+  float ds0 = 0.f, ds1 = 0.f;  // pass 1: row sums of P (dy . v)
+  float dl0 = 0.f, dl1 = 0.f;  // delta after pass 1
+
+  // steps 0 .. nkb-1: pass 1 (delta); nkb .. 2 nkb-1: pass 2 (dq)
   int stage = 0;
-  for (int kb = lo; kb < hi; kb += kB, stage ^= 1) {
-    if (kb + kB < hi) {
-      stage_tile<kB, DP, 128>(sK + (stage ^ 1) * kB * LD, LD, k + base, D, kb + kB, L, 0, D, vec);
-      stage_tile<kB, DP, 128>(sV + (stage ^ 1) * kB * LD, LD, v + base, D, kb + kB, L, 0, D, vec);
+  for (int step = 0; step < 2 * nkb; ++step, stage ^= 1) {
+    if (step + 1 < 2 * nkb) {
+      issue(step + 1, stage ^ 1);
       cp_async_commit();
       asm volatile("cp.async.wait_group 1;\n" ::);
     } else {
       cp_async_wait_all();
     }
     __syncthreads();
-    const bf16* tK = sK + stage * kB * LD;
-    const bf16* tV = sV + stage * kB * LD;
+    if (step == 0) {
+#pragma unroll
+      for (int kk = 0; kk < DP / 16; ++kk) {
+        lda_rm(qa[kk], sQ, LD, 16 * warp, 16 * kk);
+        if (SPLIT) lda_rm(qla[kk], sQl, LD, 16 * warp, 16 * kk);
+        lda_rm(ga[kk], sDy, LD, 16 * warp, 16 * kk);
+      }
+    }
+    const bool pass2 = step >= nkb;
+    const int kb = lo + (step % nkb) * kB;
+    const bf16* tK = sK(stage);
+    const bf16* tV = sV(stage);
     float s[8][4], dp[8][4];
+    scores<DP, SPLIT>(s, qa, qla, tK, sKl(stage));
 #pragma unroll
     for (int c = 0; c < 8; ++c)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) s[c][e] = dp[c][e] = 0.f;
+      for (int e = 0; e < 4; ++e) dp[c][e] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < DP / 16; ++kk) {
-      uint32_t a[4], g[4];
-      lda_rm(a, sQ, LD, 16 * warp, 16 * kk);
-      lda_rm(g, sDy, LD, 16 * warp, 16 * kk);
 #pragma unroll
       for (int np = 0; np < 4; ++np) {
-        uint32_t bk[4], bv[4];
-        ldb_nk(bk, tK, LD, 16 * np, 16 * kk);
+        uint32_t bv[4];
         ldb_nk(bv, tV, LD, 16 * np, 16 * kk);
-        mma16816(s[2 * np], a, bk[0], bk[1]);
-        mma16816(s[2 * np + 1], a, bk[2], bk[3]);
-        mma16816(dp[2 * np], g, bv[0], bv[1]);
-        mma16816(dp[2 * np + 1], g, bv[2], bv[3]);
+        mma16816(dp[2 * np], ga[kk], bv[0], bv[1]);
+        mma16816(dp[2 * np + 1], ga[kk], bv[2], bv[3]);
       }
     }
-    uint32_t da[4][4];
+    if (!pass2) {
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      float x[4];
+      for (int nt = 0; nt < 8; ++nt) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int t = kb + 8 * nt + 2 * cq + (e & 1);
-        const int i = (e < 2) ? i0 : i1;
-        const float p = in_window(i, t, L, W) ? __expf(s[nt][e] * scale - ((e < 2) ? lse0 : lse1)) : 0.f;
-        x[e] = p * (dp[nt][e] - ((e < 2) ? dl0 : dl1));
+        for (int e = 0; e < 4; ++e) {
+          const int t = kb + 8 * nt + 2 * cq + (e & 1);
+          const int i = (e < 2) ? i0 : i1;
+          const float p =
+              in_window(i, t, L, W) ? __expf(s[nt][e] * scale - ((e < 2) ? lse0 : lse1)) : 0.f;
+          if (e < 2) ds0 += p * dp[nt][e]; else ds1 += p * dp[nt][e];
+        }
       }
-      da[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16(x[0], x[1]);
-      da[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(x[2], x[3]);
-    }
+      if (step == nkb - 1) {
+        dl0 = quad_sum(ds0);
+        dl1 = quad_sum(ds1);
+      }
+    } else {
+      uint32_t da[4][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+      for (int nt = 0; nt < 8; ++nt) {
+        float x[4];
 #pragma unroll
-      for (int np = 0; np < NTD / 2; ++np) {
-        uint32_t bb[4];
-        ldb_kn(bb, tK, LD, 16 * j, 16 * np);
-        mma16816(acc[2 * np], da[j], bb[0], bb[1]);
-        mma16816(acc[2 * np + 1], da[j], bb[2], bb[3]);
+        for (int e = 0; e < 4; ++e) {
+          const int t = kb + 8 * nt + 2 * cq + (e & 1);
+          const int i = (e < 2) ? i0 : i1;
+          const float p =
+              in_window(i, t, L, W) ? __expf(s[nt][e] * scale - ((e < 2) ? lse0 : lse1)) : 0.f;
+          x[e] = p * (dp[nt][e] - ((e < 2) ? dl0 : dl1));
+        }
+        da[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16(x[0], x[1]);
+        da[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(x[2], x[3]);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int np = 0; np < NTD / 2; ++np) {
+          uint32_t bb[4];
+          ldb_kn(bb, tK, LD, 16 * j, 16 * np);
+          mma16816(acc[2 * np], da[j], bb[0], bb[1]);
+          mma16816(acc[2 * np + 1], da[j], bb[2], bb[3]);
+        }
       }
     }
     __syncthreads();
@@ -341,24 +391,67 @@ swa_bwd_dq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
       if (d + 1 < D) store_grad(dq, base + (size_t)i1 * D + d + 1, acc[nt][3] * scale, gdt);
     }
   }
+  if (cq == 0) {
+    if (i0 < L) delta_out[(size_t)bh * L + i0] = dl0;
+    if (i1 < L) delta_out[(size_t)bh * L + i1] = dl1;
+  }
+  // per-block partials of sum_i exp(meta_j - lse_i) delta_i, in a fixed order
+  if (n_meta > 0) {
+    for (int j = 0; j < n_meta; ++j) {
+      float x = 0.f;
+      if (cq == 0) {
+        if (i0 < L) x += __expf(meta[j] - lse0) * dl0;
+        if (i1 < L) x += __expf(meta[j] - lse1) * dl1;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+      if (lane == 0) sRed[warp * kMaxMeta + j] = x;
+    }
+    __syncthreads();
+    if (tid < n_meta)
+      partial[(size_t)blockIdx.x * n_meta + tid] =
+          sRed[tid] + sRed[kMaxMeta + tid] + sRed[2 * kMaxMeta + tid] + sRed[3 * kMaxMeta + tid];
+  }
+}
+
+__global__ void swa_dmeta_kernel(const float* __restrict__ partial, int nblocks, int n_meta,
+                                 float* __restrict__ dmeta) {
+  const int j = threadIdx.x;
+  if (j >= n_meta) return;
+  float s = 0.f;
+  for (int b = 0; b < nblocks; ++b) s += partial[(size_t)b * n_meta + j];
+  dmeta[j] = -s;
 }
 
 // ------------------------------------------------------- backward: dk, dv
 // Works on transposed scores s^T = k q^T so every operand stays row-major.
-template <int DP>
+template <int DP, bool SPLIT>
+struct DkvSmem {
+  static constexpr size_t T = Tile<DP>::bytes;
+  static constexpr size_t k = 0, kl = k + T, v = kl + (SPLIT ? T : 0), q = v + T,
+                          ql = q + 2 * T, dy = ql + (SPLIT ? 2 * T : 0), rows = dy + 2 * T,
+                          bytes = rows + 4 * kB * 4;
+};
+
+template <int DP, bool SPLIT>
 __global__ void __launch_bounds__(128)
 swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
-                   const bf16* __restrict__ v, const bf16* __restrict__ dy,
+                   const bf16* __restrict__ v, const bf16* __restrict__ ql,
+                   const bf16* __restrict__ kl, const bf16* __restrict__ dy,
                    const float* __restrict__ lse, const float* __restrict__ delta, int W,
                    float scale, int L, int D, int nkb, int vec, void* __restrict__ dk,
                    void* __restrict__ dv, int gdt) {
-  constexpr int LD = DP + 8, NTD = DP / 8;
+  using SM = DkvSmem<DP, SPLIT>;
+  constexpr int LD = Tile<DP>::LD, NTD = DP / 8;
+  constexpr size_t T = Tile<DP>::bytes;
   extern __shared__ __align__(128) unsigned char smem[];
-  bf16* sK = reinterpret_cast<bf16*>(smem);
-  bf16* sV = sK + kB * LD;
-  bf16* sQ = sV + kB * LD;     // 2 stages
-  bf16* sDy = sQ + 2 * kB * LD;  // 2 stages
-  float* sRow = reinterpret_cast<float*>(sDy + 2 * kB * LD);  // 2 stages x (lse, delta)
+  bf16* sK = reinterpret_cast<bf16*>(smem + SM::k);
+  bf16* sKl = reinterpret_cast<bf16*>(smem + SM::kl);
+  bf16* sV = reinterpret_cast<bf16*>(smem + SM::v);
+  auto sQ = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::q + s * T); };
+  auto sQl = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::ql + s * T); };
+  auto sDy = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::dy + s * T); };
+  float* sRow = reinterpret_cast<float*>(smem + SM::rows);  // 2 stages x (lse, delta)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, cq = lane & 3;
   const int kbk = blockIdx.x % nkb, bh = blockIdx.x / nkb;
@@ -367,8 +460,9 @@ swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
   const int qlo = k0;  // query blocks start at the key block (causal)
   const int qhi = min(k0 + kB + W - 1, L);
   auto issue = [&](int qb, int st) {
-    stage_tile<kB, DP, 128>(sQ + st * kB * LD, LD, q + base, D, qb, L, 0, D, vec);
-    stage_tile<kB, DP, 128>(sDy + st * kB * LD, LD, dy + base, D, qb, L, 0, D, vec);
+    stage_tile<kB, DP, 128>(sQ(st), LD, q + base, D, qb, L, 0, D, vec);
+    if (SPLIT) stage_tile<kB, DP, 128>(sQl(st), LD, ql + base, D, qb, L, 0, D, vec);
+    stage_tile<kB, DP, 128>(sDy(st), LD, dy + base, D, qb, L, 0, D, vec);
     cp_async_commit();
     if (tid < kB) {
       const int r = qb + tid;
@@ -377,6 +471,7 @@ swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
     }
   };
   stage_tile<kB, DP, 128>(sK, LD, k + base, D, k0, L, 0, D, vec);
+  if (SPLIT) stage_tile<kB, DP, 128>(sKl, LD, kl + base, D, k0, L, 0, D, vec);
   stage_tile<kB, DP, 128>(sV, LD, v + base, D, k0, L, 0, D, vec);
   issue(qlo, 0);
   const int t0 = k0 + 16 * warp + gq, t1 = t0 + 8;  // this thread's key rows
@@ -385,7 +480,7 @@ swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
   for (int c = 0; c < NTD; ++c)
 #pragma unroll
     for (int e = 0; e < 4; ++e) dka[c][e] = dva[c][e] = 0.f;
-  uint32_t ka[DP / 16][4], va[DP / 16][4];
+  uint32_t ka[DP / 16][4], kla[DP / 16][4], va[DP / 16][4];
   int stage = 0;
   for (int qb = qlo; qb < qhi; qb += kB, stage ^= 1) {
     if (qb + kB < qhi) {
@@ -399,26 +494,25 @@ swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
 #pragma unroll
       for (int kk = 0; kk < DP / 16; ++kk) {
         lda_rm(ka[kk], sK, LD, 16 * warp, 16 * kk);
+        if (SPLIT) lda_rm(kla[kk], sKl, LD, 16 * warp, 16 * kk);
         lda_rm(va[kk], sV, LD, 16 * warp, 16 * kk);
       }
     }
-    const bf16* tQ = sQ + stage * kB * LD;
-    const bf16* tDy = sDy + stage * kB * LD;
+    const bf16* tQ = sQ(stage);
+    const bf16* tDy = sDy(stage);
     const float* rl = sRow + stage * 2 * kB;
     float s[8][4], dp[8][4];
+    scores<DP, SPLIT>(s, ka, kla, tQ, sQl(stage));
 #pragma unroll
     for (int c = 0; c < 8; ++c)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) s[c][e] = dp[c][e] = 0.f;
+      for (int e = 0; e < 4; ++e) dp[c][e] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < DP / 16; ++kk) {
 #pragma unroll
       for (int np = 0; np < 4; ++np) {
-        uint32_t bq[4], bg[4];
-        ldb_nk(bq, tQ, LD, 16 * np, 16 * kk);
+        uint32_t bg[4];
         ldb_nk(bg, tDy, LD, 16 * np, 16 * kk);
-        mma16816(s[2 * np], ka[kk], bq[0], bq[1]);
-        mma16816(s[2 * np + 1], ka[kk], bq[2], bq[3]);
         mma16816(dp[2 * np], va[kk], bg[0], bg[1]);
         mma16816(dp[2 * np + 1], va[kk], bg[2], bg[3]);
       }
@@ -482,87 +576,98 @@ swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
   }
 }
 
-template <int DP>
-size_t fwd_smem() { return (size_t)5 * kB * (DP + 8) * 2; }
-template <int DP>
-size_t dq_smem() { return (size_t)6 * kB * (DP + 8) * 2; }
-template <int DP>
-size_t dkv_smem() { return (size_t)6 * kB * (DP + 8) * 2 + 4 * kB * 4; }
-
-template <int DP>
-int launch_swa_fwd(const bf16* q, const bf16* k, const bf16* v, const float* meta, int n_meta,
-                   int W, int BH, int L, int D, int vec, bf16* y, float* lse, cudaStream_t st) {
+template <int DP, bool SPLIT>
+int launch_swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
+                   const float* meta, int n_meta, int W, int BH, int L, int D, int vec, bf16* y,
+                   float* lse, cudaStream_t st) {
+  using SM = FwdSmem<DP, SPLIT>;
   static bool done[64] = {false};
-  int rc = ensure_smem_swa(swa_fwd_kernel<DP>, fwd_smem<DP>(), done);
+  int rc = ensure_smem_swa(swa_fwd_kernel<DP, SPLIT>, SM::bytes, done);
   if (rc) return rc;
   const int nqb = ceil_div(L, kB);
   const float scale_log2 = kLog2e / sqrtf((float)D);
-  swa_fwd_kernel<DP><<<(unsigned)((long long)BH * nqb), 128, fwd_smem<DP>(), st>>>(
-      q, k, v, meta, n_meta, W, scale_log2, L, D, nqb, vec, y, lse);
+  swa_fwd_kernel<DP, SPLIT><<<(unsigned)((long long)BH * nqb), 128, SM::bytes, st>>>(
+      q, k, v, ql, kl, meta, n_meta, W, scale_log2, L, D, nqb, vec, y, lse);
   count_launches(1);
   return check_launch("swa_fwd_kernel");
 }
 
-template <int DP>
-int launch_swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* dy,
-                   const float* lse, const float* delta, int W, int BH, int L, int D, int vec,
-                   void* dq, void* dk, void* dv, int gdt, cudaStream_t st) {
+template <int DP, bool SPLIT>
+int launch_swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
+                   const bf16* dy, const float* meta, int n_meta, const float* lse,
+                   const SwaWork& wk, int W, int BH, int L, int D, int vec, void* dq, void* dk,
+                   void* dv, int gdt, cudaStream_t st) {
+  using SQ = DqSmem<DP, SPLIT>;
+  using SKV = DkvSmem<DP, SPLIT>;
   static bool done_q[64] = {false}, done_kv[64] = {false};
-  int rc = ensure_smem_swa(swa_bwd_dq_kernel<DP>, dq_smem<DP>(), done_q);
+  int rc = ensure_smem_swa(swa_bwd_dq_kernel<DP, SPLIT>, SQ::bytes, done_q);
   if (rc) return rc;
-  rc = ensure_smem_swa(swa_bwd_dkv_kernel<DP>, dkv_smem<DP>(), done_kv);
+  rc = ensure_smem_swa(swa_bwd_dkv_kernel<DP, SPLIT>, SKV::bytes, done_kv);
   if (rc) return rc;
   const int nb = ceil_div(L, kB);
   const float scale = 1.f / sqrtf((float)D);
-  swa_bwd_dq_kernel<DP><<<(unsigned)((long long)BH * nb), 128, dq_smem<DP>(), st>>>(
-      q, k, v, dy, lse, delta, W, scale, L, D, nb, vec, dq, gdt);
+  swa_bwd_dq_kernel<DP, SPLIT><<<(unsigned)((long long)BH * nb), 128, SQ::bytes, st>>>(
+      q, k, v, ql, kl, dy, meta, n_meta, lse, W, scale, L, D, nb, vec, dq, gdt, wk.delta,
+      wk.partial);
   count_launches(1);
   rc = check_launch("swa_bwd_dq_kernel");
   if (rc) return rc;
-  swa_bwd_dkv_kernel<DP><<<(unsigned)((long long)BH * nb), 128, dkv_smem<DP>(), st>>>(
-      q, k, v, dy, lse, delta, W, scale, L, D, nb, vec, dk, dv, gdt);
+  swa_bwd_dkv_kernel<DP, SPLIT><<<(unsigned)((long long)BH * nb), 128, SKV::bytes, st>>>(
+      q, k, v, ql, kl, dy, lse, wk.delta, W, scale, L, D, nb, vec, dk, dv, gdt);
   count_launches(1);
   return check_launch("swa_bwd_dkv_kernel");
 }
 
 }  // namespace
 
-int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const float* meta, int n_meta, int W,
-            bf16* y, float* lse, int B, int H, int L, int D, cudaStream_t st) {
+int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
+            const float* meta, int n_meta, int W, bf16* y, float* lse, int B, int H, int L, int D,
+            cudaStream_t st) {
   const int BH = B * H;
-  const int vec = (D % 8 == 0) && aligned16(q) && aligned16(k) && aligned16(v);
-  if (D <= 32) return launch_swa_fwd<32>(q, k, v, meta, n_meta, W, BH, L, D, vec, y, lse, st);
-  if (D <= 64) return launch_swa_fwd<64>(q, k, v, meta, n_meta, W, BH, L, D, vec, y, lse, st);
-  if (D <= 128) return launch_swa_fwd<128>(q, k, v, meta, n_meta, W, BH, L, D, vec, y, lse, st);
+  const bool split = ql != nullptr;
+  int vec = (D % 8 == 0) && aligned16(q) && aligned16(k) && aligned16(v);
+  if (split) vec = vec && aligned16(ql) && aligned16(kl);
+#define LZ_SWA_FWD(dp)                                                                       \
+  return split ? launch_swa_fwd<dp, true>(q, k, v, ql, kl, meta, n_meta, W, BH, L, D, vec, y, \
+                                          lse, st)                                           \
+               : launch_swa_fwd<dp, false>(q, k, v, ql, kl, meta, n_meta, W, BH, L, D, vec, y, \
+                                           lse, st);
+  if (D <= 32) { LZ_SWA_FWD(32) }
+  if (D <= 64) { LZ_SWA_FWD(64) }
+  if (D <= 128) { LZ_SWA_FWD(128) }
+#undef LZ_SWA_FWD
   set_error("swa_fwd: head dim above 128 is not supported");
   return LZ_ERR_UNSUPPORTED;
 }
 
-int swa_bwd(const bf16* q, const bf16* k, const bf16* v, const float* meta, int n_meta, int W,
-            const bf16* y, const float* lse, const bf16* dy, void* dq, void* dk, void* dv,
-            int gdt, float* dmeta, const SwaWork& wk, int B, int H, int L, int D,
-            cudaStream_t st) {
+int swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
+            const float* meta, int n_meta, int W, const float* lse, const bf16* dy, void* dq,
+            void* dk, void* dv, int gdt, float* dmeta, const SwaWork& wk, int B, int H, int L,
+            int D, cudaStream_t st) {
   const int BH = B * H;
-  const long long rows = (long long)BH * L;
-  const int nblocks = (int)((rows + kPrepRows - 1) / kPrepRows);
-  swa_bwd_prep_kernel<<<nblocks, 256, 0, st>>>(dy, y, lse, meta, n_meta, rows, D, wk.delta,
-                                               wk.partial);
-  count_launches(1);
-  int rc = check_launch("swa_bwd_prep_kernel");
-  if (rc) return rc;
-  const int vec = (D % 8 == 0) && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(dy);
-  if (D <= 32)
-    rc = launch_swa_bwd<32>(q, k, v, dy, lse, wk.delta, W, BH, L, D, vec, dq, dk, dv, gdt, st);
-  else if (D <= 64)
-    rc = launch_swa_bwd<64>(q, k, v, dy, lse, wk.delta, W, BH, L, D, vec, dq, dk, dv, gdt, st);
-  else if (D <= 128)
-    rc = launch_swa_bwd<128>(q, k, v, dy, lse, wk.delta, W, BH, L, D, vec, dq, dk, dv, gdt, st);
-  else {
+  const bool split = ql != nullptr;
+  int vec = (D % 8 == 0) && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(dy);
+  if (split) vec = vec && aligned16(ql) && aligned16(kl);
+  int rc;
+#define LZ_SWA_BWD(dp)                                                                         \
+  rc = split ? launch_swa_bwd<dp, true>(q, k, v, ql, kl, dy, meta, n_meta, lse, wk, W, BH, L, D, \
+                                        vec, dq, dk, dv, gdt, st)                              \
+             : launch_swa_bwd<dp, false>(q, k, v, ql, kl, dy, meta, n_meta, lse, wk, W, BH, L, \
+                                         D, vec, dq, dk, dv, gdt, st);
+  if (D <= 32) {
+    LZ_SWA_BWD(32)
+  } else if (D <= 64) {
+    LZ_SWA_BWD(64)
+  } else if (D <= 128) {
+    LZ_SWA_BWD(128)
+  } else {
     set_error("swa_bwd: head dim above 128 is not supported");
     return LZ_ERR_UNSUPPORTED;
   }
+#undef LZ_SWA_BWD
   if (rc) return rc;
   if (n_meta > 0 && dmeta) {
+    const int nblocks = BH * ceil_div(L, kB);
     swa_dmeta_kernel<<<1, kMaxMeta, 0, st>>>(wk.partial, nblocks, n_meta, dmeta);
     count_launches(1);
     rc = check_launch("swa_dmeta_kernel");

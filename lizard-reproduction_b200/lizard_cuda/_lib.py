@@ -30,10 +30,10 @@ _SIGNATURES = {
                             _vp, _vp, _c_size] + [_c_int] * 6 + [_vp]),
     "lz_swa_saved_bytes": (_c_size, [_c_int] * 4),
     "lz_swa_bwd_workspace_bytes": (_c_size, [_c_int] * 5),
-    "lz_swa_fwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _c_size] + [_c_int] * 4
+    "lz_swa_fwd": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp, _vp, _c_size] + [_c_int] * 4
                    + [_vp]),
-    "lz_swa_bwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _c_size, _vp, _vp, _vp,
-                            _vp, _c_int, _vp, _vp, _c_size] + [_c_int] * 4 + [_vp]),
+    "lz_swa_bwd": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp, _c_size, _vp, _vp, _vp, _vp,
+                                        _c_int, _vp, _vp, _c_size] + [_c_int] * 4 + [_vp]),
 }
 
 _lock = threading.Lock()

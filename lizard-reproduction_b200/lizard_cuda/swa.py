@@ -5,6 +5,10 @@ Drop-in for the reference's kernels.swa (src/kernels/swa.py:182-183): same
 arguments and defaults, bf16 output, gradients in each input's dtype
 (swa.py:139, 178). `meta` may be empty (no sinks). The block tuples are
 accepted for signature compatibility; the kernels use 64 x 64 tiles.
+
+When q or k is not bf16 (the Lizard layer passes fp32), each is sent as a bf16
+value plus its bf16 residual, and the kernels form the logits from both, so a
+large logit keeps about 16 mantissa bits instead of 8.
 """
 import torch
 
@@ -26,7 +30,13 @@ class _SWA(torch.autograd.Function):
         B, H, L, D = q.shape
         lib = _lib.load()
         ctx.dtypes = (q.dtype, k.dtype, v.dtype, meta.dtype)
-        q, k, v = (t.to(torch.bfloat16).contiguous() for t in (q, k, v))
+        q_lo = k_lo = None
+        if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+            q, q_lo = _split(q)
+            k, k_lo = _split(k)
+        else:
+            q, k = q.contiguous(), k.contiguous()
+        v = v.to(torch.bfloat16).contiguous()
         meta = meta.float().contiguous()
         n_meta = meta.numel()
         y = torch.empty(B, H, L, D, device=q.device, dtype=torch.bfloat16)
@@ -36,20 +46,21 @@ class _SWA(torch.autograd.Function):
             saved = torch.empty(lib.lz_swa_saved_bytes(B, H, L, D), device=q.device,
                                 dtype=torch.uint8)
         with torch.cuda.device(q.device):
-            rc = lib.lz_swa_fwd(_lib.ptr(q), _lib.ptr(k), _lib.ptr(v),
-                                _lib.ptr(meta) if n_meta else None, n_meta, int(window),
+            rc = lib.lz_swa_fwd(_lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(q_lo),
+                                _lib.ptr(k_lo), _lib.ptr(meta) if n_meta else None, n_meta,
+                                int(window),
                                 _lib.ptr(y), _lib.ptr(saved),
                                 0 if saved is None else saved.numel(), B, H, L, D,
                                 _lib.stream_of(q))
         _lib.check(rc, "swa forward")
         if save:
-            ctx.save_for_backward(q, k, v, meta, y, saved)
+            ctx.save_for_backward(q, k, v, meta, saved, q_lo, k_lo)
         ctx.window = int(window)
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        q, k, v, meta, y, saved = ctx.saved_tensors
+        q, k, v, meta, saved, q_lo, k_lo = ctx.saved_tensors
         B, H, L, D = q.shape
         n_meta = meta.numel()
         lib = _lib.load()
@@ -64,9 +75,9 @@ class _SWA(torch.autograd.Function):
         ws = torch.empty(lib.lz_swa_bwd_workspace_bytes(B, H, L, D, n_meta), device=q.device,
                          dtype=torch.uint8)
         with torch.cuda.device(q.device):
-            rc = lib.lz_swa_bwd(_lib.ptr(q), _lib.ptr(k), _lib.ptr(v),
-                                _lib.ptr(meta) if n_meta else None, n_meta, ctx.window,
-                                _lib.ptr(y), _lib.ptr(saved), saved.numel(), _lib.ptr(dy),
+            rc = lib.lz_swa_bwd(_lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(q_lo),
+                                _lib.ptr(k_lo), _lib.ptr(meta) if n_meta else None, n_meta,
+                                ctx.window, _lib.ptr(saved), saved.numel(), _lib.ptr(dy),
                                 _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv), gdt,
                                 _lib.ptr(dmeta) if n_meta else None, _lib.ptr(ws), ws.numel(),
                                 B, H, L, D, _lib.stream_of(q))
@@ -74,6 +85,13 @@ class _SWA(torch.autograd.Function):
         grads = (dq, dk, dv, dmeta)
         dq, dk, dv, dmeta = (g.to(d) for g, d in zip(grads, ctx.dtypes))
         return dq, dk, dv, dmeta, None, None, None
+
+
+def _split(x):
+    """x -> (bf16(x), bf16(x - bf16(x))), both contiguous."""
+    hi = x.to(torch.bfloat16).contiguous()
+    lo = (x.float() - hi.float()).to(torch.bfloat16).contiguous()
+    return hi, lo
 
 
 def _check_blocks(blocks, name):

@@ -2,7 +2,9 @@
 
 Runs the reference's own torch backend (src/lizard_attention.py of
 mahdikhashan/lizard-reproduction: gla, awa, LizardAttention) in fp32 on the
-seeded inputs of cases.py and stores outputs and gradients. This is exactly
+seeded inputs of cases.py and stores outputs and gradients, the latter both
+for the fp32 upstream gradient and for its bf16 rounding (keys ending in _b),
+which is what a bf16-output kernel receives from autograd. This is exactly
 how the reference checks its kernels (tests/test_kernels.py:32-42, 61-70,
 121-122, 137-156). Needs a checkout of the reference; the path comes from
 LIZARD_REFERENCE_SRC (default: the reference's src/ directory mounted beside
@@ -30,8 +32,7 @@ def reference():
     return lz
 
 
-def gla_golden(lz, name, kw):
-    inp = cases.gla_case(**kw)
+def gla_run(lz, inp, dy):
     fq, fk, v = (inp[n].float().requires_grad_() for n in ("fq", "fk", "v"))
     lg = inp["log_gamma"].clone().requires_grad_()
     gamma = lg.exp()
@@ -43,13 +44,21 @@ def gla_golden(lz, name, kw):
         def fold(t):
             return t.reshape(b * h, 1, n, -1)
         y = lz.gla(fold(fq), fold(fk), fold(v), gamma.reshape(b * h, n)).reshape(b, h, n, -1)
-    y.backward(inp["dy"])
-    return dict(kind="gla", kw=kw, inputs=inp, y=y.detach(), dfq=fq.grad, dfk=fk.grad,
-                dv=v.grad, dlog_gamma=lg.grad)
+    y.backward(dy)
+    return y.detach(), (fq.grad, fk.grad, v.grad, lg.grad)
 
 
-def swa_golden(lz, name, kw, window):
-    inp = cases.swa_case(**kw)
+def gla_golden(lz, name, kw):
+    inp = cases.gla_case(**kw)
+    y, (dfq, dfk, dv, dlg) = gla_run(lz, inp, inp["dy"])
+    # the kernels return bf16, so autograd hands them bf16(dy): the reference's
+    # gradients for that upstream gradient (suffix _b)
+    _, (dfq_b, dfk_b, dv_b, dlg_b) = gla_run(lz, inp, inp["dy"].bfloat16().float())
+    return dict(kind="gla", kw=kw, inputs=inp, y=y, dfq=dfq, dfk=dfk, dv=dv, dlog_gamma=dlg,
+                dfq_b=dfq_b, dfk_b=dfk_b, dv_b=dv_b, dlog_gamma_b=dlg_b)
+
+
+def swa_run(lz, inp, window, dy):
     q, k, v = (inp[n].float().requires_grad_() for n in ("q", "k", "v"))
     meta = inp["meta"].clone().requires_grad_()
     if meta.numel() == 0:  # no sinks: the reference evaluates it with a -1e4 sink
@@ -57,11 +66,17 @@ def swa_golden(lz, name, kw, window):
     else:
         ref_meta = meta
     y = lz.awa(q, k, v, ref_meta, window)
-    y.backward(inp["dy"])
-    out = dict(kind="swa", kw=kw, window=window, inputs=inp, y=y.detach(), dq=q.grad,
-               dk=k.grad, dv=v.grad)
-    out["dmeta"] = meta.grad if meta.numel() else torch.zeros(0)
-    return out
+    y.backward(dy)
+    dmeta = meta.grad if meta.numel() else torch.zeros(0)
+    return y.detach(), (q.grad, k.grad, v.grad, dmeta)
+
+
+def swa_golden(lz, name, kw, window):
+    inp = cases.swa_case(**kw)
+    y, (dq, dk, dv, dmeta) = swa_run(lz, inp, window, inp["dy"])
+    _, (dq_b, dk_b, dv_b, dmeta_b) = swa_run(lz, inp, window, inp["dy"].bfloat16().float())
+    return dict(kind="swa", kw=kw, window=window, inputs=inp, y=y, dq=dq, dk=dk, dv=dv,
+                dmeta=dmeta, dq_b=dq_b, dk_b=dk_b, dv_b=dv_b, dmeta_b=dmeta_b)
 
 
 def layer_golden(lz, name, case):

@@ -85,12 +85,14 @@ def test_gla_bwd_rejects_bad_grad_dtype(lib):
 
 
 def test_swa_rejects_bad_window_and_sinks(lib):
-    p = _fake(5)
-    assert lib.lz_swa_fwd(*p[:3], None, 0, 0, p[4], None, 0, 1, 1, 8, 8, None) == 1
+    p = _fake(6)
+    assert lib.lz_swa_fwd(*p[:3], None, None, None, 0, 0, p[4], None, 0, 1, 1, 8, 8, None) == 1
     assert b"window" in lib.lz_last_error_string()
-    assert lib.lz_swa_fwd(*p[:3], None, 2, 4, p[4], None, 0, 1, 1, 8, 8, None) == 1
-    assert lib.lz_swa_fwd(*p[:3], p[3], 33, 4, p[4], None, 0, 1, 1, 8, 8, None) == 2
-    assert lib.lz_swa_fwd(*p[:3], p[3], 1, 4, p[4], None, 0, 1, 1, 8, 256, None) == 2
+    assert lib.lz_swa_fwd(*p[:3], None, None, None, 2, 4, p[4], None, 0, 1, 1, 8, 8, None) == 1
+    assert lib.lz_swa_fwd(*p[:3], None, None, p[3], 33, 4, p[4], None, 0, 1, 1, 8, 8, None) == 2
+    assert lib.lz_swa_fwd(*p[:3], None, None, p[3], 1, 4, p[4], None, 0, 1, 1, 8, 256, None) == 2
+    assert lib.lz_swa_fwd(*p[:3], p[5], None, p[3], 1, 4, p[4], None, 0, 1, 1, 8, 8, None) == 1
+    assert b"q_lo" in lib.lz_last_error_string()
 
 
 def test_error_string_is_cleared_by_a_new_call(lib):
@@ -98,7 +100,7 @@ def test_error_string_is_cleared_by_a_new_call(lib):
     assert lib.lz_last_error_string() != b""
     lib.lz_abi_version()
     p = _fake(5)
-    lib.lz_swa_fwd(*p[:3], None, 0, 0, p[4], None, 0, 1, 1, 8, 8, None)
+    lib.lz_swa_fwd(*p[:3], None, None, None, 0, 0, p[4], None, 0, 1, 1, 8, 8, None)
     assert b"window" in lib.lz_last_error_string()
 
 

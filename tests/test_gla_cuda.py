@@ -50,7 +50,7 @@ def test_gla_matches_reference_fixture(name):
     for g, key in zip(grads, GRAD_NAMES):
         assert g.dtype == fx["inputs"][{"dfq": "fq", "dfk": "fk", "dv": "v",
                                         "dlog_gamma": "log_gamma"}[key]].dtype
-        assert_grad(g, fx[key], f"{name} {key}")
+        assert_grad(g, fx[key + "_b"], f"{name} {key}")
 
 
 def baseline_inputs(B, H, L, Fd, D, per_head, seed=0, device=DEV):
@@ -87,7 +87,7 @@ def test_gla_config3_forward_backward_all_heads():
     ys, dfq, dfk, dv, dlg = [], [], [], [], torch.zeros(1, 2048, dtype=torch.float32)
     for h0 in range(0, 32, 8):
         sl = (slice(None), slice(h0, h0 + 8))
-        r, (a, b_, c, d) = oracle_gla(fq[sl], fk[sl], v[sl], lg, dy[sl])
+        r, (a, b_, c, d) = oracle_gla(fq[sl], fk[sl], v[sl], lg, dy[sl].bfloat16())
         ys.append(r), dfq.append(a), dfk.append(b_), dv.append(c)
         dlg += d
     assert_output(y, torch.cat(ys, 1), "cfg3 y")
@@ -111,7 +111,7 @@ def test_gla_model_feature_dim_256():
     """F = 2 * feature_dim = 256 (the 1B model), D = 64, fwd + bwd."""
     fq, fk, v, lg, dy = baseline_inputs(1, 4, 300, 256, 64, per_head=False, seed=5)
     y, grads = cuda_gla(fq, fk, v, lg, dy)
-    ref, rgrads = oracle_gla(fq, fk, v, lg, dy)
+    ref, rgrads = oracle_gla(fq, fk, v, lg, dy.bfloat16())
     assert_output(y, ref, "F=256 y")
     for got, r, n in zip(grads, rgrads, GRAD_NAMES):
         assert_grad(got, r, f"F=256 {n}")
@@ -162,7 +162,7 @@ def test_gla_fp32_strided_inputs_give_fp32_grads():
     assert not fq.is_contiguous()
     y, grads = cuda_gla(fq, fk, v, inp["log_gamma"], inp["dy"])
     assert all(g.dtype == torch.float32 for g in grads)
-    ref, rgrads = oracle_gla(fq, fk, v, inp["log_gamma"], inp["dy"])
+    ref, rgrads = oracle_gla(fq, fk, v, inp["log_gamma"], inp["dy"].bfloat16())
     assert_output(y, ref, "fp32 y")
     for got, r, n in zip(grads, rgrads, GRAD_NAMES):
         assert_grad(got, r, f"fp32 {n}")
@@ -196,7 +196,7 @@ def test_gla_f128_d128_forward_backward(per_head, L):
     training mode, the 64-token state walk feeding the backward."""
     fq, fk, v, lg, dy = baseline_inputs(2, 3, L, 128, 128, per_head=per_head, seed=11)
     y, grads = cuda_gla(fq, fk, v, lg, dy)
-    ref, rgrads = oracle_gla(fq, fk, v, lg, dy)
+    ref, rgrads = oracle_gla(fq, fk, v, lg, dy.bfloat16())
     assert_output(y, ref, f"F=D=128 L={L} y")
     for got, r, n in zip(grads, rgrads, GRAD_NAMES):
         assert_grad(got, r, f"F=D=128 L={L} {n}")

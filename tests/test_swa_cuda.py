@@ -43,11 +43,10 @@ def test_swa_matches_reference_fixture(name):
                                       inp["dy"])
     assert y.dtype == torch.bfloat16
     assert_output(y, fx["y"], f"{name} y")
-    assert_grad(dq, fx["dq"], f"{name} dq")
-    assert_grad(dk, fx["dk"], f"{name} dk")
-    assert_grad(dv, fx["dv"], f"{name} dv")
+    for g, key in zip((dq, dk, dv), ("dq", "dk", "dv")):
+        assert_grad(g, fx[key + "_b"], f"{name} {key}")
     if inp["meta"].numel():
-        assert_grad(dmeta, fx["dmeta"], f"{name} dmeta")
+        assert_grad(dmeta, fx["dmeta_b"], f"{name} dmeta")
 
 
 def config3_inputs(seed=0):
@@ -66,7 +65,7 @@ def config3_inputs(seed=0):
 def test_swa_config3_forward_backward():
     q, k, v, meta, dy = config3_inputs()
     y, grads = cuda_swa(q, k, v, meta, 64, dy)
-    ref, rgrads = oracle_swa(q, k, v, meta, 64, dy)
+    ref, rgrads = oracle_swa(q, k, v, meta, 64, dy.bfloat16())
     assert_output(y, ref, "cfg3 y")
     for got, r, n in zip(grads, rgrads, ("dq", "dk", "dv", "dmeta")):
         assert_grad(got, r, f"cfg3 {n}")
@@ -78,7 +77,7 @@ def test_swa_head_dim_128_and_wide_window():
     meta = torch.randn(3, generator=g, device=DEV)
     dy = torch.randn(2, 2, 300, 128, generator=g, device=DEV)
     y, grads = cuda_swa(q, k, v, meta, 200, dy)
-    ref, rgrads = oracle_swa(q, k, v, meta, 200, dy)
+    ref, rgrads = oracle_swa(q, k, v, meta, 200, dy.bfloat16())
     assert_output(y, ref, "D=128 y")
     for got, r, n in zip(grads, rgrads, ("dq", "dk", "dv", "dmeta")):
         assert_grad(got, r, f"D=128 {n}")
@@ -112,6 +111,22 @@ def test_swa_gradient_only_inside_the_window():
     lizard_cuda.swa(q, k, v, inp["meta"].to(DEV), 16)[:, :, 39].float().sum().backward()
     assert (k.grad[:, :, :24] == 0).all()
     assert (k.grad[:, :, 24:].float().abs().sum(-1) > 0).all()
+
+
+def test_swa_fp32_inputs_use_residual_logits():
+    """fp32 q, k with large logits (|s| ~ 40): the bf16 residuals keep the
+    sink gradient within 1e-2 of the fp32 oracle."""
+    g = torch.Generator(device=DEV).manual_seed(4)
+    q, k = (3 * torch.randn(1, 4, 90, 32, generator=g, device=DEV) for _ in range(2))
+    v = torch.randn(1, 4, 90, 32, generator=g, device=DEV)
+    meta = torch.randn(4, generator=g, device=DEV)
+    dy = torch.randn(1, 4, 90, 32, generator=g, device=DEV)
+    y, grads = cuda_swa(q, k, v, meta, 16, dy)
+    assert all(t.dtype == torch.float32 for t in grads)
+    ref, rgrads = oracle_swa(q, k, v, meta, 16, dy.bfloat16())
+    assert_output(y, ref, "fp32 y")
+    for got, r, n in zip(grads, rgrads, ("dq", "dk", "dv", "dmeta")):
+        assert_grad(got, r, f"fp32 {n}")
 
 
 def test_swa_without_grad_gives_the_same_output():
