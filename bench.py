@@ -130,7 +130,7 @@ def measured_peaks():
 
 def profiled_traffic():
     """dram bytes per launch of the forward kernel from the committed ncu summary."""
-    p = ROOT / "profiles" / "gla_fwd_kernel_cfg2.txt"
+    p = ROOT / "profiles" / "gla_fwd_tc_kernel_cfg2.md"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
