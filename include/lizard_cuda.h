@@ -133,6 +133,25 @@ int lz_swa_bwd(const void* q, const void* k, const void* v,
                float* dmeta, void* workspace, size_t workspace_bytes,
                int B, int H, int L, int D, void* stream);
 
+/* lz_swa_bwd for callers that cannot allocate (no counterpart in the
+ * reference, whose kernels always allocate through torch). Some hosts give a
+ * plugin only its input and output buffers, for example a serving runtime's
+ * custom-op hook without a workspace request, so they cannot supply the
+ * workspace of lz_swa_bwd. This variant takes the same arguments minus the
+ * workspace and uses a fixed 4 MiB scratch array compiled into the library
+ * (held on every GPU that loads it). It allocates nothing. It returns
+ * LZ_ERR_UNSUPPORTED when lz_swa_bwd_workspace_bytes(B, H, L, D, n_meta)
+ * exceeds 4 MiB (about B*H*L = 1,000,000 rows). All calls on a device share
+ * the array; calls that overlap on the GPU race on it. The first call on a
+ * device looks up the array's address and should come before any stream
+ * capture. */
+int lz_swa_bwd_noalloc(const void* q, const void* k, const void* v,
+                       const void* q_lo, const void* k_lo,
+                       const float* meta, int n_meta, int window,
+                       const void* saved, size_t saved_bytes,
+                       const void* dy, void* dq, void* dk, void* dv, int grad_dtype,
+                       float* dmeta, int B, int H, int L, int D, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

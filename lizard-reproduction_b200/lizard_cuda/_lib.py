@@ -34,6 +34,8 @@ _SIGNATURES = {
                    + [_vp]),
     "lz_swa_bwd": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp, _c_size, _vp, _vp, _vp, _vp,
                                         _c_int, _vp, _vp, _c_size] + [_c_int] * 4 + [_vp]),
+    "lz_swa_bwd_noalloc": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp, _c_size, _vp, _vp, _vp,
+                                                _vp, _c_int, _vp] + [_c_int] * 4 + [_vp]),
 }
 
 _lock = threading.Lock()
