@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define LZ_ABI_VERSION 1
+#define LZ_ABI_VERSION 2
 
 enum {
   LZ_OK = 0,
@@ -73,19 +73,38 @@ int lz_device_timeout_flag(unsigned int* site);
  * cumulative log gate G, the per-chunk states S (bf16) and z (fp32). */
 size_t lz_gla_saved_bytes(int B, int H, int L, int F, int D, int chunk);
 
-/* Bytes of scratch lz_gla_bwd needs (delta, dS, dz, dG). */
+/* Bytes of scratch lz_gla_bwd needs (delta, dS, dz, dG, and the per-chunk
+ * increments when the chunk-parallel schedule is planned). */
 size_t lz_gla_bwd_workspace_bytes(int B, int H, int L, int F, int D, int chunk);
+
+/* Bytes of scratch lz_gla_fwd needs: 0 when the sequential walk is planned
+ * for this shape, else the per-chunk increments and states of the
+ * chunk-parallel schedule. No counterpart in the reference, whose forward
+ * allocates its state tensors itself (src/kernels/gla.py:221-222). */
+size_t lz_gla_fwd_workspace_bytes(int B, int H, int L, int F, int D, int chunk);
+
+/* Schedule of the GLA kernels, process-wide: 0 = chosen per shape (default),
+ * 1 = sequential walk over the chunks of each head (state kept on chip),
+ * 2 = chunk-parallel (every chunk's state increment at once, then a scan over
+ * chunks, then every chunk's output at once). Both give the same results
+ * within bf16 rounding. Returns the previous setting, or -LZ_ERR_INVALID_ARGUMENT
+ * for a value outside 0..2 (the setting is then unchanged). The workspace queries
+ * depend on it: do not change it between a query and the call it sizes.
+ * No counterpart in the reference; a hook for tests and tuning. */
+int lz_gla_set_schedule(int schedule);
 
 /* Forward of gla(fq, fk, v, log_gamma, chunk).
  * Replaces gla() + _GLA.forward of the reference (src/kernels/gla.py:259-263
- * and 213-234): G = cumsum(log_gamma) is computed inside the kernel, so one
- * launch covers the whole forward. y is bf16. When saved is non-null the
- * forward also fills it for the backward; y is bit-identical either way.
+ * and 213-234): G = cumsum(log_gamma) is computed on the device, chunk by
+ * chunk. y is bf16. When saved is non-null the forward also fills it for the
+ * backward; y is bit-identical either way. workspace may be null when
+ * lz_gla_fwd_workspace_bytes returns 0.
  * chunk is the reference's chunk length argument; the kernels use 64-token
  * chunks and accept any chunk >= 1 (results agree within bf16 tolerance). */
 int lz_gla_fwd(const void* fq, const void* fk, const void* v,
                const float* log_gamma, int gate_per_head,
                void* y, void* saved, size_t saved_bytes,
+               void* workspace, size_t workspace_bytes,
                int B, int H, int L, int F, int D, int chunk, void* stream);
 
 /* Backward of gla(). Replaces _GLA.backward (src/kernels/gla.py:236-256)

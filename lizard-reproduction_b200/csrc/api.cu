@@ -35,12 +35,33 @@ extern "C" size_t lz_gla_saved_bytes(int B, int H, int L, int F, int D, int chun
 extern "C" size_t lz_gla_bwd_workspace_bytes(int B, int H, int L, int F, int D, int chunk) {
   (void)chunk;
   if (B < 1 || H < 1 || L < 1 || F < 1 || D < 1) return 0;
-  return lz::gla_work_layout(B, H, L, F, D, nullptr, nullptr);
+  return lz::gla_work_layout(B, H, L, F, D, lz::gla_bwd_split(B, H, L, F, D), nullptr, nullptr);
+}
+
+extern "C" size_t lz_gla_fwd_workspace_bytes(int B, int H, int L, int F, int D, int chunk) {
+  (void)chunk;
+  if (B < 1 || H < 1 || L < 1 || F < 1 || D < 1) return 0;
+  if (!lz::gla_fwd_split(B, H, L, F, D)) return 0;
+  return lz::gla_fwd_work_layout(B, H, L, F, D, nullptr, nullptr);
+}
+
+namespace lz {
+int gla_set_schedule(int s);
+}
+
+extern "C" int lz_gla_set_schedule(int schedule) {
+  lz::clear_error();
+  if (schedule < 0 || schedule > 2) {
+    lz::set_error("schedule must be 0 (auto), 1 (walk) or 2 (chunk-parallel)");
+    return -LZ_ERR_INVALID_ARGUMENT;
+  }
+  return lz::gla_set_schedule(schedule);
 }
 
 extern "C" int lz_gla_fwd(const void* fq, const void* fk, const void* v, const float* log_gamma,
-                          int gate_per_head, void* y, void* saved, size_t saved_bytes, int B,
-                          int H, int L, int F, int D, int chunk, void* stream) {
+                          int gate_per_head, void* y, void* saved, size_t saved_bytes,
+                          void* workspace, size_t workspace_bytes, int B, int H, int L, int F,
+                          int D, int chunk, void* stream) {
   lz::clear_error();
   int rc = check_sizes(B, H, L, F, D);
   if (rc) return rc;
@@ -55,9 +76,18 @@ extern "C" int lz_gla_fwd(const void* fq, const void* fk, const void* v, const f
     LZ_REQUIRE(lz::aligned16(saved), LZ_ERR_INVALID_ARGUMENT, "saved buffer must be 16-byte aligned");
     lz::gla_saved_layout(B, H, L, F, D, static_cast<unsigned char*>(saved), &sv);
   }
+  lz::GlaFwdWork fw;
+  if (lz::gla_fwd_split(B, H, L, F, D)) {
+    const size_t need = lz::gla_fwd_work_layout(B, H, L, F, D, nullptr, nullptr);
+    LZ_REQUIRE(workspace && workspace_bytes >= need, LZ_ERR_WORKSPACE,
+               "workspace too small (lz_gla_fwd_workspace_bytes)");
+    LZ_REQUIRE(lz::aligned16(workspace), LZ_ERR_INVALID_ARGUMENT,
+               "workspace must be 16-byte aligned");
+    lz::gla_fwd_work_layout(B, H, L, F, D, static_cast<unsigned char*>(workspace), &fw);
+  }
   return lz::gla_fwd(static_cast<const bf16*>(fq), static_cast<const bf16*>(fk),
                      static_cast<const bf16*>(v), log_gamma, gate_per_head ? 1 : 0,
-                     static_cast<bf16*>(y), sv, B, H, L, F, D,
+                     static_cast<bf16*>(y), sv, fw, B, H, L, F, D,
                      static_cast<cudaStream_t>(stream));
 }
 
@@ -78,7 +108,8 @@ extern "C" int lz_gla_bwd(const void* fq, const void* fk, const void* v, const f
   LZ_REQUIRE(F <= 256, LZ_ERR_UNSUPPORTED, "feature dim above 256 is not supported");
   LZ_REQUIRE(D <= 128, LZ_ERR_UNSUPPORTED, "value dim above 128 is not supported in the backward");
   const size_t need_s = lz::gla_saved_layout(B, H, L, F, D, nullptr, nullptr);
-  const size_t need_w = lz::gla_work_layout(B, H, L, F, D, nullptr, nullptr);
+  const bool split = lz::gla_bwd_split(B, H, L, F, D);
+  const size_t need_w = lz::gla_work_layout(B, H, L, F, D, split, nullptr, nullptr);
   LZ_REQUIRE(saved_bytes >= need_s, LZ_ERR_WORKSPACE, "saved buffer too small");
   LZ_REQUIRE(workspace_bytes >= need_w, LZ_ERR_WORKSPACE, "workspace too small");
   LZ_REQUIRE(lz::aligned16(saved) && lz::aligned16(workspace), LZ_ERR_INVALID_ARGUMENT,
@@ -86,7 +117,7 @@ extern "C" int lz_gla_bwd(const void* fq, const void* fk, const void* v, const f
   lz::GlaSaved sv;
   lz::GlaWork wk;
   lz::gla_saved_layout(B, H, L, F, D, (unsigned char*)const_cast<void*>(saved), &sv);
-  lz::gla_work_layout(B, H, L, F, D, static_cast<unsigned char*>(workspace), &wk);
+  lz::gla_work_layout(B, H, L, F, D, split, static_cast<unsigned char*>(workspace), &wk);
   return lz::gla_bwd(static_cast<const bf16*>(fq), static_cast<const bf16*>(fk),
                      static_cast<const bf16*>(v), log_gamma, gate_per_head ? 1 : 0, sv,
                      static_cast<const bf16*>(dy), dfq, dfk, dv, grad_dtype, dlog_gamma, wk, B,

@@ -488,21 +488,26 @@ gla_bwd_chunk_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
 
 // --------------------------------------------------- 4. log-gate gradient
 // out[j] = sum_{i >= j} x[i], x = dG (per-head gate) or sum over heads of dG
-// (gate shared by the heads of a batch row). Heads are summed in a fixed order.
-__global__ void __launch_bounds__(256)
+// (gate shared by the heads of a batch row). One CTA per gate row, 1024
+// threads; tiles of 1024 positions from the end, heads summed in a fixed order,
+// a two-level warp scan inside the tile and a carry across tiles.
+__global__ void __launch_bounds__(1024)
 gla_bwd_gate_kernel(const float* __restrict__ dG, float* __restrict__ out, int H, int L,
                     int gate_per_head) {
-  __shared__ float warp_tot[8];
+  __shared__ float warp_tot[32];
+  __shared__ float carry_s;
   const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  float carry = 0.f;
-  for (int base = ((L - 1) / 256) * 256; base >= 0; base -= 256) {
+  if (tid == 0) carry_s = 0.f;
+  for (int base = ((L - 1) / 1024) * 1024; base >= 0; base -= 1024) {
     const int j = base + tid;
     float x = 0.f;
     if (j < L) {
       if (gate_per_head) {
         x = dG[(size_t)row * L + j];
       } else {
-        for (int h = 0; h < H; ++h) x += dG[((size_t)row * H + h) * L + j];
+        const float* p = dG + (size_t)row * H * L + j;
+#pragma unroll 8
+        for (int h = 0; h < H; ++h) x += p[(size_t)h * L];
       }
     }
     // suffix scan within the warp
@@ -513,12 +518,21 @@ gla_bwd_gate_kernel(const float* __restrict__ dG, float* __restrict__ out, int H
     }
     if (lane == 0) warp_tot[warp] = x;
     __syncthreads();
-    float later = 0.f;
-    for (int w = warp + 1; w < 8; ++w) later += warp_tot[w];
-    float block_tot = 0.f;
-    for (int w = 0; w < 8; ++w) block_tot += warp_tot[w];
+    if (warp == 0) {  // suffix scan of the 32 warp totals
+      float w = warp_tot[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_down_sync(0xffffffffu, w, o);
+        if (lane + o < 32) w += u;
+      }
+      warp_tot[lane] = w;  // sum of warps >= lane
+    }
+    __syncthreads();
+    const float carry = carry_s;
+    const float later = warp + 1 < 32 ? warp_tot[warp + 1] : 0.f;
     if (j < L) out[(size_t)row * L + j] = carry + later + x;
-    carry += block_tot;
+    __syncthreads();
+    if (tid == 0) carry_s = carry + warp_tot[0];
     __syncthreads();
   }
 }
@@ -569,14 +583,17 @@ int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int 
   const int vec_f = (F % 8 == 0) && aligned16(fq) && aligned16(fk);
   const int vec_d = (D % 8 == 0) && aligned16(v) && aligned16(dy) && aligned16(sv.s) &&
                     aligned16(wk.ds);
-  const long long rows = (long long)BH * L;
-  gla_bwd_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(dy, sv.y32, wk.delta,
-                                                                       rows, D);
-  count_launches(1);
-  int rc = check_launch("gla_bwd_delta_kernel");
-  if (rc) return rc;
-
-  {
+  int rc = LZ_OK;
+  if (wk.inc) {
+    rc = gla_bwd_split_states(fq, dy, sv, wk, B, H, L, F, D, stream);
+    if (rc) return rc;
+  } else {
+    const long long rows = (long long)BH * L;
+    gla_bwd_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(dy, sv.y32, wk.delta,
+                                                                         rows, D);
+    count_launches(1);
+    rc = check_launch("gla_bwd_delta_kernel");
+    if (rc) return rc;
     static bool done[64] = {false};
     rc = ensure_smem(gla_bwd_state_kernel, StateSmem::bytes, done);
     if (rc) return rc;
@@ -608,7 +625,7 @@ int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int 
   if (rc) return rc;
 
   const int gate_rows = gph ? BH : B;
-  gla_bwd_gate_kernel<<<gate_rows, 256, 0, stream>>>(wk.dg, dlg, H, L, gph);
+  gla_bwd_gate_kernel<<<gate_rows, 1024, 0, stream>>>(wk.dg, dlg, H, L, gph);
   count_launches(1);
   return check_launch("gla_bwd_gate_kernel");
 }

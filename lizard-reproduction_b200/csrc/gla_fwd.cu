@@ -18,6 +18,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "gla_chunk.cuh"
 #include "gla_layout.h"
 
 namespace lz {
@@ -124,129 +125,9 @@ gla_fwd_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
     const float end = sG[nvalid - 1];
     carry = end;
 
-    const int i0 = 16 * warp + gq, i1 = i0 + 8;
-    const float gi0 = sG[i0], gi1 = sG[i1];
-
-    // (a) intra-chunk scores s = fq fk^T for this warp's 16 rows
-    float sacc[8][4];
-#pragma unroll
-    for (int c = 0; c < 8; ++c)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) sacc[c][e] = 0.f;
-#pragma unroll 2
-    for (int k0 = 0; k0 < FP; k0 += 16) {
-      uint32_t a[4];
-      lda_rm(a, sQ, LDQ, 16 * warp, k0);
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        uint32_t bb[4];
-        ldb_nk(bb, sK, LDQ, 16 * np, k0);
-        mma16816(sacc[2 * np], a, bb[0], bb[1]);
-        mma16816(sacc[2 * np + 1], a, bb[2], bb[3]);
-      }
-    }
-    // (b) causal decay, bf16 rounding; the row sum uses the rounded weights
-    float den0 = 0.f, den1 = 0.f;
-    uint32_t af[4][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const int t = 8 * nt + 2 * cq;
-      const float gt0 = sG[t], gt1 = sG[t + 1];
-      const float w00 = (t <= i0 && i0 < nvalid) ? sacc[nt][0] * __expf(gi0 - gt0) : 0.f;
-      const float w01 = (t + 1 <= i0 && i0 < nvalid) ? sacc[nt][1] * __expf(gi0 - gt1) : 0.f;
-      const float w10 = (t <= i1 && i1 < nvalid) ? sacc[nt][2] * __expf(gi1 - gt0) : 0.f;
-      const float w11 = (t + 1 <= i1 && i1 < nvalid) ? sacc[nt][3] * __expf(gi1 - gt1) : 0.f;
-      const uint32_t p0 = pack_bf16(w00, w01), p1 = pack_bf16(w10, w11);
-      den0 += bf16_lo(p0) + bf16_hi(p0);
-      den1 += bf16_lo(p1) + bf16_hi(p1);
-      af[nt >> 1][(nt & 1) * 2 + 0] = p0;
-      af[nt >> 1][(nt & 1) * 2 + 1] = p1;
-    }
-    // (c) o = a V
-    float oacc[NTV][4];
-#pragma unroll
-    for (int c = 0; c < NTV; ++c)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) oacc[c][e] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-#pragma unroll
-      for (int np = 0; np < NTV / 2; ++np) {
-        uint32_t bb[4];
-        ldb_kn(bb, sV, LDV, 16 * j, 16 * np);
-        mma16816(oacc[2 * np], af[j], bb[0], bb[1]);
-        mma16816(oacc[2 * np + 1], af[j], bb[2], bb[3]);
-      }
-    }
-    // (d) inter-chunk: o += Q~ S_n, den += Q~ . z_n
-    if (n > 0) {
-      const float qs0 = __expf(gi0 - start), qs1 = __expf(gi1 - start);
-#pragma unroll 2
-      for (int k0 = 0; k0 < FP; k0 += 16) {
-        uint32_t a[4];
-        lda_rm(a, sQ, LDQ, 16 * warp, k0);
-        a[0] = pack_bf16(bf16_lo(a[0]) * qs0, bf16_hi(a[0]) * qs0);
-        a[1] = pack_bf16(bf16_lo(a[1]) * qs1, bf16_hi(a[1]) * qs1);
-        a[2] = pack_bf16(bf16_lo(a[2]) * qs0, bf16_hi(a[2]) * qs0);
-        a[3] = pack_bf16(bf16_lo(a[3]) * qs1, bf16_hi(a[3]) * qs1);
-        const int f = k0 + 2 * cq;
-        const float z0 = sZ[f], z1 = sZ[f + 1], z8 = sZ[f + 8], z9 = sZ[f + 9];
-        den0 += bf16_lo(a[0]) * z0 + bf16_hi(a[0]) * z1 + bf16_lo(a[2]) * z8 + bf16_hi(a[2]) * z9;
-        den1 += bf16_lo(a[1]) * z0 + bf16_hi(a[1]) * z1 + bf16_lo(a[3]) * z8 + bf16_hi(a[3]) * z9;
-#pragma unroll
-        for (int np = 0; np < NTV / 2; ++np) {
-          uint32_t bb[4];
-          ldb_kn(bb, sS, LDV, k0, 16 * np);
-          mma16816(oacc[2 * np], a, bb[0], bb[1]);
-          mma16816(oacc[2 * np + 1], a, bb[2], bb[3]);
-        }
-      }
-    }
-    // (e) normalise and store
-    den0 = quad_sum(den0);
-    den1 = quad_sum(den1);
-    const float inv0 = 1.f / fmaxf(den0, kTiny), inv1 = 1.f / fmaxf(den1, kTiny);
-    {
-      const size_t row0 = ((size_t)bh * L + r0 + i0) * D, row1 = ((size_t)bh * L + r0 + i1) * D;
-      const bool pair = (D & 1) == 0;
-#pragma unroll
-      for (int nt = 0; nt < NTV; ++nt) {
-        const int d = d0 + 8 * nt + 2 * cq;
-        if (d >= D) continue;
-        const float y00 = oacc[nt][0] * inv0, y01 = oacc[nt][1] * inv0;
-        const float y10 = oacc[nt][2] * inv1, y11 = oacc[nt][3] * inv1;
-        if (i0 < nvalid) {
-          if (pair) {
-            *reinterpret_cast<__nv_bfloat162*>(y + row0 + d) = __floats2bfloat162_rn(y00, y01);
-            if (save) *reinterpret_cast<float2*>(y32 + row0 + d) = make_float2(y00, y01);
-          } else {
-            y[row0 + d] = __float2bfloat16_rn(y00);
-            if (d + 1 < D) y[row0 + d + 1] = __float2bfloat16_rn(y01);
-            if (save) {
-              y32[row0 + d] = y00;
-              if (d + 1 < D) y32[row0 + d + 1] = y01;
-            }
-          }
-        }
-        if (i1 < nvalid) {
-          if (pair) {
-            *reinterpret_cast<__nv_bfloat162*>(y + row1 + d) = __floats2bfloat162_rn(y10, y11);
-            if (save) *reinterpret_cast<float2*>(y32 + row1 + d) = make_float2(y10, y11);
-          } else {
-            y[row1 + d] = __float2bfloat16_rn(y10);
-            if (d + 1 < D) y[row1 + d + 1] = __float2bfloat16_rn(y11);
-            if (save) {
-              y32[row1 + d] = y10;
-              if (d + 1 < D) y32[row1 + d + 1] = y11;
-            }
-          }
-        }
-      }
-      if (save && lead && cq == 0) {
-        if (i0 < nvalid) den_out[(size_t)bh * L + r0 + i0] = den0;
-        if (i1 < nvalid) den_out[(size_t)bh * L + r0 + i1] = den1;
-      }
-    }
+    gla_chunk_output<FP, DV>(sQ, sK, sV, sS, sZ, sG, start, nvalid, n > 0,
+                             (size_t)bh * L + r0, D, d0, y, save ? y32 : nullptr,
+                             (save && lead) ? den_out + (size_t)bh * L + r0 : nullptr);
     __syncthreads();  // sQ, sS, sZ no longer read in this chunk
     if (n + 1 < NT) {
       stage_tile<kChunk, FP, 128>(sQ, LDQ, Q, F, r0 + kChunk, L, 0, F, vec_f);
@@ -489,7 +370,9 @@ int gla_fwd_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
                const GlaSaved& sv, int B, int H, int L, int F, int D, cudaStream_t stream);
 
 int gla_fwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, bf16* y,
-            const GlaSaved& sv, int B, int H, int L, int F, int D, cudaStream_t stream) {
+            const GlaSaved& sv, const GlaFwdWork& fw, int B, int H, int L, int F, int D,
+            cudaStream_t stream) {
+  if (fw.inc) return gla_fwd_split_run(fq, fk, v, lg, gph, y, sv, fw, B, H, L, F, D, stream);
   const int BH = B * H;
   {
     int rc = gla_fwd_tc(fq, fk, v, lg, gph, y, sv, B, H, L, F, D, stream);

@@ -22,7 +22,48 @@ struct GlaWork {
   bf16* ds = nullptr;      // [BH, NT, F, D] state gradient leaving each chunk
   float* dz = nullptr;     // [BH, NT, F]
   float* dg = nullptr;     // [BH, L] gradient w.r.t. G
+  // chunk-parallel schedule only (null for the sequential walk)
+  float* inc = nullptr;    // [BH, NT, F, D] per-chunk increment Q^_n^T dY_n (fp32)
+  float* incz = nullptr;   // [BH, NT, F]   per-chunk increment Q^_n^T delta_n
+  float* lam = nullptr;    // [BH, NT]      log decay of each chunk, G_end - G_start
 };
+
+// Forward scratch of the chunk-parallel schedule.
+struct GlaFwdWork {
+  float* inc = nullptr;   // [BH, NT, F, D] per-chunk increment K~_n^T V_n (fp32)
+  float* incz = nullptr;  // [BH, NT, F]   per-chunk increment sum_t K~_t
+  float* lam = nullptr;   // [BH, NT]      log decay of each chunk
+  float* gs = nullptr;    // [BH, NT]      G just before each chunk
+  bf16* s = nullptr;      // [BH, NT, F, D] states when there is no saved buffer
+  float* z = nullptr;     // [BH, NT, F]
+};
+
+// Schedule of a GLA call. The sequential walk keeps the running state on chip
+// and moves the fewest bytes, but runs one chain of chunks per (batch*head,
+// block) and so leaves most SMs idle when batch*heads is small. The
+// chunk-parallel schedule computes every chunk's state increment at once,
+// combines them with an elementwise scan over chunks and then forms every
+// chunk's output at once, at the cost of fp32 increments through HBM/L2.
+enum GlaSchedule { kScheduleAuto = 0, kScheduleWalk = 1, kScheduleSplit = 2 };
+int gla_schedule_override();  // process-wide, set by lz_gla_set_schedule
+
+inline bool gla_fwd_split(int B, int H, int L, int F, int D) {
+  const int o = gla_schedule_override();
+  if (o == kScheduleWalk) return false;
+  if (o == kScheduleSplit) return true;
+  if (L <= 64) return false;  // a single chunk: both schedules are the same work
+  const long long BH = (long long)B * H;
+  if (F == 128 && D == 128) return BH <= 40;  // tensor-core walk, one CTA per head
+  return BH * ((F + 63) / 64) * ((D + 63) / 64) <= 148;
+}
+
+inline bool gla_bwd_split(int B, int H, int L, int F, int D) {
+  const int o = gla_schedule_override();
+  if (o == kScheduleWalk) return false;
+  if (o == kScheduleSplit) return true;
+  if (L <= 64) return false;
+  return (long long)B * H * ((F + 63) / 64) * ((D + 63) / 64) <= 148;
+}
 
 inline size_t gla_nt(int L) { return (size_t)((L + 63) / 64); }
 
@@ -50,8 +91,8 @@ inline size_t gla_saved_layout(int B, int H, int L, int F, int D, unsigned char*
   return off;
 }
 
-inline size_t gla_work_layout(int B, int H, int L, int F, int D, unsigned char* base,
-                              GlaWork* out) {
+inline size_t gla_work_layout(int B, int H, int L, int F, int D, bool split,
+                              unsigned char* base, GlaWork* out) {
   const size_t BH = (size_t)B * H, NT = gla_nt(L);
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -63,17 +104,59 @@ inline size_t gla_work_layout(int B, int H, int L, int F, int D, unsigned char* 
   const size_t o_ds = take(BH * NT * F * D * 2);
   const size_t o_dz = take(BH * NT * F * 4);
   const size_t o_dg = take(BH * L * 4);
+  const size_t o_inc = split ? take(BH * NT * F * D * 4) : 0;
+  const size_t o_incz = split ? take(BH * NT * F * 4) : 0;
+  const size_t o_lam = split ? take(BH * NT * 4) : 0;
   if (out && base) {
     out->delta = reinterpret_cast<float*>(base + o_delta);
     out->ds = reinterpret_cast<bf16*>(base + o_ds);
     out->dz = reinterpret_cast<float*>(base + o_dz);
     out->dg = reinterpret_cast<float*>(base + o_dg);
+    if (split) {
+      out->inc = reinterpret_cast<float*>(base + o_inc);
+      out->incz = reinterpret_cast<float*>(base + o_incz);
+      out->lam = reinterpret_cast<float*>(base + o_lam);
+    }
+  }
+  return off;
+}
+
+inline size_t gla_fwd_work_layout(int B, int H, int L, int F, int D, unsigned char* base,
+                                  GlaFwdWork* out) {
+  const size_t BH = (size_t)B * H, NT = gla_nt(L);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 256);
+    return o;
+  };
+  const size_t o_inc = take(BH * NT * F * D * 4);
+  const size_t o_incz = take(BH * NT * F * 4);
+  const size_t o_lam = take(BH * NT * 4);
+  const size_t o_gs = take(BH * NT * 4);
+  const size_t o_s = take(BH * NT * F * D * 2);
+  const size_t o_z = take(BH * NT * F * 4);
+  if (out && base) {
+    out->inc = reinterpret_cast<float*>(base + o_inc);
+    out->incz = reinterpret_cast<float*>(base + o_incz);
+    out->lam = reinterpret_cast<float*>(base + o_lam);
+    out->gs = reinterpret_cast<float*>(base + o_gs);
+    out->s = reinterpret_cast<bf16*>(base + o_s);
+    out->z = reinterpret_cast<float*>(base + o_z);
   }
   return off;
 }
 
 int gla_fwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, bf16* y,
-            const GlaSaved& sv, int B, int H, int L, int F, int D, cudaStream_t stream);
+            const GlaSaved& sv, const GlaFwdWork& fw, int B, int H, int L, int F, int D,
+            cudaStream_t stream);
+
+// Chunk-parallel schedule (gla_split.cu).
+int gla_fwd_split_run(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
+                      bf16* y, const GlaSaved& sv, const GlaFwdWork& fw, int B, int H, int L,
+                      int F, int D, cudaStream_t stream);
+int gla_bwd_split_states(const bf16* fq, const bf16* dy, const GlaSaved& sv, const GlaWork& wk,
+                         int B, int H, int L, int F, int D, cudaStream_t stream);
 
 int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
             const GlaSaved& sv, const bf16* dy, void* dfq, void* dfk, void* dv, int gdt,

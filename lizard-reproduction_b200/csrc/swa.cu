@@ -414,13 +414,25 @@ swa_bwd_dq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
   }
 }
 
-__global__ void swa_dmeta_kernel(const float* __restrict__ partial, int nblocks, int n_meta,
-                                 float* __restrict__ dmeta) {
-  const int j = threadIdx.x;
-  if (j >= n_meta) return;
-  float s = 0.f;
-  for (int b = 0; b < nblocks; ++b) s += partial[(size_t)b * n_meta + j];
-  dmeta[j] = -s;
+// dmeta_j = -sum_b partial[b][j]: 256 threads, each summing a fixed strided
+// subset of blocks, then a fixed-order tree in shared memory.
+__global__ void __launch_bounds__(256)
+swa_dmeta_kernel(const float* __restrict__ partial, int nblocks, int n_meta,
+                 float* __restrict__ dmeta) {
+  __shared__ float red[256];
+  const int tid = threadIdx.x;
+  for (int j = 0; j < n_meta; ++j) {
+    float s = 0.f;
+    for (int b = tid; b < nblocks; b += 256) s += partial[(size_t)b * n_meta + j];
+    red[tid] = s;
+    __syncthreads();
+    for (int w = 128; w > 0; w >>= 1) {
+      if (tid < w) red[tid] += red[tid + w];
+      __syncthreads();
+    }
+    if (tid == 0) dmeta[j] = -red[0];
+    __syncthreads();
+  }
 }
 
 // ------------------------------------------------------- backward: dk, dv
@@ -668,7 +680,7 @@ int swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const b
   if (rc) return rc;
   if (n_meta > 0 && dmeta) {
     const int nblocks = BH * ceil_div(L, kB);
-    swa_dmeta_kernel<<<1, kMaxMeta, 0, st>>>(wk.partial, nblocks, n_meta, dmeta);
+    swa_dmeta_kernel<<<1, 256, 0, st>>>(wk.partial, nblocks, n_meta, dmeta);
     count_launches(1);
     rc = check_launch("swa_dmeta_kernel");
   }

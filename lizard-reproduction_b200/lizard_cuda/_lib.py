@@ -10,7 +10,7 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 LIB_PATH = Path(__file__).resolve().with_name("liblizard_cuda.so")
 HEADER = Path(__file__).resolve().parents[2] / "include" / "lizard_cuda.h"
 
@@ -25,7 +25,10 @@ _SIGNATURES = {
     "lz_device_timeout_flag": (_c_int, [ctypes.POINTER(ctypes.c_uint)]),
     "lz_gla_saved_bytes": (_c_size, [_c_int] * 6),
     "lz_gla_bwd_workspace_bytes": (_c_size, [_c_int] * 6),
-    "lz_gla_fwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_size] + [_c_int] * 6 + [_vp]),
+    "lz_gla_fwd_workspace_bytes": (_c_size, [_c_int] * 6),
+    "lz_gla_set_schedule": (_c_int, [_c_int]),
+    "lz_gla_fwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_size, _vp, _c_size]
+                   + [_c_int] * 6 + [_vp]),
     "lz_gla_bwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _c_size, _vp, _vp, _vp, _vp, _c_int,
                             _vp, _vp, _c_size] + [_c_int] * 6 + [_vp]),
     "lz_swa_saved_bytes": (_c_size, [_c_int] * 4),
@@ -79,6 +82,17 @@ def device_timeout_flag():
     out = ctypes.c_uint(0)
     check(load().lz_device_timeout_flag(ctypes.byref(out)), "timeout flag query")
     return int(out.value)
+
+
+SCHEDULES = {"auto": 0, "walk": 1, "split": 2}
+
+
+def set_schedule(name):
+    """Process-wide GLA schedule ("auto", "walk" or "split"); returns the previous name."""
+    prev = load().lz_gla_set_schedule(SCHEDULES[name])
+    if prev < 0:
+        check(-prev, "set schedule")
+    return {v: k for k, v in SCHEDULES.items()}[prev]
 
 
 def ptr(t):

@@ -43,11 +43,13 @@ class _GLA(torch.autograd.Function):
         if save:
             nbytes = lib.lz_gla_saved_bytes(B, H, L, F, D, chunk)
             saved = torch.empty(nbytes, device=v.device, dtype=torch.uint8)
+        wbytes = lib.lz_gla_fwd_workspace_bytes(B, H, L, F, D, chunk)
+        ws = torch.empty(wbytes, device=v.device, dtype=torch.uint8) if wbytes else None
         with torch.cuda.device(v.device):
             rc = lib.lz_gla_fwd(_lib.ptr(fq), _lib.ptr(fk), _lib.ptr(v), _lib.ptr(lg), per_head,
                                 _lib.ptr(y), _lib.ptr(saved),
-                                0 if saved is None else saved.numel(), B, H, L, F, D, chunk,
-                                _lib.stream_of(v))
+                                0 if saved is None else saved.numel(), _lib.ptr(ws), wbytes,
+                                B, H, L, F, D, chunk, _lib.stream_of(v))
         _lib.check(rc, "gla forward")
         if save:
             ctx.save_for_backward(fq, fk, v, lg, saved)

@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 def test_abi_version(lib):
     from lizard_cuda import _lib
-    assert lib.lz_abi_version() == _lib.ABI_VERSION == 1
+    assert lib.lz_abi_version() == _lib.ABI_VERSION == 2
 
 
 def test_buffer_size_queries(lib):
@@ -56,24 +56,53 @@ def _fake(n=1):
 
 
 def test_gla_fwd_rejects_null_pointers(lib):
-    rc = lib.lz_gla_fwd(None, None, None, None, 0, None, None, 0, 1, 1, 8, 8, 8, 64, None)
+    rc = lib.lz_gla_fwd(None, None, None, None, 0, None, None, 0, None, 0, 1, 1, 8, 8, 8, 64, None)
     assert rc == 1
     assert b"null" in lib.lz_last_error_string()
 
 
 def test_gla_fwd_rejects_bad_sizes(lib):
     p = _fake(5)
-    assert lib.lz_gla_fwd(*p[:4], 0, p[4], None, 0, 0, 1, 8, 8, 8, 64, None) == 1
-    assert lib.lz_gla_fwd(*p[:4], 0, p[4], None, 0, 1, 1, 8, 8, 8, 0, None) == 1
-    assert lib.lz_gla_fwd(*p[:4], 0, p[4], None, 0, 1, 1, 8, 300, 8, 64, None) == 2
+    assert lib.lz_gla_fwd(*p[:4], 0, p[4], None, 0, None, 0, 0, 1, 8, 8, 8, 64, None) == 1
+    assert lib.lz_gla_fwd(*p[:4], 0, p[4], None, 0, None, 0, 1, 1, 8, 8, 8, 0, None) == 1
+    assert lib.lz_gla_fwd(*p[:4], 0, p[4], None, 0, None, 0, 1, 1, 8, 300, 8, 64, None) == 2
     assert b"feature dim" in lib.lz_last_error_string()
 
 
 def test_gla_fwd_rejects_small_saved_buffer(lib):
     p = _fake(6)
-    rc = lib.lz_gla_fwd(*p[:4], 0, p[4], p[5], 16, 1, 1, 8, 8, 8, 64, None)
+    rc = lib.lz_gla_fwd(*p[:4], 0, p[4], p[5], 16, None, 0, 1, 1, 8, 8, 8, 64, None)
     assert rc == 4
     assert b"saved" in lib.lz_last_error_string()
+
+
+def test_schedule_setting_and_forward_workspace(lib):
+    # one chunk: both schedules are the same work, the walk is planned
+    assert lib.lz_gla_fwd_workspace_bytes(1, 32, 64, 64, 64, 64) == 0
+    # 32 heads of 2048 tokens: too few chains for a walk, chunk-parallel planned
+    auto = lib.lz_gla_fwd_workspace_bytes(1, 32, 2048, 64, 64, 64)
+    assert auto >= 32 * 32 * 64 * 64 * 4
+    # many heads: the walk
+    assert lib.lz_gla_fwd_workspace_bytes(8, 32, 2048, 128, 128, 64) == 0
+    assert lib.lz_gla_set_schedule(1) == 0
+    try:
+        assert lib.lz_gla_fwd_workspace_bytes(1, 32, 2048, 64, 64, 64) == 0
+        walk_bwd = lib.lz_gla_bwd_workspace_bytes(1, 32, 2048, 64, 64, 64)
+        assert lib.lz_gla_set_schedule(2) == 1
+        assert lib.lz_gla_fwd_workspace_bytes(8, 32, 2048, 128, 128, 64) > 0
+        assert lib.lz_gla_bwd_workspace_bytes(1, 32, 2048, 64, 64, 64) > walk_bwd
+        assert lib.lz_gla_set_schedule(7) == -1
+        assert b"schedule" in lib.lz_last_error_string()
+        assert lib.lz_gla_set_schedule(2) == 2
+    finally:
+        lib.lz_gla_set_schedule(0)
+
+
+def test_gla_fwd_rejects_missing_workspace(lib):
+    p = _fake(5)
+    rc = lib.lz_gla_fwd(*p[:4], 0, p[4], None, 0, None, 0, 1, 32, 2048, 64, 64, 64, None)
+    assert rc == 4
+    assert b"workspace" in lib.lz_last_error_string()
 
 
 def test_gla_bwd_rejects_bad_grad_dtype(lib):
@@ -96,7 +125,7 @@ def test_swa_rejects_bad_window_and_sinks(lib):
 
 
 def test_error_string_is_cleared_by_a_new_call(lib):
-    lib.lz_gla_fwd(None, None, None, None, 0, None, None, 0, 1, 1, 8, 8, 8, 64, None)
+    lib.lz_gla_fwd(None, None, None, None, 0, None, None, 0, None, 0, 1, 1, 8, 8, 8, 64, None)
     assert lib.lz_last_error_string() != b""
     lib.lz_abi_version()
     p = _fake(5)

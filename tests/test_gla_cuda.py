@@ -1,4 +1,8 @@
-"""GLA kernels on the GPU against the reference fixtures and the CPU oracle."""
+"""GLA kernels on the GPU against the reference fixtures and the CPU oracle.
+
+Every test runs under both schedules of the kernels: the sequential walk
+over each head's chunks and the chunk-parallel schedule."""
+import functools
 import math
 
 import pytest
@@ -18,6 +22,14 @@ DEV = "cuda"
 def _lib(built_lib):
     import lizard_cuda
     lizard_cuda.load()
+
+
+@pytest.fixture(autouse=True, params=["walk", "split"])
+def schedule(request, _lib):
+    from lizard_cuda import _lib as binding
+    prev = binding.set_schedule(request.param)
+    yield request.param
+    binding.set_schedule(prev)
 
 
 def cuda_gla(fq, fk, v, lg, dy=None, chunk=64):
@@ -66,6 +78,19 @@ def baseline_inputs(B, H, L, Fd, D, per_head, seed=0, device=DEV):
     return fq, fk, v, lg, dy
 
 
+CFG2_HEADS = ((0, 0), (3, 17), (5, 31), (7, 8))
+
+
+@functools.lru_cache(maxsize=None)
+def _cfg2_reference():
+    fq, fk, v, lg, _ = baseline_inputs(8, 32, 2048, 128, 128, per_head=True)
+    refs = {}
+    for b, h in CFG2_HEADS:
+        sl = (slice(b, b + 1), slice(h, h + 1))
+        refs[b, h] = oracle_gla(fq[sl], fk[sl], v[sl], lg[sl])[0]
+    return refs
+
+
 def test_gla_config2_forward_sampled_heads():
     """B=8, L=2048, H=32, F=D=128, per-head gate; 4 (b, h) slices checked."""
     import lizard_cuda
@@ -73,10 +98,21 @@ def test_gla_config2_forward_sampled_heads():
     with torch.no_grad():
         y = lizard_cuda.gla(fq, fk, v, lg)
     torch.cuda.synchronize()
-    for b, h in ((0, 0), (3, 17), (5, 31), (7, 8)):
+    for (b, h), ref in _cfg2_reference().items():
         sl = (slice(b, b + 1), slice(h, h + 1))
-        ref, _ = oracle_gla(fq[sl], fk[sl], v[sl], lg[sl])
         assert_output(y[sl], ref, f"cfg2 y[{b},{h}]")
+
+
+@functools.lru_cache(maxsize=None)
+def _cfg3_reference():
+    fq, fk, v, lg, dy = baseline_inputs(1, 32, 2048, 64, 64, per_head=False)
+    ys, dfq, dfk, dv, dlg = [], [], [], [], torch.zeros(1, 2048, dtype=torch.float32)
+    for h0 in range(0, 32, 8):
+        sl = (slice(None), slice(h0, h0 + 8))
+        r, (a, b_, c, d) = oracle_gla(fq[sl], fk[sl], v[sl], lg, dy[sl].bfloat16())
+        ys.append(r), dfq.append(a), dfk.append(b_), dv.append(c)
+        dlg += d
+    return torch.cat(ys, 1), (torch.cat(dfq, 1), torch.cat(dfk, 1), torch.cat(dv, 1), dlg)
 
 
 def test_gla_config3_forward_backward_all_heads():
@@ -84,16 +120,38 @@ def test_gla_config3_forward_backward_all_heads():
     fq, fk, v, lg, dy = baseline_inputs(1, 32, 2048, 64, 64, per_head=False)
     y, grads = cuda_gla(fq, fk, v, lg, dy)
     torch.cuda.synchronize()
-    ys, dfq, dfk, dv, dlg = [], [], [], [], torch.zeros(1, 2048, dtype=torch.float32)
-    for h0 in range(0, 32, 8):
-        sl = (slice(None), slice(h0, h0 + 8))
-        r, (a, b_, c, d) = oracle_gla(fq[sl], fk[sl], v[sl], lg, dy[sl].bfloat16())
-        ys.append(r), dfq.append(a), dfk.append(b_), dv.append(c)
-        dlg += d
-    assert_output(y, torch.cat(ys, 1), "cfg3 y")
-    for got, ref, n in zip(grads, (torch.cat(dfq, 1), torch.cat(dfk, 1), torch.cat(dv, 1), dlg),
-                           GRAD_NAMES):
+    ref_y, ref_grads = _cfg3_reference()
+    assert_output(y, ref_y, "cfg3 y")
+    for got, ref, n in zip(grads, ref_grads, GRAD_NAMES):
         assert_grad(got, ref, f"cfg3 {n}")
+
+
+def test_gla_schedules_agree():
+    """Both schedules on one input: outputs and all gradients within bf16 rounding."""
+    from lizard_cuda import _lib as binding
+    fq, fk, v, lg, dy = baseline_inputs(2, 3, 777, 64, 48, per_head=False, seed=11)
+    prev = binding.set_schedule("walk")
+    try:
+        yw, gw = cuda_gla(fq, fk, v, lg, dy)
+        binding.set_schedule("split")
+        ys, gs = cuda_gla(fq, fk, v, lg, dy)
+    finally:
+        binding.set_schedule(prev)
+    assert_output(ys, yw.float(), "split vs walk y")
+    for a, b, n in zip(gs, gw, GRAD_NAMES):
+        assert_grad(a, b.float(), f"split vs walk {n}")
+
+
+def test_gla_many_chunks_against_recurrent_float64():
+    """256 chunks of one head (L=16384), F=D=64, per-token gate: the scan over
+    chunks against the float64 recurrence."""
+    import lizard_cuda
+    fq, fk, v, lg, _ = baseline_inputs(1, 1, 16384, 64, 64, per_head=False, seed=9)
+    with torch.no_grad():
+        y = lizard_cuda.gla(fq, fk, v, lg)
+    ref = orc.gla_recurrent(fq.double().cpu(), fk.double().cpu(), v.double().cpu(),
+                            lg.double().cpu())
+    assert_output(y, ref, "L=16384 y")
 
 
 def test_gla_long_sequence_against_recurrent_float64():
@@ -180,8 +238,11 @@ def test_gla_poisoned_outputs_are_fully_written():
     y = torch.full((B, H, L, D), float("nan"), device=DEV, dtype=torch.bfloat16)
     nbytes = lib.lz_gla_saved_bytes(B, H, L, Fd, D, 64)
     saved = torch.full((nbytes // 4,), float("nan"), device=DEV, dtype=torch.float32)
+    wbytes = lib.lz_gla_fwd_workspace_bytes(B, H, L, Fd, D, 64)
+    ws = torch.full((wbytes // 4 + 1,), float("nan"), device=DEV, dtype=torch.float32)
     rc = lib.lz_gla_fwd(_lib.ptr(fq), _lib.ptr(fk), _lib.ptr(v), _lib.ptr(lg), 1, _lib.ptr(y),
-                        _lib.ptr(saved), nbytes, B, H, L, Fd, D, 64, _lib.stream_of(fq))
+                        _lib.ptr(saved), nbytes, _lib.ptr(ws), wbytes, B, H, L, Fd, D, 64,
+                        _lib.stream_of(fq))
     _lib.check(rc, "gla forward")
     torch.cuda.synchronize()
     assert torch.isfinite(y).all()
