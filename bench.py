@@ -207,7 +207,12 @@ def make_cpu_inputs(torch):
 # ---------------------------------------------------------------- ours
 def secondary(torch, lizard_cuda, device, steps=50, warmup=5):
     """Config 3 (B=1, L=2048, H=32, F=D=64): GLA fwd+bwd with a per-token gate
-    and SWA fwd+bwd (window 64, 4 sinks); device ms per step."""
+    and SWA fwd+bwd (window 64, 4 sinks); device ms per step.
+
+    "ms" is eager (one Python call per step, host launch overhead included);
+    "ms_graph" replays the same step captured in a CUDA graph, which shows the
+    device time without the host in the way (back to back: the 8 MB inputs stay
+    in L2); "ms_graph_l2_flushed" flushes L2 before every replay."""
     import torch.nn.functional as F
     g = torch.Generator(device=device).manual_seed(7)
     Bs, Hs, Ls, Ds = 1, 32, 2048, 64
@@ -238,8 +243,45 @@ def secondary(torch, lizard_cuda, device, steps=50, warmup=5):
         e.record()
         torch.cuda.synchronize()
         ms = s.elapsed_time(e) / steps
-        out[name] = {"ms": ms, "tokens_per_s": Bs * Ls / (ms / 1e3),
-                     "launches_per_step": (lizard_cuda.launch_count() - n0) / steps}
+        launches = (lizard_cuda.launch_count() - n0) / steps
+
+        def step():
+            for t in leaves:
+                t.grad = None
+            fn()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        for _ in range(warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(steps):
+            graph.replay()
+        e.record()
+        torch.cuda.synchronize()
+        msg = s.elapsed_time(e) / steps
+        # the same replays with L2 flushed before each (a 256 MB write, untimed)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+        tot = 0.0
+        for _ in range(steps):
+            flush.fill_(1)
+            s.record()
+            graph.replay()
+            e.record()
+            e.synchronize()
+            tot += s.elapsed_time(e)
+        del graph, flush
+        msf = tot / steps
+        out[name] = {"ms": ms, "tokens_per_s": Bs * Ls / (ms / 1e3), "ms_graph": msg,
+                     "tokens_per_s_graph": Bs * Ls / (msg / 1e3), "ms_graph_l2_flushed": msf,
+                     "launches_per_step": launches}
 
     timed("gla_fwd_bwd_cfg3", lambda: lizard_cuda.gla(fq, fk, v, lg).backward(dy),
           (fq, fk, v, lg))

@@ -122,7 +122,9 @@ int lz_gla_bwd(const void* fq, const void* fk, const void* v,
 /* SWA                                                                      */
 /* ------------------------------------------------------------------------ */
 
-/* Bytes of the opaque buffer lz_swa_fwd fills (log-sum-exp per row). */
+/* Bytes of the opaque buffer lz_swa_fwd fills for lz_swa_bwd: the log-sum-exp
+ * per row (the reference's lse, src/kernels/swa.py:145-155) and the output in
+ * fp32, from which the backward forms delta. */
 size_t lz_swa_saved_bytes(int B, int H, int L, int D);
 
 /* Bytes of scratch lz_swa_bwd needs (delta per row, per-block sink partials). */

@@ -125,9 +125,8 @@ extern "C" int lz_gla_bwd(const void* fq, const void* fk, const void* v, const f
 }
 
 extern "C" size_t lz_swa_saved_bytes(int B, int H, int L, int D) {
-  (void)D;
-  if (B < 1 || H < 1 || L < 1) return 0;
-  return lz::swa_saved_bytes(B, H, L);
+  if (B < 1 || H < 1 || L < 1 || D < 1) return 0;
+  return lz::swa_saved_layout(B, H, L, D, nullptr, nullptr);
 }
 
 extern "C" size_t lz_swa_bwd_workspace_bytes(int B, int H, int L, int D, int n_meta) {
@@ -151,16 +150,18 @@ extern "C" int lz_swa_fwd(const void* q, const void* k, const void* v, const voi
   LZ_REQUIRE(n_meta <= lz::kMaxMeta, LZ_ERR_UNSUPPORTED, "more than 32 sink logits");
   LZ_REQUIRE(window >= 1, LZ_ERR_INVALID_ARGUMENT, "window must be >= 1");
   LZ_REQUIRE(D <= 128, LZ_ERR_UNSUPPORTED, "head dim above 128 is not supported");
-  float* lse = nullptr;
+  lz::SwaSaved sv;
   if (saved) {
-    LZ_REQUIRE(saved_bytes >= lz::swa_saved_bytes(B, H, L), LZ_ERR_WORKSPACE,
-               "saved buffer too small");
-    lse = static_cast<float*>(saved);
+    LZ_REQUIRE(saved_bytes >= lz::swa_saved_layout(B, H, L, D, nullptr, nullptr),
+               LZ_ERR_WORKSPACE, "saved buffer too small");
+    LZ_REQUIRE(lz::aligned16(saved), LZ_ERR_INVALID_ARGUMENT,
+               "saved buffer must be 16-byte aligned");
+    lz::swa_saved_layout(B, H, L, D, static_cast<unsigned char*>(saved), &sv);
   }
   return lz::swa_fwd(static_cast<const bf16*>(q), static_cast<const bf16*>(k),
                      static_cast<const bf16*>(v), static_cast<const bf16*>(q_lo),
                      static_cast<const bf16*>(k_lo), meta, n_meta, window,
-                     static_cast<bf16*>(y), lse, B, H, L, D, static_cast<cudaStream_t>(stream));
+                     static_cast<bf16*>(y), sv, B, H, L, D, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int lz_swa_bwd(const void* q, const void* k, const void* v, const void* q_lo,
@@ -182,15 +183,19 @@ extern "C" int lz_swa_bwd(const void* q, const void* k, const void* v, const voi
   LZ_REQUIRE(grad_dtype == LZ_DTYPE_F32 || grad_dtype == LZ_DTYPE_BF16, LZ_ERR_INVALID_ARGUMENT,
              "grad_dtype must be LZ_DTYPE_F32 or LZ_DTYPE_BF16");
   LZ_REQUIRE(D <= 128, LZ_ERR_UNSUPPORTED, "head dim above 128 is not supported");
-  LZ_REQUIRE(saved_bytes >= lz::swa_saved_bytes(B, H, L), LZ_ERR_WORKSPACE,
-             "saved buffer too small");
+  LZ_REQUIRE(saved_bytes >= lz::swa_saved_layout(B, H, L, D, nullptr, nullptr),
+             LZ_ERR_WORKSPACE, "saved buffer too small");
   LZ_REQUIRE(workspace_bytes >= lz::swa_work_layout(B, H, L, n_meta, nullptr, nullptr),
              LZ_ERR_WORKSPACE, "workspace too small");
+  LZ_REQUIRE(lz::aligned16(saved), LZ_ERR_INVALID_ARGUMENT,
+             "saved buffer must be 16-byte aligned");
+  lz::SwaSaved sv;
+  lz::swa_saved_layout(B, H, L, D, (unsigned char*)const_cast<void*>(saved), &sv);
   lz::SwaWork wk;
   lz::swa_work_layout(B, H, L, n_meta, static_cast<unsigned char*>(workspace), &wk);
   return lz::swa_bwd(static_cast<const bf16*>(q), static_cast<const bf16*>(k),
                      static_cast<const bf16*>(v), static_cast<const bf16*>(q_lo),
                      static_cast<const bf16*>(k_lo), meta, n_meta, window,
-                     static_cast<const float*>(saved), static_cast<const bf16*>(dy), dq, dk, dv,
+                     sv, static_cast<const bf16*>(dy), dq, dk, dv,
                      grad_dtype, dmeta, wk, B, H, L, D, static_cast<cudaStream_t>(stream));
 }

@@ -168,6 +168,62 @@ __device__ __forceinline__ void store_grad(void* p, size_t i, float x, int dtype
     store_val<float>(p, i, x);
 }
 
+// Stores x0 (element i) and x1 (element i + 1, when has1) of a gradient row.
+__device__ __forceinline__ void store_grad2(void* p, size_t i, float x0, float x1, bool has1,
+                                            bool pair, int dtype) {
+  if (pair && has1) {
+    if (dtype == LZ_DTYPE_BF16)
+      *reinterpret_cast<__nv_bfloat162*>(static_cast<bf16*>(p) + i) = __floats2bfloat162_rn(x0, x1);
+    else
+      *reinterpret_cast<float2*>(static_cast<float*>(p) + i) = make_float2(x0, x1);
+  } else {
+    store_grad(p, i, x0, dtype);
+    if (has1) store_grad(p, i + 1, x1, dtype);
+  }
+}
+
+// out[r] = sum_d a[r][d] * b[r][d] for the 64 rows of a block (0 for r >=
+// nrows), a bf16 and b fp32, both [rows, D] row-major and already offset to
+// the block's first row. 128 threads (4 warps x 16 rows). With vec (D % 4 == 0,
+// a 8-byte and b 16-byte aligned) a row is split over 16 or 32 lanes that
+// load 4 elements each; loads of several rows are in flight at once.
+__device__ __forceinline__ void block_row_dots64(const bf16* __restrict__ a,
+                                                 const float* __restrict__ b, int nrows, int D,
+                                                 bool vec, float* out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (vec && D <= 128) {
+    const int hw = D <= 64 ? 16 : 32;  // lanes per row
+    const int sub = lane / hw, l = lane % hw;
+#pragma unroll 4
+    for (int rr = 0; rr < 16; rr += 32 / hw) {
+      const int r = warp * 16 + rr + sub;
+      float acc = 0.f;
+      if (r < nrows) {
+        for (int d = 4 * l; d < D; d += 4 * hw) {
+          const uint2 x = *reinterpret_cast<const uint2*>(a + (size_t)r * D + d);
+          const float4 w = *reinterpret_cast<const float4*>(b + (size_t)r * D + d);
+          acc += bf16_lo(x.x) * w.x + bf16_hi(x.x) * w.y + bf16_lo(x.y) * w.z +
+                 bf16_hi(x.y) * w.w;
+        }
+      }
+      for (int o = hw / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (l == 0) out[r] = acc;
+    }
+  } else {
+#pragma unroll 2
+    for (int rr = 0; rr < 16; ++rr) {
+      const int r = warp * 16 + rr;
+      float acc = 0.f;
+      if (r < nrows)
+        for (int d = lane; d < D; d += 32)
+          acc += __bfloat162float(a[(size_t)r * D + d]) * b[(size_t)r * D + d];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) out[r] = acc;
+    }
+  }
+}
+
 __device__ __forceinline__ float quad_sum(float x) {
   x += __shfl_xor_sync(0xffffffffu, x, 1);
   x += __shfl_xor_sync(0xffffffffu, x, 2);

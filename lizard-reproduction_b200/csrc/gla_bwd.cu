@@ -2,6 +2,8 @@
 //   1. delta_i = dy_i . y_i (fp32 y saved by the forward; gla.py:242)
 //   2. reverse walk over chunks writing the state gradient leaving each chunk,
 //      dS_n (bf16) and dz_n (fp32)                       (gla.py:104-132)
+//      (with the chunk-parallel schedule, 1 and 2 are gla_split.cu's
+//      increment and scan kernels instead)
 //   3. one CTA per (chunk, batch*head): dfq, dfk, dv and dG = sum_f(fq dfq -
 //      fk dfk) for its 64 rows                         (gla.py:135-194, 254)
 //   4. dlog_gamma = reverse cumsum of dG (summed over heads for a per-token
@@ -162,9 +164,21 @@ gla_bwd_state_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ dy,
 }
 
 // ------------------------------------------------------ 3. per-chunk gradients
+// One CTA of 8 warps per (chunk, batch*head). Warp w owns the 16-row strip
+// (w & 3) of the chunk and the column half (w >> 2) of every output, so the
+// per-warp accumulators stay small; the chunk's S and dS tiles are fetched
+// while the scores are formed. Same algebra as gla.py:135-194:
+//   a    = bf16(s * decay), s = fq fk^T, decay_it = exp(G_i - G_t), t <= i
+//   da   = (dy v^T - delta) / den, dad = da * decay
+//   dv   = (a / den)^T dy + bf16(fk * ks) dS
+//   dfq  = qs/den * (dy S^T - delta z) + dad fk
+//   dfk  = ks * (v dS^T - dz) + dad^T fq
+//   dG_i = fq_i . dfq_i - fk_i . dfk_i                     (gla.py:254)
+// with qs = exp(G_i - start), ks = exp(end - G_i). The chunk's sum of dG goes
+// to dGt for the log-gate kernel.
 template <int FP, int DP>
 struct ChunkSmem {
-  static constexpr int FB = FP < 64 ? FP : 64;  // feature block for S / dS
+  static constexpr int FB = FP < 64 ? FP : 64;  // feature block of S / dS
   static constexpr int LDF = FP + 8, LDD = DP + 8, LDT = kC + 8;
   static constexpr size_t q = 0;
   static constexpr size_t k = q + (size_t)kC * LDF * 2;
@@ -174,13 +188,15 @@ struct ChunkSmem {
   static constexpr size_t dS = s + (size_t)FB * LDD * 2;
   static constexpr size_t dad = dS + (size_t)FB * LDD * 2;
   static constexpr size_t aden = dad + (size_t)kC * LDT * 2;
-  static constexpr size_t rows = aden + (size_t)kC * LDT * 2;  // g, den, delta
+  static constexpr size_t rows = aden + (size_t)kC * LDT * 2;  // g, 1/den, delta
   static constexpr size_t zz = rows + 3 * kC * 4;               // z, dz
-  static constexpr size_t bytes = zz + 2 * FP * 4;
+  static constexpr size_t dgp = zz + 2 * FP * 4;                // dG of each column half
+  static constexpr size_t red = dgp + 2 * kC * 4;
+  static constexpr size_t bytes = red + 16;
 };
 
 template <int FP, int DP>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(256, (FP <= 64 && DP <= 64) ? 2 : 1)
 gla_bwd_chunk_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
                      const bf16* __restrict__ v, const bf16* __restrict__ dy,
                      const float* __restrict__ G, const float* __restrict__ den,
@@ -188,10 +204,12 @@ gla_bwd_chunk_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
                      const float* __restrict__ Z, const bf16* __restrict__ dS,
                      const float* __restrict__ dZ, void* __restrict__ dfq,
                      void* __restrict__ dfk, void* __restrict__ dv, int gdt,
-                     float* __restrict__ dG, int L, int F, int D, int NT, int vec_f, int vec_d) {
+                     float* __restrict__ dG, float* __restrict__ dGt, int L, int F, int D, int NT,
+                     int vec_f, int vec_d, int s_seeded, int ds_seeded) {
   using SM = ChunkSmem<FP, DP>;
   constexpr int FB = SM::FB, LDF = SM::LDF, LDD = SM::LDD, LDT = SM::LDT;
-  constexpr int NTD = DP / 8, NTF = FB / 8;
+  constexpr int NDH = DP / 16;  // n8 tiles of one column half of dv
+  constexpr int NFH = FB / 16;  // n8 tiles of one column half of a feature block
   extern __shared__ __align__(128) unsigned char smem[];
   bf16* sQ = reinterpret_cast<bf16*>(smem + SM::q);
   bf16* sK = reinterpret_cast<bf16*>(smem + SM::k);
@@ -202,57 +220,69 @@ gla_bwd_chunk_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
   bf16* sDad = reinterpret_cast<bf16*>(smem + SM::dad);
   bf16* sAden = reinterpret_cast<bf16*>(smem + SM::aden);
   float* sG = reinterpret_cast<float*>(smem + SM::rows);
-  float* sDen = sG + kC;
+  float* sRden = sG + kC;
   float* sDel = sG + 2 * kC;
   float* sZ = reinterpret_cast<float*>(smem + SM::zz);
   float* sDZ = sZ + FP;
+  float* sDgp = reinterpret_cast<float*>(smem + SM::dgp);
+  float* sRed = reinterpret_cast<float*>(smem + SM::red);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, cq = lane & 3;
+  const int strip = warp & 3, half = warp >> 2;
   const int n = blockIdx.x % NT, bh = blockIdx.x / NT;
   const int r0 = n * kC, nvalid = min(kC, L - r0);
   const size_t rowF = (size_t)bh * L * F, rowD = (size_t)bh * L * D;
   const size_t chunk = (size_t)bh * NT + n;
+  const bool with_s = n > 0 || s_seeded;       // state entering the chunk is not zero
+  const bool with_ds = n + 1 < NT || ds_seeded;  // gradient leaving the chunk is not zero
 
-  stage_tile<kC, FP, 128>(sQ, LDF, fq + rowF, F, r0, L, 0, F, vec_f);
-  stage_tile<kC, FP, 128>(sK, LDF, fk + rowF, F, r0, L, 0, F, vec_f);
-  stage_tile<kC, DP, 128>(sV, LDD, v + rowD, D, r0, L, 0, D, vec_d);
-  stage_tile<kC, DP, 128>(sDy, LDD, dy + rowD, D, r0, L, 0, D, vec_d);
+  stage_tile<kC, FP, 256>(sQ, LDF, fq + rowF, F, r0, L, 0, F, vec_f);
+  stage_tile<kC, FP, 256>(sK, LDF, fk + rowF, F, r0, L, 0, F, vec_f);
+  stage_tile<kC, DP, 256>(sV, LDD, v + rowD, D, r0, L, 0, D, vec_d);
+  stage_tile<kC, DP, 256>(sDy, LDD, dy + rowD, D, r0, L, 0, D, vec_d);
   cp_async_commit();
+  auto stage_state = [&](int fo) {
+    if (with_s) stage_tile<FB, DP, 256>(sS, LDD, S + chunk * F * D, D, fo, F, 0, D, vec_d);
+    if (with_ds) stage_tile<FB, DP, 256>(sDS, LDD, dS + chunk * F * D, D, fo, F, 0, D, vec_d);
+    cp_async_commit();
+  };
+  stage_state(0);
   if (tid < kC) {
     const int r = r0 + tid;
     sG[tid] = r < L ? G[(size_t)bh * L + r] : 0.f;
-    sDen[tid] = r < L ? fmaxf(den[(size_t)bh * L + r], kTiny) : 1.f;
+    sRden[tid] = r < L ? 1.f / fmaxf(den[(size_t)bh * L + r], kTiny) : 1.f;
     sDel[tid] = r < L ? delta[(size_t)bh * L + r] : 0.f;
   }
-  for (int f = tid; f < FP; f += 128) {
-    sZ[f] = f < F ? Z[chunk * F + f] : 0.f;
-    sDZ[f] = f < F ? dZ[chunk * F + f] : 0.f;
+  for (int f = tid; f < FP; f += 256) {
+    sZ[f] = (with_s && f < F) ? Z[chunk * F + f] : 0.f;
+    sDZ[f] = (with_ds && f < F) ? dZ[chunk * F + f] : 0.f;
   }
-  cp_async_wait_all();
+  asm volatile("cp.async.wait_group 1;\n" ::);
   __syncthreads();
 
   const float start = n > 0 ? G[(size_t)bh * L + r0 - 1] : 0.f;
   const float end = sG[nvalid - 1];
-  const int i0 = 16 * warp + gq, i1 = i0 + 8;  // query rows; also key rows t
+  const int i0 = 16 * strip + gq, i1 = i0 + 8;  // rows of this thread (queries or keys)
   const float gi0 = sG[i0], gi1 = sG[i1];
-  const float den0 = sDen[i0], den1 = sDen[i1];
+  const float rd0 = sRden[i0], rd1 = sRden[i1];
   const float del0 = sDel[i0], del1 = sDel[i1];
+  const int tc = 32 * half;  // this warp's 32 key columns in the score phase
 
-  // (1) s = fq fk^T and p = dy v^T for this warp's rows
-  float sacc[8][4], pacc[8][4];
+  // (1) s = fq fk^T and p = dy v^T: 16 rows x 32 columns
+  float sacc[4][4], pacc[4][4];
 #pragma unroll
-  for (int c = 0; c < 8; ++c)
+  for (int c = 0; c < 4; ++c)
 #pragma unroll
     for (int e = 0; e < 4; ++e) sacc[c][e] = pacc[c][e] = 0.f;
 #pragma unroll 2
   for (int k0 = 0; k0 < FP; k0 += 16) {
     uint32_t a[4];
-    lda_rm(a, sQ, LDF, 16 * warp, k0);
+    lda_rm(a, sQ, LDF, 16 * strip, k0);
 #pragma unroll
-    for (int np = 0; np < 4; ++np) {
+    for (int np = 0; np < 2; ++np) {
       uint32_t bb[4];
-      ldb_nk(bb, sK, LDF, 16 * np, k0);
+      ldb_nk(bb, sK, LDF, tc + 16 * np, k0);
       mma16816(sacc[2 * np], a, bb[0], bb[1]);
       mma16816(sacc[2 * np + 1], a, bb[2], bb[3]);
     }
@@ -260,20 +290,19 @@ gla_bwd_chunk_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
 #pragma unroll 2
   for (int k0 = 0; k0 < DP; k0 += 16) {
     uint32_t a[4];
-    lda_rm(a, sDy, LDD, 16 * warp, k0);
+    lda_rm(a, sDy, LDD, 16 * strip, k0);
 #pragma unroll
-    for (int np = 0; np < 4; ++np) {
+    for (int np = 0; np < 2; ++np) {
       uint32_t bb[4];
-      ldb_nk(bb, sV, LDD, 16 * np, k0);
+      ldb_nk(bb, sV, LDD, tc + 16 * np, k0);
       mma16816(pacc[2 * np], a, bb[0], bb[1]);
       mma16816(pacc[2 * np + 1], a, bb[2], bb[3]);
     }
   }
-  // (2) a (bf16-rounded), da = (p - delta)/den, dad = da * decay
-  uint32_t adad[4][4];
+  // (2) dad = (p - delta)/den * decay and a/den, both bf16, into shared memory
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    const int t = 8 * nt + 2 * cq;
+  for (int nt = 0; nt < 4; ++nt) {
+    const int t = tc + 8 * nt + 2 * cq;
     float dadv[4], adv[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -282,78 +311,76 @@ gla_bwd_chunk_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
       const bool m = tt <= i && i < nvalid;
       const float dec = m ? __expf(((e < 2) ? gi0 : gi1) - sG[tt]) : 0.f;
       const float a = round_bf16(sacc[nt][e] * dec);
-      const float dn = (e < 2) ? den0 : den1;
-      const float da = m ? (pacc[nt][e] - ((e < 2) ? del0 : del1)) / dn : 0.f;
+      const float rd = (e < 2) ? rd0 : rd1;
+      const float da = m ? (pacc[nt][e] - ((e < 2) ? del0 : del1)) * rd : 0.f;
       dadv[e] = da * dec;
-      adv[e] = a / dn;
+      adv[e] = a * rd;
     }
-    const uint32_t p0 = pack_bf16(dadv[0], dadv[1]), p1 = pack_bf16(dadv[2], dadv[3]);
-    adad[nt >> 1][(nt & 1) * 2 + 0] = p0;
-    adad[nt >> 1][(nt & 1) * 2 + 1] = p1;
-    *reinterpret_cast<uint32_t*>(sDad + i0 * LDT + t) = p0;
-    *reinterpret_cast<uint32_t*>(sDad + i1 * LDT + t) = p1;
+    *reinterpret_cast<uint32_t*>(sDad + i0 * LDT + t) = pack_bf16(dadv[0], dadv[1]);
+    *reinterpret_cast<uint32_t*>(sDad + i1 * LDT + t) = pack_bf16(dadv[2], dadv[3]);
     *reinterpret_cast<uint32_t*>(sAden + i0 * LDT + t) = pack_bf16(adv[0], adv[1]);
     *reinterpret_cast<uint32_t*>(sAden + i1 * LDT + t) = pack_bf16(adv[2], adv[3]);
   }
   __syncthreads();
 
-  // (3) dv (intra) = (a/den)^T dy for key rows t of this warp
-  float dvacc[NTD][4];
+  // (3) dv (intra) = (a/den)^T dy: key rows of the strip, value columns of the half
+  const int dc = half * (DP / 2);
+  float dvacc[NDH][4];
 #pragma unroll
-  for (int c = 0; c < NTD; ++c)
+  for (int c = 0; c < NDH; ++c)
 #pragma unroll
     for (int e = 0; e < 4; ++e) dvacc[c][e] = 0.f;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     uint32_t a[4];
-    lda_tr(a, sAden, LDT, 16 * warp, 16 * j);
+    lda_tr(a, sAden, LDT, 16 * strip, 16 * j);
 #pragma unroll
-    for (int np = 0; np < NTD / 2; ++np) {
+    for (int np = 0; np < NDH / 2; ++np) {
       uint32_t bb[4];
-      ldb_kn(bb, sDy, LDD, 16 * j, 16 * np);
+      ldb_kn(bb, sDy, LDD, 16 * j, dc + 16 * np);
       mma16816(dvacc[2 * np], a, bb[0], bb[1]);
       mma16816(dvacc[2 * np + 1], a, bb[2], bb[3]);
     }
   }
 
   const bool v0 = i0 < nvalid, v1 = i1 < nvalid;
-  const float qsd0 = v0 ? __expf(gi0 - start) / den0 : 0.f;
-  const float qsd1 = v1 ? __expf(gi1 - start) / den1 : 0.f;
+  const float qsd0 = v0 ? __expf(gi0 - start) * rd0 : 0.f;
+  const float qsd1 = v1 ? __expf(gi1 - start) * rd1 : 0.f;
   const float ks0 = v0 ? __expf(end - gi0) : 0.f;
   const float ks1 = v1 ? __expf(end - gi1) : 0.f;
+  const bool fpair = (F & 1) == 0;
   float dg0 = 0.f, dg1 = 0.f;
 
   for (int fb = 0; fb < FP / FB; ++fb) {
     const int fo = fb * FB;
-    stage_tile<FB, DP, 128>(sS, LDD, S + chunk * F * D, D, fo, F, 0, D, vec_d);
-    stage_tile<FB, DP, 128>(sDS, LDD, dS + chunk * F * D, D, fo, F, 0, D, vec_d);
-    cp_async_commit();
+    if (fb > 0) stage_state(fo);
     cp_async_wait_all();
     __syncthreads();
+    const int fcl = half * (FB / 2);  // this warp's columns inside the feature block
     // (4) dfq = qs/den (dy S^T - delta z) + dad fk
     {
-      float acc[NTF][4];
+      float acc[NFH][4];
 #pragma unroll
-      for (int c = 0; c < NTF; ++c)
+      for (int c = 0; c < NFH; ++c)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[c][e] = 0.f;
-      if (n > 0) {
+      if (with_s) {
 #pragma unroll 2
         for (int k0 = 0; k0 < DP; k0 += 16) {
           uint32_t a[4];
-          lda_rm(a, sDy, LDD, 16 * warp, k0);
+          lda_rm(a, sDy, LDD, 16 * strip, k0);
 #pragma unroll
-          for (int np = 0; np < NTF / 2; ++np) {
+          for (int np = 0; np < NFH / 2; ++np) {
             uint32_t bb[4];
-            ldb_nk(bb, sS, LDD, 16 * np, k0);
+            ldb_nk(bb, sS, LDD, fcl + 16 * np, k0);
             mma16816(acc[2 * np], a, bb[0], bb[1]);
             mma16816(acc[2 * np + 1], a, bb[2], bb[3]);
           }
         }
       }
 #pragma unroll
-      for (int nt = 0; nt < NTF; ++nt) {
-        const int f = fo + 8 * nt + 2 * cq;
+      for (int nt = 0; nt < NFH; ++nt) {
+        const int f = fo + fcl + 8 * nt + 2 * cq;
         acc[nt][0] = qsd0 * (acc[nt][0] - del0 * sZ[f]);
         acc[nt][1] = qsd0 * (acc[nt][1] - del0 * sZ[f + 1]);
         acc[nt][2] = qsd1 * (acc[nt][2] - del1 * sZ[f]);
@@ -361,55 +388,53 @@ gla_bwd_chunk_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
+        uint32_t a[4];
+        lda_rm(a, sDad, LDT, 16 * strip, 16 * j);
 #pragma unroll
-        for (int np = 0; np < NTF / 2; ++np) {
+        for (int np = 0; np < NFH / 2; ++np) {
           uint32_t bb[4];
-          ldb_kn(bb, sK, LDF, 16 * j, fo + 16 * np);
-          mma16816(acc[2 * np], adad[j], bb[0], bb[1]);
-          mma16816(acc[2 * np + 1], adad[j], bb[2], bb[3]);
+          ldb_kn(bb, sK, LDF, 16 * j, fo + fcl + 16 * np);
+          mma16816(acc[2 * np], a, bb[0], bb[1]);
+          mma16816(acc[2 * np + 1], a, bb[2], bb[3]);
         }
       }
 #pragma unroll
-      for (int nt = 0; nt < NTF; ++nt) {
-        const int f = fo + 8 * nt + 2 * cq;
-        if (f < F) {
-          dg0 += __bfloat162float(sQ[i0 * LDF + f]) * acc[nt][0];
-          dg1 += __bfloat162float(sQ[i1 * LDF + f]) * acc[nt][2];
-          if (v0) store_grad(dfq, rowF + (size_t)(r0 + i0) * F + f, acc[nt][0], gdt);
-          if (v1) store_grad(dfq, rowF + (size_t)(r0 + i1) * F + f, acc[nt][2], gdt);
-        }
-        if (f + 1 < F) {
-          dg0 += __bfloat162float(sQ[i0 * LDF + f + 1]) * acc[nt][1];
-          dg1 += __bfloat162float(sQ[i1 * LDF + f + 1]) * acc[nt][3];
-          if (v0) store_grad(dfq, rowF + (size_t)(r0 + i0) * F + f + 1, acc[nt][1], gdt);
-          if (v1) store_grad(dfq, rowF + (size_t)(r0 + i1) * F + f + 1, acc[nt][3], gdt);
-        }
+      for (int nt = 0; nt < NFH; ++nt) {
+        const int f = fo + fcl + 8 * nt + 2 * cq;
+        if (f >= F) continue;
+        const bool has1 = f + 1 < F;
+        dg0 += __bfloat162float(sQ[i0 * LDF + f]) * acc[nt][0] +
+               (has1 ? __bfloat162float(sQ[i0 * LDF + f + 1]) * acc[nt][1] : 0.f);
+        dg1 += __bfloat162float(sQ[i1 * LDF + f]) * acc[nt][2] +
+               (has1 ? __bfloat162float(sQ[i1 * LDF + f + 1]) * acc[nt][3] : 0.f);
+        if (v0) store_grad2(dfq, rowF + (size_t)(r0 + i0) * F + f, acc[nt][0], acc[nt][1], has1, fpair, gdt);
+        if (v1) store_grad2(dfq, rowF + (size_t)(r0 + i1) * F + f, acc[nt][2], acc[nt][3], has1, fpair, gdt);
       }
     }
     // (5) dfk = ks (v dS^T - dz) + dad^T fq
     {
-      float acc[NTF][4];
+      float acc[NFH][4];
 #pragma unroll
-      for (int c = 0; c < NTF; ++c)
+      for (int c = 0; c < NFH; ++c)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[c][e] = 0.f;
-      if (n + 1 < NT) {
+      if (with_ds) {
 #pragma unroll 2
         for (int k0 = 0; k0 < DP; k0 += 16) {
           uint32_t a[4];
-          lda_rm(a, sV, LDD, 16 * warp, k0);
+          lda_rm(a, sV, LDD, 16 * strip, k0);
 #pragma unroll
-          for (int np = 0; np < NTF / 2; ++np) {
+          for (int np = 0; np < NFH / 2; ++np) {
             uint32_t bb[4];
-            ldb_nk(bb, sDS, LDD, 16 * np, k0);
+            ldb_nk(bb, sDS, LDD, fcl + 16 * np, k0);
             mma16816(acc[2 * np], a, bb[0], bb[1]);
             mma16816(acc[2 * np + 1], a, bb[2], bb[3]);
           }
         }
       }
 #pragma unroll
-      for (int nt = 0; nt < NTF; ++nt) {
-        const int f = fo + 8 * nt + 2 * cq;
+      for (int nt = 0; nt < NFH; ++nt) {
+        const int f = fo + fcl + 8 * nt + 2 * cq;
         acc[nt][0] = ks0 * (acc[nt][0] - sDZ[f]);
         acc[nt][1] = ks0 * (acc[nt][1] - sDZ[f + 1]);
         acc[nt][2] = ks1 * (acc[nt][2] - sDZ[f]);
@@ -418,123 +443,119 @@ gla_bwd_chunk_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         uint32_t a[4];
-        lda_tr(a, sDad, LDT, 16 * warp, 16 * j);
+        lda_tr(a, sDad, LDT, 16 * strip, 16 * j);
 #pragma unroll
-        for (int np = 0; np < NTF / 2; ++np) {
+        for (int np = 0; np < NFH / 2; ++np) {
           uint32_t bb[4];
-          ldb_kn(bb, sQ, LDF, 16 * j, fo + 16 * np);
+          ldb_kn(bb, sQ, LDF, 16 * j, fo + fcl + 16 * np);
           mma16816(acc[2 * np], a, bb[0], bb[1]);
           mma16816(acc[2 * np + 1], a, bb[2], bb[3]);
         }
       }
 #pragma unroll
-      for (int nt = 0; nt < NTF; ++nt) {
-        const int f = fo + 8 * nt + 2 * cq;
-        if (f < F) {
-          dg0 -= __bfloat162float(sK[i0 * LDF + f]) * acc[nt][0];
-          dg1 -= __bfloat162float(sK[i1 * LDF + f]) * acc[nt][2];
-          if (v0) store_grad(dfk, rowF + (size_t)(r0 + i0) * F + f, acc[nt][0], gdt);
-          if (v1) store_grad(dfk, rowF + (size_t)(r0 + i1) * F + f, acc[nt][2], gdt);
-        }
-        if (f + 1 < F) {
-          dg0 -= __bfloat162float(sK[i0 * LDF + f + 1]) * acc[nt][1];
-          dg1 -= __bfloat162float(sK[i1 * LDF + f + 1]) * acc[nt][3];
-          if (v0) store_grad(dfk, rowF + (size_t)(r0 + i0) * F + f + 1, acc[nt][1], gdt);
-          if (v1) store_grad(dfk, rowF + (size_t)(r0 + i1) * F + f + 1, acc[nt][3], gdt);
-        }
+      for (int nt = 0; nt < NFH; ++nt) {
+        const int f = fo + fcl + 8 * nt + 2 * cq;
+        if (f >= F) continue;
+        const bool has1 = f + 1 < F;
+        dg0 -= __bfloat162float(sK[i0 * LDF + f]) * acc[nt][0] +
+               (has1 ? __bfloat162float(sK[i0 * LDF + f + 1]) * acc[nt][1] : 0.f);
+        dg1 -= __bfloat162float(sK[i1 * LDF + f]) * acc[nt][2] +
+               (has1 ? __bfloat162float(sK[i1 * LDF + f + 1]) * acc[nt][3] : 0.f);
+        if (v0) store_grad2(dfk, rowF + (size_t)(r0 + i0) * F + f, acc[nt][0], acc[nt][1], has1, fpair, gdt);
+        if (v1) store_grad2(dfk, rowF + (size_t)(r0 + i1) * F + f, acc[nt][2], acc[nt][3], has1, fpair, gdt);
       }
     }
-    // (6) dv (inter) += bf16(fk * ks) dS
-    if (n + 1 < NT) {
+    // (6) dv (inter) += bf16(fk * ks) dS over this feature block
+    if (with_ds) {
 #pragma unroll
       for (int k0 = 0; k0 < FB; k0 += 16) {
         uint32_t a[4];
-        lda_rm(a, sK, LDF, 16 * warp, fo + k0);
+        lda_rm(a, sK, LDF, 16 * strip, fo + k0);
         a[0] = pack_bf16(bf16_lo(a[0]) * ks0, bf16_hi(a[0]) * ks0);
         a[1] = pack_bf16(bf16_lo(a[1]) * ks1, bf16_hi(a[1]) * ks1);
         a[2] = pack_bf16(bf16_lo(a[2]) * ks0, bf16_hi(a[2]) * ks0);
         a[3] = pack_bf16(bf16_lo(a[3]) * ks1, bf16_hi(a[3]) * ks1);
 #pragma unroll
-        for (int np = 0; np < NTD / 2; ++np) {
+        for (int np = 0; np < NDH / 2; ++np) {
           uint32_t bb[4];
-          ldb_kn(bb, sDS, LDD, k0, 16 * np);
+          ldb_kn(bb, sDS, LDD, k0, dc + 16 * np);
           mma16816(dvacc[2 * np], a, bb[0], bb[1]);
           mma16816(dvacc[2 * np + 1], a, bb[2], bb[3]);
         }
       }
     }
-    __syncthreads();
+    __syncthreads();  // sS, sDS are restaged for the next feature block
   }
-  // (7) dv and dG
+  // (7) dv, dG and the chunk's sum of dG
+  const bool dpair = (D & 1) == 0;
 #pragma unroll
-  for (int nt = 0; nt < NTD; ++nt) {
-    const int d = 8 * nt + 2 * cq;
-    if (v0) {
-      if (d < D) store_grad(dv, rowD + (size_t)(r0 + i0) * D + d, dvacc[nt][0], gdt);
-      if (d + 1 < D) store_grad(dv, rowD + (size_t)(r0 + i0) * D + d + 1, dvacc[nt][1], gdt);
-    }
-    if (v1) {
-      if (d < D) store_grad(dv, rowD + (size_t)(r0 + i1) * D + d, dvacc[nt][2], gdt);
-      if (d + 1 < D) store_grad(dv, rowD + (size_t)(r0 + i1) * D + d + 1, dvacc[nt][3], gdt);
-    }
+  for (int nt = 0; nt < NDH; ++nt) {
+    const int d = dc + 8 * nt + 2 * cq;
+    if (d >= D) continue;
+    const bool has1 = d + 1 < D;
+    if (v0) store_grad2(dv, rowD + (size_t)(r0 + i0) * D + d, dvacc[nt][0], dvacc[nt][1], has1, dpair, gdt);
+    if (v1) store_grad2(dv, rowD + (size_t)(r0 + i1) * D + d, dvacc[nt][2], dvacc[nt][3], has1, dpair, gdt);
   }
   dg0 = quad_sum(dg0);
   dg1 = quad_sum(dg1);
   if (cq == 0) {
-    if (v0) dG[(size_t)bh * L + r0 + i0] = dg0;
-    if (v1) dG[(size_t)bh * L + r0 + i1] = dg1;
+    sDgp[half * kC + i0] = dg0;
+    sDgp[half * kC + i1] = dg1;
   }
+  __syncthreads();
+  if (tid < kC) {
+    float x = tid < nvalid ? sDgp[tid] + sDgp[kC + tid] : 0.f;
+    if (tid < nvalid) dG[(size_t)bh * L + r0 + tid] = x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    if (lane == 0) sRed[warp] = x;
+  }
+  __syncthreads();
+  if (tid == 0) dGt[chunk] = sRed[0] + sRed[1];
 }
 
 // --------------------------------------------------- 4. log-gate gradient
-// out[j] = sum_{i >= j} x[i], x = dG (per-head gate) or sum over heads of dG
-// (gate shared by the heads of a batch row). One CTA per gate row, 1024
-// threads; tiles of 1024 positions from the end, heads summed in a fixed order,
-// a two-level warp scan inside the tile and a carry across tiles.
-__global__ void __launch_bounds__(1024)
-gla_bwd_gate_kernel(const float* __restrict__ dG, float* __restrict__ out, int H, int L,
-                    int gate_per_head) {
-  __shared__ float warp_tot[32];
-  __shared__ float carry_s;
-  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) carry_s = 0.f;
-  for (int base = ((L - 1) / 1024) * 1024; base >= 0; base -= 1024) {
-    const int j = base + tid;
-    float x = 0.f;
-    if (j < L) {
-      if (gate_per_head) {
-        x = dG[(size_t)row * L + j];
-      } else {
-        const float* p = dG + (size_t)row * H * L + j;
-#pragma unroll 8
-        for (int h = 0; h < H; ++h) x += p[(size_t)h * L];
-      }
-    }
-    // suffix scan within the warp
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float u = __shfl_down_sync(0xffffffffu, x, o);
-      if (lane + o < 32) x += u;
-    }
-    if (lane == 0) warp_tot[warp] = x;
-    __syncthreads();
-    if (warp == 0) {  // suffix scan of the 32 warp totals
-      float w = warp_tot[lane];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float u = __shfl_down_sync(0xffffffffu, w, o);
-        if (lane + o < 32) w += u;
-      }
-      warp_tot[lane] = w;  // sum of warps >= lane
-    }
-    __syncthreads();
-    const float carry = carry_s;
-    const float later = warp + 1 < 32 ? warp_tot[warp + 1] : 0.f;
-    if (j < L) out[(size_t)row * L + j] = carry + later + x;
-    __syncthreads();
-    if (tid == 0) carry_s = carry + warp_tot[0];
+// out[j] = sum_{i >= j} x[i], x = dG (per-head gate) or the sum over heads of
+// dG (gate shared by the heads of a batch row): the autograd of the cumsum and
+// expand of gla.py:260-262. One CTA of 64 threads per (gate row, chunk): the
+// carry is the sum of the later chunks' totals (dGt), added in a fixed order,
+// then a suffix scan over the chunk's rows. Deterministic.
+__global__ void __launch_bounds__(64)
+gla_bwd_gate_kernel(const float* __restrict__ dG, const float* __restrict__ dGt,
+                    float* __restrict__ out, int H, int L, int NT, int gate_per_head) {
+  __shared__ float red[64];
+  __shared__ float wtot[2];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = blockIdx.x % NT, row = blockIdx.x / NT;
+  const int h0 = gate_per_head ? row : row * H;  // first batch*head row of this gate row
+  const int nh = gate_per_head ? 1 : H;
+  const int later = NT - 1 - n;
+  float c = 0.f;
+  for (int i = tid; i < nh * later; i += 64) {
+    const int h = i / later, m = n + 1 + i % later;
+    c += dGt[(size_t)(h0 + h) * NT + m];
+  }
+  red[tid] = c;
+  __syncthreads();
+  for (int w = 32; w > 0; w >>= 1) {
+    if (tid < w) red[tid] += red[tid + w];
     __syncthreads();
   }
+  const float carry = red[0];
+  const int r0 = n * kC, j = r0 + tid;
+  float x = 0.f;
+  if (j < L) {
+    const float* p = dG + (size_t)h0 * L + j;
+    for (int h = 0; h < nh; ++h) x += p[(size_t)h * L];
+  }
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float u = __shfl_down_sync(0xffffffffu, x, o);
+    if (lane + o < 32) x += u;
+  }
+  if (lane == 0) wtot[warp] = x;
+  __syncthreads();
+  if (j < L) out[(size_t)row * L + j] = carry + x + (warp == 0 ? wtot[1] : 0.f);
 }
 
 std::mutex g_attr_mu;
@@ -564,9 +585,9 @@ int launch_chunk(const bf16* fq, const bf16* fk, const bf16* v, const bf16* dy,
   static bool done[64] = {false};
   int rc = ensure_smem(gla_bwd_chunk_kernel<FP, DP>, SM::bytes, done);
   if (rc) return rc;
-  gla_bwd_chunk_kernel<FP, DP><<<(unsigned)((long long)BH * NT), 128, SM::bytes, st>>>(
+  gla_bwd_chunk_kernel<FP, DP><<<(unsigned)((long long)BH * NT), 256, SM::bytes, st>>>(
       fq, fk, v, dy, sv.g, sv.den, wk.delta, sv.s, sv.z, wk.ds, wk.dz, dfq, dfk, dv, gdt, wk.dg,
-      L, F, D, NT, vec_f, vec_d);
+      wk.dgt, L, F, D, NT, vec_f, vec_d, 0, 0);
   count_launches(1);
   return check_launch("gla_bwd_chunk_kernel");
 }
@@ -625,7 +646,8 @@ int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int 
   if (rc) return rc;
 
   const int gate_rows = gph ? BH : B;
-  gla_bwd_gate_kernel<<<gate_rows, 1024, 0, stream>>>(wk.dg, dlg, H, L, gph);
+  gla_bwd_gate_kernel<<<(unsigned)((long long)gate_rows * NT), 64, 0, stream>>>(
+      wk.dg, wk.dgt, dlg, H, L, NT, gph);
   count_launches(1);
   return check_launch("gla_bwd_gate_kernel");
 }

@@ -22,6 +22,7 @@ struct GlaWork {
   bf16* ds = nullptr;      // [BH, NT, F, D] state gradient leaving each chunk
   float* dz = nullptr;     // [BH, NT, F]
   float* dg = nullptr;     // [BH, L] gradient w.r.t. G
+  float* dgt = nullptr;    // [BH, NT] sum of dg over each chunk
   // chunk-parallel schedule only (null for the sequential walk)
   float* inc = nullptr;    // [BH, NT, F, D] per-chunk increment Q^_n^T dY_n (fp32)
   float* incz = nullptr;   // [BH, NT, F]   per-chunk increment Q^_n^T delta_n
@@ -104,6 +105,7 @@ inline size_t gla_work_layout(int B, int H, int L, int F, int D, bool split,
   const size_t o_ds = take(BH * NT * F * D * 2);
   const size_t o_dz = take(BH * NT * F * 4);
   const size_t o_dg = take(BH * L * 4);
+  const size_t o_dgt = take(BH * NT * 4);
   const size_t o_inc = split ? take(BH * NT * F * D * 4) : 0;
   const size_t o_incz = split ? take(BH * NT * F * 4) : 0;
   const size_t o_lam = split ? take(BH * NT * 4) : 0;
@@ -112,6 +114,7 @@ inline size_t gla_work_layout(int B, int H, int L, int F, int D, bool split,
     out->ds = reinterpret_cast<bf16*>(base + o_ds);
     out->dz = reinterpret_cast<float*>(base + o_dz);
     out->dg = reinterpret_cast<float*>(base + o_dg);
+    out->dgt = reinterpret_cast<float*>(base + o_dgt);
     if (split) {
       out->inc = reinterpret_cast<float*>(base + o_inc);
       out->incz = reinterpret_cast<float*>(base + o_incz);

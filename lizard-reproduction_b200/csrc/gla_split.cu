@@ -8,7 +8,7 @@
 // chunk n, so it splits into
 //   1. increments: every chunk's K~_n^T V_n and sum_t K~_t at once (fp32),
 //      together with lam_n, from a chunk-local scan of the log gates;
-//   2. scan: an elementwise walk over the chunks, one thread per 4 state
+//   2. scan: an elementwise walk over the chunks, one thread per 2 state
 //      entries, writing the bf16 state entering every chunk (the layout the
 //      reference stores, gla.py:48-51) -- in fp32 the same products and sums
 //      as the reference's walk;
@@ -195,13 +195,13 @@ __global__ void __launch_bounds__(128)
 gla_split_binc_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ dy,
                       const float* __restrict__ y32, const float* __restrict__ G,
                       const float* __restrict__ den, int L, int F, int D, int NT, int nfb,
-                      int ndb, int vec_f, int vec_d, float* __restrict__ delta_out,
+                      int ndb, int vec_f, int vec_d, int vec_dots, float* __restrict__ delta_out,
                       float* __restrict__ inc, float* __restrict__ incz,
                       float* __restrict__ lam) {
   __shared__ __align__(16) bf16 sQ[kC * kLD];
   __shared__ __align__(16) bf16 sDy[kC * kLD];
   __shared__ float sGl[kC], sDen[kC], sDel[kC];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x;
   int idx = blockIdx.x;
   const int db = idx % ndb;
   idx /= ndb;
@@ -220,37 +220,14 @@ gla_split_binc_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ dy,
     sGl[tid] = ok ? G[rowb + r0 + tid] - start : 0.f;
     sDen[tid] = ok ? den[rowb + r0 + tid] : 1.f;
   }
-  // delta over the full value dim: warp w takes rows 16w..16w+15
-  const bool write_delta = (fb == 0 && db == 0);
-#pragma unroll 4
-  for (int rr = 0; rr < 16; ++rr) {
-    const int t = 16 * warp + rr;
-    float acc = 0.f;
-    if (t < nvalid) {
-      const bf16* a = dy + (rowb + r0 + t) * D;
-      const float* b = y32 + (rowb + r0 + t) * D;
-      if ((D & 1) == 0) {
-        for (int d = 2 * lane; d < D; d += 64) {
-          const __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162*>(a + d);
-          const float2 w = *reinterpret_cast<const float2*>(b + d);
-          acc += __bfloat162float(x.x) * w.x + __bfloat162float(x.y) * w.y;
-        }
-      } else {
-        for (int d = lane; d < D; d += 32) acc += __bfloat162float(a[d]) * b[d];
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) {
-      sDel[t] = acc;
-      if (write_delta && t < nvalid) delta_out[rowb + r0 + t] = acc;
-    }
-  }
+  // delta over the full value dim
+  block_row_dots64(dy + (rowb + r0) * D, y32 + (rowb + r0) * D, nvalid, D, vec_dots, sDel);
   cp_async_wait_all();
   __syncthreads();
   scale_rows(sQ, [&](int t) {
     return t < nvalid ? __expf(sGl[t]) / fmaxf(sDen[t], kTiny) : 0.f;
   });
+  if (fb == 0 && db == 0 && tid < nvalid) delta_out[rowb + r0 + tid] = sDel[tid];
   __syncthreads();
   const size_t chunk = (size_t)bh * NT + n;
   if (db == 0 && tid < 64 && f0 + tid < F) {
@@ -272,7 +249,7 @@ gla_split_binc_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ dy,
 // Items of one batch*head: F*D/VEC state items, F normaliser items and one
 // gate item (forward only: gs_n = sum_{m<n} lam_m, gtot = sum of all).
 // Loads run kStep chunks ahead of the dependent multiply-adds.
-constexpr int kStep = 8;
+constexpr int kStep = 16;
 
 template <int VEC>
 __global__ void __launch_bounds__(256)
@@ -337,9 +314,9 @@ gla_split_scan_kernel(const float* __restrict__ inc, const float* __restrict__ i
       const int n = reverse ? NT - 1 - st : st;
       const float* p = inc + ((size_t)bh * NT + n) * FD + e0;
       if (st < NT) {
-        if constexpr (VEC == 4) {
-          const float4 w = __ldg(reinterpret_cast<const float4*>(p));
-          u[j][0] = w.x, u[j][1] = w.y, u[j][2] = w.z, u[j][3] = w.w;
+        if constexpr (VEC == 2) {
+          const float2 w = __ldg(reinterpret_cast<const float2*>(p));
+          u[j][0] = w.x, u[j][1] = w.y;
         } else {
 #pragma unroll
           for (int c = 0; c < VEC; ++c) u[j][c] = __ldg(p + c);
@@ -358,11 +335,8 @@ gla_split_scan_kernel(const float* __restrict__ inc, const float* __restrict__ i
       const int n = reverse ? NT - 1 - st : st;
       if (s_out) {
         bf16* q = s_out + ((size_t)bh * NT + n) * FD + e0;
-        if constexpr (VEC == 4) {
-          uint2 w;
-          w.x = pack_bf16(h[0], h[1]);
-          w.y = pack_bf16(h[2], h[3]);
-          *reinterpret_cast<uint2*>(q) = w;
+        if constexpr (VEC == 2) {
+          *reinterpret_cast<uint32_t*>(q) = pack_bf16(h[0], h[1]);
         } else {
 #pragma unroll
           for (int c = 0; c < VEC; ++c) q[c] = __float2bfloat16_rn(h[c]);
@@ -461,13 +435,14 @@ int launch_scan(const float* inc, const float* incz, const float* lam, int BH, i
                 int D, int reverse, const float* seed, const float* seedz, bf16* s_out,
                 float* z_out, float* fin, float* finz, float* gs, float* gtot, cudaStream_t st) {
   const size_t FD = (size_t)F * D;
-  const bool v4 = FD % 4 == 0 && aligned16(inc) && (!seed || aligned16(seed)) &&
-                  (!fin || aligned16(fin)) && (!s_out || ((uintptr_t)s_out & 7) == 0);
-  const long long per = (long long)(v4 ? FD / 4 : FD) + F + 1;
+  auto a8 = [](const void* p) { return ((uintptr_t)p & 7) == 0; };
+  const bool v2 = FD % 2 == 0 && a8(inc) && (!seed || a8(seed)) && (!fin || a8(fin)) &&
+                  (!s_out || ((uintptr_t)s_out & 3) == 0);
+  const long long per = (long long)(v2 ? FD / 2 : FD) + F + 1;
   const long long threads = (long long)BH * per;
   const unsigned grid = (unsigned)((threads + 255) / 256);
-  if (v4)
-    gla_split_scan_kernel<4><<<grid, 256, 0, st>>>(inc, incz, lam, BH, NT, F, D, reverse, seed,
+  if (v2)
+    gla_split_scan_kernel<2><<<grid, 256, 0, st>>>(inc, incz, lam, BH, NT, F, D, reverse, seed,
                                                    seedz, s_out, z_out, fin, finz, gs, gtot);
   else
     gla_split_scan_kernel<1><<<grid, 256, 0, st>>>(inc, incz, lam, BH, NT, F, D, reverse, seed,
@@ -523,9 +498,10 @@ int gla_bwd_split_states(const bf16* fq, const bf16* dy, const GlaSaved& sv, con
   const int nfb = ceil_div(F, 64), ndb = ceil_div(D, 64);
   const int vec_f = (F % 8 == 0) && aligned16(fq);
   const int vec_d = (D % 8 == 0) && aligned16(dy);
+  const int vec_dots = (D % 4 == 0) && ((uintptr_t)dy & 7) == 0 && aligned16(sv.y32);
   gla_split_binc_kernel<<<(unsigned)((long long)BH * NT * nfb * ndb), 128, 0, stream>>>(
-      fq, dy, sv.y32, sv.g, sv.den, L, F, D, NT, nfb, ndb, vec_f, vec_d, wk.delta, wk.inc,
-      wk.incz, wk.lam);
+      fq, dy, sv.y32, sv.g, sv.den, L, F, D, NT, nfb, ndb, vec_f, vec_d, vec_dots, wk.delta,
+      wk.inc, wk.incz, wk.lam);
   count_launches(1);
   int rc = check_launch("gla_split_binc_kernel");
   if (rc) return rc;

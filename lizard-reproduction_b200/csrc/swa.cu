@@ -5,11 +5,12 @@
 //
 // Forward: flash-style online softmax whose running max / sum start from the
 // sinks (src/kernels/swa.py:34-38), so the sinks add to the denominator only.
-// Backward (src/kernels/swa.py:62-133, 158-179), three launches:
-//   dq kernel  : per query block, pass 1 forms delta_i = sum_t P_it (dy_i . v_t)
-//                in fp32 (the reference uses dy . bf16(y), swa.py:164, which
-//                loses the small 1 - P differences); pass 2 accumulates dq.
-//                It also writes delta and per-block sink-gradient partials.
+// The forward also keeps y in fp32 when the caller trains.
+// Backward (src/kernels/swa.py:62-133, 158-179), four launches:
+//   delta      : delta_i = dy_i . y32_i in fp32 (the reference uses dy . bf16(y),
+//                swa.py:164, which loses the small 1 - P differences the sink
+//                gradient is made of), and per-block sink-gradient partials.
+//   dq kernel  : per query block, dq over the key blocks in its window.
 //   dkv kernel : per key block, dk and dv over the query blocks in its window.
 //   dmeta      : dmeta_j = -sum_i exp(meta_j - lse_i) delta_i (swa.py:175-176),
 //                reduced over the per-block partials in a fixed order.
@@ -95,12 +96,17 @@ struct FwdSmem {
                           v = kl + (SPLIT ? 2 * T : 0), bytes = v + 2 * T;
 };
 
+// P enters the P.V product as bf16 hi + lo parts, so the output (and the fp32
+// copy kept for the backward's delta) carries about 16 mantissa bits of P
+// instead of 8: the sink gradient is a small difference of such sums. The same
+// product runs with and without a saved buffer, so y does not depend on it.
 template <int DP, bool SPLIT>
 __global__ void __launch_bounds__(128)
 swa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
                const bf16* __restrict__ ql, const bf16* __restrict__ kl,
                const float* __restrict__ meta, int n_meta, int W, float scale_log2, int L, int D,
-               int nqb, int vec, bf16* __restrict__ y, float* __restrict__ lse) {
+               int nqb, int vec, bf16* __restrict__ y, float* __restrict__ lse,
+               float* __restrict__ y32) {
   using SM = FwdSmem<DP, SPLIT>;
   constexpr int LD = Tile<DP>::LD, NTD = DP / 8;
   constexpr size_t T = Tile<DP>::bytes;
@@ -181,15 +187,20 @@ swa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
     const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
     float rs0 = 0.f, rs1 = 0.f;
-    uint32_t pa[4][4];
+    uint32_t pa[4][4], pl[4][4];
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
       const float p0 = exp2f(s[nt][0] - mn0), p1 = exp2f(s[nt][1] - mn0);
       const float p2 = exp2f(s[nt][2] - mn1), p3 = exp2f(s[nt][3] - mn1);
       rs0 += p0 + p1;
       rs1 += p2 + p3;
-      pa[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16(p0, p1);
-      pa[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(p2, p3);
+      const uint32_t h01 = pack_bf16(p0, p1), h23 = pack_bf16(p2, p3);
+      pa[nt >> 1][(nt & 1) * 2 + 0] = h01;
+      pa[nt >> 1][(nt & 1) * 2 + 1] = h23;
+      {
+        pl[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16(p0 - bf16_lo(h01), p1 - bf16_hi(h01));
+        pl[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(p2 - bf16_lo(h23), p3 - bf16_hi(h23));
+      }
     }
     rs0 = quad_sum(rs0);
     rs1 = quad_sum(rs1);
@@ -213,21 +224,37 @@ swa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         ldb_kn(bb, tV, LD, 16 * j, 16 * np);
         mma16816(o[2 * np], pa[j], bb[0], bb[1]);
         mma16816(o[2 * np + 1], pa[j], bb[2], bb[3]);
+        mma16816(o[2 * np], pl[j], bb[0], bb[1]);
+        mma16816(o[2 * np + 1], pl[j], bb[2], bb[3]);
       }
     }
     __syncthreads();
   }
   const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+  const bool pair = (D & 1) == 0;
 #pragma unroll
   for (int nt = 0; nt < NTD; ++nt) {
     const int d = 8 * nt + 2 * cq;
-    if (i0 < L) {
-      if (d < D) y[base + (size_t)i0 * D + d] = __float2bfloat16_rn(o[nt][0] * inv0);
-      if (d + 1 < D) y[base + (size_t)i0 * D + d + 1] = __float2bfloat16_rn(o[nt][1] * inv0);
-    }
-    if (i1 < L) {
-      if (d < D) y[base + (size_t)i1 * D + d] = __float2bfloat16_rn(o[nt][2] * inv1);
-      if (d + 1 < D) y[base + (size_t)i1 * D + d + 1] = __float2bfloat16_rn(o[nt][3] * inv1);
+    if (d >= D) continue;
+    const bool has1 = d + 1 < D;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int i = h ? i1 : i0;
+      if (i >= L) continue;
+      const float inv = h ? inv1 : inv0;
+      const float a = o[nt][2 * h] * inv, b = o[nt][2 * h + 1] * inv;
+      const size_t at = base + (size_t)i * D + d;
+      if (pair && has1) {
+        *reinterpret_cast<__nv_bfloat162*>(y + at) = __floats2bfloat162_rn(a, b);
+        if (y32) *reinterpret_cast<float2*>(y32 + at) = make_float2(a, b);
+      } else {
+        y[at] = __float2bfloat16_rn(a);
+        if (has1) y[at + 1] = __float2bfloat16_rn(b);
+        if (y32) {
+          y32[at] = a;
+          if (has1) y32[at + 1] = b;
+        }
+      }
     }
   }
   if (lse && cq == 0) {
@@ -236,13 +263,46 @@ swa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   }
 }
 
+// ------------------------------------------------------- backward: delta
+// delta_i = dy_i . y32_i (the fp32 output saved by the forward; the reference
+// uses dy . bf16(y), swa.py:164) and, per 64-row block, the sink-gradient
+// partials sum_i exp(meta_j - lse_i) delta_i (swa.py:175-176) in a fixed
+// order. 4 warps, 16 rows each.
+__global__ void __launch_bounds__(128)
+swa_bwd_delta_kernel(const bf16* __restrict__ dy, const float* __restrict__ y32,
+                     const float* __restrict__ lse, const float* __restrict__ meta, int n_meta,
+                     int L, int D, int nqb, int vec, float* __restrict__ delta,
+                     float* __restrict__ partial) {
+  __shared__ float sDel[kB], sLse[kB];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qb = blockIdx.x % nqb, bh = blockIdx.x / nqb;
+  const int q0 = qb * kB, nrows = min(kB, L - q0);
+  const size_t rowb = (size_t)bh * L + q0;
+  if (tid < kB) sLse[tid] = tid < nrows ? lse[rowb + tid] : 0.f;
+  block_row_dots64(dy + rowb * D, y32 + rowb * D, nrows, D, vec, sDel);
+  __syncthreads();
+  if (tid < nrows) delta[rowb + tid] = sDel[tid];
+  // warp w sums sinks j = w, w+4, ... over the block's rows (2 rows per lane)
+  for (int j = warp; j < n_meta; j += 4) {
+    float x = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int t = lane + 32 * h;
+      if (t < nrows) x += __expf(meta[j] - sLse[t]) * sDel[t];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    if (lane == 0) partial[(size_t)blockIdx.x * n_meta + j] = x;
+  }
+}
+
 // ------------------------------------------------------- backward: dq
+// dq_i = scale * sum_t P_it (dy_i . v_t - delta_i) k_t   (swa.py:62-95)
 template <int DP, bool SPLIT>
 struct DqSmem {
   static constexpr size_t T = Tile<DP>::bytes;
   static constexpr size_t q = 0, ql = q + T, dy = ql + (SPLIT ? T : 0), k = dy + T,
-                          kl = k + 2 * T, v = kl + (SPLIT ? 2 * T : 0), red = v + 2 * T,
-                          bytes = red + 4 * kMaxMeta * 4;
+                          kl = k + 2 * T, v = kl + (SPLIT ? 2 * T : 0), bytes = v + 2 * T;
 };
 
 template <int DP, bool SPLIT>
@@ -250,9 +310,8 @@ __global__ void __launch_bounds__(128)
 swa_bwd_dq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
                   const bf16* __restrict__ v, const bf16* __restrict__ ql,
                   const bf16* __restrict__ kl, const bf16* __restrict__ dy,
-                  const float* __restrict__ meta, int n_meta, const float* __restrict__ lse,
-                  int W, float scale, int L, int D, int nqb, int vec, void* __restrict__ dq,
-                  int gdt, float* __restrict__ delta_out, float* __restrict__ partial) {
+                  const float* __restrict__ lse, const float* __restrict__ delta, int W,
+                  float scale, int L, int D, int nqb, int vec, void* __restrict__ dq, int gdt) {
   using SM = DqSmem<DP, SPLIT>;
   constexpr int LD = Tile<DP>::LD, NTD = DP / 8;
   constexpr size_t T = Tile<DP>::bytes;
@@ -260,7 +319,6 @@ swa_bwd_dq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
   bf16* sQ = reinterpret_cast<bf16*>(smem + SM::q);
   bf16* sQl = reinterpret_cast<bf16*>(smem + SM::ql);
   bf16* sDy = reinterpret_cast<bf16*>(smem + SM::dy);
-  float* sRed = reinterpret_cast<float*>(smem + SM::red);
   auto sK = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::k + s * T); };
   auto sKl = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::kl + s * T); };
   auto sV = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::v + s * T); };
@@ -271,9 +329,7 @@ swa_bwd_dq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
   const size_t base = (size_t)bh * L * D;
   const int lo = max(q0 - W + 1, 0) / kB * kB;
   const int hi = min(q0 + kB, L);
-  const int nkb = (hi - lo + kB - 1) / kB;
-  auto issue = [&](int step, int s) {
-    const int kb = lo + (step % nkb) * kB;
+  auto issue = [&](int kb, int s) {
     stage_tile<kB, DP, 128>(sK(s), LD, k + base, D, kb, L, 0, D, vec);
     if (SPLIT) stage_tile<kB, DP, 128>(sKl(s), LD, kl + base, D, kb, L, 0, D, vec);
     stage_tile<kB, DP, 128>(sV(s), LD, v + base, D, kb, L, 0, D, vec);
@@ -281,32 +337,31 @@ swa_bwd_dq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
   stage_tile<kB, DP, 128>(sQ, LD, q + base, D, q0, L, 0, D, vec);
   if (SPLIT) stage_tile<kB, DP, 128>(sQl, LD, ql + base, D, q0, L, 0, D, vec);
   stage_tile<kB, DP, 128>(sDy, LD, dy + base, D, q0, L, 0, D, vec);
-  issue(0, 0);
+  issue(lo, 0);
   cp_async_commit();
   const int i0 = q0 + 16 * warp + gq, i1 = i0 + 8;
   const float lse0 = i0 < L ? lse[(size_t)bh * L + i0] : 0.f;
   const float lse1 = i1 < L ? lse[(size_t)bh * L + i1] : 0.f;
+  const float dl0 = i0 < L ? delta[(size_t)bh * L + i0] : 0.f;
+  const float dl1 = i1 < L ? delta[(size_t)bh * L + i1] : 0.f;
   float acc[NTD][4];
 #pragma unroll
   for (int c = 0; c < NTD; ++c)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[c][e] = 0.f;
   uint32_t qa[DP / 16][4], qla[DP / 16][4], ga[DP / 16][4];
-  float ds0 = 0.f, ds1 = 0.f;  // pass 1: row sums of P (dy . v)
-  float dl0 = 0.f, dl1 = 0.f;  // delta after pass 1
 
-  // steps 0 .. nkb-1: pass 1 (delta); nkb .. 2 nkb-1: pass 2 (dq)
   int stage = 0;
-  for (int step = 0; step < 2 * nkb; ++step, stage ^= 1) {
-    if (step + 1 < 2 * nkb) {
-      issue(step + 1, stage ^ 1);
+  for (int kb = lo; kb < hi; kb += kB, stage ^= 1) {
+    if (kb + kB < hi) {
+      issue(kb + kB, stage ^ 1);
       cp_async_commit();
       asm volatile("cp.async.wait_group 1;\n" ::);
     } else {
       cp_async_wait_all();
     }
     __syncthreads();
-    if (step == 0) {
+    if (kb == lo) {
 #pragma unroll
       for (int kk = 0; kk < DP / 16; ++kk) {
         lda_rm(qa[kk], sQ, LD, 16 * warp, 16 * kk);
@@ -314,8 +369,6 @@ swa_bwd_dq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
         lda_rm(ga[kk], sDy, LD, 16 * warp, 16 * kk);
       }
     }
-    const bool pass2 = step >= nkb;
-    const int kb = lo + (step % nkb) * kB;
     const bf16* tK = sK(stage);
     const bf16* tV = sV(stage);
     float s[8][4], dp[8][4];
@@ -334,83 +387,45 @@ swa_bwd_dq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
         mma16816(dp[2 * np + 1], ga[kk], bv[2], bv[3]);
       }
     }
-    if (!pass2) {
+    uint32_t da[4][4];
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+    for (int nt = 0; nt < 8; ++nt) {
+      float x[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = kb + 8 * nt + 2 * cq + (e & 1);
-          const int i = (e < 2) ? i0 : i1;
-          const float p =
-              in_window(i, t, L, W) ? __expf(s[nt][e] * scale - ((e < 2) ? lse0 : lse1)) : 0.f;
-          if (e < 2) ds0 += p * dp[nt][e]; else ds1 += p * dp[nt][e];
-        }
+      for (int e = 0; e < 4; ++e) {
+        const int t = kb + 8 * nt + 2 * cq + (e & 1);
+        const int i = (e < 2) ? i0 : i1;
+        const float p =
+            in_window(i, t, L, W) ? __expf(s[nt][e] * scale - ((e < 2) ? lse0 : lse1)) : 0.f;
+        x[e] = p * (dp[nt][e] - ((e < 2) ? dl0 : dl1));
       }
-      if (step == nkb - 1) {
-        dl0 = quad_sum(ds0);
-        dl1 = quad_sum(ds1);
-      }
-    } else {
-      uint32_t da[4][4];
+      da[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16(x[0], x[1]);
+      da[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(x[2], x[3]);
+    }
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        float x[4];
+    for (int j = 0; j < 4; ++j) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = kb + 8 * nt + 2 * cq + (e & 1);
-          const int i = (e < 2) ? i0 : i1;
-          const float p =
-              in_window(i, t, L, W) ? __expf(s[nt][e] * scale - ((e < 2) ? lse0 : lse1)) : 0.f;
-          x[e] = p * (dp[nt][e] - ((e < 2) ? dl0 : dl1));
-        }
-        da[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16(x[0], x[1]);
-        da[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(x[2], x[3]);
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-#pragma unroll
-        for (int np = 0; np < NTD / 2; ++np) {
-          uint32_t bb[4];
-          ldb_kn(bb, tK, LD, 16 * j, 16 * np);
-          mma16816(acc[2 * np], da[j], bb[0], bb[1]);
-          mma16816(acc[2 * np + 1], da[j], bb[2], bb[3]);
-        }
+      for (int np = 0; np < NTD / 2; ++np) {
+        uint32_t bb[4];
+        ldb_kn(bb, tK, LD, 16 * j, 16 * np);
+        mma16816(acc[2 * np], da[j], bb[0], bb[1]);
+        mma16816(acc[2 * np + 1], da[j], bb[2], bb[3]);
       }
     }
     __syncthreads();
   }
+  const bool pair = (D & 1) == 0;
 #pragma unroll
   for (int nt = 0; nt < NTD; ++nt) {
     const int d = 8 * nt + 2 * cq;
-    if (i0 < L) {
-      if (d < D) store_grad(dq, base + (size_t)i0 * D + d, acc[nt][0] * scale, gdt);
-      if (d + 1 < D) store_grad(dq, base + (size_t)i0 * D + d + 1, acc[nt][1] * scale, gdt);
-    }
-    if (i1 < L) {
-      if (d < D) store_grad(dq, base + (size_t)i1 * D + d, acc[nt][2] * scale, gdt);
-      if (d + 1 < D) store_grad(dq, base + (size_t)i1 * D + d + 1, acc[nt][3] * scale, gdt);
-    }
-  }
-  if (cq == 0) {
-    if (i0 < L) delta_out[(size_t)bh * L + i0] = dl0;
-    if (i1 < L) delta_out[(size_t)bh * L + i1] = dl1;
-  }
-  // per-block partials of sum_i exp(meta_j - lse_i) delta_i, in a fixed order
-  if (n_meta > 0) {
-    for (int j = 0; j < n_meta; ++j) {
-      float x = 0.f;
-      if (cq == 0) {
-        if (i0 < L) x += __expf(meta[j] - lse0) * dl0;
-        if (i1 < L) x += __expf(meta[j] - lse1) * dl1;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-      if (lane == 0) sRed[warp * kMaxMeta + j] = x;
-    }
-    __syncthreads();
-    if (tid < n_meta)
-      partial[(size_t)blockIdx.x * n_meta + tid] =
-          sRed[tid] + sRed[kMaxMeta + tid] + sRed[2 * kMaxMeta + tid] + sRed[3 * kMaxMeta + tid];
+    if (d >= D) continue;
+    const bool has1 = d + 1 < D;
+    if (i0 < L)
+      store_grad2(dq, base + (size_t)i0 * D + d, acc[nt][0] * scale, acc[nt][1] * scale, has1,
+                  pair, gdt);
+    if (i1 < L)
+      store_grad2(dq, base + (size_t)i1 * D + d, acc[nt][2] * scale, acc[nt][3] * scale, has1,
+                  pair, gdt);
   }
 }
 
@@ -591,7 +606,7 @@ swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
 template <int DP, bool SPLIT>
 int launch_swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
                    const float* meta, int n_meta, int W, int BH, int L, int D, int vec, bf16* y,
-                   float* lse, cudaStream_t st) {
+                   const SwaSaved& sv, cudaStream_t st) {
   using SM = FwdSmem<DP, SPLIT>;
   static bool done[64] = {false};
   int rc = ensure_smem_swa(swa_fwd_kernel<DP, SPLIT>, SM::bytes, done);
@@ -599,16 +614,17 @@ int launch_swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, 
   const int nqb = ceil_div(L, kB);
   const float scale_log2 = kLog2e / sqrtf((float)D);
   swa_fwd_kernel<DP, SPLIT><<<(unsigned)((long long)BH * nqb), 128, SM::bytes, st>>>(
-      q, k, v, ql, kl, meta, n_meta, W, scale_log2, L, D, nqb, vec, y, lse);
+      q, k, v, ql, kl, meta, n_meta, W, scale_log2, L, D, nqb, vec, y, sv.lse, sv.y32);
   count_launches(1);
   return check_launch("swa_fwd_kernel");
 }
 
 template <int DP, bool SPLIT>
 int launch_swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
-                   const bf16* dy, const float* meta, int n_meta, const float* lse,
+                   const bf16* dy, const float* meta, int n_meta, const SwaSaved& sv,
                    const SwaWork& wk, int W, int BH, int L, int D, int vec, void* dq, void* dk,
                    void* dv, int gdt, cudaStream_t st) {
+  const float* lse = sv.lse;
   using SQ = DqSmem<DP, SPLIT>;
   using SKV = DkvSmem<DP, SPLIT>;
   static bool done_q[64] = {false}, done_kv[64] = {false};
@@ -618,9 +634,14 @@ int launch_swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, 
   if (rc) return rc;
   const int nb = ceil_div(L, kB);
   const float scale = 1.f / sqrtf((float)D);
+  const int vec_dots = (D % 4 == 0) && ((uintptr_t)dy & 7) == 0 && aligned16(sv.y32);
+  swa_bwd_delta_kernel<<<(unsigned)((long long)BH * nb), 128, 0, st>>>(
+      dy, sv.y32, lse, meta, n_meta, L, D, nb, vec_dots, wk.delta, wk.partial);
+  count_launches(1);
+  rc = check_launch("swa_bwd_delta_kernel");
+  if (rc) return rc;
   swa_bwd_dq_kernel<DP, SPLIT><<<(unsigned)((long long)BH * nb), 128, SQ::bytes, st>>>(
-      q, k, v, ql, kl, dy, meta, n_meta, lse, W, scale, L, D, nb, vec, dq, gdt, wk.delta,
-      wk.partial);
+      q, k, v, ql, kl, dy, lse, wk.delta, W, scale, L, D, nb, vec, dq, gdt);
   count_launches(1);
   rc = check_launch("swa_bwd_dq_kernel");
   if (rc) return rc;
@@ -633,17 +654,17 @@ int launch_swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, 
 }  // namespace
 
 int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
-            const float* meta, int n_meta, int W, bf16* y, float* lse, int B, int H, int L, int D,
-            cudaStream_t st) {
+            const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B, int H,
+            int L, int D, cudaStream_t st) {
   const int BH = B * H;
   const bool split = ql != nullptr;
   int vec = (D % 8 == 0) && aligned16(q) && aligned16(k) && aligned16(v);
   if (split) vec = vec && aligned16(ql) && aligned16(kl);
 #define LZ_SWA_FWD(dp)                                                                       \
   return split ? launch_swa_fwd<dp, true>(q, k, v, ql, kl, meta, n_meta, W, BH, L, D, vec, y, \
-                                          lse, st)                                           \
+                                          sv, st)                                            \
                : launch_swa_fwd<dp, false>(q, k, v, ql, kl, meta, n_meta, W, BH, L, D, vec, y, \
-                                           lse, st);
+                                           sv, st);
   if (D <= 32) { LZ_SWA_FWD(32) }
   if (D <= 64) { LZ_SWA_FWD(64) }
   if (D <= 128) { LZ_SWA_FWD(128) }
@@ -653,7 +674,7 @@ int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const b
 }
 
 int swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
-            const float* meta, int n_meta, int W, const float* lse, const bf16* dy, void* dq,
+            const float* meta, int n_meta, int W, const SwaSaved& sv, const bf16* dy, void* dq,
             void* dk, void* dv, int gdt, float* dmeta, const SwaWork& wk, int B, int H, int L,
             int D, cudaStream_t st) {
   const int BH = B * H;
@@ -662,9 +683,9 @@ int swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const b
   if (split) vec = vec && aligned16(ql) && aligned16(kl);
   int rc;
 #define LZ_SWA_BWD(dp)                                                                         \
-  rc = split ? launch_swa_bwd<dp, true>(q, k, v, ql, kl, dy, meta, n_meta, lse, wk, W, BH, L, D, \
+  rc = split ? launch_swa_bwd<dp, true>(q, k, v, ql, kl, dy, meta, n_meta, sv, wk, W, BH, L, D,  \
                                         vec, dq, dk, dv, gdt, st)                              \
-             : launch_swa_bwd<dp, false>(q, k, v, ql, kl, dy, meta, n_meta, lse, wk, W, BH, L, \
+             : launch_swa_bwd<dp, false>(q, k, v, ql, kl, dy, meta, n_meta, sv, wk, W, BH, L,  \
                                          D, vec, dq, dk, dv, gdt, st);
   if (D <= 32) {
     LZ_SWA_BWD(32)

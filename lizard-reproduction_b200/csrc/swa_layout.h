@@ -1,4 +1,5 @@
-// Layout of the SWA saved buffer (log-sum-exp per row) and backward workspace.
+// Layout of the SWA saved buffer (log-sum-exp and fp32 output per row) and of
+// the backward workspace.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -15,8 +16,20 @@ struct SwaWork {
   float* partial = nullptr;  // [BH * ceil(L/64), n_meta] sink-gradient partials
 };
 
-inline size_t swa_saved_bytes(int B, int H, int L) {
-  return align_up((size_t)B * H * L * 4, 256);
+struct SwaSaved {
+  float* lse = nullptr;  // [BH, L] log of the softmax denominator (sinks included)
+  float* y32 = nullptr;  // [BH, L, D] fp32 output; delta = dy . y32 in the backward
+};
+
+inline size_t swa_saved_layout(int B, int H, int L, int D, unsigned char* base, SwaSaved* out) {
+  const size_t rows = (size_t)B * H * L;
+  const size_t o_y32 = align_up(rows * 4, 256);
+  const size_t total = align_up(o_y32 + rows * (size_t)D * 4, 256);
+  if (out && base) {
+    out->lse = reinterpret_cast<float*>(base);
+    out->y32 = reinterpret_cast<float*>(base + o_y32);
+  }
+  return total;
 }
 
 inline size_t swa_work_layout(int B, int H, int L, int n_meta, unsigned char* base,
@@ -34,11 +47,11 @@ inline size_t swa_work_layout(int B, int H, int L, int n_meta, unsigned char* ba
 }
 
 int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
-            const float* meta, int n_meta, int W, bf16* y, float* lse, int B, int H, int L, int D,
-            cudaStream_t st);
+            const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B, int H,
+            int L, int D, cudaStream_t st);
 
 int swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
-            const float* meta, int n_meta, int W, const float* lse, const bf16* dy, void* dq,
+            const float* meta, int n_meta, int W, const SwaSaved& sv, const bf16* dy, void* dq,
             void* dk, void* dv, int gdt, float* dmeta, const SwaWork& wk, int B, int H, int L,
             int D, cudaStream_t st);
 

@@ -45,7 +45,7 @@ def test_buffer_size_queries(lib):
     saved = lib.lz_gla_saved_bytes(B, H, L, F, D, 64)
     assert saved >= B * H * L * D * 4 + 2 * B * H * L * 4 + B * H * nt * F * (2 * D + 4)
     assert lib.lz_gla_bwd_workspace_bytes(B, H, L, F, D, 64) >= B * H * nt * F * D * 2
-    assert lib.lz_swa_saved_bytes(B, H, L, D) >= B * H * L * 4
+    assert lib.lz_swa_saved_bytes(B, H, L, D) >= B * H * L * 4 * (1 + D)
     assert lib.lz_swa_bwd_workspace_bytes(B, H, L, D, 4) >= B * H * L * 4
     assert lib.lz_gla_saved_bytes(0, H, L, F, D, 64) == 0
 
