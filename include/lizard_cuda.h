@@ -119,6 +119,78 @@ int lz_gla_bwd(const void* fq, const void* fk, const void* v,
                int B, int H, int L, int F, int D, int chunk, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* GLA, sequence-parallel segments                                          */
+/* ------------------------------------------------------------------------ */
+/* A long sequence split over P ranks: rank r owns tokens [r*Ls, (r+1)*Ls)
+ * of every head (fq, fk, v, y, dy are that rank's [BH, Ls, *] slices and
+ * log_gamma its [B or BH, Ls] slice; Ls a multiple of 64 except on the last
+ * rank). Each rank runs its segment in its own gate frame and only a summary
+ * per rank crosses ranks (one all_gather; the transport is the caller's):
+ *   summary (fp32) = state [BH,F,D] | zstate [BH,F] | logdecay [BH]
+ *   seed    (fp32) = state [BH,F,D] | zstate [BH,F]
+ * Forward:  seg_fwd_begin -> gather summaries -> seg_combine(reverse=0)
+ *           -> seg_fwd_end(seed; null on rank 0).
+ * Backward: seg_bwd_begin -> gather -> seg_combine(reverse=1)
+ *           -> seg_bwd_end(dseed; null on the last rank)
+ *           -> gather each rank's dlog_gamma[:, 0] -> seg_gate_offset.
+ * The reference has no sequence-parallel path; these entry points restate its
+ * state recurrence (src/kernels/gla.py:44-57 forward, 118-132 backward) across
+ * segments. The workspace must be the same buffer from a begin call to the
+ * matching end call. */
+
+/* Workspace bytes of the segment calls (one buffer serves both directions). */
+size_t lz_gla_seg_workspace_bytes(int B, int H, int L, int F, int D);
+
+/* Floats of one rank's summary. */
+size_t lz_gla_seg_summary_floats(int B, int H, int F, int D);
+
+/* Forward, part 1: per-chunk state increments of the segment (kept in the
+ * workspace) and the summary: the state after the segment from a zero start,
+ * its normaliser and the segment's total log decay per head. */
+int lz_gla_seg_fwd_begin(const void* fk, const void* v, const float* log_gamma,
+                         int gate_per_head, float* summary, void* workspace,
+                         size_t workspace_bytes, int B, int H, int L, int F, int D,
+                         void* stream);
+
+/* Forward, part 2: the states of every chunk from the seed (the state
+ * entering the segment; null = zero) and y; fills saved as lz_gla_fwd does. */
+int lz_gla_seg_fwd_end(const void* fq, const void* fk, const void* v,
+                       const float* log_gamma, int gate_per_head, const float* seed,
+                       void* y, void* saved, size_t saved_bytes, void* workspace,
+                       size_t workspace_bytes, int B, int H, int L, int F, int D,
+                       void* stream);
+
+/* Backward, part 1: per-chunk state-gradient increments and the summary: the
+ * gradient w.r.t. the state entering the segment from the segment's own
+ * outputs, and the total log decay. saved comes from lz_gla_seg_fwd_end. */
+int lz_gla_seg_bwd_begin(const void* fq, const void* saved, size_t saved_bytes,
+                         const void* dy, float* summary, void* workspace,
+                         size_t workspace_bytes, int B, int H, int L, int F, int D,
+                         void* stream);
+
+/* Backward, part 2: dfq, dfk, dv and this segment's part of dlog_gamma (the
+ * reverse cumsum restricted to the segment), from dseed (the gradient w.r.t.
+ * the state leaving the segment; null = zero). seeded_forward: the forward's
+ * seed was not null. */
+int lz_gla_seg_bwd_end(const void* fq, const void* fk, const void* v, int gate_per_head,
+                       const void* saved, size_t saved_bytes, const void* dy,
+                       const float* dseed, int seeded_forward, void* dfq, void* dfk,
+                       void* dv, int grad_dtype, float* dlog_gamma, void* workspace,
+                       size_t workspace_bytes, int B, int H, int L, int F, int D,
+                       void* stream);
+
+/* seed of `rank` from the P gathered summaries ([P][summary floats]):
+ * forward (reverse = 0) combines ranks 0..rank-1, backward (reverse = 1)
+ * ranks rank+1..P-1, each step h = h * exp(logdecay_q) + state_q. */
+int lz_gla_seg_combine(const float* summaries, int P, int rank, int reverse, float* seed,
+                       int B, int H, int F, int D, void* stream);
+
+/* dlog_gamma [rows, L] += the sum over ranks after `rank` of totals[q][row],
+ * where totals [P][rows] holds every rank's dlog_gamma[row, 0]. */
+int lz_gla_seg_gate_offset(float* dlog_gamma, const float* totals, int P, int rank,
+                           int rows, int L, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* SWA                                                                      */
 /* ------------------------------------------------------------------------ */
 

@@ -1,5 +1,7 @@
 // extern "C" entry points declared in include/lizard_cuda.h: argument
 // validation, carving of caller-owned buffers, dispatch to the kernels.
+#include <algorithm>
+
 #include "common.cuh"
 #include "gla_layout.h"
 #include "swa_layout.h"
@@ -198,4 +200,144 @@ extern "C" int lz_swa_bwd(const void* q, const void* k, const void* v, const voi
                      static_cast<const bf16*>(k_lo), meta, n_meta, window,
                      sv, static_cast<const bf16*>(dy), dq, dk, dv,
                      grad_dtype, dmeta, wk, B, H, L, D, static_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------ sequence-parallel segments
+namespace {
+
+int seg_common(int B, int H, int L, int F, int D, void* workspace, size_t workspace_bytes) {
+  int rc = check_sizes(B, H, L, F, D);
+  if (rc) return rc;
+  LZ_REQUIRE(F <= 256, LZ_ERR_UNSUPPORTED, "feature dim above 256 is not supported");
+  LZ_REQUIRE(D <= 128, LZ_ERR_UNSUPPORTED, "value dim above 128 is not supported");
+  LZ_REQUIRE(workspace, LZ_ERR_INVALID_ARGUMENT, "null workspace");
+  LZ_REQUIRE(lz::aligned16(workspace), LZ_ERR_INVALID_ARGUMENT,
+             "workspace must be 16-byte aligned");
+  const size_t need = std::max(lz::gla_fwd_work_layout(B, H, L, F, D, nullptr, nullptr),
+                               lz::gla_work_layout(B, H, L, F, D, true, nullptr, nullptr));
+  LZ_REQUIRE(workspace_bytes >= need, LZ_ERR_WORKSPACE,
+             "workspace too small (lz_gla_seg_workspace_bytes)");
+  return LZ_OK;
+}
+
+int seg_saved(int B, int H, int L, int F, int D, const void* saved, size_t saved_bytes,
+              lz::GlaSaved* sv) {
+  LZ_REQUIRE(saved_bytes >= lz::gla_saved_layout(B, H, L, F, D, nullptr, nullptr),
+             LZ_ERR_WORKSPACE, "saved buffer too small");
+  LZ_REQUIRE(lz::aligned16(saved), LZ_ERR_INVALID_ARGUMENT, "saved buffer must be 16-byte aligned");
+  lz::gla_saved_layout(B, H, L, F, D, (unsigned char*)const_cast<void*>(saved), sv);
+  return LZ_OK;
+}
+
+}  // namespace
+
+extern "C" size_t lz_gla_seg_workspace_bytes(int B, int H, int L, int F, int D) {
+  if (B < 1 || H < 1 || L < 1 || F < 1 || D < 1) return 0;
+  return std::max(lz::gla_fwd_work_layout(B, H, L, F, D, nullptr, nullptr),
+                  lz::gla_work_layout(B, H, L, F, D, true, nullptr, nullptr));
+}
+
+extern "C" size_t lz_gla_seg_summary_floats(int B, int H, int F, int D) {
+  if (B < 1 || H < 1 || F < 1 || D < 1) return 0;
+  return lz::gla_seg_summary_floats(B * H, F, D);
+}
+
+extern "C" int lz_gla_seg_fwd_begin(const void* fk, const void* v, const float* log_gamma,
+                                    int gate_per_head, float* summary, void* workspace,
+                                    size_t workspace_bytes, int B, int H, int L, int F, int D,
+                                    void* stream) {
+  lz::clear_error();
+  int rc = seg_common(B, H, L, F, D, workspace, workspace_bytes);
+  if (rc) return rc;
+  LZ_REQUIRE(fk && v && log_gamma && summary, LZ_ERR_INVALID_ARGUMENT, "null pointer");
+  lz::GlaFwdWork fw;
+  lz::gla_fwd_work_layout(B, H, L, F, D, static_cast<unsigned char*>(workspace), &fw);
+  return lz::gla_seg_fwd_begin(static_cast<const bf16*>(fk), static_cast<const bf16*>(v),
+                               log_gamma, gate_per_head ? 1 : 0, summary, fw, B, H, L, F, D,
+                               static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lz_gla_seg_fwd_end(const void* fq, const void* fk, const void* v,
+                                  const float* log_gamma, int gate_per_head, const float* seed,
+                                  void* y, void* saved, size_t saved_bytes, void* workspace,
+                                  size_t workspace_bytes, int B, int H, int L, int F, int D,
+                                  void* stream) {
+  lz::clear_error();
+  int rc = seg_common(B, H, L, F, D, workspace, workspace_bytes);
+  if (rc) return rc;
+  LZ_REQUIRE(fq && fk && v && log_gamma && y, LZ_ERR_INVALID_ARGUMENT, "null pointer");
+  lz::GlaSaved sv;
+  if (saved) {
+    rc = seg_saved(B, H, L, F, D, saved, saved_bytes, &sv);
+    if (rc) return rc;
+  }
+  lz::GlaFwdWork fw;
+  lz::gla_fwd_work_layout(B, H, L, F, D, static_cast<unsigned char*>(workspace), &fw);
+  return lz::gla_seg_fwd_end(static_cast<const bf16*>(fq), static_cast<const bf16*>(fk),
+                             static_cast<const bf16*>(v), log_gamma, gate_per_head ? 1 : 0, seed,
+                             static_cast<bf16*>(y), sv, fw, B, H, L, F, D,
+                             static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lz_gla_seg_bwd_begin(const void* fq, const void* saved, size_t saved_bytes,
+                                    const void* dy, float* summary, void* workspace,
+                                    size_t workspace_bytes, int B, int H, int L, int F, int D,
+                                    void* stream) {
+  lz::clear_error();
+  int rc = seg_common(B, H, L, F, D, workspace, workspace_bytes);
+  if (rc) return rc;
+  LZ_REQUIRE(fq && saved && dy && summary, LZ_ERR_INVALID_ARGUMENT, "null pointer");
+  lz::GlaSaved sv;
+  rc = seg_saved(B, H, L, F, D, saved, saved_bytes, &sv);
+  if (rc) return rc;
+  lz::GlaWork wk;
+  lz::gla_work_layout(B, H, L, F, D, true, static_cast<unsigned char*>(workspace), &wk);
+  return lz::gla_seg_bwd_begin(static_cast<const bf16*>(fq), static_cast<const bf16*>(dy), sv,
+                               summary, wk, B, H, L, F, D, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lz_gla_seg_bwd_end(const void* fq, const void* fk, const void* v,
+                                  int gate_per_head, const void* saved, size_t saved_bytes,
+                                  const void* dy, const float* dseed, int seeded_forward,
+                                  void* dfq, void* dfk, void* dv, int grad_dtype,
+                                  float* dlog_gamma, void* workspace, size_t workspace_bytes,
+                                  int B, int H, int L, int F, int D, void* stream) {
+  lz::clear_error();
+  int rc = seg_common(B, H, L, F, D, workspace, workspace_bytes);
+  if (rc) return rc;
+  LZ_REQUIRE(fq && fk && v && saved && dy && dfq && dfk && dv && dlog_gamma,
+             LZ_ERR_INVALID_ARGUMENT, "null pointer");
+  LZ_REQUIRE(grad_dtype == LZ_DTYPE_F32 || grad_dtype == LZ_DTYPE_BF16, LZ_ERR_INVALID_ARGUMENT,
+             "grad_dtype must be LZ_DTYPE_F32 or LZ_DTYPE_BF16");
+  lz::GlaSaved sv;
+  rc = seg_saved(B, H, L, F, D, saved, saved_bytes, &sv);
+  if (rc) return rc;
+  lz::GlaWork wk;
+  lz::gla_work_layout(B, H, L, F, D, true, static_cast<unsigned char*>(workspace), &wk);
+  return lz::gla_seg_bwd_end(static_cast<const bf16*>(fq), static_cast<const bf16*>(fk),
+                             static_cast<const bf16*>(v), gate_per_head ? 1 : 0, sv,
+                             static_cast<const bf16*>(dy), dseed, seeded_forward ? 1 : 0, dfq,
+                             dfk, dv, grad_dtype, dlog_gamma, wk, B, H, L, F, D,
+                             static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lz_gla_seg_combine(const float* summaries, int P, int rank, int reverse,
+                                  float* seed, int B, int H, int F, int D, void* stream) {
+  lz::clear_error();
+  LZ_REQUIRE(summaries && seed, LZ_ERR_INVALID_ARGUMENT, "null pointer");
+  LZ_REQUIRE(P >= 1 && rank >= 0 && rank < P, LZ_ERR_INVALID_ARGUMENT, "rank must be in [0, P)");
+  LZ_REQUIRE(B >= 1 && H >= 1 && F >= 1 && D >= 1, LZ_ERR_INVALID_ARGUMENT,
+             "sizes must be positive");
+  return lz::gla_seg_combine(summaries, P, rank, reverse ? 1 : 0, seed, B * H, F, D,
+                             static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lz_gla_seg_gate_offset(float* dlog_gamma, const float* totals, int P, int rank,
+                                      int rows, int L, void* stream) {
+  lz::clear_error();
+  LZ_REQUIRE(dlog_gamma && totals, LZ_ERR_INVALID_ARGUMENT, "null pointer");
+  LZ_REQUIRE(P >= 1 && rank >= 0 && rank < P, LZ_ERR_INVALID_ARGUMENT, "rank must be in [0, P)");
+  LZ_REQUIRE(rows >= 1 && L >= 1, LZ_ERR_INVALID_ARGUMENT, "sizes must be positive");
+  return lz::gla_seg_gate_offset(dlog_gamma, totals, P, rank, rows, L,
+                                 static_cast<cudaStream_t>(stream));
 }

@@ -580,60 +580,37 @@ int ensure_smem(Kern k, size_t bytes, bool* done) {
 template <int FP, int DP>
 int launch_chunk(const bf16* fq, const bf16* fk, const bf16* v, const bf16* dy,
                  const GlaSaved& sv, const GlaWork& wk, void* dfq, void* dfk, void* dv, int gdt,
-                 int BH, int L, int F, int D, int NT, int vec_f, int vec_d, cudaStream_t st) {
+                 int BH, int L, int F, int D, int NT, int vec_f, int vec_d, int s_seeded,
+                 int ds_seeded, cudaStream_t st) {
   using SM = ChunkSmem<FP, DP>;
   static bool done[64] = {false};
   int rc = ensure_smem(gla_bwd_chunk_kernel<FP, DP>, SM::bytes, done);
   if (rc) return rc;
   gla_bwd_chunk_kernel<FP, DP><<<(unsigned)((long long)BH * NT), 256, SM::bytes, st>>>(
       fq, fk, v, dy, sv.g, sv.den, wk.delta, sv.s, sv.z, wk.ds, wk.dz, dfq, dfk, dv, gdt, wk.dg,
-      wk.dgt, L, F, D, NT, vec_f, vec_d, 0, 0);
+      wk.dgt, L, F, D, NT, vec_f, vec_d, s_seeded, ds_seeded);
   count_launches(1);
   return check_launch("gla_bwd_chunk_kernel");
 }
 
 }  // namespace
 
-int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
-            const GlaSaved& sv, const bf16* dy, void* dfq, void* dfk, void* dv, int gdt,
-            float* dlg, const GlaWork& wk, int B, int H, int L, int F, int D,
-            cudaStream_t stream) {
-  (void)lg;
+int gla_bwd_tail(const bf16* fq, const bf16* fk, const bf16* v, int gph, const GlaSaved& sv,
+                 const bf16* dy, void* dfq, void* dfk, void* dv, int gdt, float* dlg,
+                 const GlaWork& wk, int B, int H, int L, int F, int D, int s_seeded,
+                 int ds_seeded, cudaStream_t stream) {
   const int BH = B * H;
   const int NT = (int)gla_nt(L);
   const int vec_f = (F % 8 == 0) && aligned16(fq) && aligned16(fk);
   const int vec_d = (D % 8 == 0) && aligned16(v) && aligned16(dy) && aligned16(sv.s) &&
                     aligned16(wk.ds);
-  int rc = LZ_OK;
-  if (wk.inc) {
-    rc = gla_bwd_split_states(fq, dy, sv, wk, B, H, L, F, D, stream);
-    if (rc) return rc;
-  } else {
-    const long long rows = (long long)BH * L;
-    gla_bwd_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(dy, sv.y32, wk.delta,
-                                                                         rows, D);
-    count_launches(1);
-    rc = check_launch("gla_bwd_delta_kernel");
-    if (rc) return rc;
-    static bool done[64] = {false};
-    rc = ensure_smem(gla_bwd_state_kernel, StateSmem::bytes, done);
-    if (rc) return rc;
-    const int nfb = ceil_div(F, 64), ndb = ceil_div(D, 64);
-    gla_bwd_state_kernel<<<(unsigned)((long long)BH * nfb * ndb), 128, StateSmem::bytes,
-                           stream>>>(fq, dy, sv.g, sv.den, wk.delta, wk.ds, wk.dz, L, F, D, NT,
-                                     nfb, ndb, vec_f && (F % 8 == 0),
-                                     vec_d && (D % 8 == 0));
-    count_launches(1);
-    rc = check_launch("gla_bwd_state_kernel");
-    if (rc) return rc;
-  }
-
   const int FP = F <= 32 ? 32 : F <= 64 ? 64 : F <= 128 ? 128 : 256;
   const int DP = D <= 32 ? 32 : D <= 64 ? 64 : 128;
+  int rc = LZ_OK;
 #define LZ_CHUNK_CASE(fp, dp)                                                                  \
   if (FP == fp && DP == dp)                                                                    \
     rc = launch_chunk<fp, dp>(fq, fk, v, dy, sv, wk, dfq, dfk, dv, gdt, BH, L, F, D, NT, vec_f, \
-                              vec_d, stream);                                                  \
+                              vec_d, s_seeded, ds_seeded, stream);                             \
   else
   LZ_CHUNK_CASE(32, 32) LZ_CHUNK_CASE(32, 64) LZ_CHUNK_CASE(32, 128)
   LZ_CHUNK_CASE(64, 32) LZ_CHUNK_CASE(64, 64) LZ_CHUNK_CASE(64, 128)
@@ -650,6 +627,41 @@ int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int 
       wk.dg, wk.dgt, dlg, H, L, NT, gph);
   count_launches(1);
   return check_launch("gla_bwd_gate_kernel");
+}
+
+int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
+            const GlaSaved& sv, const bf16* dy, void* dfq, void* dfk, void* dv, int gdt,
+            float* dlg, const GlaWork& wk, int B, int H, int L, int F, int D,
+            cudaStream_t stream) {
+  (void)lg;
+  const int BH = B * H;
+  const int NT = (int)gla_nt(L);
+  int rc = LZ_OK;
+  if (wk.inc) {
+    rc = gla_bwd_split_states(fq, dy, sv, wk, B, H, L, F, D, stream);
+    if (rc) return rc;
+  } else {
+    const int vec_f = (F % 8 == 0) && aligned16(fq);
+    const int vec_d = (D % 8 == 0) && aligned16(dy);
+    const long long rows = (long long)BH * L;
+    gla_bwd_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(dy, sv.y32, wk.delta,
+                                                                         rows, D);
+    count_launches(1);
+    rc = check_launch("gla_bwd_delta_kernel");
+    if (rc) return rc;
+    static bool done[64] = {false};
+    rc = ensure_smem(gla_bwd_state_kernel, StateSmem::bytes, done);
+    if (rc) return rc;
+    const int nfb = ceil_div(F, 64), ndb = ceil_div(D, 64);
+    gla_bwd_state_kernel<<<(unsigned)((long long)BH * nfb * ndb), 128, StateSmem::bytes,
+                           stream>>>(fq, dy, sv.g, sv.den, wk.delta, wk.ds, wk.dz, L, F, D, NT,
+                                     nfb, ndb, vec_f, vec_d);
+    count_launches(1);
+    rc = check_launch("gla_bwd_state_kernel");
+    if (rc) return rc;
+  }
+  return gla_bwd_tail(fq, fk, v, gph, sv, dy, dfq, dfk, dv, gdt, dlg, wk, B, H, L, F, D, 0, 0,
+                      stream);
 }
 
 }  // namespace lz

@@ -161,6 +161,33 @@ int gla_fwd_split_run(const bf16* fq, const bf16* fk, const bf16* v, const float
 int gla_bwd_split_states(const bf16* fq, const bf16* dy, const GlaSaved& sv, const GlaWork& wk,
                          int B, int H, int L, int F, int D, cudaStream_t stream);
 
+// Sequence-parallel segments (gla_split.cu).
+size_t gla_seg_summary_floats(int BH, int F, int D);
+int gla_seg_fwd_begin(const bf16* fk, const bf16* v, const float* lg, int gph, float* summary,
+                      const GlaFwdWork& fw, int B, int H, int L, int F, int D,
+                      cudaStream_t stream);
+int gla_seg_fwd_end(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
+                    const float* seed, bf16* y, const GlaSaved& sv, const GlaFwdWork& fw, int B,
+                    int H, int L, int F, int D, cudaStream_t stream);
+int gla_seg_bwd_begin(const bf16* fq, const bf16* dy, const GlaSaved& sv, float* summary,
+                      const GlaWork& wk, int B, int H, int L, int F, int D, cudaStream_t stream);
+int gla_seg_bwd_end(const bf16* fq, const bf16* fk, const bf16* v, int gph, const GlaSaved& sv,
+                    const bf16* dy, const float* dseed, int s_seeded, void* dfq, void* dfk,
+                    void* dv, int gdt, float* dlg, const GlaWork& wk, int B, int H, int L, int F,
+                    int D, cudaStream_t stream);
+int gla_seg_combine(const float* summaries, int P, int rank, int reverse, float* seed, int BH,
+                    int F, int D, cudaStream_t stream);
+int gla_seg_gate_offset(float* dlg, const float* totals, int P, int rank, int rows, int L,
+                        cudaStream_t stream);
+
+// Per-chunk gradients and the log-gate gradient, once wk.ds / wk.dz / wk.delta
+// hold the state gradients (s_seeded / ds_seeded: the state entering the first
+// chunk / the gradient leaving the last chunk is not zero).
+int gla_bwd_tail(const bf16* fq, const bf16* fk, const bf16* v, int gph, const GlaSaved& sv,
+                 const bf16* dy, void* dfq, void* dfk, void* dv, int gdt, float* dlg,
+                 const GlaWork& wk, int B, int H, int L, int F, int D, int s_seeded,
+                 int ds_seeded, cudaStream_t stream);
+
 int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
             const GlaSaved& sv, const bf16* dy, void* dfq, void* dfk, void* dv, int gdt,
             float* dlg, const GlaWork& wk, int B, int H, int L, int F, int D,

@@ -247,7 +247,7 @@ gla_split_binc_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ dy,
 // (reverse = 1); h starts at the seed (or 0) and at each chunk n
 //   out_n = bf16(h)  (z: fp32),  h = h * exp(lam_n) + inc_n.
 // Items of one batch*head: F*D/VEC state items, F normaliser items and one
-// gate item (forward only: gs_n = sum_{m<n} lam_m, gtot = sum of all).
+// gate item (gs_n = sum_{m<n} lam_m in the forward; gtot = sum of all lam).
 // Loads run kStep chunks ahead of the dependent multiply-adds.
 constexpr int kStep = 16;
 
@@ -267,11 +267,10 @@ gla_split_scan_kernel(const float* __restrict__ inc, const float* __restrict__ i
   const int bh = (int)(gid / per), item = (int)(gid % per);
   const float* LAM = lam + (size_t)bh * NT;
 
-  if (item == nS + F) {  // gate offsets
-    if (reverse) return;
+  if (item == nS + F) {  // gate offsets (gs: forward only) and the total log decay
     float acc = 0.f;
     for (int n = 0; n < NT; ++n) {
-      if (gs) gs[(size_t)bh * NT + n] = acc;
+      if (gs && !reverse) gs[(size_t)bh * NT + n] = acc;
       acc += LAM[n];
     }
     if (gtot) gtot[bh] = acc;
@@ -507,6 +506,152 @@ int gla_bwd_split_states(const bf16* fq, const bf16* dy, const GlaSaved& sv, con
   if (rc) return rc;
   return launch_scan(wk.inc, wk.incz, wk.lam, BH, NT, F, D, 1, nullptr, nullptr, wk.ds, wk.dz,
                      nullptr, nullptr, nullptr, nullptr, stream);
+}
+
+// ------------------------------------------------ sequence-parallel segments
+// A rank that owns a contiguous segment of the sequence runs the schedule
+// above on its segment in the segment's own gate frame (G = 0 before its first
+// token). The only data that crosses ranks is one summary per rank:
+//   state [BH, F, D] | zstate [BH, F] | logdecay [BH]      (fp32)
+// forward: the state after the segment from a zero start and its total log
+// decay; backward: the gradient w.r.t. the state entering the segment from
+// the segment's own outputs, and again the log decay.
+namespace {
+
+// seed_r = walk over the ranks before r (forward) or after r (backward):
+// h <- h * exp(logdecay_q) + state_q, in rank order (reverse: from the last).
+__global__ void __launch_bounds__(256)
+gla_seg_combine_kernel(const float* __restrict__ summ, int P, int rank, int reverse, int BH,
+                       int F, int D, float* __restrict__ seed) {
+  const size_t FD = (size_t)F * D, nS = (size_t)BH * FD, nZ = (size_t)BH * F;
+  const size_t per = nS + nZ + BH;
+  const size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= nS + nZ) return;
+  const int bh = e < nS ? (int)(e / FD) : (int)((e - nS) / F);
+  float h = 0.f;
+  if (!reverse) {
+    for (int q = 0; q < rank; ++q)
+      h = h * __expf(summ[q * per + nS + nZ + bh]) + summ[q * per + e];
+  } else {
+    for (int q = P - 1; q > rank; --q)
+      h = h * __expf(summ[q * per + nS + nZ + bh]) + summ[q * per + e];
+  }
+  seed[e] = h;
+}
+
+// dlog_gamma[row, :] += sum over the ranks after `rank` of their totals[row]
+// (each rank's total is its own dlog_gamma[row, 0]): the reverse cumsum of the
+// log-gate gradient continues across the later segments.
+__global__ void __launch_bounds__(256)
+gla_seg_gate_offset_kernel(float* __restrict__ dlg, const float* __restrict__ totals, int P,
+                           int rank, int rows, int L) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)rows * L) return;
+  const int row = (int)(i / L);
+  float off = 0.f;
+  for (int q = P - 1; q > rank; --q) off += totals[(size_t)q * rows + row];
+  dlg[i] += off;
+}
+
+}  // namespace
+
+size_t gla_seg_summary_floats(int BH, int F, int D) {
+  return (size_t)BH * F * D + (size_t)BH * F + BH;
+}
+
+int gla_seg_fwd_begin(const bf16* fk, const bf16* v, const float* lg, int gph, float* summary,
+                      const GlaFwdWork& fw, int B, int H, int L, int F, int D,
+                      cudaStream_t stream) {
+  const int BH = B * H, NT = (int)gla_nt(L);
+  const int nfb = ceil_div(F, 64), ndb = ceil_div(D, 64);
+  const int vec_f = (F % 8 == 0) && aligned16(fk);
+  const int vec_d = (D % 8 == 0) && aligned16(v);
+  gla_split_finc_kernel<<<(unsigned)((long long)BH * NT * nfb * ndb), 128, 0, stream>>>(
+      fk, v, lg, gph, H, L, F, D, NT, nfb, ndb, vec_f, vec_d, fw.inc, fw.incz, fw.lam);
+  count_launches(1);
+  int rc = check_launch("gla_split_finc_kernel");
+  if (rc) return rc;
+  const size_t nS = (size_t)BH * F * D, nZ = (size_t)BH * F;
+  return launch_scan(fw.inc, fw.incz, fw.lam, BH, NT, F, D, 0, nullptr, nullptr, nullptr,
+                     nullptr, summary, summary + nS, nullptr, summary + nS + nZ, stream);
+}
+
+int gla_seg_fwd_end(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
+                    const float* seed, bf16* y, const GlaSaved& sv, const GlaFwdWork& fw, int B,
+                    int H, int L, int F, int D, cudaStream_t stream) {
+  const int BH = B * H, NT = (int)gla_nt(L);
+  const bool save = sv.y32 != nullptr;
+  bf16* s = save ? sv.s : fw.s;
+  float* z = save ? sv.z : fw.z;
+  const size_t nS = (size_t)BH * F * D;
+  int rc = launch_scan(fw.inc, fw.incz, fw.lam, BH, NT, F, D, 0, seed, seed ? seed + nS : nullptr,
+                       s, z, nullptr, nullptr, save ? fw.gs : nullptr, nullptr, stream);
+  if (rc) return rc;
+  const int FP = F <= 32 ? 32 : F <= 64 ? 64 : F <= 128 ? 128 : 256;
+  const int DV = D <= 16 ? 16 : D <= 32 ? 32 : 64;
+  float* y32 = save ? sv.y32 : nullptr;
+  const int seeded = seed != nullptr;
+#define LZ_OUT_CASE(fp, dv)                                                                   \
+  if (FP == fp && DV == dv)                                                                   \
+    return launch_out<fp, dv>(fq, fk, v, lg, gph, BH, H, L, F, D, NT, s, z, fw.gs, seeded, y, \
+                              y32, sv.den, save ? sv.g : nullptr, stream);
+  LZ_OUT_CASE(32, 16) LZ_OUT_CASE(32, 32) LZ_OUT_CASE(32, 64)
+  LZ_OUT_CASE(64, 16) LZ_OUT_CASE(64, 32) LZ_OUT_CASE(64, 64)
+  LZ_OUT_CASE(128, 16) LZ_OUT_CASE(128, 32) LZ_OUT_CASE(128, 64)
+  LZ_OUT_CASE(256, 16) LZ_OUT_CASE(256, 32) LZ_OUT_CASE(256, 64)
+#undef LZ_OUT_CASE
+  set_error("gla segment forward: no kernel for this feature/value size");
+  return LZ_ERR_UNSUPPORTED;
+}
+
+int gla_seg_bwd_begin(const bf16* fq, const bf16* dy, const GlaSaved& sv, float* summary,
+                      const GlaWork& wk, int B, int H, int L, int F, int D, cudaStream_t stream) {
+  const int BH = B * H, NT = (int)gla_nt(L);
+  const int nfb = ceil_div(F, 64), ndb = ceil_div(D, 64);
+  const int vec_f = (F % 8 == 0) && aligned16(fq);
+  const int vec_d = (D % 8 == 0) && aligned16(dy);
+  const int vec_dots = (D % 4 == 0) && ((uintptr_t)dy & 7) == 0 && aligned16(sv.y32);
+  gla_split_binc_kernel<<<(unsigned)((long long)BH * NT * nfb * ndb), 128, 0, stream>>>(
+      fq, dy, sv.y32, sv.g, sv.den, L, F, D, NT, nfb, ndb, vec_f, vec_d, vec_dots, wk.delta,
+      wk.inc, wk.incz, wk.lam);
+  count_launches(1);
+  int rc = check_launch("gla_split_binc_kernel");
+  if (rc) return rc;
+  const size_t nS = (size_t)BH * F * D, nZ = (size_t)BH * F;
+  return launch_scan(wk.inc, wk.incz, wk.lam, BH, NT, F, D, 1, nullptr, nullptr, nullptr,
+                     nullptr, summary, summary + nS, nullptr, summary + nS + nZ, stream);
+}
+
+int gla_seg_bwd_end(const bf16* fq, const bf16* fk, const bf16* v, int gph, const GlaSaved& sv,
+                    const bf16* dy, const float* dseed, int s_seeded, void* dfq, void* dfk,
+                    void* dv, int gdt, float* dlg, const GlaWork& wk, int B, int H, int L, int F,
+                    int D, cudaStream_t stream) {
+  const int BH = B * H, NT = (int)gla_nt(L);
+  const size_t nS = (size_t)BH * F * D;
+  int rc = launch_scan(wk.inc, wk.incz, wk.lam, BH, NT, F, D, 1, dseed,
+                       dseed ? dseed + nS : nullptr, wk.ds, wk.dz, nullptr, nullptr, nullptr,
+                       nullptr, stream);
+  if (rc) return rc;
+  return gla_bwd_tail(fq, fk, v, gph, sv, dy, dfq, dfk, dv, gdt, dlg, wk, B, H, L, F, D, s_seeded,
+                      dseed != nullptr, stream);
+}
+
+int gla_seg_combine(const float* summaries, int P, int rank, int reverse, float* seed, int BH,
+                    int F, int D, cudaStream_t stream) {
+  const size_t n = (size_t)BH * F * D + (size_t)BH * F;
+  gla_seg_combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(summaries, P, rank,
+                                                                          reverse, BH, F, D, seed);
+  count_launches(1);
+  return check_launch("gla_seg_combine_kernel");
+}
+
+int gla_seg_gate_offset(float* dlg, const float* totals, int P, int rank, int rows, int L,
+                        cudaStream_t stream) {
+  const size_t n = (size_t)rows * L;
+  gla_seg_gate_offset_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(dlg, totals, P,
+                                                                              rank, rows, L);
+  count_launches(1);
+  return check_launch("gla_seg_gate_offset_kernel");
 }
 
 }  // namespace lz

@@ -31,6 +31,18 @@ _SIGNATURES = {
                    + [_c_int] * 6 + [_vp]),
     "lz_gla_bwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _c_size, _vp, _vp, _vp, _vp, _c_int,
                             _vp, _vp, _c_size] + [_c_int] * 6 + [_vp]),
+    "lz_gla_seg_workspace_bytes": (_c_size, [_c_int] * 5),
+    "lz_gla_seg_summary_floats": (_c_size, [_c_int] * 4),
+    "lz_gla_seg_fwd_begin": (_c_int, [_vp, _vp, _vp, _c_int, _vp, _vp, _c_size] + [_c_int] * 5
+                             + [_vp]),
+    "lz_gla_seg_fwd_end": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _vp, _c_size, _vp,
+                                    _c_size] + [_c_int] * 5 + [_vp]),
+    "lz_gla_seg_bwd_begin": (_c_int, [_vp, _vp, _c_size, _vp, _vp, _vp, _c_size] + [_c_int] * 5
+                             + [_vp]),
+    "lz_gla_seg_bwd_end": (_c_int, [_vp, _vp, _vp, _c_int, _vp, _c_size, _vp, _vp, _c_int, _vp,
+                                    _vp, _vp, _c_int, _vp, _vp, _c_size] + [_c_int] * 5 + [_vp]),
+    "lz_gla_seg_combine": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp] + [_c_int] * 4 + [_vp]),
+    "lz_gla_seg_gate_offset": (_c_int, [_vp, _vp] + [_c_int] * 4 + [_vp]),
     "lz_swa_saved_bytes": (_c_size, [_c_int] * 4),
     "lz_swa_bwd_workspace_bytes": (_c_size, [_c_int] * 5),
     "lz_swa_fwd": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp, _vp, _c_size] + [_c_int] * 4

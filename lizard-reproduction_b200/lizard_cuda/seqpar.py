@@ -1,0 +1,183 @@
+"""Sequence-parallel GLA: one long sequence split over the ranks of a group.
+
+Rank r of P owns tokens [r*Ls, (r+1)*Ls) of every head. The chunked GLA
+recurrence (the reference's state pass, src/kernels/gla.py:44-57 forward and
+118-132 backward) is linear in the state, so each rank runs its own segment
+from a zero state and the ranks only exchange one summary each:
+
+forward   state after the segment from a zero start, its normaliser z, and the
+          segment's total log decay; rank r's incoming state is the walk
+          h <- h * exp(logdecay_q) + state_q over the ranks q < r.
+backward  the gradient w.r.t. the state entering the segment from the
+          segment's own outputs (computed after the forward, so it already
+          uses the final denominators); rank r's outgoing-state gradient is the
+          same walk over the ranks q > r, last rank first. The log-gate
+          gradient is a reverse cumsum, so each rank also adds the totals of
+          the later ranks.
+
+One all_gather per direction (plus one of P*rows floats for the gate totals)
+replaces a rank-to-rank chain of P-1 dependent hops. The arithmetic of every
+phase runs in liblizard_cuda (lz_gla_seg_*); torch.distributed only moves the
+summaries.
+"""
+import torch
+
+from . import _lib
+from .gla import _shapes
+
+
+class DistExchange:
+    """all_gather over a torch.distributed process group (NCCL on GPUs)."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist, self.group = dist, group
+        self.rank = dist.get_rank(group)
+        self.size = dist.get_world_size(group)
+
+    def all_gather(self, t):
+        parts = [torch.empty_like(t) for _ in range(self.size)]
+        self.dist.all_gather(parts, t.contiguous(), group=self.group)
+        return torch.stack(parts)
+
+
+class CudaSegmentOps:
+    """The segment phases through the C ABI (lz_gla_seg_* in include/lizard_cuda.h)."""
+
+    def __init__(self, B, H, L, F, D, per_head, device):
+        self.lib = _lib.load()
+        self.dims = (B, H, L, F, D)
+        self.per_head = per_head
+        self.device = device
+        self.nsum = self.lib.lz_gla_seg_summary_floats(B, H, F, D)
+        nbytes = self.lib.lz_gla_seg_workspace_bytes(B, H, L, F, D)
+        self.ws = torch.empty(nbytes, device=device, dtype=torch.uint8)
+
+    def _call(self, name, *args):
+        with torch.cuda.device(self.device):
+            rc = getattr(self.lib, name)(*args)
+        _lib.check(rc, name)
+
+    def _stream(self):
+        return _lib.stream_of(self.ws)
+
+    def fwd_begin(self, fk, v, lg):
+        B, H, L, F, D = self.dims
+        summary = torch.empty(self.nsum, device=self.device, dtype=torch.float32)
+        self._call("lz_gla_seg_fwd_begin", _lib.ptr(fk), _lib.ptr(v), _lib.ptr(lg), self.per_head,
+                   _lib.ptr(summary), _lib.ptr(self.ws), self.ws.numel(), B, H, L, F, D,
+                   self._stream())
+        return summary
+
+    def combine(self, summaries, rank, reverse):
+        B, H, L, F, D = self.dims
+        P = summaries.shape[0]
+        seed = torch.empty(B * H * F * (D + 1), device=self.device, dtype=torch.float32)
+        self._call("lz_gla_seg_combine", _lib.ptr(summaries), P, rank, int(reverse),
+                   _lib.ptr(seed), B, H, F, D, self._stream())
+        return seed
+
+    def fwd_end(self, fq, fk, v, lg, seed, save):
+        B, H, L, F, D = self.dims
+        y = torch.empty(B, H, L, D, device=self.device, dtype=torch.bfloat16)
+        saved = None
+        if save:
+            saved = torch.empty(self.lib.lz_gla_saved_bytes(B, H, L, F, D, 64),
+                                device=self.device, dtype=torch.uint8)
+        self._call("lz_gla_seg_fwd_end", _lib.ptr(fq), _lib.ptr(fk), _lib.ptr(v), _lib.ptr(lg),
+                   self.per_head, _lib.ptr(seed), _lib.ptr(y), _lib.ptr(saved),
+                   0 if saved is None else saved.numel(), _lib.ptr(self.ws), self.ws.numel(),
+                   B, H, L, F, D, self._stream())
+        return y, saved
+
+    def bwd_begin(self, fq, saved, dy):
+        B, H, L, F, D = self.dims
+        summary = torch.empty(self.nsum, device=self.device, dtype=torch.float32)
+        self._call("lz_gla_seg_bwd_begin", _lib.ptr(fq), _lib.ptr(saved), saved.numel(),
+                   _lib.ptr(dy), _lib.ptr(summary), _lib.ptr(self.ws), self.ws.numel(),
+                   B, H, L, F, D, self._stream())
+        return summary
+
+    def bwd_end(self, fq, fk, v, saved, dy, dseed, seeded_forward, grad_dtype):
+        B, H, L, F, D = self.dims
+        gdt = _lib.LZ_DTYPE_BF16 if grad_dtype == torch.bfloat16 else _lib.LZ_DTYPE_F32
+        dfq = torch.empty(B, H, L, F, device=self.device, dtype=grad_dtype)
+        dfk = torch.empty_like(dfq)
+        dv = torch.empty(B, H, L, D, device=self.device, dtype=grad_dtype)
+        shape = (B, H, L) if self.per_head else (B, L)
+        dlg = torch.empty(shape, device=self.device, dtype=torch.float32)
+        self._call("lz_gla_seg_bwd_end", _lib.ptr(fq), _lib.ptr(fk), _lib.ptr(v), self.per_head,
+                   _lib.ptr(saved), saved.numel(), _lib.ptr(dy), _lib.ptr(dseed),
+                   int(seeded_forward), _lib.ptr(dfq), _lib.ptr(dfk), _lib.ptr(dv), gdt,
+                   _lib.ptr(dlg), _lib.ptr(self.ws), self.ws.numel(), B, H, L, F, D,
+                   self._stream())
+        return dfq, dfk, dv, dlg
+
+    def gate_offset(self, dlg, totals, rank):
+        rows, L = dlg.numel() // dlg.shape[-1], dlg.shape[-1]
+        self._call("lz_gla_seg_gate_offset", _lib.ptr(dlg), _lib.ptr(totals), totals.shape[0],
+                   rank, rows, L, self._stream())
+
+
+def forward_phases(ops, comm, fq, fk, v, lg, save):
+    """One rank's forward: returns (y, saved, seeded)."""
+    summary = ops.fwd_begin(fk, v, lg)
+    summaries = comm.all_gather(summary)
+    seed = ops.combine(summaries, comm.rank, reverse=False) if comm.rank > 0 else None
+    y, saved = ops.fwd_end(fq, fk, v, lg, seed, save)
+    return y, saved, seed is not None
+
+
+def backward_phases(ops, comm, fq, fk, v, saved, dy, seeded, grad_dtype):
+    """One rank's backward: returns (dfq, dfk, dv, dlog_gamma) for its segment."""
+    summary = ops.bwd_begin(fq, saved, dy)
+    summaries = comm.all_gather(summary)
+    last = comm.rank == comm.size - 1
+    dseed = None if last else ops.combine(summaries, comm.rank, reverse=True)
+    dfq, dfk, dv, dlg = ops.bwd_end(fq, fk, v, saved, dy, dseed, seeded, grad_dtype)
+    totals = comm.all_gather(dlg[..., 0].contiguous().reshape(-1))
+    ops.gate_offset(dlg, totals, comm.rank)
+    return dfq, dfk, dv, dlg
+
+
+class _GLASeq(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, fq, fk, v, log_gamma, comm, ops):
+        ctx.dtypes = (fq.dtype, fk.dtype, v.dtype, log_gamma.dtype)
+        fq, fk, v = (t.to(torch.bfloat16).contiguous() for t in (fq, fk, v))
+        lg = log_gamma.float().contiguous()
+        save = any(ctx.needs_input_grad[:4])
+        y, saved, seeded = forward_phases(ops, comm, fq, fk, v, lg, save)
+        if save:
+            ctx.save_for_backward(fq, fk, v, saved)
+        ctx.comm, ctx.ops, ctx.seeded = comm, ops, seeded
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        fq, fk, v, saved = ctx.saved_tensors
+        dy = dy.to(torch.bfloat16).contiguous()
+        all_bf16 = all(d == torch.bfloat16 for d in ctx.dtypes[:3])
+        gtorch = torch.bfloat16 if all_bf16 else torch.float32
+        grads = backward_phases(ctx.ops, ctx.comm, fq, fk, v, saved, dy, ctx.seeded, gtorch)
+        dfq, dfk, dv, dlg = (g.to(d) for g, d in zip(grads, ctx.dtypes))
+        return dfq, dfk, dv, dlg, None, None
+
+
+def gla_seqpar(fq, fk, v, log_gamma, group=None, comm=None, ops=None):
+    """gla() of one sequence split over the ranks of `group` (default: the world).
+
+    fq, fk [B, H, Ls, F], v [B, H, Ls, D] and log_gamma [B, Ls] or [B, H, Ls] are
+    this rank's contiguous slice of the sequence (rank order = sequence order;
+    the slices may differ in length). Returns this rank's slice of
+    y (bf16); gradients flow to all four inputs as in gla(). `comm` (an object
+    with rank, size and all_gather) and `ops` (the segment phases) default to
+    torch.distributed and the CUDA library.
+    """
+    B, H, L, F, D, per_head = _shapes(fq, fk, v, log_gamma)
+    if comm is None:
+        comm = DistExchange(group)
+    if ops is None:
+        _lib.require_cuda(fq, fk, v, log_gamma)
+        ops = CudaSegmentOps(B, H, L, F, D, per_head, fq.device)
+    return _GLASeq.apply(fq, fk, v, log_gamma, comm, ops)

@@ -1,0 +1,98 @@
+"""Sequence-parallel GLA orchestration over gloo ranks on the CPU.
+
+Each rank runs lizard_cuda.seqpar's real forward/backward orchestration with
+the float64 segment oracle (tests/seq_oracle.py) in place of the CUDA phases;
+every rank's slice of y and of all four gradients must match the unsharded
+oracle. World sizes 2 and 3, equal and unequal slices, per-token and per-head
+gates.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from conftest import ROOT
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs(B, H, L, F, D, per_head, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    bf = lambda t: t.bfloat16().float()  # noqa: E731  (values the kernels see)
+    fq = bf(torch.nn.functional.softplus(torch.randn(B, H, L, F, generator=g)) / F ** 0.5)
+    fk = bf(torch.nn.functional.softplus(torch.randn(B, H, L, F, generator=g)) / F ** 0.5)
+    v = bf(torch.randn(B, H, L, D, generator=g))
+    lg = torch.nn.functional.logsigmoid(2 + torch.randn((B, H, L) if per_head else (B, L),
+                                                        generator=g))
+    dy = bf(torch.randn(B, H, L, D, generator=g))
+    return fq, fk, v, lg, dy
+
+
+def _worker(rank, world, port, bounds, per_head, errq):
+    import sys
+    for p in (ROOT, ROOT / "lizard-reproduction_b200", ROOT / "oracle", ROOT / "tests"):
+        sys.path.insert(0, str(p))
+    try:
+        import torch.distributed as dist
+        import lizard_oracle as orc
+        from lizard_cuda import seqpar
+        from seq_oracle import OracleSegmentOps
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=__import__("datetime").timedelta(seconds=60))
+        B, H, F, D = 2, 3, 8, 6
+        L = bounds[-1]
+        fq, fk, v, lg, dy = _inputs(B, H, L, F, D, per_head)
+        a, b = bounds[rank], bounds[rank + 1]
+        sl = lambda t: t[..., a:b, :] if t.dim() == 4 else t[..., a:b]  # noqa: E731
+        leaves = [sl(t).clone().requires_grad_() for t in (fq, fk, v, lg)]
+        y = seqpar.gla_seqpar(*leaves, ops=OracleSegmentOps(per_head, H))
+        y.backward(sl(dy))
+        # unsharded float64 oracle
+        ref_leaves = [t.double().clone().requires_grad_() for t in (fq, fk, v, lg)]
+        ref = orc.gla(*ref_leaves)
+        ref.backward(dy.double())
+        checks = [("y", y, sl(ref.detach()))] + [
+            (n, lf.grad, sl(r.grad)) for n, lf, r in zip(("dfq", "dfk", "dv", "dlog_gamma"),
+                                                        leaves, ref_leaves)]
+        for n, got, want in checks:
+            err = (got.double() - want).abs().max().item() / want.abs().max().item()
+            if not err < 1e-5:
+                raise AssertionError(f"rank {rank}: {n} max rel err {err:.3e}")
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as e:  # report to the parent, then fail this process
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+@pytest.mark.parametrize("bounds,per_head", [
+    ((0, 96, 192), False),        # 2 ranks, equal 96-token slices (chunk tails on both)
+    ((0, 128, 200, 330), True),   # 3 ranks, unequal slices, per-head gates
+    ((0, 64, 128, 130), False),   # 3 ranks, a 2-token last slice
+])
+def test_seqpar_matches_unsharded_oracle(bounds, per_head):
+    world = len(bounds) - 1
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, bounds, per_head, errq))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            errs.append("a rank did not finish in 180 s")
+    assert not errs and all(p.exitcode == 0 for p in procs), errs
