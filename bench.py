@@ -205,6 +205,107 @@ def make_cpu_inputs(torch):
 
 
 # ---------------------------------------------------------------- ours
+SEQ_L, SEQ_H, SEQ_FD = 16384, 32, 128
+
+
+def seqpar_measure(torch, lizard_cuda, device, dist, world, rank, steps=10, warmup=3):
+    """Config 4's long sequence: B=1, L=16384, H=32, F=D=128, per-head gate. With
+    N ranks each owns L/N tokens of every head and the ranks hand the chunk
+    state over through lizard_cuda.seqpar (one all_gather per direction);
+    with one GPU it is the plain call. Device ms per step, max over ranks,
+    for the forward (no grad) and forward+backward; L2 is not flushed (every
+    rank's inputs are >= 201 MB / N per tensor)."""
+    import torch.nn.functional as F
+    from lizard_cuda import seqpar
+    Ls = SEQ_L // world
+    g = torch.Generator(device=device).manual_seed(4321 + rank)
+    shape = (1, SEQ_H, Ls, SEQ_FD)
+    fq = (F.softplus(torch.randn(shape, generator=g, device=device)) / math.sqrt(SEQ_FD)).bfloat16()
+    fk = (F.softplus(torch.randn(shape, generator=g, device=device)) / math.sqrt(SEQ_FD)).bfloat16()
+    v = torch.randn(shape, generator=g, device=device).bfloat16()
+    lg = F.logsigmoid(3 + 1.5 * torch.randn(1, SEQ_H, Ls, generator=g, device=device))
+    dy = torch.randn(shape, generator=g, device=device).bfloat16()
+    call = (lambda *a: lizard_cuda.gla(*a)) if world == 1 else seqpar.gla_seqpar
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s.elapsed_time(e) / steps], device=device, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.no_grad():
+        fwd = timed(lambda: call(fq, fk, v, lg))
+    leaves = [t.detach().requires_grad_() for t in (fq, fk, v, lg)]
+
+    def step():
+        for t in leaves:
+            t.grad = None
+        call(*leaves).backward(dy)
+    both = timed(step)
+    return {"workload": f"gla config 4 long sequence: B=1 L={SEQ_L} H={SEQ_H} F=D={SEQ_FD}, "
+                        f"per-head gate, {world} rank(s) x {Ls} tokens",
+            "exchange": "none" if world == 1 else "one NCCL all_gather of the chunk-state "
+                                                  "summaries per direction",
+            "fwd_ms": fwd, "fwd_tokens_per_s": SEQ_L / (fwd / 1e3),
+            "fwd_bwd_ms": both, "fwd_bwd_tokens_per_s": SEQ_L / (both / 1e3)}
+
+
+def length_sweep(torch, lizard_cuda, device, lengths=(512, 1024, 2048, 4096, 8192, 16384),
+                 steps=5, warmup=3):
+    """Config 4 sweep: B=16, H=32, F=D=128, per-head gate; device ms of the
+    forward (no grad) and of forward+backward at each L (inputs >= 67 MB per
+    tensor; from L=1024 on every tensor is larger than L2)."""
+    import torch.nn.functional as F
+    out = {}
+    for Lx in lengths:
+        g = torch.Generator(device=device).manual_seed(99)
+        shape = (16, 32, Lx, 128)
+        fq = (F.softplus(torch.randn(shape, generator=g, device=device)) / math.sqrt(128)).bfloat16()
+        fk = (F.softplus(torch.randn(shape, generator=g, device=device)) / math.sqrt(128)).bfloat16()
+        v = torch.randn(shape, generator=g, device=device).bfloat16()
+        lg = F.logsigmoid(3 + 1.5 * torch.randn(16, 32, Lx, generator=g, device=device))
+        dy = torch.randn(shape, generator=g, device=device).bfloat16()
+        leaves = [t.detach().requires_grad_() for t in (fq, fk, v, lg)]
+
+        def timed(fn):
+            for _ in range(warmup):
+                fn()
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(steps):
+                fn()
+            e.record()
+            torch.cuda.synchronize()
+            return s.elapsed_time(e) / steps
+
+        with torch.no_grad():
+            fwd = timed(lambda: lizard_cuda.gla(fq, fk, v, lg))
+
+        def step():
+            for t in leaves:
+                t.grad = None
+            lizard_cuda.gla(*leaves).backward(dy)
+        both = timed(step)
+        tok = 16 * Lx
+        out[f"L{Lx}"] = {"fwd_ms": fwd, "fwd_tokens_per_s": tok / (fwd / 1e3),
+                         "fwd_bwd_ms": both, "fwd_bwd_tokens_per_s": tok / (both / 1e3)}
+        del fq, fk, v, lg, dy, leaves
+        torch.cuda.empty_cache()
+    return out
+
+
 def secondary(torch, lizard_cuda, device, steps=50, warmup=5):
     """Config 3 (B=1, L=2048, H=32, F=D=64): GLA fwd+bwd with a per-token gate
     and SWA fwd+bwd (window 64, 4 sinks); device ms per step.
@@ -374,8 +475,13 @@ def run_ours(args, torch):
     e2e_ms = float(t2.item())
 
     side = None
-    if rank == 0 and not args.no_secondary:
-        side = secondary(torch, lizard_cuda, device)
+    seq = None
+    if not args.no_secondary:
+        seq = seqpar_measure(torch, lizard_cuda, device, dist, world, rank)
+        if rank == 0:
+            side = secondary(torch, lizard_cuda, device)
+            if world == 1:
+                side["cfg4_length_sweep"] = length_sweep(torch, lizard_cuda, device)
 
     cpu = None
     if rank == 0 and world == 1:
@@ -421,6 +527,8 @@ def run_ours(args, torch):
     }
     if side:
         line["secondary"] = side
+    if seq:
+        line["seqpar"] = seq
     print(json.dumps(line), flush=True)
 
 
