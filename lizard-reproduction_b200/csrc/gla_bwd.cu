@@ -517,32 +517,33 @@ gla_bwd_chunk_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
 // --------------------------------------------------- 4. log-gate gradient
 // out[j] = sum_{i >= j} x[i], x = dG (per-head gate) or the sum over heads of
 // dG (gate shared by the heads of a batch row): the autograd of the cumsum and
-// expand of gla.py:260-262. One CTA of 64 threads per (gate row, chunk): the
-// carry is the sum of the later chunks' totals (dGt), added in a fixed order,
-// then a suffix scan over the chunk's rows. Deterministic.
-__global__ void __launch_bounds__(64)
+// expand of gla.py:260-262. One CTA of C threads (C = the chunk length of dGt,
+// 64 or 128) per (gate row, chunk): the carry is the sum of the later chunks'
+// totals (dGt), added in a fixed order, then a suffix scan over the chunk's
+// rows. Deterministic.
+__global__ void __launch_bounds__(128)
 gla_bwd_gate_kernel(const float* __restrict__ dG, const float* __restrict__ dGt,
                     float* __restrict__ out, int H, int L, int NT, int gate_per_head) {
-  __shared__ float red[64];
-  __shared__ float wtot[2];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float red[128];
+  __shared__ float wtot[4];
+  const int C = blockDim.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = blockIdx.x % NT, row = blockIdx.x / NT;
   const int h0 = gate_per_head ? row : row * H;  // first batch*head row of this gate row
   const int nh = gate_per_head ? 1 : H;
   const int later = NT - 1 - n;
   float c = 0.f;
-  for (int i = tid; i < nh * later; i += 64) {
+  for (int i = tid; i < nh * later; i += C) {
     const int h = i / later, m = n + 1 + i % later;
     c += dGt[(size_t)(h0 + h) * NT + m];
   }
   red[tid] = c;
   __syncthreads();
-  for (int w = 32; w > 0; w >>= 1) {
+  for (int w = C / 2; w > 0; w >>= 1) {
     if (tid < w) red[tid] += red[tid + w];
     __syncthreads();
   }
   const float carry = red[0];
-  const int r0 = n * kC, j = r0 + tid;
+  const int j = n * C + tid;
   float x = 0.f;
   if (j < L) {
     const float* p = dG + (size_t)h0 * L + j;
@@ -555,7 +556,18 @@ gla_bwd_gate_kernel(const float* __restrict__ dG, const float* __restrict__ dGt,
   }
   if (lane == 0) wtot[warp] = x;
   __syncthreads();
-  if (j < L) out[(size_t)row * L + j] = carry + x + (warp == 0 ? wtot[1] : 0.f);
+  float after = 0.f;
+  for (int w = warp + 1; w < C / 32; ++w) after += wtot[w];
+  if (j < L) out[(size_t)row * L + j] = carry + x + after;
+}
+
+int launch_gate(const float* dg, const float* dgt, float* dlg, int B, int H, int L, int NT, int C,
+                int gph, cudaStream_t stream) {
+  const int gate_rows = gph ? B * H : B;
+  gla_bwd_gate_kernel<<<(unsigned)((long long)gate_rows * NT), C, 0, stream>>>(dg, dgt, dlg, H, L,
+                                                                               NT, gph);
+  count_launches(1);
+  return check_launch("gla_bwd_gate_kernel");
 }
 
 std::mutex g_attr_mu;
@@ -622,11 +634,7 @@ int gla_bwd_tail(const bf16* fq, const bf16* fk, const bf16* v, int gph, const G
 #undef LZ_CHUNK_CASE
   if (rc) return rc;
 
-  const int gate_rows = gph ? BH : B;
-  gla_bwd_gate_kernel<<<(unsigned)((long long)gate_rows * NT), 64, 0, stream>>>(
-      wk.dg, wk.dgt, dlg, H, L, NT, gph);
-  count_launches(1);
-  return check_launch("gla_bwd_gate_kernel");
+  return launch_gate(wk.dg, wk.dgt, dlg, B, H, L, NT, kC, gph, stream);
 }
 
 int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
@@ -637,6 +645,14 @@ int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int 
   const int BH = B * H;
   const int NT = (int)gla_nt(L);
   int rc = LZ_OK;
+  if (gla_saved_chunk(B, H, L, F, D, fq, fk, v) == 128) {
+    // states on the tensor-core forward's 128-token boundaries
+    rc = gla_bwd_tc_states(fq, dy, sv, wk, B, H, L, stream);
+    if (rc) return rc;
+    rc = gla_bwd_tc_chunks(fq, fk, v, dy, sv, wk, dfq, dfk, dv, gdt, B, H, L, 0, 0, stream);
+    if (rc) return rc;
+    return launch_gate(wk.dg, wk.dgt, dlg, B, H, L, (L + 127) / 128, 128, gph, stream);
+  }
   if (wk.inc) {
     rc = gla_bwd_split_states(fq, dy, sv, wk, B, H, L, F, D, stream);
     if (rc) return rc;

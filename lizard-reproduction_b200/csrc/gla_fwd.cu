@@ -218,118 +218,6 @@ gla_fwd_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
   }
 }
 
-// Forward walk over 64-token chunks writing the state entering each chunk,
-// S_n (bf16) and z_n (fp32), for the backward. Used in training mode when the
-// forward output came from the 128-token-chunk tensor-core kernel, whose
-// states sit on other boundaries. Same recurrence as gla.py:44-57.
-// Grid: (F/64 feature blocks) x (D/64 value blocks) x BH; 4 warps, each warp
-// owns 16 state rows x 64 columns.
-struct FwdStateSmem {
-  static constexpr int LD = 64 + 8;
-  static constexpr size_t tile = (size_t)kChunk * LD * 2;
-  static constexpr size_t k = 0;              // 2 stages
-  static constexpr size_t v = k + 2 * tile;   // 2 stages
-  static constexpr size_t bytes = v + 2 * tile;
-};
-
-__global__ void __launch_bounds__(128)
-gla_fwd_state_kernel(const bf16* __restrict__ fk, const bf16* __restrict__ v,
-                     const float* __restrict__ G, bf16* __restrict__ s_out,
-                     float* __restrict__ z_out, int L, int F, int D, int NT, int nfb, int ndb,
-                     int vec_f, int vec_d) {
-  using SM = FwdStateSmem;
-  constexpr int LD = SM::LD;
-  extern __shared__ __align__(128) unsigned char smem[];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int gq = lane >> 2, cq = lane & 3;
-  int idx = blockIdx.x;
-  const int db = idx % ndb;
-  idx /= ndb;
-  const int fb = idx % nfb;
-  const int bh = idx / nfb;
-  const int f0 = fb * 64, d0 = db * 64;
-  const bf16* K = fk + (size_t)bh * L * F;
-  const bf16* V = v + (size_t)bh * L * D;
-  const float* Gr = G + (size_t)bh * L;
-  auto sK = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::k + s * SM::tile); };
-  auto sV = [&](int s) { return reinterpret_cast<bf16*>(smem + SM::v + s * SM::tile); };
-  auto issue = [&](int n, int s) {
-    stage_tile<kChunk, 64, 128>(sK(s), LD, K, F, n * kChunk, L, f0, F, vec_f);
-    stage_tile<kChunk, 64, 128>(sV(s), LD, V, D, n * kChunk, L, d0, D, vec_d);
-    cp_async_commit();
-  };
-  float acc[8][4];
-#pragma unroll
-  for (int c = 0; c < 8; ++c)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[c][e] = 0.f;
-  float z = 0.f;
-  issue(0, 0);
-  for (int n = 0; n < NT; ++n) {
-    const int s = n & 1;
-    {
-      const size_t base = ((size_t)bh * NT + n) * F * D;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const int f = f0 + 16 * warp + gq, d = d0 + 8 * nt + 2 * cq;
-        if (f < F) {
-          if (d < D) s_out[base + (size_t)f * D + d] = __float2bfloat16_rn(acc[nt][0]);
-          if (d + 1 < D) s_out[base + (size_t)f * D + d + 1] = __float2bfloat16_rn(acc[nt][1]);
-        }
-        if (f + 8 < F) {
-          if (d < D) s_out[base + (size_t)(f + 8) * D + d] = __float2bfloat16_rn(acc[nt][2]);
-          if (d + 1 < D) s_out[base + (size_t)(f + 8) * D + d + 1] = __float2bfloat16_rn(acc[nt][3]);
-        }
-      }
-      if (db == 0 && tid < 64 && f0 + tid < F) z_out[((size_t)bh * NT + n) * F + f0 + tid] = z;
-    }
-    if (n + 1 == NT) break;  // the state after the last chunk is not needed
-    issue(n + 1, s ^ 1);
-    asm volatile("cp.async.wait_group 1;\n" ::);
-    __syncthreads();
-    const int r0 = n * kChunk, nvalid = min(kChunk, L - r0);
-    const float start = n > 0 ? Gr[r0 - 1] : 0.f;
-    const float end = Gr[r0 + nvalid - 1];
-    const float decay = __expf(end - start);
-    bf16* k = sK(s);
-    for (int i = tid; i < kChunk * 8; i += 128) {
-      const int t = i >> 3, c = (i & 7) * 8;
-      const float sc = t < nvalid ? __expf(end - Gr[r0 + t]) : 0.f;
-      uint4* p = reinterpret_cast<uint4*>(k + t * LD + c);
-      uint4 w = *p;
-      w.x = pack_bf16(bf16_lo(w.x) * sc, bf16_hi(w.x) * sc);
-      w.y = pack_bf16(bf16_lo(w.y) * sc, bf16_hi(w.y) * sc);
-      w.z = pack_bf16(bf16_lo(w.z) * sc, bf16_hi(w.z) * sc);
-      w.w = pack_bf16(bf16_lo(w.w) * sc, bf16_hi(w.w) * sc);
-      *p = w;
-    }
-    __syncthreads();
-    if (tid < 64) {
-      float sum = 0.f;
-#pragma unroll 8
-      for (int t = 0; t < kChunk; ++t) sum += __bfloat162float(k[t * LD + tid]);
-      z = z * decay + sum;
-    }
-#pragma unroll
-    for (int c = 0; c < 8; ++c)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[c][e] *= decay;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint32_t a[4];
-      lda_tr(a, k, LD, 16 * warp, 16 * j);
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        uint32_t bb[4];
-        ldb_kn(bb, sV(s), LD, 16 * j, 16 * np);
-        mma16816(acc[2 * np], a, bb[0], bb[1]);
-        mma16816(acc[2 * np + 1], a, bb[2], bb[3]);
-      }
-    }
-    __syncthreads();
-  }
-}
-
 namespace {
 
 template <int FP, int DV>
@@ -374,35 +262,14 @@ int gla_fwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int 
             cudaStream_t stream) {
   if (fw.inc) return gla_fwd_split_run(fq, fk, v, lg, gph, y, sv, fw, B, H, L, F, D, stream);
   const int BH = B * H;
-  {
-    int rc = gla_fwd_tc(fq, fk, v, lg, gph, y, sv, B, H, L, F, D, stream);
-    if (rc == LZ_OK && sv.s) {
-      // 64-token chunk states for the backward
-      static std::mutex mu;
-      static bool done[64] = {false};
-      int dev = 0;
-      cudaGetDevice(&dev);
-      {
-        std::lock_guard<std::mutex> lock(mu);
-        if (dev < 64 && !done[dev]) {
-          cudaError_t e = cudaFuncSetAttribute(gla_fwd_state_kernel,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)FwdStateSmem::bytes);
-          if (e != cudaSuccess) {
-            set_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-            return LZ_ERR_CUDA;
-          }
-          done[dev] = true;
-        }
-      }
-      const int NT = ceil_div(L, kChunk), nfb = ceil_div(F, 64), ndb = ceil_div(D, 64);
-      const int vf = (F % 8 == 0) && aligned16(fk), vd = (D % 8 == 0) && aligned16(v);
-      gla_fwd_state_kernel<<<(unsigned)((long long)BH * nfb * ndb), 128, FwdStateSmem::bytes,
-                             stream>>>(fk, v, sv.g, sv.s, sv.z, L, F, D, NT, nfb, ndb, vf, vd);
-      count_launches(1);
-      rc = check_launch("gla_fwd_state_kernel");
-    }
+  if (gla_saved_chunk(B, H, L, F, D, fq, fk, v) == 128) {
+    // tensor-core kernel; in training it also saves the 128-token chunk states
+    const int rc = gla_fwd_tc(fq, fk, v, lg, gph, y, sv, B, H, L, F, D, stream);
     if (rc != LZ_ERR_UNSUPPORTED) return rc;
+    if (sv.y32) {
+      set_error("gla_fwd: the tensor-core forward is unavailable (tensor map encoding failed)");
+      return LZ_ERR_CUDA;
+    }
   }
   const int FP = F <= 32 ? 32 : F <= 64 ? 64 : F <= 128 ? 128 : 256;
   int DV = D <= 16 ? 16 : D <= 32 ? 32 : (FP <= 128 ? 64 : 32);

@@ -14,7 +14,10 @@
 //    thread)       S <- 2^(end-start) S + dS (fp32, registers) -> bf16 S (smem)
 //
 // This is the chunked GLA of the reference (src/kernels/gla.py:19-101) with
-// 128-token chunks; the per-chunk state never leaves the SM. G is the running
+// 128-token chunks; the running state stays on the SM. In training mode the
+// kernel also stores y in fp32, the row sums, G, and the bf16 state and fp32
+// normaliser entering every 128-token chunk (TMA store of the operand block)
+// for the backward (gla_bwd_tc.cu). G is the running
 // sum of the log gates, kept in base-2 units (g2 = G log2 e) so every decay is
 // one ex2. The normaliser state z is fp32 in shared memory and den_i = Q~_i.z
 // is summed on the CUDA cores; the intra-chunk row sum uses the same
@@ -44,7 +47,7 @@ constexpr int kSmemBytes = kOffMisc + kMiscBytes;  // = 232448, the sm_100 maxim
 // den_inter = Q~ . (row 1 + row 2) land in TMEM columns; the products of the
 // other rows land in columns that are never read, so the remaining bytes hold
 // barriers and per-chunk scalars.
-constexpr int kMiscBars = 384;    // 12 mbarriers (rows 3..)
+constexpr int kMiscBars = 384;    // up to 16 mbarriers (rows 3..)
 constexpr int kMiscGS = 512;      // (start2, end2) per chunk parity
 constexpr int kMiscScan = 544;    // 4 warp totals
 constexpr int kMiscTmem = 560;    // TMEM base address
@@ -57,7 +60,7 @@ constexpr uint32_t kTSA = 0, kTO = 128, kTSF = 256, kTZ = 384, kTA = 400, kTDI =
                    kTDQ = 480, kTCols = 512;
 
 enum { BAR_FULL0 = 0, BAR_FULL1, BAR_EMPTY0, BAR_EMPTY1, BAR_SFULL, BAR_AREADY, BAR_OFULL,
-       BAR_SREADY, BAR_GATE, BAR_SFDONE, BAR_COUNT };
+       BAR_SREADY, BAR_GATE, BAR_SFDONE, BAR_SSTAGE, BAR_DSYNC, BAR_YSYNC, BAR_COUNT };
 
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 decay, warps 6-9 output
 
@@ -72,10 +75,11 @@ __device__ __forceinline__ uint4 scale8(uint4 w, float sc) {
 __global__ void __launch_bounds__(kThreads, 1)
 gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap ty,
-                  const float* __restrict__ lg,
+                  const __grid_constant__ CUtensorMap ts, const float* __restrict__ lg,
                   int gate_per_head, int H, int L, int NT, bf16* __restrict__ y,
                   float* __restrict__ y32, float* __restrict__ den_out,
-                  float* __restrict__ g_out) {
+                  float* __restrict__ g_out, bf16* __restrict__ s_out,
+                  float* __restrict__ z_out) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   if (smem_u32(smem_raw) & 1023) {  // the tile swizzle needs a 1024-byte aligned window
     if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 99u);
@@ -107,6 +111,9 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     tc::mbar_init(&bars[BAR_SREADY], 128);
     tc::mbar_init(&bars[BAR_GATE], 128);
     tc::mbar_init(&bars[BAR_SFDONE], 1);
+    tc::mbar_init(&bars[BAR_SSTAGE], 128);  // output warps around the S store
+    tc::mbar_init(&bars[BAR_DSYNC], 128);   // decay warps: gate scan
+    tc::mbar_init(&bars[BAR_YSYNC], 128);   // output warps: y staged
     tc::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -114,6 +121,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     tc::prefetch_tmap(&tk);
     tc::prefetch_tmap(&tv);
     tc::prefetch_tmap(&ty);
+    if (save) tc::prefetch_tmap(&ts);
   }
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, kTCols);
@@ -233,6 +241,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
                        (n > 0 || j > 0) ? 1u : 0u);
           tc::mma_commit(&bars[BAR_SFDONE]);
           tc::mma_commit(&bars[BAR_EMPTY0 + st]);
+          if (n == NT - 1) tc::mbar_wait(&bars[BAR_SFDONE], n & 1, 17);  // none in flight at exit
         }
       }
     }
@@ -243,6 +252,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
     const float* LG = lg + (size_t)(gate_per_head ? bh : b) * L;
     float carry = 0.f;
+    uint32_t dphase = 0;
     float lg_next = (r < L) ? LG[r] : 0.f;
     for (int n = 0; n < NT; ++n) {
       const int r0 = n * kC;
@@ -259,7 +269,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         if (lane >= o) x += u;
       }
       if (lane == 31) sScan[quad] = x;
-      tc::named_bar_sync(1, 128);
+      if (!__all_sync(0xffffffffu, tc::group_sync(&bars[BAR_DSYNC], dphase, 14))) break;
       float pre = 0.f;
 #pragma unroll
       for (int qq = 0; qq < 4; ++qq)
@@ -271,7 +281,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       const float start2 = carry;
       if (r == 0) sGS[(n & 1) * 2] = start2;
       if (r == nvalid - 1) sGS[(n & 1) * 2 + 1] = g2;
-      tc::named_bar_sync(1, 128);
+      if (!__all_sync(0xffffffffu, tc::group_sync(&bars[BAR_DSYNC], dphase, 15))) break;
       const float end2 = sGS[(n & 1) * 2 + 1];
       carry = end2;
       tc::mbar_arrive(&bars[BAR_GATE]);
@@ -362,6 +372,13 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     unsigned char* zblk = misc + (r >> 6) * 1024;
     const int zcol = ((((r & 63) >> 3) ^ 1) << 4) + (r & 7) * 2;
     const int zcol2 = ((((r & 63) >> 3) ^ 2) << 4) + (r & 7) * 2;
+    uint32_t sstage_phase = 0, yphase = 0;
+    if (save) {  // the state entering chunk 0 is zero
+      uint4* p = reinterpret_cast<uint4*>(s_out + ((size_t)bh * NT * 128 + r) * 128);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) p[i] = make_uint4(0u, 0u, 0u, 0u);
+      z_out[(size_t)bh * NT * 128 + r] = 0.f;
+    }
     for (int n = 0; n < NT; ++n) {
       const int r0 = n * kC;
       const int nvalid = min(kC, L - r0);
@@ -402,7 +419,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         }
       }
       tc::fence_proxy_async_smem();
-      tc::named_bar_sync(2, 128);
+      if (!__all_sync(0xffffffffu, tc::group_sync(&bars[BAR_YSYNC], yphase, 16))) break;
       if (r == 0) {
         tc::tma_store_3d(&ty, ystage, 0, r0, bh);
         tc::tma_store_3d(&ty, ystage + 16384, 64, r0, bh);
@@ -420,6 +437,12 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         const float g2r = sG[r];
         const float zn = tc::tmem_ld1(trow + kTZ);
         tc::tmem_wait_ld();
+        if (save) {
+          z_out[((size_t)bh * NT + n + 1) * 128 + r] = zn;
+          // the previous S store must have read the staging block
+          if (r == 0) tc::bulk_wait_read0();
+          if (!__all_sync(0xffffffffu, tc::group_sync(&bars[BAR_SSTAGE], sstage_phase, 12))) break;
+        }
         {
           const bf16 zh = __float2bfloat16_rn(zn);
           *reinterpret_cast<bf16*>(zblk + 128 + zcol) = zh;
@@ -449,6 +472,15 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 #pragma unroll
             for (int j = 0; j < 16; ++j) sc[j] = __float_as_uint(sv[16 * q + j] * decay);
             tc::tmem_st16(trow + kTSF + 64 * hb + 16 * q, sc);
+          }
+        }
+        if (save) {  // bf16 S_{n+1} to HBM for the backward, from the operand block
+          tc::fence_proxy_async_smem();
+          if (!__all_sync(0xffffffffu, tc::group_sync(&bars[BAR_SSTAGE], sstage_phase, 13))) break;
+          if (r == 0) {
+            tc::tma_store_3d(&ts, base + kOffS, 0, (n + 1) * kC, bh);
+            tc::tma_store_3d(&ts, base + kOffS + 16384, 64, (n + 1) * kC, bh);
+            tc::bulk_commit();
           }
         }
         {
@@ -527,8 +559,16 @@ bool make_map(CUtensorMap* m, const void* ptr, int BH, int L, int cols) {
 int gla_fwd_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, bf16* y,
                const GlaSaved& sv, int B, int H, int L, int F, int D, cudaStream_t stream) {
   if (F != 128 || D != 128) return LZ_ERR_UNSUPPORTED;
-  if (!aligned16(fq) || !aligned16(fk) || !aligned16(v) || !aligned16(y)) return LZ_ERR_UNSUPPORTED;
-  if (sv.y32 && !aligned16(sv.y32)) return LZ_ERR_UNSUPPORTED;
+  if (!aligned16(fq) || !aligned16(fk) || !aligned16(v)) return LZ_ERR_UNSUPPORTED;
+  if (!aligned16(y) || (sv.y32 && (!aligned16(sv.y32) || !aligned16(sv.s)))) {
+    // training with these inputs saves 128-token chunk states, which only this
+    // kernel writes: the output buffers must suit its TMA stores
+    if (sv.y32) {
+      set_error("gla_fwd: y and the saved buffer must be 16-byte aligned when F = D = 128");
+      return LZ_ERR_INVALID_ARGUMENT;
+    }
+    return LZ_ERR_UNSUPPORTED;
+  }
   const int BH = B * H;
   CUtensorMap mq, mk, mv, my;
   if (!make_map(&mq, fq, BH, L, F) || !make_map(&mk, fk, BH, L, F) || !make_map(&mv, v, BH, L, D) ||
@@ -552,8 +592,10 @@ int gla_fwd_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
     }
   }
   const int NT = (L + kC - 1) / kC;
-  gla_fwd_tc_kernel<<<BH, kThreads, kSmemBytes, stream>>>(mq, mk, mv, my, lg, gph, H, L, NT, y, sv.y32,
-                                                     sv.den, sv.g);
+  CUtensorMap ms = my;  // unused (not prefetched, not stored) in inference
+  if (sv.y32 && !make_map(&ms, sv.s, BH, NT * kC, 128)) return LZ_ERR_UNSUPPORTED;
+  gla_fwd_tc_kernel<<<BH, kThreads, kSmemBytes, stream>>>(mq, mk, mv, my, ms, lg, gph, H, L, NT, y,
+                                                     sv.y32, sv.den, sv.g, sv.s, sv.z);
   count_launches(1);
   return check_launch("gla_fwd_tc_kernel");
 }

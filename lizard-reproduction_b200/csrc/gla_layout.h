@@ -68,6 +68,17 @@ inline bool gla_bwd_split(int B, int H, int L, int F, int D) {
 
 inline size_t gla_nt(int L) { return (size_t)((L + 63) / 64); }
 
+// Chunk length of the states in the saved buffer: 128 when the forward runs on
+// the tensor-core kernel (F = D = 128, the walk schedule, 16-byte aligned
+// inputs), whose states sit on 128-token boundaries; 64 otherwise. The forward
+// and the backward both decide with this rule. The saved buffer is sized for
+// 64-token chunks, which also holds the 128-token layout.
+inline int gla_saved_chunk(int B, int H, int L, int F, int D, const void* fq, const void* fk,
+                           const void* v) {
+  if (F != 128 || D != 128 || gla_fwd_split(B, H, L, F, D)) return 64;
+  return (aligned16(fq) && aligned16(fk) && aligned16(v)) ? 128 : 64;
+}
+
 inline size_t gla_saved_layout(int B, int H, int L, int F, int D, unsigned char* base,
                                GlaSaved* out) {
   const size_t BH = (size_t)B * H, NT = gla_nt(L);
@@ -187,6 +198,14 @@ int gla_bwd_tail(const bf16* fq, const bf16* fk, const bf16* v, int gph, const G
                  const bf16* dy, void* dfq, void* dfk, void* dv, int gdt, float* dlg,
                  const GlaWork& wk, int B, int H, int L, int F, int D, int s_seeded,
                  int ds_seeded, cudaStream_t stream);
+
+// Tensor-core backward for the 128-token chunk layout (gla_bwd_tc.cu).
+int gla_bwd_tc_states(const bf16* fq, const bf16* dy, const GlaSaved& sv, const GlaWork& wk,
+                      int B, int H, int L, cudaStream_t stream);
+int gla_bwd_tc_chunks(const bf16* fq, const bf16* fk, const bf16* v, const bf16* dy,
+                      const GlaSaved& sv, const GlaWork& wk, void* dfq, void* dfk, void* dv,
+                      int gdt, int B, int H, int L, int s_seeded, int ds_seeded,
+                      cudaStream_t stream);
 
 int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
             const GlaSaved& sv, const bf16* dy, void* dfq, void* dfk, void* dv, int gdt,

@@ -263,6 +263,48 @@ def test_gla_f128_d128_forward_backward(per_head, L):
         assert_grad(got, r, f"F=D=128 L={L} {n}")
 
 
+def _oracle_all_heads(fq, fk, v, lg, dy, group=8):
+    """Oracle fwd+bwd head group by head group (the dense L x L temporaries of
+    all heads at once would be large); the per-token gate gradient is summed."""
+    ys, g = [], [[], [], [], None]
+    for h0 in range(0, fq.shape[1], group):
+        sl = (slice(None), slice(h0, h0 + group))
+        lgs = lg[sl] if lg.dim() == 3 else lg
+        r, (a, b_, c, d) = oracle_gla(fq[sl], fk[sl], v[sl], lgs, dy[sl].bfloat16())
+        ys.append(r)
+        g[0].append(a), g[1].append(b_), g[2].append(c)
+        if lg.dim() == 3:
+            g[3] = d if g[3] is None else torch.cat([g[3], d], 1)
+        else:
+            g[3] = d if g[3] is None else g[3] + d
+    return torch.cat(ys, 1), [torch.cat(x, 1) for x in g[:3]] + [g[3]]
+
+
+@pytest.mark.parametrize("per_head", [True, False])
+def test_gla_f128_training_many_chunks(per_head):
+    """F = D = 128, 64 sequences of 1100 tokens (8 chunks of 128 and a tail):
+    with the walk schedule this is the tensor-core forward and backward."""
+    fq, fk, v, lg, dy = baseline_inputs(2, 32, 1100, 128, 128, per_head=per_head, seed=17)
+    y, grads = cuda_gla(fq, fk, v, lg, dy)
+    torch.cuda.synchronize()
+    ref, rgrads = _oracle_all_heads(fq, fk, v, lg, dy)
+    assert_output(y, ref, "F=D=128 L=1100 y")
+    for got, r, n in zip(grads, rgrads, GRAD_NAMES):
+        assert_grad(got, r, f"F=D=128 L=1100 {n}")
+
+
+def test_gla_f128_fp32_inputs_give_fp32_grads():
+    """fp32 fq, fk, v at F = D = 128: fp32 gradients (stored without staging)."""
+    fq, fk, v, lg, dy = baseline_inputs(1, 4, 520, 128, 128, per_head=True, seed=23)
+    fq, fk, v = fq.float(), fk.float(), v.float()
+    y, grads = cuda_gla(fq, fk, v, lg, dy)
+    assert all(g.dtype == torch.float32 for g in grads)
+    ref, rgrads = oracle_gla(fq, fk, v, lg, dy.bfloat16())
+    assert_output(y, ref, "fp32 F=D=128 y")
+    for got, r, n in zip(grads, rgrads, GRAD_NAMES):
+        assert_grad(got, r, f"fp32 F=D=128 {n}")
+
+
 def test_gla_f128_without_grad_gives_the_same_output():
     import lizard_cuda
     fq, fk, v, lg, _ = baseline_inputs(2, 2, 333, 128, 128, per_head=True, seed=12)
