@@ -25,8 +25,10 @@
 //
 // Warp roles in both kernels: warp 0 TMA, warp 1 MMA (one thread), warps 2-5
 // and 6-9 two groups of 128 threads, thread = TMEM lane = chunk row. Every
-// wait is an mbarrier wait bounded at 2 s (tc.cuh); group barriers are
-// mbarriers too, so a warp that gives up cannot leave others parked.
+// wait is an mbarrier wait bounded at 2 s (tc.cuh). The row groups synchronise
+// with bar.sync and never leave their code path early: a wait that gives up
+// sets the device flag, every later wait returns at once, and the groups run
+// on (writing in-bounds garbage) through every barrier to the end.
 #include <mutex>
 
 #include "common.cuh"
@@ -107,8 +109,7 @@ constexpr int kS1OffMisc = kS1OffDel + 2 * 4096;
 constexpr int kS1Smem = kS1OffMisc + 1024;
 constexpr uint32_t kT1H = 0, kT1Z = 128, kT1Cols = 256;
 
-enum { B1_FULL0 = 0, B1_FULL1, B1_EMPTY0, B1_EMPTY1, B1_QREADY, B1_HREADY, B1_HDONE, B1_STG,
-       B1_COUNT };
+enum { B1_FULL0 = 0, B1_FULL1, B1_EMPTY0, B1_EMPTY1, B1_QREADY, B1_HREADY, B1_HDONE, B1_COUNT };
 
 __global__ void __launch_bounds__(kThreads, 1)
 gla_bwd_state_tc_kernel(const __grid_constant__ CUtensorMap tq,
@@ -138,7 +139,6 @@ gla_bwd_state_tc_kernel(const __grid_constant__ CUtensorMap tq,
     tc::mbar_init(&bars[B1_QREADY], 128);
     tc::mbar_init(&bars[B1_HREADY], 128);
     tc::mbar_init(&bars[B1_HDONE], 1);
-    tc::mbar_init(&bars[B1_STG], 128);
     tc::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -211,7 +211,7 @@ gla_bwd_state_tc_kernel(const __grid_constant__ CUtensorMap tq,
       const float start = n > 0 ? G[rowb + r0 - 1] : 0.f;
       float qs = 0.f;
       if (valid) qs = __expf(G[rowb + r0 + t] - start) / fmaxf(den[rowb + r0 + t], kTiny);
-      if (!__all_sync(0xffffffffu, tc::mbar_wait(&bars[B1_FULL0 + st], (it >> 1) & 1, 25))) break;
+      tc::mbar_wait(&bars[B1_FULL0 + st], (it >> 1) & 1, 25);
       unsigned char* stage = base + st * kS1Stage;
       // delta_t = dy_t . y32_t
       float dl = 0.f;
@@ -251,14 +251,13 @@ gla_bwd_state_tc_kernel(const __grid_constant__ CUtensorMap tq,
     const int quad = warp & 3, f = quad * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
     unsigned char* stg = base + kS1OffStg;
-    uint32_t stg_phase = 0;
     for (int it = 0; it < NT; ++it) {
       const int n = NT - 1 - it, r0 = n * kC;
       const size_t chunk = (size_t)bh * NT + n;
       const int last = min(r0 + kC, L) - 1;
       const float lam = G[rowb + last] - (n > 0 ? G[rowb + r0 - 1] : 0.f);
       if (f == 0) tc::bulk_wait_read0();  // the previous store has read the staging tile
-      if (!__all_sync(0xffffffffu, tc::group_sync(&bars[B1_STG], stg_phase, 26))) break;
+      tc::named_bar_sync(1, 128);
       if (it == 0) {
         uint4 z[16];
 #pragma unroll
@@ -266,7 +265,7 @@ gla_bwd_state_tc_kernel(const __grid_constant__ CUtensorMap tq,
         tile_row_store(stg, f, z);
         dz_out[chunk * 128 + f] = 0.f;
       } else {
-        if (!__all_sync(0xffffffffu, tc::mbar_wait(&bars[B1_HDONE], (it - 1) & 1, 27))) break;
+        tc::mbar_wait(&bars[B1_HDONE], (it - 1) & 1, 27);
         tc::tc_fence_after();
         const float e = __expf(lam);
         float zz[32];
@@ -293,7 +292,7 @@ gla_bwd_state_tc_kernel(const __grid_constant__ CUtensorMap tq,
       tc::fence_proxy_async_smem();
       tc::tmem_wait_st();
       tc::tc_fence_before();
-      if (!__all_sync(0xffffffffu, tc::group_sync(&bars[B1_STG], stg_phase, 28))) break;
+      tc::named_bar_sync(1, 128);
       if (f == 0) {
         tc::tma_store_3d(&tds, stg, 0, n * kC, bh);
         tc::tma_store_3d(&tds, stg + 16384, 64, n * kC, bh);
@@ -321,8 +320,8 @@ constexpr int kSmem2 = kOMisc + kMiscBytes2;  // 232448
 constexpr int kMB = 0, kMTmem = 128, kMRed = 192, kMG = 256, kMZ = 768, kMDZ = 1280, kMDGa = 1792;
 constexpr uint32_t kTS = 0, kTP = 128, kTDV = 256, kT5 = 384, kT2Cols = 512;
 
-enum { B2_FULL = 0, B2_SPFULL, B2_EWSYNC, B2_EWDONE, B2_P3DONE, B2_T12FREE, B2_DSFULL, B2_P4DONE,
-       B2_DGA, B2_STGA, B2_STGB, B2_COUNT };
+enum { B2_FULL = 0, B2_SPFULL, B2_EWDONE, B2_P3DONE, B2_T12FREE, B2_DSFULL, B2_P4DONE, B2_DGA,
+       B2_COUNT };
 
 __global__ void __launch_bounds__(kThreads, 1)
 gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -363,15 +362,12 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
   if (tid == 0) {
     tc::mbar_init(&bars[B2_FULL], 1);
     tc::mbar_init(&bars[B2_SPFULL], 1);
-    tc::mbar_init(&bars[B2_EWSYNC], 256);
     tc::mbar_init(&bars[B2_EWDONE], 256);
     tc::mbar_init(&bars[B2_P3DONE], 1);
     tc::mbar_init(&bars[B2_T12FREE], 128);
     tc::mbar_init(&bars[B2_DSFULL], 1);
     tc::mbar_init(&bars[B2_P4DONE], 1);
     tc::mbar_init(&bars[B2_DGA], 128);
-    tc::mbar_init(&bars[B2_STGA], 128);
-    tc::mbar_init(&bars[B2_STGB], 128);
     tc::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -497,19 +493,17 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
     const float g2i = gi * kLog2e;
     const float rden = valid ? 1.f / fmaxf(den[rowb + r0 + i], kTiny) : 0.f;
     const float dl = valid ? delta[rowb + r0 + i] : 0.f;
-    uint32_t ew_phase = 0;
-    bool ok = true;
     if (grpA) {
       sG2[i] = g2i;
       sZ[i] = with_s ? Z[chunk * 128 + i] : 0.f;
       sDZ[i] = with_ds ? dZ[chunk * 128 + i] : 0.f;
     }
-    ok = __all_sync(0xffffffffu, tc::group_sync(&bars[B2_EWSYNC], ew_phase, 40));
+    tc::named_bar_sync(1, 256);
     const float g2end = sG2[nvalid - 1];
     // --- phase 2: dad, aden for columns [64 h, 64 h + 64)
-    if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B2_SPFULL], 0, 41));
-    if (ok) {
-      tc::tc_fence_after();
+    tc::mbar_wait(&bars[B2_SPFULL], 0, 41);
+    tc::tc_fence_after();
+    {
       const int h = grpA ? 0 : 1;
 #pragma unroll 1
       for (int cb = 0; cb < 2; ++cb) {
@@ -536,148 +530,142 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
         }
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8) {
-          const int col = c0 + 8 * c8;
-          const uint32_t off = tile_off(i, col);
+          const uint32_t off = tile_off(i, c0 + 8 * c8);
           *reinterpret_cast<uint4*>(base + kODAD + off) =
               make_uint4(dadp[4 * c8], dadp[4 * c8 + 1], dadp[4 * c8 + 2], dadp[4 * c8 + 3]);
           *reinterpret_cast<uint4*>(base + kOADEN + off) =
               make_uint4(adenp[4 * c8], adenp[4 * c8 + 1], adenp[4 * c8 + 2], adenp[4 * c8 + 3]);
         }
       }
-      tc::fence_proxy_async_smem();
-      tc::tc_fence_before();
     }
+    tc::fence_proxy_async_smem();
+    tc::tc_fence_before();
     tc::mbar_arrive(&bars[B2_EWDONE]);
-    const float qsd = valid ? tc::ex2(g2i) * rden : 0.f;          // exp(G_i - start) / den_i
-    const float ks = valid ? tc::ex2(g2end - g2i) : 0.f;          // exp(G_end - G_i)
-    uint32_t stg_phase = 0;
+    const float qsd = valid ? tc::ex2(g2i) * rden : 0.f;  // exp(G_i - start) / den_i
+    const float ks = valid ? tc::ex2(g2end - g2i) : 0.f;  // exp(G_end - G_i)
     if (grpA) {
       // --- dfq = T1 + qs/den (T2 - delta z); staged in the freed aden tile
       float dgq = 0.f;
-      if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B2_P3DONE], 0, 42));
-      if (ok) {
-        tc::tc_fence_after();
+      tc::mbar_wait(&bars[B2_P3DONE], 0, 42);
+      tc::tc_fence_after();
 #pragma unroll 1
-        for (int hb = 0; hb < 2; ++hb) {
-          float t1[64], t2[64];
-          tc::tmem_ld64(trow + kTS + 64 * hb, t1);
-          if (with_s) tc::tmem_ld64(trow + kTP + 64 * hb, t2);
-          tc::tmem_wait_ld();
+      for (int hb = 0; hb < 2; ++hb) {
+        float t1[64], t2[64];
+        tc::tmem_ld64(trow + kTS + 64 * hb, t1);
+        if (with_s) tc::tmem_ld64(trow + kTP + 64 * hb, t2);
+        tc::tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
-            const float t2v = with_s ? t2[c] : 0.f;
-            t1[c] = t1[c] + qsd * (t2v - dl * sZ[64 * hb + c]);
-          }
-          dgq += row_dot64(base + kOQ, i, hb, t1);
-          if (bf16_out) {
-            tile_row_store64(base + kOADEN, i, hb, t1);
-          } else if (valid) {
-            float4* o = reinterpret_cast<float4*>(static_cast<float*>(dfq) +
-                                                  (rowb + r0 + i) * 128 + 64 * hb);
-#pragma unroll
-            for (int c = 0; c < 16; ++c)
-              o[c] = make_float4(t1[4 * c], t1[4 * c + 1], t1[4 * c + 2], t1[4 * c + 3]);
-          }
+        for (int c = 0; c < 64; ++c) {
+          const float t2v = with_s ? t2[c] : 0.f;
+          t1[c] = t1[c] + qsd * (t2v - dl * sZ[64 * hb + c]);
         }
-        tc::tc_fence_before();
+        dgq += row_dot64(base + kOQ, i, hb, t1);
+        if (bf16_out) {
+          tile_row_store64(base + kOADEN, i, hb, t1);
+        } else if (valid) {
+          float4* o = reinterpret_cast<float4*>(static_cast<float*>(dfq) + (rowb + r0 + i) * 128 +
+                                                64 * hb);
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            o[c] = make_float4(t1[4 * c], t1[4 * c + 1], t1[4 * c + 2], t1[4 * c + 3]);
+        }
       }
+      tc::tc_fence_before();
       tc::mbar_arrive(&bars[B2_T12FREE]);
       sDGa[i] = dgq;
       tc::mbar_arrive(&bars[B2_DGA]);
-      if (bf16_out && ok) {
+      if (bf16_out) {
         tc::fence_proxy_async_smem();
-        ok = __all_sync(0xffffffffu, tc::group_sync(&bars[B2_STGA], stg_phase, 43));
-        if (ok && i == 0) {
+        tc::named_bar_sync(2, 128);
+        if (i == 0) {
           tc::tma_store_3d(&tdfq, base + kOADEN, 0, r0, bh);
           tc::tma_store_3d(&tdfq, base + kOADEN + 16384, 64, r0, bh);
           tc::bulk_commit();
         }
       }
       // --- dv = dv_intra + ks T5; staged in the freed S / dS tile
-      if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B2_P4DONE], 0, 44));
-      if (ok) {
-        tc::tc_fence_after();
+      tc::mbar_wait(&bars[B2_P4DONE], 0, 44);
+      tc::tc_fence_after();
 #pragma unroll 1
-        for (int hb = 0; hb < 2; ++hb) {
-          float dvv[64], t5[64];
-          tc::tmem_ld64(trow + kTDV + 64 * hb, dvv);
-          if (with_ds) tc::tmem_ld64(trow + kT5 + 64 * hb, t5);
-          tc::tmem_wait_ld();
-          if (with_ds) {
+      for (int hb = 0; hb < 2; ++hb) {
+        float dvv[64], t5[64];
+        tc::tmem_ld64(trow + kTDV + 64 * hb, dvv);
+        if (with_ds) tc::tmem_ld64(trow + kT5 + 64 * hb, t5);
+        tc::tmem_wait_ld();
+        if (with_ds) {
 #pragma unroll
-            for (int c = 0; c < 64; ++c) dvv[c] += ks * t5[c];
-          }
-          if (bf16_out) {
-            tile_row_store64(base + kOX, i, hb, dvv);
-          } else if (valid) {
-            float4* o = reinterpret_cast<float4*>(static_cast<float*>(dv) +
-                                                  (rowb + r0 + i) * 128 + 64 * hb);
-#pragma unroll
-            for (int c = 0; c < 16; ++c)
-              o[c] = make_float4(dvv[4 * c], dvv[4 * c + 1], dvv[4 * c + 2], dvv[4 * c + 3]);
-          }
+          for (int c = 0; c < 64; ++c) dvv[c] += ks * t5[c];
         }
         if (bf16_out) {
-          tc::fence_proxy_async_smem();
-          ok = __all_sync(0xffffffffu, tc::group_sync(&bars[B2_STGA], stg_phase, 45));
-          if (ok && i == 0) {
-            tc::tma_store_3d(&tdv, base + kOX, 0, r0, bh);
-            tc::tma_store_3d(&tdv, base + kOX + 16384, 64, r0, bh);
-            tc::bulk_commit();
-          }
+          tile_row_store64(base + kOX, i, hb, dvv);
+        } else if (valid) {
+          float4* o = reinterpret_cast<float4*>(static_cast<float*>(dv) + (rowb + r0 + i) * 128 +
+                                                64 * hb);
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            o[c] = make_float4(dvv[4 * c], dvv[4 * c + 1], dvv[4 * c + 2], dvv[4 * c + 3]);
+        }
+      }
+      if (bf16_out) {
+        tc::fence_proxy_async_smem();
+        tc::named_bar_sync(2, 128);
+        if (i == 0) {
+          tc::tma_store_3d(&tdv, base + kOX, 0, r0, bh);
+          tc::tma_store_3d(&tdv, base + kOX + 16384, 64, r0, bh);
+          tc::bulk_commit();
         }
       }
       if (i == 0) tc::bulk_wait0();
     } else {
       // --- dfk = T3 + ks (T4 - dz); staged in the freed dad tile; dG
       float dgk = 0.f;
-      if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B2_P4DONE], 0, 46));
-      if (ok) {
-        tc::tc_fence_after();
+      tc::mbar_wait(&bars[B2_P4DONE], 0, 46);
+      tc::tc_fence_after();
 #pragma unroll 1
-        for (int hb = 0; hb < 2; ++hb) {
-          float t3[64], t4[64];
-          tc::tmem_ld64(trow + kTS + 64 * hb, t3);
-          if (with_ds) tc::tmem_ld64(trow + kTP + 64 * hb, t4);
-          tc::tmem_wait_ld();
+      for (int hb = 0; hb < 2; ++hb) {
+        float t3[64], t4[64];
+        tc::tmem_ld64(trow + kTS + 64 * hb, t3);
+        if (with_ds) tc::tmem_ld64(trow + kTP + 64 * hb, t4);
+        tc::tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
-            const float t4v = with_ds ? t4[c] : 0.f;
-            t3[c] = t3[c] + ks * (t4v - sDZ[64 * hb + c]);
-          }
-          dgk += row_dot64(base + kOK, i, hb, t3);
-          if (bf16_out) {
-            tile_row_store64(base + kODAD, i, hb, t3);
-          } else if (valid) {
-            float4* o = reinterpret_cast<float4*>(static_cast<float*>(dfk) +
-                                                  (rowb + r0 + i) * 128 + 64 * hb);
-#pragma unroll
-            for (int c = 0; c < 16; ++c)
-              o[c] = make_float4(t3[4 * c], t3[4 * c + 1], t3[4 * c + 2], t3[4 * c + 3]);
-          }
+        for (int c = 0; c < 64; ++c) {
+          const float t4v = with_ds ? t4[c] : 0.f;
+          t3[c] = t3[c] + ks * (t4v - sDZ[64 * hb + c]);
         }
+        dgk += row_dot64(base + kOK, i, hb, t3);
         if (bf16_out) {
-          tc::fence_proxy_async_smem();
-          ok = __all_sync(0xffffffffu, tc::group_sync(&bars[B2_STGB], stg_phase, 47));
-          if (ok && i == 0) {
-            tc::tma_store_3d(&tdfk, base + kODAD, 0, r0, bh);
-            tc::tma_store_3d(&tdfk, base + kODAD + 16384, 64, r0, bh);
-            tc::bulk_commit();
-          }
+          tile_row_store64(base + kODAD, i, hb, t3);
+        } else if (valid) {
+          float4* o = reinterpret_cast<float4*>(static_cast<float*>(dfk) + (rowb + r0 + i) * 128 +
+                                                64 * hb);
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            o[c] = make_float4(t3[4 * c], t3[4 * c + 1], t3[4 * c + 2], t3[4 * c + 3]);
         }
       }
-      if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars[B2_DGA], 0, 48));
+      if (bf16_out) {
+        tc::fence_proxy_async_smem();
+        tc::named_bar_sync(3, 128);
+        if (i == 0) {
+          tc::tma_store_3d(&tdfk, base + kODAD, 0, r0, bh);
+          tc::tma_store_3d(&tdfk, base + kODAD + 16384, 64, r0, bh);
+          tc::bulk_commit();
+        }
+      }
+      tc::mbar_wait(&bars[B2_DGA], 0, 48);
       float x = 0.f;
-      if (ok && valid) {
+      if (valid) {
         x = sDGa[i] - dgk;
         dG[rowb + r0 + i] = x;
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
       if (lane == 0) sRed[quad] = x;
-      if (ok) ok = __all_sync(0xffffffffu, tc::group_sync(&bars[B2_STGB], stg_phase, 49));
-      if (ok && i == 0) dGt[chunk] = sRed[0] + sRed[1] + sRed[2] + sRed[3];
-      if (i == 0) tc::bulk_wait0();
+      tc::named_bar_sync(3, 128);
+      if (i == 0) {
+        dGt[chunk] = sRed[0] + sRed[1] + sRed[2] + sRed[3];
+        tc::bulk_wait0();
+      }
     }
   }
   tc::tc_fence_before();

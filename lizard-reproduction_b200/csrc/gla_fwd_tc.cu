@@ -60,9 +60,16 @@ constexpr uint32_t kTSA = 0, kTO = 128, kTSF = 256, kTZ = 384, kTA = 400, kTDI =
                    kTDQ = 480, kTCols = 512;
 
 enum { BAR_FULL0 = 0, BAR_FULL1, BAR_EMPTY0, BAR_EMPTY1, BAR_SFULL, BAR_AREADY, BAR_OFULL,
-       BAR_SREADY, BAR_GATE, BAR_SFDONE, BAR_SSTAGE, BAR_DSYNC, BAR_YSYNC, BAR_COUNT };
+       BAR_SREADY, BAR_GATE, BAR_SFDONE, BAR_COUNT };
 
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 decay, warps 6-9 output
+
+// Timeouts: the decay and output warpgroups synchronise with bar.sync among
+// themselves, so they never leave their chunk loop early. A wait that gives up
+// sets the device flag; every later wait then returns at once, the groups run
+// through their remaining iterations (writing in-bounds garbage) and reach
+// every barrier, and the kernel ends. The TMA and MMA warps use no bar.sync and
+// stop at their first failed wait.
 
 __device__ __forceinline__ uint4 scale8(uint4 w, float sc) {
   w.x = pack_bf16(bf16_lo(w.x) * sc, bf16_hi(w.x) * sc);
@@ -111,9 +118,6 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     tc::mbar_init(&bars[BAR_SREADY], 128);
     tc::mbar_init(&bars[BAR_GATE], 128);
     tc::mbar_init(&bars[BAR_SFDONE], 1);
-    tc::mbar_init(&bars[BAR_SSTAGE], 128);  // output warps around the S store
-    tc::mbar_init(&bars[BAR_DSYNC], 128);   // decay warps: gate scan
-    tc::mbar_init(&bars[BAR_YSYNC], 128);   // output warps: y staged
     tc::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -252,7 +256,6 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
     const float* LG = lg + (size_t)(gate_per_head ? bh : b) * L;
     float carry = 0.f;
-    uint32_t dphase = 0;
     float lg_next = (r < L) ? LG[r] : 0.f;
     for (int n = 0; n < NT; ++n) {
       const int r0 = n * kC;
@@ -260,7 +263,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       const bool valid = r < nvalid;
       float x = valid ? lg_next * kLog2e : 0.f;
       if (r0 + kC + r < L) lg_next = LG[r0 + kC + r];  // prefetch the next chunk's gate
-      if (!__all_sync(0xffffffffu, tc::mbar_wait(&bars[BAR_SFULL], n & 1, 5))) break;
+      tc::mbar_wait(&bars[BAR_SFULL], n & 1, 5);
       tc::tc_fence_after();
       // running log2 gate: inclusive scan over the chunk's 128 rows
 #pragma unroll
@@ -269,7 +272,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         if (lane >= o) x += u;
       }
       if (lane == 31) sScan[quad] = x;
-      if (!__all_sync(0xffffffffu, tc::group_sync(&bars[BAR_DSYNC], dphase, 14))) break;
+      tc::named_bar_sync(1, 128);
       float pre = 0.f;
 #pragma unroll
       for (int qq = 0; qq < 4; ++qq)
@@ -281,7 +284,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       const float start2 = carry;
       if (r == 0) sGS[(n & 1) * 2] = start2;
       if (r == nvalid - 1) sGS[(n & 1) * 2 + 1] = g2;
-      if (!__all_sync(0xffffffffu, tc::group_sync(&bars[BAR_DSYNC], dphase, 15))) break;
+      tc::named_bar_sync(1, 128);
       const float end2 = sGS[(n & 1) * 2 + 1];
       carry = end2;
       tc::mbar_arrive(&bars[BAR_GATE]);
@@ -372,7 +375,6 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     unsigned char* zblk = misc + (r >> 6) * 1024;
     const int zcol = ((((r & 63) >> 3) ^ 1) << 4) + (r & 7) * 2;
     const int zcol2 = ((((r & 63) >> 3) ^ 2) << 4) + (r & 7) * 2;
-    uint32_t sstage_phase = 0, yphase = 0;
     if (save) {  // the state entering chunk 0 is zero
       uint4* p = reinterpret_cast<uint4*>(s_out + ((size_t)bh * NT * 128 + r) * 128);
 #pragma unroll
@@ -383,7 +385,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       const int r0 = n * kC;
       const int nvalid = min(kC, L - r0);
       const bool valid = r < nvalid;
-      if (!__all_sync(0xffffffffu, tc::mbar_wait(&bars[BAR_OFULL], n & 1, 6))) break;
+      tc::mbar_wait(&bars[BAR_OFULL], n & 1, 6);
       tc::tc_fence_after();
       // y = o / max(den, FLT_MIN), den = a . 1 + Q~ . z_hi + Q~ . z_lo
       float dv[32];
@@ -419,7 +421,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         }
       }
       tc::fence_proxy_async_smem();
-      if (!__all_sync(0xffffffffu, tc::group_sync(&bars[BAR_YSYNC], yphase, 16))) break;
+      tc::named_bar_sync(2, 128);
       if (r == 0) {
         tc::tma_store_3d(&ty, ystage, 0, r0, bh);
         tc::tma_store_3d(&ty, ystage + 16384, 64, r0, bh);
@@ -429,8 +431,8 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       if (n + 1 < NT) {
         // prepare chunk n+1: bf16 S_{n+1}; S and z pre-scaled by its decay;
         // Q~_{n+1} in place and its row sums against z_{n+1}
-        if (!__all_sync(0xffffffffu, tc::mbar_wait(&bars[BAR_GATE], (n + 1) & 1, 10))) break;
-        if (!__all_sync(0xffffffffu, tc::mbar_wait(&bars[BAR_SFDONE], n & 1, 11))) break;
+        tc::mbar_wait(&bars[BAR_GATE], (n + 1) & 1, 10);
+        tc::mbar_wait(&bars[BAR_SFDONE], n & 1, 11);
         tc::tc_fence_after();
         const float start2 = sGS[((n + 1) & 1) * 2], end2 = sGS[((n + 1) & 1) * 2 + 1];
         const float decay = tc::ex2(end2 - start2);
@@ -441,7 +443,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
           z_out[((size_t)bh * NT + n + 1) * 128 + r] = zn;
           // the previous S store must have read the staging block
           if (r == 0) tc::bulk_wait_read0();
-          if (!__all_sync(0xffffffffu, tc::group_sync(&bars[BAR_SSTAGE], sstage_phase, 12))) break;
+          tc::named_bar_sync(3, 128);
         }
         {
           const bf16 zh = __float2bfloat16_rn(zn);
@@ -476,7 +478,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         }
         if (save) {  // bf16 S_{n+1} to HBM for the backward, from the operand block
           tc::fence_proxy_async_smem();
-          if (!__all_sync(0xffffffffu, tc::group_sync(&bars[BAR_SSTAGE], sstage_phase, 13))) break;
+          tc::named_bar_sync(3, 128);
           if (r == 0) {
             tc::tma_store_3d(&ts, base + kOffS, 0, (n + 1) * kC, bh);
             tc::tma_store_3d(&ts, base + kOffS + 16384, 64, (n + 1) * kC, bh);

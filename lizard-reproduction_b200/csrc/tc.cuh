@@ -68,16 +68,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
-// Barrier of a thread group on an mbarrier initialised with the group's size:
-// every thread arrives, then waits (bounded) for the phase to complete. Unlike
-// bar.sync it cannot hang when a member has given up on an earlier wait.
-__device__ __forceinline__ bool group_sync(uint64_t* bar, uint32_t& phase, uint32_t site) {
-  mbar_arrive(bar);
-  const bool ok = mbar_wait(bar, phase & 1, site);
-  ++phase;
-  return ok;
-}
-
 // 2^x with the hardware approximation (relative error ~2^-22, denormal
 // results flushed to zero); every use here has x <= 0 or feeds a bf16 value.
 __device__ __forceinline__ float ex2(float x) {
