@@ -41,6 +41,15 @@ CONFIG = {
 }
 
 
+# --case workloads: (B, H, L, F = D, per-head gate, forward+backward, op)
+CASES = {
+    "cfg2-fwd": (8, 32, 2048, 128, True, False, "gla"),
+    "cfg3-gla-train": (1, 32, 2048, 64, False, True, "gla"),
+    "cfg3-swa-train": (1, 32, 2048, 64, False, True, "swa"),
+    "cfg4-train": (16, 32, 16384, 128, True, True, "gla"),
+}
+
+
 def parse():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -49,6 +58,11 @@ def parse():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the config-3 fwd+bwd side measurements")
+    ap.add_argument("--case", choices=sorted(CASES),
+                    help="run only this workload for --steps steps after --warmup steps and "
+                         "print its device ms per step (for profiling; not the driver contract)")
+    ap.add_argument("--B", type=int, help="batch for --case (default: the config's)")
+    ap.add_argument("--L", type=int, help="sequence length for --case (default: the config's)")
     return ap.parse_args()
 
 
@@ -532,9 +546,61 @@ def run_ours(args, torch):
     print(json.dumps(line), flush=True)
 
 
+def run_case(args, torch):
+    """One named workload, K steps after W warm-up steps, device time by CUDA events."""
+    import torch.nn.functional as F
+    import lizard_cuda
+    lizard_cuda.load()
+    name = args.case
+    Bc, Hc, Lc, FDc, per_head, train, op = CASES[name]
+    Bc, Lc = args.B or Bc, args.L or Lc
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    shape = (Bc, Hc, Lc, FDc)
+    a = (F.softplus(torch.randn(shape, generator=g, device=dev)) / math.sqrt(FDc)).bfloat16()
+    b = (F.softplus(torch.randn(shape, generator=g, device=dev)) / math.sqrt(FDc)).bfloat16()
+    v = torch.randn(shape, generator=g, device=dev).bfloat16()
+    lg = F.logsigmoid(3 + 1.5 * torch.randn((Bc, Hc, Lc) if per_head else (Bc, Lc),
+                                            generator=g, device=dev))
+    meta = torch.randn(4, generator=g, device=dev)
+    dy = torch.randn(shape, generator=g, device=dev).bfloat16()
+    if op == "gla":
+        args_in = [a, b, v, lg]
+        call = lizard_cuda.gla
+    else:
+        args_in = [torch.randn(shape, generator=g, device=dev).bfloat16(),
+                   torch.randn(shape, generator=g, device=dev).bfloat16(), v, meta]
+        call = lambda q, k, vv, m: lizard_cuda.swa(q, k, vv, m, 64)  # noqa: E731
+    leaves = [t.detach().requires_grad_() for t in args_in] if train else args_in
+
+    def step():
+        if train:
+            for t in leaves:
+                t.grad = None
+            call(*leaves).backward(dy)
+        else:
+            with torch.no_grad():
+                call(*leaves)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / max(1, args.steps)
+    print(json.dumps({"case": name, "B": Bc, "H": Hc, "L": Lc, "F=D": FDc, "train": train,
+                      "steps": args.steps, "ms_per_step": ms}), flush=True)
+
+
 def main():
     args = parse()
     import torch
+    if args.case:
+        run_case(args, torch)
+        return
     if args.impl == "reference":
         run_reference(args, torch)
     else:
