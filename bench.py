@@ -47,6 +47,9 @@ CASES = {
     "cfg3-gla-train": (1, 32, 2048, 64, False, True, "gla"),
     "cfg3-swa-train": (1, 32, 2048, 64, False, True, "swa"),
     "cfg4-train": (16, 32, 16384, 128, True, True, "gla"),
+    # feature map of one projection: x [B, H, L, 64] fp32, feature dim 128
+    "prologue-fwd": (4, 32, 4096, 64, False, False, "hedgehog"),
+    "prologue-train": (4, 32, 4096, 64, False, True, "hedgehog"),
 }
 
 
@@ -320,6 +323,53 @@ def length_sweep(torch, lizard_cuda, device, lengths=(512, 1024, 2048, 4096, 819
     return out
 
 
+def prologue_measure(torch, lizard_cuda, device, steps=20, warmup=3):
+    """GLA prologue: the Hedgehog feature map of one projection at
+    the model's head shape (B=4, H=32, L=4096, Dh=64, feature dim 128, fp32
+    heads as the layer feeds them), fused kernel against the same torch ops
+    (matmul, two softmaxes, concatenation, bf16 cast) on the GPU; forward and
+    forward+backward device ms. Bytes moved by the fused forward: fp32 x in,
+    bf16 features out."""
+    Bp, Hp, Lp, Dh, Fd = 4, 32, 4096, 64, 128
+    g = torch.Generator(device=device).manual_seed(11)
+    x = torch.randn(Bp, Hp, Lp, Dh, generator=g, device=device)
+    w = 0.05 * torch.randn(Fd, Dh, generator=g, device=device)
+    df = torch.randn(Bp, Hp, Lp, 2 * Fd, generator=g, device=device).bfloat16()
+
+    def torch_hh(xx, ww):
+        xw = xx @ ww.T
+        return torch.cat([xw.softmax(-1), (-xw).softmax(-1)], -1).bfloat16()
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / steps
+
+    out = {"workload": f"hedgehog x [{Bp},{Hp},{Lp},{Dh}] fp32, W [{Fd},{Dh}] -> bf16 [.., {2 * Fd}]"}
+    with torch.no_grad():
+        out["fused_fwd_ms"] = timed(lambda: lizard_cuda.hedgehog(x, w))
+        out["torch_fwd_ms"] = timed(lambda: torch_hh(x, w))
+    xl, wl = x.clone().requires_grad_(), w.clone().requires_grad_()
+
+    def fb(fn):
+        def step():
+            xl.grad = wl.grad = None
+            fn(xl, wl).backward(df)
+        return step
+    out["fused_fwd_bwd_ms"] = timed(fb(lizard_cuda.hedgehog))
+    out["torch_fwd_bwd_ms"] = timed(fb(torch_hh))
+    rows = Bp * Hp * Lp
+    out["fused_fwd_gbs"] = rows * (4 * Dh + 2 * 2 * Fd) / (out["fused_fwd_ms"] / 1e3) / 1e9
+    return out
+
+
 def secondary(torch, lizard_cuda, device, steps=50, warmup=5):
     """Config 3 (B=1, L=2048, H=32, F=D=64): GLA fwd+bwd with a per-token gate
     and SWA fwd+bwd (window 64, 4 sinks); device ms per step.
@@ -496,6 +546,7 @@ def run_ours(args, torch):
             side = secondary(torch, lizard_cuda, device)
             if world == 1:
                 side["cfg4_length_sweep"] = length_sweep(torch, lizard_cuda, device)
+                side["prologue_hedgehog"] = prologue_measure(torch, lizard_cuda, device)
 
     cpu = None
     if rank == 0 and world == 1:
@@ -567,6 +618,11 @@ def run_case(args, torch):
     if op == "gla":
         args_in = [a, b, v, lg]
         call = lizard_cuda.gla
+    elif op == "hedgehog":
+        args_in = [torch.randn(shape, generator=g, device=dev),
+                   0.05 * torch.randn(128, FDc, generator=g, device=dev)]
+        call = lizard_cuda.hedgehog
+        dy = torch.randn(Bc, Hc, Lc, 256, generator=g, device=dev).bfloat16()
     else:
         args_in = [torch.randn(shape, generator=g, device=dev).bfloat16(),
                    torch.randn(shape, generator=g, device=dev).bfloat16(), v, meta]

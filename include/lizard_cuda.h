@@ -191,6 +191,28 @@ int lz_gla_seg_gate_offset(float* dlog_gamma, const float* totals, int P, int ra
                            int rows, int L, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Hedgehog feature map (the GLA prologue)                                  */
+/* ------------------------------------------------------------------------ */
+/* f [R, 2 Fd] (bf16) = [softmax(x W^T), softmax(-x W^T)] per row, fused.
+ * Replaces hedgehog() of the reference (src/lizard_attention.py:9-11) as the
+ * layer calls it on each head's queries and keys before gla(); the reference
+ * keeps the result in x's dtype and gla() then casts it to bf16.
+ * x [R, Dh] in x_dtype (LZ_DTYPE_F32 or LZ_DTYPE_BF16), weight [Fd, Dh] fp32,
+ * Dh <= 128, Fd <= 128. */
+int lz_hedgehog_fwd(const void* x, int x_dtype, const float* weight, void* f, int R, int Dh,
+                    int Fd, void* stream);
+
+/* Bytes of scratch lz_hedgehog_bwd needs (per-CTA partial weight gradients). */
+size_t lz_hedgehog_bwd_workspace_bytes(int R, int Dh, int Fd);
+
+/* Backward of lz_hedgehog_fwd (the autograd of the reference's matmul,
+ * softmax and concatenation): dx [R, Dh] and dweight [Fd, Dh] in fp32 from
+ * df [R, 2 Fd] in df_dtype. dweight is reduced over rows in a fixed order. */
+int lz_hedgehog_bwd(const void* x, int x_dtype, const float* weight, const void* df,
+                    int df_dtype, float* dx, float* dweight, void* workspace,
+                    size_t workspace_bytes, int R, int Dh, int Fd, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* SWA                                                                      */
 /* ------------------------------------------------------------------------ */
 

@@ -1,0 +1,747 @@
+// Hedgehog feature map, fused: f = [softmax(x W^T), softmax(-x W^T)] in bf16
+// (reference: src/lizard_attention.py:9-11), the GLA prologue that turns a
+// head's queries / keys x [R, Dh] into features [R, 2 Fd].
+//
+// Forward, per 64-row tile and 8 warps (warp = 16 rows x half of the feature
+// columns): xw = x W^T on the tensor cores (mma.sync bf16 -> fp32; an fp32 x
+// or W enters as bf16 hi + lo parts, xw = hi.hi + hi.lo + lo.hi, so the
+// logits carry ~16 mantissa bits, as the reference's fp32 matmul does to
+// within the bf16 output rounding), both softmaxes in registers (quad shuffles,
+// then the two column halves through shared memory), and the bf16 features
+// written from the fragments with 16-byte stores after a quad transpose. The
+// next tile's x is loaded into registers while this tile computes. The
+// reference materialises xw, two fp32 softmaxes and their concatenation, and
+// GLA then casts them.
+//
+// Backward (the autograd of the same three torch ops): per tile, recompute xw
+// and both softmaxes, then
+//   g = p+ (df+ - sum p+ df+) - p- (df- - sum p- df-)     (d xw, fp32)
+//   dx = g W,  dW += g^T x
+// with g entering both products as bf16 hi + lo. dW is accumulated per CTA in
+// registers over the CTA's tiles (persistent grid) and reduced over CTAs in a
+// fixed order by a second kernel: deterministic.
+//
+// Bandwidth-bound: 2 Dh Fd flop per (Dh + 2 Fd) x 2-4 bytes.
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace lz {
+
+namespace {
+
+constexpr int kR = 64;   // rows per tile
+constexpr int kT = 256;  // threads: 8 warps = 4 row blocks x 2 column halves
+
+template <int DHP, int FDP>
+struct HhSmem {
+  static constexpr int LDX = DHP + 8, LDW = DHP + 8, LDG = FDP + 8;
+  static constexpr size_t whi = 0;
+  static constexpr size_t wlo = whi + (size_t)FDP * LDW * 2;
+  static constexpr size_t xhi = wlo + (size_t)FDP * LDW * 2;
+  static constexpr size_t xlo = xhi + (size_t)kR * LDX * 2;
+  static constexpr size_t red = xlo + (size_t)kR * LDX * 2;  // 4 stats x 2 halves x 64 rows
+  static constexpr size_t fwd_bytes = red + 4 * 2 * kR * 4;
+  static constexpr size_t ghi = fwd_bytes;                   // backward: g hi / lo
+  static constexpr size_t glo = ghi + (size_t)kR * LDG * 2;
+  static constexpr size_t bwd_bytes = glo + (size_t)kR * LDG * 2;
+};
+
+template <typename T>
+__device__ __forceinline__ float ld_f(const T* p, size_t i);
+template <>
+__device__ __forceinline__ float ld_f<float>(const float* p, size_t i) { return p[i]; }
+template <>
+__device__ __forceinline__ float ld_f<bf16>(const bf16* p, size_t i) {
+  return __bfloat162float(p[i]);
+}
+
+// rows x cols of a row-major [*, ld] matrix -> bf16 hi / lo tiles, zero padded
+template <typename T, int ROWS, int COLS>
+__device__ __forceinline__ void split_tile(bf16* hi, bf16* lo, int lds, const T* g, int ld,
+                                           int r0, int nrows, int ncols) {
+  for (int i = threadIdx.x; i < ROWS * COLS; i += kT) {
+    const int r = i / COLS, c = i % COLS;
+    const float x = (r0 + r < nrows && c < ncols) ? ld_f<T>(g, (size_t)(r0 + r) * ld + c) : 0.f;
+    const bf16 h = __float2bfloat16_rn(x);
+    hi[r * lds + c] = h;
+    lo[r * lds + c] = __float2bfloat16_rn(x - __bfloat162float(h));
+  }
+}
+
+// Vector loads of one 64-row tile of x (fp32 or bf16) into registers,
+// 16 bytes per load, zero beyond R; stored to the hi / lo tiles afterwards.
+template <typename XT, int DHP>
+struct XTile {
+  static constexpr int EPV = 16 / sizeof(XT);
+  static constexpr int VPR = DHP / EPV;
+  static constexpr int NV = (kR * VPR + kT - 1) / kT;
+  uint4 v[NV];
+  __device__ __forceinline__ void load(const XT* x, int r0, int R, int Dh) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int i = threadIdx.x + kT * k;
+      const int r = i / VPR, c = (i % VPR) * EPV;
+      v[k] = (i < kR * VPR && r0 + r < R && c < Dh)
+                 ? *reinterpret_cast<const uint4*>(x + (size_t)(r0 + r) * Dh + c)
+                 : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  __device__ __forceinline__ void store(bf16* hi, bf16* lo, int lds) const {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int i = threadIdx.x + kT * k;
+      if (i >= kR * VPR) continue;
+      const int r = i / VPR, c = (i % VPR) * EPV;
+      if constexpr (sizeof(XT) == 4) {
+        const float f[4] = {__uint_as_float(v[k].x), __uint_as_float(v[k].y),
+                            __uint_as_float(v[k].z), __uint_as_float(v[k].w)};
+        uint32_t h[2], l[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          h[j] = pack_bf16(f[2 * j], f[2 * j + 1]);
+          l[j] = pack_bf16(f[2 * j] - bf16_lo(h[j]), f[2 * j + 1] - bf16_hi(h[j]));
+        }
+        *reinterpret_cast<uint2*>(hi + r * lds + c) = make_uint2(h[0], h[1]);
+        *reinterpret_cast<uint2*>(lo + r * lds + c) = make_uint2(l[0], l[1]);
+      } else {
+        *reinterpret_cast<uint4*>(hi + r * lds + c) = v[k];
+      }
+    }
+  }
+};
+
+__device__ __forceinline__ uint32_t sel4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, int i) {
+  return i == 0 ? a : i == 1 ? b : i == 2 ? c : d;
+}
+// Quad transpose of 32-bit words. In: lane cq holds word in[j] of n-tile 4k+j
+// (the fragment pair at columns 2 cq, 2 cq + 1 of that tile). Out: lane cq
+// holds words 0..3 of n-tile 4k + cq, i.e. its 8 consecutive columns. The
+// same exchange turns 8 loaded consecutive columns back into fragment pairs.
+__device__ __forceinline__ void quad_xpose(const uint32_t (&in)[4], uint32_t (&out)[4]) {
+  const int lane = threadIdx.x & 31, cq = lane & 3;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const uint32_t send = sel4(in[0], in[1], in[2], in[3], (cq + r) & 3);
+    const uint32_t recv = __shfl_sync(0xffffffffu, send, (lane & ~3) | ((cq - r) & 3));
+    const int slot = (cq - r) & 3;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) out[q] = (q == slot) ? recv : (r == 0 ? 0u : out[q]);
+  }
+}
+
+// xw for this warp's 16 rows (row block rb) and FDP / 2 columns from c0;
+// XS: x has a lo part (fp32 x). W (fp32) always has one.
+template <int DHP, int FDP, bool XS>
+__device__ __forceinline__ void logits(float (&acc)[FDP / 16][4], const bf16* xh, const bf16* xl,
+                                       const bf16* wh, const bf16* wl, int rb, int c0) {
+  using SM = HhSmem<DHP, FDP>;
+  constexpr int NTH = FDP / 16;
+#pragma unroll
+  for (int c = 0; c < NTH; ++c)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[c][e] = 0.f;
+#pragma unroll
+  for (int k0 = 0; k0 < DHP; k0 += 16) {
+    uint32_t ah[4], al[4];
+    lda_rm(ah, xh, SM::LDX, 16 * rb, k0);
+    if constexpr (XS) lda_rm(al, xl, SM::LDX, 16 * rb, k0);
+#pragma unroll
+    for (int np = 0; np < NTH / 2; ++np) {
+      uint32_t bh[4], bl[4];
+      ldb_nk(bh, wh, SM::LDW, c0 + 16 * np, k0);
+      mma16816(acc[2 * np], ah, bh[0], bh[1]);
+      mma16816(acc[2 * np + 1], ah, bh[2], bh[3]);
+      ldb_nk(bl, wl, SM::LDW, c0 + 16 * np, k0);
+      mma16816(acc[2 * np], ah, bl[0], bl[1]);
+      mma16816(acc[2 * np + 1], ah, bl[2], bl[3]);
+      if constexpr (XS) {
+        mma16816(acc[2 * np], al, bh[0], bh[1]);
+        mma16816(acc[2 * np + 1], al, bh[2], bh[3]);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float quad_max(float x) {
+  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
+  return fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
+}
+
+// Row statistic over the two column halves: every quad writes its half's
+// value for rows `row` and `row + 8`, then all read both (fixed order).
+__device__ __forceinline__ void exchange2(float* red, int stat, int half, int row, float (&v)[2],
+                                          int op /* 0 max, 1 min, 2 sum */) {
+  const int cq = threadIdx.x & 3;
+  if (cq == 0) {
+    red[(stat * 2 + half) * kR + row] = v[0];
+    red[(stat * 2 + half) * kR + row + 8] = v[1];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float a = red[(stat * 2 + 0) * kR + row + 8 * h];
+    const float b = red[(stat * 2 + 1) * kR + row + 8 * h];
+    v[h] = op == 0 ? fmaxf(a, b) : op == 1 ? fminf(a, b) : a + b;
+  }
+}
+
+// Both softmaxes of this warp's fragments (columns c0 + ..): acc -> p+, pm -> p-.
+// FULL: Fd == FDP, no column is masked.
+template <int FDP, bool FULL>
+__device__ __forceinline__ void softmaxes(float (&acc)[FDP / 16][4], float (&pm)[FDP / 16][4],
+                                          int c0, int Fd, float* red, int half, int row) {
+  constexpr int NTH = FDP / 16;
+  const int cq = threadIdx.x & 3;
+  float mx[2] = {-INFINITY, -INFINITY}, mn[2] = {INFINITY, INFINITY};
+#pragma unroll
+  for (int nt = 0; nt < NTH; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = c0 + 8 * nt + 2 * cq + (e & 1);
+      if (FULL || c < Fd) {
+        mx[e >> 1] = fmaxf(mx[e >> 1], acc[nt][e]);
+        mn[e >> 1] = fminf(mn[e >> 1], acc[nt][e]);
+      }
+    }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    mx[h] = quad_max(mx[h]);
+    mn[h] = -quad_max(-mn[h]);
+  }
+  exchange2(red, 0, half, row, mx, 0);
+  exchange2(red, 1, half, row, mn, 1);
+  float sp[2] = {0.f, 0.f}, sm[2] = {0.f, 0.f};
+#pragma unroll
+  for (int nt = 0; nt < NTH; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = c0 + 8 * nt + 2 * cq + (e & 1), h = e >> 1;
+      const bool ok = FULL || c < Fd;
+      const float ep = ok ? __expf(acc[nt][e] - mx[h]) : 0.f;
+      const float em = ok ? __expf(mn[h] - acc[nt][e]) : 0.f;
+      acc[nt][e] = ep;
+      pm[nt][e] = em;
+      sp[h] += ep;
+      sm[h] += em;
+    }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    sp[h] = quad_sum(sp[h]);
+    sm[h] = quad_sum(sm[h]);
+  }
+  exchange2(red, 2, half, row, sp, 2);
+  exchange2(red, 3, half, row, sm, 2);
+  const float ip[2] = {1.f / sp[0], 1.f / sp[1]}, im[2] = {1.f / sm[0], 1.f / sm[1]};
+#pragma unroll
+  for (int nt = 0; nt < NTH; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      acc[nt][e] *= ip[e >> 1];
+      pm[nt][e] *= im[e >> 1];
+    }
+}
+
+template <typename XT, int DHP, int FDP, bool FULL>
+__global__ void __launch_bounds__(kT)
+hedgehog_fwd_kernel(const XT* __restrict__ x, const float* __restrict__ w, int R, int Dh, int Fd,
+                    int vec, bf16* __restrict__ f) {
+  using SM = HhSmem<DHP, FDP>;
+  constexpr int NTH = FDP / 16;
+  extern __shared__ __align__(128) unsigned char smem[];
+  bf16* wh = reinterpret_cast<bf16*>(smem + SM::whi);
+  bf16* wl = reinterpret_cast<bf16*>(smem + SM::wlo);
+  bf16* xh = reinterpret_cast<bf16*>(smem + SM::xhi);
+  bf16* xl = reinterpret_cast<bf16*>(smem + SM::xlo);
+  float* red = reinterpret_cast<float*>(smem + SM::red);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, cq = lane & 3;
+  const int rb = warp & 3, half = warp >> 2, c0 = half * (FDP / 2);
+  const int lrow = 16 * rb + gq;  // this thread's tile rows: lrow, lrow + 8
+  split_tile<float, FDP, DHP>(wh, wl, SM::LDW, w, Dh, 0, Fd, Dh);
+  const int ntiles = (R + kR - 1) / kR;
+  const int F2 = 2 * Fd;
+  XTile<XT, DHP> xt;
+  if (vec && (int)blockIdx.x < ntiles) xt.load(x, blockIdx.x * kR, R, Dh);
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int r0 = tile * kR;
+    __syncthreads();  // the previous tile's x is consumed; W is staged
+    if (vec)
+      xt.store(xh, xl, SM::LDX);
+    else
+      split_tile<XT, kR, DHP>(xh, xl, SM::LDX, x, Dh, r0, R, Dh);
+    __syncthreads();
+    if (vec && tile + (int)gridDim.x < ntiles) xt.load(x, r0 + gridDim.x * kR, R, Dh);
+    float acc[NTH][4], pm[NTH][4];
+    logits<DHP, FDP, sizeof(XT) == 4>(acc, xh, xl, wh, wl, rb, c0);
+    softmaxes<FDP, FULL>(acc, pm, c0, Fd, red, half, lrow);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = r0 + lrow + 8 * h;
+      bf16* out = f + (size_t)row * F2;
+      bool done = false;
+      if constexpr (NTH % 4 == 0) {
+        if (vec && (Fd % 8) == 0) {
+#pragma unroll
+          for (int k = 0; k < NTH / 4; ++k) {
+            uint32_t ip[4], im[4], op[4], om[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              ip[j] = pack_bf16(acc[4 * k + j][2 * h], acc[4 * k + j][2 * h + 1]);
+              im[j] = pack_bf16(pm[4 * k + j][2 * h], pm[4 * k + j][2 * h + 1]);
+            }
+            quad_xpose(ip, op);
+            quad_xpose(im, om);
+            const int c = c0 + 8 * (4 * k + cq);
+            if (row < R && (FULL || c < Fd)) {
+              *reinterpret_cast<uint4*>(out + c) = make_uint4(op[0], op[1], op[2], op[3]);
+              *reinterpret_cast<uint4*>(out + Fd + c) = make_uint4(om[0], om[1], om[2], om[3]);
+            }
+          }
+          done = true;
+        }
+      }
+      if (!done && row < R) {
+#pragma unroll
+        for (int nt = 0; nt < NTH; ++nt) {
+          const int c = c0 + 8 * nt + 2 * cq;
+          if (c < Fd) {
+            out[c] = __float2bfloat16_rn(acc[nt][2 * h]);
+            out[Fd + c] = __float2bfloat16_rn(pm[nt][2 * h]);
+          }
+          if (c + 1 < Fd) {
+            out[c + 1] = __float2bfloat16_rn(acc[nt][2 * h + 1]);
+            out[Fd + c + 1] = __float2bfloat16_rn(pm[nt][2 * h + 1]);
+          }
+        }
+      }
+    }
+  }
+}
+
+// The fragment pairs of df for this warp's columns: pr[nt][h] = columns
+// c0 + 8 nt + 2 cq, +1 of row `row + 8 h`, read from `src` = the row's first
+// column of the half (p+ or p-). With vec, 16-byte loads of 8 consecutive
+// columns and a quad transpose; else element loads.
+template <typename GT, int NTH>
+__device__ __forceinline__ void load_df(float2 (&pr)[NTH][2], const GT* __restrict__ df,
+                                        int row, int R, int F2, int cbase, int Fd, int c0,
+                                        bool vec) {
+  const int cq = threadIdx.x & 3;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = row + 8 * h;
+    const GT* src = df + (size_t)r * F2 + cbase;
+    bool done = false;
+    if constexpr (NTH % 4 == 0) {
+      if (vec) {
+#pragma unroll
+        for (int k = 0; k < NTH / 4; ++k) {
+          const int c = c0 + 8 * (4 * k + cq);
+          const bool ok = r < R && c < Fd;
+          if constexpr (sizeof(GT) == 2) {
+            const uint4 w = ok ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0);
+            const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+            uint32_t out[4];
+            quad_xpose(in, out);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              pr[4 * k + j][h] = make_float2(bf16_lo(out[j]), bf16_hi(out[j]));
+          } else {
+            const uint4 a = ok ? *reinterpret_cast<const uint4*>(src + c) : make_uint4(0, 0, 0, 0);
+            const uint4 b =
+                ok ? *reinterpret_cast<const uint4*>(src + c + 4) : make_uint4(0, 0, 0, 0);
+            const uint32_t lo_in[4] = {a.x, a.z, b.x, b.z}, hi_in[4] = {a.y, a.w, b.y, b.w};
+            uint32_t lo_out[4], hi_out[4];
+            quad_xpose(lo_in, lo_out);
+            quad_xpose(hi_in, hi_out);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              pr[4 * k + j][h] =
+                  make_float2(__uint_as_float(lo_out[j]), __uint_as_float(hi_out[j]));
+          }
+        }
+        done = true;
+      }
+    }
+    if (!done) {
+#pragma unroll
+      for (int nt = 0; nt < NTH; ++nt) {
+        const int c = c0 + 8 * nt + 2 * cq;
+        const float a = (r < R && c < Fd) ? ld_f<GT>(src, c) : 0.f;
+        const float b = (r < R && c + 1 < Fd) ? ld_f<GT>(src, c + 1) : 0.f;
+        pr[nt][h] = make_float2(a, b);
+      }
+    }
+  }
+}
+
+template <typename XT, typename GT, int DHP, int FDP, bool FULL>
+__global__ void __launch_bounds__(kT)
+hedgehog_bwd_kernel(const XT* __restrict__ x, const float* __restrict__ w,
+                    const GT* __restrict__ df, int R, int Dh, int Fd, int vec, int vec_df,
+                    float* __restrict__ dx, float* __restrict__ dw_part) {
+  using SM = HhSmem<DHP, FDP>;
+  constexpr int NTH = FDP / 16;
+  extern __shared__ __align__(128) unsigned char smem[];
+  bf16* wh = reinterpret_cast<bf16*>(smem + SM::whi);
+  bf16* wl = reinterpret_cast<bf16*>(smem + SM::wlo);
+  bf16* xh = reinterpret_cast<bf16*>(smem + SM::xhi);
+  bf16* xl = reinterpret_cast<bf16*>(smem + SM::xlo);
+  float* red = reinterpret_cast<float*>(smem + SM::red);
+  bf16* gh = reinterpret_cast<bf16*>(smem + SM::ghi);
+  bf16* gl = reinterpret_cast<bf16*>(smem + SM::glo);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, cq = lane & 3;
+  const int rb = warp & 3, half = warp >> 2, c0 = half * (FDP / 2);
+  const int lrow = 16 * rb + gq;
+  split_tile<float, FDP, DHP>(wh, wl, SM::LDW, w, Dh, 0, Fd, Dh);
+  constexpr int MT = FDP / 16;       // 16-row tiles of dW (rows = features)
+  constexpr int MTW = (MT + 7) / 8;  // per warp
+  float dwa[MTW][DHP / 8][4];
+#pragma unroll
+  for (int a = 0; a < MTW; ++a)
+#pragma unroll
+    for (int c = 0; c < DHP / 8; ++c)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dwa[a][c][e] = 0.f;
+  const int ntiles = (R + kR - 1) / kR;
+  const int F2 = 2 * Fd;
+  XTile<XT, DHP> xt;
+  if (vec && (int)blockIdx.x < ntiles) xt.load(x, blockIdx.x * kR, R, Dh);
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int r0 = tile * kR;
+    __syncthreads();
+    if (vec)
+      xt.store(xh, xl, SM::LDX);
+    else
+      split_tile<XT, kR, DHP>(xh, xl, SM::LDX, x, Dh, r0, R, Dh);
+    __syncthreads();
+    if (vec && tile + (int)gridDim.x < ntiles) xt.load(x, r0 + gridDim.x * kR, R, Dh);
+    float acc[NTH][4], pm[NTH][4];
+    logits<DHP, FDP, sizeof(XT) == 4>(acc, xh, xl, wh, wl, rb, c0);
+    softmaxes<FDP, FULL>(acc, pm, c0, Fd, red, half, lrow);
+    // g = p+ (df+ - s+) - p- (df- - s-)
+    {
+      float2 dp[NTH][2], dm[NTH][2];
+      load_df<GT, NTH>(dp, df, r0 + lrow, R, F2, 0, Fd, c0, vec_df);
+      load_df<GT, NTH>(dm, df, r0 + lrow, R, F2, Fd, Fd, c0, vec_df);
+      float sp[2] = {0.f, 0.f}, sm[2] = {0.f, 0.f};
+#pragma unroll
+      for (int nt = 0; nt < NTH; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          sp[h] += acc[nt][2 * h] * dp[nt][h].x + acc[nt][2 * h + 1] * dp[nt][h].y;
+          sm[h] += pm[nt][2 * h] * dm[nt][h].x + pm[nt][2 * h + 1] * dm[nt][h].y;
+        }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        sp[h] = quad_sum(sp[h]);
+        sm[h] = quad_sum(sm[h]);
+      }
+      // the max / min slots of `red` are free again at this point
+      exchange2(red, 0, half, lrow, sp, 2);
+      exchange2(red, 1, half, lrow, sm, 2);
+#pragma unroll
+      for (int nt = 0; nt < NTH; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          acc[nt][2 * h] =
+              acc[nt][2 * h] * (dp[nt][h].x - sp[h]) - pm[nt][2 * h] * (dm[nt][h].x - sm[h]);
+          acc[nt][2 * h + 1] = acc[nt][2 * h + 1] * (dp[nt][h].y - sp[h]) -
+                               pm[nt][2 * h + 1] * (dm[nt][h].y - sm[h]);
+        }
+    }
+    // g (bf16 hi / lo) to shared memory
+#pragma unroll
+    for (int nt = 0; nt < NTH; ++nt) {
+      const int c = c0 + 8 * nt + 2 * cq;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = lrow + 8 * h;
+        const uint32_t hi = pack_bf16(acc[nt][2 * h], acc[nt][2 * h + 1]);
+        const uint32_t lo =
+            pack_bf16(acc[nt][2 * h] - bf16_lo(hi), acc[nt][2 * h + 1] - bf16_hi(hi));
+        *reinterpret_cast<uint32_t*>(gh + row * SM::LDG + c) = hi;
+        *reinterpret_cast<uint32_t*>(gl + row * SM::LDG + c) = lo;
+      }
+    }
+    __syncthreads();
+    // dx = g W: this warp's 16 rows, value columns [half * DHP/2, +DHP/2)
+    {
+      constexpr int NDH = DHP / 16;
+      const int d0 = half * (DHP / 2);
+      float dxa[NDH][4];
+#pragma unroll
+      for (int c = 0; c < NDH; ++c)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dxa[c][e] = 0.f;
+#pragma unroll
+      for (int k0 = 0; k0 < FDP; k0 += 16) {
+        uint32_t ah[4], al[4];
+        lda_rm(ah, gh, SM::LDG, 16 * rb, k0);
+        lda_rm(al, gl, SM::LDG, 16 * rb, k0);
+#pragma unroll
+        for (int np = 0; np < NDH / 2; ++np) {
+          uint32_t bh[4], bl[4];
+          ldb_kn(bh, wh, SM::LDW, k0, d0 + 16 * np);
+          mma16816(dxa[2 * np], ah, bh[0], bh[1]);
+          mma16816(dxa[2 * np + 1], ah, bh[2], bh[3]);
+          mma16816(dxa[2 * np], al, bh[0], bh[1]);
+          mma16816(dxa[2 * np + 1], al, bh[2], bh[3]);
+          ldb_kn(bl, wl, SM::LDW, k0, d0 + 16 * np);
+          mma16816(dxa[2 * np], ah, bl[0], bl[1]);
+          mma16816(dxa[2 * np + 1], ah, bl[2], bl[3]);
+        }
+      }
+      const bool pair = (Dh & 1) == 0;
+#pragma unroll
+      for (int nt = 0; nt < NDH; ++nt) {
+        const int d = d0 + 8 * nt + 2 * cq;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = r0 + lrow + 8 * h;
+          if (row >= R || d >= Dh) continue;
+          float* o = dx + (size_t)row * Dh + d;
+          if (pair) {
+            *reinterpret_cast<float2*>(o) = make_float2(dxa[nt][2 * h], dxa[nt][2 * h + 1]);
+          } else {
+            o[0] = dxa[nt][2 * h];
+            if (d + 1 < Dh) o[1] = dxa[nt][2 * h + 1];
+          }
+        }
+      }
+    }
+    // dW += g^T x: M = features (this warp's 16-row tiles), K = rows, N = Dh
+#pragma unroll
+    for (int mi = 0; mi < MTW; ++mi) {
+      const int mt = warp + 8 * mi;
+      if (mt >= MT) continue;
+#pragma unroll
+      for (int k0 = 0; k0 < kR; k0 += 16) {
+        uint32_t ah[4], al[4];
+        lda_tr(ah, gh, SM::LDG, 16 * mt, k0);
+        lda_tr(al, gl, SM::LDG, 16 * mt, k0);
+#pragma unroll
+        for (int np = 0; np < DHP / 16; ++np) {
+          uint32_t bh[4], bl[4];
+          ldb_kn(bh, xh, SM::LDX, k0, 16 * np);
+          mma16816(dwa[mi][2 * np], ah, bh[0], bh[1]);
+          mma16816(dwa[mi][2 * np + 1], ah, bh[2], bh[3]);
+          mma16816(dwa[mi][2 * np], al, bh[0], bh[1]);
+          mma16816(dwa[mi][2 * np + 1], al, bh[2], bh[3]);
+          if constexpr (sizeof(XT) == 4) {
+            ldb_kn(bl, xl, SM::LDX, k0, 16 * np);
+            mma16816(dwa[mi][2 * np], ah, bl[0], bl[1]);
+            mma16816(dwa[mi][2 * np + 1], ah, bl[2], bl[3]);
+          }
+        }
+      }
+    }
+  }
+  // this CTA's dW partial [FDP, DHP] (the reduction reads only [Fd, Dh])
+  float* part = dw_part + (size_t)blockIdx.x * FDP * DHP;
+#pragma unroll
+  for (int mi = 0; mi < MTW; ++mi) {
+    const int mt = warp + 8 * mi;
+    if (mt >= MT) continue;
+#pragma unroll
+    for (int nt = 0; nt < DHP / 8; ++nt) {
+      const int d = 8 * nt + 2 * cq;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = 16 * mt + gq + 8 * h;
+        *reinterpret_cast<float2*>(part + c * DHP + d) =
+            make_float2(dwa[mi][nt][2 * h], dwa[mi][nt][2 * h + 1]);
+      }
+    }
+  }
+}
+
+// dW[c][d] = sum over CTAs of the partials, in CTA order
+__global__ void __launch_bounds__(256)
+hedgehog_dw_reduce_kernel(const float* __restrict__ part, int nparts, int FDP, int DHP, int Fd,
+                          int Dh, float* __restrict__ dw) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= Fd * Dh) return;
+  const int c = i / Dh, d = i % Dh;
+  float s = 0.f;
+  for (int p = 0; p < nparts; ++p) s += part[((size_t)p * FDP + c) * DHP + d];
+  dw[i] = s;
+}
+
+std::mutex g_hh_mu;
+template <typename Kern>
+int hh_attr(Kern k, size_t bytes, bool* done) {
+  if (bytes <= 48 * 1024) return LZ_OK;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(g_hh_mu);
+  if (dev < 64 && !done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) {
+      set_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+      return LZ_ERR_CUDA;
+    }
+    done[dev] = true;
+  }
+  return LZ_OK;
+}
+
+int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && n[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev] = v > 0 ? v : 148;
+  }
+  return dev < 64 ? n[dev] : 148;
+}
+
+int dims_pad(int Dh, int Fd, int* dhp, int* fdp) {
+  *dhp = Dh <= 32 ? 32 : Dh <= 64 ? 64 : Dh <= 128 ? 128 : 0;
+  *fdp = Fd <= 32 ? 32 : Fd <= 64 ? 64 : Fd <= 128 ? 128 : 0;
+  return (*dhp && *fdp) ? LZ_OK : LZ_ERR_UNSUPPORTED;
+}
+
+// persistent grid: two CTAs of 8 warps per SM
+int hh_grid(int R) {
+  const int ntiles = (R + kR - 1) / kR;
+  return std::max(1, std::min(ntiles, sm_count() * 2));
+}
+
+template <typename XT, int DHP, int FDP, bool FULL>
+int launch_fwd_t(const void* x, const float* w, int R, int Dh, int Fd, int xs, int ws, bf16* f,
+                 cudaStream_t st) {
+  using SM = HhSmem<DHP, FDP>;
+  static bool done[64] = {false};
+  int rc = hh_attr(hedgehog_fwd_kernel<XT, DHP, FDP, FULL>, SM::fwd_bytes, done);
+  if (rc) return rc;
+  const int vec = (Dh % (16 / (int)sizeof(XT)) == 0) && aligned16(x) && aligned16(f);
+  hedgehog_fwd_kernel<XT, DHP, FDP, FULL><<<hh_grid(R), kT, SM::fwd_bytes, st>>>(
+      static_cast<const XT*>(x), w, R, Dh, Fd, vec, f);
+  count_launches(1);
+  return check_launch("hedgehog_fwd_kernel");
+}
+template <typename XT, int DHP, int FDP>
+int launch_fwd(const void* x, const float* w, int R, int Dh, int Fd, int xs, int ws, bf16* f,
+               cudaStream_t st) {
+  return Fd == FDP ? launch_fwd_t<XT, DHP, FDP, true>(x, w, R, Dh, Fd, xs, ws, f, st)
+                   : launch_fwd_t<XT, DHP, FDP, false>(x, w, R, Dh, Fd, xs, ws, f, st);
+}
+
+template <typename XT, typename GT, int DHP, int FDP, bool FULL>
+int launch_bwd_t(const void* x, const float* w, const void* df, int R, int Dh, int Fd, int xs,
+                 int ws, float* dx, float* dw, void* work, cudaStream_t st) {
+  using SM = HhSmem<DHP, FDP>;
+  static bool done[64] = {false};
+  int rc = hh_attr(hedgehog_bwd_kernel<XT, GT, DHP, FDP, FULL>, SM::bwd_bytes, done);
+  if (rc) return rc;
+  const int grid = hh_grid(R);
+  const int vec = (Dh % (16 / (int)sizeof(XT)) == 0) && aligned16(x);
+  const int vec_df = (Fd % 8 == 0) && aligned16(df);
+  float* part = static_cast<float*>(work);
+  hedgehog_bwd_kernel<XT, GT, DHP, FDP, FULL><<<grid, kT, SM::bwd_bytes, st>>>(
+      static_cast<const XT*>(x), w, static_cast<const GT*>(df), R, Dh, Fd, vec, vec_df, dx, part);
+  count_launches(1);
+  rc = check_launch("hedgehog_bwd_kernel");
+  if (rc) return rc;
+  hedgehog_dw_reduce_kernel<<<(Fd * Dh + 255) / 256, 256, 0, st>>>(part, grid, FDP, DHP, Fd, Dh,
+                                                                   dw);
+  count_launches(1);
+  return check_launch("hedgehog_dw_reduce_kernel");
+}
+template <typename XT, typename GT, int DHP, int FDP>
+int launch_bwd(const void* x, const float* w, const void* df, int R, int Dh, int Fd, int xs,
+               int ws, float* dx, float* dw, void* work, cudaStream_t st) {
+  return Fd == FDP
+             ? launch_bwd_t<XT, GT, DHP, FDP, true>(x, w, df, R, Dh, Fd, xs, ws, dx, dw, work, st)
+             : launch_bwd_t<XT, GT, DHP, FDP, false>(x, w, df, R, Dh, Fd, xs, ws, dx, dw, work, st);
+}
+
+}  // namespace
+
+size_t hedgehog_bwd_workspace(int R, int Dh, int Fd) {
+  int dhp, fdp;
+  if (dims_pad(Dh, Fd, &dhp, &fdp)) return 0;
+  return (size_t)hh_grid(R) * fdp * dhp * 4;
+}
+
+int hedgehog_fwd(const void* x, int x_dtype, const float* w, int R, int Dh, int Fd, bf16* f,
+                 cudaStream_t st) {
+  int dhp, fdp;
+  if (dims_pad(Dh, Fd, &dhp, &fdp)) {
+    set_error("hedgehog: head dim and feature dim must be <= 128");
+    return LZ_ERR_UNSUPPORTED;
+  }
+  const int xs = x_dtype == LZ_DTYPE_F32;
+#define LZ_HH_FWD(dh, fd)                                                                 \
+  if (dhp == dh && fdp == fd)                                                             \
+    return xs ? launch_fwd<float, dh, fd>(x, w, R, Dh, Fd, 1, 1, f, st)                   \
+              : launch_fwd<bf16, dh, fd>(x, w, R, Dh, Fd, 0, 1, f, st);
+  LZ_HH_FWD(32, 32) LZ_HH_FWD(32, 64) LZ_HH_FWD(32, 128)
+  LZ_HH_FWD(64, 32) LZ_HH_FWD(64, 64) LZ_HH_FWD(64, 128)
+  LZ_HH_FWD(128, 32) LZ_HH_FWD(128, 64) LZ_HH_FWD(128, 128)
+#undef LZ_HH_FWD
+  return LZ_ERR_UNSUPPORTED;
+}
+
+int hedgehog_bwd(const void* x, int x_dtype, const float* w, const void* df, int df_dtype, int R,
+                 int Dh, int Fd, float* dx, float* dw, void* work, cudaStream_t st) {
+  int dhp, fdp;
+  if (dims_pad(Dh, Fd, &dhp, &fdp)) {
+    set_error("hedgehog: head dim and feature dim must be <= 128");
+    return LZ_ERR_UNSUPPORTED;
+  }
+  const bool xf = x_dtype == LZ_DTYPE_F32, gf = df_dtype == LZ_DTYPE_F32;
+#define LZ_HH_BWD(dh, fd)                                                                        \
+  if (dhp == dh && fdp == fd) {                                                                  \
+    if (xf && gf)                                                                                \
+      return launch_bwd<float, float, dh, fd>(x, w, df, R, Dh, Fd, 1, 1, dx, dw, work, st);      \
+    if (xf) return launch_bwd<float, bf16, dh, fd>(x, w, df, R, Dh, Fd, 1, 1, dx, dw, work, st); \
+    if (gf) return launch_bwd<bf16, float, dh, fd>(x, w, df, R, Dh, Fd, 0, 1, dx, dw, work, st); \
+    return launch_bwd<bf16, bf16, dh, fd>(x, w, df, R, Dh, Fd, 0, 1, dx, dw, work, st);          \
+  }
+  LZ_HH_BWD(32, 32) LZ_HH_BWD(32, 64) LZ_HH_BWD(32, 128)
+  LZ_HH_BWD(64, 32) LZ_HH_BWD(64, 64) LZ_HH_BWD(64, 128)
+  LZ_HH_BWD(128, 32) LZ_HH_BWD(128, 64) LZ_HH_BWD(128, 128)
+#undef LZ_HH_BWD
+  return LZ_ERR_UNSUPPORTED;
+}
+
+}  // namespace lz
+
+extern "C" size_t lz_hedgehog_bwd_workspace_bytes(int R, int Dh, int Fd) {
+  if (R < 1 || Dh < 1 || Fd < 1) return 0;
+  return lz::hedgehog_bwd_workspace(R, Dh, Fd);
+}
+
+extern "C" int lz_hedgehog_fwd(const void* x, int x_dtype, const float* weight, void* f, int R,
+                               int Dh, int Fd, void* stream) {
+  lz::clear_error();
+  LZ_REQUIRE(x && weight && f, LZ_ERR_INVALID_ARGUMENT, "null pointer");
+  LZ_REQUIRE(R >= 1 && Dh >= 1 && Fd >= 1, LZ_ERR_INVALID_ARGUMENT, "sizes must be positive");
+  LZ_REQUIRE(x_dtype == LZ_DTYPE_F32 || x_dtype == LZ_DTYPE_BF16, LZ_ERR_INVALID_ARGUMENT,
+             "x_dtype must be LZ_DTYPE_F32 or LZ_DTYPE_BF16");
+  return lz::hedgehog_fwd(x, x_dtype, weight, R, Dh, Fd, static_cast<bf16*>(f),
+                          static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lz_hedgehog_bwd(const void* x, int x_dtype, const float* weight, const void* df,
+                               int df_dtype, float* dx, float* dweight, void* workspace,
+                               size_t workspace_bytes, int R, int Dh, int Fd, void* stream) {
+  lz::clear_error();
+  LZ_REQUIRE(x && weight && df && dx && dweight && workspace, LZ_ERR_INVALID_ARGUMENT,
+             "null pointer");
+  LZ_REQUIRE(R >= 1 && Dh >= 1 && Fd >= 1, LZ_ERR_INVALID_ARGUMENT, "sizes must be positive");
+  LZ_REQUIRE((x_dtype == LZ_DTYPE_F32 || x_dtype == LZ_DTYPE_BF16) &&
+                 (df_dtype == LZ_DTYPE_F32 || df_dtype == LZ_DTYPE_BF16),
+             LZ_ERR_INVALID_ARGUMENT, "dtypes must be LZ_DTYPE_F32 or LZ_DTYPE_BF16");
+  LZ_REQUIRE(workspace_bytes >= lz::hedgehog_bwd_workspace(R, Dh, Fd), LZ_ERR_WORKSPACE,
+             "workspace too small (lz_hedgehog_bwd_workspace_bytes)");
+  return lz::hedgehog_bwd(x, x_dtype, weight, df, df_dtype, R, Dh, Fd, dx, dweight, workspace,
+                          static_cast<cudaStream_t>(stream));
+}

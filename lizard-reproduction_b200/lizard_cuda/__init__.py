@@ -8,6 +8,7 @@ Everything runs in liblizard_cuda.so through its C ABI; there is no CPU path.
 """
 from ._lib import launch_count, load  # noqa: F401
 from .gla import gla
+from .hedgehog import hedgehog
 from .swa import swa
 
-__all__ = ["gla", "swa", "load", "launch_count"]
+__all__ = ["gla", "swa", "hedgehog", "load", "launch_count"]

@@ -43,6 +43,10 @@ _SIGNATURES = {
                                     _vp, _vp, _c_int, _vp, _vp, _c_size] + [_c_int] * 5 + [_vp]),
     "lz_gla_seg_combine": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp] + [_c_int] * 4 + [_vp]),
     "lz_gla_seg_gate_offset": (_c_int, [_vp, _vp] + [_c_int] * 4 + [_vp]),
+    "lz_hedgehog_fwd": (_c_int, [_vp, _c_int, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
+    "lz_hedgehog_bwd": (_c_int, [_vp, _c_int, _vp, _vp, _c_int, _vp, _vp, _vp, _c_size, _c_int,
+                                 _c_int, _c_int, _vp]),
+    "lz_hedgehog_bwd_workspace_bytes": (_c_size, [_c_int] * 3),
     "lz_swa_saved_bytes": (_c_size, [_c_int] * 4),
     "lz_swa_bwd_workspace_bytes": (_c_size, [_c_int] * 5),
     "lz_swa_fwd": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp, _vp, _c_size] + [_c_int] * 4

@@ -5,23 +5,19 @@ constructor arguments, parameter names and forward contract
 (forward(hidden_states, position_embeddings) -> (out, None)), with the two
 attention branches running on this package's gla / swa kernels exactly where
 the reference's `triton` backend calls kernels.gla / kernels.swa
-(src/lizard_attention.py:90-93). The projections, feature map, gate and RoPE
-are the same torch operations as the reference.
+(src/lizard_attention.py:90-93), and the Hedgehog feature map on the fused
+kernel (lizard_cuda.hedgehog, bf16 features straight into gla). The
+projections, gate and RoPE are the same torch operations as the reference.
 """
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
 from .gla import gla
+from .hedgehog import hedgehog as fused_hedgehog
 from .swa import swa
 
 BACKENDS = ("cuda",)
-
-
-def hedgehog(x, weight):
-    """[softmax(x W^T), softmax(-x W^T)] (src/lizard_attention.py:9-11)."""
-    xw = x @ weight.T
-    return torch.cat([xw.softmax(-1), (-xw).softmax(-1)], dim=-1)
 
 
 def _rotate_half(x):
@@ -75,8 +71,8 @@ class LizardAttention(nn.Module):
         k = self.split(self.k_proj(x), self.kv_heads).to(dtype)
         v = self.split(self.v_proj(x), self.kv_heads).to(dtype)
         z = self.W_gamma(x).to(dtype).squeeze(-1)
-        fq = hedgehog(q, self.phi_q.weight.to(dtype))
-        fk = hedgehog(k, self.phi_k.weight.to(dtype))
+        fq = fused_hedgehog(q, self.phi_q.weight.to(dtype))
+        fk = fused_hedgehog(k, self.phi_k.weight.to(dtype))
         cos, sin = (t.to(dtype) for t in position_embeddings)
         qr, kr = apply_rotary(q, k, cos, sin)
         alpha, meta = self.alpha_blend.to(dtype), self.meta_tokens.to(dtype)

@@ -1,0 +1,59 @@
+"""Fused Hedgehog feature map against the oracle's restatement of the
+reference (float64 autograd): features and the gradients w.r.t. x and W."""
+import pytest
+import torch
+
+import lizard_oracle as orc
+from parity import assert_grad, assert_output
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib(built_lib):
+    import lizard_cuda
+    lizard_cuda.load()
+
+
+@pytest.mark.parametrize("shape,Fd,xdt,std", [
+    ((2, 4, 40, 32), 8, torch.float32, 0.3 * 8),     # layer_tiny: head dim 32, feature dim 8
+    ((1, 4, 256, 64), 128, torch.float32, 0.02),     # config 1 layer: the init scale
+    ((2, 3, 300, 64), 128, torch.bfloat16, 0.16),    # bf16 heads, trained-size weights
+    ((1, 2, 77, 20), 24, torch.float32, 0.5),        # odd sizes, padded tiles
+    ((1, 1, 1000, 128), 100, torch.float32, 0.1),
+])
+def test_hedgehog_matches_reference(shape, Fd, xdt, std):
+    import lizard_cuda
+    g = torch.Generator(device=DEV).manual_seed(3)
+    x = torch.randn(shape, generator=g, device=DEV).to(xdt)
+    w = std * torch.randn(Fd, shape[-1], generator=g, device=DEV)
+    df = torch.randn(*shape[:-1], 2 * Fd, generator=g, device=DEV)
+    xl, wl = x.clone().requires_grad_(), w.clone().requires_grad_()
+    f = lizard_cuda.hedgehog(xl, wl)
+    assert f.dtype == torch.bfloat16 and f.shape == (*shape[:-1], 2 * Fd)
+    f.backward(df.bfloat16())
+    xr = x.double().cpu().requires_grad_()
+    wr = w.double().cpu().requires_grad_()
+    ref = orc.hedgehog(xr, wr)
+    ref.backward(df.bfloat16().double().cpu())
+    assert_output(f, ref.float(), f"hedgehog {shape} f")
+    assert_grad(xl.grad, xr.grad.float(), f"hedgehog {shape} dx")
+    assert_grad(wl.grad, wr.grad.float(), f"hedgehog {shape} dW")
+    assert xl.grad.dtype == xdt and wl.grad.dtype == torch.float32
+
+
+def test_hedgehog_rows_sum_to_one_and_weights_are_deterministic():
+    import lizard_cuda
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x = torch.randn(3, 4, 500, 64, generator=g, device=DEV)
+    w = (0.05 * torch.randn(128, 64, generator=g, device=DEV)).requires_grad_()
+    f = lizard_cuda.hedgehog(x, w)
+    s = f.float().view(-1, 2, 128).sum(-1)
+    assert torch.allclose(s, torch.ones_like(s), atol=2e-2)
+    df = torch.randn_like(f)
+    f.backward(df)
+    g1 = w.grad.clone()
+    w.grad = None
+    lizard_cuda.hedgehog(x, w).backward(df)
+    assert torch.equal(w.grad, g1)
