@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define LZ_ABI_VERSION 2
+#define LZ_ABI_VERSION 3
 
 enum {
   LZ_OK = 0,
@@ -117,6 +117,29 @@ int lz_gla_bwd(const void* fq, const void* fk, const void* v,
                void* dfq, void* dfk, void* dv, int grad_dtype,
                float* dlog_gamma, void* workspace, size_t workspace_bytes,
                int B, int H, int L, int F, int D, int chunk, void* stream);
+
+/* Grouped-query forms (GQA): fk [B*Hkv, L, F] and v [B*Hkv, L, D] with
+ * H % Hkv == 0; query head h reads key/value head h / (H / Hkv). In the
+ * reference's caller fk = hedgehog(repeat_interleave(k)) and v is
+ * repeat_interleaved (src/lizard_attention.py:73-85), so every head of a group
+ * sees the same fk and v: these entries take them once. fq, y, log_gamma, the
+ * saved buffer and the forward workspace keep H heads (the sizes above); the
+ * backward workspace is lz_gla_bwd_gqa_workspace_bytes (it adds fp32 room for
+ * the per-head dfk and dv). dfk and dv are [B*Hkv, L, *], each the sum over its
+ * group of query heads in a fixed order (the autograd of repeat_interleave).
+ * lz_gla_fwd / lz_gla_bwd are these with Hkv = H. */
+size_t lz_gla_bwd_gqa_workspace_bytes(int B, int H, int Hkv, int L, int F, int D, int chunk);
+int lz_gla_fwd_gqa(const void* fq, const void* fk, const void* v,
+                   const float* log_gamma, int gate_per_head,
+                   void* y, void* saved, size_t saved_bytes,
+                   void* workspace, size_t workspace_bytes,
+                   int B, int H, int Hkv, int L, int F, int D, int chunk, void* stream);
+int lz_gla_bwd_gqa(const void* fq, const void* fk, const void* v,
+                   const float* log_gamma, int gate_per_head,
+                   const void* saved, size_t saved_bytes, const void* dy,
+                   void* dfq, void* dfk, void* dv, int grad_dtype,
+                   float* dlog_gamma, void* workspace, size_t workspace_bytes,
+                   int B, int H, int Hkv, int L, int F, int D, int chunk, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* GLA, sequence-parallel segments                                          */
@@ -213,6 +236,31 @@ int lz_hedgehog_bwd(const void* x, int x_dtype, const float* weight, const void*
                     size_t workspace_bytes, int R, int Dh, int Fd, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Rotary embedding for the SWA operands (no counterpart in the reference's   */
+/* kernels: its caller rotates with torch ops, src/lizard_attention.py:87-88, */
+/* and kernels.swa splits nothing)                                           */
+/* ------------------------------------------------------------------------ */
+
+/* r = x * cos + rotate_half(x) * sin (Llama's rotate-half RoPE), written as
+ * hi = bf16(r) and, when lo is not null, lo = bf16(r - hi): the q / k and
+ * q_lo / k_lo operands of lz_swa_fwd_gqa. x is [B, Hx, L, Dh] in x_dtype
+ * (LZ_DTYPE_F32 or LZ_DTYPE_BF16) at element strides x_sb, x_sh, x_sl (Dh
+ * contiguous), so a projection output [B, L, Hx * Dh] is read in place with
+ * x_sb = L * Hx * Dh, x_sh = Dh, x_sl = Hx * Dh. cos and sin are [B, L, Dh]
+ * in cs_dtype at strides cs_sb (0 broadcasts one table over the batch) and
+ * cs_sl. hi and lo are contiguous [B, Hx, L, Dh] bf16. Dh must be even. */
+int lz_rope_split(const void* x, int x_dtype, long long x_sb, long long x_sh, long long x_sl,
+                  const void* cos, const void* sin, int cs_dtype, long long cs_sb,
+                  long long cs_sl, void* hi, void* lo, int B, int Hx, int L, int Dh,
+                  void* stream);
+
+/* Gradient of lz_rope_split's r: dx = R^T dr, dr fp32 contiguous
+ * [B, Hx, L, Dh], dx contiguous [B, Hx, L, Dh] in dx_dtype. */
+int lz_rope_bwd(const float* dr, const void* cos, const void* sin, int cs_dtype,
+                long long cs_sb, long long cs_sl, void* dx, int dx_dtype, int B, int Hx,
+                int L, int Dh, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* SWA                                                                      */
 /* ------------------------------------------------------------------------ */
 
@@ -247,6 +295,26 @@ int lz_swa_bwd(const void* q, const void* k, const void* v,
                const void* dy, void* dq, void* dk, void* dv, int grad_dtype,
                float* dmeta, void* workspace, size_t workspace_bytes,
                int B, int H, int L, int D, void* stream);
+
+/* Grouped-query forms (GQA): k, k_lo and v carry Hkv heads [B*Hkv, L, D],
+ * H % Hkv == 0, and query head h attends with key/value head h / (H / Hkv).
+ * This is the reference caller's repeat_interleave of K and V
+ * (src/lizard_attention.py:73-76) without the copies. q, y, saved and the
+ * workspace keep H heads (the same sizes as above); dk and dv are
+ * [B*Hkv, L, D], each the sum over its group of query heads (the autograd
+ * of repeat_interleave). lz_swa_fwd / lz_swa_bwd are these with Hkv = H. */
+int lz_swa_fwd_gqa(const void* q, const void* k, const void* v,
+                   const void* q_lo, const void* k_lo,
+                   const float* meta, int n_meta, int window,
+                   void* y, void* saved, size_t saved_bytes,
+                   int B, int H, int Hkv, int L, int D, void* stream);
+int lz_swa_bwd_gqa(const void* q, const void* k, const void* v,
+                   const void* q_lo, const void* k_lo,
+                   const float* meta, int n_meta, int window,
+                   const void* saved, size_t saved_bytes,
+                   const void* dy, void* dq, void* dk, void* dv, int grad_dtype,
+                   float* dmeta, void* workspace, size_t workspace_bytes,
+                   int B, int H, int Hkv, int L, int D, void* stream);
 
 /* lz_swa_bwd for callers that cannot allocate (no counterpart in the
  * reference, whose kernels always allocate through torch). Some hosts give a

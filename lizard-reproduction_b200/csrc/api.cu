@@ -40,6 +40,14 @@ extern "C" size_t lz_gla_bwd_workspace_bytes(int B, int H, int L, int F, int D, 
   return lz::gla_work_layout(B, H, L, F, D, lz::gla_bwd_split(B, H, L, F, D), nullptr, nullptr);
 }
 
+extern "C" size_t lz_gla_bwd_gqa_workspace_bytes(int B, int H, int Hkv, int L, int F, int D,
+                                                 int chunk) {
+  (void)chunk;
+  if (B < 1 || H < 1 || L < 1 || F < 1 || D < 1 || Hkv < 1 || H % Hkv) return 0;
+  return lz::gla_work_layout(B, H, L, F, D, lz::gla_bwd_split(B, H, L, F, D), nullptr, nullptr,
+                             Hkv != H);
+}
+
 extern "C" size_t lz_gla_fwd_workspace_bytes(int B, int H, int L, int F, int D, int chunk) {
   (void)chunk;
   if (B < 1 || H < 1 || L < 1 || F < 1 || D < 1) return 0;
@@ -60,13 +68,15 @@ extern "C" int lz_gla_set_schedule(int schedule) {
   return lz::gla_set_schedule(schedule);
 }
 
-extern "C" int lz_gla_fwd(const void* fq, const void* fk, const void* v, const float* log_gamma,
-                          int gate_per_head, void* y, void* saved, size_t saved_bytes,
-                          void* workspace, size_t workspace_bytes, int B, int H, int L, int F,
-                          int D, int chunk, void* stream) {
+extern "C" int lz_gla_fwd_gqa(const void* fq, const void* fk, const void* v,
+                              const float* log_gamma, int gate_per_head, void* y, void* saved,
+                              size_t saved_bytes, void* workspace, size_t workspace_bytes, int B,
+                              int H, int Hkv, int L, int F, int D, int chunk, void* stream) {
   lz::clear_error();
   int rc = check_sizes(B, H, L, F, D);
   if (rc) return rc;
+  LZ_REQUIRE(Hkv >= 1 && H % Hkv == 0, LZ_ERR_INVALID_ARGUMENT,
+             "the key/value head count must divide the query head count");
   LZ_REQUIRE(fq && fk && v && log_gamma && y, LZ_ERR_INVALID_ARGUMENT, "null tensor pointer");
   LZ_REQUIRE(chunk >= 1, LZ_ERR_INVALID_ARGUMENT, "chunk must be >= 1");
   LZ_REQUIRE(F <= 256, LZ_ERR_UNSUPPORTED, "feature dim above 256 is not supported");
@@ -89,18 +99,29 @@ extern "C" int lz_gla_fwd(const void* fq, const void* fk, const void* v, const f
   }
   return lz::gla_fwd(static_cast<const bf16*>(fq), static_cast<const bf16*>(fk),
                      static_cast<const bf16*>(v), log_gamma, gate_per_head ? 1 : 0,
-                     static_cast<bf16*>(y), sv, fw, B, H, L, F, D,
+                     static_cast<bf16*>(y), sv, fw, B, H, Hkv, L, F, D,
                      static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int lz_gla_bwd(const void* fq, const void* fk, const void* v, const float* log_gamma,
-                          int gate_per_head, const void* saved, size_t saved_bytes,
-                          const void* dy, void* dfq, void* dfk, void* dv, int grad_dtype,
-                          float* dlog_gamma, void* workspace, size_t workspace_bytes, int B,
-                          int H, int L, int F, int D, int chunk, void* stream) {
+extern "C" int lz_gla_fwd(const void* fq, const void* fk, const void* v, const float* log_gamma,
+                          int gate_per_head, void* y, void* saved, size_t saved_bytes,
+                          void* workspace, size_t workspace_bytes, int B, int H, int L, int F,
+                          int D, int chunk, void* stream) {
+  return lz_gla_fwd_gqa(fq, fk, v, log_gamma, gate_per_head, y, saved, saved_bytes, workspace,
+                        workspace_bytes, B, H, H, L, F, D, chunk, stream);
+}
+
+extern "C" int lz_gla_bwd_gqa(const void* fq, const void* fk, const void* v,
+                              const float* log_gamma, int gate_per_head, const void* saved,
+                              size_t saved_bytes, const void* dy, void* dfq, void* dfk, void* dv,
+                              int grad_dtype, float* dlog_gamma, void* workspace,
+                              size_t workspace_bytes, int B, int H, int Hkv, int L, int F, int D,
+                              int chunk, void* stream) {
   lz::clear_error();
   int rc = check_sizes(B, H, L, F, D);
   if (rc) return rc;
+  LZ_REQUIRE(Hkv >= 1 && H % Hkv == 0, LZ_ERR_INVALID_ARGUMENT,
+             "the key/value head count must divide the query head count");
   LZ_REQUIRE(fq && fk && v && log_gamma && saved && dy && dfq && dfk && dv && dlog_gamma &&
                  workspace,
              LZ_ERR_INVALID_ARGUMENT, "null pointer");
@@ -111,7 +132,7 @@ extern "C" int lz_gla_bwd(const void* fq, const void* fk, const void* v, const f
   LZ_REQUIRE(D <= 128, LZ_ERR_UNSUPPORTED, "value dim above 128 is not supported in the backward");
   const size_t need_s = lz::gla_saved_layout(B, H, L, F, D, nullptr, nullptr);
   const bool split = lz::gla_bwd_split(B, H, L, F, D);
-  const size_t need_w = lz::gla_work_layout(B, H, L, F, D, split, nullptr, nullptr);
+  const size_t need_w = lz::gla_work_layout(B, H, L, F, D, split, nullptr, nullptr, Hkv != H);
   LZ_REQUIRE(saved_bytes >= need_s, LZ_ERR_WORKSPACE, "saved buffer too small");
   LZ_REQUIRE(workspace_bytes >= need_w, LZ_ERR_WORKSPACE, "workspace too small");
   LZ_REQUIRE(lz::aligned16(saved) && lz::aligned16(workspace), LZ_ERR_INVALID_ARGUMENT,
@@ -119,11 +140,22 @@ extern "C" int lz_gla_bwd(const void* fq, const void* fk, const void* v, const f
   lz::GlaSaved sv;
   lz::GlaWork wk;
   lz::gla_saved_layout(B, H, L, F, D, (unsigned char*)const_cast<void*>(saved), &sv);
-  lz::gla_work_layout(B, H, L, F, D, split, static_cast<unsigned char*>(workspace), &wk);
+  lz::gla_work_layout(B, H, L, F, D, split, static_cast<unsigned char*>(workspace), &wk,
+                      Hkv != H);
   return lz::gla_bwd(static_cast<const bf16*>(fq), static_cast<const bf16*>(fk),
                      static_cast<const bf16*>(v), log_gamma, gate_per_head ? 1 : 0, sv,
                      static_cast<const bf16*>(dy), dfq, dfk, dv, grad_dtype, dlog_gamma, wk, B,
-                     H, L, F, D, static_cast<cudaStream_t>(stream));
+                     H, Hkv, L, F, D, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lz_gla_bwd(const void* fq, const void* fk, const void* v, const float* log_gamma,
+                          int gate_per_head, const void* saved, size_t saved_bytes,
+                          const void* dy, void* dfq, void* dfk, void* dv, int grad_dtype,
+                          float* dlog_gamma, void* workspace, size_t workspace_bytes, int B,
+                          int H, int L, int F, int D, int chunk, void* stream) {
+  return lz_gla_bwd_gqa(fq, fk, v, log_gamma, gate_per_head, saved, saved_bytes, dy, dfq, dfk, dv,
+                        grad_dtype, dlog_gamma, workspace, workspace_bytes, B, H, H, L, F, D,
+                        chunk, stream);
 }
 
 extern "C" size_t lz_swa_saved_bytes(int B, int H, int L, int D) {
@@ -137,13 +169,15 @@ extern "C" size_t lz_swa_bwd_workspace_bytes(int B, int H, int L, int D, int n_m
   return lz::swa_work_layout(B, H, L, n_meta, nullptr, nullptr);
 }
 
-extern "C" int lz_swa_fwd(const void* q, const void* k, const void* v, const void* q_lo,
-                          const void* k_lo, const float* meta, int n_meta, int window, void* y,
-                          void* saved, size_t saved_bytes, int B, int H, int L, int D,
-                          void* stream) {
+extern "C" int lz_swa_fwd_gqa(const void* q, const void* k, const void* v, const void* q_lo,
+                              const void* k_lo, const float* meta, int n_meta, int window,
+                              void* y, void* saved, size_t saved_bytes, int B, int H, int Hkv,
+                              int L, int D, void* stream) {
   lz::clear_error();
   int rc = check_sizes(B, H, L, 1, D);
   if (rc) return rc;
+  LZ_REQUIRE(Hkv >= 1 && H % Hkv == 0, LZ_ERR_INVALID_ARGUMENT,
+             "the key/value head count must divide the query head count");
   LZ_REQUIRE(q && k && v && y, LZ_ERR_INVALID_ARGUMENT, "null tensor pointer");
   LZ_REQUIRE((q_lo == nullptr) == (k_lo == nullptr), LZ_ERR_INVALID_ARGUMENT,
              "q_lo and k_lo must be both null or both set");
@@ -163,17 +197,29 @@ extern "C" int lz_swa_fwd(const void* q, const void* k, const void* v, const voi
   return lz::swa_fwd(static_cast<const bf16*>(q), static_cast<const bf16*>(k),
                      static_cast<const bf16*>(v), static_cast<const bf16*>(q_lo),
                      static_cast<const bf16*>(k_lo), meta, n_meta, window,
-                     static_cast<bf16*>(y), sv, B, H, L, D, static_cast<cudaStream_t>(stream));
+                     static_cast<bf16*>(y), sv, B, H, Hkv, L, D,
+                     static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int lz_swa_bwd(const void* q, const void* k, const void* v, const void* q_lo,
-                          const void* k_lo, const float* meta, int n_meta, int window,
-                          const void* saved, size_t saved_bytes, const void* dy, void* dq,
-                          void* dk, void* dv, int grad_dtype, float* dmeta, void* workspace,
-                          size_t workspace_bytes, int B, int H, int L, int D, void* stream) {
+extern "C" int lz_swa_fwd(const void* q, const void* k, const void* v, const void* q_lo,
+                          const void* k_lo, const float* meta, int n_meta, int window, void* y,
+                          void* saved, size_t saved_bytes, int B, int H, int L, int D,
+                          void* stream) {
+  return lz_swa_fwd_gqa(q, k, v, q_lo, k_lo, meta, n_meta, window, y, saved, saved_bytes, B, H,
+                        H, L, D, stream);
+}
+
+extern "C" int lz_swa_bwd_gqa(const void* q, const void* k, const void* v, const void* q_lo,
+                              const void* k_lo, const float* meta, int n_meta, int window,
+                              const void* saved, size_t saved_bytes, const void* dy, void* dq,
+                              void* dk, void* dv, int grad_dtype, float* dmeta,
+                              void* workspace, size_t workspace_bytes, int B, int H, int Hkv,
+                              int L, int D, void* stream) {
   lz::clear_error();
   int rc = check_sizes(B, H, L, 1, D);
   if (rc) return rc;
+  LZ_REQUIRE(Hkv >= 1 && H % Hkv == 0, LZ_ERR_INVALID_ARGUMENT,
+             "the key/value head count must divide the query head count");
   LZ_REQUIRE(q && k && v && saved && dy && dq && dk && dv && workspace,
              LZ_ERR_INVALID_ARGUMENT, "null pointer");
   LZ_REQUIRE((q_lo == nullptr) == (k_lo == nullptr), LZ_ERR_INVALID_ARGUMENT,
@@ -199,7 +245,17 @@ extern "C" int lz_swa_bwd(const void* q, const void* k, const void* v, const voi
                      static_cast<const bf16*>(v), static_cast<const bf16*>(q_lo),
                      static_cast<const bf16*>(k_lo), meta, n_meta, window,
                      sv, static_cast<const bf16*>(dy), dq, dk, dv,
-                     grad_dtype, dmeta, wk, B, H, L, D, static_cast<cudaStream_t>(stream));
+                     grad_dtype, dmeta, wk, B, H, Hkv, L, D, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lz_swa_bwd(const void* q, const void* k, const void* v, const void* q_lo,
+                          const void* k_lo, const float* meta, int n_meta, int window,
+                          const void* saved, size_t saved_bytes, const void* dy, void* dq,
+                          void* dk, void* dv, int grad_dtype, float* dmeta, void* workspace,
+                          size_t workspace_bytes, int B, int H, int L, int D, void* stream) {
+  return lz_swa_bwd_gqa(q, k, v, q_lo, k_lo, meta, n_meta, window, saved, saved_bytes, dy, dq,
+                        dk, dv, grad_dtype, dmeta, workspace, workspace_bytes, B, H, H, L, D,
+                        stream);
 }
 
 // ------------------------------------------------ sequence-parallel segments

@@ -40,6 +40,13 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 constexpr float kTiny = 1.1754943508222875e-38f;
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Key/value head read by query head row block bh = b * H + h when keys and
+// values carry H / grp heads (grouped-query attention): b * (H / grp) + h / grp.
+__host__ __device__ __forceinline__ int kv_head(int bh, int H, int grp) {
+  const int b = bh / H;
+  return b * (H / grp) + (bh - b * H) / grp;
+}
+
 // ------------------------------------------------------------ device side
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

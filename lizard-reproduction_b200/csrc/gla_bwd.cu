@@ -203,9 +203,9 @@ gla_bwd_chunk_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
                      const float* __restrict__ delta, const bf16* __restrict__ S,
                      const float* __restrict__ Z, const bf16* __restrict__ dS,
                      const float* __restrict__ dZ, void* __restrict__ dfq,
-                     void* __restrict__ dfk, void* __restrict__ dv, int gdt,
-                     float* __restrict__ dG, float* __restrict__ dGt, int L, int F, int D, int NT,
-                     int vec_f, int vec_d, int s_seeded, int ds_seeded) {
+                     void* __restrict__ dfk, void* __restrict__ dv, int gdt, int gdt_kv,
+                     float* __restrict__ dG, float* __restrict__ dGt, int H, int grp, int L, int F,
+                     int D, int NT, int vec_f, int vec_d, int s_seeded, int ds_seeded) {
   using SM = ChunkSmem<FP, DP>;
   constexpr int FB = SM::FB, LDF = SM::LDF, LDD = SM::LDD, LDT = SM::LDT;
   constexpr int NDH = DP / 16;  // n8 tiles of one column half of dv
@@ -233,13 +233,14 @@ gla_bwd_chunk_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
   const int n = blockIdx.x % NT, bh = blockIdx.x / NT;
   const int r0 = n * kC, nvalid = min(kC, L - r0);
   const size_t rowF = (size_t)bh * L * F, rowD = (size_t)bh * L * D;
+  const size_t kvr = (size_t)kv_head(bh, H, grp) * L;  // rows of fk and v (GQA)
   const size_t chunk = (size_t)bh * NT + n;
   const bool with_s = n > 0 || s_seeded;       // state entering the chunk is not zero
   const bool with_ds = n + 1 < NT || ds_seeded;  // gradient leaving the chunk is not zero
 
   stage_tile<kC, FP, 256>(sQ, LDF, fq + rowF, F, r0, L, 0, F, vec_f);
-  stage_tile<kC, FP, 256>(sK, LDF, fk + rowF, F, r0, L, 0, F, vec_f);
-  stage_tile<kC, DP, 256>(sV, LDD, v + rowD, D, r0, L, 0, D, vec_d);
+  stage_tile<kC, FP, 256>(sK, LDF, fk + kvr * F, F, r0, L, 0, F, vec_f);
+  stage_tile<kC, DP, 256>(sV, LDD, v + kvr * D, D, r0, L, 0, D, vec_d);
   stage_tile<kC, DP, 256>(sDy, LDD, dy + rowD, D, r0, L, 0, D, vec_d);
   cp_async_commit();
   auto stage_state = [&](int fo) {
@@ -461,8 +462,8 @@ gla_bwd_chunk_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
                (has1 ? __bfloat162float(sK[i0 * LDF + f + 1]) * acc[nt][1] : 0.f);
         dg1 -= __bfloat162float(sK[i1 * LDF + f]) * acc[nt][2] +
                (has1 ? __bfloat162float(sK[i1 * LDF + f + 1]) * acc[nt][3] : 0.f);
-        if (v0) store_grad2(dfk, rowF + (size_t)(r0 + i0) * F + f, acc[nt][0], acc[nt][1], has1, fpair, gdt);
-        if (v1) store_grad2(dfk, rowF + (size_t)(r0 + i1) * F + f, acc[nt][2], acc[nt][3], has1, fpair, gdt);
+        if (v0) store_grad2(dfk, rowF + (size_t)(r0 + i0) * F + f, acc[nt][0], acc[nt][1], has1, fpair, gdt_kv);
+        if (v1) store_grad2(dfk, rowF + (size_t)(r0 + i1) * F + f, acc[nt][2], acc[nt][3], has1, fpair, gdt_kv);
       }
     }
     // (6) dv (inter) += bf16(fk * ks) dS over this feature block
@@ -493,8 +494,8 @@ gla_bwd_chunk_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
     const int d = dc + 8 * nt + 2 * cq;
     if (d >= D) continue;
     const bool has1 = d + 1 < D;
-    if (v0) store_grad2(dv, rowD + (size_t)(r0 + i0) * D + d, dvacc[nt][0], dvacc[nt][1], has1, dpair, gdt);
-    if (v1) store_grad2(dv, rowD + (size_t)(r0 + i1) * D + d, dvacc[nt][2], dvacc[nt][3], has1, dpair, gdt);
+    if (v0) store_grad2(dv, rowD + (size_t)(r0 + i0) * D + d, dvacc[nt][0], dvacc[nt][1], has1, dpair, gdt_kv);
+    if (v1) store_grad2(dv, rowD + (size_t)(r0 + i1) * D + d, dvacc[nt][2], dvacc[nt][3], has1, dpair, gdt_kv);
   }
   dg0 = quad_sum(dg0);
   dg1 = quad_sum(dg1);
@@ -589,18 +590,78 @@ int ensure_smem(Kern k, size_t bytes, bool* done) {
   return LZ_OK;
 }
 
+// Gradients of grouped keys / values (GQA): out[kvh] = sum_g in[kvh * grp + g]
+// over the grp query heads that read key/value head kvh, added in head order
+// in fp32 (the autograd of the caller's repeat_interleave,
+// src/lizard_attention.py:76). per_head = L * cols elements; 4 per thread
+// when per_head % 4 == 0 (the scratch is 256-byte aligned).
+template <int V>
+__global__ void __launch_bounds__(256)
+gla_group_sum_kernel(const float* __restrict__ in, void* __restrict__ out, int gdt, int grp,
+                     long long per_head, long long n_items) {
+  for (long long e = blockIdx.x * 256ll + threadIdx.x; e < n_items;
+       e += (long long)gridDim.x * 256) {
+    const long long o = e * V;
+    const long long kvh = o / per_head, r = o - kvh * per_head;
+    const float* src = in + kvh * grp * per_head + r;
+    float acc[V];
+    if constexpr (V == 4) {
+      float4 a = *reinterpret_cast<const float4*>(src);
+      for (int g = 1; g < grp; ++g) {
+        const float4 b = *reinterpret_cast<const float4*>(src + g * per_head);
+        a.x += b.x;
+        a.y += b.y;
+        a.z += b.z;
+        a.w += b.w;
+      }
+      acc[0] = a.x;
+      acc[1] = a.y;
+      acc[2] = a.z;
+      acc[3] = a.w;
+    } else {
+      acc[0] = src[0];
+      for (int g = 1; g < grp; ++g) acc[0] += src[g * per_head];
+    }
+#pragma unroll
+    for (int u = 0; u < V; u += 2) {
+      if constexpr (V == 1)
+        store_grad(out, (size_t)o, acc[0], gdt);
+      else
+        store_grad2(out, (size_t)(o + u), acc[u], acc[u + 1], true, true, gdt);
+    }
+  }
+}
+
+int launch_group_sum(const float* in, void* out, int gdt, int n_kv, int grp, long long per_head,
+                     cudaStream_t st) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const bool v4 = per_head % 4 == 0 && aligned16(in) &&
+                  (reinterpret_cast<uintptr_t>(out) & (gdt == LZ_DTYPE_BF16 ? 3 : 7)) == 0;
+  const long long n_items = (long long)n_kv * per_head / (v4 ? 4 : 1);
+  const long long want = (n_items + 255) / 256, cap = (long long)sms * 8;
+  const unsigned grid = (unsigned)(want < cap ? (want > 0 ? want : 1) : cap);
+  if (v4)
+    gla_group_sum_kernel<4><<<grid, 256, 0, st>>>(in, out, gdt, grp, per_head, n_items);
+  else
+    gla_group_sum_kernel<1><<<grid, 256, 0, st>>>(in, out, gdt, grp, per_head, n_items);
+  count_launches(1);
+  return check_launch("gla_group_sum_kernel");
+}
+
 template <int FP, int DP>
 int launch_chunk(const bf16* fq, const bf16* fk, const bf16* v, const bf16* dy,
                  const GlaSaved& sv, const GlaWork& wk, void* dfq, void* dfk, void* dv, int gdt,
-                 int BH, int L, int F, int D, int NT, int vec_f, int vec_d, int s_seeded,
-                 int ds_seeded, cudaStream_t st) {
+                 int gdt_kv, int BH, int H, int grp, int L, int F, int D, int NT, int vec_f,
+                 int vec_d, int s_seeded, int ds_seeded, cudaStream_t st) {
   using SM = ChunkSmem<FP, DP>;
   static bool done[64] = {false};
   int rc = ensure_smem(gla_bwd_chunk_kernel<FP, DP>, SM::bytes, done);
   if (rc) return rc;
   gla_bwd_chunk_kernel<FP, DP><<<(unsigned)((long long)BH * NT), 256, SM::bytes, st>>>(
-      fq, fk, v, dy, sv.g, sv.den, wk.delta, sv.s, sv.z, wk.ds, wk.dz, dfq, dfk, dv, gdt, wk.dg,
-      wk.dgt, L, F, D, NT, vec_f, vec_d, s_seeded, ds_seeded);
+      fq, fk, v, dy, sv.g, sv.den, wk.delta, sv.s, sv.z, wk.ds, wk.dz, dfq, dfk, dv, gdt, gdt_kv,
+      wk.dg, wk.dgt, H, grp, L, F, D, NT, vec_f, vec_d, s_seeded, ds_seeded);
   count_launches(1);
   return check_launch("gla_bwd_chunk_kernel");
 }
@@ -608,10 +669,10 @@ int launch_chunk(const bf16* fq, const bf16* fk, const bf16* v, const bf16* dy,
 }  // namespace
 
 int gla_bwd_tail(const bf16* fq, const bf16* fk, const bf16* v, int gph, const GlaSaved& sv,
-                 const bf16* dy, void* dfq, void* dfk, void* dv, int gdt, float* dlg,
-                 const GlaWork& wk, int B, int H, int L, int F, int D, int s_seeded,
+                 const bf16* dy, void* dfq, void* dfk, void* dv, int gdt, int gdt_kv, float* dlg,
+                 const GlaWork& wk, int B, int H, int Hkv, int L, int F, int D, int s_seeded,
                  int ds_seeded, cudaStream_t stream) {
-  const int BH = B * H;
+  const int BH = B * H, grp = H / Hkv;
   const int NT = (int)gla_nt(L);
   const int vec_f = (F % 8 == 0) && aligned16(fq) && aligned16(fk);
   const int vec_d = (D % 8 == 0) && aligned16(v) && aligned16(dy) && aligned16(sv.s) &&
@@ -621,8 +682,8 @@ int gla_bwd_tail(const bf16* fq, const bf16* fk, const bf16* v, int gph, const G
   int rc = LZ_OK;
 #define LZ_CHUNK_CASE(fp, dp)                                                                  \
   if (FP == fp && DP == dp)                                                                    \
-    rc = launch_chunk<fp, dp>(fq, fk, v, dy, sv, wk, dfq, dfk, dv, gdt, BH, L, F, D, NT, vec_f, \
-                              vec_d, s_seeded, ds_seeded, stream);                             \
+    rc = launch_chunk<fp, dp>(fq, fk, v, dy, sv, wk, dfq, dfk, dv, gdt, gdt_kv, BH, H, grp, L, \
+                              F, D, NT, vec_f, vec_d, s_seeded, ds_seeded, stream);            \
   else
   LZ_CHUNK_CASE(32, 32) LZ_CHUNK_CASE(32, 64) LZ_CHUNK_CASE(32, 128)
   LZ_CHUNK_CASE(64, 32) LZ_CHUNK_CASE(64, 64) LZ_CHUNK_CASE(64, 128)
@@ -639,19 +700,33 @@ int gla_bwd_tail(const bf16* fq, const bf16* fk, const bf16* v, int gph, const G
 
 int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
             const GlaSaved& sv, const bf16* dy, void* dfq, void* dfk, void* dv, int gdt,
-            float* dlg, const GlaWork& wk, int B, int H, int L, int F, int D,
+            float* dlg, const GlaWork& wk, int B, int H, int Hkv, int L, int F, int D,
             cudaStream_t stream) {
   (void)lg;
   const int BH = B * H;
   const int NT = (int)gla_nt(L);
   int rc = LZ_OK;
+  // grouped keys / values: per-query-head dfk, dv into fp32 scratch, then summed
+  const bool gqa = Hkv != H;
+  void* dfk_h = gqa ? static_cast<void*>(wk.gk) : dfk;
+  void* dv_h = gqa ? static_cast<void*>(wk.gv) : dv;
+  const int gdt_kv = gqa ? LZ_DTYPE_F32 : gdt;
+  auto finish = [&]() -> int {
+    if (!gqa) return LZ_OK;
+    int r = launch_group_sum(wk.gk, dfk, gdt, B * Hkv, H / Hkv, (long long)L * F, stream);
+    if (r) return r;
+    return launch_group_sum(wk.gv, dv, gdt, B * Hkv, H / Hkv, (long long)L * D, stream);
+  };
   if (gla_saved_chunk(B, H, L, F, D, fq, fk, v) == 128) {
     // states on the tensor-core forward's 128-token boundaries
     rc = gla_bwd_tc_states(fq, dy, sv, wk, B, H, L, stream);
     if (rc) return rc;
-    rc = gla_bwd_tc_chunks(fq, fk, v, dy, sv, wk, dfq, dfk, dv, gdt, B, H, L, 0, 0, stream);
+    rc = gla_bwd_tc_chunks(fq, fk, v, dy, sv, wk, dfq, dfk_h, dv_h, gdt, gdt_kv, B, H, Hkv, L, 0,
+                           0, stream);
     if (rc) return rc;
-    return launch_gate(wk.dg, wk.dgt, dlg, B, H, L, (L + 127) / 128, 128, gph, stream);
+    rc = launch_gate(wk.dg, wk.dgt, dlg, B, H, L, (L + 127) / 128, 128, gph, stream);
+    if (rc) return rc;
+    return finish();
   }
   if (wk.inc) {
     rc = gla_bwd_split_states(fq, dy, sv, wk, B, H, L, F, D, stream);
@@ -676,8 +751,10 @@ int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int 
     rc = check_launch("gla_bwd_state_kernel");
     if (rc) return rc;
   }
-  return gla_bwd_tail(fq, fk, v, gph, sv, dy, dfq, dfk, dv, gdt, dlg, wk, B, H, L, F, D, 0, 0,
-                      stream);
+  rc = gla_bwd_tail(fq, fk, v, gph, sv, dy, dfq, dfk_h, dv_h, gdt, gdt_kv, dlg, wk, B, H, Hkv, L,
+                    F, D, 0, 0, stream);
+  if (rc) return rc;
+  return finish();
 }
 
 }  // namespace lz

@@ -333,8 +333,9 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
                         const __grid_constant__ CUtensorMap tdfk,
                         const __grid_constant__ CUtensorMap tdv, const float* __restrict__ G,
                         const float* __restrict__ den, const float* __restrict__ delta,
-                        const float* __restrict__ Z, const float* __restrict__ dZ, int L, int NT,
-                        int gdt, void* __restrict__ dfq, void* __restrict__ dfk,
+                        const float* __restrict__ Z, const float* __restrict__ dZ, int H, int grp,
+                        int L, int NT, int gdt, int gdt_kv, void* __restrict__ dfq,
+                        void* __restrict__ dfk,
                         void* __restrict__ dv, float* __restrict__ dG, float* __restrict__ dGt,
                         int s_seeded, int ds_seeded) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -353,11 +354,13 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
   float* sDGa = reinterpret_cast<float*>(misc + kMDGa);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = blockIdx.x % NT, bh = blockIdx.x / NT;
+  const int kvh = kv_head(bh, H, grp);  // head of fk and v (GQA)
   const int r0 = n * kC, nvalid = min(kC, L - r0);
   const size_t rowb = (size_t)bh * L, chunk = (size_t)bh * NT + n;
   const bool with_s = n > 0 || s_seeded;
   const bool with_ds = n + 1 < NT || ds_seeded;
-  const bool bf16_out = gdt == LZ_DTYPE_BF16;
+  const bool bf16_out = gdt == LZ_DTYPE_BF16;    // dfq
+  const bool bf16_kv = gdt_kv == LZ_DTYPE_BF16;  // dfk, dv (per query head)
 
   if (tid == 0) {
     tc::mbar_init(&bars[B2_FULL], 1);
@@ -392,10 +395,10 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
       tc::mbar_expect_tx(full, (with_s ? 5 : 4) * kTile);
       tc::tma_load_3d(base + kOQ, &tq, 0, r0, bh, full);
       tc::tma_load_3d(base + kOQ + 16384, &tq, 64, r0, bh, full);
-      tc::tma_load_3d(base + kOK, &tk, 0, r0, bh, full);
-      tc::tma_load_3d(base + kOK + 16384, &tk, 64, r0, bh, full);
-      tc::tma_load_3d(base + kOV, &tv, 0, r0, bh, full);
-      tc::tma_load_3d(base + kOV + 16384, &tv, 64, r0, bh, full);
+      tc::tma_load_3d(base + kOK, &tk, 0, r0, kvh, full);
+      tc::tma_load_3d(base + kOK + 16384, &tk, 64, r0, kvh, full);
+      tc::tma_load_3d(base + kOV, &tv, 0, r0, kvh, full);
+      tc::tma_load_3d(base + kOV + 16384, &tv, 64, r0, kvh, full);
       tc::tma_load_3d(base + kODY, &tdy, 0, r0, bh, full);
       tc::tma_load_3d(base + kODY + 16384, &tdy, 64, r0, bh, full);
       if (with_s) {
@@ -596,7 +599,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
 #pragma unroll
           for (int c = 0; c < 64; ++c) dvv[c] += ks * t5[c];
         }
-        if (bf16_out) {
+        if (bf16_kv) {
           tile_row_store64(base + kOX, i, hb, dvv);
         } else if (valid) {
           float4* o = reinterpret_cast<float4*>(static_cast<float*>(dv) + (rowb + r0 + i) * 128 +
@@ -606,7 +609,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
             o[c] = make_float4(dvv[4 * c], dvv[4 * c + 1], dvv[4 * c + 2], dvv[4 * c + 3]);
         }
       }
-      if (bf16_out) {
+      if (bf16_kv) {
         tc::fence_proxy_async_smem();
         tc::named_bar_sync(2, 128);
         if (i == 0) {
@@ -633,7 +636,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
           t3[c] = t3[c] + ks * (t4v - sDZ[64 * hb + c]);
         }
         dgk += row_dot64(base + kOK, i, hb, t3);
-        if (bf16_out) {
+        if (bf16_kv) {
           tile_row_store64(base + kODAD, i, hb, t3);
         } else if (valid) {
           float4* o = reinterpret_cast<float4*>(static_cast<float*>(dfk) + (rowb + r0 + i) * 128 +
@@ -643,7 +646,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
             o[c] = make_float4(t3[4 * c], t3[4 * c + 1], t3[4 * c + 2], t3[4 * c + 3]);
         }
       }
-      if (bf16_out) {
+      if (bf16_kv) {
         tc::fence_proxy_async_smem();
         tc::named_bar_sync(3, 128);
         if (i == 0) {
@@ -748,18 +751,18 @@ int gla_bwd_tc_states(const bf16* fq, const bf16* dy, const GlaSaved& sv, const 
 
 int gla_bwd_tc_chunks(const bf16* fq, const bf16* fk, const bf16* v, const bf16* dy,
                       const GlaSaved& sv, const GlaWork& wk, void* dfq, void* dfk, void* dv,
-                      int gdt, int B, int H, int L, int s_seeded, int ds_seeded,
-                      cudaStream_t stream) {
+                      int gdt, int gdt_kv, int B, int H, int Hkv, int L, int s_seeded,
+                      int ds_seeded, cudaStream_t stream) {
   const int BH = B * H, NT = (L + kC - 1) / kC;
   CUtensorMap mq, mk, mv, mdy, ms, mds, mdfq, mdfk, mdv;
-  bool ok = make_map(&mq, fq, BH, L) && make_map(&mk, fk, BH, L) && make_map(&mv, v, BH, L) &&
-            make_map(&mdy, dy, BH, L) && make_map(&ms, sv.s, BH, NT * kC) &&
-            make_map(&mds, wk.ds, BH, NT * kC);
-  if (gdt == LZ_DTYPE_BF16)
-    ok = ok && make_map(&mdfq, dfq, BH, L) && make_map(&mdfk, dfk, BH, L) &&
-         make_map(&mdv, dv, BH, L);
-  else
-    mdfq = mdfk = mdv = mq;  // fp32 gradients are stored directly, the maps are unused
+  bool ok = make_map(&mq, fq, BH, L) && make_map(&mk, fk, B * Hkv, L) &&
+            make_map(&mv, v, B * Hkv, L) && make_map(&mdy, dy, BH, L) &&
+            make_map(&ms, sv.s, BH, NT * kC) && make_map(&mds, wk.ds, BH, NT * kC);
+  // fp32 gradients are stored directly; their maps are unused
+  mdfq = mdfk = mdv = mq;
+  if (gdt == LZ_DTYPE_BF16) ok = ok && make_map(&mdfq, dfq, BH, L);
+  if (gdt_kv == LZ_DTYPE_BF16)
+    ok = ok && make_map(&mdfk, dfk, BH, L) && make_map(&mdv, dv, BH, L);
   if (!ok) {
     set_error("gla_bwd: tensor map encoding failed");
     return LZ_ERR_CUDA;
@@ -768,8 +771,8 @@ int gla_bwd_tc_chunks(const bf16* fq, const bf16* fk, const bf16* v, const bf16*
   int rc = ensure_attr(reinterpret_cast<const void*>(gla_bwd_chunk_tc_kernel), kSmem2, done);
   if (rc) return rc;
   gla_bwd_chunk_tc_kernel<<<(unsigned)((long long)BH * NT), kThreads, kSmem2, stream>>>(
-      mq, mk, mv, mdy, ms, mds, mdfq, mdfk, mdv, sv.g, sv.den, wk.delta, sv.z, wk.dz, L, NT, gdt,
-      dfq, dfk, dv, wk.dg, wk.dgt, s_seeded, ds_seeded);
+      mq, mk, mv, mdy, ms, mds, mdfq, mdfk, mdv, sv.g, sv.den, wk.delta, sv.z, wk.dz, H, H / Hkv,
+      L, NT, gdt, gdt_kv, dfq, dfk, dv, wk.dg, wk.dgt, s_seeded, ds_seeded);
   count_launches(1);
   return check_launch("gla_bwd_chunk_tc_kernel");
 }

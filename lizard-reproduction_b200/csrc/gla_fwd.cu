@@ -43,7 +43,7 @@ template <int FP, int DV>
 __global__ void __launch_bounds__(128, 2)
 gla_fwd_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
                const bf16* __restrict__ v, const float* __restrict__ lg, int gate_per_head,
-               int H, int L, int F, int D, int NT, int nslices, int vec_f, int vec_d,
+               int H, int grp, int L, int F, int D, int NT, int nslices, int vec_f, int vec_d,
                bf16* __restrict__ y, float* __restrict__ y32, float* __restrict__ den_out,
                float* __restrict__ g_out, bf16* __restrict__ s_out, float* __restrict__ z_out) {
   using SM = GlaFwdSmem<FP, DV>;
@@ -69,8 +69,9 @@ gla_fwd_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
   const bool save = (y32 != nullptr);
   const bool lead = (slice == 0);  // writes per-row / per-feature saves once
   const bf16* Q = fq + (size_t)bh * L * F;
-  const bf16* K = fk + (size_t)bh * L * F;
-  const bf16* V = v + (size_t)bh * L * D;
+  const size_t kvr = (size_t)kv_head(bh, H, grp) * L;  // key/value rows (GQA)
+  const bf16* K = fk + kvr * F;
+  const bf16* V = v + kvr * D;
   const float* LG = lg + (size_t)(gate_per_head ? bh : b) * L;
 
   for (int i = tid; i < FP; i += 128) sZ[i] = 0.f;
@@ -222,8 +223,8 @@ namespace {
 
 template <int FP, int DV>
 int launch_fwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, int B,
-               int H, int L, int F, int D, int vec_f, int vec_d, bf16* y, const GlaSaved& sv,
-               cudaStream_t stream) {
+               int H, int grp, int L, int F, int D, int vec_f, int vec_d, bf16* y,
+               const GlaSaved& sv, cudaStream_t stream) {
   using SM = GlaFwdSmem<FP, DV>;
   static std::mutex mu;
   static bool attr_done[64] = {false};
@@ -246,8 +247,8 @@ int launch_fwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
   const int nslices = ceil_div(D, DV);
   const long long grid = (long long)B * H * nslices;
   gla_fwd_kernel<FP, DV><<<(unsigned)grid, 128, SM::bytes, stream>>>(
-      fq, fk, v, lg, gph, H, L, F, D, NT, nslices, vec_f, vec_d, y, sv.y32, sv.den, sv.g, sv.s,
-      sv.z);
+      fq, fk, v, lg, gph, H, grp, L, F, D, NT, nslices, vec_f, vec_d, y, sv.y32, sv.den, sv.g,
+      sv.s, sv.z);
   count_launches(1);
   return check_launch("gla_fwd_kernel");
 }
@@ -255,16 +256,18 @@ int launch_fwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
 }  // namespace
 
 int gla_fwd_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, bf16* y,
-               const GlaSaved& sv, int B, int H, int L, int F, int D, cudaStream_t stream);
+               const GlaSaved& sv, int B, int H, int Hkv, int L, int F, int D,
+               cudaStream_t stream);
 
 int gla_fwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, bf16* y,
-            const GlaSaved& sv, const GlaFwdWork& fw, int B, int H, int L, int F, int D,
+            const GlaSaved& sv, const GlaFwdWork& fw, int B, int H, int Hkv, int L, int F, int D,
             cudaStream_t stream) {
-  if (fw.inc) return gla_fwd_split_run(fq, fk, v, lg, gph, y, sv, fw, B, H, L, F, D, stream);
-  const int BH = B * H;
+  if (fw.inc)
+    return gla_fwd_split_run(fq, fk, v, lg, gph, y, sv, fw, B, H, Hkv, L, F, D, stream);
+  const int BH = B * H, grp = H / Hkv;
   if (gla_saved_chunk(B, H, L, F, D, fq, fk, v) == 128) {
     // tensor-core kernel; in training it also saves the 128-token chunk states
-    const int rc = gla_fwd_tc(fq, fk, v, lg, gph, y, sv, B, H, L, F, D, stream);
+    const int rc = gla_fwd_tc(fq, fk, v, lg, gph, y, sv, B, H, Hkv, L, F, D, stream);
     if (rc != LZ_ERR_UNSUPPORTED) return rc;
     if (sv.y32) {
       set_error("gla_fwd: the tensor-core forward is unavailable (tensor map encoding failed)");
@@ -278,7 +281,8 @@ int gla_fwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int 
   const int vec_d = (D % 8 == 0) && aligned16(v);
 #define LZ_FWD_CASE(fp, dv) \
   if (FP == fp && DV == dv) \
-    return launch_fwd<fp, dv>(fq, fk, v, lg, gph, B, H, L, F, D, vec_f, vec_d, y, sv, stream);
+    return launch_fwd<fp, dv>(fq, fk, v, lg, gph, B, H, grp, L, F, D, vec_f, vec_d, y, sv, \
+                              stream);
   LZ_FWD_CASE(32, 16) LZ_FWD_CASE(32, 32) LZ_FWD_CASE(32, 64)
   LZ_FWD_CASE(64, 16) LZ_FWD_CASE(64, 32) LZ_FWD_CASE(64, 64)
   LZ_FWD_CASE(128, 16) LZ_FWD_CASE(128, 32) LZ_FWD_CASE(128, 64)

@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap ty,
                   const __grid_constant__ CUtensorMap ts, const float* __restrict__ lg,
-                  int gate_per_head, int H, int L, int NT, bf16* __restrict__ y,
+                  int gate_per_head, int H, int grp, int L, int NT, bf16* __restrict__ y,
                   float* __restrict__ y32, float* __restrict__ den_out,
                   float* __restrict__ g_out, bf16* __restrict__ s_out,
                   float* __restrict__ z_out) {
@@ -103,6 +103,7 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x, b = bh / H;
+  const int kvh = kv_head(bh, H, grp);  // head of fk and v (GQA)
   const bool save = (y32 != nullptr);
 
   if (tid == 0) {
@@ -163,10 +164,10 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         tc::mbar_expect_tx(full, kStageBytes);
         tc::tma_load_3d(stage + kOffQ, &tq, 0, n * kC, bh, full);
         tc::tma_load_3d(stage + kOffQ + 16384, &tq, 64, n * kC, bh, full);
-        tc::tma_load_3d(stage + kOffK, &tk, 0, n * kC, bh, full);
-        tc::tma_load_3d(stage + kOffK + 16384, &tk, 64, n * kC, bh, full);
-        tc::tma_load_3d(stage + kOffV, &tv, 0, n * kC, bh, full);
-        tc::tma_load_3d(stage + kOffV + 16384, &tv, 64, n * kC, bh, full);
+        tc::tma_load_3d(stage + kOffK, &tk, 0, n * kC, kvh, full);
+        tc::tma_load_3d(stage + kOffK + 16384, &tk, 64, n * kC, kvh, full);
+        tc::tma_load_3d(stage + kOffV, &tv, 0, n * kC, kvh, full);
+        tc::tma_load_3d(stage + kOffV + 16384, &tv, 64, n * kC, kvh, full);
         ++issued[st];
       }
       for (int st = 0; st < 2; ++st)  // every issued copy lands before exit
@@ -559,7 +560,8 @@ bool make_map(CUtensorMap* m, const void* ptr, int BH, int L, int cols) {
 // Returns LZ_ERR_UNSUPPORTED (without launching) for shapes this kernel does
 // not cover; the caller then uses the general kernel.
 int gla_fwd_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, bf16* y,
-               const GlaSaved& sv, int B, int H, int L, int F, int D, cudaStream_t stream) {
+               const GlaSaved& sv, int B, int H, int Hkv, int L, int F, int D,
+               cudaStream_t stream) {
   if (F != 128 || D != 128) return LZ_ERR_UNSUPPORTED;
   if (!aligned16(fq) || !aligned16(fk) || !aligned16(v)) return LZ_ERR_UNSUPPORTED;
   if (!aligned16(y) || (sv.y32 && (!aligned16(sv.y32) || !aligned16(sv.s)))) {
@@ -573,8 +575,8 @@ int gla_fwd_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
   }
   const int BH = B * H;
   CUtensorMap mq, mk, mv, my;
-  if (!make_map(&mq, fq, BH, L, F) || !make_map(&mk, fk, BH, L, F) || !make_map(&mv, v, BH, L, D) ||
-      !make_map(&my, y, BH, L, D))
+  if (!make_map(&mq, fq, BH, L, F) || !make_map(&mk, fk, B * Hkv, L, F) ||
+      !make_map(&mv, v, B * Hkv, L, D) || !make_map(&my, y, BH, L, D))
     return LZ_ERR_UNSUPPORTED;
   static std::mutex mu;
   static bool attr_done[64] = {false};
@@ -596,8 +598,8 @@ int gla_fwd_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
   const int NT = (L + kC - 1) / kC;
   CUtensorMap ms = my;  // unused (not prefetched, not stored) in inference
   if (sv.y32 && !make_map(&ms, sv.s, BH, NT * kC, 128)) return LZ_ERR_UNSUPPORTED;
-  gla_fwd_tc_kernel<<<BH, kThreads, kSmemBytes, stream>>>(mq, mk, mv, my, ms, lg, gph, H, L, NT, y,
-                                                     sv.y32, sv.den, sv.g, sv.s, sv.z);
+  gla_fwd_tc_kernel<<<BH, kThreads, kSmemBytes, stream>>>(mq, mk, mv, my, ms, lg, gph, H, H / Hkv,
+                                                     L, NT, y, sv.y32, sv.den, sv.g, sv.s, sv.z);
   count_launches(1);
   return check_launch("gla_fwd_tc_kernel");
 }

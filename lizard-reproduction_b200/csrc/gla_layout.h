@@ -27,6 +27,10 @@ struct GlaWork {
   float* inc = nullptr;    // [BH, NT, F, D] per-chunk increment Q^_n^T dY_n (fp32)
   float* incz = nullptr;   // [BH, NT, F]   per-chunk increment Q^_n^T delta_n
   float* lam = nullptr;    // [BH, NT]      log decay of each chunk, G_end - G_start
+  // grouped keys / values only (fk, v with fewer heads than fq): per-query-head
+  // gradients before the sum over each group
+  float* gk = nullptr;     // [BH, L, F] fp32
+  float* gv = nullptr;     // [BH, L, D] fp32
 };
 
 // Forward scratch of the chunk-parallel schedule.
@@ -104,7 +108,7 @@ inline size_t gla_saved_layout(int B, int H, int L, int F, int D, unsigned char*
 }
 
 inline size_t gla_work_layout(int B, int H, int L, int F, int D, bool split,
-                              unsigned char* base, GlaWork* out) {
+                              unsigned char* base, GlaWork* out, bool gqa = false) {
   const size_t BH = (size_t)B * H, NT = gla_nt(L);
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -120,6 +124,8 @@ inline size_t gla_work_layout(int B, int H, int L, int F, int D, bool split,
   const size_t o_inc = split ? take(BH * NT * F * D * 4) : 0;
   const size_t o_incz = split ? take(BH * NT * F * 4) : 0;
   const size_t o_lam = split ? take(BH * NT * 4) : 0;
+  const size_t o_gk = gqa ? take(BH * L * F * 4) : 0;
+  const size_t o_gv = gqa ? take(BH * L * D * 4) : 0;
   if (out && base) {
     out->delta = reinterpret_cast<float*>(base + o_delta);
     out->ds = reinterpret_cast<bf16*>(base + o_ds);
@@ -130,6 +136,10 @@ inline size_t gla_work_layout(int B, int H, int L, int F, int D, bool split,
       out->inc = reinterpret_cast<float*>(base + o_inc);
       out->incz = reinterpret_cast<float*>(base + o_incz);
       out->lam = reinterpret_cast<float*>(base + o_lam);
+    }
+    if (gqa) {
+      out->gk = reinterpret_cast<float*>(base + o_gk);
+      out->gv = reinterpret_cast<float*>(base + o_gv);
     }
   }
   return off;
@@ -161,14 +171,15 @@ inline size_t gla_fwd_work_layout(int B, int H, int L, int F, int D, unsigned ch
   return off;
 }
 
+// Hkv: heads of fk and v (H % Hkv == 0; query head h reads head h / (H / Hkv)).
 int gla_fwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, bf16* y,
-            const GlaSaved& sv, const GlaFwdWork& fw, int B, int H, int L, int F, int D,
+            const GlaSaved& sv, const GlaFwdWork& fw, int B, int H, int Hkv, int L, int F, int D,
             cudaStream_t stream);
 
 // Chunk-parallel schedule (gla_split.cu).
 int gla_fwd_split_run(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
-                      bf16* y, const GlaSaved& sv, const GlaFwdWork& fw, int B, int H, int L,
-                      int F, int D, cudaStream_t stream);
+                      bf16* y, const GlaSaved& sv, const GlaFwdWork& fw, int B, int H, int Hkv,
+                      int L, int F, int D, cudaStream_t stream);
 int gla_bwd_split_states(const bf16* fq, const bf16* dy, const GlaSaved& sv, const GlaWork& wk,
                          int B, int H, int L, int F, int D, cudaStream_t stream);
 
@@ -193,10 +204,11 @@ int gla_seg_gate_offset(float* dlg, const float* totals, int P, int rank, int ro
 
 // Per-chunk gradients and the log-gate gradient, once wk.ds / wk.dz / wk.delta
 // hold the state gradients (s_seeded / ds_seeded: the state entering the first
-// chunk / the gradient leaving the last chunk is not zero).
+// chunk / the gradient leaving the last chunk is not zero). fk and v carry Hkv
+// heads; dfk and dv are written per query head ([B*H, L, *]) in gdt_kv.
 int gla_bwd_tail(const bf16* fq, const bf16* fk, const bf16* v, int gph, const GlaSaved& sv,
-                 const bf16* dy, void* dfq, void* dfk, void* dv, int gdt, float* dlg,
-                 const GlaWork& wk, int B, int H, int L, int F, int D, int s_seeded,
+                 const bf16* dy, void* dfq, void* dfk, void* dv, int gdt, int gdt_kv, float* dlg,
+                 const GlaWork& wk, int B, int H, int Hkv, int L, int F, int D, int s_seeded,
                  int ds_seeded, cudaStream_t stream);
 
 // Tensor-core backward for the 128-token chunk layout (gla_bwd_tc.cu).
@@ -204,12 +216,14 @@ int gla_bwd_tc_states(const bf16* fq, const bf16* dy, const GlaSaved& sv, const 
                       int B, int H, int L, cudaStream_t stream);
 int gla_bwd_tc_chunks(const bf16* fq, const bf16* fk, const bf16* v, const bf16* dy,
                       const GlaSaved& sv, const GlaWork& wk, void* dfq, void* dfk, void* dv,
-                      int gdt, int B, int H, int L, int s_seeded, int ds_seeded,
-                      cudaStream_t stream);
+                      int gdt, int gdt_kv, int B, int H, int Hkv, int L, int s_seeded,
+                      int ds_seeded, cudaStream_t stream);
 
+// fk and v carry Hkv heads (H % Hkv == 0); dfk and dv are [B*Hkv, L, *], each
+// the sum over its group of query heads (wk.gk / wk.gv hold the per-head terms).
 int gla_bwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
             const GlaSaved& sv, const bf16* dy, void* dfq, void* dfk, void* dv, int gdt,
-            float* dlg, const GlaWork& wk, int B, int H, int L, int F, int D,
+            float* dlg, const GlaWork& wk, int B, int H, int Hkv, int L, int F, int D,
             cudaStream_t stream);
 
 }  // namespace lz

@@ -146,8 +146,8 @@ __device__ __forceinline__ void store_block_f32(float* __restrict__ m, const flo
 //   lam_n = G_end - G_start
 __global__ void __launch_bounds__(128)
 gla_split_finc_kernel(const bf16* __restrict__ fk, const bf16* __restrict__ v,
-                      const float* __restrict__ lg, int gph, int H, int L, int F, int D, int NT,
-                      int nfb, int ndb, int vec_f, int vec_d, float* __restrict__ inc,
+                      const float* __restrict__ lg, int gph, int H, int grp, int L, int F, int D,
+                      int NT, int nfb, int ndb, int vec_f, int vec_d, float* __restrict__ inc,
                       float* __restrict__ incz, float* __restrict__ lam) {
   __shared__ __align__(16) bf16 sK[kC * kLD];
   __shared__ __align__(16) bf16 sV[kC * kLD];
@@ -163,8 +163,9 @@ gla_split_finc_kernel(const bf16* __restrict__ fk, const bf16* __restrict__ v,
   const int f0 = fb * 64, d0 = db * 64, r0 = n * kC, nvalid = min(kC, L - r0);
   const float* LG = lg + (size_t)(gph ? bh : bh / H) * L;
 
-  stage_tile<kC, 64, 128>(sK, kLD, fk + (size_t)bh * L * F, F, r0, L, f0, F, vec_f);
-  stage_tile<kC, 64, 128>(sV, kLD, v + (size_t)bh * L * D, D, r0, L, d0, D, vec_d);
+  const size_t kvr = (size_t)kv_head(bh, H, grp) * L;
+  stage_tile<kC, 64, 128>(sK, kLD, fk + kvr * F, F, r0, L, f0, F, vec_f);
+  stage_tile<kC, 64, 128>(sV, kLD, v + kvr * D, D, r0, L, d0, D, vec_d);
   cp_async_commit();
   chunk_gate_scan(LG, r0, nvalid, sG, sScan);
   cp_async_wait_all();
@@ -371,7 +372,8 @@ template <int FP, int DV>
 __global__ void __launch_bounds__(128)
 gla_split_out_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
                      const bf16* __restrict__ v, const float* __restrict__ lg, int gph, int H,
-                     int L, int F, int D, int NT, int nslices, int vec_f, int vec_d, int vec_s,
+                     int grp, int L, int F, int D, int NT, int nslices, int vec_f, int vec_d,
+                     int vec_s,
                      const bf16* __restrict__ s_in, const float* __restrict__ z_in,
                      const float* __restrict__ gs, int seeded, bf16* __restrict__ y,
                      float* __restrict__ y32, float* __restrict__ den_out,
@@ -397,8 +399,9 @@ gla_split_out_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
   const bool with_state = n > 0 || seeded;
 
   stage_tile<kC, FP, 128>(sQ, SM::LDQ, fq + rowb * F, F, r0, L, 0, F, vec_f);
-  stage_tile<kC, FP, 128>(sK, SM::LDQ, fk + rowb * F, F, r0, L, 0, F, vec_f);
-  stage_tile<kC, DV, 128>(sV, SM::LDV, v + rowb * D, D, r0, L, d0, D, vec_d);
+  const size_t kvr = (size_t)kv_head(bh, H, grp) * L;
+  stage_tile<kC, FP, 128>(sK, SM::LDQ, fk + kvr * F, F, r0, L, 0, F, vec_f);
+  stage_tile<kC, DV, 128>(sV, SM::LDV, v + kvr * D, D, r0, L, d0, D, vec_d);
   if (with_state) stage_tile<FP, DV, 128>(sS, SM::LDV, s_in + chunk * F * D, D, 0, F, d0, D, vec_s);
   cp_async_commit();
   for (int f = tid; f < FP; f += 128) sZ[f] = (with_state && f < F) ? z_in[chunk * F + f] : 0.f;
@@ -412,7 +415,7 @@ gla_split_out_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
 
 template <int FP, int DV>
 int launch_out(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, int BH,
-               int H, int L, int F, int D, int NT, const bf16* s_in, const float* z_in,
+               int H, int grp, int L, int F, int D, int NT, const bf16* s_in, const float* z_in,
                const float* gs, int seeded, bf16* y, float* y32, float* den, float* g_out,
                cudaStream_t st) {
   using SM = SplitOutSmem<FP, DV>;
@@ -424,8 +427,8 @@ int launch_out(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
   const int vec_d = (D % 8 == 0) && aligned16(v);
   const int vec_s = (D % 8 == 0) && aligned16(s_in);
   gla_split_out_kernel<FP, DV><<<(unsigned)((long long)BH * NT * nslices), 128, SM::bytes, st>>>(
-      fq, fk, v, lg, gph, H, L, F, D, NT, nslices, vec_f, vec_d, vec_s, s_in, z_in, gs, seeded,
-      y, y32, den, g_out);
+      fq, fk, v, lg, gph, H, grp, L, F, D, NT, nslices, vec_f, vec_d, vec_s, s_in, z_in, gs,
+      seeded, y, y32, den, g_out);
   count_launches(1);
   return check_launch("gla_split_out_kernel");
 }
@@ -457,14 +460,14 @@ int gla_schedule_override() { return g_schedule.load(std::memory_order_relaxed);
 int gla_set_schedule(int s) { return g_schedule.exchange(s); }
 
 int gla_fwd_split_run(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
-                      bf16* y, const GlaSaved& sv, const GlaFwdWork& fw, int B, int H, int L,
-                      int F, int D, cudaStream_t stream) {
-  const int BH = B * H, NT = (int)gla_nt(L);
+                      bf16* y, const GlaSaved& sv, const GlaFwdWork& fw, int B, int H, int Hkv,
+                      int L, int F, int D, cudaStream_t stream) {
+  const int BH = B * H, NT = (int)gla_nt(L), grp = H / Hkv;
   const int nfb = ceil_div(F, 64), ndb = ceil_div(D, 64);
   const int vec_f = (F % 8 == 0) && aligned16(fk);
   const int vec_d = (D % 8 == 0) && aligned16(v);
   gla_split_finc_kernel<<<(unsigned)((long long)BH * NT * nfb * ndb), 128, 0, stream>>>(
-      fk, v, lg, gph, H, L, F, D, NT, nfb, ndb, vec_f, vec_d, fw.inc, fw.incz, fw.lam);
+      fk, v, lg, gph, H, grp, L, F, D, NT, nfb, ndb, vec_f, vec_d, fw.inc, fw.incz, fw.lam);
   count_launches(1);
   int rc = check_launch("gla_split_finc_kernel");
   if (rc) return rc;
@@ -479,8 +482,8 @@ int gla_fwd_split_run(const bf16* fq, const bf16* fk, const bf16* v, const float
   float* y32 = save ? sv.y32 : nullptr;
 #define LZ_OUT_CASE(fp, dv)                                                                   \
   if (FP == fp && DV == dv)                                                                   \
-    return launch_out<fp, dv>(fq, fk, v, lg, gph, BH, H, L, F, D, NT, s, z, fw.gs, 0, y, y32, \
-                              sv.den, save ? sv.g : nullptr, stream);
+    return launch_out<fp, dv>(fq, fk, v, lg, gph, BH, H, grp, L, F, D, NT, s, z, fw.gs, 0, y,  \
+                              y32, sv.den, save ? sv.g : nullptr, stream);
   LZ_OUT_CASE(32, 16) LZ_OUT_CASE(32, 32) LZ_OUT_CASE(32, 64)
   LZ_OUT_CASE(64, 16) LZ_OUT_CASE(64, 32) LZ_OUT_CASE(64, 64)
   LZ_OUT_CASE(128, 16) LZ_OUT_CASE(128, 32) LZ_OUT_CASE(128, 64)
@@ -567,7 +570,7 @@ int gla_seg_fwd_begin(const bf16* fk, const bf16* v, const float* lg, int gph, f
   const int vec_f = (F % 8 == 0) && aligned16(fk);
   const int vec_d = (D % 8 == 0) && aligned16(v);
   gla_split_finc_kernel<<<(unsigned)((long long)BH * NT * nfb * ndb), 128, 0, stream>>>(
-      fk, v, lg, gph, H, L, F, D, NT, nfb, ndb, vec_f, vec_d, fw.inc, fw.incz, fw.lam);
+      fk, v, lg, gph, H, 1, L, F, D, NT, nfb, ndb, vec_f, vec_d, fw.inc, fw.incz, fw.lam);
   count_launches(1);
   int rc = check_launch("gla_split_finc_kernel");
   if (rc) return rc;
@@ -593,8 +596,8 @@ int gla_seg_fwd_end(const bf16* fq, const bf16* fk, const bf16* v, const float* 
   const int seeded = seed != nullptr;
 #define LZ_OUT_CASE(fp, dv)                                                                   \
   if (FP == fp && DV == dv)                                                                   \
-    return launch_out<fp, dv>(fq, fk, v, lg, gph, BH, H, L, F, D, NT, s, z, fw.gs, seeded, y, \
-                              y32, sv.den, save ? sv.g : nullptr, stream);
+    return launch_out<fp, dv>(fq, fk, v, lg, gph, BH, H, 1, L, F, D, NT, s, z, fw.gs, seeded, \
+                              y, y32, sv.den, save ? sv.g : nullptr, stream);
   LZ_OUT_CASE(32, 16) LZ_OUT_CASE(32, 32) LZ_OUT_CASE(32, 64)
   LZ_OUT_CASE(64, 16) LZ_OUT_CASE(64, 32) LZ_OUT_CASE(64, 64)
   LZ_OUT_CASE(128, 16) LZ_OUT_CASE(128, 32) LZ_OUT_CASE(128, 64)
@@ -632,8 +635,8 @@ int gla_seg_bwd_end(const bf16* fq, const bf16* fk, const bf16* v, int gph, cons
                        dseed ? dseed + nS : nullptr, wk.ds, wk.dz, nullptr, nullptr, nullptr,
                        nullptr, stream);
   if (rc) return rc;
-  return gla_bwd_tail(fq, fk, v, gph, sv, dy, dfq, dfk, dv, gdt, dlg, wk, B, H, L, F, D, s_seeded,
-                      dseed != nullptr, stream);
+  return gla_bwd_tail(fq, fk, v, gph, sv, dy, dfq, dfk, dv, gdt, gdt, dlg, wk, B, H, H, L, F, D,
+                      s_seeded, dseed != nullptr, stream);
 }
 
 int gla_seg_combine(const float* summaries, int P, int rank, int reverse, float* seed, int BH,

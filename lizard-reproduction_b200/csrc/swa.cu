@@ -14,6 +14,11 @@
 //   dkv kernel : per key block, dk and dv over the query blocks in its window.
 //   dmeta      : dmeta_j = -sum_i exp(meta_j - lse_i) delta_i (swa.py:175-176),
 //                reduced over the per-block partials in a fixed order.
+// Grouped keys and values (GQA): k and v may carry Hkv heads with H % Hkv == 0;
+// query head h reads key/value head h / (H / Hkv), which is what the
+// reference's caller builds with repeat_interleave (src/lizard_attention.py:
+// 73-76). The dk / dv of a key/value head sum over its group of query heads
+// inside one CTA, in a fixed order (the autograd of repeat_interleave).
 // Optional bf16 residuals q_lo, k_lo (q = q_hi + q_lo) make the logits
 // q_hi.k_hi + q_hi.k_lo + q_lo.k_hi, about 16 mantissa bits, for callers whose
 // queries and keys are fp32: softmax turns logit rounding into relative
@@ -45,6 +50,11 @@ int ensure_smem_swa(Kern k, size_t bytes, bool* done) {
     done[dev] = true;
   }
   return LZ_OK;
+}
+
+// Element offset of the key/value head that query row block bh reads.
+__device__ __forceinline__ size_t kv_base(int bh, int H, int grp, int L, int D) {
+  return (size_t)kv_head(bh, H, grp) * L * D;
 }
 
 __device__ __forceinline__ bool in_window(int i, int t, int L, int W) {
@@ -104,8 +114,9 @@ template <int DP, bool SPLIT>
 __global__ void __launch_bounds__(128)
 swa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
                const bf16* __restrict__ ql, const bf16* __restrict__ kl,
-               const float* __restrict__ meta, int n_meta, int W, float scale_log2, int L, int D,
-               int nqb, int vec, bf16* __restrict__ y, float* __restrict__ lse,
+               const float* __restrict__ meta, int n_meta, int W, float scale_log2, int H,
+               int grp, int L, int D, int nqb, int vec, bf16* __restrict__ y,
+               float* __restrict__ lse,
                float* __restrict__ y32) {
   using SM = FwdSmem<DP, SPLIT>;
   constexpr int LD = Tile<DP>::LD, NTD = DP / 8;
@@ -120,7 +131,7 @@ swa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   const int gq = lane >> 2, cq = lane & 3;
   const int qb = blockIdx.x % nqb, bh = blockIdx.x / nqb;
   const int q0 = qb * kB;
-  const size_t base = (size_t)bh * L * D;
+  const size_t base = (size_t)bh * L * D, kvb = kv_base(bh, H, grp, L, D);
 
   // sinks seed the running max / sum (log2 domain)
   float ms = -1e30f;
@@ -131,9 +142,9 @@ swa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   const int lo = max(q0 - W + 1, 0) / kB * kB;
   const int hi = min(q0 + kB, L);
   auto issue = [&](int kb, int s) {
-    stage_tile<kB, DP, 128>(sK(s), LD, k + base, D, kb, L, 0, D, vec);
-    if (SPLIT) stage_tile<kB, DP, 128>(sKl(s), LD, kl + base, D, kb, L, 0, D, vec);
-    stage_tile<kB, DP, 128>(sV(s), LD, v + base, D, kb, L, 0, D, vec);
+    stage_tile<kB, DP, 128>(sK(s), LD, k + kvb, D, kb, L, 0, D, vec);
+    if (SPLIT) stage_tile<kB, DP, 128>(sKl(s), LD, kl + kvb, D, kb, L, 0, D, vec);
+    stage_tile<kB, DP, 128>(sV(s), LD, v + kvb, D, kb, L, 0, D, vec);
   };
   stage_tile<kB, DP, 128>(sQ, LD, q + base, D, q0, L, 0, D, vec);
   if (SPLIT) stage_tile<kB, DP, 128>(sQl, LD, ql + base, D, q0, L, 0, D, vec);
@@ -311,7 +322,8 @@ swa_bwd_dq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
                   const bf16* __restrict__ v, const bf16* __restrict__ ql,
                   const bf16* __restrict__ kl, const bf16* __restrict__ dy,
                   const float* __restrict__ lse, const float* __restrict__ delta, int W,
-                  float scale, int L, int D, int nqb, int vec, void* __restrict__ dq, int gdt) {
+                  float scale, int H, int grp, int L, int D, int nqb, int vec,
+                  void* __restrict__ dq, int gdt) {
   using SM = DqSmem<DP, SPLIT>;
   constexpr int LD = Tile<DP>::LD, NTD = DP / 8;
   constexpr size_t T = Tile<DP>::bytes;
@@ -326,13 +338,13 @@ swa_bwd_dq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
   const int gq = lane >> 2, cq = lane & 3;
   const int qb = blockIdx.x % nqb, bh = blockIdx.x / nqb;
   const int q0 = qb * kB;
-  const size_t base = (size_t)bh * L * D;
+  const size_t base = (size_t)bh * L * D, kvb = kv_base(bh, H, grp, L, D);
   const int lo = max(q0 - W + 1, 0) / kB * kB;
   const int hi = min(q0 + kB, L);
   auto issue = [&](int kb, int s) {
-    stage_tile<kB, DP, 128>(sK(s), LD, k + base, D, kb, L, 0, D, vec);
-    if (SPLIT) stage_tile<kB, DP, 128>(sKl(s), LD, kl + base, D, kb, L, 0, D, vec);
-    stage_tile<kB, DP, 128>(sV(s), LD, v + base, D, kb, L, 0, D, vec);
+    stage_tile<kB, DP, 128>(sK(s), LD, k + kvb, D, kb, L, 0, D, vec);
+    if (SPLIT) stage_tile<kB, DP, 128>(sKl(s), LD, kl + kvb, D, kb, L, 0, D, vec);
+    stage_tile<kB, DP, 128>(sV(s), LD, v + kvb, D, kb, L, 0, D, vec);
   };
   stage_tile<kB, DP, 128>(sQ, LD, q + base, D, q0, L, 0, D, vec);
   if (SPLIT) stage_tile<kB, DP, 128>(sQl, LD, ql + base, D, q0, L, 0, D, vec);
@@ -452,6 +464,10 @@ swa_dmeta_kernel(const float* __restrict__ partial, int nblocks, int n_meta,
 
 // ------------------------------------------------------- backward: dk, dv
 // Works on transposed scores s^T = k q^T so every operand stays row-major.
+// One CTA per (key block, key/value head): it walks the query blocks of every
+// query head in the head's group, one double-buffered loop over
+// (group head, query block), so dk and dv are summed over the group in
+// registers.
 template <int DP, bool SPLIT>
 struct DkvSmem {
   static constexpr size_t T = Tile<DP>::bytes;
@@ -466,8 +482,8 @@ swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
                    const bf16* __restrict__ v, const bf16* __restrict__ ql,
                    const bf16* __restrict__ kl, const bf16* __restrict__ dy,
                    const float* __restrict__ lse, const float* __restrict__ delta, int W,
-                   float scale, int L, int D, int nkb, int vec, void* __restrict__ dk,
-                   void* __restrict__ dv, int gdt) {
+                   float scale, int H, int grp, int L, int D, int nkb, int vec,
+                   void* __restrict__ dk, void* __restrict__ dv, int gdt) {
   using SM = DkvSmem<DP, SPLIT>;
   constexpr int LD = Tile<DP>::LD, NTD = DP / 8;
   constexpr size_t T = Tile<DP>::bytes;
@@ -481,12 +497,18 @@ swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
   float* sRow = reinterpret_cast<float*>(smem + SM::rows);  // 2 stages x (lse, delta)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, cq = lane & 3;
-  const int kbk = blockIdx.x % nkb, bh = blockIdx.x / nkb;
+  const int kbk = blockIdx.x % nkb, bkv = blockIdx.x / nkb;  // bkv = b * Hkv + kv head
+  const int Hkv = H / grp, b = bkv / Hkv;
+  const int bh0 = b * H + (bkv - b * Hkv) * grp;  // first query head of the group
   const int k0 = kbk * kB;
-  const size_t base = (size_t)bh * L * D;
+  const size_t kvb = (size_t)bkv * L * D;
   const int qlo = k0;  // query blocks start at the key block (causal)
   const int qhi = min(k0 + kB + W - 1, L);
-  auto issue = [&](int qb, int st) {
+  const int nq = (qhi - qlo + kB - 1) / kB;  // query blocks per head, >= 1
+  const int nit = grp * nq;
+  auto issue = [&](int it, int st) {
+    const int bh = bh0 + it / nq, qb = qlo + (it % nq) * kB;
+    const size_t base = (size_t)bh * L * D;
     stage_tile<kB, DP, 128>(sQ(st), LD, q + base, D, qb, L, 0, D, vec);
     if (SPLIT) stage_tile<kB, DP, 128>(sQl(st), LD, ql + base, D, qb, L, 0, D, vec);
     stage_tile<kB, DP, 128>(sDy(st), LD, dy + base, D, qb, L, 0, D, vec);
@@ -497,10 +519,10 @@ swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
       sRow[st * 2 * kB + kB + tid] = r < L ? delta[(size_t)bh * L + r] : 0.f;
     }
   };
-  stage_tile<kB, DP, 128>(sK, LD, k + base, D, k0, L, 0, D, vec);
-  if (SPLIT) stage_tile<kB, DP, 128>(sKl, LD, kl + base, D, k0, L, 0, D, vec);
-  stage_tile<kB, DP, 128>(sV, LD, v + base, D, k0, L, 0, D, vec);
-  issue(qlo, 0);
+  stage_tile<kB, DP, 128>(sK, LD, k + kvb, D, k0, L, 0, D, vec);
+  if (SPLIT) stage_tile<kB, DP, 128>(sKl, LD, kl + kvb, D, k0, L, 0, D, vec);
+  stage_tile<kB, DP, 128>(sV, LD, v + kvb, D, k0, L, 0, D, vec);
+  issue(0, 0);
   const int t0 = k0 + 16 * warp + gq, t1 = t0 + 8;  // this thread's key rows
   float dka[NTD][4], dva[NTD][4];
 #pragma unroll
@@ -509,15 +531,16 @@ swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
     for (int e = 0; e < 4; ++e) dka[c][e] = dva[c][e] = 0.f;
   uint32_t ka[DP / 16][4], kla[DP / 16][4], va[DP / 16][4];
   int stage = 0;
-  for (int qb = qlo; qb < qhi; qb += kB, stage ^= 1) {
-    if (qb + kB < qhi) {
-      issue(qb + kB, stage ^ 1);
+  for (int it = 0; it < nit; ++it, stage ^= 1) {
+    const int qb = qlo + (it % nq) * kB;
+    if (it + 1 < nit) {
+      issue(it + 1, stage ^ 1);
       asm volatile("cp.async.wait_group 1;\n" ::);
     } else {
       cp_async_wait_all();
     }
     __syncthreads();
-    if (qb == qlo) {
+    if (it == 0) {
 #pragma unroll
       for (int kk = 0; kk < DP / 16; ++kk) {
         lda_rm(ka[kk], sK, LD, 16 * warp, 16 * kk);
@@ -582,22 +605,22 @@ swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
     const int d = 8 * nt + 2 * cq;
     if (t0 < L) {
       if (d < D) {
-        store_grad(dk, base + (size_t)t0 * D + d, dka[nt][0] * scale, gdt);
-        store_grad(dv, base + (size_t)t0 * D + d, dva[nt][0], gdt);
+        store_grad(dk, kvb + (size_t)t0 * D + d, dka[nt][0] * scale, gdt);
+        store_grad(dv, kvb + (size_t)t0 * D + d, dva[nt][0], gdt);
       }
       if (d + 1 < D) {
-        store_grad(dk, base + (size_t)t0 * D + d + 1, dka[nt][1] * scale, gdt);
-        store_grad(dv, base + (size_t)t0 * D + d + 1, dva[nt][1], gdt);
+        store_grad(dk, kvb + (size_t)t0 * D + d + 1, dka[nt][1] * scale, gdt);
+        store_grad(dv, kvb + (size_t)t0 * D + d + 1, dva[nt][1], gdt);
       }
     }
     if (t1 < L) {
       if (d < D) {
-        store_grad(dk, base + (size_t)t1 * D + d, dka[nt][2] * scale, gdt);
-        store_grad(dv, base + (size_t)t1 * D + d, dva[nt][2], gdt);
+        store_grad(dk, kvb + (size_t)t1 * D + d, dka[nt][2] * scale, gdt);
+        store_grad(dv, kvb + (size_t)t1 * D + d, dva[nt][2], gdt);
       }
       if (d + 1 < D) {
-        store_grad(dk, base + (size_t)t1 * D + d + 1, dka[nt][3] * scale, gdt);
-        store_grad(dv, base + (size_t)t1 * D + d + 1, dva[nt][3], gdt);
+        store_grad(dk, kvb + (size_t)t1 * D + d + 1, dka[nt][3] * scale, gdt);
+        store_grad(dv, kvb + (size_t)t1 * D + d + 1, dva[nt][3], gdt);
       }
     }
   }
@@ -605,8 +628,8 @@ swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
 
 template <int DP, bool SPLIT>
 int launch_swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
-                   const float* meta, int n_meta, int W, int BH, int L, int D, int vec, bf16* y,
-                   const SwaSaved& sv, cudaStream_t st) {
+                   const float* meta, int n_meta, int W, int BH, int H, int grp, int L, int D,
+                   int vec, bf16* y, const SwaSaved& sv, cudaStream_t st) {
   using SM = FwdSmem<DP, SPLIT>;
   static bool done[64] = {false};
   int rc = ensure_smem_swa(swa_fwd_kernel<DP, SPLIT>, SM::bytes, done);
@@ -614,7 +637,7 @@ int launch_swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, 
   const int nqb = ceil_div(L, kB);
   const float scale_log2 = kLog2e / sqrtf((float)D);
   swa_fwd_kernel<DP, SPLIT><<<(unsigned)((long long)BH * nqb), 128, SM::bytes, st>>>(
-      q, k, v, ql, kl, meta, n_meta, W, scale_log2, L, D, nqb, vec, y, sv.lse, sv.y32);
+      q, k, v, ql, kl, meta, n_meta, W, scale_log2, H, grp, L, D, nqb, vec, y, sv.lse, sv.y32);
   count_launches(1);
   return check_launch("swa_fwd_kernel");
 }
@@ -622,8 +645,8 @@ int launch_swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, 
 template <int DP, bool SPLIT>
 int launch_swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
                    const bf16* dy, const float* meta, int n_meta, const SwaSaved& sv,
-                   const SwaWork& wk, int W, int BH, int L, int D, int vec, void* dq, void* dk,
-                   void* dv, int gdt, cudaStream_t st) {
+                   const SwaWork& wk, int W, int BH, int H, int grp, int L, int D, int vec,
+                   void* dq, void* dk, void* dv, int gdt, cudaStream_t st) {
   const float* lse = sv.lse;
   using SQ = DqSmem<DP, SPLIT>;
   using SKV = DkvSmem<DP, SPLIT>;
@@ -641,12 +664,12 @@ int launch_swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, 
   rc = check_launch("swa_bwd_delta_kernel");
   if (rc) return rc;
   swa_bwd_dq_kernel<DP, SPLIT><<<(unsigned)((long long)BH * nb), 128, SQ::bytes, st>>>(
-      q, k, v, ql, kl, dy, lse, wk.delta, W, scale, L, D, nb, vec, dq, gdt);
+      q, k, v, ql, kl, dy, lse, wk.delta, W, scale, H, grp, L, D, nb, vec, dq, gdt);
   count_launches(1);
   rc = check_launch("swa_bwd_dq_kernel");
   if (rc) return rc;
-  swa_bwd_dkv_kernel<DP, SPLIT><<<(unsigned)((long long)BH * nb), 128, SKV::bytes, st>>>(
-      q, k, v, ql, kl, dy, lse, wk.delta, W, scale, L, D, nb, vec, dk, dv, gdt);
+  swa_bwd_dkv_kernel<DP, SPLIT><<<(unsigned)((long long)(BH / grp) * nb), 128, SKV::bytes, st>>>(
+      q, k, v, ql, kl, dy, lse, wk.delta, W, scale, H, grp, L, D, nb, vec, dk, dv, gdt);
   count_launches(1);
   return check_launch("swa_bwd_dkv_kernel");
 }
@@ -655,16 +678,16 @@ int launch_swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, 
 
 int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
             const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B, int H,
-            int L, int D, cudaStream_t st) {
-  const int BH = B * H;
+            int Hkv, int L, int D, cudaStream_t st) {
+  const int BH = B * H, grp = H / Hkv;
   const bool split = ql != nullptr;
   int vec = (D % 8 == 0) && aligned16(q) && aligned16(k) && aligned16(v);
   if (split) vec = vec && aligned16(ql) && aligned16(kl);
 #define LZ_SWA_FWD(dp)                                                                       \
-  return split ? launch_swa_fwd<dp, true>(q, k, v, ql, kl, meta, n_meta, W, BH, L, D, vec, y, \
-                                          sv, st)                                            \
-               : launch_swa_fwd<dp, false>(q, k, v, ql, kl, meta, n_meta, W, BH, L, D, vec, y, \
-                                           sv, st);
+  return split ? launch_swa_fwd<dp, true>(q, k, v, ql, kl, meta, n_meta, W, BH, H, grp, L, D,  \
+                                          vec, y, sv, st)                                    \
+               : launch_swa_fwd<dp, false>(q, k, v, ql, kl, meta, n_meta, W, BH, H, grp, L, D, \
+                                           vec, y, sv, st);
   if (D <= 32) { LZ_SWA_FWD(32) }
   if (D <= 64) { LZ_SWA_FWD(64) }
   if (D <= 128) { LZ_SWA_FWD(128) }
@@ -675,18 +698,18 @@ int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const b
 
 int swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
             const float* meta, int n_meta, int W, const SwaSaved& sv, const bf16* dy, void* dq,
-            void* dk, void* dv, int gdt, float* dmeta, const SwaWork& wk, int B, int H, int L,
-            int D, cudaStream_t st) {
-  const int BH = B * H;
+            void* dk, void* dv, int gdt, float* dmeta, const SwaWork& wk, int B, int H, int Hkv,
+            int L, int D, cudaStream_t st) {
+  const int BH = B * H, grp = H / Hkv;
   const bool split = ql != nullptr;
   int vec = (D % 8 == 0) && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(dy);
   if (split) vec = vec && aligned16(ql) && aligned16(kl);
   int rc;
 #define LZ_SWA_BWD(dp)                                                                         \
-  rc = split ? launch_swa_bwd<dp, true>(q, k, v, ql, kl, dy, meta, n_meta, sv, wk, W, BH, L, D,  \
-                                        vec, dq, dk, dv, gdt, st)                              \
-             : launch_swa_bwd<dp, false>(q, k, v, ql, kl, dy, meta, n_meta, sv, wk, W, BH, L,  \
-                                         D, vec, dq, dk, dv, gdt, st);
+  rc = split ? launch_swa_bwd<dp, true>(q, k, v, ql, kl, dy, meta, n_meta, sv, wk, W, BH, H, grp, \
+                                        L, D, vec, dq, dk, dv, gdt, st)                        \
+             : launch_swa_bwd<dp, false>(q, k, v, ql, kl, dy, meta, n_meta, sv, wk, W, BH, H,  \
+                                         grp, L, D, vec, dq, dk, dv, gdt, st);
   if (D <= 32) {
     LZ_SWA_BWD(32)
   } else if (D <= 64) {

@@ -1,5 +1,6 @@
 // Layout of the SWA saved buffer (log-sum-exp and fp32 output per row) and of
-// the backward workspace.
+// the backward workspace. Both are per query row (B * H * L rows) also when the
+// keys and values carry fewer heads (Hkv, GQA).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -48,11 +49,11 @@ inline size_t swa_work_layout(int B, int H, int L, int n_meta, unsigned char* ba
 
 int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
             const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B, int H,
-            int L, int D, cudaStream_t st);
+            int Hkv, int L, int D, cudaStream_t st);
 
 int swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
             const float* meta, int n_meta, int W, const SwaSaved& sv, const bf16* dy, void* dq,
-            void* dk, void* dv, int gdt, float* dmeta, const SwaWork& wk, int B, int H, int L,
-            int D, cudaStream_t st);
+            void* dk, void* dv, int gdt, float* dmeta, const SwaWork& wk, int B, int H, int Hkv,
+            int L, int D, cudaStream_t st);
 
 }  // namespace lz

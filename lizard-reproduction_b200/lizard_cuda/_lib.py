@@ -10,7 +10,7 @@ from pathlib import Path
 
 import torch
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 LIB_PATH = Path(__file__).resolve().with_name("liblizard_cuda.so")
 HEADER = Path(__file__).resolve().parents[2] / "include" / "lizard_cuda.h"
 
@@ -31,6 +31,11 @@ _SIGNATURES = {
                    + [_c_int] * 6 + [_vp]),
     "lz_gla_bwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _c_size, _vp, _vp, _vp, _vp, _c_int,
                             _vp, _vp, _c_size] + [_c_int] * 6 + [_vp]),
+    "lz_gla_bwd_gqa_workspace_bytes": (_c_size, [_c_int] * 7),
+    "lz_gla_fwd_gqa": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_size, _vp, _c_size]
+                       + [_c_int] * 7 + [_vp]),
+    "lz_gla_bwd_gqa": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _c_size, _vp, _vp, _vp, _vp,
+                                _c_int, _vp, _vp, _c_size] + [_c_int] * 7 + [_vp]),
     "lz_gla_seg_workspace_bytes": (_c_size, [_c_int] * 5),
     "lz_gla_seg_summary_floats": (_c_size, [_c_int] * 4),
     "lz_gla_seg_fwd_begin": (_c_int, [_vp, _vp, _vp, _c_int, _vp, _vp, _c_size] + [_c_int] * 5
@@ -47,12 +52,21 @@ _SIGNATURES = {
     "lz_hedgehog_bwd": (_c_int, [_vp, _c_int, _vp, _vp, _c_int, _vp, _vp, _vp, _c_size, _c_int,
                                  _c_int, _c_int, _vp]),
     "lz_hedgehog_bwd_workspace_bytes": (_c_size, [_c_int] * 3),
+    "lz_rope_split": (_c_int, [_vp, _c_int, ctypes.c_longlong, ctypes.c_longlong,
+                               ctypes.c_longlong, _vp, _vp, _c_int, ctypes.c_longlong,
+                               ctypes.c_longlong, _vp, _vp] + [_c_int] * 4 + [_vp]),
+    "lz_rope_bwd": (_c_int, [_vp, _vp, _vp, _c_int, ctypes.c_longlong, ctypes.c_longlong, _vp,
+                             _c_int] + [_c_int] * 4 + [_vp]),
     "lz_swa_saved_bytes": (_c_size, [_c_int] * 4),
     "lz_swa_bwd_workspace_bytes": (_c_size, [_c_int] * 5),
     "lz_swa_fwd": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp, _vp, _c_size] + [_c_int] * 4
                    + [_vp]),
     "lz_swa_bwd": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp, _c_size, _vp, _vp, _vp, _vp,
                                         _c_int, _vp, _vp, _c_size] + [_c_int] * 4 + [_vp]),
+    "lz_swa_fwd_gqa": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp, _vp, _c_size] + [_c_int] * 5
+                       + [_vp]),
+    "lz_swa_bwd_gqa": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp, _c_size, _vp, _vp, _vp, _vp,
+                                            _c_int, _vp, _vp, _c_size] + [_c_int] * 5 + [_vp]),
     "lz_swa_bwd_noalloc": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp, _c_size, _vp, _vp, _vp,
                                                 _vp, _c_int, _vp] + [_c_int] * 4 + [_vp]),
 }

@@ -6,8 +6,15 @@ constructor arguments, parameter names and forward contract
 attention branches running on this package's gla / swa kernels exactly where
 the reference's `triton` backend calls kernels.gla / kernels.swa
 (src/lizard_attention.py:90-93), and the Hedgehog feature map on the fused
-kernel (lizard_cuda.hedgehog, bf16 features straight into gla). The
-projections, gate and RoPE are the same torch operations as the reference.
+kernel (lizard_cuda.hedgehog, bf16 features straight into gla).
+
+Keys and values stay at their Hkv heads: the reference repeat_interleaves k
+and v to H heads (src/lizard_attention.py:73-76) before the feature map and
+both branches, which gives every query head of a group the same fk and v; the
+grouped-query kernels read each key/value head once instead, and the feature
+map runs on Hkv heads of k. RoPE is fused into the SWA operand pass
+(lizard_cuda.swa_rope) and reads the projections in place. The projections and
+the gate are the same torch operations as the reference.
 """
 import torch
 import torch.nn as nn
@@ -15,20 +22,9 @@ import torch.nn.functional as F
 
 from .gla import gla
 from .hedgehog import hedgehog as fused_hedgehog
-from .swa import swa
+from .rope import swa_rope
 
 BACKENDS = ("cuda",)
-
-
-def _rotate_half(x):
-    half = x.shape[-1] // 2
-    return torch.cat([-x[..., half:], x[..., :half]], dim=-1)
-
-
-def apply_rotary(q, k, cos, sin):
-    """Llama rotate-half RoPE with cos/sin [B, L, Dh] broadcast over heads."""
-    cos, sin = cos[:, None], sin[:, None]
-    return q * cos + _rotate_half(q) * sin, k * cos + _rotate_half(k) * sin
 
 
 class LizardAttention(nn.Module):
@@ -60,24 +56,29 @@ class LizardAttention(nn.Module):
         nn.init.zeros_(self.W_gamma.weight)
 
     def split(self, x, heads):
+        """The reference's head split with repeat_interleave to H heads
+        (src/lizard_attention.py:73-76); kept for callers of the method. The
+        forward uses heads_view instead."""
+        return self.heads_view(x, heads).repeat_interleave(self.heads // heads, dim=1)
+
+    def heads_view(self, x, heads):
+        """[B, L, heads * Dh] -> [B, heads, L, Dh] as a view (no copy)."""
         b, n, _ = x.shape
-        x = x.view(b, n, heads, self.head_dim).transpose(1, 2)
-        return x.repeat_interleave(self.heads // heads, dim=1)
+        return x.view(b, n, heads, self.head_dim).transpose(1, 2)
 
     def forward(self, hidden_states, position_embeddings, **kwargs):
         x = hidden_states
         dtype = torch.promote_types(x.dtype, torch.float32)
-        q = self.split(self.q_proj(x), self.heads).to(dtype)
-        k = self.split(self.k_proj(x), self.kv_heads).to(dtype)
-        v = self.split(self.v_proj(x), self.kv_heads).to(dtype)
+        q = self.heads_view(self.q_proj(x), self.heads).to(dtype)
+        k = self.heads_view(self.k_proj(x), self.kv_heads).to(dtype)
+        v = self.heads_view(self.v_proj(x), self.kv_heads).to(dtype)
         z = self.W_gamma(x).to(dtype).squeeze(-1)
         fq = fused_hedgehog(q, self.phi_q.weight.to(dtype))
-        fk = fused_hedgehog(k, self.phi_k.weight.to(dtype))
-        cos, sin = (t.to(dtype) for t in position_embeddings)
-        qr, kr = apply_rotary(q, k, cos, sin)
+        fk = fused_hedgehog(k, self.phi_k.weight.to(dtype))  # Hkv heads
+        cos, sin = position_embeddings
         alpha, meta = self.alpha_blend.to(dtype), self.meta_tokens.to(dtype)
         y = gla(fq, fk, v, F.logsigmoid(z)).to(dtype)
-        y = y + alpha * swa(qr, kr, v, meta, self.window).to(dtype)
+        y = y + alpha * swa_rope(q, k, v, cos, sin, meta, self.window).to(dtype)
         return self.o_proj(y.to(x.dtype).transpose(1, 2).flatten(2)), None
 
 

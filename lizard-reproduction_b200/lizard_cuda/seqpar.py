@@ -174,7 +174,10 @@ def gla_seqpar(fq, fk, v, log_gamma, group=None, comm=None, ops=None):
     with rank, size and all_gather) and `ops` (the segment phases) default to
     torch.distributed and the CUDA library.
     """
-    B, H, L, F, D, per_head = _shapes(fq, fk, v, log_gamma)
+    B, H, Hkv, L, F, D, per_head = _shapes(fq, fk, v, log_gamma)
+    if Hkv != H:
+        raise ValueError("gla_seqpar takes fk and v with the query head count; "
+                         "repeat_interleave grouped keys / values first")
     if comm is None:
         comm = DistExchange(group)
     if ops is None:

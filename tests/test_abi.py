@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 def test_abi_version(lib):
     from lizard_cuda import _lib
-    assert lib.lz_abi_version() == _lib.ABI_VERSION == 2
+    assert lib.lz_abi_version() == _lib.ABI_VERSION == 3
 
 
 def test_buffer_size_queries(lib):
@@ -53,6 +53,38 @@ def test_buffer_size_queries(lib):
 def _fake(n=1):
     # never dereferenced: validation rejects the calls first
     return [ctypes.c_void_p(0x1000 * (i + 1)) for i in range(n)]
+
+
+def test_gqa_entries_validate_head_counts(lib):
+    p = _fake(6)
+    # H = 6 query heads over Hkv = 4 key/value heads does not divide
+    rc = lib.lz_swa_fwd_gqa(*p[:3], None, None, None, 0, 16, p[3], None, 0, 1, 6, 4, 64, 64,
+                            None)
+    assert rc == 1 and b"divide" in lib.lz_last_error_string()
+    rc = lib.lz_gla_fwd_gqa(*p[:4], 0, p[4], None, 0, None, 0, 1, 6, 4, 64, 64, 64, 64, None)
+    assert rc == 1 and b"divide" in lib.lz_last_error_string()
+    rc = lib.lz_gla_bwd_gqa(*p[:4], 0, p[4], 1 << 30, p[5], *_fake(3), 0, p[0], p[1], 1 << 30,
+                            1, 6, 0, 64, 64, 64, 64, None)
+    assert rc == 1 and b"divide" in lib.lz_last_error_string()
+    # the grouped backward needs room for the per-head dfk / dv before the group sums
+    plain = lib.lz_gla_bwd_workspace_bytes(2, 8, 256, 64, 64, 64)
+    assert lib.lz_gla_bwd_gqa_workspace_bytes(2, 8, 8, 256, 64, 64, 64) == plain
+    assert (lib.lz_gla_bwd_gqa_workspace_bytes(2, 8, 2, 256, 64, 64, 64)
+            >= plain + 2 * 8 * 256 * (64 + 64) * 4)
+    assert lib.lz_gla_bwd_gqa_workspace_bytes(2, 8, 3, 256, 64, 64, 64) == 0
+
+
+def test_rope_entries_validate(lib):
+    p = _fake(4)
+    # odd head dim cannot be rotated in halves
+    rc = lib.lz_rope_split(p[0], 0, 0, 0, 0, p[1], p[2], 0, 0, 0, p[3], None, 1, 1, 8, 63, None)
+    assert rc == 1 and b"even" in lib.lz_last_error_string()
+    rc = lib.lz_rope_split(p[0], 7, 0, 0, 0, p[1], p[2], 0, 0, 0, p[3], None, 1, 1, 8, 64, None)
+    assert rc == 1 and b"dtype" in lib.lz_last_error_string()
+    rc = lib.lz_rope_bwd(p[0], p[1], p[2], 5, 0, 0, p[3], 0, 1, 1, 8, 64, None)
+    assert rc == 1 and b"cos" in lib.lz_last_error_string()
+    rc = lib.lz_rope_bwd(None, p[1], p[2], 0, 0, 0, p[3], 0, 1, 1, 8, 64, None)
+    assert rc == 1
 
 
 def test_gla_fwd_rejects_null_pointers(lib):
