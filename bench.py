@@ -50,6 +50,8 @@ CASES = {
     # feature map of one projection: x [B, H, L, 64] fp32, feature dim 128
     "prologue-fwd": (4, 32, 4096, 64, False, False, "hedgehog"),
     "prologue-train": (4, 32, 4096, 64, False, True, "hedgehog"),
+    # config 5: whole-model prefill (B, L only; the architecture is LLAMA_1B)
+    "cfg5-prefill": (32, 32, 4096, 64, False, False, "model"),
 }
 
 
@@ -370,6 +372,59 @@ def prologue_measure(torch, lizard_cuda, device, steps=20, warmup=3):
     return out
 
 
+# Lizard-Llama-3.2-1B shape (config 5): the public Llama 3.2 1B architecture numbers.
+LLAMA_1B = dict(hidden_size=2048, intermediate_size=8192, num_hidden_layers=16,
+                num_attention_heads=32, num_key_value_heads=8, vocab_size=128256,
+                rope_theta=500000.0, max_position_embeddings=131072, tie_word_embeddings=True,
+                rms_norm_eps=1e-5,
+                rope_scaling={"rope_type": "llama3", "factor": 32.0, "low_freq_factor": 1.0,
+                              "high_freq_factor": 4.0, "original_max_position_embeddings": 8192})
+
+
+def model_prefill_measure(torch, lizard_cuda, device, Bm=32, Lm=4096, steps=3, warmup=3):
+    """Config 5: forward prefill of a random-init bf16 Lizard-Llama-3.2-1B
+    (every attention layer swapped by lizard_cuda.model.to_lizard, window 64, 4 sinks,
+    feature dim 128 -> F = 256, GQA 32/8 heads) on uniform random token ids, full logits.
+    Device ms per step by CUDA events, tokens/s, and the same for one Lizard attention
+    layer alone at the model's shape (its share of the step)."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from lizard_cuda.model import to_lizard
+    cfg = LlamaConfig(**LLAMA_1B)
+    torch.manual_seed(0)
+    with torch.device(device):
+        model = LlamaForCausalLM(cfg).to(torch.bfloat16)
+    to_lizard(model, window=64, num_meta=4, feature_dim=128).eval()
+    g = torch.Generator(device=device).manual_seed(3)
+    ids = torch.randint(0, cfg.vocab_size, (Bm, Lm), generator=g, device=device)
+
+    def timed(fn, n, w):
+        for _ in range(w):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / n
+
+    out = {"workload": f"Lizard-Llama-3.2-1B prefill, random-init bf16, B={Bm} L={Lm}, "
+                       "uniform random ids, full logits, window 64, 4 sinks, F=256, GQA 32/8"}
+    with torch.no_grad():
+        out["ms_per_step"] = timed(lambda: model(ids, use_cache=False).logits, steps, warmup)
+        out["tokens_per_s"] = Bm * Lm / (out["ms_per_step"] / 1e3)
+        x = torch.randn(Bm, Lm, cfg.hidden_size, generator=g, device=device).bfloat16()
+        pos = torch.arange(Lm, device=device)[None].expand(Bm, Lm)
+        rope = model.model.rotary_emb(x, pos)
+        attn = model.model.layers[0].self_attn
+        out["attention_layer_ms"] = timed(lambda: attn(x, rope), steps, warmup)
+    out["attention_share"] = cfg.num_hidden_layers * out["attention_layer_ms"] / out["ms_per_step"]
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
 def secondary(torch, lizard_cuda, device, steps=50, warmup=5):
     """Config 3 (B=1, L=2048, H=32, F=D=64): GLA fwd+bwd with a per-token gate
     and SWA fwd+bwd (window 64, 4 sinks); device ms per step.
@@ -547,6 +602,7 @@ def run_ours(args, torch):
             if world == 1:
                 side["cfg4_length_sweep"] = length_sweep(torch, lizard_cuda, device)
                 side["prologue_hedgehog"] = prologue_measure(torch, lizard_cuda, device)
+                side["cfg5_model_prefill"] = model_prefill_measure(torch, lizard_cuda, device)
 
     cpu = None
     if rank == 0 and world == 1:
@@ -606,6 +662,11 @@ def run_case(args, torch):
     Bc, Hc, Lc, FDc, per_head, train, op = CASES[name]
     Bc, Lc = args.B or Bc, args.L or Lc
     dev = torch.device("cuda", 0)
+    if op == "model":
+        res = model_prefill_measure(torch, lizard_cuda, dev, Bc, Lc, max(1, args.steps),
+                                    args.warmup)
+        print(json.dumps({"case": name, "B": Bc, "L": Lc, **res}), flush=True)
+        return
     g = torch.Generator(device=dev).manual_seed(5)
     shape = (Bc, Hc, Lc, FDc)
     a = (F.softplus(torch.randn(shape, generator=g, device=dev)) / math.sqrt(FDc)).bfloat16()

@@ -261,6 +261,31 @@ int lz_rope_bwd(const float* dr, const void* cos, const void* sin, int cs_dtype,
                 int L, int Dh, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Output blend of the two branches (no counterpart in the reference's        */
+/* kernels: its caller does this with torch ops, src/lizard_attention.py:92-97) */
+/* ------------------------------------------------------------------------ */
+
+/* out[b, l, h * D + d] = float(y_gla[b, h, l, d]) + alpha * float(y_swa[b, h, l, d]),
+ * stored in out_dtype (LZ_DTYPE_BF16 or LZ_DTYPE_F32): the blend, the cast to
+ * the hidden dtype and the [B, H, L, D] -> [B, L, H * D] transpose the output
+ * projection reads, in one pass. y_gla, y_swa bf16 [B*H, L, D]; alpha is a
+ * device pointer to one fp32 value (alpha_blend in the compute dtype). The
+ * product and the sum round once each, as the reference's torch ops do. */
+int lz_blend_fwd(const void* y_gla, const void* y_swa, const float* alpha, void* out,
+                 int out_dtype, int B, int H, int L, int D, void* stream);
+
+/* Bytes of scratch lz_blend_bwd needs (per-block d alpha partials). */
+size_t lz_blend_bwd_workspace_bytes(int B, int H, int L, int D);
+
+/* Gradient of lz_blend_fwd for dout [B, L, H * D] in dout_dtype:
+ * dy_gla = bf16(dout), dy_swa = bf16(alpha * dout) (both [B*H, L, D], the
+ * dtype the GLA and SWA backward consume) and *dalpha = sum dout * y_swa (fp32,
+ * reduced over per-block partials in a fixed order). */
+int lz_blend_bwd(const void* dout, int dout_dtype, const void* y_swa, const float* alpha,
+                 void* dy_gla, void* dy_swa, float* dalpha, void* workspace,
+                 size_t workspace_bytes, int B, int H, int L, int D, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* SWA                                                                      */
 /* ------------------------------------------------------------------------ */
 

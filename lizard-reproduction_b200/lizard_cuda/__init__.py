@@ -7,12 +7,13 @@ Drop-in for the reference's `kernels` package (src/kernels/__init__.py):
 Everything runs in liblizard_cuda.so through its C ABI; there is no CPU path.
 Beyond the reference's two entry points: grouped-query k / v (fewer heads than
 q) in gla and swa, swa_rope (RoPE fused into the SWA operand pass) and hedgehog
-(the fused feature map).
+(the fused feature map) and blend (the layer's output blend).
 """
 from ._lib import launch_count, load  # noqa: F401
+from .blend import blend
 from .gla import gla
 from .hedgehog import hedgehog
 from .rope import swa_rope
 from .swa import swa
 
-__all__ = ["gla", "swa", "swa_rope", "hedgehog", "load", "launch_count"]
+__all__ = ["gla", "swa", "swa_rope", "hedgehog", "blend", "load", "launch_count"]

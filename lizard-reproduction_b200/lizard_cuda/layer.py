@@ -13,13 +13,19 @@ and v to H heads (src/lizard_attention.py:73-76) before the feature map and
 both branches, which gives every query head of a group the same fk and v; the
 grouped-query kernels read each key/value head once instead, and the feature
 map runs on Hkv heads of k. RoPE is fused into the SWA operand pass
-(lizard_cuda.swa_rope) and reads the projections in place. The projections and
+(lizard_cuda.swa_rope) and reads the projections in place, and the output
+blend, cast and transpose are one kernel (lizard_cuda.blend). Under
+torch.no_grad the projections go to the kernels without the reference's fp32
+upcast: every kernel converts its inputs to fp32 itself, so the values are the
+same, and the upcast copies are skipped. With autograd on, the upcast stays, so
+the gradients of q and k add in fp32 as in the reference. The projections and
 the gate are the same torch operations as the reference.
 """
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from .blend import blend
 from .gla import gla
 from .hedgehog import hedgehog as fused_hedgehog
 from .rope import swa_rope
@@ -69,17 +75,20 @@ class LizardAttention(nn.Module):
     def forward(self, hidden_states, position_embeddings, **kwargs):
         x = hidden_states
         dtype = torch.promote_types(x.dtype, torch.float32)
-        q = self.heads_view(self.q_proj(x), self.heads).to(dtype)
-        k = self.heads_view(self.k_proj(x), self.kv_heads).to(dtype)
-        v = self.heads_view(self.v_proj(x), self.kv_heads).to(dtype)
+        up = torch.is_grad_enabled()
+        q = self.heads_view(self.q_proj(x), self.heads)
+        k = self.heads_view(self.k_proj(x), self.kv_heads)
+        v = self.heads_view(self.v_proj(x), self.kv_heads)
+        if up:
+            q, k, v = q.to(dtype), k.to(dtype), v.to(dtype)
         z = self.W_gamma(x).to(dtype).squeeze(-1)
         fq = fused_hedgehog(q, self.phi_q.weight.to(dtype))
         fk = fused_hedgehog(k, self.phi_k.weight.to(dtype))  # Hkv heads
         cos, sin = position_embeddings
         alpha, meta = self.alpha_blend.to(dtype), self.meta_tokens.to(dtype)
-        y = gla(fq, fk, v, F.logsigmoid(z)).to(dtype)
-        y = y + alpha * swa_rope(q, k, v, cos, sin, meta, self.window).to(dtype)
-        return self.o_proj(y.to(x.dtype).transpose(1, 2).flatten(2)), None
+        y_gla = gla(fq, fk, v, F.logsigmoid(z))
+        y_swa = swa_rope(q, k, v, cos, sin, meta, self.window)
+        return self.o_proj(blend(y_gla, y_swa, alpha, x.dtype)), None
 
 
 def from_llama(attention, config, **options):
