@@ -360,6 +360,44 @@ int lz_swa_bwd_noalloc(const void* q, const void* k, const void* v,
                        const void* dy, void* dq, void* dk, void* dv, int grad_dtype,
                        float* dmeta, int B, int H, int L, int D, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Recurrent decode (no counterpart in the reference, which has no cache: its */
+/* layer recomputes the whole sequence, src/lizard_attention.py:78-97)        */
+/* ------------------------------------------------------------------------ */
+
+/* One GLA decode step for every sequence of the batch: with lg the new
+ * token's log gate,
+ *   S <- exp(lg) S + fk^T v,  z <- exp(lg) z + fk,  y = fq S / max(fq . z, FLT_MIN)
+ * which equals the full-sequence gla() output at that position. fq bf16
+ * [B*H, F]; fk bf16 [B*Hkv, F]; v bf16 [B*Hkv, D]; log_gamma fp32 [B] (gate
+ * shared by the heads) or [B*H] (gate_per_head). state fp32 [B*Hs, F, D] and
+ * zstate fp32 [B*Hs, F] are updated in place; y bf16 [B*H, D]. Hs, the state
+ * head count, is H, or Hkv when the gate is shared by the heads: then the
+ * H / Hkv query heads of a group read one state (they are identical in the
+ * reference, which repeat_interleaves k and v). F <= 256, D % 4 == 0, D <= 256,
+ * H / Hs in {1, 2, 4, 8, 16}. A zero state starts a sequence; the state after a
+ * prompt is the summary of lz_gla_seg_fwd_begin over it (state | zstate). */
+int lz_gla_decode(const void* fq, const void* fk, const void* v, const float* log_gamma,
+                  int gate_per_head, float* state, float* zstate, void* y,
+                  int B, int H, int Hkv, int Hs, int F, int D, void* stream);
+
+/* One SWA decode step: rotates the new key k (Llama rotate-half RoPE with
+ * cos / sin of the token's position) and writes it with v into slot
+ * pos[b] % window of the rings k_ring / v_ring (fp32 [B*Hkv, window, D]), then
+ * every query head attends (q rotated the same way) over the
+ * min(pos[b] + 1, window) newest entries with the n_meta sink logits in the
+ * denominator, scale 1/sqrt(D): the full-sequence swa() output at position
+ * pos[b]. q [B, H, D], k, v [B, Hkv, D] in x_dtype at element strides
+ * (batch, head) with D contiguous; cos, sin [B, D] in cs_dtype at batch
+ * stride cs_sb (0 broadcasts); pos int32 [B] (tokens before the new one; the
+ * caller advances it); y bf16 [B*H, D]. D even, D <= 256, window <= 4096. */
+int lz_swa_decode(const void* q, const void* k, const void* v, int x_dtype,
+                  long long q_sb, long long q_sh, long long k_sb, long long k_sh,
+                  long long v_sb, long long v_sh, const void* cos, const void* sin,
+                  int cs_dtype, long long cs_sb, float* k_ring, float* v_ring,
+                  const int* pos, const float* meta, int n_meta, void* y,
+                  int B, int H, int Hkv, int window, int D, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,6 +61,10 @@ _SIGNATURES = {
     "lz_blend_bwd_workspace_bytes": (_c_size, [_c_int] * 4),
     "lz_blend_bwd": (_c_int, [_vp, _c_int, _vp, _vp, _vp, _vp, _vp, _vp, _c_size] + [_c_int] * 4
                      + [_vp]),
+    "lz_gla_decode": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _vp] + [_c_int] * 6 + [_vp]),
+    "lz_swa_decode": (_c_int, [_vp, _vp, _vp, _c_int] + [ctypes.c_longlong] * 6 + [_vp, _vp, _c_int, ctypes.c_longlong,
+                                                                     _vp, _vp, _vp, _vp, _c_int,
+                                                                     _vp] + [_c_int] * 5 + [_vp]),
     "lz_swa_saved_bytes": (_c_size, [_c_int] * 4),
     "lz_swa_bwd_workspace_bytes": (_c_size, [_c_int] * 5),
     "lz_swa_fwd": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp, _vp, _c_size] + [_c_int] * 4

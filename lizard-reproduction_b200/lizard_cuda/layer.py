@@ -26,6 +26,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .blend import blend
+from .decode import LayerCache, gla_decode, gla_state, swa_decode, swa_ring
 from .gla import gla
 from .hedgehog import hedgehog as fused_hedgehog
 from .rope import swa_rope
@@ -72,7 +73,14 @@ class LizardAttention(nn.Module):
         b, n, _ = x.shape
         return x.view(b, n, heads, self.head_dim).transpose(1, 2)
 
-    def forward(self, hidden_states, position_embeddings, **kwargs):
+    def forward(self, hidden_states, position_embeddings, lizard_cache=None, **kwargs):
+        """(out, None) as the reference layer. With `lizard_cache` (a
+        decode.LizardCache), a layer whose index is in the cache decodes its
+        tokens one at a time against the stored state; otherwise it runs the
+        full forward and, given a cache, stores its state there."""
+        if lizard_cache is not None and self.layer_idx in lizard_cache:
+            return self.decode(hidden_states, position_embeddings,
+                               lizard_cache[self.layer_idx]), None
         x = hidden_states
         dtype = torch.promote_types(x.dtype, torch.float32)
         up = torch.is_grad_enabled()
@@ -86,9 +94,43 @@ class LizardAttention(nn.Module):
         fk = fused_hedgehog(k, self.phi_k.weight.to(dtype))  # Hkv heads
         cos, sin = position_embeddings
         alpha, meta = self.alpha_blend.to(dtype), self.meta_tokens.to(dtype)
-        y_gla = gla(fq, fk, v, F.logsigmoid(z))
+        lg = F.logsigmoid(z)
+        y_gla = gla(fq, fk, v, lg)
         y_swa = swa_rope(q, k, v, cos, sin, meta, self.window)
+        if lizard_cache is not None:
+            with torch.no_grad():
+                state, zstate = gla_state(fk, v, lg)  # Hkv states: the gate is per token
+                k_ring, v_ring = swa_ring(k, v, cos, sin, self.window)
+                pos = torch.full((x.shape[0],), x.shape[1], dtype=torch.int32, device=x.device)
+                lizard_cache[self.layer_idx] = LayerCache(state, zstate, k_ring, v_ring, pos)
         return self.o_proj(blend(y_gla, y_swa, alpha, x.dtype)), None
+
+    @torch.no_grad()
+    def decode(self, hidden_states, position_embeddings, cache):
+        """Output for new tokens hidden_states [B, T, hidden] that follow the
+        tokens in `cache` (advanced in place), one token at a time: the same
+        values as the full forward at those positions, within bf16 rounding.
+        position_embeddings are the new tokens' (cos, sin) [B, T, Dh]."""
+        x = hidden_states
+        dtype = torch.promote_types(x.dtype, torch.float32)
+        q = self.heads_view(self.q_proj(x), self.heads)
+        k = self.heads_view(self.k_proj(x), self.kv_heads)
+        v = self.heads_view(self.v_proj(x), self.kv_heads)
+        lg = F.logsigmoid(self.W_gamma(x).to(dtype).squeeze(-1))
+        fq = fused_hedgehog(q, self.phi_q.weight.to(dtype))
+        fk = fused_hedgehog(k, self.phi_k.weight.to(dtype))
+        cos, sin = position_embeddings
+        meta = self.meta_tokens.to(dtype)
+        y_gla, y_swa = [], []
+        for t in range(x.shape[1]):
+            y_gla.append(gla_decode(fq[:, :, t], fk[:, :, t], v[:, :, t], lg[:, t], cache.state,
+                                    cache.zstate))
+            y_swa.append(swa_decode(q[:, :, t], k[:, :, t], v[:, :, t], cos[:, t], sin[:, t],
+                                    meta, cache.k_ring, cache.v_ring, cache.pos))
+            cache.pos += 1
+        y = blend(torch.stack(y_gla, 2), torch.stack(y_swa, 2), self.alpha_blend.to(dtype),
+                  x.dtype)
+        return self.o_proj(y)
 
 
 def from_llama(attention, config, **options):

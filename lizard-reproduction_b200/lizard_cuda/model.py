@@ -11,7 +11,15 @@ check_kernels(api, cfg) is the reference's pre-flight check
 (src/check.py:39-45) with a branch for the `cuda` backend: it loads
 liblizard_cuda.so (which verifies its ABI revision) and checks that the GPU
 is a compute capability 10.0 part, the one the library is built for.
+
+greedy_generate(model, input_ids, steps) decodes with the recurrent cache
+(lizard_cuda.decode): one full forward over the prompt, then one token per
+step at O(1) cost per layer (the reference has no cache and would recompute
+the whole sequence for every new token).
 """
+import torch
+
+from .decode import LizardCache
 from .layer import LizardAttention, from_llama  # noqa: F401
 from . import _lib
 
@@ -35,10 +43,27 @@ def check_kernels(api, cfg):
     backend = cfg.lizard.backend
     if backend != "cuda":
         return f"skipped, backend {backend}"
-    import torch
     assert torch.cuda.is_available(), "the cuda backend needs a CUDA GPU"
     lib = _lib.load()
     major, minor = torch.cuda.get_device_capability()
     assert (major, minor) == (10, 0), (
         f"liblizard_cuda.so is built for sm_100a; this GPU is sm_{major}{minor}")
     return f"lizard_cuda ABI {lib.lz_abi_version()} on {torch.cuda.get_device_name()}"
+
+
+@torch.no_grad()
+def greedy_generate(model, input_ids, steps):
+    """Greedy continuation of input_ids [B, L] by `steps` tokens with a
+    LizardCache: the prompt runs through the full forward (which stores every
+    layer's state), each new token through the layers' decode path. Returns the
+    new token ids [B, steps] and the cache."""
+    cache = LizardCache()
+    B, L = input_ids.shape
+    logits = model(input_ids, lizard_cache=cache, use_cache=False, logits_to_keep=1).logits
+    tokens = [logits[:, -1].argmax(-1)]
+    for i in range(1, steps):
+        pos = torch.full((B, 1), L + i - 1, dtype=torch.long, device=input_ids.device)
+        logits = model(tokens[-1][:, None], position_ids=pos, lizard_cache=cache,
+                       use_cache=False).logits
+        tokens.append(logits[:, -1].argmax(-1))
+    return torch.stack(tokens, 1), cache

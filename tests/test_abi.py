@@ -87,6 +87,23 @@ def test_rope_entries_validate(lib):
     assert rc == 1
 
 
+def test_decode_entries_validate(lib):
+    p = _fake(8)
+    # state heads must be H, or Hkv with a shared gate
+    rc = lib.lz_gla_decode(*p[:4], 1, p[4], p[5], p[6], 2, 8, 2, 2, 64, 64, None)
+    assert rc == 1 and b"state heads" in lib.lz_last_error_string()
+    rc = lib.lz_gla_decode(*p[:4], 0, p[4], p[5], p[6], 2, 8, 2, 2, 300, 64, None)
+    assert rc == 2
+    rc = lib.lz_gla_decode(*p[:4], 0, p[4], p[5], p[6], 2, 6, 2, 2, 64, 64, None)
+    assert rc == 2 and b"query heads per state" in lib.lz_last_error_string()
+    rc = lib.lz_swa_decode(*p[:3], 0, 0, 0, 0, 0, 0, 0, p[3], p[4], 0, 0, p[5], p[6], p[7],
+                           None, 0, p[0], 1, 4, 3, 16, 64, None)
+    assert rc == 1 and b"divide" in lib.lz_last_error_string()
+    rc = lib.lz_swa_decode(*p[:3], 0, 0, 0, 0, 0, 0, 0, p[3], p[4], 0, 0, p[5], p[6], p[7],
+                           None, 0, p[0], 1, 4, 2, 16, 63, None)
+    assert rc == 1 and b"even" in lib.lz_last_error_string()
+
+
 def test_gla_fwd_rejects_null_pointers(lib):
     rc = lib.lz_gla_fwd(None, None, None, None, 0, None, None, 0, None, 0, 1, 1, 8, 8, 8, 64, None)
     assert rc == 1
