@@ -420,8 +420,82 @@ def model_prefill_measure(torch, lizard_cuda, device, Bm=32, Lm=4096, steps=3, w
         attn = model.model.layers[0].self_attn
         out["attention_layer_ms"] = timed(lambda: attn(x, rope), steps, warmup)
     out["attention_share"] = cfg.num_hidden_layers * out["attention_layer_ms"] / out["ms_per_step"]
+    out["decode"] = decode_measure(torch, model, cfg, ids, device, steps=max(4, steps))
     del model
     torch.cuda.empty_cache()
+    return out
+
+
+def decode_measure(torch, model, cfg, ids, device, steps=8, warmup=2):
+    """Recurrent decode of the config-5 model: the prompt ids [B, L]
+    through the full forward into a LizardCache, then one greedy token per step
+    for the whole batch (eager, one model call per step). Also the GLA decode
+    kernel alone at the model's shape against its state traffic (the fp32 state
+    and normaliser read and written once per step)."""
+    from lizard_cuda.decode import LizardCache, gla_decode
+    Bm, Lm = ids.shape
+    out = {"workload": f"greedy decode after a {Lm}-token prompt, B={Bm}, one token per step"}
+    with torch.no_grad():
+        cache = LizardCache()
+        tok = model(ids, lizard_cache=cache, use_cache=False,
+                    logits_to_keep=1).logits[:, -1].argmax(-1, keepdim=True)
+        pos = torch.full((Bm, 1), Lm, dtype=torch.long, device=device)
+
+        def step():
+            nonlocal tok
+            tok = model(tok, position_ids=pos, lizard_cache=cache,
+                        use_cache=False).logits[:, -1].argmax(-1, keepdim=True)
+            pos.add_(1)
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / steps
+        out["ms_per_step"] = ms
+        out["tokens_per_s"] = Bm / (ms / 1e3)
+        # the same step as one CUDA graph launch (lizard_cuda.model.GraphedDecoder)
+        from lizard_cuda.model import GraphedDecoder
+        dec = GraphedDecoder(model, cache, tok, pos)
+        for _ in range(warmup):
+            dec.step()
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(steps):
+            dec.step()
+        e.record()
+        torch.cuda.synchronize()
+        gms = s.elapsed_time(e) / steps
+        out["graph_ms_per_step"] = gms
+        out["graph_tokens_per_s"] = Bm / (gms / 1e3)
+        del dec
+        c0 = cache[0]
+        Hs, F, D = c0.state.shape[1:]
+        H = cfg.num_attention_heads
+        g = torch.Generator(device=device).manual_seed(9)
+        fq = torch.rand(Bm, H, F, generator=g, device=device).bfloat16()
+        fk = torch.rand(Bm, Hs, F, generator=g, device=device).bfloat16()
+        v = torch.randn(Bm, Hs, D, generator=g, device=device).bfloat16()
+        lg = -torch.rand(Bm, generator=g, device=device)
+        st, zs = c0.state.clone(), c0.zstate.clone()
+        for _ in range(3):
+            gla_decode(fq, fk, v, lg, st, zs)
+        torch.cuda.synchronize()
+        n = 50
+        s.record()
+        for _ in range(n):
+            gla_decode(fq, fk, v, lg, st, zs)
+        e.record()
+        torch.cuda.synchronize()
+        us = s.elapsed_time(e) / n * 1e3
+        state_bytes = 2 * (st.numel() + zs.numel()) * 4
+        out["gla_decode_kernel_us"] = us
+        out["gla_decode_state_bytes"] = state_bytes
+        out["gla_decode_gbs"] = state_bytes / (us / 1e6) / 1e9
     return out
 
 

@@ -79,21 +79,33 @@ gla_decode_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
   for (int h = 0; h < QS; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
   if (rg < RG) {
     const float4 vv = reinterpret_cast<const float4*>(sV)[cg];
-    for (int f = rg; f < F; f += RG) {
-      float4 sv = Sb[(size_t)f * CG + cg];
-      const float kf = sK[f];
-      sv.x = gamma * sv.x + kf * vv.x;
-      sv.y = gamma * sv.y + kf * vv.y;
-      sv.z = gamma * sv.z + kf * vv.z;
-      sv.w = gamma * sv.w + kf * vv.w;
-      Sb[(size_t)f * CG + cg] = sv;
+    // 8 rows per pass: their loads are all in flight before the first update
+    for (int f0 = rg; f0 < F; f0 += 8 * RG) {
+      float4 sv[8];
 #pragma unroll
-      for (int h = 0; h < QS; ++h) {
-        const float qf = sQ[h * F + f];
-        acc[h].x += qf * sv.x;
-        acc[h].y += qf * sv.y;
-        acc[h].z += qf * sv.z;
-        acc[h].w += qf * sv.w;
+      for (int u = 0; u < 8; ++u) {
+        const int f = f0 + u * RG;
+        if (f < F) sv[u] = Sb[(size_t)f * CG + cg];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int f = f0 + u * RG;
+        if (f < F) {
+          const float kf = sK[f];
+          sv[u].x = gamma * sv[u].x + kf * vv.x;
+          sv[u].y = gamma * sv[u].y + kf * vv.y;
+          sv[u].z = gamma * sv[u].z + kf * vv.z;
+          sv[u].w = gamma * sv[u].w + kf * vv.w;
+          Sb[(size_t)f * CG + cg] = sv[u];
+#pragma unroll
+          for (int h = 0; h < QS; ++h) {
+            const float qf = sQ[h * F + f];
+            acc[h].x += qf * sv[u].x;
+            acc[h].y += qf * sv[u].y;
+            acc[h].z += qf * sv[u].z;
+            acc[h].w += qf * sv[u].w;
+          }
+        }
       }
     }
     // RG * CG = 256 threads exactly when CG divides 256 (D in {4, 8, ..., 256} of powers

@@ -15,7 +15,8 @@ is a compute capability 10.0 part, the one the library is built for.
 greedy_generate(model, input_ids, steps) decodes with the recurrent cache
 (lizard_cuda.decode): one full forward over the prompt, then one token per
 step at O(1) cost per layer (the reference has no cache and would recompute
-the whole sequence for every new token).
+the whole sequence for every new token); GraphedDecoder replays a captured
+decode step as one CUDA graph launch.
 """
 import torch
 
@@ -51,19 +52,59 @@ def check_kernels(api, cfg):
     return f"lizard_cuda ABI {lib.lz_abi_version()} on {torch.cuda.get_device_name()}"
 
 
+class GraphedDecoder:
+    """One greedy decode step of the whole model for a fixed batch, captured
+    as a CUDA graph: a step is one graph launch instead of several hundred
+    kernel launches from Python. The step reads the token and position
+    buffers, advances every layer's cache in place (the cache tensors are the
+    graph's static buffers) and writes the next token and position back.
+
+    Construction runs one eager step (which also prepares every kernel's
+    launch attributes) and then captures the next; `tokens` / `position`
+    ([B, 1], the last token and its position) are copied into the static
+    buffers. step() replays the graph and returns the new tokens [B, 1]."""
+
+    def __init__(self, model, cache, tokens, position):
+        self.model, self.cache = model, cache
+        self.tok = tokens.clone()
+        self.pos = position.clone()
+        self._step()  # eager: the kernels' one-time setup happens outside the capture
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+
+    def _step(self):
+        logits = self.model(self.tok, position_ids=self.pos, lizard_cache=self.cache,
+                            use_cache=False).logits
+        self.tok.copy_(logits[:, -1].argmax(-1, keepdim=True))
+        self.pos.add_(1)
+
+    def step(self):
+        self.graph.replay()
+        return self.tok
+
+
 @torch.no_grad()
-def greedy_generate(model, input_ids, steps):
+def greedy_generate(model, input_ids, steps, graph=False):
     """Greedy continuation of input_ids [B, L] by `steps` tokens with a
     LizardCache: the prompt runs through the full forward (which stores every
-    layer's state), each new token through the layers' decode path. Returns the
-    new token ids [B, steps] and the cache."""
+    layer's state), each new token through the layers' decode path, eagerly or
+    (graph=True) as replays of a GraphedDecoder. Returns the new token ids
+    [B, steps] and the cache."""
     cache = LizardCache()
     B, L = input_ids.shape
     logits = model(input_ids, lizard_cache=cache, use_cache=False, logits_to_keep=1).logits
-    tokens = [logits[:, -1].argmax(-1)]
-    for i in range(1, steps):
-        pos = torch.full((B, 1), L + i - 1, dtype=torch.long, device=input_ids.device)
-        logits = model(tokens[-1][:, None], position_ids=pos, lizard_cache=cache,
-                       use_cache=False).logits
-        tokens.append(logits[:, -1].argmax(-1))
-    return torch.stack(tokens, 1), cache
+    tokens = [logits[:, -1].argmax(-1, keepdim=True)]
+    pos = torch.full((B, 1), L, dtype=torch.long, device=input_ids.device)
+    if graph and steps > 2:
+        dec = GraphedDecoder(model, cache, tokens[-1], pos)  # runs step 2 eagerly
+        tokens.append(dec.tok.clone())
+        for _ in range(2, steps):
+            tokens.append(dec.step().clone())
+        return torch.cat(tokens, 1), cache
+    for _ in range(1, steps):
+        logits = model(tokens[-1], position_ids=pos, lizard_cache=cache, use_cache=False).logits
+        tokens.append(logits[:, -1].argmax(-1, keepdim=True))
+        pos = pos + 1
+    return torch.cat(tokens, 1), cache

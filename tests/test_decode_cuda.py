@@ -163,7 +163,11 @@ def test_model_decode_logits_match_full_forward():
             got.append(model(ids[:, t:t + 1], position_ids=pos, lizard_cache=cache,
                              use_cache=False).logits)
     assert_output(torch.cat(got, 1), full[:, L0:], "model decode logits", layer=True)
-    toks, cache2 = greedy_generate(model, ids[:, :L0], 4)
-    assert toks.shape == (B, 4) and int(cache2[0].pos[0]) == L0 + 3
+    toks, cache2 = greedy_generate(model, ids[:, :L0], 6)
+    assert toks.shape == (B, 6) and int(cache2[0].pos[0]) == L0 + 5
     with torch.no_grad():  # the first generated token is the prompt's argmax
         assert torch.equal(toks[:, 0], full[:, L0 - 1].argmax(-1))
+    # a decode step replayed from a CUDA graph runs the same kernels on the same data
+    gtoks, gcache = greedy_generate(model, ids[:, :L0], 6, graph=True)
+    assert torch.equal(gtoks, toks)
+    assert torch.equal(gcache[1].state, cache2[1].state)
