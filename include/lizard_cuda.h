@@ -390,7 +390,7 @@ int lz_gla_decode(const void* fq, const void* fk, const void* v, const float* lo
  * pos[b]. q [B, H, D], k, v [B, Hkv, D] in x_dtype at element strides
  * (batch, head) with D contiguous; cos, sin [B, D] in cs_dtype at batch
  * stride cs_sb (0 broadcasts); pos int32 [B] (tokens before the new one; the
- * caller advances it); y bf16 [B*H, D]. D even, D <= 256, window <= 4096. */
+ * caller advances it); y bf16 [B*H, D]. D even, D <= 256, window <= 1024. */
 int lz_swa_decode(const void* q, const void* k, const void* v, int x_dtype,
                   long long q_sb, long long q_sh, long long k_sb, long long k_sh,
                   long long v_sb, long long v_sh, const void* cos, const void* sin,

@@ -19,6 +19,8 @@
 // ring of the last W rotated keys / values (fp32); each query head of the group
 // attends over the min(pos + 1, W) most recent entries with the sink logits in
 // the denominator, scale 1/sqrt(D).
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace lz {
@@ -135,7 +137,13 @@ __device__ __forceinline__ float ldf<bf16>(const bf16* p, size_t i) {
   return __bfloat162float(p[i]);
 }
 
-// One CTA per (batch row, key/value head); 8 warps.
+// One CTA per (batch row, key/value head). The whole CTA rotates the new key
+// and writes it and v into the ring; then each warp takes query heads of the
+// group (warp, warp + nwarps, ...): lanes own keys for the scores (a key row
+// per lane, the rotated query broadcast from shared memory) and columns for
+// P V (coalesced rows of the value ring).
+constexpr int kMaxDecodeWindow = 1024;
+
 template <typename XT, typename CT>
 __global__ void __launch_bounds__(kT)
 swa_decode_kernel(const XT* __restrict__ q, long long q_sb, long long q_sh,
@@ -146,10 +154,10 @@ swa_decode_kernel(const XT* __restrict__ q, long long q_sb, long long q_sh,
                   const float* __restrict__ meta, int n_meta, bf16* __restrict__ y, int H,
                   int Hkv, int W, int D) {
   extern __shared__ __align__(16) float sm[];
-  float* sQ = sm;          // [D] rotated query of the current head
-  float* sP = sQ + D;      // [W] softmax weights
-  float* sStat = sP + W;   // [2] max, sum
+  const int nw = blockDim.x >> 5;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* sQ = sm + warp * D;                    // [nw][D] rotated query per warp
+  float* sP = sm + nw * D + warp * W;           // [nw][W] softmax weights per warp
   const int bkv = blockIdx.x, b = bkv / Hkv, j = bkv - b * Hkv;
   const int grp = H / Hkv, half = D / 2;
   const int t = pos[b];
@@ -158,65 +166,65 @@ swa_decode_kernel(const XT* __restrict__ q, long long q_sb, long long q_sh,
   const CT* sb = sn + (size_t)b * cs_sb;
   float* kring = kc + (size_t)bkv * W * D;
   float* vring = vc + (size_t)bkv * W * D;
-  // rotate and insert the new key and value
   const XT* kr = k + b * k_sb + j * k_sh;
   const XT* vr = v + b * v_sb + j * v_sh;
-  for (int d = tid; d < half; d += kT) {
+  for (int d = tid; d < half; d += blockDim.x) {
     const float x1 = ldf(kr, d), x2 = ldf(kr, d + half);
     const float c1 = ldf(cb, d), s1 = ldf(sb, d), c2 = ldf(cb, d + half), s2 = ldf(sb, d + half);
     kring[(size_t)slot * D + d] = __fadd_rn(__fmul_rn(x1, c1), -__fmul_rn(x2, s1));
     kring[(size_t)slot * D + d + half] = __fadd_rn(__fmul_rn(x2, c2), __fmul_rn(x1, s2));
   }
-  for (int d = tid; d < D; d += kT) vring[(size_t)slot * D + d] = ldf(vr, d);
+  for (int d = tid; d < D; d += blockDim.x) vring[(size_t)slot * D + d] = ldf(vr, d);
   __syncthreads();
   const float scale = rsqrtf((float)D);
   float ms = -1e30f;
   for (int m = 0; m < n_meta; ++m) ms = fmaxf(ms, meta[m]);
-  for (int g = 0; g < grp; ++g) {
+  for (int g = warp; g < grp; g += nw) {
     const int hq = j * grp + g;
     const XT* qr = q + b * q_sb + hq * q_sh;
-    for (int d = tid; d < half; d += kT) {
+    for (int d = lane; d < half; d += 32) {
       const float x1 = ldf(qr, d), x2 = ldf(qr, d + half);
       const float c1 = ldf(cb, d), s1 = ldf(sb, d), c2 = ldf(cb, d + half), s2 = ldf(sb, d + half);
       sQ[d] = __fadd_rn(__fmul_rn(x1, c1), -__fmul_rn(x2, s1));
       sQ[d + half] = __fadd_rn(__fmul_rn(x2, c2), __fmul_rn(x1, s2));
     }
-    __syncthreads();
-    // scores of the n most recent keys, one warp per key
-    for (int e = warp; e < n; e += kT / 32) {
-      const int sl = (t - e) % W;
-      const float* kk = kring + (size_t)sl * D;
+    __syncwarp();
+    // scores: key e (e = 0 the newest) per lane
+    float mx = ms;
+    for (int e = lane; e < n; e += 32) {
+      const float* kk = kring + (size_t)((t - e) % W) * D;
       float x = 0.f;
-      for (int d = lane; d < D; d += 32) x += sQ[d] * kk[d];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-      if (lane == 0) sP[e] = x * scale;
-    }
-    __syncthreads();
-    if (warp == 0) {
-      float mx = ms;
-      for (int e = lane; e < n; e += 32) mx = fmaxf(mx, sP[e]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      float sum = 0.f;
-      for (int e = lane; e < n; e += 32) {
-        const float p = __expf(sP[e] - mx);
-        sP[e] = p;
-        sum += p;
+      if ((D & 3) == 0) {
+        for (int d = 0; d < D; d += 4) {
+          const float4 kv = *reinterpret_cast<const float4*>(kk + d);
+          x += sQ[d] * kv.x + sQ[d + 1] * kv.y + sQ[d + 2] * kv.z + sQ[d + 3] * kv.w;
+        }
+      } else {
+        for (int d = 0; d < D; ++d) x += sQ[d] * kk[d];
       }
-      for (int m = lane; m < n_meta; m += 32) sum += __expf(meta[m] - mx);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      if (lane == 0) sStat[1] = sum;
+      x *= scale;
+      sP[e] = x;
+      mx = fmaxf(mx, x);
     }
-    __syncthreads();
-    const float inv = 1.f / sStat[1];
-    for (int d = tid; d < D; d += kT) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    for (int e = lane; e < n; e += 32) {
+      const float p = __expf(sP[e] - mx);
+      sP[e] = p;
+      sum += p;
+    }
+    for (int m = lane; m < n_meta; m += 32) sum += __expf(meta[m] - mx);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float inv = 1.f / sum;
+    __syncwarp();
+    for (int d = lane; d < D; d += 32) {
       float acc = 0.f;
       for (int e = 0; e < n; ++e) acc += sP[e] * vring[(size_t)((t - e) % W) * D + d];
       y[((size_t)b * H + hq) * D + d] = __float2bfloat16_rn(acc * inv);
     }
-    __syncthreads();
+    __syncwarp();
   }
 }
 
@@ -246,15 +254,21 @@ int launch_swa_decode(const void* q, long long q_sb, long long q_sh, const void*
                       long long cs_sb, float* kc, float* vc, const int* pos, const float* meta,
                       int n_meta, bf16* y, int B, int H, int Hkv, int W, int D,
                       cudaStream_t st) {
-  const size_t smem = (size_t)(D + W + 2) * 4;
+  const int nw = std::min(H / Hkv, kT / 32);  // one warp per query head of the group
+  const size_t smem = (size_t)nw * (D + W) * 4;
   const unsigned grid = (unsigned)(B * Hkv);
+  static bool done[2][64] = {{false}};
+  int rc = cs_dtype == LZ_DTYPE_F32
+               ? ensure_decode_smem(swa_decode_kernel<XT, float>, smem, done[0])
+               : ensure_decode_smem(swa_decode_kernel<XT, bf16>, smem, done[1]);
+  if (rc) return rc;
   if (cs_dtype == LZ_DTYPE_F32)
-    swa_decode_kernel<XT, float><<<grid, kT, smem, st>>>(
+    swa_decode_kernel<XT, float><<<grid, 32 * nw, smem, st>>>(
         static_cast<const XT*>(q), q_sb, q_sh, static_cast<const XT*>(k), k_sb, k_sh,
         static_cast<const XT*>(v), v_sb, v_sh, static_cast<const float*>(cs),
         static_cast<const float*>(sn), cs_sb, kc, vc, pos, meta, n_meta, y, H, Hkv, W, D);
   else
-    swa_decode_kernel<XT, bf16><<<grid, kT, smem, st>>>(
+    swa_decode_kernel<XT, bf16><<<grid, 32 * nw, smem, st>>>(
         static_cast<const XT*>(q), q_sb, q_sh, static_cast<const XT*>(k), k_sb, k_sh,
         static_cast<const XT*>(v), v_sb, v_sh, static_cast<const bf16*>(cs),
         static_cast<const bf16*>(sn), cs_sb, kc, vc, pos, meta, n_meta, y, H, Hkv, W, D);
@@ -325,8 +339,8 @@ extern "C" int lz_swa_decode(const void* q, const void* k, const void* v, int x_
   LZ_REQUIRE(H % Hkv == 0, LZ_ERR_INVALID_ARGUMENT,
              "the key/value head count must divide the query head count");
   LZ_REQUIRE(D % 2 == 0, LZ_ERR_INVALID_ARGUMENT, "the rotated head dim must be even");
-  LZ_REQUIRE(D <= 256 && window <= 4096, LZ_ERR_UNSUPPORTED,
-             "decode supports D <= 256 and windows up to 4096");
+  LZ_REQUIRE(D <= 256 && window <= kMaxDecodeWindow, LZ_ERR_UNSUPPORTED,
+             "decode supports D <= 256 and windows up to 1024");
   LZ_REQUIRE(n_meta >= 0 && n_meta <= 32 && (n_meta == 0 || meta), LZ_ERR_INVALID_ARGUMENT,
              "meta must hold n_meta (<= 32) values");
   LZ_REQUIRE(dtype_ok(x_dtype) && dtype_ok(cs_dtype), LZ_ERR_INVALID_ARGUMENT,
