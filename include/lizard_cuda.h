@@ -129,6 +129,13 @@ int lz_gla_bwd(const void* fq, const void* fk, const void* v,
  * group of query heads in a fixed order (the autograd of repeat_interleave).
  * lz_gla_fwd / lz_gla_bwd are these with Hkv = H. */
 size_t lz_gla_bwd_gqa_workspace_bytes(int B, int H, int Hkv, int L, int F, int D, int chunk);
+/* Forward workspace of lz_gla_fwd_gqa. training != 0 when a saved buffer is
+ * passed. Without one and with a gate shared by the heads (gate_per_head = 0),
+ * the chunk-parallel schedule keeps one state per key/value head (the query
+ * heads of a group have identical states), so the workspace is sized for Hkv
+ * heads. 0 when the sequential walk is planned. */
+size_t lz_gla_fwd_gqa_workspace_bytes(int B, int H, int Hkv, int L, int F, int D, int chunk,
+                                      int gate_per_head, int training);
 int lz_gla_fwd_gqa(const void* fq, const void* fk, const void* v,
                    const float* log_gamma, int gate_per_head,
                    void* y, void* saved, size_t saved_bytes,
@@ -340,6 +347,30 @@ int lz_swa_bwd_gqa(const void* q, const void* k, const void* v,
                    const void* dy, void* dq, void* dk, void* dv, int grad_dtype,
                    float* dmeta, void* workspace, size_t workspace_bytes,
                    int B, int H, int Hkv, int L, int D, void* stream);
+
+/* The SWA forward with RoPE inside: q [B, H, L, D], k and v [B, Hkv, L, D]
+ * unrotated, all in x_dtype (LZ_DTYPE_F32 or LZ_DTYPE_BF16) at element strides
+ * (batch, head, token) with D contiguous, so projection outputs are read in
+ * place; cos / sin as for lz_rope_split. The kernel loads 64-row tiles of q, k,
+ * v with TMA (k and v through a two-stage ring), rotates q and k in fp32 and
+ * splits them into bf16 value + residual tiles in shared memory, then runs the
+ * forward of lz_swa_fwd_gqa: y (and saved) equal lz_rope_split +
+ * lz_swa_fwd_gqa bit for bit. q_hi, q_lo [B*H, L, D] and k_hi, k_lo
+ * [B*Hkv, L, D] (bf16, all null or all set) receive the rotated operands that
+ * lz_swa_bwd_gqa takes. Returns LZ_ERR_UNSUPPORTED without launching when D is
+ * not 32, 64 or 128, a stride or base is not 16-byte aligned, or the tiles do
+ * not fit in shared memory (fp32 at D = 128); rotate first then. The reference
+ * rotates with torch ops in its caller (src/lizard_attention.py:87-88). */
+int lz_swa_rope_fwd(const void* q, const void* k, const void* v, int x_dtype,
+                    long long q_sb, long long q_sh, long long q_sl,
+                    long long k_sb, long long k_sh, long long k_sl,
+                    long long v_sb, long long v_sh, long long v_sl,
+                    const void* cos, const void* sin, int cs_dtype,
+                    long long cs_sb, long long cs_sl,
+                    const float* meta, int n_meta, int window,
+                    void* y, void* saved, size_t saved_bytes,
+                    void* q_hi, void* q_lo, void* k_hi, void* k_lo,
+                    int B, int H, int Hkv, int L, int D, void* stream);
 
 /* lz_swa_bwd for callers that cannot allocate (no counterpart in the
  * reference, whose kernels always allocate through torch). Some hosts give a

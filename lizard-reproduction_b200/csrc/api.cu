@@ -48,6 +48,15 @@ extern "C" size_t lz_gla_bwd_gqa_workspace_bytes(int B, int H, int Hkv, int L, i
                              Hkv != H);
 }
 
+extern "C" size_t lz_gla_fwd_gqa_workspace_bytes(int B, int H, int Hkv, int L, int F, int D,
+                                                 int chunk, int gate_per_head, int training) {
+  (void)chunk;
+  if (B < 1 || H < 1 || L < 1 || F < 1 || D < 1 || Hkv < 1 || H % Hkv) return 0;
+  if (!lz::gla_fwd_split(B, H, L, F, D)) return 0;
+  const int Hs = (!training && !gate_per_head && Hkv < H) ? Hkv : H;
+  return lz::gla_fwd_work_layout(B, H, L, F, D, nullptr, nullptr, Hs);
+}
+
 extern "C" size_t lz_gla_fwd_workspace_bytes(int B, int H, int L, int F, int D, int chunk) {
   (void)chunk;
   if (B < 1 || H < 1 || L < 1 || F < 1 || D < 1) return 0;
@@ -90,12 +99,14 @@ extern "C" int lz_gla_fwd_gqa(const void* fq, const void* fk, const void* v,
   }
   lz::GlaFwdWork fw;
   if (lz::gla_fwd_split(B, H, L, F, D)) {
-    const size_t need = lz::gla_fwd_work_layout(B, H, L, F, D, nullptr, nullptr);
+    // one state per key/value head when nothing is saved and the gate is shared
+    const int Hs = (!saved && !gate_per_head && Hkv < H) ? Hkv : H;
+    const size_t need = lz::gla_fwd_work_layout(B, H, L, F, D, nullptr, nullptr, Hs);
     LZ_REQUIRE(workspace && workspace_bytes >= need, LZ_ERR_WORKSPACE,
-               "workspace too small (lz_gla_fwd_workspace_bytes)");
+               "workspace too small (lz_gla_fwd_gqa_workspace_bytes)");
     LZ_REQUIRE(lz::aligned16(workspace), LZ_ERR_INVALID_ARGUMENT,
                "workspace must be 16-byte aligned");
-    lz::gla_fwd_work_layout(B, H, L, F, D, static_cast<unsigned char*>(workspace), &fw);
+    lz::gla_fwd_work_layout(B, H, L, F, D, static_cast<unsigned char*>(workspace), &fw, Hs);
   }
   return lz::gla_fwd(static_cast<const bf16*>(fq), static_cast<const bf16*>(fk),
                      static_cast<const bf16*>(v), log_gamma, gate_per_head ? 1 : 0,
@@ -199,6 +210,54 @@ extern "C" int lz_swa_fwd_gqa(const void* q, const void* k, const void* v, const
                      static_cast<const bf16*>(k_lo), meta, n_meta, window,
                      static_cast<bf16*>(y), sv, B, H, Hkv, L, D,
                      static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lz_swa_rope_fwd(const void* q, const void* k, const void* v, int x_dtype,
+                               long long q_sb, long long q_sh, long long q_sl, long long k_sb,
+                               long long k_sh, long long k_sl, long long v_sb, long long v_sh,
+                               long long v_sl, const void* cos, const void* sin, int cs_dtype,
+                               long long cs_sb, long long cs_sl, const float* meta, int n_meta,
+                               int window, void* y, void* saved, size_t saved_bytes, void* q_hi,
+                               void* q_lo, void* k_hi, void* k_lo, int B, int H, int Hkv, int L,
+                               int D, void* stream) {
+  lz::clear_error();
+  int rc = check_sizes(B, H, L, 1, D);
+  if (rc) return rc;
+  LZ_REQUIRE(Hkv >= 1 && H % Hkv == 0, LZ_ERR_INVALID_ARGUMENT,
+             "the key/value head count must divide the query head count");
+  LZ_REQUIRE(q && k && v && cos && sin && y, LZ_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  LZ_REQUIRE((x_dtype == LZ_DTYPE_F32 || x_dtype == LZ_DTYPE_BF16) &&
+                 (cs_dtype == LZ_DTYPE_F32 || cs_dtype == LZ_DTYPE_BF16),
+             LZ_ERR_INVALID_ARGUMENT, "dtypes must be LZ_DTYPE_F32 or LZ_DTYPE_BF16");
+  LZ_REQUIRE(n_meta >= 0 && (n_meta == 0 || meta), LZ_ERR_INVALID_ARGUMENT,
+             "meta must be non-null when n_meta > 0");
+  LZ_REQUIRE(n_meta <= lz::kMaxMeta, LZ_ERR_UNSUPPORTED, "more than 32 sink logits");
+  LZ_REQUIRE(window >= 1, LZ_ERR_INVALID_ARGUMENT, "window must be >= 1");
+  LZ_REQUIRE(D % 2 == 0, LZ_ERR_INVALID_ARGUMENT, "the rotated head dim must be even");
+  LZ_REQUIRE((q_hi == nullptr) == (q_lo == nullptr) && (q_hi == nullptr) == (k_hi == nullptr) &&
+                 (k_hi == nullptr) == (k_lo == nullptr),
+             LZ_ERR_INVALID_ARGUMENT, "the rotated operand outputs must be all null or all set");
+  LZ_REQUIRE(!q_hi || (lz::aligned16(q_hi) && lz::aligned16(q_lo) && lz::aligned16(k_hi) &&
+                       lz::aligned16(k_lo)),
+             LZ_ERR_INVALID_ARGUMENT, "rotated operand outputs must be 16-byte aligned");
+  LZ_REQUIRE(lz::aligned16(y), LZ_ERR_INVALID_ARGUMENT, "y must be 16-byte aligned");
+  lz::SwaSaved sv;
+  if (saved) {
+    LZ_REQUIRE(saved_bytes >= lz::swa_saved_layout(B, H, L, D, nullptr, nullptr),
+               LZ_ERR_WORKSPACE, "saved buffer too small");
+    LZ_REQUIRE(lz::aligned16(saved), LZ_ERR_INVALID_ARGUMENT,
+               "saved buffer must be 16-byte aligned");
+    lz::swa_saved_layout(B, H, L, D, static_cast<unsigned char*>(saved), &sv);
+  }
+  lz::SwaRopeArgs a{q, k, v, x_dtype, q_sb, q_sh, q_sl, k_sb, k_sh, k_sl, v_sb, v_sh, v_sl,
+                    cos, sin, cs_dtype, cs_sb, cs_sl, meta, n_meta, window,
+                    static_cast<bf16*>(y), static_cast<bf16*>(q_hi), static_cast<bf16*>(q_lo),
+                    static_cast<bf16*>(k_hi), static_cast<bf16*>(k_lo), B, H, Hkv, L, D};
+  rc = lz::swa_rope_fwd(a, sv, static_cast<cudaStream_t>(stream));
+  if (rc == LZ_ERR_UNSUPPORTED)
+    lz::set_error("lz_swa_rope_fwd: head dim or strides outside the TMA path (rotate with "
+                  "lz_rope_split and call lz_swa_fwd_gqa)");
+  return rc;
 }
 
 extern "C" int lz_swa_fwd(const void* q, const void* k, const void* v, const void* q_lo,

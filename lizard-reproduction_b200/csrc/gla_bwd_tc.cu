@@ -680,28 +680,10 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
 }
 
 // ------------------------------------------------------------ host helpers
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
 
 // [BH, rows, 128] bf16 as 3-D {128, rows, BH}, box {64, 128, 1}, 128-byte swizzle
 bool make_map(CUtensorMap* m, const void* ptr, int BH, int rows) {
-  EncodeTiledFn fn = encode_fn();
+  tc::EncodeTiledFn fn = tc::encode_tiled_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)BH};
   cuuint64_t strides[2] = {256, (cuuint64_t)rows * 256};

@@ -522,29 +522,11 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 }
 
 // ------------------------------------------------------------ host helpers
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
 
 // [rows = BH x L, cols] bf16 viewed as 3-D {cols, L, BH}, box {64, 128, 1},
 // 128-byte swizzle, zero fill outside.
 bool make_map(CUtensorMap* m, const void* ptr, int BH, int L, int cols) {
-  EncodeTiledFn fn = encode_fn();
+  tc::EncodeTiledFn fn = tc::encode_tiled_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)L, (cuuint64_t)BH};
   cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)L * cols * 2};

@@ -59,6 +59,10 @@ inline bool gla_fwd_split(int B, int H, int L, int F, int D) {
   if (L <= 64) return false;  // a single chunk: both schedules are the same work
   const long long BH = (long long)B * H;
   if (F == 128 && D == 128) return BH <= 40;  // tensor-core walk, one CTA per head
+  // F = 256 (the model's feature map): the warp-MMA walk splits the value
+  // columns and waits on every chunk's loads; the chunk-parallel kernels were
+  // 1.6-3x faster at config-5 shapes, and equal without shared states at B=32
+  if (F > 128) return true;
   return BH * ((F + 63) / 64) * ((D + 63) / 64) <= 148;
 }
 
@@ -145,9 +149,11 @@ inline size_t gla_work_layout(int B, int H, int L, int F, int D, bool split,
   return off;
 }
 
+// Hs: heads that carry states (H, or Hkv when a group of query heads shares
+// one state: inference with a gate shared by the heads, gla_split.cu); 0 = H.
 inline size_t gla_fwd_work_layout(int B, int H, int L, int F, int D, unsigned char* base,
-                                  GlaFwdWork* out) {
-  const size_t BH = (size_t)B * H, NT = gla_nt(L);
+                                  GlaFwdWork* out, int Hs = 0) {
+  const size_t BH = (size_t)B * (Hs > 0 ? Hs : H), NT = gla_nt(L);
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;

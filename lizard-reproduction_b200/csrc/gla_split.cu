@@ -372,8 +372,8 @@ template <int FP, int DV>
 __global__ void __launch_bounds__(128)
 gla_split_out_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
                      const bf16* __restrict__ v, const float* __restrict__ lg, int gph, int H,
-                     int grp, int L, int F, int D, int NT, int nslices, int vec_f, int vec_d,
-                     int vec_s,
+                     int grp, int sgrp, int L, int F, int D, int NT, int nslices, int vec_f,
+                     int vec_d, int vec_s,
                      const bf16* __restrict__ s_in, const float* __restrict__ z_in,
                      const float* __restrict__ gs, int seeded, bf16* __restrict__ y,
                      float* __restrict__ y32, float* __restrict__ den_out,
@@ -394,7 +394,9 @@ gla_split_out_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
   const int n = idx % NT, bh = idx / NT;
   const int r0 = n * kC, nvalid = min(kC, L - r0), d0 = slice * DV;
   const bool lead = slice == 0;
-  const size_t chunk = (size_t)bh * NT + n;
+  // states, normalisers and gate offsets: per query head, or per key/value head
+  // when the gate is shared by the heads (sgrp query heads per state)
+  const size_t chunk = (size_t)(sgrp > 1 ? kv_head(bh, H, sgrp) : bh) * NT + n;
   const size_t rowb = (size_t)bh * L;
   const bool with_state = n > 0 || seeded;
 
@@ -415,7 +417,8 @@ gla_split_out_kernel(const bf16* __restrict__ fq, const bf16* __restrict__ fk,
 
 template <int FP, int DV>
 int launch_out(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, int BH,
-               int H, int grp, int L, int F, int D, int NT, const bf16* s_in, const float* z_in,
+               int H, int grp, int sgrp, int L, int F, int D, int NT, const bf16* s_in,
+               const float* z_in,
                const float* gs, int seeded, bf16* y, float* y32, float* den, float* g_out,
                cudaStream_t st) {
   using SM = SplitOutSmem<FP, DV>;
@@ -427,8 +430,8 @@ int launch_out(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
   const int vec_d = (D % 8 == 0) && aligned16(v);
   const int vec_s = (D % 8 == 0) && aligned16(s_in);
   gla_split_out_kernel<FP, DV><<<(unsigned)((long long)BH * NT * nslices), 128, SM::bytes, st>>>(
-      fq, fk, v, lg, gph, H, grp, L, F, D, NT, nslices, vec_f, vec_d, vec_s, s_in, z_in, gs,
-      seeded, y, y32, den, g_out);
+      fq, fk, v, lg, gph, H, grp, sgrp, L, F, D, NT, nslices, vec_f, vec_d, vec_s, s_in, z_in,
+      gs, seeded, y, y32, den, g_out);
   count_launches(1);
   return check_launch("gla_split_out_kernel");
 }
@@ -466,15 +469,21 @@ int gla_fwd_split_run(const bf16* fq, const bf16* fk, const bf16* v, const float
   const int nfb = ceil_div(F, 64), ndb = ceil_div(D, 64);
   const int vec_f = (F % 8 == 0) && aligned16(fk);
   const int vec_d = (D % 8 == 0) && aligned16(v);
-  gla_split_finc_kernel<<<(unsigned)((long long)BH * NT * nfb * ndb), 128, 0, stream>>>(
-      fk, v, lg, gph, H, grp, L, F, D, NT, nfb, ndb, vec_f, vec_d, fw.inc, fw.incz, fw.lam);
+  const bool save = sv.y32 != nullptr;
+  // With a gate shared by the heads, the query heads of a key/value group have
+  // identical chunk states: without a backward to feed (which reads states per
+  // query head), increments and scan run once per key/value head.
+  const bool share = !save && !gph && grp > 1;
+  const int Hs = share ? Hkv : H, BHs = B * Hs;
+  gla_split_finc_kernel<<<(unsigned)((long long)BHs * NT * nfb * ndb), 128, 0, stream>>>(
+      fk, v, lg, gph, Hs, share ? 1 : grp, L, F, D, NT, nfb, ndb, vec_f, vec_d, fw.inc, fw.incz,
+      fw.lam);
   count_launches(1);
   int rc = check_launch("gla_split_finc_kernel");
   if (rc) return rc;
-  const bool save = sv.y32 != nullptr;
   bf16* s = save ? sv.s : fw.s;
   float* z = save ? sv.z : fw.z;
-  rc = launch_scan(fw.inc, fw.incz, fw.lam, BH, NT, F, D, 0, nullptr, nullptr, s, z, nullptr,
+  rc = launch_scan(fw.inc, fw.incz, fw.lam, BHs, NT, F, D, 0, nullptr, nullptr, s, z, nullptr,
                    nullptr, save ? fw.gs : nullptr, nullptr, stream);
   if (rc) return rc;
   const int FP = F <= 32 ? 32 : F <= 64 ? 64 : F <= 128 ? 128 : 256;
@@ -482,8 +491,8 @@ int gla_fwd_split_run(const bf16* fq, const bf16* fk, const bf16* v, const float
   float* y32 = save ? sv.y32 : nullptr;
 #define LZ_OUT_CASE(fp, dv)                                                                   \
   if (FP == fp && DV == dv)                                                                   \
-    return launch_out<fp, dv>(fq, fk, v, lg, gph, BH, H, grp, L, F, D, NT, s, z, fw.gs, 0, y,  \
-                              y32, sv.den, save ? sv.g : nullptr, stream);
+    return launch_out<fp, dv>(fq, fk, v, lg, gph, BH, H, grp, share ? grp : 1, L, F, D, NT, s, \
+                              z, fw.gs, 0, y, y32, sv.den, save ? sv.g : nullptr, stream);
   LZ_OUT_CASE(32, 16) LZ_OUT_CASE(32, 32) LZ_OUT_CASE(32, 64)
   LZ_OUT_CASE(64, 16) LZ_OUT_CASE(64, 32) LZ_OUT_CASE(64, 64)
   LZ_OUT_CASE(128, 16) LZ_OUT_CASE(128, 32) LZ_OUT_CASE(128, 64)
@@ -596,8 +605,8 @@ int gla_seg_fwd_end(const bf16* fq, const bf16* fk, const bf16* v, const float* 
   const int seeded = seed != nullptr;
 #define LZ_OUT_CASE(fp, dv)                                                                   \
   if (FP == fp && DV == dv)                                                                   \
-    return launch_out<fp, dv>(fq, fk, v, lg, gph, BH, H, 1, L, F, D, NT, s, z, fw.gs, seeded, \
-                              y, y32, sv.den, save ? sv.g : nullptr, stream);
+    return launch_out<fp, dv>(fq, fk, v, lg, gph, BH, H, 1, 1, L, F, D, NT, s, z, fw.gs,      \
+                              seeded, y, y32, sv.den, save ? sv.g : nullptr, stream);
   LZ_OUT_CASE(32, 16) LZ_OUT_CASE(32, 32) LZ_OUT_CASE(32, 64)
   LZ_OUT_CASE(64, 16) LZ_OUT_CASE(64, 32) LZ_OUT_CASE(64, 64)
   LZ_OUT_CASE(128, 16) LZ_OUT_CASE(128, 32) LZ_OUT_CASE(128, 64)

@@ -27,6 +27,7 @@
 
 #include "common.cuh"
 #include "swa_layout.h"
+#include "tc.cuh"
 
 namespace lz {
 
@@ -626,6 +627,295 @@ swa_bwd_dkv_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
   }
 }
 
+// ------------------------------------------------- forward, RoPE inside
+// The SWA forward for unrotated queries and keys: q, k, v tiles come straight
+// from the caller's tensors (any batch / head / token strides, fp32 or bf16)
+// through TMA, the key / value tiles into a 2-stage ring; the CTA rotates the
+// q and k tiles in fp32 (Llama rotate-half with cos / sin of each row's
+// position; products and sum rounded once each) and splits them into the
+// bf16 value + residual tiles the MMAs read, and converts v to bf16. From
+// there the online softmax and P V are the forward kernel's, so the results
+// equal rotating first (lz_rope_split) and calling the forward. With
+// qh_out.. given (training) the kernel also writes the rotated operands the
+// backward reads: q rows by their CTA, each key block by the CTA of the
+// group's first query head whose query block starts at it.
+template <int DP, typename XT>
+struct RopeSmem {
+  static constexpr size_t T = Tile<DP>::bytes;               // padded bf16 tile
+  static constexpr size_t R = (size_t)kB * DP * sizeof(XT);  // raw TMA tile
+  static constexpr size_t q = 0, ql = q + T, k = ql + T, kl = k + T, v = kl + T, rq = v + T,
+                          rk = rq + R, rv = rk + 2 * R, bars = rv + 2 * R, bytes = bars + 64;
+};
+
+template <typename T>
+__device__ __forceinline__ float ldv(const T* p, size_t i);
+template <>
+__device__ __forceinline__ float ldv<float>(const float* p, size_t i) { return p[i]; }
+template <>
+__device__ __forceinline__ float ldv<bf16>(const bf16* p, size_t i) {
+  return __bfloat162float(p[i]);
+}
+
+// 8 consecutive elements of a row as fp32 (16-byte loads; p 16-byte aligned
+// for bf16, 32-byte for fp32 rows of 32 / 64 / 128 elements).
+__device__ __forceinline__ void load8(const bf16* p, float (&x)[8]) {
+  const uint4 w = *reinterpret_cast<const uint4*>(p);
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = bf16_lo(u[i]);
+    x[2 * i + 1] = bf16_hi(u[i]);
+  }
+}
+__device__ __forceinline__ void load8(const float* p, float (&x)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+}
+__device__ __forceinline__ uint4 pack8(const float (&x)[8]) {
+  return make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]),
+                    pack_bf16(x[6], x[7]));
+}
+__device__ __forceinline__ uint4 resid8(const float (&x)[8], uint4 h) {
+  const uint32_t u[4] = {h.x, h.y, h.z, h.w};
+  float r[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    r[2 * i] = x[2 * i] - bf16_lo(u[i]);
+    r[2 * i + 1] = x[2 * i + 1] - bf16_hi(u[i]);
+  }
+  return pack8(r);
+}
+
+// raw [64][DP] (rows t0 ..) -> rotated hi / lo padded tiles, 8 columns of each
+// half per item; rows >= L are zero. Optional copies of the rotated rows to
+// global hi / lo [.., DP] from row 0 of the head. cos / sin rows must be
+// 16-byte aligned (their token stride and base: checked by the host).
+template <int DP, typename XT, typename CT>
+__device__ __forceinline__ void rotate_tile(const XT* raw, bf16* hi, bf16* lo, int t0, int L,
+                                            const CT* cs, const CT* sn, long long cs_sl,
+                                            bf16* ghi, bf16* glo) {
+  constexpr int LD = Tile<DP>::LD, HALF = DP / 2, G = HALF / 8;
+  for (int e = threadIdx.x; e < kB * G; e += 128) {
+    const int r = e / G, c = 8 * (e - r * G), t = t0 + r;
+    float o1[8], o2[8];
+    if (t < L) {
+      float x1[8], x2[8], c1[8], c2[8], s1[8], s2[8];
+      load8(raw + (size_t)r * DP + c, x1);
+      load8(raw + (size_t)r * DP + c + HALF, x2);
+      const CT* cr = cs + (size_t)t * cs_sl;
+      const CT* sr = sn + (size_t)t * cs_sl;
+      load8(cr + c, c1);
+      load8(cr + c + HALF, c2);
+      load8(sr + c, s1);
+      load8(sr + c + HALF, s2);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        o1[u] = __fadd_rn(__fmul_rn(x1[u], c1[u]), -__fmul_rn(x2[u], s1[u]));
+        o2[u] = __fadd_rn(__fmul_rn(x2[u], c2[u]), __fmul_rn(x1[u], s2[u]));
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o1[u] = o2[u] = 0.f;
+    }
+    const uint4 h1 = pack8(o1), h2 = pack8(o2);
+    const uint4 l1 = resid8(o1, h1), l2 = resid8(o2, h2);
+    *reinterpret_cast<uint4*>(hi + r * LD + c) = h1;
+    *reinterpret_cast<uint4*>(hi + r * LD + c + HALF) = h2;
+    *reinterpret_cast<uint4*>(lo + r * LD + c) = l1;
+    *reinterpret_cast<uint4*>(lo + r * LD + c + HALF) = l2;
+    if (ghi && t < L) {
+      const size_t g = (size_t)t * DP + c;
+      *reinterpret_cast<uint4*>(ghi + g) = h1;
+      *reinterpret_cast<uint4*>(ghi + g + HALF) = h2;
+      *reinterpret_cast<uint4*>(glo + g) = l1;
+      *reinterpret_cast<uint4*>(glo + g + HALF) = l2;
+    }
+  }
+}
+
+template <int DP, typename XT, typename CT>
+__global__ void __launch_bounds__(128)
+swa_rope_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                    const __grid_constant__ CUtensorMap tv, const CT* __restrict__ cs,
+                    const CT* __restrict__ sn, long long cs_sb, long long cs_sl,
+                    const float* __restrict__ meta, int n_meta, int W, float scale_log2, int H,
+                    int grp, int L, int nqb, bf16* __restrict__ y, float* __restrict__ lse,
+                    float* __restrict__ y32, bf16* __restrict__ qh_out,
+                    bf16* __restrict__ ql_out, bf16* __restrict__ kh_out,
+                    bf16* __restrict__ kl_out) {
+  using SM = RopeSmem<DP, XT>;
+  constexpr int LD = Tile<DP>::LD, NTD = DP / 8, D = DP;
+  extern __shared__ __align__(128) unsigned char smem[];
+  bf16* sQ = reinterpret_cast<bf16*>(smem + SM::q);
+  bf16* sQl = reinterpret_cast<bf16*>(smem + SM::ql);
+  bf16* sK = reinterpret_cast<bf16*>(smem + SM::k);
+  bf16* sKl = reinterpret_cast<bf16*>(smem + SM::kl);
+  bf16* sV = reinterpret_cast<bf16*>(smem + SM::v);
+  const XT* rQ = reinterpret_cast<const XT*>(smem + SM::rq);
+  auto rK = [&](int st) { return reinterpret_cast<XT*>(smem + SM::rk + st * SM::R); };
+  auto rV = [&](int st) { return reinterpret_cast<XT*>(smem + SM::rv + st * SM::R); };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::bars);  // q, stage 0, stage 1
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, cq = lane & 3;
+  const int qb = blockIdx.x % nqb, bh = blockIdx.x / nqb;
+  const int b = bh / H, h = bh - b * H, hk = h / grp;  // key/value head within the row
+  const int q0 = qb * kB;
+  const size_t base = (size_t)bh * L * D;
+  const int Hkv = H / grp;
+  const size_t kbase = ((size_t)b * Hkv + hk) * L * D;
+  const CT* csb = cs + (size_t)b * cs_sb;
+  const CT* snb = sn + (size_t)b * cs_sb;
+  const int lo = max(q0 - W + 1, 0) / kB * kB;
+  const int hi = min(q0 + kB, L);
+  const int nblk = (hi - lo + kB - 1) / kB;
+  if (tid == 0) {
+    tc::mbar_init(&bars[0], 1);
+    tc::mbar_init(&bars[1], 1);
+    tc::mbar_init(&bars[2], 1);
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue_kv = [&](int i) {  // key block i (from lo) into stage i & 1
+    const int st = i & 1;
+    tc::mbar_expect_tx(&bars[1 + st], (uint32_t)(2 * SM::R));
+    tc::tma_load_4d(rK(st), &tk, 0, lo + i * kB, hk, b, &bars[1 + st]);
+    tc::tma_load_4d(rV(st), &tv, 0, lo + i * kB, hk, b, &bars[1 + st]);
+  };
+  if (tid == 0) {
+    tc::mbar_expect_tx(&bars[0], (uint32_t)SM::R);
+    tc::tma_load_4d(const_cast<XT*>(rQ), &tq, 0, q0, h, b, &bars[0]);
+    issue_kv(0);
+    if (nblk > 1) issue_kv(1);
+  }
+
+  // sinks seed the running max / sum (log2 domain)
+  float ms = -1e30f;
+  for (int j = 0; j < n_meta; ++j) ms = fmaxf(ms, meta[j] * kLog2e);
+  float ls = 0.f;
+  for (int j = 0; j < n_meta; ++j) ls += exp2f(meta[j] * kLog2e - ms);
+
+  tc::mbar_wait(&bars[0], 0, 40);
+  rotate_tile<DP, XT, CT>(rQ, sQ, sQl, q0, L, csb, snb, cs_sl,
+                          qh_out ? qh_out + base : nullptr, qh_out ? ql_out + base : nullptr);
+
+  const int i0 = q0 + 16 * warp + gq, i1 = i0 + 8;
+  float m0 = ms, m1 = ms, l0 = ls, l1 = ls;
+  float o[NTD][4];
+#pragma unroll
+  for (int c = 0; c < NTD; ++c)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[c][e] = 0.f;
+  uint32_t qa[DP / 16][4], qla[DP / 16][4];
+
+  for (int it = 0; it < nblk; ++it) {
+    const int st = it & 1, kb = lo + it * kB;
+    tc::mbar_wait(&bars[1 + st], (it >> 1) & 1, 41);
+    const bool writer = kh_out && kb == q0 && h % grp == 0;
+    rotate_tile<DP, XT, CT>(rK(st), sK, sKl, kb, L, csb, snb, cs_sl,
+                            writer ? kh_out + kbase : nullptr, writer ? kl_out + kbase : nullptr);
+    {
+      const XT* rv = rV(st);
+      for (int e = tid; e < kB * D / 8; e += 128) {
+        const int r = e / (D / 8), c = 8 * (e - r * (D / 8));
+        float x[8];
+        load8(rv + (size_t)r * D + c, x);
+        *reinterpret_cast<uint4*>(sV + r * LD + c) = pack8(x);
+      }
+    }
+    __syncthreads();  // tiles ready; the raw stage is free
+    if (tid == 0 && it + 2 < nblk) {
+      tc::fence_proxy_async_smem();
+      issue_kv(it + 2);
+    }
+    if (it == 0) {
+#pragma unroll
+      for (int kk = 0; kk < DP / 16; ++kk) {
+        lda_rm(qa[kk], sQ, LD, 16 * warp, 16 * kk);
+        lda_rm(qla[kk], sQl, LD, 16 * warp, 16 * kk);
+      }
+    }
+    float s[8][4];
+    scores<DP, true>(s, qa, qla, sK, sKl);
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = kb + 8 * nt + 2 * cq + (e & 1);
+        const int i = (e < 2) ? i0 : i1;
+        const float x = in_window(i, t, L, W) ? s[nt][e] * scale_log2 : -INFINITY;
+        s[nt][e] = x;
+        if (e < 2) mx0 = fmaxf(mx0, x); else mx1 = fmaxf(mx1, x);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+    float rs0 = 0.f, rs1 = 0.f;
+    uint32_t pa[4][4], pl[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const float p0 = exp2f(s[nt][0] - mn0), p1 = exp2f(s[nt][1] - mn0);
+      const float p2 = exp2f(s[nt][2] - mn1), p3 = exp2f(s[nt][3] - mn1);
+      rs0 += p0 + p1;
+      rs1 += p2 + p3;
+      const uint32_t h01 = pack_bf16(p0, p1), h23 = pack_bf16(p2, p3);
+      pa[nt >> 1][(nt & 1) * 2 + 0] = h01;
+      pa[nt >> 1][(nt & 1) * 2 + 1] = h23;
+      pl[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16(p0 - bf16_lo(h01), p1 - bf16_hi(h01));
+      pl[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(p2 - bf16_lo(h23), p3 - bf16_hi(h23));
+    }
+    rs0 = quad_sum(rs0);
+    rs1 = quad_sum(rs1);
+    l0 = l0 * al0 + rs0;
+    l1 = l1 * al1 + rs1;
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int c = 0; c < NTD; ++c) {
+      o[c][0] *= al0;
+      o[c][1] *= al0;
+      o[c][2] *= al1;
+      o[c][3] *= al1;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int np = 0; np < NTD / 2; ++np) {
+        uint32_t bb[4];
+        ldb_kn(bb, sV, LD, 16 * j, 16 * np);
+        mma16816(o[2 * np], pa[j], bb[0], bb[1]);
+        mma16816(o[2 * np + 1], pa[j], bb[2], bb[3]);
+        mma16816(o[2 * np], pl[j], bb[0], bb[1]);
+        mma16816(o[2 * np + 1], pl[j], bb[2], bb[3]);
+      }
+    }
+    __syncthreads();  // sK, sKl, sV are rewritten by the next block
+  }
+  const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+#pragma unroll
+  for (int nt = 0; nt < NTD; ++nt) {
+    const int d = 8 * nt + 2 * cq;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int i = hh ? i1 : i0;
+      if (i >= L) continue;
+      const float inv = hh ? inv1 : inv0;
+      const float a = o[nt][2 * hh] * inv, bq = o[nt][2 * hh + 1] * inv;
+      const size_t at = base + (size_t)i * D + d;
+      *reinterpret_cast<__nv_bfloat162*>(y + at) = __floats2bfloat162_rn(a, bq);
+      if (y32) *reinterpret_cast<float2*>(y32 + at) = make_float2(a, bq);
+    }
+  }
+  if (lse && cq == 0) {
+    if (i0 < L) lse[(size_t)bh * L + i0] = m0 * kLn2 + logf(l0);
+    if (i1 < L) lse[(size_t)bh * L + i1] = m1 * kLn2 + logf(l1);
+  }
+}
+
 template <int DP, bool SPLIT>
 int launch_swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
                    const float* meta, int n_meta, int W, int BH, int H, int grp, int L, int D,
@@ -674,6 +964,54 @@ int launch_swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, 
   return check_launch("swa_bwd_dkv_kernel");
 }
 
+// [B, Hx, L, D] at element strides (sb, sh, sl, 1) as a 4-D map {D, L, Hx, B},
+// box {D, 64, 1, 1} (one 64-row tile of one head), zero fill past L.
+bool make_rope_map(CUtensorMap* m, const void* ptr, int x_dtype, int D, int L, int Hx, int B,
+                   long long sb, long long sh, long long sl) {
+  tc::EncodeTiledFn fn = tc::encode_tiled_fn();
+  if (!fn) return false;
+  const long long es = x_dtype == LZ_DTYPE_F32 ? 4 : 2;
+  if (Hx == 1) sh = (long long)L * sl;  // strides of size-1 dims are not used; keep them legal
+  if (B == 1) sb = (long long)Hx * sh;
+  if (!aligned16(ptr) || sl <= 0 || sh <= 0 || sb <= 0 || (sl * es) % 16 || (sh * es) % 16 ||
+      (sb * es) % 16 || (D * es) % 16)
+    return false;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)L, (cuuint64_t)Hx, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)(sl * es), (cuuint64_t)(sh * es), (cuuint64_t)(sb * es)};
+  cuuint32_t box[4] = {(cuuint32_t)D, (cuuint32_t)kB, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(m, x_dtype == LZ_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                       : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+            4, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int DP, typename XT, typename CT>
+int launch_swa_rope(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st) {
+  using SM = RopeSmem<DP, XT>;
+  if (SM::bytes > 227 * 1024) return LZ_ERR_UNSUPPORTED;
+  const long long ces = a.cs_dtype == LZ_DTYPE_F32 ? 4 : 2;
+  if (!aligned16(a.cos) || !aligned16(a.sin) || (a.cs_sl * ces) % 16 || (a.cs_sb * ces) % 16)
+    return LZ_ERR_UNSUPPORTED;  // the rotation reads cos / sin rows with 16-byte loads
+  CUtensorMap mq, mk, mv;
+  if (!make_rope_map(&mq, a.q, a.x_dtype, DP, a.L, a.H, a.B, a.q_sb, a.q_sh, a.q_sl) ||
+      !make_rope_map(&mk, a.k, a.x_dtype, DP, a.L, a.Hkv, a.B, a.k_sb, a.k_sh, a.k_sl) ||
+      !make_rope_map(&mv, a.v, a.x_dtype, DP, a.L, a.Hkv, a.B, a.v_sb, a.v_sh, a.v_sl))
+    return LZ_ERR_UNSUPPORTED;
+  static bool done[64] = {false};
+  int rc = ensure_smem_swa(swa_rope_fwd_kernel<DP, XT, CT>, SM::bytes, done);
+  if (rc) return rc;
+  const int nqb = ceil_div(a.L, kB);
+  const float scale_log2 = kLog2e / sqrtf((float)DP);
+  swa_rope_fwd_kernel<DP, XT, CT><<<(unsigned)((long long)a.B * a.H * nqb), 128, SM::bytes, st>>>(
+      mq, mk, mv, static_cast<const CT*>(a.cos), static_cast<const CT*>(a.sin), a.cs_sb, a.cs_sl,
+      a.meta, a.n_meta, a.window, scale_log2, a.H, a.H / a.Hkv, a.L, nqb, a.y, sv.lse, sv.y32,
+      a.q_hi, a.q_lo, a.k_hi, a.k_lo);
+  count_launches(1);
+  return check_launch("swa_rope_fwd_kernel");
+}
+
 }  // namespace
 
 int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
@@ -694,6 +1032,20 @@ int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const b
 #undef LZ_SWA_FWD
   set_error("swa_fwd: head dim above 128 is not supported");
   return LZ_ERR_UNSUPPORTED;
+}
+
+int swa_rope_fwd(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st) {
+  const bool f32 = a.x_dtype == LZ_DTYPE_F32, cf32 = a.cs_dtype == LZ_DTYPE_F32;
+#define LZ_ROPE(dp)                                                                          \
+  if (a.D == dp) {                                                                           \
+    if (f32) return cf32 ? launch_swa_rope<dp, float, float>(a, sv, st)                     \
+                         : launch_swa_rope<dp, float, bf16>(a, sv, st);                     \
+    return cf32 ? launch_swa_rope<dp, bf16, float>(a, sv, st)                               \
+                : launch_swa_rope<dp, bf16, bf16>(a, sv, st);                               \
+  }
+  LZ_ROPE(32) LZ_ROPE(64) LZ_ROPE(128)
+#undef LZ_ROPE
+  return LZ_ERR_UNSUPPORTED;  // other head dims: rotate first (lz_rope_split) and lz_swa_fwd_gqa
 }
 
 int swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,

@@ -47,6 +47,25 @@ inline size_t swa_work_layout(int B, int H, int L, int n_meta, unsigned char* ba
   return total;
 }
 
+// Arguments of the SWA forward with RoPE inside (lz_swa_rope_fwd).
+struct SwaRopeArgs {
+  const void *q, *k, *v;  // unrotated, x_dtype, element strides (batch, head, token)
+  int x_dtype;
+  long long q_sb, q_sh, q_sl, k_sb, k_sh, k_sl, v_sb, v_sh, v_sl;
+  const void *cos, *sin;  // [B or broadcast, L, D], cs_dtype
+  int cs_dtype;
+  long long cs_sb, cs_sl;
+  const float* meta;
+  int n_meta, window;
+  bf16* y;
+  bf16 *q_hi, *q_lo, *k_hi, *k_lo;  // optional rotated operands for the backward
+  int B, H, Hkv, L, D;
+};
+
+// LZ_ERR_UNSUPPORTED (without launching) when the TMA tiles cannot take the
+// shape or strides.
+int swa_rope_fwd(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st);
+
 int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
             const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B, int H,
             int Hkv, int L, int D, cudaStream_t st);

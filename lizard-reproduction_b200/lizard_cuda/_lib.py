@@ -16,6 +16,7 @@ HEADER = Path(__file__).resolve().parents[2] / "include" / "lizard_cuda.h"
 
 LZ_DTYPE_F32 = 0
 LZ_DTYPE_BF16 = 1
+LZ_ERR_UNSUPPORTED = 2
 
 _c_int, _c_size, _vp = ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p
 _SIGNATURES = {
@@ -32,6 +33,7 @@ _SIGNATURES = {
     "lz_gla_bwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _c_size, _vp, _vp, _vp, _vp, _c_int,
                             _vp, _vp, _c_size] + [_c_int] * 6 + [_vp]),
     "lz_gla_bwd_gqa_workspace_bytes": (_c_size, [_c_int] * 7),
+    "lz_gla_fwd_gqa_workspace_bytes": (_c_size, [_c_int] * 9),
     "lz_gla_fwd_gqa": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_size, _vp, _c_size]
                        + [_c_int] * 7 + [_vp]),
     "lz_gla_bwd_gqa": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _c_size, _vp, _vp, _vp, _vp,
@@ -65,6 +67,11 @@ _SIGNATURES = {
     "lz_swa_decode": (_c_int, [_vp, _vp, _vp, _c_int] + [ctypes.c_longlong] * 6 + [_vp, _vp, _c_int, ctypes.c_longlong,
                                                                      _vp, _vp, _vp, _vp, _c_int,
                                                                      _vp] + [_c_int] * 5 + [_vp]),
+    "lz_swa_rope_fwd": (_c_int, [_vp, _vp, _vp, _c_int] + [ctypes.c_longlong] * 9 + [_vp, _vp, _c_int, ctypes.c_longlong,
+                                                                     ctypes.c_longlong, _vp, _c_int, _c_int,
+                                                                     _vp, _vp, _c_size, _vp, _vp,
+                                                                     _vp, _vp] + [_c_int] * 5
+                        + [_vp]),
     "lz_swa_saved_bytes": (_c_size, [_c_int] * 4),
     "lz_swa_bwd_workspace_bytes": (_c_size, [_c_int] * 5),
     "lz_swa_fwd": (_c_int, [_vp] * 6 + [_c_int, _c_int, _vp, _vp, _c_size] + [_c_int] * 4

@@ -51,7 +51,8 @@ class _GLA(torch.autograd.Function):
         if save:
             nbytes = lib.lz_gla_saved_bytes(B, H, L, F, D, chunk)
             saved = torch.empty(nbytes, device=v.device, dtype=torch.uint8)
-        wbytes = lib.lz_gla_fwd_workspace_bytes(B, H, L, F, D, chunk)
+        wbytes = lib.lz_gla_fwd_gqa_workspace_bytes(B, H, Hkv, L, F, D, chunk, per_head,
+                                                    int(save))
         ws = torch.empty(wbytes, device=v.device, dtype=torch.uint8) if wbytes else None
         with torch.cuda.device(v.device):
             rc = lib.lz_gla_fwd_gqa(_lib.ptr(fq), _lib.ptr(fk), _lib.ptr(v), _lib.ptr(lg),

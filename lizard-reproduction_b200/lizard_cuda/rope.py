@@ -8,7 +8,10 @@ reads the unrotated q and k (any batch / head / token strides, so the
 projection output [B, L, H * Dh] is read in place as [B, H, L, Dh]), rotates
 them in fp32 and writes the bf16 value and bf16 residual pair the SWA kernels
 take (about 16 mantissa bits of each rotated element, as swa() keeps for fp32
-inputs). k and v may carry fewer heads than q (GQA). The backward runs the SWA
+inputs). k and v may carry fewer heads than q (GQA). The forward is one
+kernel (lz_swa_rope_fwd: TMA tiles of q, k, v, rotation inside the CTA); for
+head dims or strides its TMA tiles cannot take it rotates first (lz_rope_split)
+and calls the SWA forward, with the same results. The backward runs the SWA
 backward and then the transpose rotation, dx = R^T dr, in one more pass.
 
     swa_rope(q, k, v, cos, sin, meta, window)
@@ -75,6 +78,49 @@ def rope_grad(dr, cos, sin, csb, csl, dtype):
     return dx.to(dtype)
 
 
+def _fused_forward(q, k, v, cos, sin, csb, csl, meta32, window, y, saved, rot):
+    """One kernel: TMA tiles of the unrotated q, k, v, rotation and split in the
+    CTA, the SWA forward. rot = (q_hi, q_lo, k_hi, k_lo) to fill for the
+    backward, or None. Returns False (nothing launched) when the head dim or the
+    strides are outside the kernel's TMA tiles."""
+    B, H, L, D = q.shape
+    Hkv = k.shape[1]
+    xdt = q.dtype if q.dtype in _DT else torch.float32
+    q, k, v = (_as_input(t.to(xdt)) for t in (q, k, v))
+    lib = _lib.load()
+    n_meta = meta32.numel()
+    rp = [_lib.ptr(t) for t in rot] if rot is not None else [None] * 4
+    rc = lib.lz_swa_rope_fwd(_lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _DT[xdt], q.stride(0),
+                             q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
+                             v.stride(0), v.stride(1), v.stride(2), _lib.ptr(cos), _lib.ptr(sin),
+                             _DT[cos.dtype], csb, csl, _lib.ptr(meta32) if n_meta else None,
+                             n_meta, window, _lib.ptr(y), _lib.ptr(saved),
+                             0 if saved is None else saved.numel(), *rp, B, H, Hkv, L, D,
+                             _lib.stream_of(q))
+    if rc == _lib.LZ_ERR_UNSUPPORTED:
+        return False
+    _lib.check(rc, "swa_rope forward")
+    return True
+
+
+def _two_pass_forward(q, k, v, cos, sin, csb, csl, meta32, window, y, saved):
+    """lz_rope_split on q and k, then lz_swa_fwd_gqa. Returns (q_hi, q_lo, k_hi, k_lo)."""
+    B, H, L, D = q.shape
+    Hkv = k.shape[1]
+    q_hi, q_lo = rope_split(_as_input(q), cos, sin, csb, csl)
+    k_hi, k_lo = rope_split(_as_input(k), cos, sin, csb, csl)
+    v16 = v.to(torch.bfloat16).contiguous()
+    lib = _lib.load()
+    n_meta = meta32.numel()
+    rc = lib.lz_swa_fwd_gqa(_lib.ptr(q_hi), _lib.ptr(k_hi), _lib.ptr(v16), _lib.ptr(q_lo),
+                            _lib.ptr(k_lo), _lib.ptr(meta32) if n_meta else None, n_meta,
+                            window, _lib.ptr(y), _lib.ptr(saved),
+                            0 if saved is None else saved.numel(), B, H, Hkv, L, D,
+                            _lib.stream_of(q))
+    _lib.check(rc, "swa_rope forward")
+    return q_hi, q_lo, k_hi, k_lo
+
+
 class _SWARope(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, cos, sin, meta, window):
@@ -92,28 +138,24 @@ class _SWARope(torch.autograd.Function):
             raise ValueError(f"the rotated head dim must be even, got {D}")
         ctx.dtypes = (q.dtype, k.dtype, v.dtype, meta.dtype)
         cos, sin, csb, csl = _tables(cos, sin, B, L, D)
-        q_hi, q_lo = rope_split(_as_input(q), cos, sin, csb, csl)
-        k_hi, k_lo = rope_split(_as_input(k), cos, sin, csb, csl)
-        v16 = v.to(torch.bfloat16).contiguous()
         meta32 = meta.float().contiguous()
-        n_meta = meta32.numel()
         lib = _lib.load()
         y = torch.empty(B, H, L, D, device=q.device, dtype=torch.bfloat16)
         save = any(ctx.needs_input_grad[:3]) or ctx.needs_input_grad[5]
-        saved = None
+        saved = rot = None
         if save:
             saved = torch.empty(lib.lz_swa_saved_bytes(B, H, L, D), device=q.device,
                                 dtype=torch.uint8)
+            rot = tuple(torch.empty(B, n, L, D, device=q.device, dtype=torch.bfloat16)
+                        for n in (H, H, Hkv, Hkv))
         with torch.cuda.device(q.device):
-            rc = lib.lz_swa_fwd_gqa(_lib.ptr(q_hi), _lib.ptr(k_hi), _lib.ptr(v16),
-                                    _lib.ptr(q_lo), _lib.ptr(k_lo),
-                                    _lib.ptr(meta32) if n_meta else None, n_meta, int(window),
-                                    _lib.ptr(y), _lib.ptr(saved),
-                                    0 if saved is None else saved.numel(), B, H, Hkv, L, D,
-                                    _lib.stream_of(q))
-        _lib.check(rc, "swa_rope forward")
+            if not _fused_forward(q, k, v, cos, sin, csb, csl, meta32, int(window), y, saved,
+                                  rot):
+                rot = _two_pass_forward(q, k, v, cos, sin, csb, csl, meta32, int(window), y,
+                                        saved)
         if save:
-            ctx.save_for_backward(q_hi, q_lo, k_hi, k_lo, v16, meta32, saved, cos, sin)
+            v16 = v.to(torch.bfloat16).contiguous()
+            ctx.save_for_backward(*rot, v16, meta32, saved, cos, sin)
             ctx.tables = (csb, csl)
         ctx.window = int(window)
         return y

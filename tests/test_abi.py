@@ -74,6 +74,18 @@ def test_gqa_entries_validate_head_counts(lib):
     assert lib.lz_gla_bwd_gqa_workspace_bytes(2, 8, 3, 256, 64, 64, 64) == 0
 
 
+def test_forward_workspace_plans_shared_states(lib):
+    # F = 256 runs the chunk-parallel schedule; without a saved buffer and with a
+    # gate shared by the heads, its states are per key/value head
+    B, H, Hkv, L, F, D = 4, 32, 8, 1024, 256, 64
+    per_q = lib.lz_gla_fwd_gqa_workspace_bytes(B, H, Hkv, L, F, D, 64, 0, 1)
+    shared = lib.lz_gla_fwd_gqa_workspace_bytes(B, H, Hkv, L, F, D, 64, 0, 0)
+    assert per_q == lib.lz_gla_fwd_workspace_bytes(B, H, L, F, D, 64) > 0
+    assert per_q >= 4 * (shared - 4096) and shared >= B * Hkv * (L // 64) * F * D * 4
+    assert lib.lz_gla_fwd_gqa_workspace_bytes(B, H, Hkv, L, F, D, 64, 1, 0) == per_q
+    assert lib.lz_gla_fwd_gqa_workspace_bytes(B, H, 3, L, F, D, 64, 0, 0) == 0
+
+
 def test_rope_entries_validate(lib):
     p = _fake(4)
     # odd head dim cannot be rotated in halves

@@ -225,3 +225,88 @@ def test_swa_rope_matches_oracle(H, Hkv, xdt):
     for t, r, n in zip((qp_, kp_, v_, meta_), lv, ("dq", "dk", "dv", "dmeta")):
         assert t.grad.dtype == t.dtype
         assert_grad(t.grad.float(), r.grad, f"{what} {n}")
+
+
+@pytest.mark.parametrize("schedule", ["walk", "split"])
+@pytest.mark.parametrize("shape", [(2, 8, 2, 300, 64, 64), (1, 4, 1, 200, 256, 64)])
+def test_gla_gqa_inference_shared_gate(schedule, shape):
+    """Without autograd and with a gate shared by the heads, the chunk-parallel
+    schedule keeps one state per key/value head (the query heads of a group
+    have identical states): the output matches the oracle under both schedules."""
+    import lizard_cuda
+    from lizard_cuda import _lib
+    B, H, Hkv, L, F, D = shape
+    fq, fk, v, lg, _ = _gla_inputs(B, H, Hkv, L, F, D, 0, seed=L + F)
+    prev = _lib.set_schedule(schedule)
+    try:
+        with torch.no_grad():
+            y = lizard_cuda.gla(fq, fk, v, lg)
+    finally:
+        _lib.set_schedule(prev)
+    ref = orc.gla(fq.double().cpu(), _rep(fk, H // Hkv).double().cpu(),
+                  _rep(v, H // Hkv).double().cpu(), lg.double().cpu())
+    assert_output(y, ref.float(), f"gla gqa inference {shape} {schedule}")
+
+
+@pytest.mark.parametrize("D,xdt,csdt,H,Hkv,W,L", [
+    (64, torch.bfloat16, torch.bfloat16, 4, 2, 64, 200),
+    (64, torch.float32, torch.float32, 4, 4, 16, 130),
+    (128, torch.bfloat16, torch.float32, 2, 1, 100, 257),
+    (32, torch.float32, torch.bfloat16, 4, 2, 200, 64),
+])
+def test_swa_rope_fused_equals_two_pass(D, xdt, csdt, H, Hkv, W, L):
+    """The one-kernel forward (TMA tiles of the unrotated projections, rotation
+    and split inside the CTA) equals rotating first and calling the SWA forward:
+    the same output, saved buffer and rotated operands, bit for bit."""
+    from lizard_cuda import _lib
+    from lizard_cuda.rope import _fused_forward, _tables, _two_pass_forward
+    lib = _lib.load()
+    g = torch.Generator(device=DEV).manual_seed(D + L)
+    B = 2
+    qp = torch.randn(B, L, H * D, generator=g, device=DEV).to(xdt)
+    kp = torch.randn(B, L, Hkv * D, generator=g, device=DEV).to(xdt)
+    vp = torch.randn(B, L, Hkv * D, generator=g, device=DEV).to(xdt)
+    q = qp.view(B, L, H, D).transpose(1, 2)
+    k = kp.view(B, L, Hkv, D).transpose(1, 2)
+    v = vp.view(B, L, Hkv, D).transpose(1, 2)
+    meta = torch.randn(4, generator=g, device=DEV)
+    cos, sin = (t.to(DEV).to(csdt).expand(B, L, D) for t in orc.rotary_tables(L, D, 5e5))
+    c, s, csb, csl = _tables(cos, sin, B, L, D)
+    outs = []
+    for fused in (True, False):
+        y = torch.empty(B, H, L, D, device=DEV, dtype=torch.bfloat16)
+        # zeroed: the alignment padding inside the buffer is written by neither path
+        saved = torch.zeros(lib.lz_swa_saved_bytes(B, H, L, D), device=DEV, dtype=torch.uint8)
+        if fused:
+            rot = tuple(torch.empty(B, n, L, D, device=DEV, dtype=torch.bfloat16)
+                        for n in (H, H, Hkv, Hkv))
+            assert _fused_forward(q, k, v, c, s, csb, csl, meta, W, y, saved, rot)
+        else:
+            rot = _two_pass_forward(q, k, v, c, s, csb, csl, meta, W, y, saved)
+        outs.append((y, saved, rot))
+    (y1, s1, r1), (y2, s2, r2) = outs
+    assert torch.equal(y1, y2)
+    assert torch.equal(s1, s2)
+    for a, b_ in zip(r1, r2):
+        assert torch.equal(a, b_)
+
+
+@pytest.mark.parametrize("D,xdt", [(20, torch.bfloat16), (128, torch.float32)])
+def test_swa_rope_fused_declines_shapes_outside_its_tiles(D, xdt):
+    """Head dims outside {32, 64, 128}, or tiles that do not fit in shared memory
+    (fp32 at D = 128), are declined without a launch; swa_rope then rotates first."""
+    import lizard_cuda
+    from lizard_cuda.rope import _fused_forward, _tables
+    B, H, L = 1, 2, 100
+    g = torch.Generator(device=DEV).manual_seed(D)
+    q, k, v = (torch.randn(B, H, L, D, generator=g, device=DEV).to(xdt) for _ in range(3))
+    meta = torch.randn(2, generator=g, device=DEV)
+    cos, sin = (t.to(DEV) for t in orc.rotary_tables(L, D, 1e4))
+    c, s, csb, csl = _tables(cos, sin, B, L, D)
+    y = torch.empty(B, H, L, D, device=DEV, dtype=torch.bfloat16)
+    assert not _fused_forward(q, k, v, c, s, csb, csl, meta, 16, y, None, None)
+    out = lizard_cuda.swa_rope(q, k, v, cos, sin, meta, 16)
+    qr, kr = orc.rope(q.double().cpu(), cos.double().cpu(), sin.double().cpu()), \
+        orc.rope(k.double().cpu(), cos.double().cpu(), sin.double().cpu())
+    ref = orc.awa(qr, kr, v.double().cpu(), meta.double().cpu(), 16)
+    assert_output(out, ref.float(), f"swa_rope two-pass D={D}")
