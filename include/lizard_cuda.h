@@ -242,6 +242,19 @@ int lz_hedgehog_bwd(const void* x, int x_dtype, const float* weight, const void*
                     int df_dtype, float* dx, float* dweight, void* workspace,
                     size_t workspace_bytes, int R, int Dh, int Fd, void* stream);
 
+/* The same for x [B, Hx, L, Dh] at element strides (x_sb, x_sh, x_sl) with Dh
+ * contiguous, e.g. a projection output [B, L, Hx * Dh] read in place as heads
+ * (x_sb = L * Hx * Dh, x_sh = Dh, x_sl = Hx * Dh). R = B * Hx * L rows in
+ * (batch, head, token) order; f, df and dx are contiguous [R, ...]. */
+int lz_hedgehog_fwd_strided(const void* x, int x_dtype, long long x_sb, long long x_sh,
+                            long long x_sl, int B, int Hx, int L, const float* weight, void* f,
+                            int Dh, int Fd, void* stream);
+int lz_hedgehog_bwd_strided(const void* x, int x_dtype, long long x_sb, long long x_sh,
+                            long long x_sl, int B, int Hx, int L, const float* weight,
+                            const void* df, int df_dtype, float* dx, float* dweight,
+                            void* workspace, size_t workspace_bytes, int Dh, int Fd,
+                            void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Rotary embedding for the SWA operands (no counterpart in the reference's   */
 /* kernels: its caller rotates with torch ops, src/lizard_attention.py:87-88, */

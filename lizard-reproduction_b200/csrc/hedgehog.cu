@@ -70,6 +70,31 @@ __device__ __forceinline__ void split_tile(bf16* hi, bf16* lo, int lds, const T*
   }
 }
 
+// Row r of x (r over the B*H*L rows in (batch, head, token) order) starts at
+// element b*sb + h*sh + t*sl, so a projection output [B, L, H*Dh] is read in
+// place as [B, H, L, Dh]; a contiguous [R, Dh] x is H = 1, L = R, sl = Dh.
+struct XRows {
+  int H, L;
+  long long sb, sh, sl;
+  __host__ __device__ __forceinline__ size_t off(long long r) const {
+    const long long t = r % L, bh = r / L;
+    return (size_t)((bh / H) * sb + (bh % H) * sh + t * sl);
+  }
+};
+
+// rows x cols of x -> bf16 hi / lo tiles, zero padded
+template <typename T, int ROWS, int COLS>
+__device__ __forceinline__ void split_rows(bf16* hi, bf16* lo, int lds, const T* g,
+                                           const XRows& m, int r0, int nrows, int ncols) {
+  for (int i = threadIdx.x; i < ROWS * COLS; i += kT) {
+    const int r = i / COLS, c = i % COLS;
+    const float x = (r0 + r < nrows && c < ncols) ? ld_f<T>(g, m.off(r0 + r) + c) : 0.f;
+    const bf16 h = __float2bfloat16_rn(x);
+    hi[r * lds + c] = h;
+    lo[r * lds + c] = __float2bfloat16_rn(x - __bfloat162float(h));
+  }
+}
+
 // Vector loads of one 64-row tile of x (fp32 or bf16) into registers,
 // 16 bytes per load, zero beyond R; stored to the hi / lo tiles afterwards.
 template <typename XT, int DHP>
@@ -78,13 +103,13 @@ struct XTile {
   static constexpr int VPR = DHP / EPV;
   static constexpr int NV = (kR * VPR + kT - 1) / kT;
   uint4 v[NV];
-  __device__ __forceinline__ void load(const XT* x, int r0, int R, int Dh) {
+  __device__ __forceinline__ void load(const XT* x, const XRows& m, int r0, int R, int Dh) {
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int i = threadIdx.x + kT * k;
       const int r = i / VPR, c = (i % VPR) * EPV;
       v[k] = (i < kR * VPR && r0 + r < R && c < Dh)
-                 ? *reinterpret_cast<const uint4*>(x + (size_t)(r0 + r) * Dh + c)
+                 ? *reinterpret_cast<const uint4*>(x + m.off(r0 + r) + c)
                  : make_uint4(0u, 0u, 0u, 0u);
     }
   }
@@ -245,8 +270,8 @@ __device__ __forceinline__ void softmaxes(float (&acc)[FDP / 16][4], float (&pm)
 
 template <typename XT, int DHP, int FDP, bool FULL>
 __global__ void __launch_bounds__(kT)
-hedgehog_fwd_kernel(const XT* __restrict__ x, const float* __restrict__ w, int R, int Dh, int Fd,
-                    int vec, bf16* __restrict__ f) {
+hedgehog_fwd_kernel(const XT* __restrict__ x, XRows xm, const float* __restrict__ w, int R,
+                    int Dh, int Fd, int vec, bf16* __restrict__ f) {
   using SM = HhSmem<DHP, FDP>;
   constexpr int NTH = FDP / 16;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -263,16 +288,16 @@ hedgehog_fwd_kernel(const XT* __restrict__ x, const float* __restrict__ w, int R
   const int ntiles = (R + kR - 1) / kR;
   const int F2 = 2 * Fd;
   XTile<XT, DHP> xt;
-  if (vec && (int)blockIdx.x < ntiles) xt.load(x, blockIdx.x * kR, R, Dh);
+  if (vec && (int)blockIdx.x < ntiles) xt.load(x, xm, blockIdx.x * kR, R, Dh);
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const int r0 = tile * kR;
     __syncthreads();  // the previous tile's x is consumed; W is staged
     if (vec)
       xt.store(xh, xl, SM::LDX);
     else
-      split_tile<XT, kR, DHP>(xh, xl, SM::LDX, x, Dh, r0, R, Dh);
+      split_rows<XT, kR, DHP>(xh, xl, SM::LDX, x, xm, r0, R, Dh);
     __syncthreads();
-    if (vec && tile + (int)gridDim.x < ntiles) xt.load(x, r0 + gridDim.x * kR, R, Dh);
+    if (vec && tile + (int)gridDim.x < ntiles) xt.load(x, xm, r0 + gridDim.x * kR, R, Dh);
     float acc[NTH][4], pm[NTH][4];
     logits<DHP, FDP, sizeof(XT) == 4>(acc, xh, xl, wh, wl, rb, c0);
     softmaxes<FDP, FULL>(acc, pm, c0, Fd, red, half, lrow);
@@ -380,7 +405,8 @@ __device__ __forceinline__ void load_df(float2 (&pr)[NTH][2], const GT* __restri
 template <typename XT, typename GT, int DHP, int FDP, bool FULL>
 __global__ void __launch_bounds__(kT)
 hedgehog_bwd_kernel(const XT* __restrict__ x, const float* __restrict__ w,
-                    const GT* __restrict__ df, int R, int Dh, int Fd, int vec, int vec_df,
+                    const GT* __restrict__ df, XRows xm, int R, int Dh, int Fd, int vec,
+                    int vec_df,
                     float* __restrict__ dx, float* __restrict__ dw_part) {
   using SM = HhSmem<DHP, FDP>;
   constexpr int NTH = FDP / 16;
@@ -409,16 +435,16 @@ hedgehog_bwd_kernel(const XT* __restrict__ x, const float* __restrict__ w,
   const int ntiles = (R + kR - 1) / kR;
   const int F2 = 2 * Fd;
   XTile<XT, DHP> xt;
-  if (vec && (int)blockIdx.x < ntiles) xt.load(x, blockIdx.x * kR, R, Dh);
+  if (vec && (int)blockIdx.x < ntiles) xt.load(x, xm, blockIdx.x * kR, R, Dh);
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const int r0 = tile * kR;
     __syncthreads();
     if (vec)
       xt.store(xh, xl, SM::LDX);
     else
-      split_tile<XT, kR, DHP>(xh, xl, SM::LDX, x, Dh, r0, R, Dh);
+      split_rows<XT, kR, DHP>(xh, xl, SM::LDX, x, xm, r0, R, Dh);
     __syncthreads();
-    if (vec && tile + (int)gridDim.x < ntiles) xt.load(x, r0 + gridDim.x * kR, R, Dh);
+    if (vec && tile + (int)gridDim.x < ntiles) xt.load(x, xm, r0 + gridDim.x * kR, R, Dh);
     float acc[NTH][4], pm[NTH][4];
     logits<DHP, FDP, sizeof(XT) == 4>(acc, xh, xl, wh, wl, rb, c0);
     softmaxes<FDP, FULL>(acc, pm, c0, Fd, red, half, lrow);
@@ -613,39 +639,46 @@ int hh_grid(int R) {
   return std::max(1, std::min(ntiles, sm_count() * 2));
 }
 
+// 16-byte x loads need every row start 16-byte aligned
+bool rows_vec(const void* x, const XRows& m, int Dh, int es) {
+  return Dh % (16 / es) == 0 && aligned16(x) && (m.sl * es) % 16 == 0 &&
+         (m.sh * es) % 16 == 0 && (m.sb * es) % 16 == 0;
+}
+
 template <typename XT, int DHP, int FDP, bool FULL>
-int launch_fwd_t(const void* x, const float* w, int R, int Dh, int Fd, int xs, int ws, bf16* f,
+int launch_fwd_t(const void* x, const XRows& xm, const float* w, int R, int Dh, int Fd, bf16* f,
                  cudaStream_t st) {
   using SM = HhSmem<DHP, FDP>;
   static bool done[64] = {false};
   int rc = hh_attr(hedgehog_fwd_kernel<XT, DHP, FDP, FULL>, SM::fwd_bytes, done);
   if (rc) return rc;
-  const int vec = (Dh % (16 / (int)sizeof(XT)) == 0) && aligned16(x) && aligned16(f);
+  const int vec = rows_vec(x, xm, Dh, (int)sizeof(XT)) && aligned16(f);
   hedgehog_fwd_kernel<XT, DHP, FDP, FULL><<<hh_grid(R), kT, SM::fwd_bytes, st>>>(
-      static_cast<const XT*>(x), w, R, Dh, Fd, vec, f);
+      static_cast<const XT*>(x), xm, w, R, Dh, Fd, vec, f);
   count_launches(1);
   return check_launch("hedgehog_fwd_kernel");
 }
 template <typename XT, int DHP, int FDP>
-int launch_fwd(const void* x, const float* w, int R, int Dh, int Fd, int xs, int ws, bf16* f,
+int launch_fwd(const void* x, const XRows& xm, const float* w, int R, int Dh, int Fd, bf16* f,
                cudaStream_t st) {
-  return Fd == FDP ? launch_fwd_t<XT, DHP, FDP, true>(x, w, R, Dh, Fd, xs, ws, f, st)
-                   : launch_fwd_t<XT, DHP, FDP, false>(x, w, R, Dh, Fd, xs, ws, f, st);
+  return Fd == FDP ? launch_fwd_t<XT, DHP, FDP, true>(x, xm, w, R, Dh, Fd, f, st)
+                   : launch_fwd_t<XT, DHP, FDP, false>(x, xm, w, R, Dh, Fd, f, st);
 }
 
 template <typename XT, typename GT, int DHP, int FDP, bool FULL>
-int launch_bwd_t(const void* x, const float* w, const void* df, int R, int Dh, int Fd, int xs,
-                 int ws, float* dx, float* dw, void* work, cudaStream_t st) {
+int launch_bwd_t(const void* x, const XRows& xm, const float* w, const void* df, int R, int Dh,
+                 int Fd, float* dx, float* dw, void* work, cudaStream_t st) {
   using SM = HhSmem<DHP, FDP>;
   static bool done[64] = {false};
   int rc = hh_attr(hedgehog_bwd_kernel<XT, GT, DHP, FDP, FULL>, SM::bwd_bytes, done);
   if (rc) return rc;
   const int grid = hh_grid(R);
-  const int vec = (Dh % (16 / (int)sizeof(XT)) == 0) && aligned16(x);
+  const int vec = rows_vec(x, xm, Dh, (int)sizeof(XT));
   const int vec_df = (Fd % 8 == 0) && aligned16(df);
   float* part = static_cast<float*>(work);
   hedgehog_bwd_kernel<XT, GT, DHP, FDP, FULL><<<grid, kT, SM::bwd_bytes, st>>>(
-      static_cast<const XT*>(x), w, static_cast<const GT*>(df), R, Dh, Fd, vec, vec_df, dx, part);
+      static_cast<const XT*>(x), w, static_cast<const GT*>(df), xm, R, Dh, Fd, vec, vec_df, dx,
+      part);
   count_launches(1);
   rc = check_launch("hedgehog_bwd_kernel");
   if (rc) return rc;
@@ -655,11 +688,11 @@ int launch_bwd_t(const void* x, const float* w, const void* df, int R, int Dh, i
   return check_launch("hedgehog_dw_reduce_kernel");
 }
 template <typename XT, typename GT, int DHP, int FDP>
-int launch_bwd(const void* x, const float* w, const void* df, int R, int Dh, int Fd, int xs,
-               int ws, float* dx, float* dw, void* work, cudaStream_t st) {
+int launch_bwd(const void* x, const XRows& xm, const float* w, const void* df, int R, int Dh,
+               int Fd, float* dx, float* dw, void* work, cudaStream_t st) {
   return Fd == FDP
-             ? launch_bwd_t<XT, GT, DHP, FDP, true>(x, w, df, R, Dh, Fd, xs, ws, dx, dw, work, st)
-             : launch_bwd_t<XT, GT, DHP, FDP, false>(x, w, df, R, Dh, Fd, xs, ws, dx, dw, work, st);
+             ? launch_bwd_t<XT, GT, DHP, FDP, true>(x, xm, w, df, R, Dh, Fd, dx, dw, work, st)
+             : launch_bwd_t<XT, GT, DHP, FDP, false>(x, xm, w, df, R, Dh, Fd, dx, dw, work, st);
 }
 
 }  // namespace
@@ -670,8 +703,8 @@ size_t hedgehog_bwd_workspace(int R, int Dh, int Fd) {
   return (size_t)hh_grid(R) * fdp * dhp * 4;
 }
 
-int hedgehog_fwd(const void* x, int x_dtype, const float* w, int R, int Dh, int Fd, bf16* f,
-                 cudaStream_t st) {
+int hedgehog_fwd(const void* x, int x_dtype, const XRows& xm, const float* w, int R, int Dh,
+                 int Fd, bf16* f, cudaStream_t st) {
   int dhp, fdp;
   if (dims_pad(Dh, Fd, &dhp, &fdp)) {
     set_error("hedgehog: head dim and feature dim must be <= 128");
@@ -680,8 +713,8 @@ int hedgehog_fwd(const void* x, int x_dtype, const float* w, int R, int Dh, int 
   const int xs = x_dtype == LZ_DTYPE_F32;
 #define LZ_HH_FWD(dh, fd)                                                                 \
   if (dhp == dh && fdp == fd)                                                             \
-    return xs ? launch_fwd<float, dh, fd>(x, w, R, Dh, Fd, 1, 1, f, st)                   \
-              : launch_fwd<bf16, dh, fd>(x, w, R, Dh, Fd, 0, 1, f, st);
+    return xs ? launch_fwd<float, dh, fd>(x, xm, w, R, Dh, Fd, f, st)                     \
+              : launch_fwd<bf16, dh, fd>(x, xm, w, R, Dh, Fd, f, st);
   LZ_HH_FWD(32, 32) LZ_HH_FWD(32, 64) LZ_HH_FWD(32, 128)
   LZ_HH_FWD(64, 32) LZ_HH_FWD(64, 64) LZ_HH_FWD(64, 128)
   LZ_HH_FWD(128, 32) LZ_HH_FWD(128, 64) LZ_HH_FWD(128, 128)
@@ -689,8 +722,9 @@ int hedgehog_fwd(const void* x, int x_dtype, const float* w, int R, int Dh, int 
   return LZ_ERR_UNSUPPORTED;
 }
 
-int hedgehog_bwd(const void* x, int x_dtype, const float* w, const void* df, int df_dtype, int R,
-                 int Dh, int Fd, float* dx, float* dw, void* work, cudaStream_t st) {
+int hedgehog_bwd(const void* x, int x_dtype, const XRows& xm, const float* w, const void* df,
+                 int df_dtype, int R, int Dh, int Fd, float* dx, float* dw, void* work,
+                 cudaStream_t st) {
   int dhp, fdp;
   if (dims_pad(Dh, Fd, &dhp, &fdp)) {
     set_error("hedgehog: head dim and feature dim must be <= 128");
@@ -700,10 +734,10 @@ int hedgehog_bwd(const void* x, int x_dtype, const float* w, const void* df, int
 #define LZ_HH_BWD(dh, fd)                                                                        \
   if (dhp == dh && fdp == fd) {                                                                  \
     if (xf && gf)                                                                                \
-      return launch_bwd<float, float, dh, fd>(x, w, df, R, Dh, Fd, 1, 1, dx, dw, work, st);      \
-    if (xf) return launch_bwd<float, bf16, dh, fd>(x, w, df, R, Dh, Fd, 1, 1, dx, dw, work, st); \
-    if (gf) return launch_bwd<bf16, float, dh, fd>(x, w, df, R, Dh, Fd, 0, 1, dx, dw, work, st); \
-    return launch_bwd<bf16, bf16, dh, fd>(x, w, df, R, Dh, Fd, 0, 1, dx, dw, work, st);          \
+      return launch_bwd<float, float, dh, fd>(x, xm, w, df, R, Dh, Fd, dx, dw, work, st);        \
+    if (xf) return launch_bwd<float, bf16, dh, fd>(x, xm, w, df, R, Dh, Fd, dx, dw, work, st);   \
+    if (gf) return launch_bwd<bf16, float, dh, fd>(x, xm, w, df, R, Dh, Fd, dx, dw, work, st);   \
+    return launch_bwd<bf16, bf16, dh, fd>(x, xm, w, df, R, Dh, Fd, dx, dw, work, st);            \
   }
   LZ_HH_BWD(32, 32) LZ_HH_BWD(32, 64) LZ_HH_BWD(32, 128)
   LZ_HH_BWD(64, 32) LZ_HH_BWD(64, 64) LZ_HH_BWD(64, 128)
@@ -726,7 +760,24 @@ extern "C" int lz_hedgehog_fwd(const void* x, int x_dtype, const float* weight, 
   LZ_REQUIRE(R >= 1 && Dh >= 1 && Fd >= 1, LZ_ERR_INVALID_ARGUMENT, "sizes must be positive");
   LZ_REQUIRE(x_dtype == LZ_DTYPE_F32 || x_dtype == LZ_DTYPE_BF16, LZ_ERR_INVALID_ARGUMENT,
              "x_dtype must be LZ_DTYPE_F32 or LZ_DTYPE_BF16");
-  return lz::hedgehog_fwd(x, x_dtype, weight, R, Dh, Fd, static_cast<bf16*>(f),
+  const lz::XRows xm{1, R, (long long)R * Dh, (long long)R * Dh, Dh};
+  return lz::hedgehog_fwd(x, x_dtype, xm, weight, R, Dh, Fd, static_cast<bf16*>(f),
+                          static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lz_hedgehog_fwd_strided(const void* x, int x_dtype, long long x_sb,
+                                       long long x_sh, long long x_sl, int B, int Hx, int L,
+                                       const float* weight, void* f, int Dh, int Fd,
+                                       void* stream) {
+  lz::clear_error();
+  LZ_REQUIRE(x && weight && f, LZ_ERR_INVALID_ARGUMENT, "null pointer");
+  LZ_REQUIRE(B >= 1 && Hx >= 1 && L >= 1 && Dh >= 1 && Fd >= 1, LZ_ERR_INVALID_ARGUMENT,
+             "sizes must be positive");
+  LZ_REQUIRE((long long)B * Hx * L < (1ll << 31), LZ_ERR_INVALID_ARGUMENT, "too many rows");
+  LZ_REQUIRE(x_dtype == LZ_DTYPE_F32 || x_dtype == LZ_DTYPE_BF16, LZ_ERR_INVALID_ARGUMENT,
+             "x_dtype must be LZ_DTYPE_F32 or LZ_DTYPE_BF16");
+  const lz::XRows xm{Hx, L, x_sb, x_sh, x_sl};
+  return lz::hedgehog_fwd(x, x_dtype, xm, weight, B * Hx * L, Dh, Fd, static_cast<bf16*>(f),
                           static_cast<cudaStream_t>(stream));
 }
 
@@ -742,6 +793,29 @@ extern "C" int lz_hedgehog_bwd(const void* x, int x_dtype, const float* weight, 
              LZ_ERR_INVALID_ARGUMENT, "dtypes must be LZ_DTYPE_F32 or LZ_DTYPE_BF16");
   LZ_REQUIRE(workspace_bytes >= lz::hedgehog_bwd_workspace(R, Dh, Fd), LZ_ERR_WORKSPACE,
              "workspace too small (lz_hedgehog_bwd_workspace_bytes)");
-  return lz::hedgehog_bwd(x, x_dtype, weight, df, df_dtype, R, Dh, Fd, dx, dweight, workspace,
-                          static_cast<cudaStream_t>(stream));
+  const lz::XRows xm{1, R, (long long)R * Dh, (long long)R * Dh, Dh};
+  return lz::hedgehog_bwd(x, x_dtype, xm, weight, df, df_dtype, R, Dh, Fd, dx, dweight,
+                          workspace, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lz_hedgehog_bwd_strided(const void* x, int x_dtype, long long x_sb,
+                                       long long x_sh, long long x_sl, int B, int Hx, int L,
+                                       const float* weight, const void* df, int df_dtype,
+                                       float* dx, float* dweight, void* workspace,
+                                       size_t workspace_bytes, int Dh, int Fd, void* stream) {
+  lz::clear_error();
+  LZ_REQUIRE(x && weight && df && dx && dweight && workspace, LZ_ERR_INVALID_ARGUMENT,
+             "null pointer");
+  LZ_REQUIRE(B >= 1 && Hx >= 1 && L >= 1 && Dh >= 1 && Fd >= 1, LZ_ERR_INVALID_ARGUMENT,
+             "sizes must be positive");
+  LZ_REQUIRE((long long)B * Hx * L < (1ll << 31), LZ_ERR_INVALID_ARGUMENT, "too many rows");
+  LZ_REQUIRE((x_dtype == LZ_DTYPE_F32 || x_dtype == LZ_DTYPE_BF16) &&
+                 (df_dtype == LZ_DTYPE_F32 || df_dtype == LZ_DTYPE_BF16),
+             LZ_ERR_INVALID_ARGUMENT, "dtypes must be LZ_DTYPE_F32 or LZ_DTYPE_BF16");
+  const int R = B * Hx * L;
+  LZ_REQUIRE(workspace_bytes >= lz::hedgehog_bwd_workspace(R, Dh, Fd), LZ_ERR_WORKSPACE,
+             "workspace too small (lz_hedgehog_bwd_workspace_bytes)");
+  const lz::XRows xm{Hx, L, x_sb, x_sh, x_sl};
+  return lz::hedgehog_bwd(x, x_dtype, xm, weight, df, df_dtype, R, Dh, Fd, dx, dweight,
+                          workspace, static_cast<cudaStream_t>(stream));
 }

@@ -57,3 +57,29 @@ def test_hedgehog_rows_sum_to_one_and_weights_are_deterministic():
     w.grad = None
     lizard_cuda.hedgehog(x, w).backward(df)
     assert torch.equal(w.grad, g1)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_hedgehog_reads_projection_views_in_place(dtype):
+    """A [B, L, H * Dh] projection viewed as [B, H, L, Dh] goes to the strided
+    entry points: features, dx and dW equal those of the contiguous copy."""
+    import lizard_cuda
+    g = torch.Generator(device="cuda").manual_seed(4)
+    B, L, H, Dh, Fd = 2, 77, 3, 64, 128
+    proj = torch.randn(B, L, H * Dh, generator=g, device="cuda").to(dtype)
+    w = 0.2 * torch.randn(Fd, Dh, generator=g, device="cuda")
+    df = torch.randn(B, H, L, 2 * Fd, generator=g, device="cuda").bfloat16()
+    outs = []
+    for contig in (False, True):
+        p = proj.clone().requires_grad_()
+        wl = w.clone().requires_grad_()
+        x = p.view(B, L, H, Dh).transpose(1, 2)
+        if contig:
+            x = x.contiguous()
+        f = lizard_cuda.hedgehog(x, wl)
+        f.backward(df)
+        outs.append((f, p.grad, wl.grad))
+    (f1, dx1, dw1), (f2, dx2, dw2) = outs
+    assert torch.equal(f1, f2)
+    assert torch.equal(dx1, dx2)
+    assert torch.equal(dw1, dw2)
