@@ -52,6 +52,11 @@ CASES = {
     "prologue-train": (4, 32, 4096, 64, False, True, "hedgehog"),
     # config 5: whole-model prefill (B, L only; the architecture is LLAMA_1B)
     "cfg5-prefill": (32, 32, 4096, 64, False, False, "model"),
+    # config-5 layer kernels at a batch slice (inference): SWA with RoPE inside on
+    # the q / k / v projections (32 / 8 heads, head dim 64, window 64, 4 sinks),
+    # and GLA with F = 256, D = 64, grouped keys / values and a per-token gate
+    "cfg5-swa-rope": (4, 32, 4096, 64, False, False, "swa_rope"),
+    "cfg5-gla": (4, 32, 4096, 256, False, False, "gla_gqa"),
 }
 
 
@@ -68,6 +73,8 @@ def parse():
                          "print its device ms per step (for profiling; not the driver contract)")
     ap.add_argument("--B", type=int, help="batch for --case (default: the config's)")
     ap.add_argument("--L", type=int, help="sequence length for --case (default: the config's)")
+    ap.add_argument("--schedule", choices=("auto", "walk", "split"), default="auto",
+                    help="GLA schedule for --case (default: chosen per shape)")
     return ap.parse_args()
 
 
@@ -752,6 +759,8 @@ def run_case(args, torch):
                                     args.warmup)
         print(json.dumps({"case": name, "B": Bc, "L": Lc, **res}), flush=True)
         return
+    from lizard_cuda import _lib
+    _lib.set_schedule(args.schedule)
     g = torch.Generator(device=dev).manual_seed(5)
     shape = (Bc, Hc, Lc, FDc)
     a = (F.softplus(torch.randn(shape, generator=g, device=dev)) / math.sqrt(FDc)).bfloat16()
@@ -764,6 +773,27 @@ def run_case(args, torch):
     if op == "gla":
         args_in = [a, b, v, lg]
         call = lizard_cuda.gla
+    elif op == "gla_gqa":  # config-5 GLA: D = 64 values, 8 key/value heads, per-token gate
+        Hkv, Dv = 8, 64
+        fk = (F.softplus(torch.randn(Bc, Hkv, Lc, FDc, generator=g, device=dev))
+              / math.sqrt(FDc)).bfloat16()
+        vv = torch.randn(Bc, Hkv, Lc, Dv, generator=g, device=dev).bfloat16()
+        args_in = [a, fk, vv, lg]
+        call = lizard_cuda.gla
+        dy = torch.randn(Bc, Hc, Lc, Dv, generator=g, device=dev).bfloat16()
+    elif op == "swa_rope":  # projections [B, L, heads * 64] read in place as heads
+        Hkv = 8
+        qp = torch.randn(Bc, Lc, Hc * FDc, generator=g, device=dev).bfloat16()
+        kp = torch.randn(Bc, Lc, Hkv * FDc, generator=g, device=dev).bfloat16()
+        vp = torch.randn(Bc, Lc, Hkv * FDc, generator=g, device=dev).bfloat16()
+        inv = 1.0 / (5e5 ** (torch.arange(0, FDc, 2, device=dev).float() / FDc))
+        ang = torch.arange(Lc, device=dev).float()[:, None] * inv
+        emb = torch.cat([ang, ang], -1)[None]
+        cos, sin = emb.cos().bfloat16(), emb.sin().bfloat16()
+        args_in = [qp.view(Bc, Lc, Hc, FDc).transpose(1, 2),
+                   kp.view(Bc, Lc, Hkv, FDc).transpose(1, 2),
+                   vp.view(Bc, Lc, Hkv, FDc).transpose(1, 2), meta]
+        call = lambda q, k, vv_, m: lizard_cuda.swa_rope(q, k, vv_, cos, sin, m, 64)  # noqa: E731
     elif op == "hedgehog":
         args_in = [torch.randn(shape, generator=g, device=dev),
                    0.05 * torch.randn(128, FDc, generator=g, device=dev)]
