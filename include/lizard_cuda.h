@@ -93,6 +93,12 @@ size_t lz_gla_fwd_workspace_bytes(int B, int H, int L, int F, int D, int chunk);
  * No counterpart in the reference; a hook for tests and tuning. */
 int lz_gla_set_schedule(int schedule);
 
+/* Chunk outputs of the chunk-parallel schedule on the tensor cores (1, the
+ * default: F in {128, 256} with D = 64, or F = D = 128) or on the warp-MMA
+ * kernel (0). Returns the previous setting. A hook for tests and tuning,
+ * process-wide; y is the same with and without a saved buffer either way. */
+int lz_gla_set_split_out_tc(int on);
+
 /* Forward of gla(fq, fk, v, log_gamma, chunk).
  * Replaces gla() + _GLA.forward of the reference (src/kernels/gla.py:259-263
  * and 213-234): G = cumsum(log_gamma) is computed on the device, chunk by

@@ -77,6 +77,12 @@ extern "C" int lz_gla_set_schedule(int schedule) {
   return lz::gla_set_schedule(schedule);
 }
 
+namespace lz {
+int gla_set_out_tc(int on);
+}
+
+extern "C" int lz_gla_set_split_out_tc(int on) { return lz::gla_set_out_tc(on); }
+
 extern "C" int lz_gla_fwd_gqa(const void* fq, const void* fk, const void* v,
                               const float* log_gamma, int gate_per_head, void* y, void* saved,
                               size_t saved_bytes, void* workspace, size_t workspace_bytes, int B,

@@ -186,6 +186,16 @@ int gla_fwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int 
 int gla_fwd_split_run(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
                       bf16* y, const GlaSaved& sv, const GlaFwdWork& fw, int B, int H, int Hkv,
                       int L, int F, int D, cudaStream_t stream);
+// Chunk outputs of the chunk-parallel schedule on the tensor cores (F in
+// {128, 256} with D = 64, or F = D = 128; 16-byte aligned buffers):
+// LZ_ERR_UNSUPPORTED without a launch otherwise. s_in / z_in: the scan's bf16
+// states and fp32 normalisers per 64-token chunk of the state heads (sgrp query
+// heads per state, 1 = one per query head). With sv.y32 set (training) it also
+// writes sv.y32, sv.den and sv.g from the chunk start offsets gs.
+int gla_out_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, int B,
+               int H, int Hkv, int sgrp, int L, int F, int D, const bf16* s_in,
+               const float* z_in, bf16* y, const GlaSaved& sv, const float* gs,
+               cudaStream_t st);
 int gla_bwd_split_states(const bf16* fq, const bf16* dy, const GlaSaved& sv, const GlaWork& wk,
                          int B, int H, int L, int F, int D, cudaStream_t stream);
 

@@ -1,0 +1,359 @@
+// Chunk outputs of the chunk-parallel GLA schedule on the 5th-generation
+// tensor cores (tcgen05 + TMEM + TMA), for F in {128, 256} with D = 64, and
+// F = D = 128. In training it also writes what the backward reads: y in fp32,
+// the row sums and the running log gate G.
+//
+// After the increments and the scan (gla_split.cu) every chunk's entering state
+// S_n (bf16) and normaliser z_n (fp32) are in HBM, so the chunks are
+// independent: one CTA of 4 warps takes one 128-token chunk (two 64-token scan
+// chunks; the state entering it is the scan's state 2c) and
+//   TMA      : fq, fk, v tiles and the bf16 state [F x D] (128-byte swizzle)
+//   thread 0 : s = fq fk^T                               -> TMEM [128 x 128]
+//   4 warps  : a = bf16(s 2^(g_i - g_t)), t <= i          -> TMEM (A operand),
+//              row i per thread (TMEM lane i): the in-chunk gate scan,
+//              Q~ = fq 2^(g_i) in place, den_i = sum_t a_it + Q~_i . z_n
+//   thread 0 : o = Q~ S_n + a V                          -> TMEM [128 x D]
+//   4 warps  : y_i = o_i / max(den_i, FLT_MIN)
+// The chunk math is that of the reference (src/kernels/gla.py:60-101) with
+// 128-token chunks; the causal decay uses per-32-column reference rows so no
+// factor exceeds 1 (as in gla_fwd_tc.cu).
+#include "common.cuh"
+#include "gla_layout.h"
+#include "tc.cuh"
+
+namespace lz {
+namespace {
+
+constexpr int kC = 128;       // tokens per CTA
+constexpr int kThreads = 128;  // row i of the chunk = thread i = TMEM lane i
+
+template <int F, int D>
+struct OutTcSmem {
+  static constexpr int FB = F / 64, DB = D / 64;
+  static constexpr size_t q = 0;                                   // fq: FB boxes 128 x 64
+  static constexpr size_t k = q + (size_t)FB * 16384;              // fk
+  static constexpr size_t v = k + (size_t)FB * 16384;              // v: DB boxes 128 x 64
+  static constexpr size_t s = v + (size_t)DB * 16384;              // S: DB boxes F x 64
+  static constexpr size_t z = s + (size_t)DB * F * 128;            // z_n [F] fp32
+  static constexpr size_t g = z + (size_t)F * 4;                   // g2 [128]
+  static constexpr size_t bf = g + 512;                            // block factors [128]
+  static constexpr size_t scan = bf + 512;                         // 4 warp totals
+  static constexpr size_t bars = scan + 32;                        // 3 mbarriers
+  static constexpr size_t slot = bars + 32;                        // TMEM base address
+  static constexpr size_t bytes = slot + 16;
+};
+
+// TMEM columns: s [128 x 128] fp32, o [128 x D] fp32, a [128 x 128] bf16 (64 columns)
+template <int D>
+struct OutTcTmem {
+  static constexpr uint32_t s = 0, o = 128, a = 128 + D, cols = (D == 64) ? 256 : 512;
+};
+enum { OB_FULL = 0, OB_SDONE, OB_ODONE };
+
+template <int F, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+gla_out_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                  const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap ts,
+                  const float* __restrict__ lg, int gph, const float* __restrict__ z_in, int H,
+                  int grp, int sgrp, int L, int NT64, int NC, bf16* __restrict__ y,
+                  float* __restrict__ y32, float* __restrict__ den_out, float* __restrict__ g_out,
+                  const float* __restrict__ gs) {
+  using SM = OutTcSmem<F, D>;
+  using TM = OutTcTmem<D>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  if (smem_u32(smem_raw) & 1023) {  // the 128-byte swizzle needs a 1024-byte aligned window
+    if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 95u);
+    return;
+  }
+  unsigned char* base = smem_raw;
+  float* sZ = reinterpret_cast<float*>(base + SM::z);
+  float* sG = reinterpret_cast<float*>(base + SM::g);
+  float* sB = reinterpret_cast<float*>(base + SM::bf);
+  float* sScan = reinterpret_cast<float*>(base + SM::scan);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + SM::bars);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(base + SM::slot);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c = blockIdx.x % NC, bh = blockIdx.x / NC;
+  const int b = bh / H;
+  const int kvh = kv_head(bh, H, grp);                        // head of fk and v
+  const int shd = sgrp > 1 ? kv_head(bh, H, sgrp) : bh;       // head of the states
+  const int r0 = c * kC, nvalid = min(kC, L - r0);
+  const size_t schunk = (size_t)shd * NT64 + 2 * c;           // scan chunk entering this one
+  const bool with_state = c > 0;
+
+  if (tid == 0) {
+    tc::mbar_init(&bars[OB_FULL], 1);
+    tc::mbar_init(&bars[OB_SDONE], 1);
+    tc::mbar_init(&bars[OB_ODONE], 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tslot, TM::cols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tslot;
+  if (tid == 0) {
+    const uint32_t bytes = (uint32_t)(SM::FB * 2 * 16384 + SM::DB * 16384) +
+                           (with_state ? (uint32_t)(SM::DB * F * 128) : 0u);
+    tc::mbar_expect_tx(&bars[OB_FULL], bytes);
+#pragma unroll
+    for (int j = 0; j < SM::FB; ++j) {
+      tc::tma_load_3d(base + SM::q + j * 16384, &tq, 64 * j, r0, bh, &bars[OB_FULL]);
+      tc::tma_load_3d(base + SM::k + j * 16384, &tk, 64 * j, r0, kvh, &bars[OB_FULL]);
+    }
+#pragma unroll
+    for (int j = 0; j < SM::DB; ++j) {
+      tc::tma_load_3d(base + SM::v + j * 16384, &tv, 64 * j, r0, kvh, &bars[OB_FULL]);
+      if (with_state)
+        tc::tma_load_3d(base + SM::s + (size_t)j * F * 128, &ts, 64 * j, 0, (int)schunk,
+                        &bars[OB_FULL]);
+    }
+  }
+
+  // in-chunk running log2 gate (the chunk's start is the frame: G_start = 0)
+  const int r = tid;
+  const bool valid = r < nvalid;
+  const float* LG = lg + (size_t)(gph ? bh : b) * L;
+  float x = valid ? LG[r0 + r] * kLog2e : 0.f;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float u = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += u;
+  }
+  if (lane == 31) sScan[warp] = x;
+  for (int f = tid; f < F; f += kThreads) sZ[f] = with_state ? z_in[schunk * F + f] : 0.f;
+  __syncthreads();
+  float pre = 0.f;
+#pragma unroll
+  for (int qq = 0; qq < 4; ++qq)
+    if (qq < warp) pre += sScan[qq];
+  const float g2 = pre + x;
+  sG[r] = g2;
+  sB[r] = tc::ex2(__shfl_sync(0xffffffffu, g2, 31) - g2);  // relative to the block's last row
+  __syncthreads();
+
+  if (tid == 0) {
+    // s = fq fk^T, K = F in steps of 16 through the 64-column swizzled blocks
+    tc::mbar_wait(&bars[OB_FULL], 0, 60);
+    tc::tc_fence_after();
+    constexpr uint32_t id_s = tc::idesc_bf16(128, 128, 0, 0);
+    const uint32_t qa = smem_u32(base + SM::q), ka = smem_u32(base + SM::k);
+#pragma unroll
+    for (int j = 0; j < F / 16; ++j) {
+      const uint32_t ko = (j >> 2) * 16384 + (j & 3) * 32;
+      tc::mma_ss(tmem + TM::s, tc::sdesc(qa + ko, 16, 1024), tc::sdesc(ka + ko, 16, 1024), id_s,
+                 j > 0);
+    }
+    tc::mma_commit(&bars[OB_SDONE]);
+  }
+  tc::mbar_wait(&bars[OB_FULL], 0, 61);
+  tc::mbar_wait(&bars[OB_SDONE], 0, 62);
+  tc::tc_fence_after();
+
+  // a = bf16(s 2^(g2_r - g2_t)) for t <= r (blocks left of the diagonal as
+  // 2^(g2_r - g2_ref) 2^(g2_ref - g2_t), both <= 1), and its row sum
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  float den = 0.f;
+#pragma unroll 1
+  for (int cb = 0; cb < 4; ++cb) {
+    uint32_t pk[16];
+    if (cb < warp) {
+      float s[32];
+      tc::tmem_ld32(trow + TM::s + 32 * cb, s);
+      const float ar = valid ? tc::ex2(g2 - sG[32 * cb + 31]) : 0.f;
+      const float4* bt = reinterpret_cast<const float4*>(sB + 32 * cb);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 f = bt[j4];
+        pk[2 * j4] = pack_bf16(s[4 * j4] * f.x * ar, s[4 * j4 + 1] * f.y * ar);
+        pk[2 * j4 + 1] = pack_bf16(s[4 * j4 + 2] * f.z * ar, s[4 * j4 + 3] * f.w * ar);
+      }
+    } else if (cb == warp) {
+      float s[32];
+      tc::tmem_ld32(trow + TM::s + 32 * cb, s);
+      const float4* gt = reinterpret_cast<const float4*>(sG + 32 * cb);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 f = gt[j4];
+        const int t = 32 * cb + 4 * j4;
+        float w0 = s[4 * j4] * tc::ex2(g2 - f.x);
+        float w1 = s[4 * j4 + 1] * tc::ex2(g2 - f.y);
+        float w2 = s[4 * j4 + 2] * tc::ex2(g2 - f.z);
+        float w3 = s[4 * j4 + 3] * tc::ex2(g2 - f.w);
+        w0 = (t <= r && valid) ? w0 : 0.f;
+        w1 = (t + 1 <= r && valid) ? w1 : 0.f;
+        w2 = (t + 2 <= r && valid) ? w2 : 0.f;
+        w3 = (t + 3 <= r && valid) ? w3 : 0.f;
+        pk[2 * j4] = pack_bf16(w0, w1);
+        pk[2 * j4 + 1] = pack_bf16(w2, w3);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) pk[j] = 0u;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) den += bf16_lo(pk[j]) + bf16_hi(pk[j]);
+    tc::tmem_st16(trow + TM::a + 16 * cb, pk);
+  }
+  // Q~ = fq 2^(g2_r) in place (row r, swizzled blocks) and its product with z_n
+  {
+    const float qs = valid ? tc::ex2(g2) : 0.f;
+#pragma unroll 1
+    for (int jb = 0; jb < SM::FB; ++jb) {
+      unsigned char* rowp = base + SM::q + jb * 16384 + r * 128;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        uint4* p = reinterpret_cast<uint4*>(rowp + ((i ^ (r & 7)) * 16));
+        uint4 w = *p;
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+        uint32_t o4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          o4[e] = pack_bf16(bf16_lo(u[e]) * qs, bf16_hi(u[e]) * qs);
+          const int f = 64 * jb + 8 * i + 2 * e;
+          den += bf16_lo(o4[e]) * sZ[f] + bf16_hi(o4[e]) * sZ[f + 1];
+        }
+        *p = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+      }
+    }
+  }
+  tc::fence_proxy_async_smem();
+  tc::tmem_wait_st();
+  tc::tc_fence_before();
+  __syncthreads();
+
+  if (tid == 0) {
+    // o = Q~ S_n + a V
+    tc::tc_fence_after();
+    constexpr uint32_t id_o = tc::idesc_bf16(128, D, 0, 1);  // Q~|a (K-major) x S|V (MN-major)
+    const uint32_t qa = smem_u32(base + SM::q), sa = smem_u32(base + SM::s),
+                   va = smem_u32(base + SM::v);
+    if (with_state) {
+#pragma unroll
+      for (int j = 0; j < F / 16; ++j) {
+        const uint32_t ko = (j >> 2) * 16384 + (j & 3) * 32;
+        tc::mma_ss(tmem + TM::o, tc::sdesc(qa + ko, 16, 1024),
+                   tc::sdesc(sa + 2048 * j, F * 128, 1024), id_o, j > 0);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kC / 16; ++j)
+      tc::mma_ts(tmem + TM::o, tmem + TM::a + 8 * j, tc::sdesc(va + 2048 * j, 16384, 1024), id_o,
+                 (with_state || j > 0) ? 1u : 0u);
+    tc::mma_commit(&bars[OB_ODONE]);
+  }
+  tc::mbar_wait(&bars[OB_ODONE], 0, 63);
+  tc::tc_fence_after();
+  const float inv = 1.f / fmaxf(den, kTiny);
+  const size_t row = (size_t)bh * L + r0 + r;
+  bf16* yrow = y + row * D;
+  if (y32 && valid) {
+    den_out[row] = den;
+    g_out[row] = gs[schunk] + g2 * 0.6931471805599453f;  // natural-log G of the row
+  }
+#pragma unroll 1
+  for (int db = 0; db < D / 32; ++db) {
+    float o[32];
+    tc::tmem_ld32(trow + TM::o + 32 * db, o);
+    tc::tmem_wait_ld();
+    if (valid) {
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint4 w;
+        w.x = pack_bf16(o[8 * q4] * inv, o[8 * q4 + 1] * inv);
+        w.y = pack_bf16(o[8 * q4 + 2] * inv, o[8 * q4 + 3] * inv);
+        w.z = pack_bf16(o[8 * q4 + 4] * inv, o[8 * q4 + 5] * inv);
+        w.w = pack_bf16(o[8 * q4 + 6] * inv, o[8 * q4 + 7] * inv);
+        *reinterpret_cast<uint4*>(yrow + 32 * db + 8 * q4) = w;
+      }
+      if (y32) {
+        float4* d32 = reinterpret_cast<float4*>(y32 + row * D + 32 * db);
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4)
+          d32[q4] = make_float4(o[4 * q4] * inv, o[4 * q4 + 1] * inv, o[4 * q4 + 2] * inv,
+                                o[4 * q4 + 3] * inv);
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, TM::cols);
+  }
+}
+
+// [rows, cols] bf16 viewed as 3-D {cols, inner, outer}, box {64, box_rows, 1},
+// 128-byte swizzle, zero fill outside.
+bool make_out_map(CUtensorMap* m, const void* ptr, int outer, int inner, int cols, int box_rows) {
+  tc::EncodeTiledFn fn = tc::encode_tiled_fn();
+  if (!fn || !aligned16(ptr)) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)inner * cols * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int F, int D>
+int launch_out_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, int B,
+                  int H, int Hkv, int sgrp, int L, int NT64, const bf16* s_in, const float* z_in,
+                  bf16* y, const GlaSaved& sv, const float* gs, cudaStream_t st) {
+  using SM = OutTcSmem<F, D>;
+  const int Hs = sgrp > 1 ? H / sgrp : H;
+  CUtensorMap mq, mk, mv, ms;
+  if (!make_out_map(&mq, fq, B * H, L, F, kC) || !make_out_map(&mk, fk, B * Hkv, L, F, kC) ||
+      !make_out_map(&mv, v, B * Hkv, L, D, kC) || !make_out_map(&ms, s_in, B * Hs * NT64, F, D, F))
+    return LZ_ERR_UNSUPPORTED;
+  const size_t smem = SM::bytes + 1024;  // room to align the window to 1024 bytes
+  static bool done[64] = {false};
+  {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(gla_out_tc_kernel<F, D>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) {
+        set_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+        return LZ_ERR_CUDA;
+      }
+      done[dev] = true;
+    }
+  }
+  const int NC = (L + kC - 1) / kC;
+  gla_out_tc_kernel<F, D><<<(unsigned)((long long)B * H * NC), kThreads, smem, st>>>(
+      mq, mk, mv, ms, lg, gph, z_in, H, H / Hkv, sgrp, L, NT64, NC, y, sv.y32, sv.den, sv.g, gs);
+  count_launches(1);
+  return check_launch("gla_out_tc_kernel");
+}
+
+}  // namespace
+
+int gla_out_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, int B,
+               int H, int Hkv, int sgrp, int L, int F, int D, const bf16* s_in,
+               const float* z_in, bf16* y, const GlaSaved& sv, const float* gs,
+               cudaStream_t st) {
+  const int NT64 = (L + 63) / 64;
+  if (!aligned16(fq) || !aligned16(fk) || !aligned16(v) || !aligned16(s_in) || !aligned16(y) ||
+      (sv.y32 && !aligned16(sv.y32)))
+    return LZ_ERR_UNSUPPORTED;
+  if (F == 256 && D == 64)
+    return launch_out_tc<256, 64>(fq, fk, v, lg, gph, B, H, Hkv, sgrp, L, NT64, s_in, z_in, y, sv, gs,
+                                   st);
+  if (F == 128 && D == 64)
+    return launch_out_tc<128, 64>(fq, fk, v, lg, gph, B, H, Hkv, sgrp, L, NT64, s_in, z_in, y, sv, gs,
+                                   st);
+  if (F == 128 && D == 128)
+    return launch_out_tc<128, 128>(fq, fk, v, lg, gph, B, H, Hkv, sgrp, L, NT64, s_in, z_in, y,
+                                   sv, gs, st);
+  return LZ_ERR_UNSUPPORTED;
+}
+
+}  // namespace lz

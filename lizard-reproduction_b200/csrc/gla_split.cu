@@ -460,6 +460,13 @@ int launch_scan(const float* inc, const float* incz, const float* lam, int BH, i
 
 int gla_schedule_override() { return g_schedule.load(std::memory_order_relaxed); }
 
+// Tensor-core chunk outputs in the chunk-parallel forward (on by default;
+// tests switch them off to compare with the warp-MMA output kernel). The
+// setting must not change between a forward and its backward.
+std::atomic<int> g_out_tc{1};
+bool gla_split_out_tc_enabled() { return g_out_tc.load(std::memory_order_relaxed) != 0; }
+int gla_set_out_tc(int on) { return g_out_tc.exchange(on ? 1 : 0); }
+
 int gla_set_schedule(int s) { return g_schedule.exchange(s); }
 
 int gla_fwd_split_run(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
@@ -486,6 +493,11 @@ int gla_fwd_split_run(const bf16* fq, const bf16* fk, const bf16* v, const float
   rc = launch_scan(fw.inc, fw.incz, fw.lam, BHs, NT, F, D, 0, nullptr, nullptr, s, z, nullptr,
                    nullptr, save ? fw.gs : nullptr, nullptr, stream);
   if (rc) return rc;
+  if (gla_split_out_tc_enabled()) {  // tensor-core chunk outputs (also in training)
+    rc = gla_out_tc(fq, fk, v, lg, gph, B, H, Hkv, share ? grp : 1, L, F, D, s, z, y, sv,
+                    save ? fw.gs : nullptr, stream);
+    if (rc != LZ_ERR_UNSUPPORTED) return rc;
+  }
   const int FP = F <= 32 ? 32 : F <= 64 ? 64 : F <= 128 ? 128 : 256;
   const int DV = D <= 16 ? 16 : D <= 32 ? 32 : 64;
   float* y32 = save ? sv.y32 : nullptr;

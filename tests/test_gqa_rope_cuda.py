@@ -310,3 +310,32 @@ def test_swa_rope_fused_declines_shapes_outside_its_tiles(D, xdt):
         orc.rope(k.double().cpu(), cos.double().cpu(), sin.double().cpu())
     ref = orc.awa(qr, kr, v.double().cpu(), meta.double().cpu(), 16)
     assert_output(out, ref.float(), f"swa_rope two-pass D={D}")
+
+
+@pytest.mark.parametrize("shape", [(1, 4, 1, 300, 256, 64, 0), (2, 4, 2, 257, 256, 64, 1),
+                                   (1, 4, 4, 200, 128, 64, 0), (1, 2, 2, 130, 128, 128, 1)])
+def test_gla_split_tensor_core_outputs(shape):
+    """Chunk outputs of the chunk-parallel schedule on the tensor cores (one
+    128-token chunk per CTA; inference) against the oracle and against the
+    warp-MMA output kernel."""
+    import lizard_cuda
+    from lizard_cuda import _lib
+    lib = _lib.load()
+    B, H, Hkv, L, F, D, per_head = shape
+    fq, fk, v, lg, _ = _gla_inputs(B, H, Hkv, L, F, D, per_head, seed=L + F + D)
+    prev = _lib.set_schedule("split")
+    ys = []
+    try:
+        for tc_on in (1, 0):
+            old = lib.lz_gla_set_split_out_tc(tc_on)
+            try:
+                with torch.no_grad():
+                    ys.append(lizard_cuda.gla(fq, fk, v, lg))
+            finally:
+                lib.lz_gla_set_split_out_tc(old)
+    finally:
+        _lib.set_schedule(prev)
+    ref = orc.gla(fq.double().cpu(), _rep(fk, H // Hkv).double().cpu(),
+                  _rep(v, H // Hkv).double().cpu(), lg.double().cpu())
+    assert_output(ys[0], ref.float(), f"gla tc outputs {shape}")
+    assert_output(ys[0], ys[1].float(), f"gla tc vs warp-MMA outputs {shape}")
