@@ -248,6 +248,11 @@ int lz_hedgehog_bwd(const void* x, int x_dtype, const float* weight, const void*
                     int df_dtype, float* dx, float* dweight, void* workspace,
                     size_t workspace_bytes, int R, int Dh, int Fd, void* stream);
 
+/* Forward on the tensor cores (1, the default) or on the warp-MMA kernel (0)
+ * for bf16 x with Dh = 64 and Fd = 128 (other shapes always take the latter).
+ * Returns the previous setting; a hook for tests and tuning, process-wide. */
+int lz_hedgehog_set_tc(int on);
+
 /* The same for x [B, Hx, L, Dh] at element strides (x_sb, x_sh, x_sl) with Dh
  * contiguous, e.g. a projection output [B, L, Hx * Dh] read in place as heads
  * (x_sb = L * Hx * Dh, x_sh = Dh, x_sl = Hx * Dh). R = B * Hx * L rows in

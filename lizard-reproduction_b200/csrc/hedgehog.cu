@@ -26,6 +26,8 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tc.cuh"
+#include <atomic>
 
 namespace lz {
 
@@ -633,6 +635,167 @@ int dims_pad(int Dh, int Fd, int* dhp, int* fdp) {
   return (*dhp && *fdp) ? LZ_OK : LZ_ERR_UNSUPPORTED;
 }
 
+// ------------------------------------------------- forward on the tensor cores
+// bf16 x with Dh = 64, Fd = 128 (the model's feature map): persistent CTAs of
+// 4 warps; W is split once into bf16 hi / lo in the 128-byte swizzled K-major
+// layout; 128-row x tiles (of one head, from any batch / head / token strides)
+// come by TMA into a two-stage ring; one thread issues x W_hi^T + x W_lo^T into
+// TMEM [128 x 128]; each thread then takes its row (TMEM lane): max and min of
+// the 128 logits, e+ = exp(l - max) and e- = exp(min - l) written back to TMEM
+// with their sums, and the normalised features stored as bf16.
+constexpr int kTcDh = 64, kTcFd = 128;
+struct HhTcSmem {
+  static constexpr size_t whi = 0, wlo = 16384, x = 32768;  // x: two stages of 16 KB
+  static constexpr size_t bars = x + 2 * 16384, slot = bars + 32, bytes = slot + 16;
+};
+
+__global__ void __launch_bounds__(128, 1)
+hedgehog_fwd_tc_kernel(const __grid_constant__ CUtensorMap tx, const float* __restrict__ w,
+                       int H, int L, int ntl, long long ntiles, bf16* __restrict__ f) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  if (smem_u32(smem_raw) & 1023) {
+    if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 94u);
+    return;
+  }
+  unsigned char* base = smem_raw;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + HhTcSmem::bars);  // full0, full1, mdone
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(base + HhTcSmem::slot);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (tid == 0) {
+    tc::mbar_init(&bars[0], 1);
+    tc::mbar_init(&bars[1], 1);
+    tc::mbar_init(&bars[2], 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tslot, 256);
+    tc::tmem_relinquish();
+  }
+  // W [Fd rows x Dh] fp32 -> bf16 hi / lo, row n at n * 128 bytes, 16-byte chunk c
+  // of the row at (c ^ (n & 7)) * 16
+  for (int e = tid; e < kTcFd * kTcDh / 8; e += 128) {
+    const int n = e >> 3, c = e & 7;
+    const float4 a = *reinterpret_cast<const float4*>(w + n * kTcDh + 8 * c);
+    const float4 b4 = *reinterpret_cast<const float4*>(w + n * kTcDh + 8 * c + 4);
+    const float v8[8] = {a.x, a.y, a.z, a.w, b4.x, b4.y, b4.z, b4.w};
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      h[j] = pack_bf16(v8[2 * j], v8[2 * j + 1]);
+      l[j] = pack_bf16(v8[2 * j] - bf16_lo(h[j]), v8[2 * j + 1] - bf16_hi(h[j]));
+    }
+    const size_t off = (size_t)n * 128 + ((c ^ (n & 7)) * 16);
+    *reinterpret_cast<uint4*>(base + HhTcSmem::whi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(base + HhTcSmem::wlo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+  tc::fence_proxy_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  auto issue = [&](long long t, int st) {
+    const int bh = (int)(t / ntl), t0 = (int)(t - (long long)bh * ntl) * 128;
+    tc::mbar_expect_tx(&bars[st], 16384);
+    tc::tma_load_4d(base + HhTcSmem::x + st * 16384, &tx, 0, t0, bh % H, bh / H, &bars[st]);
+  };
+  if (tid == 0 && (long long)blockIdx.x < ntiles) issue(blockIdx.x, 0);
+  int i = 0;
+  for (long long t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+    const int st = i & 1;
+    if (tid == 0) {
+      if (t + gridDim.x < ntiles) issue(t + gridDim.x, st ^ 1);  // that stage's MMA is done
+      tc::mbar_wait(&bars[st], (i >> 1) & 1, 70);
+      tc::tc_fence_after();
+      constexpr uint32_t id = tc::idesc_bf16(128, 128, 0, 0);
+      const uint32_t xa = smem_u32(base + HhTcSmem::x + st * 16384);
+      const uint32_t wh = smem_u32(base + HhTcSmem::whi), wl = smem_u32(base + HhTcSmem::wlo);
+#pragma unroll
+      for (int j = 0; j < kTcDh / 16; ++j)
+        tc::mma_ss(tmem, tc::sdesc(xa + 32 * j, 16, 1024), tc::sdesc(wh + 32 * j, 16, 1024), id,
+                   j > 0);
+#pragma unroll
+      for (int j = 0; j < kTcDh / 16; ++j)
+        tc::mma_ss(tmem, tc::sdesc(xa + 32 * j, 16, 1024), tc::sdesc(wl + 32 * j, 16, 1024), id,
+                   1u);
+      tc::mma_commit(&bars[2]);
+    }
+    tc::mbar_wait(&bars[2], i & 1, 71);
+    tc::tc_fence_after();
+    const int bh = (int)(t / ntl), row = (int)(t - (long long)bh * ntl) * 128 + tid;
+    float mx = -INFINITY, mn = INFINITY;
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {
+      float l[32];
+      tc::tmem_ld32(trow + 32 * q, l);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        mx = fmaxf(mx, l[j]);
+        mn = fminf(mn, l[j]);
+      }
+    }
+    float sp = 0.f, sm = 0.f;
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {  // e+ over the logits' columns, e- at 128 + the same
+      float l[32];
+      tc::tmem_ld32(trow + 32 * q, l);
+      tc::tmem_wait_ld();
+      uint32_t ep[2][16], em[2][16];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float a = __expf(l[j] - mx), b = __expf(mn - l[j]);
+        sp += a;
+        sm += b;
+        ep[j >> 4][j & 15] = __float_as_uint(a);
+        em[j >> 4][j & 15] = __float_as_uint(b);
+      }
+      tc::tmem_st16(trow + 32 * q, ep[0]);
+      tc::tmem_st16(trow + 32 * q + 16, ep[1]);
+      tc::tmem_st16(trow + 128 + 32 * q, em[0]);
+      tc::tmem_st16(trow + 128 + 32 * q + 16, em[1]);
+    }
+    tc::tmem_wait_st();
+    const float ip = 1.f / sp, im = 1.f / sm;
+    const bool valid = row < L;
+    bf16* out = f + ((size_t)bh * L + row) * (2 * kTcFd);
+#pragma unroll 1
+    for (int part = 0; part < 2; ++part) {  // e+ -> features 0..127, e- -> 128..255
+      const float inv = part ? im : ip;
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {
+        float a[32];
+        tc::tmem_ld32(trow + 128 * part + 32 * q, a);
+        tc::tmem_wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            uint4 u;
+            u.x = pack_bf16(a[8 * k] * inv, a[8 * k + 1] * inv);
+            u.y = pack_bf16(a[8 * k + 2] * inv, a[8 * k + 3] * inv);
+            u.z = pack_bf16(a[8 * k + 4] * inv, a[8 * k + 5] * inv);
+            u.w = pack_bf16(a[8 * k + 6] * inv, a[8 * k + 7] * inv);
+            *reinterpret_cast<uint4*>(out + kTcFd * part + 32 * q + 8 * k) = u;
+          }
+        }
+      }
+    }
+    tc::tc_fence_before();
+    __syncthreads();  // TMEM and the x stage are free for the next tile
+    tc::tc_fence_after();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 256);
+  }
+}
+
+// Tensor-core forward on (default) or off (the warp-MMA kernel), for tests.
+std::atomic<int> g_hh_tc{1};
+bool hh_tc_enabled() { return g_hh_tc.load(std::memory_order_relaxed) != 0; }
+
 // persistent grid: two CTAs of 8 warps per SM
 int hh_grid(int R) {
   const int ntiles = (R + kR - 1) / kR;
@@ -703,8 +866,48 @@ size_t hedgehog_bwd_workspace(int R, int Dh, int Fd) {
   return (size_t)hh_grid(R) * fdp * dhp * 4;
 }
 
+// The tensor-core forward for bf16 x, Dh = 64, Fd = 128; LZ_ERR_UNSUPPORTED
+// (nothing launched) when the rows cannot be tiled by TMA.
+int hedgehog_fwd_tc(const void* x, const XRows& xm, const float* w, int R, bf16* f,
+                    cudaStream_t st) {
+  if (!aligned16(x) || !aligned16(w) || !aligned16(f) || (xm.sl * 2) % 16 ||
+      (xm.sh * 2) % 16 || (xm.sb * 2) % 16 || xm.sl <= 0)
+    return LZ_ERR_UNSUPPORTED;
+  const long long heads = (long long)R / xm.L, B = heads / xm.H;
+  if (heads * xm.L != R || B * xm.H != heads) return LZ_ERR_UNSUPPORTED;
+  tc::EncodeTiledFn fn = tc::encode_tiled_fn();
+  if (!fn) return LZ_ERR_UNSUPPORTED;
+  const long long sh = xm.H > 1 ? xm.sh : (long long)xm.L * xm.sl;
+  const long long sb = B > 1 ? xm.sb : xm.H * sh;
+  CUtensorMap mx;
+  cuuint64_t dims[4] = {(cuuint64_t)kTcDh, (cuuint64_t)xm.L, (cuuint64_t)xm.H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)(xm.sl * 2), (cuuint64_t)(sh * 2), (cuuint64_t)(sb * 2)};
+  cuuint32_t box[4] = {(cuuint32_t)kTcDh, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  if (fn(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(x), dims, strides, box, estr,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return LZ_ERR_UNSUPPORTED;
+  // at most two CTAs per SM (each holds 256 TMEM columns): ask for more than a
+  // third of the shared memory
+  const size_t smem = std::max<size_t>(HhTcSmem::bytes, 80 * 1024);
+  static bool done[64] = {false};
+  int rc = hh_attr(hedgehog_fwd_tc_kernel, smem, done);
+  if (rc) return rc;
+  const int ntl = (xm.L + 127) / 128;
+  const long long ntiles = heads * ntl;
+  const int grid = (int)std::min<long long>(ntiles, 2LL * sm_count());
+  hedgehog_fwd_tc_kernel<<<grid, 128, smem, st>>>(mx, w, xm.H, xm.L, ntl, ntiles, f);
+  count_launches(1);
+  return check_launch("hedgehog_fwd_tc_kernel");
+}
+
 int hedgehog_fwd(const void* x, int x_dtype, const XRows& xm, const float* w, int R, int Dh,
                  int Fd, bf16* f, cudaStream_t st) {
+  if (x_dtype == LZ_DTYPE_BF16 && Dh == kTcDh && Fd == kTcFd && hh_tc_enabled()) {
+    const int rc = hedgehog_fwd_tc(x, xm, w, R, f, st);
+    if (rc != LZ_ERR_UNSUPPORTED) return rc;
+  }
   int dhp, fdp;
   if (dims_pad(Dh, Fd, &dhp, &fdp)) {
     set_error("hedgehog: head dim and feature dim must be <= 128");
@@ -747,6 +950,8 @@ int hedgehog_bwd(const void* x, int x_dtype, const XRows& xm, const float* w, co
 }
 
 }  // namespace lz
+
+extern "C" int lz_hedgehog_set_tc(int on) { return lz::g_hh_tc.exchange(on ? 1 : 0); }
 
 extern "C" size_t lz_hedgehog_bwd_workspace_bytes(int R, int Dh, int Fd) {
   if (R < 1 || Dh < 1 || Fd < 1) return 0;

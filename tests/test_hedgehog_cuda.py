@@ -83,3 +83,32 @@ def test_hedgehog_reads_projection_views_in_place(dtype):
     assert torch.equal(f1, f2)
     assert torch.equal(dx1, dx2)
     assert torch.equal(dw1, dw2)
+
+
+@pytest.mark.parametrize("strided", [False, True])
+def test_hedgehog_tensor_core_forward(strided):
+    """bf16 x with Dh = 64, Fd = 128 (the model's feature map) runs on the
+    tensor cores: against the oracle, and within bf16 rounding of the warp-MMA
+    kernel (only the order of the softmax sums differs)."""
+    import lizard_cuda
+    from lizard_cuda import _lib
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(9)
+    B, L, H, Dh, Fd = 2, 333, 3, 64, 128
+    proj = torch.randn(B, L, H * Dh, generator=g, device="cuda").bfloat16()
+    x = proj.view(B, L, H, Dh).transpose(1, 2)
+    if not strided:
+        x = x.contiguous()
+    w = 0.3 * torch.randn(Fd, Dh, generator=g, device="cuda")
+    outs = []
+    for on in (1, 0):
+        old = lib.lz_hedgehog_set_tc(on)
+        try:
+            with torch.no_grad():
+                outs.append(lizard_cuda.hedgehog(x, w))
+        finally:
+            lib.lz_hedgehog_set_tc(old)
+    ref = orc.hedgehog(x.double().cpu(), w.double().cpu())
+    assert_output(outs[0], ref.float(), "hedgehog tensor-core forward")
+    diff = (outs[0].float() - outs[1].float()).abs().max().item()
+    assert diff <= 2 ** -8 * outs[1].float().abs().max().item(), diff
