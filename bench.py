@@ -57,6 +57,12 @@ CASES = {
     # and GLA with F = 256, D = 64, grouped keys / values and a per-token gate
     "cfg5-swa-rope": (4, 32, 4096, 64, False, False, "swa_rope"),
     "cfg5-gla": (4, 32, 4096, 256, False, False, "gla_gqa"),
+    # the layer's feature map on bf16 projections [B, L, H * 64] (tensor-core forward),
+    # its output blend, and one decode step of both branches (B sequences, 8 key/value
+    # heads with F = 256 states, window 64)
+    "cfg5-hedgehog": (4, 32, 4096, 64, False, False, "hedgehog_bf16"),
+    "cfg5-blend": (8, 32, 4096, 64, False, False, "blend"),
+    "cfg5-decode": (32, 32, 4096, 256, False, False, "decode"),
 }
 
 
@@ -781,6 +787,37 @@ def run_case(args, torch):
         args_in = [a, fk, vv, lg]
         call = lizard_cuda.gla
         dy = torch.randn(Bc, Hc, Lc, Dv, generator=g, device=dev).bfloat16()
+    elif op == "hedgehog_bf16":
+        xp = torch.randn(Bc, Lc, Hc * FDc, generator=g, device=dev).bfloat16()
+        args_in = [xp.view(Bc, Lc, Hc, FDc).transpose(1, 2),
+                   0.05 * torch.randn(128, FDc, generator=g, device=dev)]
+        call = lizard_cuda.hedgehog
+    elif op == "blend":
+        args_in = [torch.randn(shape, generator=g, device=dev).bfloat16(),
+                   torch.randn(shape, generator=g, device=dev).bfloat16(),
+                   torch.tensor(0.7, device=dev)]
+        call = lambda a_, b_, al: lizard_cuda.blend(a_, b_, al, torch.bfloat16)  # noqa: E731
+    elif op == "decode":
+        from lizard_cuda.decode import gla_decode, swa_decode
+        Hkv, Dv, W = 8, 64, 64
+        st = torch.zeros(Bc, Hkv, FDc, Dv, device=dev)
+        zs = torch.zeros(Bc, Hkv, FDc, device=dev)
+        kr = torch.zeros(Bc, Hkv, W, Dv, device=dev)
+        vr = torch.zeros_like(kr)
+        pos = torch.full((Bc,), Lc, dtype=torch.int32, device=dev)
+        fq1 = torch.rand(Bc, Hc, FDc, generator=g, device=dev).bfloat16()
+        fk1 = torch.rand(Bc, Hkv, FDc, generator=g, device=dev).bfloat16()
+        q1 = torch.randn(Bc, Hc, Dv, generator=g, device=dev).bfloat16()
+        k1 = torch.randn(Bc, Hkv, Dv, generator=g, device=dev).bfloat16()
+        v1 = torch.randn(Bc, Hkv, Dv, generator=g, device=dev).bfloat16()
+        c1 = torch.ones(1, Dv, device=dev)
+        s1 = torch.zeros(1, Dv, device=dev)
+        lg1 = -torch.rand(Bc, generator=g, device=dev)
+        args_in = []
+
+        def call():
+            gla_decode(fq1, fk1, v1, lg1, st, zs)
+            swa_decode(q1, k1, v1, c1, s1, meta, kr, vr, pos)
     elif op == "swa_rope":  # projections [B, L, heads * 64] read in place as heads
         Hkv = 8
         qp = torch.randn(Bc, Lc, Hc * FDc, generator=g, device=dev).bfloat16()

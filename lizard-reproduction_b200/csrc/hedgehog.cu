@@ -79,8 +79,9 @@ struct XRows {
   int H, L;
   long long sb, sh, sl;
   __host__ __device__ __forceinline__ size_t off(long long r) const {
-    const long long t = r % L, bh = r / L;
-    return (size_t)((bh / H) * sb + (bh % H) * sh + t * sl);
+    if (H == 1 && r < L) return (size_t)(r * sl);  // one head (a contiguous x): rows are tokens
+    const int ri = (int)r, t = ri % L, bh = ri / L;  // rows < 2^31 (checked by the host)
+    return (size_t)((long long)(bh / H) * sb + (long long)(bh % H) * sh + (long long)t * sl);
   }
 };
 
