@@ -19,13 +19,32 @@ int check_sizes(int B, int H, int L, int F, int D) {
 }  // namespace
 
 namespace lz {
-int gla_tc_timeout_flag(unsigned int* out);
-}
+// Each unit whose kernels hold bounded waits has its own copy of the flag.
+int gla_fwd_tc_timeout_flag(unsigned int* out);
+int gla_bwd_tc_timeout_flag(unsigned int* out);
+int gla_out_tc_timeout_flag(unsigned int* out);
+int hedgehog_timeout_flag(unsigned int* out);
+int swa_timeout_flag(unsigned int* out);
+int decode_timeout_flag(unsigned int* out);
+}  // namespace lz
 
 extern "C" int lz_device_timeout_flag(unsigned int* site) {
   lz::clear_error();
   LZ_REQUIRE(site, LZ_ERR_INVALID_ARGUMENT, "null pointer");
-  return lz::gla_tc_timeout_flag(site);
+  int (*const readers[])(unsigned int*) = {
+      lz::gla_fwd_tc_timeout_flag, lz::gla_bwd_tc_timeout_flag, lz::gla_out_tc_timeout_flag,
+      lz::hedgehog_timeout_flag,   lz::swa_timeout_flag,        lz::decode_timeout_flag};
+  *site = 0;
+  for (auto rd : readers) {
+    unsigned int v = 0;
+    const int rc = rd(&v);
+    if (rc) return rc;
+    if (v) {
+      *site = v;
+      break;
+    }
+  }
+  return LZ_OK;
 }
 
 extern "C" size_t lz_gla_saved_bytes(int B, int H, int L, int F, int D, int chunk) {

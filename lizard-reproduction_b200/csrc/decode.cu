@@ -22,6 +22,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace lz {
 namespace {
@@ -140,11 +141,17 @@ __device__ __forceinline__ float ldf<bf16>(const bf16* p, size_t i) {
 // One CTA per (batch row, key/value head). The whole CTA rotates the new key
 // and writes it and v into the ring; then each warp takes query heads of the
 // group (warp, warp + nwarps, ...): lanes own keys for the scores (a key row
-// per lane, the rotated query broadcast from shared memory) and columns for
-// P V (coalesced rows of the value ring).
+// per lane) and columns for P V (coalesced rows of the value ring).
+// STAGE (both rings fit in shared memory, D % 4 == 0, 16-byte aligned rings):
+// one bulk copy brings the whole key and value rings of the (row, kv head)
+// into shared memory before the new entry is written there and to HBM, so the
+// warps' score and P V loops read shared memory instead of walking the ring
+// with dependent global loads. In the score loop lane l visits the 16-byte
+// chunks of its key row starting at chunk l, so the 8 lanes of a quarter warp
+// hit 8 different bank groups.
 constexpr int kMaxDecodeWindow = 1024;
 
-template <typename XT, typename CT>
+template <typename XT, typename CT, bool STAGE>
 __global__ void __launch_bounds__(kT)
 swa_decode_kernel(const XT* __restrict__ q, long long q_sb, long long q_sh,
                   const XT* __restrict__ k, long long k_sb, long long k_sh,
@@ -156,10 +163,15 @@ swa_decode_kernel(const XT* __restrict__ q, long long q_sb, long long q_sh,
   extern __shared__ __align__(16) float sm[];
   const int nw = blockDim.x >> 5;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  float* sQ = sm + warp * D;                    // [nw][D] rotated query per warp
-  float* sP = sm + nw * D + warp * W;           // [nw][W] softmax weights per warp
-  const int bkv = blockIdx.x, b = bkv / Hkv, j = bkv - b * Hkv;
+  // STAGE layout: [mbarrier, 16 B][key ring W x D][value ring W x D][sQ][sP]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
+  float* sKr = sm + 4;
+  float* sVr = sKr + (size_t)W * D;
+  float* base = STAGE ? sVr + (size_t)W * D : sm;
   const int grp = H / Hkv, half = D / 2;
+  float* sQall = base;                          // [grp][D] rotated queries of the group
+  float* sP = base + grp * D + warp * W;        // [nw][W] softmax weights per warp
+  const int bkv = blockIdx.x, b = bkv / Hkv, j = bkv - b * Hkv;
   const int t = pos[b];
   const int slot = t % W, n = min(t + 1, W);
   const CT* cb = cs + (size_t)b * cs_sb;
@@ -168,50 +180,113 @@ swa_decode_kernel(const XT* __restrict__ q, long long q_sb, long long q_sh,
   float* vring = vc + (size_t)bkv * W * D;
   const XT* kr = k + b * k_sb + j * k_sh;
   const XT* vr = v + b * v_sb + j * v_sh;
-  for (int d = tid; d < half; d += blockDim.x) {
-    const float x1 = ldf(kr, d), x2 = ldf(kr, d + half);
-    const float c1 = ldf(cb, d), s1 = ldf(sb, d), c2 = ldf(cb, d + half), s2 = ldf(sb, d + half);
-    kring[(size_t)slot * D + d] = __fadd_rn(__fmul_rn(x1, c1), -__fmul_rn(x2, s1));
-    kring[(size_t)slot * D + d + half] = __fadd_rn(__fmul_rn(x2, c2), __fmul_rn(x1, s2));
+  if constexpr (STAGE) {
+    // the old ring first (nothing writes it until the copy has landed)
+    if (tid == 0) {
+      tc::mbar_init(bar, 1);
+      tc::fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+      const uint32_t bytes = (uint32_t)W * D * 4;
+      tc::mbar_expect_tx(bar, 2 * bytes);
+      tc::bulk_load(sKr, kring, bytes, bar);
+      tc::bulk_load(sVr, vring, bytes, bar);
+    }
   }
-  for (int d = tid; d < D; d += blockDim.x) vring[(size_t)slot * D + d] = ldf(vr, d);
+  // the group's rotated queries (while the copy is in flight)
+  for (int e = tid; e < grp * half; e += blockDim.x) {
+    const int g = e / half, d = e - g * half;
+    const XT* qr = q + b * q_sb + (j * grp + g) * q_sh;
+    const float x1 = ldf(qr, d), x2 = ldf(qr, d + half);
+    const float c1 = ldf(cb, d), s1 = ldf(sb, d), c2 = ldf(cb, d + half), s2 = ldf(sb, d + half);
+    sQall[g * D + d] = __fadd_rn(__fmul_rn(x1, c1), -__fmul_rn(x2, s1));
+    sQall[g * D + d + half] = __fadd_rn(__fmul_rn(x2, c2), __fmul_rn(x1, s2));
+  }
+  // the new ring entry, held in registers until the old ring has landed
+  // (D <= 256 and blockDim >= 32: at most 4 rotated pairs and 8 values a thread)
+  float nk1[4], nk2[4], nv[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int d = tid + i * blockDim.x;
+    if (d < half) {
+      const float x1 = ldf(kr, d), x2 = ldf(kr, d + half);
+      const float c1 = ldf(cb, d), s1 = ldf(sb, d), c2 = ldf(cb, d + half), s2 = ldf(sb, d + half);
+      nk1[i] = __fadd_rn(__fmul_rn(x1, c1), -__fmul_rn(x2, s1));
+      nk2[i] = __fadd_rn(__fmul_rn(x2, c2), __fmul_rn(x1, s2));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int d = tid + i * blockDim.x;
+    if (d < D) nv[i] = ldf(vr, d);
+  }
+  if constexpr (STAGE) {
+    // one bounded wait, its outcome shared through the header's spare word so
+    // that the whole CTA leaves together on a timeout (flag set, nothing else
+    // in flight); then every thread observes the completed phase itself
+    int* ok = reinterpret_cast<int*>(sm + 2);
+    if (tid == 0) *ok = tc::mbar_wait(bar, 0, 90) ? 1 : 0;
+    __syncthreads();
+    if (!*ok) return;
+    (void)tc::mbar_try_wait(bar, 0);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int d = tid + i * blockDim.x;
+    if (d < half) {
+      kring[(size_t)slot * D + d] = nk1[i];
+      kring[(size_t)slot * D + d + half] = nk2[i];
+      if constexpr (STAGE) sKr[slot * D + d] = nk1[i], sKr[slot * D + d + half] = nk2[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int d = tid + i * blockDim.x;
+    if (d < D) {
+      vring[(size_t)slot * D + d] = nv[i];
+      if constexpr (STAGE) sVr[slot * D + d] = nv[i];
+    }
+  }
   __syncthreads();
   const float scale = rsqrtf((float)D);
   float ms = -1e30f;
   for (int m = 0; m < n_meta; ++m) ms = fmaxf(ms, meta[m]);
   for (int g = warp; g < grp; g += nw) {
     const int hq = j * grp + g;
-    const XT* qr = q + b * q_sb + hq * q_sh;
-    for (int d = lane; d < half; d += 32) {
-      const float x1 = ldf(qr, d), x2 = ldf(qr, d + half);
-      const float c1 = ldf(cb, d), s1 = ldf(sb, d), c2 = ldf(cb, d + half), s2 = ldf(sb, d + half);
-      sQ[d] = __fadd_rn(__fmul_rn(x1, c1), -__fmul_rn(x2, s1));
-      sQ[d + half] = __fadd_rn(__fmul_rn(x2, c2), __fmul_rn(x1, s2));
-    }
-    __syncwarp();
-    // scores: key e (e = 0 the newest) per lane
+    const float* sQ = sQall + g * D;
+    // The ring rows holding the last n tokens are exactly rows 0 .. n-1 (before
+    // the ring fills token t sits in row t), so the loops run over rows and the
+    // softmax weights are indexed by row. Scores: a key row per lane.
+    const float* kbase = STAGE ? sKr : kring;
+    const float* vbase = STAGE ? sVr : vring;
     float mx = ms;
-    for (int e = lane; e < n; e += 32) {
-      const float* kk = kring + (size_t)((t - e) % W) * D;
+    for (int r = lane; r < n; r += 32) {
       float x = 0.f;
       if ((D & 3) == 0) {
-        for (int d = 0; d < D; d += 4) {
-          const float4 kv = *reinterpret_cast<const float4*>(kk + d);
-          x += sQ[d] * kv.x + sQ[d + 1] * kv.y + sQ[d + 2] * kv.z + sQ[d + 3] * kv.w;
+        const float4* kk = reinterpret_cast<const float4*>(kbase + (size_t)r * D);
+        const float4* q4 = reinterpret_cast<const float4*>(sQ);
+        const int nc = D >> 2;
+        int c = STAGE ? lane % nc : 0;  // staged: a different bank group per lane
+        for (int i = 0; i < nc; ++i) {
+          const float4 kv = kk[c], qv = q4[c];
+          x += qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
+          c = c + 1 == nc ? 0 : c + 1;
         }
       } else {
+        const float* kk = kbase + (size_t)r * D;
         for (int d = 0; d < D; ++d) x += sQ[d] * kk[d];
       }
       x *= scale;
-      sP[e] = x;
+      sP[r] = x;
       mx = fmaxf(mx, x);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float sum = 0.f;
-    for (int e = lane; e < n; e += 32) {
-      const float p = __expf(sP[e] - mx);
-      sP[e] = p;
+    for (int r = lane; r < n; r += 32) {
+      const float p = __expf(sP[r] - mx);
+      sP[r] = p;
       sum += p;
     }
     for (int m = lane; m < n_meta; m += 32) sum += __expf(meta[m] - mx);
@@ -219,9 +294,19 @@ swa_decode_kernel(const XT* __restrict__ q, long long q_sb, long long q_sh,
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     const float inv = 1.f / sum;
     __syncwarp();
+    // P V: columns per lane, four rows in flight
     for (int d = lane; d < D; d += 32) {
-      float acc = 0.f;
-      for (int e = 0; e < n; ++e) acc += sP[e] * vring[(size_t)((t - e) % W) * D + d];
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      const float* vcol = vbase + d;
+      int r = 0;
+      for (; r + 4 <= n; r += 4) {
+        a0 += sP[r] * vcol[(size_t)r * D];
+        a1 += sP[r + 1] * vcol[(size_t)(r + 1) * D];
+        a2 += sP[r + 2] * vcol[(size_t)(r + 2) * D];
+        a3 += sP[r + 3] * vcol[(size_t)(r + 3) * D];
+      }
+      for (; r < n; ++r) a0 += sP[r] * vcol[(size_t)r * D];
+      const float acc = (a0 + a1) + (a2 + a3);
       y[((size_t)b * H + hq) * D + d] = __float2bfloat16_rn(acc * inv);
     }
     __syncwarp();
@@ -255,28 +340,37 @@ int launch_swa_decode(const void* q, long long q_sb, long long q_sh, const void*
                       int n_meta, bf16* y, int B, int H, int Hkv, int W, int D,
                       cudaStream_t st) {
   const int nw = std::min(H / Hkv, kT / 32);  // one warp per query head of the group
-  const size_t smem = (size_t)nw * (D + W) * 4;
+  const size_t smem0 = ((size_t)(H / Hkv) * D + (size_t)nw * W) * 4;
+  const size_t smem1 = 16 + 2 * (size_t)W * D * 4 + smem0;
+  // both rings in shared memory: they fit, rows are whole 16-byte chunks and the
+  // rings start on 16-byte boundaries (the bulk copy's rules)
+  const bool stage = smem1 <= 160 * 1024 && D % 4 == 0 &&
+                     ((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15) == 0;
+  const size_t smem = stage ? smem1 : smem0;
   const unsigned grid = (unsigned)(B * Hkv);
-  static bool done[2][64] = {{false}};
-  int rc = cs_dtype == LZ_DTYPE_F32
-               ? ensure_decode_smem(swa_decode_kernel<XT, float>, smem, done[0])
-               : ensure_decode_smem(swa_decode_kernel<XT, bf16>, smem, done[1]);
-  if (rc) return rc;
-  if (cs_dtype == LZ_DTYPE_F32)
-    swa_decode_kernel<XT, float><<<grid, 32 * nw, smem, st>>>(
-        static_cast<const XT*>(q), q_sb, q_sh, static_cast<const XT*>(k), k_sb, k_sh,
-        static_cast<const XT*>(v), v_sb, v_sh, static_cast<const float*>(cs),
-        static_cast<const float*>(sn), cs_sb, kc, vc, pos, meta, n_meta, y, H, Hkv, W, D);
-  else
-    swa_decode_kernel<XT, bf16><<<grid, 32 * nw, smem, st>>>(
-        static_cast<const XT*>(q), q_sb, q_sh, static_cast<const XT*>(k), k_sb, k_sh,
-        static_cast<const XT*>(v), v_sb, v_sh, static_cast<const bf16*>(cs),
-        static_cast<const bf16*>(sn), cs_sb, kc, vc, pos, meta, n_meta, y, H, Hkv, W, D);
+#define LZ_SWA_DEC(CT_, S_)                                                                   \
+  {                                                                                           \
+    static bool done[64] = {false};                                                           \
+    int rc = ensure_decode_smem(swa_decode_kernel<XT, CT_, S_>, smem, done);                  \
+    if (rc) return rc;                                                                        \
+    swa_decode_kernel<XT, CT_, S_><<<grid, 32 * nw, smem, st>>>(                              \
+        static_cast<const XT*>(q), q_sb, q_sh, static_cast<const XT*>(k), k_sb, k_sh,         \
+        static_cast<const XT*>(v), v_sb, v_sh, static_cast<const CT_*>(cs),                   \
+        static_cast<const CT_*>(sn), cs_sb, kc, vc, pos, meta, n_meta, y, H, Hkv, W, D);      \
+  }
+  if (cs_dtype == LZ_DTYPE_F32) {
+    if (stage) LZ_SWA_DEC(float, true) else LZ_SWA_DEC(float, false)
+  } else {
+    if (stage) LZ_SWA_DEC(bf16, true) else LZ_SWA_DEC(bf16, false)
+  }
+#undef LZ_SWA_DEC
   count_launches(1);
   return check_launch("swa_decode_kernel");
 }
 
 }  // namespace
+int decode_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
+
 }  // namespace lz
 
 extern "C" int lz_gla_decode(const void* fq, const void* fk, const void* v,

@@ -759,4 +759,6 @@ int gla_bwd_tc_chunks(const bf16* fq, const bf16* fk, const bf16* v, const bf16*
   return check_launch("gla_bwd_chunk_tc_kernel");
 }
 
+int gla_bwd_tc_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
+
 }  // namespace lz

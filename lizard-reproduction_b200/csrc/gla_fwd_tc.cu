@@ -586,13 +586,6 @@ int gla_fwd_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
   return check_launch("gla_fwd_tc_kernel");
 }
 
-int gla_tc_timeout_flag(unsigned int* out) {
-  cudaError_t e = cudaMemcpyFromSymbol(out, tc::g_timeout_flag, sizeof(unsigned int));
-  if (e != cudaSuccess) {
-    set_error(std::string("cudaMemcpyFromSymbol: ") + cudaGetErrorString(e));
-    return LZ_ERR_CUDA;
-  }
-  return LZ_OK;
-}
+int gla_fwd_tc_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
 
 }  // namespace lz

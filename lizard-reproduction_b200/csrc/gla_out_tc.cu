@@ -356,4 +356,6 @@ int gla_out_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
   return LZ_ERR_UNSUPPORTED;
 }
 
+int gla_out_tc_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
+
 }  // namespace lz

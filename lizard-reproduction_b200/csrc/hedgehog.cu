@@ -950,6 +950,8 @@ int hedgehog_bwd(const void* x, int x_dtype, const XRows& xm, const float* w, co
   return LZ_ERR_UNSUPPORTED;
 }
 
+int hedgehog_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
+
 }  // namespace lz
 
 extern "C" int lz_hedgehog_set_tc(int on) { return lz::g_hh_tc.exchange(on ? 1 : 0); }

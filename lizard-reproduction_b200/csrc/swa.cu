@@ -1083,4 +1083,6 @@ int swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const b
   return rc;
 }
 
+int swa_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
+
 }  // namespace lz

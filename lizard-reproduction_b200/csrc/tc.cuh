@@ -40,6 +40,18 @@ static __device__ unsigned int g_timeout_flag;
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// Host side: this translation unit's copy of the flag (the flag is static, so
+// every unit that includes this header has its own; each unit exports a
+// reader lz::<unit>_timeout_flag and the C ABI reports the first one set).
+static inline int read_timeout_flag_here(unsigned int* out) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_timeout_flag, sizeof(unsigned int));
+  if (e != cudaSuccess) {
+    set_error(std::string("cudaMemcpyFromSymbol: ") + cudaGetErrorString(e));
+    return LZ_ERR_CUDA;
+  }
+  return LZ_OK;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
@@ -116,6 +128,16 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
       "[%0], [%1, {%2, %3, %4, %5}], [%6];\n" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
       "r"(smem_u32(bar))
+      : "memory");
+}
+// Contiguous bulk copy global -> shared (no tensor map): both addresses
+// 16-byte aligned, `bytes` a multiple of 16; completes on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 // 3-D TMA tile store from shared memory (bulk async group); out-of-range

@@ -57,15 +57,18 @@ def test_gla_decode_matches_dense_oracle(B, H, Hkv, F, D, L0, T, per_head):
     assert_output(got, ref.float(), f"gla decode {B},{H},{Hkv},{F},{D},{L0},{T}")
 
 
-@pytest.mark.parametrize("H,Hkv,W,L0,T,dtype", [
-    (4, 2, 16, 40, 30, torch.float32),
-    (4, 4, 64, 10, 70, torch.bfloat16),   # the ring fills during the decode
-    (6, 2, 8, 0, 20, torch.float32),
+@pytest.mark.parametrize("H,Hkv,W,L0,T,dtype,D", [
+    (4, 2, 16, 40, 30, torch.float32, 64),
+    (4, 4, 64, 10, 70, torch.bfloat16, 64),   # the ring fills during the decode
+    (6, 2, 8, 0, 20, torch.float32, 64),
+    (4, 1, 5, 3, 12, torch.float32, 32),      # odd window: ring rows staged in shared memory
+    (2, 2, 24, 30, 6, torch.bfloat16, 128),
+    (8, 2, 512, 520, 8, torch.bfloat16, 64),  # rings too large to stage: read from HBM
 ])
-def test_swa_decode_matches_dense_oracle(H, Hkv, W, L0, T, dtype):
+def test_swa_decode_matches_dense_oracle(H, Hkv, W, L0, T, dtype, D):
     from lizard_cuda.decode import swa_decode, swa_ring
     g = torch.Generator(device=DEV).manual_seed(W + T)
-    B, D, L = 2, 64, L0 + T
+    B, L = 2, L0 + T
     q = torch.randn(B, H, L, D, generator=g, device=DEV).to(dtype)
     k = torch.randn(B, Hkv, L, D, generator=g, device=DEV).to(dtype)
     v = torch.randn(B, Hkv, L, D, generator=g, device=DEV).to(dtype)
