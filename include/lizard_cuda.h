@@ -253,6 +253,19 @@ int lz_hedgehog_bwd(const void* x, int x_dtype, const float* weight, const void*
  * Returns the previous setting; a hook for tests and tuning, process-wide. */
 int lz_hedgehog_set_tc(int on);
 
+/* Forwards of at most `rows` rows (R) take the warp-per-row kernel (a warp per
+ * row, W staged per CTA; for decode-sized inputs); -1 restores the default
+ * (fewer rows than one 64-row tile per SM), 0 sends every forward to the tiled
+ * kernels. Returns the previous setting (-1 for the default); a hook for
+ * tests and tuning, process-wide. */
+long long lz_hedgehog_set_rows_max(long long rows);
+
+/* SWA forwards (lz_swa_fwd_gqa and lz_swa_rope_fwd) on the tensor cores (1,
+ * the default: tcgen05 kernel for head dim 64, window <= 64, bf16 operands)
+ * or on the 64-row warp-MMA kernels (0). Returns the previous setting; a hook
+ * for tests and tuning, process-wide. */
+int lz_swa_set_tc(int on);
+
 /* The same for x [B, Hx, L, Dh] at element strides (x_sb, x_sh, x_sl) with Dh
  * contiguous, e.g. a projection output [B, L, Hx * Dh] read in place as heads
  * (x_sb = L * Hx * Dh, x_sh = Dh, x_sl = Hx * Dh). R = B * Hx * L rows in
@@ -375,16 +388,19 @@ int lz_swa_bwd_gqa(const void* q, const void* k, const void* v,
 /* The SWA forward with RoPE inside: q [B, H, L, D], k and v [B, Hkv, L, D]
  * unrotated, all in x_dtype (LZ_DTYPE_F32 or LZ_DTYPE_BF16) at element strides
  * (batch, head, token) with D contiguous, so projection outputs are read in
- * place; cos / sin as for lz_rope_split. The kernel loads 64-row tiles of q, k,
- * v with TMA (k and v through a two-stage ring), rotates q and k in fp32 and
- * splits them into bf16 value + residual tiles in shared memory, then runs the
- * forward of lz_swa_fwd_gqa: y (and saved) equal lz_rope_split +
- * lz_swa_fwd_gqa bit for bit. q_hi, q_lo [B*H, L, D] and k_hi, k_lo
- * [B*Hkv, L, D] (bf16, all null or all set) receive the rotated operands that
- * lz_swa_bwd_gqa takes. Returns LZ_ERR_UNSUPPORTED without launching when D is
- * not 32, 64 or 128, a stride or base is not 16-byte aligned, or the tiles do
- * not fit in shared memory (fp32 at D = 128); rotate first then. The reference
- * rotates with torch ops in its caller (src/lizard_attention.py:87-88). */
+ * place; cos / sin as for lz_rope_split. The kernel loads tiles of q, k, v
+ * with TMA, rotates q and k in fp32 and splits them into bf16 value + residual
+ * tiles in shared memory, then runs the forward of lz_swa_fwd_gqa: y (and
+ * saved) equal lz_rope_split + lz_swa_fwd_gqa bit for bit. With the tensor-core
+ * forward on (lz_swa_set_tc) and D = 64, window <= 64 that is the tcgen05
+ * kernel (bf16 projections); otherwise the 64-row warp-MMA kernel. q_hi, q_lo
+ * [B*H, L, D] and k_hi, k_lo [B*Hkv, L, D] (bf16, all null or all set) receive
+ * the rotated operands that lz_swa_bwd_gqa takes. Returns LZ_ERR_UNSUPPORTED
+ * without launching when D is not 32, 64 or 128, a stride or base is not
+ * 16-byte aligned, the tiles do not fit in shared memory (fp32 at D = 128), or
+ * the projections are fp32 at the tensor-core shape; rotate first then (the
+ * two passes reach the same forward kernel). The reference rotates with torch
+ * ops in its caller (src/lizard_attention.py:87-88). */
 int lz_swa_rope_fwd(const void* q, const void* k, const void* v, int x_dtype,
                     long long q_sb, long long q_sh, long long q_sl,
                     long long k_sb, long long k_sh, long long k_sl,

@@ -25,6 +25,7 @@ int gla_bwd_tc_timeout_flag(unsigned int* out);
 int gla_out_tc_timeout_flag(unsigned int* out);
 int hedgehog_timeout_flag(unsigned int* out);
 int swa_timeout_flag(unsigned int* out);
+int swa_tc_timeout_flag(unsigned int* out);
 int decode_timeout_flag(unsigned int* out);
 }  // namespace lz
 
@@ -33,7 +34,8 @@ extern "C" int lz_device_timeout_flag(unsigned int* site) {
   LZ_REQUIRE(site, LZ_ERR_INVALID_ARGUMENT, "null pointer");
   int (*const readers[])(unsigned int*) = {
       lz::gla_fwd_tc_timeout_flag, lz::gla_bwd_tc_timeout_flag, lz::gla_out_tc_timeout_flag,
-      lz::hedgehog_timeout_flag,   lz::swa_timeout_flag,        lz::decode_timeout_flag};
+      lz::hedgehog_timeout_flag,   lz::swa_timeout_flag,        lz::swa_tc_timeout_flag,
+      lz::decode_timeout_flag};
   *site = 0;
   for (auto rd : readers) {
     unsigned int v = 0;

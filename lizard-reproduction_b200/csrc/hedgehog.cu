@@ -636,6 +636,74 @@ int dims_pad(int Dh, int Fd, int* dhp, int* fdp) {
   return (*dhp && *fdp) ? LZ_OK : LZ_ERR_UNSUPPORTED;
 }
 
+// ------------------------------------------------- forward for a few rows
+// Decode-sized inputs (fewer rows than one 64-row tile per SM, e.g. one token
+// of every head of a batch): a warp per row, 8 rows per CTA, so that the grid
+// spreads over the SMs instead of a handful of tiles. Each CTA stages W in
+// shared memory ([Fd][Dh + 1] fp32: a lane's feature row, one bank apart from
+// the next lane's); lane l owns features l, l + 32, l + 64, l + 96 and takes
+// the logits as fp32 dot products, then both softmaxes with warp shuffles.
+constexpr int kRowWarps = 8;
+
+template <typename XT>
+__global__ void __launch_bounds__(kRowWarps * 32)
+hedgehog_fwd_rows_kernel(const XT* __restrict__ x, XRows xm, const float* __restrict__ w, int R,
+                         int Dh, int Fd, bf16* __restrict__ f) {
+  extern __shared__ float hsm[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int LW = Dh + 1;
+  float* sW = hsm;                                  // [Fd][Dh + 1]
+  float* sX = hsm + Fd * LW + warp * Dh;            // [8][Dh]
+  const long long r = (long long)blockIdx.x * kRowWarps + warp;
+  if (r < R) {
+    const XT* xr = x + xm.off(r);
+    for (int d = lane; d < Dh; d += 32) sX[d] = ld_f(xr, d);
+  }
+  for (int e = tid; e < Fd * Dh; e += kRowWarps * 32) {
+    const int fi = e / Dh, d = e - fi * Dh;
+    sW[fi * LW + d] = w[e];
+  }
+  __syncthreads();
+  if (r >= R) return;
+  float z[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int d = 0; d < Dh; ++d) {
+    const float xd = sX[d];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (lane + 32 * i < Fd) z[i] = fmaf(xd, sW[(lane + 32 * i) * LW + d], z[i]);
+  }
+  float mx = -INFINITY, mn = INFINITY;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (lane + 32 * i < Fd) mx = fmaxf(mx, z[i]), mn = fminf(mn, z[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+  }
+  float ep[4], em[4], sp = 0.f, sm = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool ok = lane + 32 * i < Fd;
+    ep[i] = ok ? __expf(z[i] - mx) : 0.f;
+    em[i] = ok ? __expf(mn - z[i]) : 0.f;
+    sp += ep[i], sm += em[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sp += __shfl_xor_sync(0xffffffffu, sp, o);
+    sm += __shfl_xor_sync(0xffffffffu, sm, o);
+  }
+  const float ip = 1.f / sp, im = 1.f / sm;
+  bf16* fr = f + (size_t)r * 2 * Fd;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (lane + 32 * i < Fd) {
+      fr[lane + 32 * i] = __float2bfloat16_rn(ep[i] * ip);
+      fr[Fd + lane + 32 * i] = __float2bfloat16_rn(em[i] * im);
+    }
+}
+
 // ------------------------------------------------- forward on the tensor cores
 // bf16 x with Dh = 64, Fd = 128 (the model's feature map): persistent CTAs of
 // 4 warps; W is split once into bf16 hi / lo in the 128-byte swizzled K-major
@@ -796,6 +864,27 @@ hedgehog_fwd_tc_kernel(const __grid_constant__ CUtensorMap tx, const float* __re
 // Tensor-core forward on (default) or off (the warp-MMA kernel), for tests.
 std::atomic<int> g_hh_tc{1};
 bool hh_tc_enabled() { return g_hh_tc.load(std::memory_order_relaxed) != 0; }
+// Inputs with at most this many rows take the warp-per-row forward; -1 (the
+// default) means fewer rows than one 64-row tile per SM, 0 never.
+std::atomic<long long> g_hh_rows_max{-1};
+long long hh_rows_max() {
+  const long long v = g_hh_rows_max.load(std::memory_order_relaxed);
+  return v < 0 ? (long long)kR * sm_count() - 1 : v;
+}
+
+template <typename XT>
+int launch_fwd_rows(const void* x, const XRows& xm, const float* w, int R, int Dh, int Fd,
+                    bf16* f, cudaStream_t st) {
+  const size_t smem = ((size_t)Fd * (Dh + 1) + (size_t)kRowWarps * Dh) * 4;
+  static bool done[64] = {false};
+  int rc = hh_attr(hedgehog_fwd_rows_kernel<XT>, smem, done);
+  if (rc) return rc;
+  const int grid = (R + kRowWarps - 1) / kRowWarps;
+  hedgehog_fwd_rows_kernel<XT><<<grid, kRowWarps * 32, smem, st>>>(static_cast<const XT*>(x), xm,
+                                                                    w, R, Dh, Fd, f);
+  count_launches(1);
+  return check_launch("hedgehog_fwd_rows_kernel");
+}
 
 // persistent grid: two CTAs of 8 warps per SM
 int hh_grid(int R) {
@@ -905,6 +994,9 @@ int hedgehog_fwd_tc(const void* x, const XRows& xm, const float* w, int R, bf16*
 
 int hedgehog_fwd(const void* x, int x_dtype, const XRows& xm, const float* w, int R, int Dh,
                  int Fd, bf16* f, cudaStream_t st) {
+  if (R <= hh_rows_max() && Dh <= 128 && Fd <= 128)
+    return x_dtype == LZ_DTYPE_F32 ? launch_fwd_rows<float>(x, xm, w, R, Dh, Fd, f, st)
+                                   : launch_fwd_rows<bf16>(x, xm, w, R, Dh, Fd, f, st);
   if (x_dtype == LZ_DTYPE_BF16 && Dh == kTcDh && Fd == kTcFd && hh_tc_enabled()) {
     const int rc = hedgehog_fwd_tc(x, xm, w, R, f, st);
     if (rc != LZ_ERR_UNSUPPORTED) return rc;
@@ -955,6 +1047,10 @@ int hedgehog_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here
 }  // namespace lz
 
 extern "C" int lz_hedgehog_set_tc(int on) { return lz::g_hh_tc.exchange(on ? 1 : 0); }
+
+extern "C" long long lz_hedgehog_set_rows_max(long long rows) {
+  return lz::g_hh_rows_max.exchange(rows < 0 ? -1 : rows);
+}
 
 extern "C" size_t lz_hedgehog_bwd_workspace_bytes(int R, int Dh, int Fd) {
   if (R < 1 || Dh < 1 || Fd < 1) return 0;

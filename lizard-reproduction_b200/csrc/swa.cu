@@ -26,6 +26,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "rope_math.cuh"
 #include "swa_layout.h"
 #include "tc.cuh"
 
@@ -647,44 +648,6 @@ struct RopeSmem {
                           rk = rq + R, rv = rk + 2 * R, bars = rv + 2 * R, bytes = bars + 64;
 };
 
-template <typename T>
-__device__ __forceinline__ float ldv(const T* p, size_t i);
-template <>
-__device__ __forceinline__ float ldv<float>(const float* p, size_t i) { return p[i]; }
-template <>
-__device__ __forceinline__ float ldv<bf16>(const bf16* p, size_t i) {
-  return __bfloat162float(p[i]);
-}
-
-// 8 consecutive elements of a row as fp32 (16-byte loads; p 16-byte aligned
-// for bf16, 32-byte for fp32 rows of 32 / 64 / 128 elements).
-__device__ __forceinline__ void load8(const bf16* p, float (&x)[8]) {
-  const uint4 w = *reinterpret_cast<const uint4*>(p);
-  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    x[2 * i] = bf16_lo(u[i]);
-    x[2 * i + 1] = bf16_hi(u[i]);
-  }
-}
-__device__ __forceinline__ void load8(const float* p, float (&x)[8]) {
-  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
-  x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
-}
-__device__ __forceinline__ uint4 pack8(const float (&x)[8]) {
-  return make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]),
-                    pack_bf16(x[6], x[7]));
-}
-__device__ __forceinline__ uint4 resid8(const float (&x)[8], uint4 h) {
-  const uint32_t u[4] = {h.x, h.y, h.z, h.w};
-  float r[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    r[2 * i] = x[2 * i] - bf16_lo(u[i]);
-    r[2 * i + 1] = x[2 * i + 1] - bf16_hi(u[i]);
-  }
-  return pack8(r);
-}
 
 // raw [64][DP] (rows t0 ..) -> rotated hi / lo padded tiles, 8 columns of each
 // half per item; rows >= L are zero. Optional copies of the rotated rows to
@@ -708,11 +671,7 @@ __device__ __forceinline__ void rotate_tile(const XT* raw, bf16* hi, bf16* lo, i
       load8(cr + c + HALF, c2);
       load8(sr + c, s1);
       load8(sr + c + HALF, s2);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        o1[u] = __fadd_rn(__fmul_rn(x1[u], c1[u]), -__fmul_rn(x2[u], s1[u]));
-        o2[u] = __fadd_rn(__fmul_rn(x2[u], c2[u]), __fmul_rn(x1[u], s2[u]));
-      }
+      rope8(x1, x2, c1, c2, s1, s2, o1, o2);
     } else {
 #pragma unroll
       for (int u = 0; u < 8; ++u) o1[u] = o2[u] = 0.f;
@@ -1017,6 +976,10 @@ int launch_swa_rope(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st) {
 int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
             const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B, int H,
             int Hkv, int L, int D, cudaStream_t st) {
+  {
+    const int rc = swa_fwd_tc(q, k, v, ql, kl, meta, n_meta, W, y, sv, B, H, Hkv, L, D, st);
+    if (rc != LZ_ERR_UNSUPPORTED) return rc;
+  }
   const int BH = B * H, grp = H / Hkv;
   const bool split = ql != nullptr;
   int vec = (D % 8 == 0) && aligned16(q) && aligned16(k) && aligned16(v);
@@ -1035,6 +998,11 @@ int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const b
 }
 
 int swa_rope_fwd(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st) {
+  // At the tensor-core shape the fused forward is the tcgen05 kernel or
+  // nothing: a decline (fp32 projections, strides its maps cannot take) sends
+  // the caller to rotate first, and lz_swa_fwd_gqa then runs the same kernel.
+  if (swa_tc_enabled() && a.D == 64 && a.window >= 1 && a.window <= 64)
+    return swa_rope_fwd_tc(a, sv, st);
   const bool f32 = a.x_dtype == LZ_DTYPE_F32, cf32 = a.cs_dtype == LZ_DTYPE_F32;
 #define LZ_ROPE(dp)                                                                          \
   if (a.D == dp) {                                                                           \

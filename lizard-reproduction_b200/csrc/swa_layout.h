@@ -66,6 +66,15 @@ struct SwaRopeArgs {
 // shape or strides.
 int swa_rope_fwd(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st);
 
+// The tensor-core forwards (swa_tc.cu): head dim 64, window <= 64, bf16
+// operands; LZ_ERR_UNSUPPORTED without launching for anything else or when
+// switched off (lz_swa_set_tc), and the callers then take the 64-row kernels.
+bool swa_tc_enabled();
+int swa_rope_fwd_tc(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st);
+int swa_fwd_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
+               const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B, int H,
+               int Hkv, int L, int D, cudaStream_t st);
+
 int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
             const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B, int H,
             int Hkv, int L, int D, cudaStream_t st);

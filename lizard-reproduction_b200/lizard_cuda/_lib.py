@@ -56,6 +56,8 @@ _SIGNATURES = {
                                  _c_int, _c_int, _vp]),
     "lz_hedgehog_bwd_workspace_bytes": (_c_size, [_c_int] * 3),
     "lz_hedgehog_set_tc": (_c_int, [_c_int]),
+    "lz_hedgehog_set_rows_max": (ctypes.c_longlong, [ctypes.c_longlong]),
+    "lz_swa_set_tc": (_c_int, [_c_int]),
     "lz_hedgehog_fwd_strided": (_c_int, [_vp, _c_int, ctypes.c_longlong, ctypes.c_longlong, ctypes.c_longlong, _c_int, _c_int, _c_int,
                                          _vp, _vp, _c_int, _c_int, _vp]),
     "lz_hedgehog_bwd_strided": (_c_int, [_vp, _c_int, ctypes.c_longlong, ctypes.c_longlong, ctypes.c_longlong, _c_int, _c_int, _c_int,

@@ -61,6 +61,26 @@ class LizardAttention(nn.Module):
         nn.init.normal_(self.phi_q.weight, std=0.02)
         nn.init.normal_(self.phi_k.weight, std=0.02)
         nn.init.zeros_(self.W_gamma.weight)
+        self._casts = {}
+
+    def param_as(self, p, dtype):
+        """Parameter p in `dtype`. With autograd on this is p.to(dtype). Without
+        it the cast is kept and reused while p is unchanged (same version
+        counter and storage), so inference and decode steps do not re-cast the
+        small fp32 parameters every call; a cast first made while a CUDA graph
+        is being captured is not kept (its values exist only at replay)."""
+        if p.dtype == dtype:
+            return p
+        if torch.is_grad_enabled() and p.requires_grad:
+            return p.to(dtype)
+        key = (id(p), dtype)
+        hit = self._casts.get(key)
+        if hit is not None and hit[0] == p._version and hit[1] == p.data_ptr():
+            return hit[2]
+        out = p.detach().to(dtype)
+        if not torch.cuda.is_current_stream_capturing():
+            self._casts[key] = (p._version, p.data_ptr(), out)
+        return out
 
     def split(self, x, heads):
         """The reference's head split with repeat_interleave to H heads
@@ -90,10 +110,11 @@ class LizardAttention(nn.Module):
         if up:
             q, k, v = q.to(dtype), k.to(dtype), v.to(dtype)
         z = self.W_gamma(x).to(dtype).squeeze(-1)
-        fq = fused_hedgehog(q, self.phi_q.weight.to(dtype))
-        fk = fused_hedgehog(k, self.phi_k.weight.to(dtype))  # Hkv heads
+        fq = fused_hedgehog(q, self.param_as(self.phi_q.weight, dtype))
+        fk = fused_hedgehog(k, self.param_as(self.phi_k.weight, dtype))  # Hkv heads
         cos, sin = position_embeddings
-        alpha, meta = self.alpha_blend.to(dtype), self.meta_tokens.to(dtype)
+        alpha = self.param_as(self.alpha_blend, dtype)
+        meta = self.param_as(self.meta_tokens, dtype)
         lg = F.logsigmoid(z)
         y_gla = gla(fq, fk, v, lg)
         y_swa = swa_rope(q, k, v, cos, sin, meta, self.window)
@@ -117,10 +138,10 @@ class LizardAttention(nn.Module):
         k = self.heads_view(self.k_proj(x), self.kv_heads)
         v = self.heads_view(self.v_proj(x), self.kv_heads)
         lg = F.logsigmoid(self.W_gamma(x).to(dtype).squeeze(-1))
-        fq = fused_hedgehog(q, self.phi_q.weight.to(dtype))
-        fk = fused_hedgehog(k, self.phi_k.weight.to(dtype))
+        fq = fused_hedgehog(q, self.param_as(self.phi_q.weight, dtype))
+        fk = fused_hedgehog(k, self.param_as(self.phi_k.weight, dtype))
         cos, sin = position_embeddings
-        meta = self.meta_tokens.to(dtype)
+        meta = self.param_as(self.meta_tokens, dtype)
         y_gla, y_swa = [], []
         for t in range(x.shape[1]):
             y_gla.append(gla_decode(fq[:, :, t], fk[:, :, t], v[:, :, t], lg[:, t], cache.state,
@@ -128,8 +149,11 @@ class LizardAttention(nn.Module):
             y_swa.append(swa_decode(q[:, :, t], k[:, :, t], v[:, :, t], cos[:, t], sin[:, t],
                                     meta, cache.k_ring, cache.v_ring, cache.pos))
             cache.pos += 1
-        y = blend(torch.stack(y_gla, 2), torch.stack(y_swa, 2), self.alpha_blend.to(dtype),
-                  x.dtype)
+        if len(y_gla) == 1:  # one new token: views, no stacking copies
+            y_gla, y_swa = y_gla[0].unsqueeze(2), y_swa[0].unsqueeze(2)
+        else:
+            y_gla, y_swa = torch.stack(y_gla, 2), torch.stack(y_swa, 2)
+        y = blend(y_gla, y_swa, self.param_as(self.alpha_blend, dtype), x.dtype)
         return self.o_proj(y)
 
 

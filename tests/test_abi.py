@@ -34,6 +34,12 @@ def test_library_exports_every_declared_symbol(lib):
         assert hasattr(lib, name), name
 
 
+def test_hedgehog_rows_max_switch_round_trips(lib):
+    assert lib.lz_hedgehog_set_rows_max(100) == -1
+    assert lib.lz_hedgehog_set_rows_max(-5) == 100
+    assert lib.lz_hedgehog_set_rows_max(-1) == -1
+
+
 def test_abi_version(lib):
     from lizard_cuda import _lib
     assert lib.lz_abi_version() == _lib.ABI_VERSION == 3

@@ -248,16 +248,28 @@ def test_gla_gqa_inference_shared_gate(schedule, shape):
     assert_output(y, ref.float(), f"gla gqa inference {shape} {schedule}")
 
 
+@pytest.fixture(params=[1, 0], ids=["tc", "warp_mma"])
+def swa_tc(request):
+    """SWA forwards on the tensor cores (the default) or on the 64-row kernels."""
+    from lizard_cuda import _lib
+    lib = _lib.load()
+    old = lib.lz_swa_set_tc(request.param)
+    yield request.param
+    lib.lz_swa_set_tc(old)
+
+
 @pytest.mark.parametrize("D,xdt,csdt,H,Hkv,W,L", [
     (64, torch.bfloat16, torch.bfloat16, 4, 2, 64, 200),
     (64, torch.float32, torch.float32, 4, 4, 16, 130),
     (128, torch.bfloat16, torch.float32, 2, 1, 100, 257),
     (32, torch.float32, torch.bfloat16, 4, 2, 200, 64),
 ])
-def test_swa_rope_fused_equals_two_pass(D, xdt, csdt, H, Hkv, W, L):
+def test_swa_rope_fused_equals_two_pass(D, xdt, csdt, H, Hkv, W, L, swa_tc):
     """The one-kernel forward (TMA tiles of the unrotated projections, rotation
     and split inside the CTA) equals rotating first and calling the SWA forward:
-    the same output, saved buffer and rotated operands, bit for bit."""
+    the same output, saved buffer and rotated operands, bit for bit. With the
+    tensor-core forward on, fp32 projections at its shape are declined (the two
+    passes reach the same kernel)."""
     from lizard_cuda import _lib
     from lizard_cuda.rope import _fused_forward, _tables, _two_pass_forward
     lib = _lib.load()
@@ -280,7 +292,11 @@ def test_swa_rope_fused_equals_two_pass(D, xdt, csdt, H, Hkv, W, L):
         if fused:
             rot = tuple(torch.empty(B, n, L, D, device=DEV, dtype=torch.bfloat16)
                         for n in (H, H, Hkv, Hkv))
-            assert _fused_forward(q, k, v, c, s, csb, csl, meta, W, y, saved, rot)
+            ok = _fused_forward(q, k, v, c, s, csb, csl, meta, W, y, saved, rot)
+            if swa_tc and D == 64 and W <= 64 and xdt == torch.float32:
+                assert not ok
+                return
+            assert ok
         else:
             rot = _two_pass_forward(q, k, v, c, s, csb, csl, meta, W, y, saved)
         outs.append((y, saved, rot))

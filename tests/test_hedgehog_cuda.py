@@ -16,6 +16,17 @@ def _lib(built_lib):
     lizard_cuda.load()
 
 
+@pytest.fixture(params=["rows", "tiles"])
+def forward_kernel(request):
+    """Small inputs take the warp-per-row forward by default; "tiles" sends
+    them to the tiled kernels instead, so both are checked on the same cases."""
+    from lizard_cuda import _lib
+    lib = _lib.load()
+    old = lib.lz_hedgehog_set_rows_max(-1 if request.param == "rows" else 0)
+    yield request.param
+    lib.lz_hedgehog_set_rows_max(old)
+
+
 @pytest.mark.parametrize("shape,Fd,xdt,std", [
     ((2, 4, 40, 32), 8, torch.float32, 0.3 * 8),     # layer_tiny: head dim 32, feature dim 8
     ((1, 4, 256, 64), 128, torch.float32, 0.02),     # config 1 layer: the init scale
@@ -23,7 +34,7 @@ def _lib(built_lib):
     ((1, 2, 77, 20), 24, torch.float32, 0.5),        # odd sizes, padded tiles
     ((1, 1, 1000, 128), 100, torch.float32, 0.1),
 ])
-def test_hedgehog_matches_reference(shape, Fd, xdt, std):
+def test_hedgehog_matches_reference(shape, Fd, xdt, std, forward_kernel):
     import lizard_cuda
     g = torch.Generator(device=DEV).manual_seed(3)
     x = torch.randn(shape, generator=g, device=DEV).to(xdt)
@@ -41,6 +52,33 @@ def test_hedgehog_matches_reference(shape, Fd, xdt, std):
     assert_grad(xl.grad, xr.grad.float(), f"hedgehog {shape} dx")
     assert_grad(wl.grad, wr.grad.float(), f"hedgehog {shape} dW")
     assert xl.grad.dtype == xdt and wl.grad.dtype == torch.float32
+
+
+@pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float32])
+def test_hedgehog_decode_step_rows(xdt):
+    """One token per sequence (decode): x is the [B, 1, H * Dh] projection read
+    as [B, H, 1, Dh] heads, R = B * H rows on the warp-per-row kernel; against
+    the oracle and the tiled kernels."""
+    import lizard_cuda
+    from lizard_cuda import _lib
+    lib = _lib.load()
+    g = torch.Generator(device=DEV).manual_seed(21)
+    B, H, Dh, Fd = 32, 32, 64, 128
+    proj = torch.randn(B, 1, H * Dh, generator=g, device=DEV).to(xdt)
+    x = proj.view(B, 1, H, Dh).transpose(1, 2)
+    w = 0.2 * torch.randn(Fd, Dh, generator=g, device=DEV)
+    outs = []
+    for rows in (-1, 0):
+        old = lib.lz_hedgehog_set_rows_max(rows)
+        try:
+            with torch.no_grad():
+                outs.append(lizard_cuda.hedgehog(x, w))
+        finally:
+            lib.lz_hedgehog_set_rows_max(old)
+    ref = orc.hedgehog(x.double().cpu(), w.double().cpu())
+    assert_output(outs[0], ref.float(), f"hedgehog decode rows {xdt}")
+    diff = (outs[0].float() - outs[1].float()).abs().max().item()
+    assert diff <= 2 ** -7 * outs[1].float().abs().max().item(), diff
 
 
 def test_hedgehog_rows_sum_to_one_and_weights_are_deterministic():
@@ -101,13 +139,17 @@ def test_hedgehog_tensor_core_forward(strided):
         x = x.contiguous()
     w = 0.3 * torch.randn(Fd, Dh, generator=g, device="cuda")
     outs = []
-    for on in (1, 0):
-        old = lib.lz_hedgehog_set_tc(on)
-        try:
-            with torch.no_grad():
-                outs.append(lizard_cuda.hedgehog(x, w))
-        finally:
-            lib.lz_hedgehog_set_tc(old)
+    old_rows = lib.lz_hedgehog_set_rows_max(0)  # the tiled kernels even at this size
+    try:
+        for on in (1, 0):
+            old = lib.lz_hedgehog_set_tc(on)
+            try:
+                with torch.no_grad():
+                    outs.append(lizard_cuda.hedgehog(x, w))
+            finally:
+                lib.lz_hedgehog_set_tc(old)
+    finally:
+        lib.lz_hedgehog_set_rows_max(old_rows)
     ref = orc.hedgehog(x.double().cpu(), w.double().cpu())
     assert_output(outs[0], ref.float(), "hedgehog tensor-core forward")
     diff = (outs[0].float() - outs[1].float()).abs().max().item()

@@ -1,0 +1,125 @@
+"""The tensor-core SWA forward (tcgen05 + TMEM + TMA; head dim 64, window
+<= 64) against the CPU oracle of the reference's attention
+(src/lizard_attention.py:34-44 on repeat_interleaved keys / values), through
+the public swa / swa_rope entry points, forward and backward; and against the
+64-row warp-MMA kernels it replaces at those shapes."""
+import pytest
+import torch
+
+import lizard_oracle as orc
+from parity import assert_grad, assert_output
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib(built_lib):
+    import lizard_cuda
+    lizard_cuda.load()
+
+
+def _rep(x, grp):
+    return x.repeat_interleave(grp, dim=1)
+
+
+def _set_tc(on):
+    from lizard_cuda import _lib
+    return _lib.load().lz_swa_set_tc(on)
+
+
+def _inputs(B, H, Hkv, L, W, n_meta, dtype, seed):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    q = torch.randn(B, H, L, 64, generator=g, device=DEV).to(dtype)
+    k, v = (torch.randn(B, Hkv, L, 64, generator=g, device=DEV).to(dtype) for _ in range(2))
+    meta = torch.randn(n_meta, generator=g, device=DEV)
+    dy = torch.randn(B, H, L, 64, generator=g, device=DEV).bfloat16()
+    return q, k, v, meta, dy
+
+
+def _oracle(q, k, v, meta, W, dy):
+    grp = q.shape[1] // k.shape[1]
+    lv = [t.detach().float().cpu().clone().requires_grad_() for t in (q, k, v, meta)]
+    m = lv[3] if lv[3].numel() else torch.full((1,), -1e4)
+    y = orc.awa(lv[0], _rep(lv[1], grp), _rep(lv[2], grp), m, W)
+    y.backward(dy.float().cpu())
+    return y.detach(), [t.grad for t in lv]
+
+
+@pytest.mark.parametrize("B,H,Hkv,L,W,n_meta,dtype", [
+    (1, 2, 2, 1, 8, 4, torch.bfloat16),       # one token
+    (2, 4, 2, 127, 64, 4, torch.bfloat16),    # one partial 128-row block
+    (1, 4, 1, 300, 64, 3, torch.float32),     # fp32: residual logits; grp 4
+    (2, 2, 2, 257, 1, 4, torch.bfloat16),     # window 1: each row sees itself
+    (1, 8, 2, 200, 17, 0, torch.bfloat16),    # no sinks, odd window
+    (1, 2, 2, 2048, 64, 4, torch.bfloat16),   # config-3 length
+])
+def test_swa_tc_matches_oracle(B, H, Hkv, L, W, n_meta, dtype):
+    import lizard_cuda
+    q, k, v, meta, dy = _inputs(B, H, Hkv, L, W, n_meta, dtype, seed=L + W)
+    lv = [t.detach().clone().requires_grad_() for t in (q, k, v, meta)]
+    y = lizard_cuda.swa(*lv, W)
+    y.backward(dy)
+    ref, rg = _oracle(q, k, v, meta, W, dy)
+    tag = f"swa tc B{B} H{H}/{Hkv} L{L} W{W} S{n_meta} {dtype}"
+    assert_output(y, ref, tag + " y")
+    names = ("dq", "dk", "dv", "dmeta") if n_meta else ("dq", "dk", "dv")
+    for t, r, n in zip(lv, rg, names):
+        assert_grad(t.grad, r, f"{tag} {n}")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_swa_tc_close_to_warp_mma_kernel(dtype):
+    """Same products, one softmax pass instead of the online rescaling: the
+    outputs agree to bf16 rounding, the saved log-sum-exp to fp32 rounding."""
+    import lizard_cuda
+    q, k, v, meta, dy = _inputs(2, 4, 2, 333, 64, 4, dtype, seed=5)
+    outs = []
+    for on in (1, 0):
+        old = _set_tc(on)
+        try:
+            lv = [t.detach().clone().requires_grad_() for t in (q, k, v, meta)]
+            y = lizard_cuda.swa(*lv, 64)
+            y.backward(dy)
+            outs.append((y.detach().float(), [t.grad.float() for t in lv]))
+        finally:
+            _set_tc(old)
+    (y1, g1), (y2, g2) = outs
+    diff = (y1 - y2).abs().max().item()
+    assert diff <= 2 ** -7 * y2.abs().max().item(), diff
+    for a, b in zip(g1, g2):
+        assert (a - b).abs().max().item() <= 2e-2 * b.abs().max().item()
+
+
+def test_swa_rope_tc_reads_projections_in_place():
+    """The Lizard layer's call: projections [B, L, heads * 64] (bf16) read as
+    heads, RoPE inside, GQA 8 / 2, window 64, 4 sinks; forward and backward
+    against the oracle on the rotated inputs."""
+    import lizard_cuda
+    g = torch.Generator(device=DEV).manual_seed(11)
+    B, L, H, Hkv, D, W = 2, 384, 8, 2, 64, 64
+    qp = torch.randn(B, L, H * D, generator=g, device=DEV).bfloat16()
+    kp = torch.randn(B, L, Hkv * D, generator=g, device=DEV).bfloat16()
+    vp = torch.randn(B, L, Hkv * D, generator=g, device=DEV).bfloat16()
+    meta = torch.randn(4, generator=g, device=DEV)
+    dy = torch.randn(B, H, L, D, generator=g, device=DEV).bfloat16()
+    cos, sin = (t.to(DEV).expand(B, L, D) for t in orc.rotary_tables(L, D, 5e5))
+    lv = [t.detach().clone().requires_grad_() for t in (qp, kp, vp, meta)]
+    q = lv[0].view(B, L, H, D).transpose(1, 2)
+    k = lv[1].view(B, L, Hkv, D).transpose(1, 2)
+    v = lv[2].view(B, L, Hkv, D).transpose(1, 2)
+    y = lizard_cuda.swa_rope(q, k, v, cos, sin, lv[3], W)
+    y.backward(dy)
+    with torch.no_grad():
+        y_inf = lizard_cuda.swa_rope(q, k, v, cos, sin, lv[3], W)
+    assert torch.equal(y, y_inf)  # the same kernel with and without the saved buffers
+    c, s = cos.double().cpu(), sin.double().cpu()
+    rl = [t.detach().double().cpu().clone().requires_grad_() for t in (qp, kp, vp, meta)]
+    qr = orc.rope(rl[0].view(B, L, H, D).transpose(1, 2), c, s)
+    kr = orc.rope(rl[1].view(B, L, Hkv, D).transpose(1, 2), c, s)
+    vr = rl[2].view(B, L, Hkv, D).transpose(1, 2)
+    ref = orc.awa(qr, _rep(kr, H // Hkv), _rep(vr, H // Hkv), rl[3], W)
+    ref.backward(dy.double().cpu())
+    assert_output(y, ref.float(), "swa_rope tc y")
+    for t, r, n in zip(lv, rl, ("dq", "dk", "dv", "dmeta")):
+        assert_grad(t.grad, r.grad.float(), f"swa_rope tc {n}")
