@@ -21,6 +21,36 @@ __device__ __forceinline__ void load8(const float* p, float (&x)[8]) {
   const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
   x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
 }
+// 8 consecutive row elements held as loaded (16 or 32 bytes), converted later:
+// lets a thread put several rows' loads in flight in few registers.
+template <typename T>
+struct Raw8;
+template <>
+struct Raw8<bf16> {
+  uint4 w;
+  __device__ __forceinline__ void load(const bf16* p) { w = *reinterpret_cast<const uint4*>(p); }
+  __device__ __forceinline__ void get(float (&x)[8]) const {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[2 * i] = bf16_lo(u[i]);
+      x[2 * i + 1] = bf16_hi(u[i]);
+    }
+  }
+};
+template <>
+struct Raw8<float> {
+  float4 a, b;
+  __device__ __forceinline__ void load(const float* p) {
+    a = *reinterpret_cast<const float4*>(p);
+    b = *reinterpret_cast<const float4*>(p + 4);
+  }
+  __device__ __forceinline__ void get(float (&x)[8]) const {
+    x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z,
+    x[7] = b.w;
+  }
+};
+
 __device__ __forceinline__ uint4 pack8(const float (&x)[8]) {
   return make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]),
                     pack_bf16(x[6], x[7]));

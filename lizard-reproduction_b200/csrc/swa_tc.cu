@@ -3,7 +3,7 @@
 // Lizard layer's shape (reference: src/lizard_attention.py:34-44 and the
 // Triton forward src/kernels/swa.py:19-59).
 //
-// One CTA of 4 warps takes 128 query rows [q0, q0 + 128) of one batch row and
+// One CTA of 8 warps takes 128 query rows [q0, q0 + 128) of one batch row and
 // one key/value head, and every query head of that head's group in turn:
 //   TMA      : keys and values of rows [q0 - 64, q0 + 128) (192 rows; rows
 //              outside the sequence arrive as zeros) once, and each head's 128
@@ -12,16 +12,20 @@
 //              fp32, in place, and split them into bf16 hi + lo operand tiles
 //              (the same arithmetic as the 64-row kernels and lz_rope_split)
 //   thread 0 : s = q_hi k_hi^T (+ q_hi k_lo^T + q_lo k_hi^T) -> TMEM [128 x 192]
-//   4 warps  : row i per thread (TMEM lane i) reads the 96 columns that hold
-//              its window, takes the max seeded by the sinks, p = 2^(x - max)
-//              split into bf16 hi + lo written over s as the A operand of P V,
-//              and the row sum (sinks included)
+//   8 warps  : row i = TMEM lane i, its window's 96 columns split between the
+//              two warps of the lane quadrant: the max (seeded by the sinks,
+//              exchanged through shared memory), p = 2^(x - max) split into
+//              bf16 hi + lo written over s as the A operand of P V, row sums
 //   thread 0 : o = p_hi V + p_lo V                             -> TMEM [128 x 64]
-//   4 warps  : y_i = o_i / l_i (training: also lse_i and y_i in fp32)
-// One softmax pass over the whole window replaces the online rescaling of the
-// 64-key-block kernels; the products carry the same precision (about 16
-// mantissa bits in the logits and in P). 106 KB of shared memory and 256 TMEM
-// columns per CTA: two CTAs per SM.
+//   8 warps  : y_i = o_i / l_i, 32 columns per warp (training: also lse_i and
+//              y_i in fp32)
+// The heads overlap: P V of head g runs while the warps rotate the queries of
+// head g + 1 (their TMA load was issued when the scores of head g had read the
+// query tiles), and the scores of head g + 1 run while the warps write the
+// output of head g. One softmax pass over the whole window replaces the online
+// rescaling of the 64-key-block kernels; the products carry the same precision
+// (about 16 mantissa bits in the logits and in P). 109 KB of shared memory and
+// 256 TMEM columns per CTA: two CTAs per SM.
 #include <atomic>
 
 #include "common.cuh"
@@ -33,14 +37,15 @@ namespace lz {
 namespace {
 
 constexpr int kQ = 128;   // query rows per CTA (= TMEM lanes)
+constexpr int kThreads = 256;
 constexpr int kNK = 192;  // key rows per CTA: [q0 - 64, q0 + 128)
 constexpr int kDh = 64;   // head dim (one 128-byte swizzle row)
 constexpr float kLn2f = 0.6931471805599453f;
 
 struct SwaTcSmem {
   static constexpr size_t kh = 0, kl = kh + kNK * 128, v = kl + kNK * 128, qh = v + kNK * 128,
-                          ql = qh + kQ * 128, bars = ql + kQ * 128, slot = bars + 32,
-                          bytes = slot + 16;
+                          ql = qh + kQ * 128, red = ql + kQ * 128,  // [2][2][128] fp32
+                          bars = red + 2048, slot = bars + 32, bytes = slot + 16;
 };
 // TMEM columns: s [128 x 192] fp32; p hi / lo (bf16 pairs, 96 columns each)
 // written over s; o [128 x 64] fp32
@@ -52,29 +57,48 @@ __device__ __forceinline__ uint32_t sw128(int r, int c) {
   return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
 }
 
-// Rotate rows [0, nrows) of a raw bf16 tile that sits in `lo` (token t0 + r)
-// in place: hi / lo parts of the rotated row into `hi` / `lo`, zero for tokens
-// outside [0, L). Rows r >= row_out with a token in the sequence are also
-// copied to ghi / glo ([L, 64] of the head) when given.
-template <typename CT>
-__device__ __forceinline__ void rotate_rows(unsigned char* hi, unsigned char* lo, int nrows,
-                                            int t0, int L, const CT* cs, const CT* sn,
-                                            long long cs_sl, int row_out, bf16* ghi, bf16* glo) {
-  for (int e = threadIdx.x; e < nrows * 4; e += kQ) {
-    const int r = e >> 2, c8 = e & 3, t = t0 + r;
+// Rotate rows [ROW0, ROW0 + NROWS) of a raw bf16 tile that sits in `lo` (row r
+// holds token t0 + r) in place: hi / lo parts of the rotated row into `hi` /
+// `lo`, zero for tokens outside [0, L). Rows r >= row_out with a token in the
+// sequence are also copied to ghi / glo ([L, 64] of the head) when given.
+// Items (row, 8-column pair) are spread over the CTA; a thread's loads are all
+// issued before the first rotation.
+template <int ROW0, int NROWS, typename CT>
+__device__ __forceinline__ void rotate_rows(unsigned char* hi, unsigned char* lo, int t0, int L,
+                                            const CT* cs, const CT* sn, long long cs_sl,
+                                            int row_out, bf16* ghi, bf16* glo) {
+  static_assert(NROWS * 4 % kThreads == 0, "whole items per thread");
+  constexpr int kItems = NROWS * 4 / kThreads;
+  Raw8<bf16> x1[kItems], x2[kItems];
+  Raw8<CT> c1[kItems], c2[kItems], s1[kItems], s2[kItems];
+#pragma unroll
+  for (int it = 0; it < kItems; ++it) {
+    const int e = threadIdx.x + it * kThreads, r = ROW0 + (e >> 2), c8 = e & 3, t = t0 + r;
+    if (t >= 0 && t < L) {
+      x1[it].load(reinterpret_cast<const bf16*>(lo + sw128(r, c8)));
+      x2[it].load(reinterpret_cast<const bf16*>(lo + sw128(r, c8 + 4)));
+      const CT* cr = cs + (size_t)t * cs_sl;
+      const CT* sr = sn + (size_t)t * cs_sl;
+      c1[it].load(cr + 8 * c8);
+      c2[it].load(cr + 8 * c8 + kDh / 2);
+      s1[it].load(sr + 8 * c8);
+      s2[it].load(sr + 8 * c8 + kDh / 2);
+    }
+  }
+#pragma unroll
+  for (int it = 0; it < kItems; ++it) {
+    const int e = threadIdx.x + it * kThreads, r = ROW0 + (e >> 2), c8 = e & 3, t = t0 + r;
     const uint32_t o1 = sw128(r, c8), o2 = sw128(r, c8 + 4);
     float a1[8], a2[8];
     if (t >= 0 && t < L) {
-      float x1[8], x2[8], c1[8], c2[8], s1[8], s2[8];
-      load8(reinterpret_cast<const bf16*>(lo + o1), x1);
-      load8(reinterpret_cast<const bf16*>(lo + o2), x2);
-      const CT* cr = cs + (size_t)t * cs_sl;
-      const CT* sr = sn + (size_t)t * cs_sl;
-      load8(cr + 8 * c8, c1);
-      load8(cr + 8 * c8 + kDh / 2, c2);
-      load8(sr + 8 * c8, s1);
-      load8(sr + 8 * c8 + kDh / 2, s2);
-      rope8(x1, x2, c1, c2, s1, s2, a1, a2);
+      float fx1[8], fx2[8], fc1[8], fc2[8], fs1[8], fs2[8];
+      x1[it].get(fx1);
+      x2[it].get(fx2);
+      c1[it].get(fc1);
+      c2[it].get(fc2);
+      s1[it].get(fs1);
+      s2[it].get(fs2);
+      rope8(fx1, fx2, fc1, fc2, fs1, fs2, a1, a2);
     } else {
 #pragma unroll
       for (int u = 0; u < 8; ++u) a1[u] = a2[u] = 0.f;
@@ -99,7 +123,7 @@ __device__ __forceinline__ void rotate_rows(unsigned char* hi, unsigned char* lo
 // Otherwise q, k are the rotated operands; SPLIT adds their bf16 residuals
 // (maps tql, tkl). v is bf16 in both.
 template <bool ROPE, bool SPLIT, typename CT>
-__global__ void __launch_bounds__(kQ)
+__global__ void __launch_bounds__(kThreads, 2)
 swa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tql,
                   const __grid_constant__ CUtensorMap tkl, const CT* __restrict__ cs,
@@ -116,7 +140,9 @@ swa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::bars);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + SM::slot);
-  const int tid = threadIdx.x, warp = tid >> 5;
+  float* red = reinterpret_cast<float*>(smem + SM::red);  // [max | sum][half][row]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qd = warp & 3, hf = warp >> 2;  // TMEM lane quadrant, column half
   const int qb = blockIdx.x % nqb, bk = blockIdx.x / nqb;
   const int Hkv = H / grp, b = bk / Hkv, hk = bk - b * Hkv;
   const int q0 = qb * kQ, k0 = q0 - (kNK - kQ);
@@ -146,6 +172,27 @@ swa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       if (SPLIT) tc::tma_load_4d(smem + SM::ql, &tql, 0, q0, h, b, &bars[SB_Q]);
     }
   };
+  auto issue_s = [&]() {  // s = q k^T into TMEM columns [0, 192)
+    tc::tc_fence_after();
+    constexpr uint32_t id_s = tc::idesc_bf16(kQ, kNK, 0, 0);  // q (K-major) x k (K-major)
+    const uint32_t qh = smem_u32(smem + SM::qh), ql = smem_u32(smem + SM::ql),
+                   kh = smem_u32(smem + SM::kh), kl = smem_u32(smem + SM::kl);
+#pragma unroll
+    for (int j = 0; j < kDh / 16; ++j)
+      tc::mma_ss(tmem + kTmS, tc::sdesc(qh + 32 * j, 16, 1024), tc::sdesc(kh + 32 * j, 16, 1024),
+                 id_s, j > 0);
+    if (SPLIT || ROPE) {
+#pragma unroll
+      for (int j = 0; j < kDh / 16; ++j)
+        tc::mma_ss(tmem + kTmS, tc::sdesc(qh + 32 * j, 16, 1024),
+                   tc::sdesc(kl + 32 * j, 16, 1024), id_s, 1u);
+#pragma unroll
+      for (int j = 0; j < kDh / 16; ++j)
+        tc::mma_ss(tmem + kTmS, tc::sdesc(ql + 32 * j, 16, 1024),
+                   tc::sdesc(kh + 32 * j, 16, 1024), id_s, 1u);
+    }
+    tc::mma_commit(&bars[SB_S]);
+  };
   if (tid == 0) {
     tc::mbar_expect_tx(&bars[SB_KV], (!ROPE && SPLIT) ? 3 * kTileK : 2 * kTileK);
     if (ROPE) {
@@ -166,95 +213,86 @@ swa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 
   const CT* csb = ROPE ? cs + (size_t)b * cs_sb : nullptr;
   const CT* snb = ROPE ? sn + (size_t)b * cs_sb : nullptr;
+  auto rotate_q = [&](int g) {
+    const size_t hrow = ((size_t)b * H + hk * grp + g) * L;
+    rotate_rows<0, kQ, CT>(smem + SM::qh, smem + SM::ql, q0, L, csb, snb, cs_sl, 0,
+                           qh_out ? qh_out + hrow * kDh : nullptr,
+                           qh_out ? ql_out + hrow * kDh : nullptr);
+  };
   tc::mbar_wait(&bars[SB_KV], 0, 80);
   if (ROPE) {
     const size_t kvb = ((size_t)b * Hkv + hk) * L * kDh;
-    rotate_rows<CT>(smem + SM::kh, smem + SM::kl, kNK, k0, L, csb, snb, cs_sl, kNK - kQ,
-                    kh_out ? kh_out + kvb : nullptr, kh_out ? kl_out + kvb : nullptr);
+    bf16* gh = kh_out ? kh_out + kvb : nullptr;
+    bf16* gl = kh_out ? kl_out + kvb : nullptr;
+    rotate_rows<0, 128, CT>(smem + SM::kh, smem + SM::kl, k0, L, csb, snb, cs_sl, kNK - kQ, gh,
+                            gl);
+    rotate_rows<128, kNK - 128, CT>(smem + SM::kh, smem + SM::kl, k0, L, csb, snb, cs_sl,
+                                    kNK - kQ, gh, gl);
   }
+  tc::mbar_wait(&bars[SB_Q], 0, 81);
+  if (ROPE) rotate_q(0);
+  tc::fence_proxy_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  if (tid == 0) issue_s();
 
-  const int r = tid, i = q0 + r;
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  const int r = 32 * qd + lane, i = q0 + r;
+  const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
+  const int cw = 32 * qd + 48 * hf;  // first score column of this thread's half window
   for (int g = 0; g < grp; ++g) {
-    const size_t hrow = ((size_t)b * H + hk * grp + g) * L;  // row 0 of this query head
     const uint32_t ph = (uint32_t)g & 1u;
-    tc::mbar_wait(&bars[SB_Q], ph, 81);
-    if (ROPE)
-      rotate_rows<CT>(smem + SM::qh, smem + SM::ql, kQ, q0, L, csb, snb, cs_sl, 0,
-                      qh_out ? qh_out + hrow * kDh : nullptr,
-                      qh_out ? ql_out + hrow * kDh : nullptr);
-    tc::fence_proxy_async_smem();
-    tc::tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc::tc_fence_after();
-      constexpr uint32_t id_s = tc::idesc_bf16(kQ, kNK, 0, 0);  // q (K-major) x k (K-major)
-      const uint32_t qh = smem_u32(smem + SM::qh), ql = smem_u32(smem + SM::ql),
-                     kh = smem_u32(smem + SM::kh), kl = smem_u32(smem + SM::kl);
-#pragma unroll
-      for (int j = 0; j < kDh / 16; ++j)
-        tc::mma_ss(tmem + kTmS, tc::sdesc(qh + 32 * j, 16, 1024), tc::sdesc(kh + 32 * j, 16, 1024),
-                   id_s, j > 0);
-      if (SPLIT || ROPE) {
-#pragma unroll
-        for (int j = 0; j < kDh / 16; ++j)
-          tc::mma_ss(tmem + kTmS, tc::sdesc(qh + 32 * j, 16, 1024),
-                     tc::sdesc(kl + 32 * j, 16, 1024), id_s, 1u);
-#pragma unroll
-        for (int j = 0; j < kDh / 16; ++j)
-          tc::mma_ss(tmem + kTmS, tc::sdesc(ql + 32 * j, 16, 1024),
-                     tc::sdesc(kh + 32 * j, 16, 1024), id_s, 1u);
-      }
-      tc::mma_commit(&bars[SB_S]);
-    }
+    const bool next = g + 1 < grp;
     tc::mbar_wait(&bars[SB_S], ph, 82);
     tc::tc_fence_after();
-    if (tid == 0 && g + 1 < grp) issue_q(g + 1);  // the scores have read the query tiles
+    if (tid == 0 && next) issue_q(g + 1);  // the scores have read the query tiles
 
-    // the window of row i: keys t in (i - W, i], t >= 0, i.e. columns
-    // c = t - k0 in [32 warp + 1, 32 warp + 95] for this warp's rows
-    float s[3][32];
+    // the window of row i is keys t in (i - W, i], t >= 0: columns t - k0 in
+    // [32 qd + 1, 32 qd + 95]; this thread takes 48 of them
+    float s[3][16];
 #pragma unroll
-    for (int rel = 0; rel < 3; ++rel) tc::tmem_ld32(trow + kTmS + 32 * (warp + rel), s[rel]);
+    for (int k = 0; k < 3; ++k) tc::tmem_ld16(trow + kTmS + cw + 16 * k, s[k]);
     tc::tmem_wait_ld();
     float mx = ms;
-    const int t0 = k0 + 32 * warp;
 #pragma unroll
-    for (int rel = 0; rel < 3; ++rel)
+    for (int k = 0; k < 3; ++k)
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const int t = t0 + 32 * rel + u;
+      for (int u = 0; u < 16; ++u) {
+        const int t = k0 + cw + 16 * k + u;
         const bool ok = t <= i && t > i - W && t >= 0;
-        const float x = ok ? s[rel][u] * scale_log2 : -INFINITY;
-        s[rel][u] = x;
+        const float x = ok ? s[k][u] * scale_log2 : -INFINITY;
+        s[k][u] = x;
         mx = fmaxf(mx, x);
       }
-    float l = ls * exp2f(ms - mx);
+    red[hf * kQ + r] = mx;
+    __syncthreads();
+    mx = fmaxf(mx, red[(1 - hf) * kQ + r]);
+    float l = 0.f;
 #pragma unroll
-    for (int rel = 0; rel < 3; ++rel) {
-      uint32_t phi[16], plo[16];
+    for (int k = 0; k < 3; ++k) {
+      uint32_t phi[8], plo[8];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float p0 = exp2f(s[rel][2 * j] - mx), p1 = exp2f(s[rel][2 * j + 1] - mx);
+      for (int j = 0; j < 8; ++j) {
+        const float p0 = exp2f(s[k][2 * j] - mx), p1 = exp2f(s[k][2 * j + 1] - mx);
         l += p0 + p1;
         const uint32_t hpk = pack_bf16(p0, p1);
         phi[j] = hpk;
         plo[j] = pack_bf16(p0 - bf16_lo(hpk), p1 - bf16_hi(hpk));
       }
-      tc::tmem_st16(trow + kTmPh + 16 * (warp + rel), phi);
-      tc::tmem_st16(trow + kTmPl + 16 * (warp + rel), plo);
+      tc::tmem_st8(trow + kTmPh + cw / 2 + 8 * k, phi);
+      tc::tmem_st8(trow + kTmPl + cw / 2 + 8 * k, plo);
     }
-    {
-      uint32_t zero[16];
+    {  // p is zero outside the window: packed columns [0, 16 qd) and [16 qd + 48, 96)
+      uint32_t zero[8];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) zero[j] = 0u;
+      for (int j = 0; j < 8; ++j) zero[j] = 0u;
+      const int z0 = hf ? 16 * qd + 48 : 0, z1 = hf ? kNK / 2 : 16 * qd;
 #pragma unroll 1
-      for (int cb = 0; cb < kNK / 32; ++cb)
-        if (cb < warp || cb >= warp + 3) {
-          tc::tmem_st16(trow + kTmPh + 16 * cb, zero);
-          tc::tmem_st16(trow + kTmPl + 16 * cb, zero);
-        }
+      for (int c = z0; c < z1; c += 8) {
+        tc::tmem_st8(trow + kTmPh + c, zero);
+        tc::tmem_st8(trow + kTmPl + c, zero);
+      }
     }
+    red[2 * kQ + hf * kQ + r] = l;  // row sums, read after the P V sync
     tc::tmem_wait_st();
     tc::tc_fence_before();
     __syncthreads();
@@ -272,38 +310,46 @@ swa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
                    1u);
       tc::mma_commit(&bars[SB_O]);
     }
+    const float lrow = ls * exp2f(ms - mx) + red[2 * kQ + r] + red[3 * kQ + r];
+    // while P V runs: the next head's query tiles
+    if (next) {
+      tc::mbar_wait(&bars[SB_Q], ph ^ 1u, 81);
+      if (ROPE) rotate_q(g + 1);
+      tc::fence_proxy_async_smem();
+    }
     tc::mbar_wait(&bars[SB_O], ph, 83);
     tc::tc_fence_after();
-    const float inv = 1.f / l;
-    const size_t row = hrow + i;
-#pragma unroll 1
-    for (int db = 0; db < kDh / 32; ++db) {
-      float o[32];
-      tc::tmem_ld32(trow + kTmO + 32 * db, o);
-      tc::tmem_wait_ld();
-      if (i < L) {
-        bf16* yr = y + row * kDh + 32 * db;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint4 w;
-          w.x = pack_bf16(o[8 * q4] * inv, o[8 * q4 + 1] * inv);
-          w.y = pack_bf16(o[8 * q4 + 2] * inv, o[8 * q4 + 3] * inv);
-          w.z = pack_bf16(o[8 * q4 + 4] * inv, o[8 * q4 + 5] * inv);
-          w.w = pack_bf16(o[8 * q4 + 6] * inv, o[8 * q4 + 7] * inv);
-          reinterpret_cast<uint4*>(yr)[q4] = w;
-        }
-        if (y32) {
-          float4* d32 = reinterpret_cast<float4*>(y32 + row * kDh + 32 * db);
-#pragma unroll
-          for (int q4 = 0; q4 < 8; ++q4)
-            d32[q4] = make_float4(o[4 * q4] * inv, o[4 * q4 + 1] * inv, o[4 * q4 + 2] * inv,
-                                  o[4 * q4 + 3] * inv);
-        }
-      }
-    }
-    if (lse && i < L) lse[row] = mx * kLn2f + logf(l);
     tc::tc_fence_before();
-    __syncthreads();  // o and the s / p columns are free for the next head
+    __syncthreads();  // P V done (s / p columns free), the next query tiles written
+    if (tid == 0 && next) issue_s();  // runs while the warps write this head's output
+
+    const float inv = 1.f / lrow;
+    const size_t row = ((size_t)b * H + hk * grp + g) * L + i;
+    float o[32];
+    tc::tmem_ld32(trow + kTmO + 32 * hf, o);
+    tc::tmem_wait_ld();
+    if (i < L) {
+      bf16* yr = y + row * kDh + 32 * hf;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint4 w;
+        w.x = pack_bf16(o[8 * q4] * inv, o[8 * q4 + 1] * inv);
+        w.y = pack_bf16(o[8 * q4 + 2] * inv, o[8 * q4 + 3] * inv);
+        w.z = pack_bf16(o[8 * q4 + 4] * inv, o[8 * q4 + 5] * inv);
+        w.w = pack_bf16(o[8 * q4 + 6] * inv, o[8 * q4 + 7] * inv);
+        reinterpret_cast<uint4*>(yr)[q4] = w;
+      }
+      if (y32) {
+        float4* d32 = reinterpret_cast<float4*>(y32 + row * kDh + 32 * hf);
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4)
+          d32[q4] = make_float4(o[4 * q4] * inv, o[4 * q4 + 1] * inv, o[4 * q4 + 2] * inv,
+                                o[4 * q4 + 3] * inv);
+      }
+      if (lse && hf == 0) lse[row] = mx * kLn2f + logf(lrow);
+    }
+    tc::tc_fence_before();
+    __syncthreads();  // o and the row-sum slots are free for the next head
   }
   if (warp == 0) {
     tc::tc_fence_after();
@@ -358,7 +404,7 @@ int launch_swa_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
   const int nqb = ceil_div(L, kQ);
   const float scale_log2 = kLog2e / sqrtf((float)kDh);
   swa_fwd_tc_kernel<ROPE, SPLIT, CT>
-      <<<(unsigned)((long long)B * Hkv * nqb), kQ, SwaTcSmem::bytes, st>>>(
+      <<<(unsigned)((long long)B * Hkv * nqb), kThreads, SwaTcSmem::bytes, st>>>(
           mq, mk, mv, mql, mkl, static_cast<const CT*>(cs), static_cast<const CT*>(sn), cs_sb,
           cs_sl, meta, n_meta, W, scale_log2, H, H / Hkv, L, nqb, y, sv.lse, sv.y32, qh_out,
           ql_out, kh_out, kl_out);
