@@ -260,10 +260,11 @@ int lz_hedgehog_set_tc(int on);
  * tests and tuning, process-wide. */
 long long lz_hedgehog_set_rows_max(long long rows);
 
-/* SWA forwards (lz_swa_fwd_gqa and lz_swa_rope_fwd) on the tensor cores (1,
- * the default: tcgen05 kernel for head dim 64, window <= 64, bf16 operands)
- * or on the 64-row warp-MMA kernels (0). Returns the previous setting; a hook
- * for tests and tuning, process-wide. */
+/* SWA forwards (lz_swa_fwd_gqa and lz_swa_rope_fwd) and the dq and dk / dv
+ * kernels of the backward on the tensor cores (1, the default: tcgen05
+ * kernels for head dim 64, window <= 64, bf16 operands) or on the 64-row
+ * warp-MMA kernels (0). Returns the previous setting; a hook for tests and
+ * tuning, process-wide. */
 int lz_swa_set_tc(int on);
 
 /* The same for x [B, Hx, L, Dh] at element strides (x_sb, x_sh, x_sl) with Dh

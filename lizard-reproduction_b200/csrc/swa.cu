@@ -912,11 +912,22 @@ int launch_swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, 
   count_launches(1);
   rc = check_launch("swa_bwd_delta_kernel");
   if (rc) return rc;
-  swa_bwd_dq_kernel<DP, SPLIT><<<(unsigned)((long long)BH * nb), 128, SQ::bytes, st>>>(
-      q, k, v, ql, kl, dy, lse, wk.delta, W, scale, H, grp, L, D, nb, vec, dq, gdt);
-  count_launches(1);
-  rc = check_launch("swa_bwd_dq_kernel");
+  // head dim 64, window <= 64: the tensor-core dq and dk / dv unless switched off
+  rc = D == 64 ? swa_bwd_dq_tc(q, k, v, ql, kl, dy, lse, wk.delta, W, dq, gdt, BH / H, H,
+                               H / grp, L, D, st)
+               : LZ_ERR_UNSUPPORTED;
+  if (rc == LZ_ERR_UNSUPPORTED) {
+    swa_bwd_dq_kernel<DP, SPLIT><<<(unsigned)((long long)BH * nb), 128, SQ::bytes, st>>>(
+        q, k, v, ql, kl, dy, lse, wk.delta, W, scale, H, grp, L, D, nb, vec, dq, gdt);
+    count_launches(1);
+    rc = check_launch("swa_bwd_dq_kernel");
+  }
   if (rc) return rc;
+  if (D == 64) {
+    rc = swa_bwd_dkv_tc(q, k, v, ql, kl, dy, lse, wk.delta, W, dk, dv, gdt, BH / H, H, H / grp,
+                        L, D, st);
+    if (rc != LZ_ERR_UNSUPPORTED) return rc;
+  }
   swa_bwd_dkv_kernel<DP, SPLIT><<<(unsigned)((long long)(BH / grp) * nb), 128, SKV::bytes, st>>>(
       q, k, v, ql, kl, dy, lse, wk.delta, W, scale, H, grp, L, D, nb, vec, dk, dv, gdt);
   count_launches(1);

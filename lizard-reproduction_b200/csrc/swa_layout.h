@@ -75,6 +75,14 @@ int swa_fwd_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, cons
                const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B, int H,
                int Hkv, int L, int D, cudaStream_t st);
 
+// dq and dk, dv of the backward on the tensor cores (same shapes as the forward).
+int swa_bwd_dq_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
+                  const bf16* dy, const float* lse, const float* delta, int W, void* dq, int gdt,
+                  int B, int H, int Hkv, int L, int D, cudaStream_t st);
+int swa_bwd_dkv_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
+                   const bf16* dy, const float* lse, const float* delta, int W, void* dk,
+                   void* dv, int gdt, int B, int H, int Hkv, int L, int D, cudaStream_t st);
+
 int swa_fwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
             const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B, int H,
             int Hkv, int L, int D, cudaStream_t st);

@@ -1,7 +1,9 @@
-// Sliding-window attention forward on the 5th-generation tensor cores
-// (tcgen05 + TMEM + TMA) for head dim 64 and windows of at most 64 keys, the
-// Lizard layer's shape (reference: src/lizard_attention.py:34-44 and the
-// Triton forward src/kernels/swa.py:19-59).
+// Sliding-window attention on the 5th-generation tensor cores (tcgen05 + TMEM
+// + TMA) for head dim 64 and windows of at most 64 keys, the Lizard layer's
+// shape (reference: src/lizard_attention.py:34-44 and the Triton kernels
+// src/kernels/swa.py:19-133): the forward (below), and the dq and dk / dv
+// kernels of the backward (further down; delta and the sink gradient stay in
+// swa.cu).
 //
 // One CTA of 8 warps takes 128 query rows [q0, q0 + 128) of one batch row and
 // one key/value head, and every query head of that head's group in turn:
@@ -37,7 +39,10 @@ namespace lz {
 namespace {
 
 constexpr int kQ = 128;   // query rows per CTA (= TMEM lanes)
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;  // the row warps (two per TMEM lane quadrant)
+constexpr int kCtaThreads = kThreads + 32;  // + the TMA / MMA warp of the backward kernels
+// named barriers of the backward: row warps -> MMA warp (operands in TMEM), row warps
+enum { NB_PREADY = 2, NB_ROWS = 3 };
 constexpr int kNK = 192;  // key rows per CTA: [q0 - 64, q0 + 128)
 constexpr int kDh = 64;   // head dim (one 128-byte swizzle row)
 constexpr float kLn2f = 0.6931471805599453f;
@@ -412,6 +417,477 @@ int launch_swa_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
   return check_launch("swa_fwd_tc_kernel");
 }
 
+// ------------------------------------------------------------ backward: dk, dv
+// One CTA of 9 warps per 128 key rows [k0, k0 + 128) of one (batch row,
+// key/value head); it walks the query heads of the group, each through the 192
+// query rows [k0, k0 + 192) that can see those keys (W <= 64), with the query /
+// dy tiles of the next head in a second shared-memory stage:
+//   warp 8   : TMA; s^T = k q^T (hi / lo terms as the forward), dp^T = v dy^T
+//              -> TMEM [128 x 192] each; then dv += p^T dy and dk += ds^T q
+//              with p^T, ds^T from TMEM -> TMEM [128 x 64] each, summed over
+//              the group's heads
+//   8 warps  : key row t = TMEM lane t, the 96 query columns that can see it
+//              split between the two warps of the lane quadrant:
+//              p = exp(s scale - lse_i), ds = p (dp - delta_i), written as bf16
+//              over s^T once every score column of the CTA has been read
+// The arithmetic is that of swa_bwd_dkv_kernel (bf16 p and ds, q_hi in dk;
+// the reference's Triton backward, src/kernels/swa.py:97-133). 195 KB of
+// shared memory and all 512 TMEM columns: one CTA per SM.
+constexpr int kBK = 128;  // key rows per CTA
+constexpr int kBQ = 192;  // query rows per head: [k0, k0 + 192)
+struct DkvTcSmem {
+  static constexpr size_t kh = 0, kl = kh + kBK * 128, v = kl + kBK * 128, st = v + kBK * 128;
+  static constexpr size_t sq = 0, sql = kBQ * 128, sdy = 2 * kBQ * 128, sbytes = 3 * kBQ * 128;
+  static constexpr size_t rows = st + 2 * sbytes;  // [2 stages][lse | delta][192] fp32
+  static constexpr size_t bars = rows + 2 * 2 * kBQ * 4, slot = bars + 64, bytes = slot + 16;
+};
+// TMEM: s^T [0, 192) with p^T (bf16 pairs, [0, 96)) and ds^T ([96, 192)) over
+// it; dp^T [192, 384); dv [384, 448); dk [448, 512)
+constexpr uint32_t kTbS = 0, kTbP = 0, kTbDs = 96, kTbDp = 192, kTbDv = 384, kTbDk = 448,
+                   kTbCols = 512;
+enum { DB_KV = 0, DB_Q0, DB_Q1, DB_SD, DB_PD };
+
+// 32 gradient values of a row, scaled, to fp32 or bf16 (16-byte stores)
+__device__ __forceinline__ void store_grad32(void* out, size_t at, const float (&o)[32], float mul,
+                                             int gdt) {
+  if (gdt == LZ_DTYPE_BF16) {
+    uint4* d16 = reinterpret_cast<uint4*>(static_cast<bf16*>(out) + at);
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4)
+      d16[q4] = make_uint4(pack_bf16(o[8 * q4] * mul, o[8 * q4 + 1] * mul),
+                           pack_bf16(o[8 * q4 + 2] * mul, o[8 * q4 + 3] * mul),
+                           pack_bf16(o[8 * q4 + 4] * mul, o[8 * q4 + 5] * mul),
+                           pack_bf16(o[8 * q4 + 6] * mul, o[8 * q4 + 7] * mul));
+  } else {
+    float4* d32 = reinterpret_cast<float4*>(static_cast<float*>(out) + at);
+#pragma unroll
+    for (int q4 = 0; q4 < 8; ++q4)
+      d32[q4] = make_float4(o[4 * q4] * mul, o[4 * q4 + 1] * mul, o[4 * q4 + 2] * mul,
+                            o[4 * q4 + 3] * mul);
+  }
+}
+
+template <bool SPLIT>
+__global__ void __launch_bounds__(kCtaThreads, 1)
+swa_bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tql,
+                      const __grid_constant__ CUtensorMap tdy, const __grid_constant__ CUtensorMap tk,
+                      const __grid_constant__ CUtensorMap tkl, const __grid_constant__ CUtensorMap tv,
+                      const float* __restrict__ lse, const float* __restrict__ delta, int W,
+                      float scale, int H, int grp, int L, int nkt, void* __restrict__ dk,
+                      void* __restrict__ dv, int gdt) {
+  using SM = DkvTcSmem;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 88u);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::bars);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + SM::slot);
+  float* rows = reinterpret_cast<float*>(smem + SM::rows);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kt = blockIdx.x % nkt, bk = blockIdx.x / nkt;
+  const int Hkv = H / grp, b = bk / Hkv, hk = bk - b * Hkv;
+  const int k0 = kt * kBK;
+  constexpr uint32_t kTileK = kBK * 128, kTileQ = kBQ * 128;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int j = 0; j < 5; ++j) tc::mbar_init(&bars[j], 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == 8) {
+    tc::tmem_alloc(tslot, kTbCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 8) {
+    const bool issuer = lane == 0;
+    auto load_stage = [&](int g) {  // query / dy rows of head hk * grp + g into stage g & 1
+      const int h = hk * grp + g;
+      unsigned char* st = smem + SM::st + (g & 1) * SM::sbytes;
+      uint64_t* bar = &bars[DB_Q0 + (g & 1)];
+      tc::mbar_expect_tx(bar, (SPLIT ? 3 : 2) * kTileQ);
+      tc::tma_load_4d(st + SM::sq, &tq, 0, k0, h, b, bar);
+      if (SPLIT) tc::tma_load_4d(st + SM::sql, &tql, 0, k0, h, b, bar);
+      tc::tma_load_4d(st + SM::sdy, &tdy, 0, k0, h, b, bar);
+    };
+    if (issuer) {
+      tc::mbar_expect_tx(&bars[DB_KV], (SPLIT ? 3 : 2) * kTileK);
+      tc::tma_load_4d(smem + SM::kh, &tk, 0, k0, hk, b, &bars[DB_KV]);
+      if (SPLIT) tc::tma_load_4d(smem + SM::kl, &tkl, 0, k0, hk, b, &bars[DB_KV]);
+      tc::tma_load_4d(smem + SM::v, &tv, 0, k0, hk, b, &bars[DB_KV]);
+      load_stage(0);
+      if (grp > 1) load_stage(1);
+      tc::mbar_wait(&bars[DB_KV], 0, 70);
+    }
+    __syncwarp();
+    for (int g = 0; g < grp; ++g) {
+      const uint32_t ph = (uint32_t)g & 1u;
+      unsigned char* st = smem + SM::st + (g & 1) * SM::sbytes;
+      if (issuer) {
+        tc::mbar_wait(&bars[DB_Q0 + (g & 1)], (uint32_t)(g >> 1) & 1u, 71);
+        if (g > 0) tc::mbar_wait(&bars[DB_PD], ph ^ 1u, 72);  // p / ds of head g - 1 read
+        tc::tc_fence_after();
+        constexpr uint32_t id_s = tc::idesc_bf16(kBK, kBQ, 0, 0);  // K-major x K-major
+        const uint32_t kh = smem_u32(smem + SM::kh), kl = smem_u32(smem + SM::kl),
+                       va = smem_u32(smem + SM::v), qh = smem_u32(st + SM::sq),
+                       ql = smem_u32(st + SM::sql), dya = smem_u32(st + SM::sdy);
+#pragma unroll
+        for (int j = 0; j < kDh / 16; ++j)
+          tc::mma_ss(tmem + kTbS, tc::sdesc(kh + 32 * j, 16, 1024),
+                     tc::sdesc(qh + 32 * j, 16, 1024), id_s, j > 0);
+        if (SPLIT) {
+#pragma unroll
+          for (int j = 0; j < kDh / 16; ++j)
+            tc::mma_ss(tmem + kTbS, tc::sdesc(kh + 32 * j, 16, 1024),
+                       tc::sdesc(ql + 32 * j, 16, 1024), id_s, 1u);
+#pragma unroll
+          for (int j = 0; j < kDh / 16; ++j)
+            tc::mma_ss(tmem + kTbS, tc::sdesc(kl + 32 * j, 16, 1024),
+                       tc::sdesc(qh + 32 * j, 16, 1024), id_s, 1u);
+        }
+#pragma unroll
+        for (int j = 0; j < kDh / 16; ++j)
+          tc::mma_ss(tmem + kTbDp, tc::sdesc(va + 32 * j, 16, 1024),
+                     tc::sdesc(dya + 32 * j, 16, 1024), id_s, j > 0);
+        tc::mma_commit(&bars[DB_SD]);
+      }
+      __syncwarp();
+      tc::named_bar_sync(NB_PREADY, kCtaThreads);  // p^T and ds^T in TMEM
+      if (issuer) {
+        tc::tc_fence_after();
+        constexpr uint32_t id_o = tc::idesc_bf16(kBK, kDh, 0, 1);  // TMEM x MN-major
+        const uint32_t qh = smem_u32(st + SM::sq), dya = smem_u32(st + SM::sdy);
+#pragma unroll
+        for (int j = 0; j < kBQ / 16; ++j)
+          tc::mma_ts(tmem + kTbDv, tmem + kTbP + 8 * j, tc::sdesc(dya + 2048 * j, kTileQ, 1024),
+                     id_o, (g > 0 || j > 0) ? 1u : 0u);
+#pragma unroll
+        for (int j = 0; j < kBQ / 16; ++j)
+          tc::mma_ts(tmem + kTbDk, tmem + kTbDs + 8 * j, tc::sdesc(qh + 2048 * j, kTileQ, 1024),
+                     id_o, (g > 0 || j > 0) ? 1u : 0u);
+        tc::mma_commit(&bars[DB_PD]);
+        if (g + 2 < grp) {
+          tc::mbar_wait(&bars[DB_PD], ph, 73);  // stage g & 1 read by every MMA of head g
+          load_stage(g + 2);
+        }
+      }
+      __syncwarp();
+    }
+  } else {
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = 32 * qd + lane, t = k0 + r;  // this thread's key row
+    const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
+    const int cw = 32 * qd + 48 * hf;  // first query column of this thread's half window
+    for (int g = 0; g < grp; ++g) {
+      const uint32_t ph = (uint32_t)g & 1u;
+      const size_t bh = (size_t)b * H + hk * grp + g;
+      float* rl = rows + (g & 1) * 2 * kBQ;  // lse, then delta, of query rows k0 + c
+      for (int c = tid; c < kBQ; c += kThreads) {
+        const int i = k0 + c;
+        rl[c] = i < L ? lse[bh * L + i] : 0.f;
+        rl[kBQ + c] = i < L ? delta[bh * L + i] : 0.f;
+      }
+      tc::named_bar_sync(NB_ROWS, kThreads);
+      tc::mbar_wait(&bars[DB_SD], ph, 74);
+      tc::tc_fence_after();
+      // p and ds of the 48 columns in registers (bf16 pairs) before any store:
+      // the stores land on score columns that this thread and its partner warp
+      // (the other half of the lane quadrant) read
+      uint32_t pk[3][8], dk8[3][8];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        float sv[16], dpv[16];
+        tc::tmem_ld16(trow + kTbS + cw + 16 * k, sv);
+        tc::tmem_ld16(trow + kTbDp + cw + 16 * k, dpv);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float p2[2], d2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int c = cw + 16 * k + 2 * j + e, i = k0 + c;
+            const bool ok = i >= t && i < t + W && i < L && t < L;
+            const float p = ok ? __expf(sv[2 * j + e] * scale - rl[c]) : 0.f;
+            p2[e] = p;
+            d2[e] = p * (dpv[2 * j + e] - rl[kBQ + c]);
+          }
+          pk[k][j] = pack_bf16(p2[0], p2[1]);
+          dk8[k][j] = pack_bf16(d2[0], d2[1]);
+        }
+      }
+      tc::tc_fence_before();
+      tc::named_bar_sync(NB_ROWS, kThreads);  // every score column of the CTA read
+      tc::tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        tc::tmem_st8(trow + kTbP + cw / 2 + 8 * k, pk[k]);
+        tc::tmem_st8(trow + kTbDs + cw / 2 + 8 * k, dk8[k]);
+      }
+      {  // zero outside the window: packed columns [0, 16 qd) and [16 qd + 48, 96)
+        uint32_t zero[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) zero[j] = 0u;
+        const int z0 = hf ? 16 * qd + 48 : 0, z1 = hf ? kBQ / 2 : 16 * qd;
+#pragma unroll 1
+        for (int c = z0; c < z1; c += 8) {
+          tc::tmem_st8(trow + kTbP + c, zero);
+          tc::tmem_st8(trow + kTbDs + c, zero);
+        }
+      }
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      tc::named_bar_arrive(NB_PREADY, kCtaThreads);
+    }
+    // dv (warps of half 0) and dk (half 1) of this key row, summed over the group
+    tc::mbar_wait(&bars[DB_PD], (uint32_t)(grp - 1) & 1u, 75);
+    tc::tc_fence_after();
+    const size_t orow = ((size_t)bk * L + t) * kDh;
+#pragma unroll 1
+    for (int db = 0; db < 2; ++db) {
+      float o[32];
+      tc::tmem_ld32(trow + (hf ? kTbDk : kTbDv) + 32 * db, o);
+      tc::tmem_wait_ld();
+      if (t < L) store_grad32(hf ? dk : dv, orow + 32 * db, o, hf ? scale : 1.f, gdt);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTbCols);
+  }
+}
+
+// ------------------------------------------------------------ backward: dq
+// One CTA of 9 warps per 128 query rows [q0, q0 + 128) of one (batch row,
+// key/value head) and each query head of the group in turn; keys / values
+// [q0 - 64, q0 + 128) as in the forward:
+//   warp 8   : TMA; s = q k^T (hi / lo terms), dp = dy v^T -> TMEM [128 x 192]
+//              each; then dq = ds k_hi with ds from TMEM -> TMEM [128 x 64]
+//   8 warps  : query row i = TMEM lane i, the 96 key columns of its window
+//              split between the two warps of the lane quadrant:
+//              ds = exp(s scale - lse_i) (dp - delta_i) written as bf16 over s
+//              once every score column has been read; then dq_i = scale
+//              (ds k)_i to HBM
+// The arithmetic is that of swa_bwd_dq_kernel (bf16 ds, k_hi; the reference's
+// Triton backward, src/kernels/swa.py:62-95). The query / dy tiles of the next
+// head load into a second stage. 169 KB of shared memory, 512 TMEM columns.
+struct DqTcSmem {
+  static constexpr size_t kh = 0, kl = kh + kNK * 128, v = kl + kNK * 128, st = v + kNK * 128;
+  static constexpr size_t sq = 0, sql = kQ * 128, sdy = 2 * kQ * 128, sbytes = 3 * kQ * 128;
+  static constexpr size_t bars = st + 2 * sbytes, slot = bars + 64, bytes = slot + 16;
+};
+// TMEM: s [0, 192) with ds (bf16 pairs, [0, 96)) over it; dp [192, 384); dq [384, 448)
+constexpr uint32_t kTqS = 0, kTqDs = 0, kTqDp = 192, kTqDq = 384, kTqCols = 512;
+enum { QB_KV = 0, QB_Q0, QB_Q1, QB_SD, QB_DQ };
+
+template <bool SPLIT>
+__global__ void __launch_bounds__(kCtaThreads, 1)
+swa_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tql,
+                     const __grid_constant__ CUtensorMap tdy, const __grid_constant__ CUtensorMap tk,
+                     const __grid_constant__ CUtensorMap tkl, const __grid_constant__ CUtensorMap tv,
+                     const float* __restrict__ lse, const float* __restrict__ delta, int W,
+                     float scale, int H, int grp, int L, int nqb, void* __restrict__ dq, int gdt) {
+  using SM = DqTcSmem;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 87u);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::bars);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + SM::slot);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qb = blockIdx.x % nqb, bk = blockIdx.x / nqb;
+  const int Hkv = H / grp, b = bk / Hkv, hk = bk - b * Hkv;
+  const int q0 = qb * kQ, k0 = q0 - (kNK - kQ);
+  constexpr uint32_t kTileK = kNK * 128, kTileQ = kQ * 128;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int j = 0; j < 5; ++j) tc::mbar_init(&bars[j], 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == 8) {
+    tc::tmem_alloc(tslot, kTqCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 8) {
+    const bool issuer = lane == 0;
+    auto load_stage = [&](int g) {  // query / dy rows of head hk * grp + g into stage g & 1
+      const int h = hk * grp + g;
+      unsigned char* st = smem + SM::st + (g & 1) * SM::sbytes;
+      uint64_t* bar = &bars[QB_Q0 + (g & 1)];
+      tc::mbar_expect_tx(bar, (SPLIT ? 3 : 2) * kTileQ);
+      tc::tma_load_4d(st + SM::sq, &tq, 0, q0, h, b, bar);
+      if (SPLIT) tc::tma_load_4d(st + SM::sql, &tql, 0, q0, h, b, bar);
+      tc::tma_load_4d(st + SM::sdy, &tdy, 0, q0, h, b, bar);
+    };
+    if (issuer) {
+      tc::mbar_expect_tx(&bars[QB_KV], (SPLIT ? 3 : 2) * kTileK);
+      tc::tma_load_4d(smem + SM::kh, &tk, 0, k0, hk, b, &bars[QB_KV]);
+      if (SPLIT) tc::tma_load_4d(smem + SM::kl, &tkl, 0, k0, hk, b, &bars[QB_KV]);
+      tc::tma_load_4d(smem + SM::v, &tv, 0, k0, hk, b, &bars[QB_KV]);
+      load_stage(0);
+      if (grp > 1) load_stage(1);
+      tc::mbar_wait(&bars[QB_KV], 0, 60);
+    }
+    __syncwarp();
+    for (int g = 0; g < grp; ++g) {
+      const uint32_t ph = (uint32_t)g & 1u;
+      unsigned char* st = smem + SM::st + (g & 1) * SM::sbytes;
+      if (issuer) {
+        tc::mbar_wait(&bars[QB_Q0 + (g & 1)], (uint32_t)(g >> 1) & 1u, 61);
+        if (g > 0) tc::mbar_wait(&bars[QB_DQ], ph ^ 1u, 62);  // ds of head g - 1 read
+        tc::tc_fence_after();
+        constexpr uint32_t id_s = tc::idesc_bf16(kQ, kNK, 0, 0);  // K-major x K-major
+        const uint32_t kh = smem_u32(smem + SM::kh), kl = smem_u32(smem + SM::kl),
+                       va = smem_u32(smem + SM::v), qh = smem_u32(st + SM::sq),
+                       ql = smem_u32(st + SM::sql), dya = smem_u32(st + SM::sdy);
+#pragma unroll
+        for (int j = 0; j < kDh / 16; ++j)
+          tc::mma_ss(tmem + kTqS, tc::sdesc(qh + 32 * j, 16, 1024),
+                     tc::sdesc(kh + 32 * j, 16, 1024), id_s, j > 0);
+        if (SPLIT) {
+#pragma unroll
+          for (int j = 0; j < kDh / 16; ++j)
+            tc::mma_ss(tmem + kTqS, tc::sdesc(qh + 32 * j, 16, 1024),
+                       tc::sdesc(kl + 32 * j, 16, 1024), id_s, 1u);
+#pragma unroll
+          for (int j = 0; j < kDh / 16; ++j)
+            tc::mma_ss(tmem + kTqS, tc::sdesc(ql + 32 * j, 16, 1024),
+                       tc::sdesc(kh + 32 * j, 16, 1024), id_s, 1u);
+        }
+#pragma unroll
+        for (int j = 0; j < kDh / 16; ++j)
+          tc::mma_ss(tmem + kTqDp, tc::sdesc(dya + 32 * j, 16, 1024),
+                     tc::sdesc(va + 32 * j, 16, 1024), id_s, j > 0);
+        tc::mma_commit(&bars[QB_SD]);
+      }
+      __syncwarp();
+      tc::named_bar_sync(NB_PREADY, kCtaThreads);  // ds in TMEM; the previous dq read
+      if (issuer) {
+        tc::tc_fence_after();
+        constexpr uint32_t id_o = tc::idesc_bf16(kQ, kDh, 0, 1);  // TMEM x MN-major
+        const uint32_t kh = smem_u32(smem + SM::kh);
+#pragma unroll
+        for (int j = 0; j < kNK / 16; ++j)
+          tc::mma_ts(tmem + kTqDq, tmem + kTqDs + 8 * j, tc::sdesc(kh + 2048 * j, kTileK, 1024),
+                     id_o, j > 0);
+        tc::mma_commit(&bars[QB_DQ]);
+        if (g + 2 < grp) {
+          tc::mbar_wait(&bars[QB_DQ], ph, 63);  // stage g & 1 read by every MMA of head g
+          load_stage(g + 2);
+        }
+      }
+      __syncwarp();
+    }
+  } else {
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = 32 * qd + lane, i = q0 + r;  // this thread's query row
+    const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
+    const int cw = 32 * qd + 48 * hf;  // first key column of this thread's half window
+    for (int g = 0; g < grp; ++g) {
+      const uint32_t ph = (uint32_t)g & 1u;
+      const size_t row = ((size_t)b * H + hk * grp + g) * L + i;
+      const float lse_i = i < L ? lse[row] : 0.f, dl_i = i < L ? delta[row] : 0.f;
+      tc::mbar_wait(&bars[QB_SD], ph, 64);
+      tc::tc_fence_after();
+      uint32_t dk8[3][8];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        float sv[16], dpv[16];
+        tc::tmem_ld16(trow + kTqS + cw + 16 * k, sv);
+        tc::tmem_ld16(trow + kTqDp + cw + 16 * k, dpv);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float d2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int t = k0 + cw + 16 * k + 2 * j + e;
+            const bool ok = t <= i && t > i - W && t >= 0 && i < L;
+            const float p = ok ? __expf(sv[2 * j + e] * scale - lse_i) : 0.f;
+            d2[e] = p * (dpv[2 * j + e] - dl_i);
+          }
+          dk8[k][j] = pack_bf16(d2[0], d2[1]);
+        }
+      }
+      tc::tc_fence_before();
+      tc::named_bar_sync(NB_ROWS, kThreads);  // every score column of the CTA read
+      tc::tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < 3; ++k) tc::tmem_st8(trow + kTqDs + cw / 2 + 8 * k, dk8[k]);
+      {  // zero outside the window: packed columns [0, 16 qd) and [16 qd + 48, 96)
+        uint32_t zero[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) zero[j] = 0u;
+        const int z0 = hf ? 16 * qd + 48 : 0, z1 = hf ? kNK / 2 : 16 * qd;
+#pragma unroll 1
+        for (int c = z0; c < z1; c += 8) tc::tmem_st8(trow + kTqDs + c, zero);
+      }
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      tc::named_bar_arrive(NB_PREADY, kCtaThreads);
+      tc::mbar_wait(&bars[QB_DQ], ph, 65);
+      tc::tc_fence_after();
+      float o[32];
+      tc::tmem_ld32(trow + kTqDq + 32 * hf, o);  // this warp's 32 columns of dq
+      tc::tmem_wait_ld();
+      if (i < L) store_grad32(dq, row * kDh + 32 * hf, o, scale, gdt);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTqCols);
+  }
+}
+
+// Tensor maps of the backward operands ([B, H or Hkv, L, 64] contiguous bf16);
+// false when one cannot be built.
+bool bwd_maps(const bf16* q, const bf16* ql, const bf16* dy, const bf16* k, const bf16* kl,
+              const bf16* v, int B, int H, int Hkv, int L, int qrows, int krows, CUtensorMap* m) {
+  const long long sl = kDh, sh = (long long)L * kDh;
+  if (!make_tc_map(&m[0], q, L, H, B, H * sh, sh, sl, qrows) ||
+      !make_tc_map(&m[2], dy, L, H, B, H * sh, sh, sl, qrows) ||
+      !make_tc_map(&m[3], k, L, Hkv, B, Hkv * sh, sh, sl, krows) ||
+      !make_tc_map(&m[5], v, L, Hkv, B, Hkv * sh, sh, sl, krows))
+    return false;
+  if (!ql) {
+    m[1] = m[0], m[4] = m[3];
+    return true;
+  }
+  return make_tc_map(&m[1], ql, L, H, B, H * sh, sh, sl, qrows) &&
+         make_tc_map(&m[4], kl, L, Hkv, B, Hkv * sh, sh, sl, krows);
+}
+
+template <typename Kern>
+int ensure_tc_smem(Kern kern, size_t bytes, bool* done) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)bytes);
+    if (e != cudaSuccess) {
+      set_error(std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+      return LZ_ERR_CUDA;
+    }
+    done[dev] = true;
+  }
+  return LZ_OK;
+}
+
 }  // namespace
 
 bool swa_tc_enabled() { return g_swa_tc.load(std::memory_order_relaxed) != 0; }
@@ -464,6 +940,46 @@ int swa_fwd_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, cons
   return launch_swa_tc<false, false, float>(mq, mk, mv, mq, mk, nullptr, nullptr, 0, 0, meta,
                                             n_meta, W, B, H, Hkv, L, y, sv, nullptr, nullptr,
                                             nullptr, nullptr, st);
+}
+
+int swa_bwd_dkv_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
+                   const bf16* dy, const float* lse, const float* delta, int W, void* dk,
+                   void* dv, int gdt, int B, int H, int Hkv, int L, int D, cudaStream_t st) {
+  if (!swa_tc_enabled() || D != kDh || W < 1 || W > kBQ - kBK) return LZ_ERR_UNSUPPORTED;
+  if (!aligned16(dk) || !aligned16(dv)) return LZ_ERR_UNSUPPORTED;
+  CUtensorMap m[6];
+  if (!bwd_maps(q, ql, dy, k, kl, v, B, H, Hkv, L, kBQ, kBK, m)) return LZ_ERR_UNSUPPORTED;
+  const bool split = ql != nullptr;
+  auto kern = split ? swa_bwd_dkv_tc_kernel<true> : swa_bwd_dkv_tc_kernel<false>;
+  static bool done[2][64] = {{false}};
+  const int rc = ensure_tc_smem(kern, DkvTcSmem::bytes, done[split]);
+  if (rc) return rc;
+  const int nkt = ceil_div(L, kBK);
+  kern<<<(unsigned)((long long)B * Hkv * nkt), kCtaThreads, DkvTcSmem::bytes, st>>>(
+      m[0], m[1], m[2], m[3], m[4], m[5], lse, delta, W, 1.f / sqrtf((float)kDh), H, H / Hkv, L,
+      nkt, dk, dv, gdt);
+  count_launches(1);
+  return check_launch("swa_bwd_dkv_tc_kernel");
+}
+
+int swa_bwd_dq_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
+                  const bf16* dy, const float* lse, const float* delta, int W, void* dq, int gdt,
+                  int B, int H, int Hkv, int L, int D, cudaStream_t st) {
+  if (!swa_tc_enabled() || D != kDh || W < 1 || W > kNK - kQ) return LZ_ERR_UNSUPPORTED;
+  if (!aligned16(dq)) return LZ_ERR_UNSUPPORTED;
+  CUtensorMap m[6];
+  if (!bwd_maps(q, ql, dy, k, kl, v, B, H, Hkv, L, kQ, kNK, m)) return LZ_ERR_UNSUPPORTED;
+  const bool split = ql != nullptr;
+  auto kern = split ? swa_bwd_dq_tc_kernel<true> : swa_bwd_dq_tc_kernel<false>;
+  static bool done[2][64] = {{false}};
+  const int rc = ensure_tc_smem(kern, DqTcSmem::bytes, done[split]);
+  if (rc) return rc;
+  const int nqb = ceil_div(L, kQ);
+  kern<<<(unsigned)((long long)B * Hkv * nqb), kCtaThreads, DqTcSmem::bytes, st>>>(
+      m[0], m[1], m[2], m[3], m[4], m[5], lse, delta, W, 1.f / sqrtf((float)kDh), H, H / Hkv, L,
+      nqb, dq, gdt);
+  count_launches(1);
+  return check_launch("swa_bwd_dq_tc_kernel");
 }
 
 int swa_tc_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }

@@ -322,6 +322,12 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Arrive on a named barrier without waiting (the producer side of a
+// producer / consumer hand-off; the consumer warps bar.sync with the same count).
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 __device__ __forceinline__ uint32_t elect_lane0() { return (threadIdx.x & 31) == 0; }
 
 }  // namespace tc
