@@ -329,11 +329,15 @@ def test_swa_rope_fused_declines_shapes_outside_its_tiles(D, xdt):
 
 
 @pytest.mark.parametrize("shape", [(1, 4, 1, 300, 256, 64, 0), (2, 4, 2, 257, 256, 64, 1),
-                                   (1, 4, 4, 200, 128, 64, 0), (1, 2, 2, 130, 128, 128, 1)])
+                                   (1, 4, 4, 200, 128, 64, 0), (1, 2, 2, 130, 128, 128, 1),
+                                   (2, 8, 2, 513, 128, 64, 0), (1, 2, 1, 100, 256, 64, 0),
+                                   (1, 8, 1, 260, 256, 64, 0)])
 def test_gla_split_tensor_core_outputs(shape):
-    """Chunk outputs of the chunk-parallel schedule on the tensor cores (one
-    128-token chunk per CTA; inference) against the oracle and against the
-    warp-MMA output kernel."""
+    """Chunk outputs of the chunk-parallel schedule on the tensor cores
+    (inference) against the oracle and against the warp-MMA output kernel:
+    one 128-token chunk per CTA, or, with a gate shared by the heads and
+    grouped keys / values (one state per key/value head), one CTA per
+    (key/value head, chunk) walking the group's query heads."""
     import lizard_cuda
     from lizard_cuda import _lib
     lib = _lib.load()
