@@ -26,6 +26,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "rope_math.cuh"
 #include "tc.cuh"
 #include <atomic>
 
@@ -706,34 +707,37 @@ hedgehog_fwd_rows_kernel(const XT* __restrict__ x, XRows xm, const float* __rest
 
 // ------------------------------------------------- forward on the tensor cores
 // bf16 x with Dh = 64, Fd = 128 (the model's feature map): persistent CTAs of
-// 4 warps; W is split once into bf16 hi / lo in the 128-byte swizzled K-major
-// layout; 128-row x tiles (of one head, from any batch / head / token strides)
-// come by TMA into a two-stage ring; one thread issues x W_hi^T + x W_lo^T into
-// TMEM [128 x 128]; each thread then takes its row (TMEM lane): max and min of
-// the 128 logits, e+ = exp(l - max) and e- = exp(min - l) written back to TMEM
-// with their sums, and the normalised features stored as bf16.
+// 4 warps, two per SM; W is split once into bf16 hi / lo in the 128-byte
+// swizzled K-major layout; each 128-row x tile (of one head, from any batch /
+// head / token strides) comes by TMA, and the next tile's x loads as soon as
+// this tile's product has read it; one thread issues x W_hi^T + x W_lo^T into
+// TMEM [128 x 128]; each thread then takes its row (TMEM lane): the max and
+// min of the logits, e+ = exp(l - max) and e- = exp(min - l) written back to
+// TMEM (one exponential per feature) with their sums, then the normalised
+// features as bf16 into a 128-byte swizzled staging tile, which TMA stores
+// write out (4 boxes of 128 rows x 64 features; rows past the head's end are
+// not written) while the next tile's product and first passes run.
 constexpr int kTcDh = 64, kTcFd = 128;
 struct HhTcSmem {
-  static constexpr size_t whi = 0, wlo = 16384, x = 32768;  // x: two stages of 16 KB
-  static constexpr size_t bars = x + 2 * 16384, slot = bars + 32, bytes = slot + 16;
+  static constexpr size_t whi = 0, wlo = 16384, x = 32768, out = x + 16384;  // out: 4 x 16 KB
+  static constexpr size_t bars = out + 4 * 16384, slot = bars + 32, bytes = slot + 16;
 };
 
-__global__ void __launch_bounds__(128, 1)
-hedgehog_fwd_tc_kernel(const __grid_constant__ CUtensorMap tx, const float* __restrict__ w,
-                       int H, int L, int ntl, long long ntiles, bf16* __restrict__ f) {
+__global__ void __launch_bounds__(128, 2)
+hedgehog_fwd_tc_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tf,
+                       const float* __restrict__ w, int H, int ntl, long long ntiles) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   if (smem_u32(smem_raw) & 1023) {
     if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 94u);
     return;
   }
   unsigned char* base = smem_raw;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + HhTcSmem::bars);  // full0, full1, mdone
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + HhTcSmem::bars);  // x full, MMA done
   uint32_t* tslot = reinterpret_cast<uint32_t*>(base + HhTcSmem::slot);
   const int tid = threadIdx.x, warp = tid >> 5;
   if (tid == 0) {
     tc::mbar_init(&bars[0], 1);
     tc::mbar_init(&bars[1], 1);
-    tc::mbar_init(&bars[2], 1);
     tc::fence_mbar_init();
   }
   if (warp == 0) {
@@ -763,21 +767,20 @@ hedgehog_fwd_tc_kernel(const __grid_constant__ CUtensorMap tx, const float* __re
   tc::tc_fence_after();
   const uint32_t tmem = *tslot;
   const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-  auto issue = [&](long long t, int st) {
+  auto issue = [&](long long t) {
     const int bh = (int)(t / ntl), t0 = (int)(t - (long long)bh * ntl) * 128;
-    tc::mbar_expect_tx(&bars[st], 16384);
-    tc::tma_load_4d(base + HhTcSmem::x + st * 16384, &tx, 0, t0, bh % H, bh / H, &bars[st]);
+    tc::mbar_expect_tx(&bars[0], 16384);
+    tc::tma_load_4d(base + HhTcSmem::x, &tx, 0, t0, bh % H, bh / H, &bars[0]);
   };
-  if (tid == 0 && (long long)blockIdx.x < ntiles) issue(blockIdx.x, 0);
+  if (tid == 0 && (long long)blockIdx.x < ntiles) issue(blockIdx.x);
   int i = 0;
   for (long long t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
-    const int st = i & 1;
+    const uint32_t ph = (uint32_t)i & 1u;
     if (tid == 0) {
-      if (t + gridDim.x < ntiles) issue(t + gridDim.x, st ^ 1);  // that stage's MMA is done
-      tc::mbar_wait(&bars[st], (i >> 1) & 1, 70);
+      tc::mbar_wait(&bars[0], ph, 70);
       tc::tc_fence_after();
       constexpr uint32_t id = tc::idesc_bf16(128, 128, 0, 0);
-      const uint32_t xa = smem_u32(base + HhTcSmem::x + st * 16384);
+      const uint32_t xa = smem_u32(base + HhTcSmem::x);
       const uint32_t wh = smem_u32(base + HhTcSmem::whi), wl = smem_u32(base + HhTcSmem::wlo);
 #pragma unroll
       for (int j = 0; j < kTcDh / 16; ++j)
@@ -787,11 +790,12 @@ hedgehog_fwd_tc_kernel(const __grid_constant__ CUtensorMap tx, const float* __re
       for (int j = 0; j < kTcDh / 16; ++j)
         tc::mma_ss(tmem, tc::sdesc(xa + 32 * j, 16, 1024), tc::sdesc(wl + 32 * j, 16, 1024), id,
                    1u);
-      tc::mma_commit(&bars[2]);
+      tc::mma_commit(&bars[1]);
     }
-    tc::mbar_wait(&bars[2], i & 1, 71);
+    tc::mbar_wait(&bars[1], ph, 71);
     tc::tc_fence_after();
-    const int bh = (int)(t / ntl), row = (int)(t - (long long)bh * ntl) * 128 + tid;
+    if (tid == 0 && t + gridDim.x < ntiles) issue(t + gridDim.x);  // the product has read x
+    // pass 1: max and min of the row's logits
     float mx = -INFINITY, mn = INFINITY;
 #pragma unroll 1
     for (int q = 0; q < 4; ++q) {
@@ -804,9 +808,11 @@ hedgehog_fwd_tc_kernel(const __grid_constant__ CUtensorMap tx, const float* __re
         mn = fminf(mn, l[j]);
       }
     }
+    // pass 2: e+ = exp(l - max) over the logits' columns and e- = exp(min - l) at
+    // 128 + the same (fp32 in TMEM), and their sums: one exponential per feature
     float sp = 0.f, sm = 0.f;
 #pragma unroll 1
-    for (int q = 0; q < 4; ++q) {  // e+ over the logits' columns, e- at 128 + the same
+    for (int q = 0; q < 4; ++q) {
       float l[32];
       tc::tmem_ld32(trow + 32 * q, l);
       tc::tmem_wait_ld();
@@ -826,33 +832,39 @@ hedgehog_fwd_tc_kernel(const __grid_constant__ CUtensorMap tx, const float* __re
     }
     tc::tmem_wait_st();
     const float ip = 1.f / sp, im = 1.f / sm;
-    const bool valid = row < L;
-    bf16* out = f + ((size_t)bh * L + row) * (2 * kTcFd);
+    if (tid == 0 && i > 0) tc::bulk_wait_read0();  // the last tile's stores have read the staging
+    __syncthreads();
+    // pass 3: normalised features into the staging tile (box b = features 64b..64b+63)
+    const int r = tid;
 #pragma unroll 1
-    for (int part = 0; part < 2; ++part) {  // e+ -> features 0..127, e- -> 128..255
-      const float inv = part ? im : ip;
-#pragma unroll 1
-      for (int q = 0; q < 4; ++q) {
-        float a[32];
-        tc::tmem_ld32(trow + 128 * part + 32 * q, a);
-        tc::tmem_wait_ld();
-        if (valid) {
+    for (int q = 0; q < 8; ++q) {  // feature columns 32q..32q+31 (e+ then e-)
+      float a[32];
+      tc::tmem_ld32(trow + 32 * q, a);
+      tc::tmem_wait_ld();
+      const float inv = q < 4 ? ip : im;
+      unsigned char* box = base + HhTcSmem::out + (q >> 1) * 16384 + r * 128;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            uint4 u;
-            u.x = pack_bf16(a[8 * k] * inv, a[8 * k + 1] * inv);
-            u.y = pack_bf16(a[8 * k + 2] * inv, a[8 * k + 3] * inv);
-            u.z = pack_bf16(a[8 * k + 4] * inv, a[8 * k + 5] * inv);
-            u.w = pack_bf16(a[8 * k + 6] * inv, a[8 * k + 7] * inv);
-            *reinterpret_cast<uint4*>(out + kTcFd * part + 32 * q + 8 * k) = u;
-          }
-        }
+      for (int k = 0; k < 4; ++k) {
+        float e8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) e8[u] = a[8 * k + u] * inv;
+        const int c = 4 * (q & 1) + k;  // 16-byte chunk within the box row
+        *reinterpret_cast<uint4*>(box + ((c ^ (r & 7)) << 4)) = pack8(e8);
       }
     }
+    tc::fence_proxy_async_smem();
     tc::tc_fence_before();
-    __syncthreads();  // TMEM and the x stage are free for the next tile
-    tc::tc_fence_after();
+    __syncthreads();  // staging written; TMEM free for the next product
+    if (tid == 0) {
+      tc::tc_fence_after();
+      const int bh = (int)(t / ntl), t0 = (int)(t - (long long)bh * ntl) * 128;
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+        tc::tma_store_3d(&tf, base + HhTcSmem::out + b * 16384, 64 * b, t0, bh);
+      tc::bulk_commit();
+    }
   }
+  if (tid == 0) tc::bulk_wait0();
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -978,16 +990,24 @@ int hedgehog_fwd_tc(const void* x, const XRows& xm, const float* w, int R, bf16*
          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return LZ_ERR_UNSUPPORTED;
-  // at most two CTAs per SM (each holds 256 TMEM columns): ask for more than a
-  // third of the shared memory
-  const size_t smem = std::max<size_t>(HhTcSmem::bytes, 80 * 1024);
+  // features [heads, L, 256] as a 3-D map {256, L, heads}, box {64, 128, 1}: stores clip
+  // at each head's last row
+  CUtensorMap mf;
+  cuuint64_t fdims[3] = {(cuuint64_t)(2 * kTcFd), (cuuint64_t)xm.L, (cuuint64_t)heads};
+  cuuint64_t fstr[2] = {(cuuint64_t)(2 * kTcFd * 2), (cuuint64_t)xm.L * 2 * kTcFd * 2};
+  cuuint32_t fbox[3] = {64, 128, 1};
+  cuuint32_t festr[3] = {1, 1, 1};
+  if (fn(&mf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, f, fdims, fstr, fbox, festr,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return LZ_ERR_UNSUPPORTED;
   static bool done[64] = {false};
-  int rc = hh_attr(hedgehog_fwd_tc_kernel, smem, done);
+  int rc = hh_attr(hedgehog_fwd_tc_kernel, HhTcSmem::bytes, done);
   if (rc) return rc;
   const int ntl = (xm.L + 127) / 128;
   const long long ntiles = heads * ntl;
   const int grid = (int)std::min<long long>(ntiles, 2LL * sm_count());
-  hedgehog_fwd_tc_kernel<<<grid, 128, smem, st>>>(mx, w, xm.H, xm.L, ntl, ntiles, f);
+  hedgehog_fwd_tc_kernel<<<grid, 128, HhTcSmem::bytes, st>>>(mx, mf, w, xm.H, ntl, ntiles);
   count_launches(1);
   return check_launch("hedgehog_fwd_tc_kernel");
 }

@@ -1,6 +1,7 @@
-// Element helpers of the fused RoPE operand passes (the SWA forwards with
-// RoPE inside): 8 consecutive row elements in fp32 from 16-byte loads, and
-// their bf16 value + residual parts.
+// Element helpers for rows handled 8 elements at a time: 8 consecutive row
+// elements in fp32 from 16-byte loads, their bf16 packing and value + residual
+// parts, and the rotate-half RoPE of the fused operand passes (the SWA
+// forwards with RoPE inside).
 #pragma once
 
 #include "common.cuh"
