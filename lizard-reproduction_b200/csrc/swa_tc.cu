@@ -666,34 +666,39 @@ swa_bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
 // ------------------------------------------------------------ backward: dq
 // One CTA of 9 warps per 128 query rows [q0, q0 + 128) of one (batch row,
 // key/value head) and each query head of the group in turn; keys / values
-// [q0 - 64, q0 + 128) as in the forward:
-//   warp 8   : TMA; s = q k^T (hi / lo terms), dp = dy v^T -> TMEM [128 x 192]
-//              each; then dq = ds k_hi with ds from TMEM -> TMEM [128 x 64]
-//   8 warps  : query row i = TMEM lane i, the 96 key columns of its window
-//              split between the two warps of the lane quadrant:
+// [q0 - 64, q0 + 128) as in the forward, taken in two halves of 96 keys:
+//   warp 8   : TMA; per half, s = q k^T (hi / lo terms) and dp = dy v^T
+//              -> TMEM [128 x 96] each; then dq += ds k_hi with ds from TMEM
+//              -> TMEM [128 x 64]
+//   8 warps  : query row i = TMEM lane i, the key columns of its window in
+//              this half split between the two warps of the lane quadrant:
 //              ds = exp(s scale - lse_i) (dp - delta_i) written as bf16 over s
 //              once every score column has been read; then dq_i = scale
 //              (ds k)_i to HBM
 // The arithmetic is that of swa_bwd_dq_kernel (bf16 ds, k_hi; the reference's
 // Triton backward, src/kernels/swa.py:62-95). The query / dy tiles of the next
-// head load into a second stage. 169 KB of shared memory, 512 TMEM columns.
+// head load into a second stage. 256 TMEM columns; with bf16 operands (no
+// residual tiles) 112 KB of shared memory, so two CTAs share an SM.
+constexpr int kHalf = kNK / 2;  // keys per half
+template <bool SPLIT>
 struct DqTcSmem {
-  static constexpr size_t kh = 0, kl = kh + kNK * 128, v = kl + kNK * 128, st = v + kNK * 128;
-  static constexpr size_t sq = 0, sql = kQ * 128, sdy = 2 * kQ * 128, sbytes = 3 * kQ * 128;
+  static constexpr size_t KT = kNK * 128, QT = kQ * 128;
+  static constexpr size_t kh = 0, kl = kh + KT, v = kl + (SPLIT ? KT : 0), st = v + KT;
+  static constexpr size_t sq = 0, sql = QT, sdy = sql + (SPLIT ? QT : 0), sbytes = sdy + QT;
   static constexpr size_t bars = st + 2 * sbytes, slot = bars + 64, bytes = slot + 16;
 };
-// TMEM: s [0, 192) with ds (bf16 pairs, [0, 96)) over it; dp [192, 384); dq [384, 448)
-constexpr uint32_t kTqS = 0, kTqDs = 0, kTqDp = 192, kTqDq = 384, kTqCols = 512;
-enum { QB_KV = 0, QB_Q0, QB_Q1, QB_SD, QB_DQ };
+// TMEM: s of a half [0, 96) with ds (bf16 pairs, [0, 48)) over it; dp [96, 192); dq [192, 256)
+constexpr uint32_t kTqS = 0, kTqDs = 0, kTqDp = kHalf, kTqDq = 2 * kHalf, kTqCols = 256;
+enum { QB_KV = 0, QB_Q0, QB_Q1, QB_SD, QB_HALF, QB_DQ };
 
 template <bool SPLIT>
-__global__ void __launch_bounds__(kCtaThreads, 1)
+__global__ void __launch_bounds__(kCtaThreads, SPLIT ? 1 : 2)
 swa_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tql,
                      const __grid_constant__ CUtensorMap tdy, const __grid_constant__ CUtensorMap tk,
                      const __grid_constant__ CUtensorMap tkl, const __grid_constant__ CUtensorMap tv,
                      const float* __restrict__ lse, const float* __restrict__ delta, int W,
                      float scale, int H, int grp, int L, int nqb, void* __restrict__ dq, int gdt) {
-  using SM = DqTcSmem;
+  using SM = DqTcSmem<SPLIT>;
   extern __shared__ __align__(1024) unsigned char smem[];
   if (smem_u32(smem) & 1023) {
     if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 87u);
@@ -709,7 +714,7 @@ swa_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_consta
 
   if (tid == 0) {
 #pragma unroll
-    for (int j = 0; j < 5; ++j) tc::mbar_init(&bars[j], 1);
+    for (int j = 0; j < 6; ++j) tc::mbar_init(&bars[j], 1);
     tc::fence_mbar_init();
   }
   if (warp == 8) {
@@ -745,51 +750,58 @@ swa_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_consta
     for (int g = 0; g < grp; ++g) {
       const uint32_t ph = (uint32_t)g & 1u;
       unsigned char* st = smem + SM::st + (g & 1) * SM::sbytes;
-      if (issuer) {
-        tc::mbar_wait(&bars[QB_Q0 + (g & 1)], (uint32_t)(g >> 1) & 1u, 61);
-        if (g > 0) tc::mbar_wait(&bars[QB_DQ], ph ^ 1u, 62);  // ds of head g - 1 read
-        tc::tc_fence_after();
-        constexpr uint32_t id_s = tc::idesc_bf16(kQ, kNK, 0, 0);  // K-major x K-major
-        const uint32_t kh = smem_u32(smem + SM::kh), kl = smem_u32(smem + SM::kl),
-                       va = smem_u32(smem + SM::v), qh = smem_u32(st + SM::sq),
-                       ql = smem_u32(st + SM::sql), dya = smem_u32(st + SM::sdy);
-#pragma unroll
-        for (int j = 0; j < kDh / 16; ++j)
-          tc::mma_ss(tmem + kTqS, tc::sdesc(qh + 32 * j, 16, 1024),
-                     tc::sdesc(kh + 32 * j, 16, 1024), id_s, j > 0);
-        if (SPLIT) {
+      const uint32_t kh = smem_u32(smem + SM::kh), kl = smem_u32(smem + SM::kl),
+                     va = smem_u32(smem + SM::v), qh = smem_u32(st + SM::sq),
+                     ql = smem_u32(st + SM::sql), dya = smem_u32(st + SM::sdy);
+      for (int hv = 0; hv < 2; ++hv) {
+        const uint32_t ko = (uint32_t)(hv * kHalf * 128);  // the half's first key row
+        if (issuer) {
+          if (hv == 0) {
+            tc::mbar_wait(&bars[QB_Q0 + (g & 1)], (uint32_t)(g >> 1) & 1u, 61);
+            if (g > 0) tc::mbar_wait(&bars[QB_DQ], ph ^ 1u, 62);  // head g - 1's MMAs done
+          } else {
+            tc::mbar_wait(&bars[QB_HALF], ph, 66);  // the first half's ds has been read
+          }
+          tc::tc_fence_after();
+          constexpr uint32_t id_s = tc::idesc_bf16(kQ, kHalf, 0, 0);  // K-major x K-major
 #pragma unroll
           for (int j = 0; j < kDh / 16; ++j)
             tc::mma_ss(tmem + kTqS, tc::sdesc(qh + 32 * j, 16, 1024),
-                       tc::sdesc(kl + 32 * j, 16, 1024), id_s, 1u);
+                       tc::sdesc(kh + ko + 32 * j, 16, 1024), id_s, j > 0);
+          if (SPLIT) {
+#pragma unroll
+            for (int j = 0; j < kDh / 16; ++j)
+              tc::mma_ss(tmem + kTqS, tc::sdesc(qh + 32 * j, 16, 1024),
+                         tc::sdesc(kl + ko + 32 * j, 16, 1024), id_s, 1u);
+#pragma unroll
+            for (int j = 0; j < kDh / 16; ++j)
+              tc::mma_ss(tmem + kTqS, tc::sdesc(ql + 32 * j, 16, 1024),
+                         tc::sdesc(kh + ko + 32 * j, 16, 1024), id_s, 1u);
+          }
 #pragma unroll
           for (int j = 0; j < kDh / 16; ++j)
-            tc::mma_ss(tmem + kTqS, tc::sdesc(ql + 32 * j, 16, 1024),
-                       tc::sdesc(kh + 32 * j, 16, 1024), id_s, 1u);
+            tc::mma_ss(tmem + kTqDp, tc::sdesc(dya + 32 * j, 16, 1024),
+                       tc::sdesc(va + ko + 32 * j, 16, 1024), id_s, j > 0);
+          tc::mma_commit(&bars[QB_SD]);
         }
+        __syncwarp();
+        tc::named_bar_sync(NB_PREADY, kCtaThreads);  // this half's ds in TMEM
+        if (issuer) {
+          tc::tc_fence_after();
+          constexpr uint32_t id_o = tc::idesc_bf16(kQ, kDh, 0, 1);  // TMEM x MN-major
 #pragma unroll
-        for (int j = 0; j < kDh / 16; ++j)
-          tc::mma_ss(tmem + kTqDp, tc::sdesc(dya + 32 * j, 16, 1024),
-                     tc::sdesc(va + 32 * j, 16, 1024), id_s, j > 0);
-        tc::mma_commit(&bars[QB_SD]);
-      }
-      __syncwarp();
-      tc::named_bar_sync(NB_PREADY, kCtaThreads);  // ds in TMEM; the previous dq read
-      if (issuer) {
-        tc::tc_fence_after();
-        constexpr uint32_t id_o = tc::idesc_bf16(kQ, kDh, 0, 1);  // TMEM x MN-major
-        const uint32_t kh = smem_u32(smem + SM::kh);
-#pragma unroll
-        for (int j = 0; j < kNK / 16; ++j)
-          tc::mma_ts(tmem + kTqDq, tmem + kTqDs + 8 * j, tc::sdesc(kh + 2048 * j, kTileK, 1024),
-                     id_o, j > 0);
-        tc::mma_commit(&bars[QB_DQ]);
-        if (g + 2 < grp) {
-          tc::mbar_wait(&bars[QB_DQ], ph, 63);  // stage g & 1 read by every MMA of head g
-          load_stage(g + 2);
+          for (int j = 0; j < kHalf / 16; ++j)
+            tc::mma_ts(tmem + kTqDq, tmem + kTqDs + 8 * j,
+                       tc::sdesc(kh + ko + 2048 * j, kTileK, 1024), id_o,
+                       (hv > 0 || j > 0) ? 1u : 0u);
+          tc::mma_commit(&bars[hv == 0 ? QB_HALF : QB_DQ]);
+          if (hv == 1 && g + 2 < grp) {
+            tc::mbar_wait(&bars[QB_DQ], ph, 63);  // stage g & 1 read by every MMA of head g
+            load_stage(g + 2);
+          }
         }
+        __syncwarp();
       }
-      __syncwarp();
     }
   } else {
     const int qd = warp & 3, hf = warp >> 2;
@@ -800,44 +812,60 @@ swa_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_consta
       const uint32_t ph = (uint32_t)g & 1u;
       const size_t row = ((size_t)b * H + hk * grp + g) * L + i;
       const float lse_i = i < L ? lse[row] : 0.f, dl_i = i < L ? delta[row] : 0.f;
-      tc::mbar_wait(&bars[QB_SD], ph, 64);
-      tc::tc_fence_after();
-      uint32_t dk8[3][8];
+      for (int hv = 0; hv < 2; ++hv) {
+        tc::mbar_wait(&bars[QB_SD], (uint32_t)hv, 64);  // two phases per head: parity = half
+        tc::tc_fence_after();
+        // 16-column chunks k of this thread's window that fall in this half
+        uint32_t dk8[3][8];
 #pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        float sv[16], dpv[16];
-        tc::tmem_ld16(trow + kTqS + cw + 16 * k, sv);
-        tc::tmem_ld16(trow + kTqDp + cw + 16 * k, dpv);
-        tc::tmem_wait_ld();
+        for (int k = 0; k < 3; ++k) {
+          const int c0 = cw + 16 * k;  // key column in [0, 192)
+          if (c0 >= hv * kHalf && c0 < (hv + 1) * kHalf) {
+            float sv[16], dpv[16];
+            tc::tmem_ld16(trow + kTqS + (c0 - hv * kHalf), sv);
+            tc::tmem_ld16(trow + kTqDp + (c0 - hv * kHalf), dpv);
+            tc::tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float d2[2];
+            for (int j = 0; j < 8; ++j) {
+              float d2[2];
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int t = k0 + cw + 16 * k + 2 * j + e;
-            const bool ok = t <= i && t > i - W && t >= 0 && i < L;
-            const float p = ok ? __expf(sv[2 * j + e] * scale - lse_i) : 0.f;
-            d2[e] = p * (dpv[2 * j + e] - dl_i);
+              for (int e = 0; e < 2; ++e) {
+                const int t = k0 + c0 + 2 * j + e;
+                const bool ok = t <= i && t > i - W && t >= 0 && i < L;
+                const float p = ok ? __expf(sv[2 * j + e] * scale - lse_i) : 0.f;
+                d2[e] = p * (dpv[2 * j + e] - dl_i);
+              }
+              dk8[k][j] = pack_bf16(d2[0], d2[1]);
+            }
           }
-          dk8[k][j] = pack_bf16(d2[0], d2[1]);
         }
-      }
-      tc::tc_fence_before();
-      tc::named_bar_sync(NB_ROWS, kThreads);  // every score column of the CTA read
-      tc::tc_fence_after();
-#pragma unroll
-      for (int k = 0; k < 3; ++k) tc::tmem_st8(trow + kTqDs + cw / 2 + 8 * k, dk8[k]);
-      {  // zero outside the window: packed columns [0, 16 qd) and [16 qd + 48, 96)
+        tc::tc_fence_before();
+        tc::named_bar_sync(NB_ROWS, kThreads);  // every score column of the half read
+        tc::tc_fence_after();
+        // the half's 6 packed 8-column chunks (16 keys each): this quadrant's window
+        // covers 16-key chunks [2 qd, 2 qd + 6) of the 12; half 0 of the quadrant owns
+        // its first 3 and the zeros below, half 1 its last 3 and the zeros above
         uint32_t zero[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) zero[j] = 0u;
-        const int z0 = hf ? 16 * qd + 48 : 0, z1 = hf ? kNK / 2 : 16 * qd;
-#pragma unroll 1
-        for (int c = z0; c < z1; c += 8) tc::tmem_st8(trow + kTqDs + c, zero);
+#pragma unroll
+        for (int pc = 0; pc < kHalf / 16; ++pc) {
+          const int rel = hv * (kHalf / 16) + pc - 2 * qd;  // chunk index in the window
+          const uint32_t dst = trow + kTqDs + 8 * pc;
+          if (rel >= 0 && rel < 6) {
+            if (rel / 3 == hf) {
+              if (rel % 3 == 0) tc::tmem_st8(dst, dk8[0]);
+              else if (rel % 3 == 1) tc::tmem_st8(dst, dk8[1]);
+              else tc::tmem_st8(dst, dk8[2]);
+            }
+          } else if ((rel < 0) == (hf == 0)) {
+            tc::tmem_st8(dst, zero);
+          }
+        }
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        tc::named_bar_arrive(NB_PREADY, kCtaThreads);
       }
-      tc::tmem_wait_st();
-      tc::tc_fence_before();
-      tc::named_bar_arrive(NB_PREADY, kCtaThreads);
       tc::mbar_wait(&bars[QB_DQ], ph, 65);
       tc::tc_fence_after();
       float o[32];
@@ -971,11 +999,12 @@ int swa_bwd_dq_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, c
   if (!bwd_maps(q, ql, dy, k, kl, v, B, H, Hkv, L, kQ, kNK, m)) return LZ_ERR_UNSUPPORTED;
   const bool split = ql != nullptr;
   auto kern = split ? swa_bwd_dq_tc_kernel<true> : swa_bwd_dq_tc_kernel<false>;
+  const size_t smem = split ? DqTcSmem<true>::bytes : DqTcSmem<false>::bytes;
   static bool done[2][64] = {{false}};
-  const int rc = ensure_tc_smem(kern, DqTcSmem::bytes, done[split]);
+  const int rc = ensure_tc_smem(kern, smem, done[split]);
   if (rc) return rc;
   const int nqb = ceil_div(L, kQ);
-  kern<<<(unsigned)((long long)B * Hkv * nqb), kCtaThreads, DqTcSmem::bytes, st>>>(
+  kern<<<(unsigned)((long long)B * Hkv * nqb), kCtaThreads, smem, st>>>(
       m[0], m[1], m[2], m[3], m[4], m[5], lse, delta, W, 1.f / sqrtf((float)kDh), H, H / Hkv, L,
       nqb, dq, gdt);
   count_launches(1);
