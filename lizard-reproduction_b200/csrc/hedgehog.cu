@@ -660,9 +660,31 @@ hedgehog_fwd_rows_kernel(const XT* __restrict__ x, XRows xm, const float* __rest
     const XT* xr = x + xm.off(r);
     for (int d = lane; d < Dh; d += 32) sX[d] = ld_f(xr, d);
   }
-  for (int e = tid; e < Fd * Dh; e += kRowWarps * 32) {
-    const int fi = e / Dh, d = e - fi * Dh;
-    sW[fi * LW + d] = w[e];
+  if ((Dh & 3) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) {
+    // 16-byte loads, up to 8 of a thread's in flight at once
+    const int n4 = Fd * Dh / 4;
+    for (int e0 = tid; e0 < n4; e0 += 8 * kRowWarps * 32) {
+      float4 v4[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int e = e0 + u * kRowWarps * 32;
+        if (e < n4) v4[u] = reinterpret_cast<const float4*>(w)[e];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int e = e0 + u * kRowWarps * 32;
+        if (e < n4) {
+          const int fi = (4 * e) / Dh, d = 4 * e - fi * Dh;
+          float* dst = sW + fi * LW + d;
+          dst[0] = v4[u].x, dst[1] = v4[u].y, dst[2] = v4[u].z, dst[3] = v4[u].w;
+        }
+      }
+    }
+  } else {
+    for (int e = tid; e < Fd * Dh; e += kRowWarps * 32) {
+      const int fi = e / Dh, d = e - fi * Dh;
+      sW[fi * LW + d] = w[e];
+    }
   }
   __syncthreads();
   if (r >= R) return;
