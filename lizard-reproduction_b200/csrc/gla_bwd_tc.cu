@@ -211,6 +211,8 @@ gla_bwd_state_tc_kernel(const __grid_constant__ CUtensorMap tq,
       const float start = n > 0 ? G[rowb + r0 - 1] : 0.f;
       float qs = 0.f;
       if (valid) qs = __expf(G[rowb + r0 + t] - start) / fmaxf(den[rowb + r0 + t], kTiny);
+      if (warp == 2 && lane == 0 && n > 0)  // the next chunk's fp32 y rows into L2 (64 KB)
+        tc::bulk_prefetch_l2(y32 + (rowb + r0 - kC) * 128, (uint32_t)kC * 128 * 4);
       tc::mbar_wait(&bars[B1_FULL0 + st], (it >> 1) & 1, 25);
       unsigned char* stage = base + st * kS1Stage;
       // delta_t = dy_t . y32_t
