@@ -293,10 +293,11 @@ gla_out_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 // grouped keys / values): the query heads of a group differ only in fq, so
 // one CTA per (batch row, key/value head, 128-token chunk) loads fk, v, the
 // state and z once, scans the gate once, and walks the group's query heads:
-//   warp 4   : (one thread) TMA of fk, v, S and each head's fq; per head
+//   warp 8   : (one thread) TMA of fk, v, S and each head's fq; per head
 //              s = fq fk^T and o_inter = fq S_n (unscaled) into TMEM buffers
 //              that alternate between heads, then o_intra = a V
-//   warps 0-3: row i = TMEM lane i: fq_i . z_n from shared memory (after which
+//   warps 0-7: row i = TMEM lane i, two warps per lane quadrant, each with
+//              half of the row's work: fq_i . z_n from shared memory (after which
 //              the next head's fq may load), the weights a from s as in the
 //              kernel above, and y_i = (2^(g_i) o_inter + o_intra) / max(den,
 //              FLT_MIN) with den = sum_t a_it + 2^(g_i) fq_i . z_n
@@ -304,7 +305,8 @@ gla_out_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 // Q~ = fq 2^(g_i) over fq) keeps fq unchanged, so the next head's fq loads
 // while this head's weights and output are formed, and the next head's scores
 // run while this head's output is written. All waits are on mbarriers.
-constexpr int kGroupThreads = 160;  // 4 row warps + the TMA / MMA warp
+constexpr int kGroupRows = 256;                   // 8 row warps, two per TMEM lane quadrant
+constexpr int kGroupThreads = kGroupRows + 32;     // + the TMA / MMA warp (warp 8)
 enum { GB_KV = 0, GB_FQ, GB_S0, GB_S1, GB_O, GB_FQZ, GB_A, GB_OF0, GB_OF1, GB_N };
 // TMEM: s [2 buffers x 128], o_inter [2 x 64], o_intra 64, a (bf16) 64
 constexpr uint32_t kTgS = 0, kTgOi = 256, kTgOa = 384, kTgA = 448, kTgCols = 512;
@@ -320,7 +322,8 @@ struct OutGroupSmem {
   static constexpr size_t g = z + (size_t)F * 4;          // g2 [128]
   static constexpr size_t bf = g + 512;                   // block factors [128]
   static constexpr size_t scan = bf + 512;                // 4 warp totals
-  static constexpr size_t bars = scan + 32;               // GB_N mbarriers
+  static constexpr size_t red = scan + 32;                // row-sum halves [2 heads][2][128]
+  static constexpr size_t bars = red + 2048;              // GB_N mbarriers
   static constexpr size_t slot = bars + 8 * GB_N;         // TMEM base address
   static constexpr size_t bytes = slot + 16;
 };
@@ -357,10 +360,11 @@ gla_out_group_tc_kernel(const __grid_constant__ CUtensorMap tq,
   if (tid == 0) {
 #pragma unroll
     for (int i = 0; i < GB_N; ++i)
-      tc::mbar_init(&bars[i], (i == GB_FQZ || i == GB_A || i == GB_OF0 || i == GB_OF1) ? 128 : 1);
+      tc::mbar_init(&bars[i],
+                    (i == GB_FQZ || i == GB_A || i == GB_OF0 || i == GB_OF1) ? kGroupRows : 1);
     tc::fence_mbar_init();
   }
-  if (warp == 4) {
+  if (warp == 8) {
     tc::tmem_alloc(tslot, kTgCols);
     tc::tmem_relinquish();
   }
@@ -369,7 +373,7 @@ gla_out_group_tc_kernel(const __grid_constant__ CUtensorMap tq,
   tc::tc_fence_after();
   const uint32_t tmem = *tslot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       const uint32_t kv_bytes = (uint32_t)(SM::FB * 16384 + 16384) +
                                 (with_state ? (uint32_t)(F * 128) : 0u);
@@ -430,9 +434,14 @@ gla_out_group_tc_kernel(const __grid_constant__ CUtensorMap tq,
     }
     __syncwarp();
   } else {
+    // row r = TMEM lane r; the two warps of a lane quadrant split the work of the
+    // row: fq . z over features [F/2 hf, F/2 (hf + 1)), the weight blocks 2 hf and
+    // 2 hf + 1, and output columns [32 hf, 32 hf + 32)
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = 32 * qd + lane;
+    float* red = reinterpret_cast<float*>(base + SM::red);
     // in-chunk running log2 gate (the chunk's start is the frame: G_start = 0), shared
-    // by the group's heads
-    const int r = tid;
+    // by the group's heads; both halves of a quadrant form it, half 0 publishes it
     const bool valid = r < nvalid;
     const float* LG = lg + (size_t)b * L;
     float x = valid ? LG[r0 + r] * kLog2e : 0.f;
@@ -441,19 +450,21 @@ gla_out_group_tc_kernel(const __grid_constant__ CUtensorMap tq,
       const float u = __shfl_up_sync(0xffffffffu, x, o);
       if (lane >= o) x += u;
     }
-    if (lane == 31) sScan[warp] = x;
-    for (int f = tid; f < F; f += 128) sZ[f] = with_state ? z_in[schunk * F + f] : 0.f;
-    tc::named_bar_sync(1, 128);
+    if (hf == 0 && lane == 31) sScan[qd] = x;
+    for (int f = tid; f < F; f += kGroupRows) sZ[f] = with_state ? z_in[schunk * F + f] : 0.f;
+    tc::named_bar_sync(1, kGroupRows);
     float pre = 0.f;
 #pragma unroll
     for (int qq = 0; qq < 4; ++qq)
-      if (qq < warp) pre += sScan[qq];
+      if (qq < qd) pre += sScan[qq];
     const float g2 = pre + x;
-    sG[r] = g2;
-    sB[r] = tc::ex2(__shfl_sync(0xffffffffu, g2, 31) - g2);  // relative to the block's last row
-    tc::named_bar_sync(1, 128);
+    if (hf == 0) {
+      sG[r] = g2;
+      sB[r] = tc::ex2(__shfl_sync(0xffffffffu, g2, 31) - g2);  // relative to the block's last row
+    }
+    tc::named_bar_sync(1, kGroupRows);
     const float qs = valid ? tc::ex2(g2) : 0.f;  // the row scale of fq: Q~_i = fq_i 2^(g2_i)
-    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t trow = tmem + ((uint32_t)(qd * 32) << 16);
 
     for (int g = 0; g < grp; ++g) {
       const int sb = g & 1;
@@ -463,7 +474,7 @@ gla_out_group_tc_kernel(const __grid_constant__ CUtensorMap tq,
       float fqz = 0.f;
       if (with_state) {
 #pragma unroll 1
-        for (int jb = 0; jb < F / 64; ++jb) {
+        for (int jb = hf * (F / 128); jb < (hf + 1) * (F / 128); ++jb) {
           const unsigned char* rowp = base + SM::q + jb * 16384 + r * 128;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -482,9 +493,9 @@ gla_out_group_tc_kernel(const __grid_constant__ CUtensorMap tq,
       tc::tc_fence_after();
       float den = 0.f;
 #pragma unroll 1
-      for (int cb = 0; cb < 4; ++cb) {
+      for (int cb = 2 * hf; cb < 2 * hf + 2; ++cb) {
         uint32_t pk[16];
-        if (cb < warp) {
+        if (cb < qd) {
           float sv[32];
           tc::tmem_ld32(trow + kTgS + 128 * sb + 32 * cb, sv);
           const float ar = valid ? tc::ex2(g2 - sG[32 * cb + 31]) : 0.f;
@@ -496,7 +507,7 @@ gla_out_group_tc_kernel(const __grid_constant__ CUtensorMap tq,
             pk[2 * j4] = pack_bf16(sv[4 * j4] * f.x * ar, sv[4 * j4 + 1] * f.y * ar);
             pk[2 * j4 + 1] = pack_bf16(sv[4 * j4 + 2] * f.z * ar, sv[4 * j4 + 3] * f.w * ar);
           }
-        } else if (cb == warp) {
+        } else if (cb == qd) {
           float sv[32];
           tc::tmem_ld32(trow + kTgS + 128 * sb + 32 * cb, sv);
           const float4* gt = reinterpret_cast<const float4*>(sG + 32 * cb);
@@ -524,18 +535,20 @@ gla_out_group_tc_kernel(const __grid_constant__ CUtensorMap tq,
         for (int jj = 0; jj < 16; ++jj) den += bf16_lo(pk[jj]) + bf16_hi(pk[jj]);
         tc::tmem_st16(trow + kTgA + 16 * cb, pk);
       }
-      den += qs * fqz;
+      den += qs * fqz;  // this half's part of the row sum
+      red[(sb * 2 + hf) * 128 + r] = den;
       tc::tmem_wait_st();
       tc::tc_fence_before();
       tc::mbar_arrive(&bars[GB_A]);
+      tc::named_bar_sync(2, kGroupRows);  // both halves' row sums written
 
       tc::mbar_wait(&bars[GB_O], ph, 58);
       tc::tc_fence_after();
-      const float inv = 1.f / fmaxf(den, kTiny);
+      const float inv = 1.f / fmaxf(red[(sb * 2) * 128 + r] + red[(sb * 2 + 1) * 128 + r], kTiny);
       const size_t row = ((size_t)b * H + j * grp + g) * L + r0 + r;
       bf16* yrow = y + row * D;
-#pragma unroll 1
-      for (int db = 0; db < D / 32; ++db) {
+      {
+        const int db = hf;
         float oa[32], oi[32];
         tc::tmem_ld32(trow + kTgOa + 32 * db, oa);
         if (with_state) tc::tmem_ld32(trow + kTgOi + 64 * sb + 32 * db, oi);
@@ -565,7 +578,7 @@ gla_out_group_tc_kernel(const __grid_constant__ CUtensorMap tq,
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, kTgCols);
   }
