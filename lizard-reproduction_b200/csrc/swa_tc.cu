@@ -277,7 +277,8 @@ swa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       uint32_t phi[8], plo[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float p0 = exp2f(s[k][2 * j] - mx), p1 = exp2f(s[k][2 * j + 1] - mx);
+        // x - mx <= 0 (or -inf outside the window): the hardware 2^x, error ~2^-22
+        const float p0 = tc::ex2(s[k][2 * j] - mx), p1 = tc::ex2(s[k][2 * j + 1] - mx);
         l += p0 + p1;
         const uint32_t hpk = pack_bf16(p0, p1);
         phi[j] = hpk;
