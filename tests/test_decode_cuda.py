@@ -64,6 +64,7 @@ def test_gla_decode_matches_dense_oracle(B, H, Hkv, F, D, L0, T, per_head):
     (4, 1, 5, 3, 12, torch.float32, 32),      # odd window: ring rows staged in shared memory
     (2, 2, 24, 30, 6, torch.bfloat16, 128),
     (8, 2, 512, 520, 8, torch.bfloat16, 64),  # rings too large to stage: read from HBM
+    (4, 1, 1024, 1030, 4, torch.bfloat16, 64),  # the largest window the decode step takes
 ])
 def test_swa_decode_matches_dense_oracle(H, Hkv, W, L0, T, dtype, D):
     from lizard_cuda.decode import swa_decode, swa_ring
