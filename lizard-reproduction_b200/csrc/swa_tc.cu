@@ -28,6 +28,7 @@
 // rescaling of the 64-key-block kernels; the products carry the same precision
 // (about 16 mantissa bits in the logits and in P). 109 KB of shared memory and
 // 256 TMEM columns per CTA: two CTAs per SM.
+#include <algorithm>
 #include <atomic>
 
 #include "common.cuh"
@@ -664,6 +665,228 @@ swa_bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
   }
 }
 
+// The same dk / dv for bf16 operands (no residual tiles), persistent: one CTA
+// per SM walks its tiles (b, key/value head, key tile) and, in each, the
+// group's query heads as a flat sequence of items. Two key / value buffers
+// and two query / dy stages let the next tile's and the next items' tiles
+// load while this one computes, and the next tile's scores run while the row
+// warps write this tile's dk / dv (the accumulators are overwritten only
+// after that write-out). 167 KB of shared memory, 512 TMEM columns.
+struct DkvPersistSmem {
+  static constexpr size_t KVB = 2 * kBK * 128, QB = 2 * kBQ * 128;  // k + v; q + dy
+  static constexpr size_t kv = 0, qs = 2 * KVB, rows = qs + 2 * QB;
+  static constexpr size_t bars = rows + 2 * 2 * kBQ * 4, slot = bars + 64, bytes = slot + 16;
+};
+enum { PB_KV0 = 0, PB_KV1, PB_Q0, PB_Q1, PB_SD, PB_PD, PB_EPI, PB_N };
+
+__global__ void __launch_bounds__(kCtaThreads, 1)
+swa_bwd_dkv_tc_persist_kernel(const __grid_constant__ CUtensorMap tq,
+                              const __grid_constant__ CUtensorMap tdy,
+                              const __grid_constant__ CUtensorMap tk,
+                              const __grid_constant__ CUtensorMap tv,
+                              const float* __restrict__ lse, const float* __restrict__ delta,
+                              int W, float scale, int H, int grp, int L, int nkt, int ntiles,
+                              void* __restrict__ dk, void* __restrict__ dv, int gdt) {
+  using SM = DkvPersistSmem;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 86u);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::bars);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + SM::slot);
+  float* rows = reinterpret_cast<float*>(smem + SM::rows);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Hkv = H / grp;
+  constexpr uint32_t kTileK = kBK * 128, kTileQ = kBQ * 128;
+  // this CTA's tiles: blockIdx.x + kl gridDim.x, kl < nloc; items (kl, g), w = kl grp + g
+  const int nloc = (int)((ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x);
+  const int nitems = nloc * grp;
+  auto tile = [&](int kl, int& b, int& hk, int& k0) {
+    const int tt = (int)blockIdx.x + kl * (int)gridDim.x;
+    const int kt = tt % nkt, bk = tt / nkt;
+    b = bk / Hkv, hk = bk - b * Hkv, k0 = kt * kBK;
+  };
+
+  if (tid == 0) {
+#pragma unroll
+    for (int j = 0; j < PB_N; ++j) tc::mbar_init(&bars[j], j == PB_EPI ? kThreads : 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == 8) {
+    tc::tmem_alloc(tslot, kTbCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 8) {
+    const bool issuer = lane == 0;
+    auto load_kv = [&](int kl) {
+      int b, hk, k0;
+      tile(kl, b, hk, k0);
+      unsigned char* buf = smem + SM::kv + (kl & 1) * SM::KVB;
+      uint64_t* bar = &bars[PB_KV0 + (kl & 1)];
+      tc::mbar_expect_tx(bar, 2 * kTileK);
+      tc::tma_load_4d(buf, &tk, 0, k0, hk, b, bar);
+      tc::tma_load_4d(buf + kTileK, &tv, 0, k0, hk, b, bar);
+    };
+    auto load_q = [&](int w) {
+      int b, hk, k0;
+      tile(w / grp, b, hk, k0);
+      const int h = hk * grp + w % grp;
+      unsigned char* st = smem + SM::qs + (w & 1) * SM::QB;
+      uint64_t* bar = &bars[PB_Q0 + (w & 1)];
+      tc::mbar_expect_tx(bar, 2 * kTileQ);
+      tc::tma_load_4d(st, &tq, 0, k0, h, b, bar);
+      tc::tma_load_4d(st + kTileQ, &tdy, 0, k0, h, b, bar);
+    };
+    if (issuer) {
+      if (nloc > 0) load_kv(0);
+      if (nloc > 1) load_kv(1);
+      if (nitems > 0) load_q(0);
+      if (nitems > 1) load_q(1);
+    }
+    __syncwarp();
+    for (int w = 0; w < nitems; ++w) {
+      const int kl = w / grp, g = w - kl * grp;
+      const unsigned char* kvb = smem + SM::kv + (kl & 1) * SM::KVB;
+      const unsigned char* st = smem + SM::qs + (w & 1) * SM::QB;
+      if (issuer) {
+        if (g == 0) tc::mbar_wait(&bars[PB_KV0 + (kl & 1)], (uint32_t)(kl >> 1) & 1u, 77);
+        tc::mbar_wait(&bars[PB_Q0 + (w & 1)], (uint32_t)(w >> 1) & 1u, 78);
+        if (w > 0) tc::mbar_wait(&bars[PB_PD], (uint32_t)(w - 1) & 1u, 79);  // p / ds read
+        tc::tc_fence_after();
+        constexpr uint32_t id_s = tc::idesc_bf16(kBK, kBQ, 0, 0);  // K-major x K-major
+        const uint32_t kh = smem_u32(kvb), va = kh + kTileK, qh = smem_u32(st),
+                       dya = qh + kTileQ;
+#pragma unroll
+        for (int j = 0; j < kDh / 16; ++j)
+          tc::mma_ss(tmem + kTbS, tc::sdesc(kh + 32 * j, 16, 1024),
+                     tc::sdesc(qh + 32 * j, 16, 1024), id_s, j > 0);
+#pragma unroll
+        for (int j = 0; j < kDh / 16; ++j)
+          tc::mma_ss(tmem + kTbDp, tc::sdesc(va + 32 * j, 16, 1024),
+                     tc::sdesc(dya + 32 * j, 16, 1024), id_s, j > 0);
+        tc::mma_commit(&bars[PB_SD]);
+      }
+      __syncwarp();
+      tc::named_bar_sync(NB_PREADY, kCtaThreads);  // p^T and ds^T in TMEM
+      if (issuer) {
+        // a tile's first head overwrites the accumulators: the last tile's dk / dv
+        // must have been written out
+        if (g == 0 && kl > 0) tc::mbar_wait(&bars[PB_EPI], (uint32_t)(kl - 1) & 1u, 80);
+        tc::tc_fence_after();
+        constexpr uint32_t id_o = tc::idesc_bf16(kBK, kDh, 0, 1);  // TMEM x MN-major
+        const uint32_t qh = smem_u32(st), dya = qh + kTileQ;
+#pragma unroll
+        for (int j = 0; j < kBQ / 16; ++j)
+          tc::mma_ts(tmem + kTbDv, tmem + kTbP + 8 * j, tc::sdesc(dya + 2048 * j, kTileQ, 1024),
+                     id_o, (g > 0 || j > 0) ? 1u : 0u);
+#pragma unroll
+        for (int j = 0; j < kBQ / 16; ++j)
+          tc::mma_ts(tmem + kTbDk, tmem + kTbDs + 8 * j, tc::sdesc(qh + 2048 * j, kTileQ, 1024),
+                     id_o, (g > 0 || j > 0) ? 1u : 0u);
+        tc::mma_commit(&bars[PB_PD]);
+        const bool refill_q = w + 2 < nitems, refill_kv = g == grp - 1 && kl + 2 < nloc;
+        if (refill_q || refill_kv) {
+          tc::mbar_wait(&bars[PB_PD], (uint32_t)w & 1u, 81);  // item w's tiles read
+          if (refill_q) load_q(w + 2);
+          if (refill_kv) load_kv(kl + 2);
+        }
+      }
+      __syncwarp();
+    }
+  } else {
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = 32 * qd + lane;
+    const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
+    const int cw = 32 * qd + 48 * hf;  // first query column of this thread's half window
+    for (int w = 0; w < nitems; ++w) {
+      const int kl = w / grp, g = w - kl * grp;
+      int b, hk, k0;
+      tile(kl, b, hk, k0);
+      const int t = k0 + r;  // this thread's key row
+      const size_t bh = (size_t)b * H + hk * grp + g;
+      float* rl = rows + (w & 1) * 2 * kBQ;  // lse, then delta, of query rows k0 + c
+      for (int c = tid; c < kBQ; c += kThreads) {
+        const int i = k0 + c;
+        rl[c] = i < L ? lse[bh * L + i] : 0.f;
+        rl[kBQ + c] = i < L ? delta[bh * L + i] : 0.f;
+      }
+      tc::named_bar_sync(NB_ROWS, kThreads);
+      tc::mbar_wait(&bars[PB_SD], (uint32_t)w & 1u, 82);
+      tc::tc_fence_after();
+      uint32_t pk[3][8], dk8[3][8];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        float sv[16], dpv[16];
+        tc::tmem_ld16(trow + kTbS + cw + 16 * k, sv);
+        tc::tmem_ld16(trow + kTbDp + cw + 16 * k, dpv);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float p2[2], d2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int c = cw + 16 * k + 2 * j + e, i = k0 + c;
+            const bool ok = i >= t && i < t + W && i < L && t < L;
+            const float p = ok ? __expf(sv[2 * j + e] * scale - rl[c]) : 0.f;
+            p2[e] = p;
+            d2[e] = p * (dpv[2 * j + e] - rl[kBQ + c]);
+          }
+          pk[k][j] = pack_bf16(p2[0], p2[1]);
+          dk8[k][j] = pack_bf16(d2[0], d2[1]);
+        }
+      }
+      tc::tc_fence_before();
+      tc::named_bar_sync(NB_ROWS, kThreads);  // every score column of the CTA read
+      tc::tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        tc::tmem_st8(trow + kTbP + cw / 2 + 8 * k, pk[k]);
+        tc::tmem_st8(trow + kTbDs + cw / 2 + 8 * k, dk8[k]);
+      }
+      {  // zero outside the window: packed columns [0, 16 qd) and [16 qd + 48, 96)
+        uint32_t zero[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) zero[j] = 0u;
+        const int z0 = hf ? 16 * qd + 48 : 0, z1 = hf ? kBQ / 2 : 16 * qd;
+#pragma unroll 1
+        for (int c = z0; c < z1; c += 8) {
+          tc::tmem_st8(trow + kTbP + c, zero);
+          tc::tmem_st8(trow + kTbDs + c, zero);
+        }
+      }
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      tc::named_bar_arrive(NB_PREADY, kCtaThreads);
+      if (g == grp - 1) {  // the tile's dv (half 0) and dk (half 1), summed over the group
+        tc::mbar_wait(&bars[PB_PD], (uint32_t)w & 1u, 83);
+        tc::tc_fence_after();
+        const size_t orow = (((size_t)b * Hkv + hk) * L + t) * kDh;
+#pragma unroll 1
+        for (int db = 0; db < 2; ++db) {
+          float o[32];
+          tc::tmem_ld32(trow + (hf ? kTbDk : kTbDv) + 32 * db, o);
+          tc::tmem_wait_ld();
+          if (t < L) store_grad32(hf ? dk : dv, orow + 32 * db, o, hf ? scale : 1.f, gdt);
+        }
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bars[PB_EPI]);
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTbCols);
+  }
+}
+
 // ------------------------------------------------------------ backward: dq
 // One CTA of 9 warps per 128 query rows [q0, q0 + 128) of one (batch row,
 // key/value head) and each query head of the group in turn; keys / values
@@ -979,11 +1202,27 @@ int swa_bwd_dkv_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, 
   CUtensorMap m[6];
   if (!bwd_maps(q, ql, dy, k, kl, v, B, H, Hkv, L, kBQ, kBK, m)) return LZ_ERR_UNSUPPORTED;
   const bool split = ql != nullptr;
+  const int nkt = ceil_div(L, kBK);
+  if (!split) {  // bf16 operands: the persistent kernel, one CTA per SM
+    static bool done_p[64] = {false};
+    const int rc = ensure_tc_smem(swa_bwd_dkv_tc_persist_kernel, DkvPersistSmem::bytes, done_p);
+    if (rc) return rc;
+    const long long ntiles = (long long)B * Hkv * nkt;
+    if (ntiles >= (1ll << 31)) return LZ_ERR_UNSUPPORTED;
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = (int)std::min<long long>(ntiles, nsm > 0 ? nsm : 148);
+    swa_bwd_dkv_tc_persist_kernel<<<grid, kCtaThreads, DkvPersistSmem::bytes, st>>>(
+        m[0], m[2], m[3], m[5], lse, delta, W, 1.f / sqrtf((float)kDh), H, H / Hkv, L, nkt,
+        (int)ntiles, dk, dv, gdt);
+    count_launches(1);
+    return check_launch("swa_bwd_dkv_tc_persist_kernel");
+  }
   auto kern = split ? swa_bwd_dkv_tc_kernel<true> : swa_bwd_dkv_tc_kernel<false>;
   static bool done[2][64] = {{false}};
   const int rc = ensure_tc_smem(kern, DkvTcSmem::bytes, done[split]);
   if (rc) return rc;
-  const int nkt = ceil_div(L, kBK);
   kern<<<(unsigned)((long long)B * Hkv * nkt), kCtaThreads, DkvTcSmem::bytes, st>>>(
       m[0], m[1], m[2], m[3], m[4], m[5], lse, delta, W, 1.f / sqrtf((float)kDh), H, H / Hkv, L,
       nkt, dk, dv, gdt);
