@@ -1106,6 +1106,203 @@ swa_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_consta
   }
 }
 
+// dq for bf16 operands as a persistent kernel: one CTA per SM walks its tiles
+// (b, key/value head, 128 query rows) and the group's query heads in each as
+// a flat sequence of items, with two key / value buffers and two query / dy
+// stages loading ahead, all 192 key columns in one pass (s [0, 192) with ds
+// over it, dp [192, 384)) and dq in two TMEM buffers that alternate between
+// items, so an item's dq is written out while the next item computes.
+// 161 KB of shared memory, 512 TMEM columns.
+struct DqPersistSmem {
+  static constexpr size_t KVB = 2 * kNK * 128, QB = 2 * kQ * 128;  // k + v; q + dy
+  static constexpr size_t kv = 0, qs = 2 * KVB, bars = qs + 2 * QB, slot = bars + 128,
+                          bytes = slot + 16;
+};
+enum { QP_KV0 = 0, QP_KV1, QP_Q0, QP_Q1, QP_SD, QP_DQ, QP_EPI0, QP_EPI1, QP_N };
+constexpr uint32_t kTpS = 0, kTpDs = 0, kTpDp = kNK, kTpDq = 2 * kNK, kTpCols = 512;
+
+__global__ void __launch_bounds__(kCtaThreads, 1)
+swa_bwd_dq_tc_persist_kernel(const __grid_constant__ CUtensorMap tq,
+                             const __grid_constant__ CUtensorMap tdy,
+                             const __grid_constant__ CUtensorMap tk,
+                             const __grid_constant__ CUtensorMap tv,
+                             const float* __restrict__ lse, const float* __restrict__ delta,
+                             int W, float scale, int H, int grp, int L, int nqb, int ntiles,
+                             void* __restrict__ dq, int gdt) {
+  using SM = DqPersistSmem;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 85u);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::bars);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + SM::slot);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Hkv = H / grp;
+  constexpr uint32_t kTileK = kNK * 128, kTileQ = kQ * 128;
+  const int nloc = (int)((ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x);
+  const int nitems = nloc * grp;
+  auto tile = [&](int kl, int& b, int& hk, int& q0) {
+    const int tt = (int)blockIdx.x + kl * (int)gridDim.x;
+    const int qb = tt % nqb, bk = tt / nqb;
+    b = bk / Hkv, hk = bk - b * Hkv, q0 = qb * kQ;
+  };
+
+  if (tid == 0) {
+#pragma unroll
+    for (int j = 0; j < QP_N; ++j)
+      tc::mbar_init(&bars[j], (j == QP_EPI0 || j == QP_EPI1) ? kThreads : 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == 8) {
+    tc::tmem_alloc(tslot, kTpCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 8) {
+    const bool issuer = lane == 0;
+    auto load_kv = [&](int kl) {
+      int b, hk, q0;
+      tile(kl, b, hk, q0);
+      unsigned char* buf = smem + SM::kv + (kl & 1) * SM::KVB;
+      uint64_t* bar = &bars[QP_KV0 + (kl & 1)];
+      tc::mbar_expect_tx(bar, 2 * kTileK);
+      tc::tma_load_4d(buf, &tk, 0, q0 - (kNK - kQ), hk, b, bar);
+      tc::tma_load_4d(buf + kTileK, &tv, 0, q0 - (kNK - kQ), hk, b, bar);
+    };
+    auto load_q = [&](int w) {
+      int b, hk, q0;
+      tile(w / grp, b, hk, q0);
+      const int h = hk * grp + w % grp;
+      unsigned char* st = smem + SM::qs + (w & 1) * SM::QB;
+      uint64_t* bar = &bars[QP_Q0 + (w & 1)];
+      tc::mbar_expect_tx(bar, 2 * kTileQ);
+      tc::tma_load_4d(st, &tq, 0, q0, h, b, bar);
+      tc::tma_load_4d(st + kTileQ, &tdy, 0, q0, h, b, bar);
+    };
+    if (issuer) {
+      if (nloc > 0) load_kv(0);
+      if (nloc > 1) load_kv(1);
+      if (nitems > 0) load_q(0);
+      if (nitems > 1) load_q(1);
+    }
+    __syncwarp();
+    for (int w = 0; w < nitems; ++w) {
+      const int kl = w / grp, g = w - kl * grp;
+      const unsigned char* kvb = smem + SM::kv + (kl & 1) * SM::KVB;
+      const unsigned char* st = smem + SM::qs + (w & 1) * SM::QB;
+      if (issuer) {
+        if (g == 0) tc::mbar_wait(&bars[QP_KV0 + (kl & 1)], (uint32_t)(kl >> 1) & 1u, 90);
+        tc::mbar_wait(&bars[QP_Q0 + (w & 1)], (uint32_t)(w >> 1) & 1u, 91);
+        if (w > 0) tc::mbar_wait(&bars[QP_DQ], (uint32_t)(w - 1) & 1u, 92);  // ds read
+        tc::tc_fence_after();
+        constexpr uint32_t id_s = tc::idesc_bf16(kQ, kNK, 0, 0);  // K-major x K-major
+        const uint32_t kh = smem_u32(kvb), va = kh + kTileK, qh = smem_u32(st),
+                       dya = qh + kTileQ;
+#pragma unroll
+        for (int j = 0; j < kDh / 16; ++j)
+          tc::mma_ss(tmem + kTpS, tc::sdesc(qh + 32 * j, 16, 1024),
+                     tc::sdesc(kh + 32 * j, 16, 1024), id_s, j > 0);
+#pragma unroll
+        for (int j = 0; j < kDh / 16; ++j)
+          tc::mma_ss(tmem + kTpDp, tc::sdesc(dya + 32 * j, 16, 1024),
+                     tc::sdesc(va + 32 * j, 16, 1024), id_s, j > 0);
+        tc::mma_commit(&bars[QP_SD]);
+      }
+      __syncwarp();
+      tc::named_bar_sync(NB_PREADY, kCtaThreads);  // ds in TMEM
+      if (issuer) {
+        // dq buffer w & 1 was last read by item w - 2's write-out
+        if (w >= 2) tc::mbar_wait(&bars[QP_EPI0 + (w & 1)], (((uint32_t)w >> 1) & 1u) ^ 1u, 93);
+        tc::tc_fence_after();
+        constexpr uint32_t id_o = tc::idesc_bf16(kQ, kDh, 0, 1);  // TMEM x MN-major
+        const uint32_t kh = smem_u32(kvb);
+#pragma unroll
+        for (int j = 0; j < kNK / 16; ++j)
+          tc::mma_ts(tmem + kTpDq + 64 * (w & 1), tmem + kTpDs + 8 * j,
+                     tc::sdesc(kh + 2048 * j, kTileK, 1024), id_o, j > 0);
+        tc::mma_commit(&bars[QP_DQ]);
+        const bool refill_q = w + 2 < nitems, refill_kv = g == grp - 1 && kl + 2 < nloc;
+        if (refill_q || refill_kv) {
+          tc::mbar_wait(&bars[QP_DQ], (uint32_t)w & 1u, 94);  // item w's tiles read
+          if (refill_q) load_q(w + 2);
+          if (refill_kv) load_kv(kl + 2);
+        }
+      }
+      __syncwarp();
+    }
+  } else {
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = 32 * qd + lane;
+    const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
+    const int cw = 32 * qd + 48 * hf;  // first key column of this thread's half window
+    for (int w = 0; w < nitems; ++w) {
+      const int kl = w / grp, g = w - kl * grp;
+      int b, hk, q0;
+      tile(kl, b, hk, q0);
+      const int i = q0 + r, k0 = q0 - (kNK - kQ);  // this thread's query row
+      const size_t row = ((size_t)b * H + hk * grp + g) * L + i;
+      const float lse_i = i < L ? lse[row] : 0.f, dl_i = i < L ? delta[row] : 0.f;
+      tc::mbar_wait(&bars[QP_SD], (uint32_t)w & 1u, 95);
+      tc::tc_fence_after();
+      uint32_t dk8[3][8];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        float sv[16], dpv[16];
+        tc::tmem_ld16(trow + kTpS + cw + 16 * k, sv);
+        tc::tmem_ld16(trow + kTpDp + cw + 16 * k, dpv);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float d2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int t = k0 + cw + 16 * k + 2 * j + e;
+            const bool ok = t <= i && t > i - W && t >= 0 && i < L;
+            const float p = ok ? __expf(sv[2 * j + e] * scale - lse_i) : 0.f;
+            d2[e] = p * (dpv[2 * j + e] - dl_i);
+          }
+          dk8[k][j] = pack_bf16(d2[0], d2[1]);
+        }
+      }
+      tc::tc_fence_before();
+      tc::named_bar_sync(NB_ROWS, kThreads);  // every score column of the CTA read
+      tc::tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < 3; ++k) tc::tmem_st8(trow + kTpDs + cw / 2 + 8 * k, dk8[k]);
+      {  // zero outside the window: packed columns [0, 16 qd) and [16 qd + 48, 96)
+        uint32_t zero[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) zero[j] = 0u;
+        const int z0 = hf ? 16 * qd + 48 : 0, z1 = hf ? kNK / 2 : 16 * qd;
+#pragma unroll 1
+        for (int c = z0; c < z1; c += 8) tc::tmem_st8(trow + kTpDs + c, zero);
+      }
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      tc::named_bar_arrive(NB_PREADY, kCtaThreads);
+      tc::mbar_wait(&bars[QP_DQ], (uint32_t)w & 1u, 96);
+      tc::tc_fence_after();
+      float o[32];
+      tc::tmem_ld32(trow + kTpDq + 64 * (w & 1) + 32 * hf, o);  // this warp's 32 columns
+      tc::tmem_wait_ld();
+      if (i < L) store_grad32(dq, row * kDh + 32 * hf, o, scale, gdt);
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars[QP_EPI0 + (w & 1)]);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTpCols);
+  }
+}
+
 // Tensor maps of the backward operands ([B, H or Hkv, L, 64] contiguous bf16);
 // false when one cannot be built.
 bool bwd_maps(const bf16* q, const bf16* ql, const bf16* dy, const bf16* k, const bf16* kl,
@@ -1238,6 +1435,23 @@ int swa_bwd_dq_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, c
   CUtensorMap m[6];
   if (!bwd_maps(q, ql, dy, k, kl, v, B, H, Hkv, L, kQ, kNK, m)) return LZ_ERR_UNSUPPORTED;
   const bool split = ql != nullptr;
+  if (!split) {  // bf16 operands: the persistent kernel, one CTA per SM
+    static bool done_p[64] = {false};
+    const int rc = ensure_tc_smem(swa_bwd_dq_tc_persist_kernel, DqPersistSmem::bytes, done_p);
+    if (rc) return rc;
+    const int nqb = ceil_div(L, kQ);
+    const long long ntiles = (long long)B * Hkv * nqb;
+    if (ntiles >= (1ll << 31)) return LZ_ERR_UNSUPPORTED;
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = (int)std::min<long long>(ntiles, nsm > 0 ? nsm : 148);
+    swa_bwd_dq_tc_persist_kernel<<<grid, kCtaThreads, DqPersistSmem::bytes, st>>>(
+        m[0], m[2], m[3], m[5], lse, delta, W, 1.f / sqrtf((float)kDh), H, H / Hkv, L, nqb,
+        (int)ntiles, dq, gdt);
+    count_launches(1);
+    return check_launch("swa_bwd_dq_tc_persist_kernel");
+  }
   auto kern = split ? swa_bwd_dq_tc_kernel<true> : swa_bwd_dq_tc_kernel<false>;
   const size_t smem = split ? DqTcSmem<true>::bytes : DqTcSmem<false>::bytes;
   static bool done[2][64] = {{false}};
