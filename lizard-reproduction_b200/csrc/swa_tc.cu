@@ -804,19 +804,33 @@ swa_bwd_dkv_tc_persist_kernel(const __grid_constant__ CUtensorMap tq,
     const int r = 32 * qd + lane;
     const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
     const int cw = 32 * qd + 48 * hf;  // first query column of this thread's half window
+    const float scale_log2 = scale * kLog2e;
+    static_assert(kBQ <= kThreads, "one query row's lse / delta per row thread");
+    // thread tid < kBQ loads lse and delta of query row k0 + tid of item w2,
+    // one item ahead
+    auto row_stats = [&](int w2, float& a, float& d) {
+      const int kl2 = w2 / grp, g2 = w2 - kl2 * grp;
+      int b2, hk2, k02;
+      tile(kl2, b2, hk2, k02);
+      const size_t bh2 = (size_t)b2 * H + hk2 * grp + g2;
+      const int i = k02 + tid;
+      a = tid < kBQ && i < L ? lse[bh2 * L + i] : 0.f;
+      d = tid < kBQ && i < L ? delta[bh2 * L + i] : 0.f;
+    };
+    float nl = 0.f, nd = 0.f;
+    if (nitems > 0) row_stats(0, nl, nd);
     for (int w = 0; w < nitems; ++w) {
       const int kl = w / grp, g = w - kl * grp;
       int b, hk, k0;
       tile(kl, b, hk, k0);
       const int t = k0 + r;  // this thread's key row
-      const size_t bh = (size_t)b * H + hk * grp + g;
       float* rl = rows + (w & 1) * 2 * kBQ;  // lse, then delta, of query rows k0 + c
-      for (int c = tid; c < kBQ; c += kThreads) {
-        const int i = k0 + c;
-        rl[c] = i < L ? lse[bh * L + i] : 0.f;
-        rl[kBQ + c] = i < L ? delta[bh * L + i] : 0.f;
+      if (tid < kBQ) {
+        rl[tid] = nl * kLog2e;  // lse in base 2
+        rl[kBQ + tid] = nd;
       }
       tc::named_bar_sync(NB_ROWS, kThreads);
+      if (w + 1 < nitems) row_stats(w + 1, nl, nd);
       tc::mbar_wait(&bars[PB_SD], (uint32_t)w & 1u, 82);
       tc::tc_fence_after();
       uint32_t pk[3][8], dk8[3][8];
@@ -833,7 +847,7 @@ swa_bwd_dkv_tc_persist_kernel(const __grid_constant__ CUtensorMap tq,
           for (int e = 0; e < 2; ++e) {
             const int c = cw + 16 * k + 2 * j + e, i = k0 + c;
             const bool ok = i >= t && i < t + W && i < L && t < L;
-            const float p = ok ? __expf(sv[2 * j + e] * scale - rl[c]) : 0.f;
+            const float p = ok ? tc::ex2(sv[2 * j + e] * scale_log2 - rl[c]) : 0.f;
             p2[e] = p;
             d2[e] = p * (dpv[2 * j + e] - rl[kBQ + c]);
           }
@@ -1240,13 +1254,27 @@ swa_bwd_dq_tc_persist_kernel(const __grid_constant__ CUtensorMap tq,
     const int r = 32 * qd + lane;
     const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
     const int cw = 32 * qd + 48 * hf;  // first key column of this thread's half window
+    const float scale_log2 = scale * kLog2e;
+    // lse and delta of this thread's row in item w2, loaded one item ahead
+    auto row_stats = [&](int w2, float& a, float& d) {
+      const int kl2 = w2 / grp, g2 = w2 - kl2 * grp;
+      int b2, hk2, q02;
+      tile(kl2, b2, hk2, q02);
+      const int i2 = q02 + r;
+      const size_t row2 = ((size_t)b2 * H + hk2 * grp + g2) * L + i2;
+      a = i2 < L ? lse[row2] : 0.f;
+      d = i2 < L ? delta[row2] : 0.f;
+    };
+    float nl = 0.f, nd = 0.f;
+    if (nitems > 0) row_stats(0, nl, nd);
     for (int w = 0; w < nitems; ++w) {
       const int kl = w / grp, g = w - kl * grp;
       int b, hk, q0;
       tile(kl, b, hk, q0);
       const int i = q0 + r, k0 = q0 - (kNK - kQ);  // this thread's query row
       const size_t row = ((size_t)b * H + hk * grp + g) * L + i;
-      const float lse_i = i < L ? lse[row] : 0.f, dl_i = i < L ? delta[row] : 0.f;
+      const float lse_i = nl * kLog2e, dl_i = nd;  // lse in base 2
+      if (w + 1 < nitems) row_stats(w + 1, nl, nd);
       tc::mbar_wait(&bars[QP_SD], (uint32_t)w & 1u, 95);
       tc::tc_fence_after();
       uint32_t dk8[3][8];
@@ -1263,7 +1291,7 @@ swa_bwd_dq_tc_persist_kernel(const __grid_constant__ CUtensorMap tq,
           for (int e = 0; e < 2; ++e) {
             const int t = k0 + cw + 16 * k + 2 * j + e;
             const bool ok = t <= i && t > i - W && t >= 0 && i < L;
-            const float p = ok ? __expf(sv[2 * j + e] * scale - lse_i) : 0.f;
+            const float p = ok ? tc::ex2(sv[2 * j + e] * scale_log2 - lse_i) : 0.f;
             d2[e] = p * (dpv[2 * j + e] - dl_i);
           }
           dk8[k][j] = pack_bf16(d2[0], d2[1]);
