@@ -1331,6 +1331,244 @@ swa_bwd_dq_tc_persist_kernel(const __grid_constant__ CUtensorMap tq,
   }
 }
 
+// The forward for bf16 operands (already rotated, no residual tiles) as a
+// persistent kernel, two CTAs per SM: each CTA walks its tiles (b, key/value
+// head, 128 query rows) and the group's query heads in each as one sequence of
+// items. A TMA / MMA warp (warp 8) keeps the next tile's keys and the next
+// items' queries loading ahead (two key buffers, two query stages, one value
+// buffer refilled as soon as a tile's last p V is done) and issues s = q k^T
+// and o = p_hi V + p_lo V; the next item's scores run while the row warps
+// write this item's output. The row warps' softmax is the arithmetic of
+// swa_fwd_tc_kernel. 106 KB of shared memory and 256 TMEM columns per CTA.
+struct FwdPersistSmem {
+  static constexpr size_t KB = kNK * 128, QB = kQ * 128;  // one k or v tile; one q tile
+  static constexpr size_t k = 0, v = 2 * KB, qs = v + KB, red = qs + 2 * QB;  // [max | sum][2][128]
+  static constexpr size_t bars = red + 2 * 2 * 128 * 4, slot = bars + 128, bytes = slot + 16;
+};
+enum { FP_K0 = 0, FP_K1, FP_V, FP_Q0, FP_Q1, FP_S, FP_O, FP_N };
+constexpr uint32_t kTfS = 0, kTfPh = 0, kTfPl = kNK / 2, kTfO = kNK, kTfCols = 256;
+
+__global__ void __launch_bounds__(kCtaThreads, 2)
+swa_fwd_tc_persist_kernel(const __grid_constant__ CUtensorMap tq,
+                          const __grid_constant__ CUtensorMap tk,
+                          const __grid_constant__ CUtensorMap tv,
+                          const float* __restrict__ meta, int n_meta, int W, float scale_log2,
+                          int H, int grp, int L, int nqb, int ntiles, bf16* __restrict__ y,
+                          float* __restrict__ lse, float* __restrict__ y32) {
+  using SM = FwdPersistSmem;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 84u);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::bars);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + SM::slot);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Hkv = H / grp;
+  constexpr uint32_t kTileK = kNK * 128, kTileQ = kQ * 128;
+  const int nloc = (int)((ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x);
+  const int nitems = nloc * grp;
+  auto tile = [&](int kl, int& b, int& hk, int& q0) {
+    const int tt = (int)blockIdx.x + kl * (int)gridDim.x;
+    const int qb = tt % nqb, bk = tt / nqb;
+    b = bk / Hkv, hk = bk - b * Hkv, q0 = qb * kQ;
+  };
+
+  if (tid == 0) {
+#pragma unroll
+    for (int j = 0; j < FP_N; ++j) tc::mbar_init(&bars[j], 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == 8) {
+    tc::tmem_alloc(tslot, kTfCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 8) {
+    const bool issuer = lane == 0;
+    auto load_k = [&](int kl) {
+      int b, hk, q0;
+      tile(kl, b, hk, q0);
+      uint64_t* bar = &bars[FP_K0 + (kl & 1)];
+      tc::mbar_expect_tx(bar, kTileK);
+      tc::tma_load_4d(smem + SM::k + (kl & 1) * SM::KB, &tk, 0, q0 - (kNK - kQ), hk, b, bar);
+    };
+    auto load_v = [&](int kl) {
+      int b, hk, q0;
+      tile(kl, b, hk, q0);
+      tc::mbar_expect_tx(&bars[FP_V], kTileK);
+      tc::tma_load_4d(smem + SM::v, &tv, 0, q0 - (kNK - kQ), hk, b, &bars[FP_V]);
+    };
+    auto load_q = [&](int w) {
+      int b, hk, q0;
+      tile(w / grp, b, hk, q0);
+      uint64_t* bar = &bars[FP_Q0 + (w & 1)];
+      tc::mbar_expect_tx(bar, kTileQ);
+      tc::tma_load_4d(smem + SM::qs + (w & 1) * SM::QB, &tq, 0, q0, hk * grp + w % grp, b, bar);
+    };
+    if (issuer) {
+      if (nloc > 0) load_k(0), load_v(0);
+      if (nloc > 1) load_k(1);
+      if (nitems > 0) load_q(0);
+      if (nitems > 1) load_q(1);
+    }
+    __syncwarp();
+    for (int w = 0; w < nitems; ++w) {
+      const int kl = w / grp, g = w - kl * grp;
+      if (issuer) {
+        if (g == 0) tc::mbar_wait(&bars[FP_K0 + (kl & 1)], (uint32_t)(kl >> 1) & 1u, 100);
+        tc::mbar_wait(&bars[FP_Q0 + (w & 1)], (uint32_t)(w >> 1) & 1u, 101);
+        if (w > 0) tc::mbar_wait(&bars[FP_O], (uint32_t)(w - 1) & 1u, 102);  // p read
+        tc::tc_fence_after();
+        constexpr uint32_t id_s = tc::idesc_bf16(kQ, kNK, 0, 0);  // q (K-major) x k (K-major)
+        const uint32_t kh = smem_u32(smem + SM::k + (kl & 1) * SM::KB);
+        const uint32_t qh = smem_u32(smem + SM::qs + (w & 1) * SM::QB);
+#pragma unroll
+        for (int j = 0; j < kDh / 16; ++j)
+          tc::mma_ss(tmem + kTfS, tc::sdesc(qh + 32 * j, 16, 1024),
+                     tc::sdesc(kh + 32 * j, 16, 1024), id_s, j > 0);
+        tc::mma_commit(&bars[FP_S]);
+      }
+      __syncwarp();
+      // p in TMEM; the row warps have also read the previous item's o
+      tc::named_bar_sync(NB_PREADY, kCtaThreads);
+      if (issuer) {
+        if (g == 0) tc::mbar_wait(&bars[FP_V], (uint32_t)kl & 1u, 103);
+        tc::tc_fence_after();
+        constexpr uint32_t id_o = tc::idesc_bf16(kQ, kDh, 0, 1);  // p (TMEM) x V (MN-major)
+        const uint32_t va = smem_u32(smem + SM::v);
+#pragma unroll
+        for (int j = 0; j < kNK / 16; ++j)
+          tc::mma_ts(tmem + kTfO, tmem + kTfPh + 8 * j, tc::sdesc(va + 2048 * j, kTileK, 1024),
+                     id_o, j > 0);
+#pragma unroll
+        for (int j = 0; j < kNK / 16; ++j)
+          tc::mma_ts(tmem + kTfO, tmem + kTfPl + 8 * j, tc::sdesc(va + 2048 * j, kTileK, 1024),
+                     id_o, 1u);
+        tc::mma_commit(&bars[FP_O]);
+        const bool last = g == grp - 1;
+        const bool refill = w + 2 < nitems || (last && kl + 1 < nloc);
+        if (refill) {
+          tc::mbar_wait(&bars[FP_O], (uint32_t)w & 1u, 104);  // item w's tiles read
+          if (w + 2 < nitems) load_q(w + 2);
+          if (last && kl + 1 < nloc) load_v(kl + 1);
+          if (last && kl + 2 < nloc) load_k(kl + 2);
+        }
+      }
+      __syncwarp();
+    }
+  } else {
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = 32 * qd + lane;
+    const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
+    const int cw = 32 * qd + 48 * hf;  // first score column of this thread's half window
+    float* red = reinterpret_cast<float*>(smem + SM::red);  // [max | sum][half][row]
+    // sinks seed the max and the row sum (log2 domain)
+    float ms = -1e30f;
+    for (int j = 0; j < n_meta; ++j) ms = fmaxf(ms, meta[j] * kLog2e);
+    float ls = 0.f;
+    for (int j = 0; j < n_meta; ++j) ls += exp2f(meta[j] * kLog2e - ms);
+    for (int w = 0; w < nitems; ++w) {
+      const int kl = w / grp, g = w - kl * grp;
+      int b, hk, q0;
+      tile(kl, b, hk, q0);
+      const int i = q0 + r, k0 = q0 - (kNK - kQ);
+      tc::mbar_wait(&bars[FP_S], (uint32_t)w & 1u, 105);
+      tc::tc_fence_after();
+      float sv[3][16];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) tc::tmem_ld16(trow + kTfS + cw + 16 * k, sv[k]);
+      tc::tmem_wait_ld();
+      float mx = ms;
+#pragma unroll
+      for (int k = 0; k < 3; ++k)
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const int t = k0 + cw + 16 * k + u;
+          const bool ok = t <= i && t > i - W && t >= 0;
+          const float x = ok ? sv[k][u] * scale_log2 : -INFINITY;
+          sv[k][u] = x;
+          mx = fmaxf(mx, x);
+        }
+      red[hf * kQ + r] = mx;
+      tc::tc_fence_before();
+      tc::named_bar_sync(NB_ROWS, kThreads);  // the partner's max; every score column read
+      tc::tc_fence_after();
+      mx = fmaxf(mx, red[(1 - hf) * kQ + r]);
+      float l = 0.f;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        uint32_t phi[8], plo[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float p0 = tc::ex2(sv[k][2 * j] - mx), p1 = tc::ex2(sv[k][2 * j + 1] - mx);
+          l += p0 + p1;
+          const uint32_t hpk = pack_bf16(p0, p1);
+          phi[j] = hpk;
+          plo[j] = pack_bf16(p0 - bf16_lo(hpk), p1 - bf16_hi(hpk));
+        }
+        tc::tmem_st8(trow + kTfPh + cw / 2 + 8 * k, phi);
+        tc::tmem_st8(trow + kTfPl + cw / 2 + 8 * k, plo);
+      }
+      {  // p is zero outside the window: packed columns [0, 16 qd) and [16 qd + 48, 96)
+        uint32_t zero[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) zero[j] = 0u;
+        const int z0 = hf ? 16 * qd + 48 : 0, z1 = hf ? kNK / 2 : 16 * qd;
+#pragma unroll 1
+        for (int c = z0; c < z1; c += 8) {
+          tc::tmem_st8(trow + kTfPh + c, zero);
+          tc::tmem_st8(trow + kTfPl + c, zero);
+        }
+      }
+      red[2 * kQ + hf * kQ + r] = l;
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      tc::named_bar_sync(NB_ROWS, kThreads);  // both halves' p stored and row sums written
+      tc::named_bar_arrive(NB_PREADY, kCtaThreads);
+      const float lrow = ls * exp2f(ms - mx) + red[2 * kQ + r] + red[3 * kQ + r];
+      const float inv = 1.f / lrow;
+      const size_t row = ((size_t)b * H + hk * grp + g) * L + i;
+      tc::mbar_wait(&bars[FP_O], (uint32_t)w & 1u, 106);
+      tc::tc_fence_after();
+      float o[32];
+      tc::tmem_ld32(trow + kTfO + 32 * hf, o);
+      tc::tmem_wait_ld();
+      tc::tc_fence_before();
+      if (i < L) {
+        bf16* yr = y + row * kDh + 32 * hf;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint4 wv;
+          wv.x = pack_bf16(o[8 * q4] * inv, o[8 * q4 + 1] * inv);
+          wv.y = pack_bf16(o[8 * q4 + 2] * inv, o[8 * q4 + 3] * inv);
+          wv.z = pack_bf16(o[8 * q4 + 4] * inv, o[8 * q4 + 5] * inv);
+          wv.w = pack_bf16(o[8 * q4 + 6] * inv, o[8 * q4 + 7] * inv);
+          reinterpret_cast<uint4*>(yr)[q4] = wv;
+        }
+        if (y32) {
+          float4* d32 = reinterpret_cast<float4*>(y32 + row * kDh + 32 * hf);
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4)
+            d32[q4] = make_float4(o[4 * q4] * inv, o[4 * q4 + 1] * inv, o[4 * q4 + 2] * inv,
+                                  o[4 * q4 + 3] * inv);
+        }
+        if (lse && hf == 0) lse[row] = mx * kLn2f + logf(lrow);
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTfCols);
+  }
+}
+
 // Tensor maps of the backward operands ([B, H or Hkv, L, 64] contiguous bf16);
 // false when one cannot be built.
 bool bwd_maps(const bf16* q, const bf16* ql, const bf16* dy, const bf16* k, const bf16* kl,
@@ -1414,9 +1652,29 @@ int swa_fwd_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, cons
                                              n_meta, W, B, H, Hkv, L, y, sv, nullptr, nullptr,
                                              nullptr, nullptr, st);
   }
-  return launch_swa_tc<false, false, float>(mq, mk, mv, mq, mk, nullptr, nullptr, 0, 0, meta,
-                                            n_meta, W, B, H, Hkv, L, y, sv, nullptr, nullptr,
-                                            nullptr, nullptr, st);
+  // bf16 operands: the persistent kernel, two CTAs per SM, once every CTA gets
+  // at least 8 tiles (with fewer, whole tiles split unevenly over the CTAs and
+  // the one-tile-per-CTA kernel's scheduling does better: B = 4, 8 key / value
+  // heads, L = 2048 measured 47 us against 45)
+  const int nqb = ceil_div(L, kQ);
+  const long long ntiles = (long long)B * Hkv * nqb;
+  int dev = 0, nsm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  if (nsm <= 0) nsm = 148;
+  if (ntiles < 16ll * nsm || ntiles >= (1ll << 31))
+    return launch_swa_tc<false, false, float>(mq, mk, mv, mq, mk, nullptr, nullptr, 0, 0, meta,
+                                              n_meta, W, B, H, Hkv, L, y, sv, nullptr, nullptr,
+                                              nullptr, nullptr, st);
+  static bool done_p[64] = {false};
+  const int rc = ensure_tc_smem(swa_fwd_tc_persist_kernel, FwdPersistSmem::bytes, done_p);
+  if (rc) return rc;
+  const int grid = (int)std::min<long long>(ntiles, 2ll * nsm);
+  swa_fwd_tc_persist_kernel<<<grid, kCtaThreads, FwdPersistSmem::bytes, st>>>(
+      mq, mk, mv, meta, n_meta, W, kLog2e / sqrtf((float)kDh), H, H / Hkv, L, nqb, (int)ntiles,
+      y, sv.lse, sv.y32);
+  count_launches(1);
+  return check_launch("swa_fwd_tc_persist_kernel");
 }
 
 int swa_bwd_dkv_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,

@@ -68,6 +68,39 @@ def test_swa_tc_matches_oracle(B, H, Hkv, L, W, n_meta, dtype):
         assert_grad(t.grad, r, f"{tag} {n}")
 
 
+@pytest.mark.parametrize("B,H,Hkv,L,W,n_meta,heads", [
+    (2, 32, 32, 5000, 64, 4, ((0, 0), (1, 31), (0, 17))),     # ragged last tile
+    (10, 32, 8, 4100, 17, 0, ((0, 0), (4, 13), (9, 31))),     # grp 4, odd window
+])
+def test_swa_tc_persistent_forward_matches_oracle(B, H, Hkv, L, W, n_meta, heads):
+    """bf16 operands with at least 16 x SM-count tiles of 128 query rows take
+    the persistent forward (two CTAs per SM, each walking 8 or more tiles);
+    sampled heads against the oracle, forward and backward (the backward
+    reads the lse and fp32 output it saved)."""
+    import lizard_cuda
+    nsm = torch.cuda.get_device_properties(0).multi_processor_count
+    assert B * Hkv * -(-L // 128) >= 16 * nsm, "shape too small for the persistent forward"
+    q, k, v, meta, dy = _inputs(B, H, Hkv, L, W, n_meta, torch.bfloat16, seed=L + W)
+    with torch.no_grad():
+        y_inf = lizard_cuda.swa(q, k, v, meta, W)
+    lv = [t.detach().clone().requires_grad_() for t in (q, k, v, meta)]
+    y = lizard_cuda.swa(*lv, W)
+    y.backward(dy)
+    torch.cuda.synchronize()
+    assert torch.equal(y_inf, y.detach())
+    grp = H // Hkv
+    for b, h in heads:
+        hk = h // grp
+        qs, ks, vs = q[b:b + 1, h:h + 1], k[b:b + 1, hk:hk + 1], v[b:b + 1, hk:hk + 1]
+        ref, rg = _oracle(qs, ks, vs, meta, W, dy[b:b + 1, h:h + 1])
+        tag = f"persistent swa B{B} H{H}/{Hkv} L{L} W{W} [{b},{h}]"
+        assert_output(y[b:b + 1, h:h + 1], ref, tag + " y")
+        assert_grad(lv[0].grad[b:b + 1, h:h + 1], rg[0], tag + " dq")
+        if grp == 1:  # dk / dv sum over the group's heads
+            assert_grad(lv[1].grad[b:b + 1, hk:hk + 1], rg[1], tag + " dk")
+            assert_grad(lv[2].grad[b:b + 1, hk:hk + 1], rg[2], tag + " dv")
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_swa_tc_close_to_warp_mma_kernel(dtype):
     """Same products, one softmax pass instead of the online rescaling: the
