@@ -443,23 +443,44 @@ swa_bwd_dq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k,
   }
 }
 
-// dmeta_j = -sum_b partial[b][j]: 256 threads, each summing a fixed strided
-// subset of blocks, then a fixed-order tree in shared memory.
-__global__ void __launch_bounds__(256)
+// dmeta_j = -sum_b partial[b][j]: thread t sums blocks t, t + 1024, ... for up
+// to 8 sinks at once (the block's sink partials are contiguous); a butterfly
+// over each warp's lanes, then warp 0 adds the 32 warp totals the same way:
+// the same order on every run.
+constexpr int kDmetaThreads = 1024, kDmetaSinks = 8;
+__global__ void __launch_bounds__(kDmetaThreads)
 swa_dmeta_kernel(const float* __restrict__ partial, int nblocks, int n_meta,
                  float* __restrict__ dmeta) {
-  __shared__ float red[256];
-  const int tid = threadIdx.x;
-  for (int j = 0; j < n_meta; ++j) {
-    float s = 0.f;
-    for (int b = tid; b < nblocks; b += 256) s += partial[(size_t)b * n_meta + j];
-    red[tid] = s;
-    __syncthreads();
-    for (int w = 128; w > 0; w >>= 1) {
-      if (tid < w) red[tid] += red[tid + w];
-      __syncthreads();
+  __shared__ float red[kDmetaSinks][32];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int j0 = 0; j0 < n_meta; j0 += kDmetaSinks) {
+    const int nj = min(kDmetaSinks, n_meta - j0);
+    float s[kDmetaSinks];
+#pragma unroll
+    for (int j = 0; j < kDmetaSinks; ++j) s[j] = 0.f;
+#pragma unroll 4
+    for (int b = tid; b < nblocks; b += kDmetaThreads) {
+      const float* p = partial + (size_t)b * n_meta + j0;
+#pragma unroll
+      for (int j = 0; j < kDmetaSinks; ++j)
+        if (j < nj) s[j] += p[j];
     }
-    if (tid == 0) dmeta[j] = -red[0];
+#pragma unroll
+    for (int j = 0; j < kDmetaSinks; ++j) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s[j] += __shfl_xor_sync(0xffffffffu, s[j], o);
+      if (lane == 0) red[j][warp] = s[j];
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+      for (int j = 0; j < kDmetaSinks; ++j) {
+        float x = red[j][lane];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+        if (lane == 0 && j < nj) dmeta[j0 + j] = -x;
+      }
+    }
     __syncthreads();
   }
 }
@@ -1055,7 +1076,7 @@ int swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const b
   if (rc) return rc;
   if (n_meta > 0 && dmeta) {
     const int nblocks = BH * ceil_div(L, kB);
-    swa_dmeta_kernel<<<1, 256, 0, st>>>(wk.partial, nblocks, n_meta, dmeta);
+    swa_dmeta_kernel<<<1, kDmetaThreads, 0, st>>>(wk.partial, nblocks, n_meta, dmeta);
     count_launches(1);
     rc = check_launch("swa_dmeta_kernel");
   }
