@@ -246,6 +246,11 @@ gla_bwd_state_tc_kernel(const __grid_constant__ CUtensorMap tq,
         tile_row_store(stage, t, w);
       }
       tc::fence_proxy_async_smem();
+      // Every prep thread arrives for this chunk before any arrives for the
+      // next: the next chunk's tiles are often loaded already, and one warp's
+      // arrival for it would otherwise complete this chunk's phase while
+      // another warp's rows of Q^ and delta were still being written.
+      tc::named_bar_sync(2, 128);
       tc::mbar_arrive(&bars[B1_QREADY]);
     }
   } else {

@@ -313,6 +313,29 @@ def test_gla_f128_without_grad_gives_the_same_output():
         assert torch.equal(lizard_cuda.gla(fq, fk, v, lg), y)
 
 
+def test_gla_f128_backward_is_deterministic():
+    """F = D = 128 training over 128 sequences of 16 chunks: two backward
+    passes give bit-identical gradients, and sampled heads match the oracle.
+    The reverse state walk hands each chunk from its prep warps to the MMA
+    through one barrier that all 128 prep threads arrive on; without a sync
+    among those threads a warp that ran ahead to the next chunk could complete
+    the current chunk's phase early, and a few heads' state gradients per run
+    came out wrong."""
+    fq, fk, v, lg, dy = baseline_inputs(4, 32, 2048, 128, 128, per_head=True, seed=31)
+    y0, g0 = cuda_gla(fq, fk, v, lg, dy)
+    y1, g1 = cuda_gla(fq, fk, v, lg, dy)
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1)
+    for n, a, b in zip(GRAD_NAMES, g0, g1):
+        assert torch.equal(a, b), f"{n} differs between two identical backward passes"
+    for b_, h in ((0, 0), (3, 29)):
+        sl = (slice(b_, b_ + 1), slice(h, h + 1))
+        ref, rg = oracle_gla(fq[sl], fk[sl], v[sl], lg[sl], dy[sl].bfloat16())
+        assert_output(y0[sl], ref, f"F=D=128 [{b_},{h}] y")
+        for got, r, n in zip(g0, rg, GRAD_NAMES):
+            assert_grad(got[sl], r, f"F=D=128 [{b_},{h}] {n}")
+
+
 def test_no_kernel_wait_timed_out():
     """Every bounded wait inside the tensor-core kernels completed."""
     from lizard_cuda import _lib
