@@ -339,7 +339,7 @@ def length_sweep(torch, lizard_cuda, device, lengths=(512, 1024, 2048, 4096, 819
 
 
 def prologue_measure(torch, lizard_cuda, device, steps=20, warmup=3):
-    """GLA prologue (SURVEY f1): the Hedgehog feature map of one projection at
+    """GLA prologue: the Hedgehog feature map of one projection at
     the model's head shape (B=4, H=32, L=4096, Dh=64, feature dim 128, fp32
     heads as the layer feeds them), fused kernel against the same torch ops
     (matmul, two softmaxes, concatenation, bf16 cast) on the GPU; forward and
@@ -395,7 +395,7 @@ LLAMA_1B = dict(hidden_size=2048, intermediate_size=8192, num_hidden_layers=16,
 
 
 def model_prefill_measure(torch, lizard_cuda, device, Bm=32, Lm=4096, steps=3, warmup=3):
-    """Config 5 (SURVEY f3): forward prefill of a random-init bf16 Lizard-Llama-3.2-1B
+    """Config 5: forward prefill of a random-init bf16 Lizard-Llama-3.2-1B
     (every attention layer swapped by lizard_cuda.model.to_lizard, window 64, 4 sinks,
     feature dim 128 -> F = 256, GQA 32/8 heads) on uniform random token ids, full logits.
     Device ms per step by CUDA events, tokens/s, and the same for one Lizard attention
@@ -440,7 +440,7 @@ def model_prefill_measure(torch, lizard_cuda, device, Bm=32, Lm=4096, steps=3, w
 
 
 def decode_measure(torch, model, cfg, ids, device, steps=8, warmup=2):
-    """Recurrent decode (SURVEY f4) of the config-5 model: the prompt ids [B, L]
+    """Recurrent decode of the config-5 model: the prompt ids [B, L]
     through the full forward into a LizardCache, then one greedy token per step
     for the whole batch (eager, one model call per step). Also the GLA decode
     kernel alone at the model's shape against its state traffic (the fp32 state

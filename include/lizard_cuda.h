@@ -424,7 +424,8 @@ int lz_swa_rope_fwd(const void* q, const void* k, const void* v, int x_dtype,
  * exceeds 4 MiB (about B*H*L = 1,000,000 rows). All calls on a device share
  * the array; calls that overlap on the GPU race on it. The first call on a
  * device looks up the array's address and should come before any stream
- * capture. */
+ * capture; that address is kept for the device's primary context, so after a
+ * cudaDeviceReset of the device this entry point must not be called again. */
 int lz_swa_bwd_noalloc(const void* q, const void* k, const void* v,
                        const void* q_lo, const void* k_lo,
                        const float* meta, int n_meta, int window,

@@ -19,7 +19,10 @@
 //    race on the array; serialise them.
 //  * The first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current and caches it; make that
-//    first call before any stream capture.
+//    first call before any stream capture. The cached address belongs to the
+//    device's primary context: after cudaDeviceReset (or anything else that
+//    destroys that context) it is stale, so a process that resets a device
+//    must not call this entry point on it again.
 #include <mutex>
 
 #include "common.cuh"

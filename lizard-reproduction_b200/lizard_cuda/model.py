@@ -39,16 +39,20 @@ def to_lizard(model, window=128, num_meta=4, feature_dim=128, backend="cuda"):
 
 def check_kernels(api, cfg):
     """Pre-flight check of the kernel backend named by cfg.lizard.backend.
-    Returns a one-line status; raises when the backend cannot run here (the
-    reference's check runner reports the exception as a failed check)."""
+    Returns a one-line status; raises RuntimeError when the backend cannot run
+    here (the reference's check runner reports any exception as a failed check,
+    src/check.py:39-45, where the triton branch asserts instead; a raised error
+    also survives python -O)."""
     backend = cfg.lizard.backend
     if backend != "cuda":
         return f"skipped, backend {backend}"
-    assert torch.cuda.is_available(), "the cuda backend needs a CUDA GPU"
+    if not torch.cuda.is_available():
+        raise RuntimeError("the cuda backend needs a CUDA GPU")
     lib = _lib.load()
     major, minor = torch.cuda.get_device_capability()
-    assert (major, minor) == (10, 0), (
-        f"liblizard_cuda.so is built for sm_100a; this GPU is sm_{major}{minor}")
+    if (major, minor) != (10, 0):
+        raise RuntimeError(
+            f"liblizard_cuda.so is built for sm_100a; this GPU is sm_{major}{minor}")
     return f"lizard_cuda ABI {lib.lz_abi_version()} on {torch.cuda.get_device_name()}"
 
 

@@ -7,11 +7,12 @@ for the fp32 upstream gradient and for its bf16 rounding (keys ending in _b),
 which is what a bf16-output kernel receives from autograd. This is exactly
 how the reference checks its kernels (tests/test_kernels.py:32-42, 61-70,
 121-122, 137-156). Needs a checkout of the reference; the path comes from
-LIZARD_REFERENCE_SRC (default: the reference's src/ directory mounted beside
-this repository). The fixtures are committed; the tests never need the
+LIZARD_REFERENCE_SRC when it is set, else from baseline/_ref at the root of
+this repository (where the reference's src/ modules are installed, unmodified,
+for the same-box timing). The fixtures are committed; the tests never need the
 reference.
 
-    python tests/golden/make_golden.py
+    LIZARD_REFERENCE_SRC=<reference checkout>/src python tests/golden/make_golden.py
 """
 import os
 import sys
@@ -23,11 +24,19 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
 import cases  # noqa: E402
 
-REF_SRC = os.environ.get("LIZARD_REFERENCE_SRC", "/root/reference/src")
+def _reference_src():
+    env = os.environ.get("LIZARD_REFERENCE_SRC")
+    if env:
+        return env
+    local = HERE.parents[1] / "baseline" / "_ref"
+    if (local / "lizard_attention.py").exists():
+        return str(local)
+    raise SystemExit("set LIZARD_REFERENCE_SRC to the reference's src/ directory "
+                     "(or install the reference into baseline/_ref)")
 
 
 def reference():
-    sys.path.insert(0, REF_SRC)
+    sys.path.insert(0, _reference_src())
     import lizard_attention as lz  # the reference module
     return lz
 

@@ -54,5 +54,5 @@ def test_check_kernels_skips_other_backends():
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU branch")
 def test_check_kernels_fails_without_a_gpu():
     from lizard_cuda.model import check_kernels
-    with pytest.raises(AssertionError, match="needs a CUDA GPU"):
+    with pytest.raises(RuntimeError, match="needs a CUDA GPU"):
         check_kernels(None, _cfg("cuda"))
