@@ -63,6 +63,10 @@ CASES = {
     "cfg5-hedgehog": (4, 32, 4096, 64, False, False, "hedgehog_bf16"),
     "cfg5-blend": (8, 32, 4096, 64, False, False, "blend"),
     "cfg5-decode": (32, 32, 4096, 256, False, False, "decode"),
+    # the same-box comparison against the reference's Triton kernels (and FLA)
+    "reference-gpu": (0, 0, 0, 0, False, False, "reference_gpu"),
+    # the sequence-parallel leg alone (with its parity check at N > 1)
+    "seqpar": (1, 32, 16384, 128, True, True, "seqpar"),
 }
 
 
@@ -285,12 +289,61 @@ def seqpar_measure(torch, lizard_cuda, device, dist, world, rank, steps=10, warm
             t.grad = None
         call(*leaves).backward(dy)
     both = timed(step)
+    check = None
+    if world > 1:
+        check = seqpar_check(torch, lizard_cuda, dist, world, rank,
+                             (fq, fk, v, lg, dy), [t.grad for t in leaves])
     return {"workload": f"gla config 4 long sequence: B=1 L={SEQ_L} H={SEQ_H} F=D={SEQ_FD}, "
                         f"per-head gate, {world} rank(s) x {Ls} tokens",
+            "check": check,
             "exchange": "none" if world == 1 else "one NCCL all_gather of the chunk-state "
                                                   "summaries per direction",
             "fwd_ms": fwd, "fwd_tokens_per_s": SEQ_L / (fwd / 1e3),
             "fwd_bwd_ms": both, "fwd_bwd_tokens_per_s": SEQ_L / (both / 1e3)}
+
+
+SEQ_CHECK_HEADS = (0, 17)
+SEQ_CHECK_LIMIT = 1e-2
+
+
+def seqpar_check(torch, lizard_cuda, dist, world, rank, inputs, grads):
+    """Correctness of the timed sequence-parallel call at N ranks: two sampled
+    heads of its output and of all four gradients (from the last timed step)
+    against one single-GPU gla call over the whole sequence of those heads,
+    whose inputs every rank gathers from the others. Each rank compares its
+    own slice; the result is max|err| / max|ref| over every compared tensor,
+    reduced as a max over ranks."""
+    from lizard_cuda import seqpar
+    hs = list(SEQ_CHECK_HEADS)
+    fq, fk, v, lg, dy = inputs
+    Ls = fq.shape[2]
+    full = []
+    for t in inputs:
+        part = t[:, hs].contiguous()
+        bufs = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(bufs, part)
+        full.append(torch.cat(bufs, dim=2))
+    with torch.no_grad():
+        y = seqpar.gla_seqpar(fq, fk, v, lg)[:, hs]
+    ref_leaves = [t.detach().clone().requires_grad_() for t in full[:4]]
+    ref_y = lizard_cuda.gla(*ref_leaves)
+    ref_y.backward(full[4])
+    a, b = rank * Ls, (rank + 1) * Ls
+    pairs = [("y", y, ref_y[:, :, a:b])]
+    for name, g, r in zip(("dfq", "dfk", "dv", "dlog_gamma"), grads, ref_leaves):
+        pairs.append((name, g[:, hs], r.grad[:, :, a:b]))
+    worst = {}
+    for name, got, ref in pairs:
+        err = (got.float() - ref.float()).abs().max()
+        den = ref.float().abs().max().clamp_min(1e-30)
+        worst[name] = err / den
+    vals = torch.stack([worst[n] for n, _, _ in pairs]).double()
+    dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    per = {n: float(x) for (n, _, _), x in zip(pairs, vals.tolist())}
+    mx = max(per.values())
+    return {"heads": hs, "max_rel": mx, "per_tensor": per, "limit": SEQ_CHECK_LIMIT,
+            "ok": mx <= SEQ_CHECK_LIMIT,
+            "against": "single-GPU lizard_cuda.gla over the whole sequence of the sampled heads"}
 
 
 def length_sweep(torch, lizard_cuda, device, lengths=(512, 1024, 2048, 4096, 8192, 16384),
@@ -394,12 +447,37 @@ LLAMA_1B = dict(hidden_size=2048, intermediate_size=8192, num_hidden_layers=16,
                               "high_freq_factor": 4.0, "original_max_position_embeddings": 8192})
 
 
-def model_prefill_measure(torch, lizard_cuda, device, Bm=32, Lm=4096, steps=3, warmup=3):
+def prefill_flops_per_token(cfg, Lm, window=64, feature_dim=128):
+    """Algorithmic flops per token of the config-5 prefill: 2 x every projection,
+    MLP and logit weight (2.47 GFLOP), plus per layer and head the GLA forward
+    2(2FD + CF + CD) with C = 64 (F = 2 feature_dim, D = head dim), the SWA
+    forward 4 D w (w = mean window size at length Lm) and the two Hedgehog
+    feature maps 2 Dh feature_dim (queries on all heads, keys on the KV heads)."""
+    h, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+    d = cfg.hidden_size // h
+    kv = hkv * d
+    per_layer = (2 * cfg.hidden_size * cfg.hidden_size + 2 * cfg.hidden_size * kv
+                 + 3 * cfg.hidden_size * cfg.intermediate_size + cfg.hidden_size)
+    linear = 2 * (cfg.num_hidden_layers * per_layer + cfg.hidden_size * cfg.vocab_size)
+    Fd = 2 * feature_dim
+    wbar = sum(min(i + 1, window) for i in range(Lm)) / Lm
+    attn = (h * 2 * (2 * Fd * d + 64 * Fd + 64 * d) + h * 4 * d * wbar
+            + (h + hkv) * 2 * d * feature_dim)
+    return linear + cfg.num_hidden_layers * attn
+
+
+def model_prefill_measure(torch, lizard_cuda, device, Bm=32, Lm=4096, steps=3, warmup=3,
+                          dist=None, world=1, decode=True):
     """Config 5: forward prefill of a random-init bf16 Lizard-Llama-3.2-1B
     (every attention layer swapped by lizard_cuda.model.to_lizard, window 64, 4 sinks,
     feature dim 128 -> F = 256, GQA 32/8 heads) on uniform random token ids, full logits.
     Device ms per step by CUDA events, tokens/s, and the same for one Lizard attention
-    layer alone at the model's shape (its share of the step)."""
+    layer alone at the model's shape (its share of the step). With N ranks the batch is
+    sharded: every rank runs Bm sequences (Bm = 32 / N from the caller), the ranks
+    start together after a barrier and the step time is the max over ranks; tokens/s
+    counts all ranks' tokens. The tensor roofline fraction is the whole step's
+    algorithmic flops over the sustained bf16 peak (a step of several hundred ms
+    runs under the power cap)."""
     from transformers import LlamaConfig, LlamaForCausalLM
     from lizard_cuda.model import to_lizard
     cfg = LlamaConfig(**LLAMA_1B)
@@ -407,12 +485,16 @@ def model_prefill_measure(torch, lizard_cuda, device, Bm=32, Lm=4096, steps=3, w
     with torch.device(device):
         model = LlamaForCausalLM(cfg).to(torch.bfloat16)
     to_lizard(model, window=64, num_meta=4, feature_dim=128).eval()
-    g = torch.Generator(device=device).manual_seed(3)
+    rank = dist.get_rank() if dist is not None else 0
+    g = torch.Generator(device=device).manual_seed(3 + rank)
     ids = torch.randint(0, cfg.vocab_size, (Bm, Lm), generator=g, device=device)
 
     def timed(fn, n, w):
         for _ in range(w):
             fn()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
@@ -420,23 +502,44 @@ def model_prefill_measure(torch, lizard_cuda, device, Bm=32, Lm=4096, steps=3, w
             fn()
         e.record()
         torch.cuda.synchronize()
-        return s.elapsed_time(e) / n
+        t = torch.tensor([s.elapsed_time(e) / n], device=device, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
-    out = {"workload": f"Lizard-Llama-3.2-1B prefill, random-init bf16, B={Bm} L={Lm}, "
-                       "uniform random ids, full logits, window 64, 4 sinks, F=256, GQA 32/8"}
+    out = {"workload": f"Lizard-Llama-3.2-1B prefill, random-init bf16, B={Bm * world} L={Lm} "
+                       f"({world} rank(s) x B={Bm}, batch sharded), uniform random ids, full "
+                       "logits, window 64, 4 sinks, F=256, GQA 32/8",
+           "n_gpus": world}
     with torch.no_grad():
         out["ms_per_step"] = timed(lambda: model(ids, use_cache=False).logits, steps, warmup)
-        out["tokens_per_s"] = Bm * Lm / (out["ms_per_step"] / 1e3)
+        out["tokens_per_s"] = world * Bm * Lm / (out["ms_per_step"] / 1e3)
         x = torch.randn(Bm, Lm, cfg.hidden_size, generator=g, device=device).bfloat16()
         pos = torch.arange(Lm, device=device)[None].expand(Bm, Lm)
         rope = model.model.rotary_emb(x, pos)
         attn = model.model.layers[0].self_attn
         out["attention_layer_ms"] = timed(lambda: attn(x, rope), steps, warmup)
     out["attention_share"] = cfg.num_hidden_layers * out["attention_layer_ms"] / out["ms_per_step"]
-    out["decode"] = decode_measure(torch, model, cfg, ids, device, steps=max(4, steps))
+    flops = prefill_flops_per_token(cfg, Lm) * Bm * Lm
+    tflops = flops / (out["ms_per_step"] / 1e3) / 1e12
+    sustained = measured_sustained_tflops()
+    out["tensor_roofline"] = {"flops_per_step_per_gpu": flops, "tflops_per_gpu": tflops,
+                              "peak_tflops": sustained[0], "peak_source": sustained[1],
+                              "frac": tflops / sustained[0]}
+    if decode:
+        out["decode"] = decode_measure(torch, model, cfg, ids, device, steps=max(4, steps))
     del model
     torch.cuda.empty_cache()
     return out
+
+
+def measured_sustained_tflops():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if "bf16_tflops_sustained" in d:
+            return float(d["bf16_tflops_sustained"]), "measured sustained (MEASURED_PEAKS.json)"
+    return 1400.0, "fallback sustained 1.4 PFLOP/s"
 
 
 def decode_measure(torch, model, cfg, ids, device, steps=8, warmup=2):
@@ -611,6 +714,162 @@ def secondary(torch, lizard_cuda, device, steps=50, warmup=5):
     return out
 
 
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def median_ms(torch, fn, leaves=(), reps=20, warmup=3):
+    """Median device ms of one call: CUDA events around each call, L2 flushed
+    (a 256 MB write) before each, gradients of `leaves` reset; the procedure of
+    the reference's own harness (triton.testing.do_bench with
+    return_mode="median", src/benchmark.py:57-66), written out here so every
+    implementation below is timed by the same code."""
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for _ in range(warmup):
+        for t in leaves:
+            t.grad = None
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    out = []
+    for _ in range(reps):
+        for t in leaves:
+            t.grad = None
+        flush.zero_()
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        out.append(s.elapsed_time(e))
+    del flush
+    return statistics.median(out)
+
+
+def reference_gpu_measure(torch, lizard_cuda, device, budget_s=420.0):
+    """Same-box timing of the reference's own GPU kernels: the Triton kernels.gla
+    and kernels.swa of src/kernels/ (installed unmodified in baseline/_ref), JIT
+    compiled here for sm_100, and flash-linear-attention's chunk_gla /
+    chunk_simple_gla when the fla package imports (the comparators of
+    src/benchmark.py:44-54). Every workload is timed for lizard_cuda and the
+    reference on the same inputs with median_ms; `ratio` = reference ms / our ms
+    (above 1: lizard_cuda is faster). Synthetic inputs with the BASELINE
+    distributions; FLA takes [B, L, H, D] and computes an unnormalised GLA, so
+    it is a speed comparator only."""
+    import torch.nn.functional as F
+    if not (REF_DIR / "kernels" / "__init__.py").exists():
+        return {"unavailable": "baseline/_ref/kernels is not installed"}
+    sys.path.insert(0, str(REF_DIR))
+    try:
+        import kernels as ref_kernels  # the reference's src/kernels package
+    except Exception as exc:  # noqa: BLE001 - report why the comparator is missing
+        return {"unavailable": f"import of the reference kernels failed: {exc!r}"}
+    try:
+        from fla.ops.gla import chunk_gla
+        from fla.ops.simple_gla import chunk_simple_gla
+    except Exception as exc:  # noqa: BLE001
+        chunk_gla = chunk_simple_gla = None
+        fla_note = f"fla not importable: {exc!r}"
+    else:
+        fla_note = "fla-core chunk_gla / chunk_simple_gla, scale 1.0"
+    t_start = time.perf_counter()
+    g = torch.Generator(device=device).manual_seed(77)
+
+    def feats(*shape):
+        return (F.softplus(torch.randn(shape, generator=g, device=device))
+                / math.sqrt(shape[-1])).bfloat16()
+
+    def gate(*shape):
+        return F.logsigmoid(3 + 1.5 * torch.randn(shape, generator=g, device=device))
+
+    out = {"harness": "median of per-call CUDA events, L2 flushed before each call, "
+                      "20 calls after 3 warm-ups",
+           "fla": fla_note, "workloads": {}}
+
+    def record(name, desc, ours_fn, ref_fn, leaves_ours=(), leaves_ref=(), fla=None):
+        if time.perf_counter() - t_start > budget_s:
+            out["workloads"][name] = {"skipped": f"time budget of {budget_s:.0f} s spent"}
+            return
+        row = {"workload": desc}
+        row["ours_ms"] = median_ms(torch, ours_fn, leaves_ours)
+        try:
+            row["reference_triton_ms"] = median_ms(torch, ref_fn, leaves_ref)
+            row["ratio"] = row["reference_triton_ms"] / row["ours_ms"]
+        except Exception as exc:  # noqa: BLE001 - e.g. out of memory in the reference
+            row["reference_triton_ms"] = None
+            row["reference_error"] = repr(exc)[:200]
+        if fla is not None:
+            for key, fn in fla.items():
+                try:
+                    row[key] = median_ms(torch, fn)
+                except Exception as exc:  # noqa: BLE001
+                    row[key] = None
+                    row[key + "_error"] = repr(exc)[:200]
+        out["workloads"][name] = row
+        torch.cuda.empty_cache()
+
+    def gla_case(name, Bc, Hc, Lc, FDc, per_head, train, with_fla=False):
+        fq, fk = feats(Bc, Hc, Lc, FDc), feats(Bc, Hc, Lc, FDc)
+        v = torch.randn(Bc, Hc, Lc, FDc, generator=g, device=device).bfloat16()
+        lg = gate(Bc, Hc, Lc) if per_head else gate(Bc, Lc)
+        desc = (f"gla {'fwd+bwd' if train else 'fwd'} B={Bc} H={Hc} L={Lc} F=D={FDc}, "
+                f"{'per-head' if per_head else 'per-token'} gate")
+        fla = None
+        if with_fla and chunk_gla is not None and not train:
+            qf, kf, vf = (t.transpose(1, 2).contiguous() for t in (fq, fk, v))
+            gf = lg.transpose(1, 2).contiguous() if per_head else lg
+            ge = gf[..., None].expand(*qf.shape).contiguous()
+            fla = {"fla_chunk_gla_ms": lambda: chunk_gla(qf, kf, vf, ge, scale=1.0)[0],
+                   "fla_chunk_simple_gla_ms": lambda: chunk_simple_gla(qf, kf, vf, gf,
+                                                                      scale=1.0)[0]}
+        if not train:
+            def ours():
+                with torch.no_grad():
+                    lizard_cuda.gla(fq, fk, v, lg)
+
+            def ref():
+                with torch.no_grad():
+                    ref_kernels.gla(fq, fk, v, lg)
+            record(name, desc, ours, ref, fla=fla)
+            return
+        dy = torch.randn(Bc, Hc, Lc, FDc, generator=g, device=device).bfloat16()
+        lo = [t.detach().clone().requires_grad_() for t in (fq, fk, v, lg)]
+        lr = [t.detach().clone().requires_grad_() for t in (fq, fk, v, lg)]
+        record(name, desc, lambda: lizard_cuda.gla(*lo).backward(dy),
+               lambda: ref_kernels.gla(*lr).backward(dy), lo, lr)
+
+    gla_case("cfg2_fwd", 8, 32, 2048, 128, True, False, with_fla=True)
+    gla_case("cfg3_gla_fwd_bwd", 1, 32, 2048, 64, False, True)
+    gla_case("cfg3_gla_fwd", 1, 32, 2048, 64, False, False)
+    # config 3 SWA on the same shape: window 64, 4 sinks
+    q, k = (torch.randn(1, 32, 2048, 64, generator=g, device=device).bfloat16()
+            for _ in range(2))
+    v = torch.randn(1, 32, 2048, 64, generator=g, device=device).bfloat16()
+    meta = torch.randn(4, generator=g, device=device)
+    dy = torch.randn(1, 32, 2048, 64, generator=g, device=device).bfloat16()
+    lo = [t.detach().clone().requires_grad_() for t in (q, k, v, meta)]
+    lr = [t.detach().clone().requires_grad_() for t in (q, k, v, meta)]
+    record("cfg3_swa_fwd_bwd", "swa fwd+bwd B=1 H=32 L=2048 D=64, window 64, 4 sinks",
+           lambda: lizard_cuda.swa(*lo, 64).backward(dy),
+           lambda: ref_kernels.swa(*lr, 64).backward(dy), lo, lr)
+
+    def swa_fwd_ours():
+        with torch.no_grad():
+            lizard_cuda.swa(q, k, v, meta, 64)
+
+    def swa_fwd_ref():
+        with torch.no_grad():
+            ref_kernels.swa(q, k, v, meta, 64)
+    record("cfg3_swa_fwd", "swa fwd B=1 H=32 L=2048 D=64, window 64, 4 sinks",
+           swa_fwd_ours, swa_fwd_ref)
+    del q, k, v, meta, dy, lo, lr
+    gla_case("cfg4_L2048_fwd_bwd", 16, 32, 2048, 128, True, True)
+    gla_case("cfg4_L8192_fwd_bwd", 16, 32, 8192, 128, True, True)
+    # the reference's own Table-3 forward shapes (src/benchmark.py:8-9), H=32, D=128
+    for Bt, Lt in ((16, 2048), (16, 4096), (16, 8192), (32, 8192)):
+        gla_case(f"table3_B{Bt}_L{Lt}_fwd", Bt, 32, Lt, 128, True, False, with_fla=True)
+    out["seconds"] = time.perf_counter() - t_start
+    return out
+
+
 def run_ours(args, torch):
     import lizard_cuda
     rank, local, world = env_rank()
@@ -718,12 +977,17 @@ def run_ours(args, torch):
     seq = None
     if not args.no_secondary:
         seq = seqpar_measure(torch, lizard_cuda, device, dist, world, rank)
+        model = None
+        if 32 % world == 0:  # config 5, batch sharded over every rank
+            model = model_prefill_measure(torch, lizard_cuda, device, Bm=32 // world,
+                                          dist=dist, world=world, decode=(world == 1))
         if rank == 0:
             side = secondary(torch, lizard_cuda, device)
+            side["cfg5_model_prefill"] = model
             if world == 1:
                 side["cfg4_length_sweep"] = length_sweep(torch, lizard_cuda, device)
                 side["prologue_hedgehog"] = prologue_measure(torch, lizard_cuda, device)
-                side["cfg5_model_prefill"] = model_prefill_measure(torch, lizard_cuda, device)
+                side["reference_gpu"] = reference_gpu_measure(torch, lizard_cuda, device)
 
     cpu = None
     if rank == 0 and world == 1:
@@ -772,6 +1036,9 @@ def run_ours(args, torch):
     if seq:
         line["seqpar"] = seq
     print(json.dumps(line), flush=True)
+    if seq and seq.get("check") and not seq["check"]["ok"]:
+        raise SystemExit(f"sequence-parallel check failed: max_rel {seq['check']['max_rel']:.3e} "
+                         f"> {SEQ_CHECK_LIMIT}")
 
 
 def run_case(args, torch):
@@ -782,11 +1049,33 @@ def run_case(args, torch):
     name = args.case
     Bc, Hc, Lc, FDc, per_head, train, op = CASES[name]
     Bc, Lc = args.B or Bc, args.L or Lc
+    if op == "seqpar":  # launched like the main bench: torchrun for N > 1
+        rank, local, world = env_rank()
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        dist = None
+        if world > 1:
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        res = seqpar_measure(torch, lizard_cuda, dev, dist, world, rank,
+                             steps=max(1, args.steps), warmup=args.warmup)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"case": name, "n_gpus": world, **res}), flush=True)
+            if res.get("check") and not res["check"]["ok"]:
+                raise SystemExit("sequence-parallel check failed")
+        return
     dev = torch.device("cuda", 0)
     if op == "model":
         res = model_prefill_measure(torch, lizard_cuda, dev, Bc, Lc, max(1, args.steps),
                                     args.warmup)
         print(json.dumps({"case": name, "B": Bc, "L": Lc, **res}), flush=True)
+        return
+    if op == "reference_gpu":
+        res = reference_gpu_measure(torch, lizard_cuda, dev)
+        print(json.dumps({"case": name, **res}), flush=True)
         return
     from lizard_cuda import _lib
     _lib.set_schedule(args.schedule)

@@ -96,6 +96,47 @@ def gla_recurrent(fq, fk, v, log_gamma):
     return torch.stack(out, dim=2)
 
 
+def gla_chunked(fq, fk, v, log_gamma, chunk=256):
+    """The same map as gla(), evaluated chunk by chunk with a carried state, so
+    memory is O(L chunk) instead of O(L^2) and long sequences (L = 16384) fit,
+    gradients included (plain autograd through the chunk loop).
+
+    Within a chunk the weights are dense, (fq_i . fk_t) exp(G_i - G_t) for
+    t <= i; the keys before the chunk enter through
+    S = sum_t exp(G_prev - G_t) fk_t v_t^T and z = sum_t exp(G_prev - G_t) fk_t,
+    G_prev the running log gate at the chunk's start, so every exponent is
+    <= 0. This is the chunk decomposition of src/kernels/gla.py:33-101
+    (states measured from chunk boundaries) without its bf16 roundings; in
+    float64 it agrees with gla() and gla_recurrent() to rounding.
+    """
+    b, h, n, f = fq.shape
+    G = torch.cumsum(log_gamma, -1)
+    if G.dim() == 2:
+        G = G[:, None].expand(b, h, n)
+    S = fq.new_zeros(b, h, f, v.shape[-1])
+    z = fq.new_zeros(b, h, f)
+    g_prev = fq.new_zeros(b, h)
+    tiny = torch.finfo(fq.dtype).tiny
+    out = []
+    for c0 in range(0, n, chunk):
+        c1 = min(n, c0 + chunk)
+        q, k, vv, g = fq[:, :, c0:c1], fk[:, :, c0:c1], v[:, :, c0:c1], G[:, :, c0:c1]
+        causal = torch.ones(c1 - c0, c1 - c0, dtype=torch.bool, device=fq.device).tril()
+        diff = (g[..., :, None] - g[..., None, :]).masked_fill(~causal, float("-inf"))
+        A = (q @ k.transpose(-1, -2)) * torch.exp(diff)
+        qt = q * torch.exp(g - g_prev[..., None])[..., None]
+        num = A @ vv + qt @ S
+        den = A.sum(-1) + (qt * z[:, :, None, :]).sum(-1)
+        out.append(num / den.clamp_min(tiny)[..., None])
+        g_end = g[..., -1]
+        kt = k * torch.exp(g_end[..., None] - g)[..., None]
+        lam = torch.exp(g_end - g_prev)
+        S = lam[..., None, None] * S + kt.transpose(-1, -2) @ vv
+        z = lam[..., None] * z + kt.sum(-2)
+        g_prev = g_end
+    return torch.cat(out, dim=2)
+
+
 def sink_softmax(scores, meta):
     """Softmax over the last axis with exp(meta_j) added to the denominator.
 

@@ -165,6 +165,40 @@ def test_gla_long_sequence_against_recurrent_float64():
     assert_output(y, ref, "L=4096 y")
 
 
+CFG4_HEADS = ((0, 0), (1, 13))
+
+
+@functools.lru_cache(maxsize=None)
+def _cfg4_long_reference(L):
+    """float64 forward and gradients of two sampled heads, chunk by chunk."""
+    fq, fk, v, lg, dy = baseline_inputs(2, 16, L, 128, 128, per_head=True, seed=41)
+    refs = {}
+    for b, h in CFG4_HEADS:
+        sl = (slice(b, b + 1), slice(h, h + 1))
+        leaves = [t[sl].double().cpu().clone().requires_grad_() for t in (fq, fk, v, lg)]
+        y = orc.gla_chunked(*leaves)
+        y.backward(dy[sl].bfloat16().double().cpu())
+        refs[b, h] = (y.detach(), [t.grad for t in leaves])
+    return refs
+
+
+@pytest.mark.parametrize("L", [8192, 16384])
+def test_gla_config4_top_length_forward_backward(L):
+    """Config 4's longest sequences (F = D = 128, per-head gate), forward and
+    backward over 64 / 128 chunks of 128 tokens: with the walk schedule the
+    tensor-core forward, state walk and chunk-gradient kernels (2 x 16
+    sequences, 4096 chunk CTAs at L = 16384); two sampled heads against the
+    float64 chunked form of the oracle, y and all four gradients."""
+    fq, fk, v, lg, dy = baseline_inputs(2, 16, L, 128, 128, per_head=True, seed=41)
+    y, grads = cuda_gla(fq, fk, v, lg, dy)
+    torch.cuda.synchronize()
+    for (b, h), (ref, rgrads) in _cfg4_long_reference(L).items():
+        sl = (slice(b, b + 1), slice(h, h + 1))
+        assert_output(y[sl], ref, f"L={L} y[{b},{h}]")
+        for got, r, n in zip(grads, rgrads, GRAD_NAMES):
+            assert_grad(got[sl], r, f"L={L} [{b},{h}] {n}")
+
+
 def test_gla_model_feature_dim_256():
     """F = 2 * feature_dim = 256 (the 1B model), D = 64, fwd + bwd."""
     fq, fk, v, lg, dy = baseline_inputs(1, 4, 300, 256, 64, per_head=False, seed=5)

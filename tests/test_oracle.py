@@ -1,5 +1,6 @@
 """The CPU oracle against the reference's own outputs (golden fixtures) and
 against the invariants the reference's tests pin (tests/test_lizard.py)."""
+import functools
 import math
 
 import pytest
@@ -84,6 +85,28 @@ def test_dense_matches_recurrent(length, per_head):
     torch.manual_seed(0)
     fq, fk, v, lg = _gla64(length, per_head=per_head)
     assert orc.rel(orc.gla(fq, fk, v, lg), orc.gla_recurrent(fq, fk, v, lg)) < EXACT
+
+
+@pytest.mark.parametrize("length,per_head,chunk,shift", [
+    (1, False, 256, 0.0), (77, False, 7, 0.0), (150, True, 64, 0.0), (300, True, 256, 0.0),
+    (200, False, 16, -6.0)])
+def test_chunked_matches_dense_with_gradients(length, per_head, chunk, shift):
+    """gla_chunked (the long-sequence checker of the GPU tests) equals the dense
+    form in float64, outputs and all four gradients, for chunk lengths that do
+    and do not divide L, both gate layouts and strong decay."""
+    torch.manual_seed(1)
+    fq, fk, v, lg = _gla64(length, per_head=per_head)
+    lg = lg + shift
+    dy = torch.randn(*fq.shape[:3], v.shape[-1], dtype=torch.float64)
+    outs = []
+    for fn in (orc.gla, functools.partial(orc.gla_chunked, chunk=chunk)):
+        leaves = [t.clone().requires_grad_() for t in (fq, fk, v, lg)]
+        y = fn(*leaves)
+        y.backward(dy)
+        outs.append([y.detach()] + [t.grad for t in leaves])
+    for a, b in zip(*outs):
+        # one token: y = v, so the feature gradients are exactly zero in both
+        assert (a - b).norm() <= EXACT * max(b.norm().item(), 1.0)
 
 
 def test_gate_zero_keeps_only_current_token():
