@@ -3,25 +3,44 @@
 //
 // One CTA per (batch*head) sequence walks 128-token chunks in order:
 //
-//   TMA warp     : fq, fk, v chunk tiles -> 2-stage shared-memory ring
-//                  (128-byte swizzle, 96 KB per stage)
-//   MMA thread   : s  = fq fk^T                        -> TMEM [128 x 128] f32
-//                  o  = Q~ S_n  +  a V   (a from TMEM)  -> TMEM [128 x 128] f32
-//                  dS = K~^T V,  dz = K~^T 1             -> TMEM
-//   epilogue WG  : a = bf16(s * 2^(g2_i - g2_t)), t <= i  -> TMEM (A operand)
-//   (4 warps,      Q~ = fq 2^(g2_i - start), K~ = fk 2^(end - g2_t) in place
-//    row i per     y_i = o_i / max(den_i, FLT_MIN) -> HBM
-//    thread)       S <- 2^(end-start) S + dS (fp32, registers) -> bf16 S (smem)
+//   TMA warp      : fq, fk, v chunk tiles -> 2-stage shared-memory ring
+//                   (128-byte swizzle, 96 KB per stage); the y tile of each
+//                   chunk out of its stage's fq block (TMA store)
+//   MMA thread    : s  = fq fk^T                        -> TMEM [128 x 128] f32
+//                   o  = a V  (a from TMEM), then  o += Q~ S_n
+//                   dS = K~^T V,  dz = K~^T 1             -> TMEM
+//   decay warps   : a = bf16(s * 2^(g2_i - g2_t)), t <= i  -> TMEM (A operand)
+//   (8 warps, two   and its row sums; K~ = fk 2^(end - g2_t) in place
+//    per TMEM lane
+//    quadrant)
+//   output warps  : y_i = o_i / max(den_i, FLT_MIN) -> staged for the TMA store
+//   (8 warps)       Q~ = fq 2^(g2_i - start) in place and Q~ . z;
+//                   S <- 2^(end-start) S + dS (fp32, TMEM) -> bf16 S (smem)
 //
 // This is the chunked GLA of the reference (src/kernels/gla.py:19-101) with
 // 128-token chunks; the running state stays on the SM. In training mode the
 // kernel also stores y in fp32, the row sums, G, and the bf16 state and fp32
 // normaliser entering every 128-token chunk (TMA store of the operand block)
-// for the backward (gla_bwd_tc.cu). G is the running
-// sum of the log gates, kept in base-2 units (g2 = G log2 e) so every decay is
-// one ex2. The normaliser state z is fp32 in shared memory and den_i = Q~_i.z
-// is summed on the CUDA cores; the intra-chunk row sum uses the same
-// bf16-rounded weights as the numerator (gla.py:90-95).
+// for the backward (gla_bwd_tc.cu). G is the running sum of the log gates,
+// kept in base-2 units (g2 = G log2 e) so every decay is one ex2.
+//
+// Pipeline. The shared-memory port is the busiest resource: every N = 128
+// MMA with both operands in shared memory reads about 128 B per cycle, so the
+// kernel keeps the CUDA cores' shared-memory traffic to the in-place Q~ / K~
+// scaling, the bf16 state and the y tile, and keeps the per-chunk chain short:
+//  * a V is issued as soon as the decay warps have written a and the output
+//    warps have read the previous o, ahead of Q~ S_n, which waits for the state;
+//  * K~ has its own barrier, so only the state MMAs wait for it;
+//  * the row sums run on the CUDA cores (an N = 16 MMA costs about as much
+//    issue time as an N = 128 one): the decay warps sum the same bf16-rounded
+//    weights the numerator uses (gla.py:90-95) and leave them in TMEM, the
+//    output warps form Q~ . z from the scaled Q~ values in registers;
+//  * Q~_{n+1} is scaled while the state MMAs of chunk n still run;
+//  * the fk / v blocks of a stage go back to TMA when the state MMAs are done,
+//    its fq block once the y store has read it (the TMA thread stores y and
+//    reloads fq in order);
+//  * each TMEM lane quadrant has two decay and two output warps, each taking
+//    half of the row's columns.
 #include <mutex>
 
 #include "common.cuh"
@@ -39,32 +58,33 @@ constexpr int kOffS = 2 * kStageBytes;      // bf16 state S [F x D], MN-major
 constexpr int kOffMisc = kOffS + 32768;     // ones row + barriers + per-chunk scalars
 constexpr int kMiscBytes = 3072;
 constexpr int kSmemBytes = kOffMisc + kMiscBytes;  // = 232448, the sm_100 maximum
-// misc block layout. It doubles as the 16-row K-major B operand of the
-// row-sum MMAs:
-//   block A = bytes [0, 2048): row 0 ones, row 1 z_hi[0:64], row 2 z_lo[0:64]
-//   block B = bytes [1024, 3072): row 0 ones, row 1 z_hi[64:128], row 2 z_lo[64:128]
-// (block B's rows 0-7 are block A's rows 8-15). den_intra = a . (row 0) and
-// den_inter = Q~ . (row 1 + row 2) land in TMEM columns; the products of the
-// other rows land in columns that are never read, so the remaining bytes hold
-// barriers and per-chunk scalars.
-constexpr int kMiscBars = 384;    // up to 16 mbarriers (rows 3..)
-constexpr int kMiscGS = 512;      // (start2, end2) per chunk parity
-constexpr int kMiscScan = 544;    // 4 warp totals
-constexpr int kMiscTmem = 560;    // TMEM base address
-constexpr int kMiscG = 1408;      // g2 of the current chunk, 128 floats
-constexpr int kMiscB = 2048;      // column decay factors 2^(g2_ref - g2_t), 128 floats
+// misc block layout. Bytes [0, 2048) double as the 16-row K-major B operand of
+// the normaliser MMA dz = K~^T 1: row 0 (bytes [0, 128)) holds ones, so result
+// column 0 is the column sum; the other rows only feed result columns that are
+// never read, so their bytes hold barriers and per-chunk scalars.
+constexpr int kMiscBars = 128;    // up to 16 mbarriers
+constexpr int kMiscGS = 256;      // (start2, end2) per chunk parity
+constexpr int kMiscScan = 272;    // 4 warp totals
+constexpr int kMiscTmem = 288;    // TMEM base address
+constexpr int kMiscG = 512;       // g2 of the current chunk, 128 floats
+constexpr int kMiscB = 1024;      // column decay factors 2^(g2_ref - g2_t), 128 floats
+constexpr int kMiscZ = 1536;      // fp32 normaliser z entering the chunk, 128 floats
+constexpr int kMiscDQ = 2048;     // Q~ . z halves of every row, 2 x 128 floats
 // TMEM columns: scores s, output o, running state S (fp32), normaliser z
-// (col 0), bf16 intra weights a (the A operand of a V), row sums: a . 1 at
-// kTDI, Q~ . z_hi and Q~ . z_lo at kTDQ + 1, + 2
+// (col 0 of a 16-column MMA result), bf16 intra weights a (the A operand of
+// a V), intra row sums (chunk parity x column half)
 constexpr uint32_t kTSA = 0, kTO = 128, kTSF = 256, kTZ = 384, kTA = 400, kTDI = 464,
-                   kTDQ = 480, kTCols = 512;
+                   kTCols = 512;
 
-enum { BAR_FULL0 = 0, BAR_FULL1, BAR_EMPTY0, BAR_EMPTY1, BAR_SFULL, BAR_AREADY, BAR_OFULL,
-       BAR_SREADY, BAR_GATE, BAR_SFDONE, BAR_COUNT };
+enum { BAR_FULL0 = 0, BAR_FULL1, BAR_EMPTY0, BAR_EMPTY1, BAR_SFULL, BAR_AREADY, BAR_KREADY,
+       BAR_OFULL, BAR_OFREE, BAR_SREADY, BAR_GATE, BAR_SFDONE, BAR_YREADY0, BAR_YREADY1,
+       BAR_COUNT };
 
-constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 decay, warps 6-9 output
+// warp 0 TMA, warp 1 MMA, warps 2-9 decay, warps 10-17 output
+constexpr int kThreads = 576;
+constexpr int kGroup = 256;  // threads of the decay group and of the output group
 
-// Timeouts: the decay and output warpgroups synchronise with bar.sync among
+// Timeouts: the decay and output warp groups synchronise with bar.sync among
 // themselves, so they never leave their chunk loop early. A wait that gives up
 // sets the device flag; every later wait then returns at once, the groups run
 // through their remaining iterations (writing in-bounds garbage) and reach
@@ -78,6 +98,8 @@ __device__ __forceinline__ uint4 scale8(uint4 w, float sc) {
   w.w = pack_bf16(bf16_lo(w.w) * sc, bf16_hi(w.w) * sc);
   return w;
 }
+
+__device__ __forceinline__ float sum_bf16x2(uint32_t p) { return bf16_lo(p) + bf16_hi(p); }
 
 __global__ void __launch_bounds__(kThreads, 1)
 gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -97,6 +119,8 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   uint64_t* bars = reinterpret_cast<uint64_t*>(misc + kMiscBars);
   float* sG = reinterpret_cast<float*>(misc + kMiscG);
   float* sB = reinterpret_cast<float*>(misc + kMiscB);
+  float* sZ = reinterpret_cast<float*>(misc + kMiscZ);
+  float* sDQ = reinterpret_cast<float*>(misc + kMiscDQ);
   float* sGS = reinterpret_cast<float*>(misc + kMiscGS);
   float* sScan = reinterpret_cast<float*>(misc + kMiscScan);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + kMiscTmem);
@@ -109,15 +133,21 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   if (tid == 0) {
     tc::mbar_init(&bars[BAR_FULL0], 1);
     tc::mbar_init(&bars[BAR_FULL1], 1);
-    // a stage is free once its MMAs are done and its fq block, reused as the
-    // y staging tile, has been read by the output store
-    tc::mbar_init(&bars[BAR_EMPTY0], 2);
-    tc::mbar_init(&bars[BAR_EMPTY1], 2);
+    // a stage's fk and v blocks are free once its state MMAs are done; its fq
+    // block, reused as the y staging tile, once the TMA thread's y store has read it
+    tc::mbar_init(&bars[BAR_EMPTY0], 1);
+    tc::mbar_init(&bars[BAR_EMPTY1], 1);
+    // y of a chunk is staged (one barrier per stage: its phases are the
+    // stage's chunks, so a wait is never two phases behind)
+    tc::mbar_init(&bars[BAR_YREADY0], kGroup);
+    tc::mbar_init(&bars[BAR_YREADY1], kGroup);
     tc::mbar_init(&bars[BAR_SFULL], 1);
-    tc::mbar_init(&bars[BAR_AREADY], 128);
+    tc::mbar_init(&bars[BAR_AREADY], kGroup);
+    tc::mbar_init(&bars[BAR_KREADY], kGroup);
     tc::mbar_init(&bars[BAR_OFULL], 1);
-    tc::mbar_init(&bars[BAR_SREADY], 128);
-    tc::mbar_init(&bars[BAR_GATE], 128);
+    tc::mbar_init(&bars[BAR_OFREE], kGroup);
+    tc::mbar_init(&bars[BAR_SREADY], kGroup);
+    tc::mbar_init(&bars[BAR_GATE], kGroup);
     tc::mbar_init(&bars[BAR_SFDONE], 1);
     tc::fence_mbar_init();
   }
@@ -132,19 +162,8 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     tc::tmem_alloc(tmem_slot, kTCols);
     tc::tmem_relinquish();
   }
-  if (warp >= 2 && warp < 6) {
-    const int e = tid - 64;  // 0..127
-    // ones in row 0 of both operand blocks, z = 0 in rows 1 and 2
-    if (e < 64) {
-      reinterpret_cast<bf16*>(misc)[e] = __float2bfloat16_rn(1.f);
-      reinterpret_cast<bf16*>(misc + 1024)[e] = __float2bfloat16_rn(1.f);
-    } else {
-      const int i = e - 64;
-      reinterpret_cast<bf16*>(misc + 128)[i] = __float2bfloat16_rn(0.f);
-      reinterpret_cast<bf16*>(misc + 256)[i] = __float2bfloat16_rn(0.f);
-      reinterpret_cast<bf16*>(misc + 1024 + 128)[i] = __float2bfloat16_rn(0.f);
-      reinterpret_cast<bf16*>(misc + 1024 + 256)[i] = __float2bfloat16_rn(0.f);
-    }
+  if (warp >= 2 && warp < 4) {  // the ones row of the normaliser MMA's B operand
+    reinterpret_cast<bf16*>(misc)[tid - 64] = __float2bfloat16_rn(1.f);
     tc::fence_proxy_async_smem();
   }
   tc::tc_fence_before();
@@ -153,23 +172,44 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- TMA
+    // ------------------------------------------------- TMA loads and y stores
     if (lane == 0) {
       int issued[2] = {0, 0};
+      int stored = 0;  // y tiles of chunks [0, stored) are stored
+      // y of chunk m leaves from its stage's fq block; the block is reusable
+      // once the store has read it
+      auto store_y = [&](int m) -> bool {
+        if (!tc::mbar_wait(&bars[BAR_YREADY0 + (m & 1)], (m >> 1) & 1, 14)) return false;
+        unsigned char* ystage = base + (m & 1) * kStageBytes + kOffQ;
+        tc::tma_store_3d(&ty, ystage, 0, m * kC, bh);
+        tc::tma_store_3d(&ty, ystage + 16384, 64, m * kC, bh);
+        tc::bulk_commit();
+        ++stored;
+        return true;
+      };
       for (int n = 0; n < NT; ++n) {
         const int st = n & 1;
-        if (n >= 2 && !tc::mbar_wait(&bars[BAR_EMPTY0 + st], ((n - 2) >> 1) & 1, 1)) break;
         unsigned char* stage = base + st * kStageBytes;
         uint64_t* full = &bars[BAR_FULL0 + st];
+        // fk and v of chunk n - 2 are consumed once its state MMAs are done
+        if (n >= 2 && !tc::mbar_wait(&bars[BAR_EMPTY0 + st], ((n - 2) >> 1) & 1, 1)) break;
         tc::mbar_expect_tx(full, kStageBytes);
-        tc::tma_load_3d(stage + kOffQ, &tq, 0, n * kC, bh, full);
-        tc::tma_load_3d(stage + kOffQ + 16384, &tq, 64, n * kC, bh, full);
         tc::tma_load_3d(stage + kOffK, &tk, 0, n * kC, kvh, full);
         tc::tma_load_3d(stage + kOffK + 16384, &tk, 64, n * kC, kvh, full);
         tc::tma_load_3d(stage + kOffV, &tv, 0, n * kC, kvh, full);
         tc::tma_load_3d(stage + kOffV + 16384, &tv, 64, n * kC, kvh, full);
         ++issued[st];
+        // the fq block holds y of chunk n - 2 until its store has read it
+        if (n >= 2) {
+          if (!store_y(n - 2)) break;
+          tc::bulk_wait_read0();
+        }
+        tc::tma_load_3d(stage + kOffQ, &tq, 0, n * kC, bh, full);
+        tc::tma_load_3d(stage + kOffQ + 16384, &tq, 64, n * kC, bh, full);
       }
+      while (stored < NT && !*(volatile unsigned int*)&tc::g_timeout_flag && store_y(stored)) {
+      }
+      tc::bulk_wait0();  // every y store is complete before the CTA exits
       for (int st = 0; st < 2; ++st)  // every issued copy lands before exit
         if (issued[st]) tc::mbar_wait(&bars[BAR_FULL0 + st], (issued[st] - 1) & 1, 9);
     }
@@ -180,7 +220,6 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       constexpr uint32_t id_o = tc::idesc_bf16(128, 128, 0, 1);   // Q~|a (K) x S|V (MN)
       constexpr uint32_t id_ds = tc::idesc_bf16(128, 128, 1, 1);  // K~ (MN) x V (MN)
       constexpr uint32_t id_dz = tc::idesc_bf16(128, 16, 1, 0);   // K~ (MN) x ones (K)
-      constexpr uint32_t id_n16 = tc::idesc_bf16(128, 16, 0, 0);  // Q~|a (K) x ones|z (K)
       const uint32_t s_addr = smem_u32(base + kOffS);
       const uint32_t ones = smem_u32(misc);
       // s = fq fk^T of chunk m into TMEM, signalled on BAR_SFULL
@@ -203,36 +242,31 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
           const int st = n & 1;
           const uint32_t stage = smem_u32(base + st * kStageBytes);
           const uint32_t qa = stage + kOffQ, ka = stage + kOffK, va = stage + kOffV;
+          // o = a V: the weights are written and the previous o has been read
           if (!tc::mbar_wait(&bars[BAR_AREADY], n & 1, 3)) break;
-          if (n > 0 && !tc::mbar_wait(&bars[BAR_SREADY], (n - 1) & 1, 4)) break;
+          if (n > 0 && !tc::mbar_wait(&bars[BAR_OFREE], (n - 1) & 1, 12)) break;
           tc::tc_fence_after();
-          // o = Q~ S_n + a V; row sums Q~ . z_n and a . 1
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            tc::mma_ts(tmem + kTO, tmem + kTA + 8 * j, tc::sdesc(va + 2048 * j, 16384, 1024),
+                       id_o, j > 0);
+          // o += Q~ S_n once the state and Q~ are in shared memory
           if (n > 0) {
+            if (!tc::mbar_wait(&bars[BAR_SREADY], (n - 1) & 1, 4)) break;
+            tc::tc_fence_after();
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               const uint32_t ko = (j >> 2) * 16384 + (j & 3) * 32;
               tc::mma_ss(tmem + kTO, tc::sdesc(qa + ko, 16, 1024),
-                         tc::sdesc(s_addr + 2048 * j, 16384, 1024), id_o, j > 0);
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const uint32_t ko = (j >> 2) * 16384 + (j & 3) * 32;
-              tc::mma_ss(tmem + kTDQ, tc::sdesc(qa + ko, 16, 1024),
-                         tc::sdesc(ones + (j >> 2) * 1024 + (j & 3) * 32, 16, 1024), id_n16,
-                         j > 0);
+                         tc::sdesc(s_addr + 2048 * j, 16384, 1024), id_o, 1u);
             }
           }
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            tc::mma_ts(tmem + kTO, tmem + kTA + 8 * j, tc::sdesc(va + 2048 * j, 16384, 1024),
-                       id_o, (n > 0 || j > 0) ? 1u : 0u);
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            tc::mma_ts(tmem + kTDI, tmem + kTA + 8 * j, tc::sdesc(ones + 32 * (j & 3), 16, 1024),
-                       id_n16, j > 0);
           tc::mma_commit(&bars[BAR_OFULL]);
-          // next chunk's scores go ahead of this chunk's state update, so the
-          // decay warps can start on them while the state MMAs run
+          // K~ of this chunk is scaled; the next chunk's scores go ahead of this
+          // chunk's state update so the decay warps can start on them while the
+          // state MMAs run
+          if (!tc::mbar_wait(&bars[BAR_KREADY], n & 1, 13)) break;
+          tc::tc_fence_after();
           if (n + 1 < NT && !issue_scores(n + 1)) break;
           // running state: the output warps pre-scaled S and z by this chunk's decay
 #pragma unroll
@@ -250,160 +284,167 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         }
       }
     }
-  } else if (warp < 6) {
-    // ------------------------------- decay warps: gates, s -> a, K~ in place
+  } else if (warp < 10) {
+    // ------------------- decay warps: gates, s -> a and its row sums, K~ in place
+    const int dw = warp - 2;             // 0..7
+    const int h = dw >> 2;               // column half of every 32-column score block
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // chunk row == TMEM lane
+    const int r = quad * 32 + lane;      // chunk row == TMEM lane
+    const int et = (dw << 5) | lane;     // 0..255 within the group
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
     const float* LG = lg + (size_t)(gate_per_head ? bh : b) * L;
     float carry = 0.f;
-    float lg_next = (r < L) ? LG[r] : 0.f;
+    float lg_next = (h == 0 && r < L) ? LG[r] : 0.f;
     for (int n = 0; n < NT; ++n) {
       const int r0 = n * kC;
       const int nvalid = min(kC, L - r0);
       const bool valid = r < nvalid;
-      float x = valid ? lg_next * kLog2e : 0.f;
-      if (r0 + kC + r < L) lg_next = LG[r0 + kC + r];  // prefetch the next chunk's gate
+      float x = (h == 0 && valid) ? lg_next * kLog2e : 0.f;
+      if (h == 0 && r0 + kC + r < L) lg_next = LG[r0 + kC + r];  // the next chunk's gate
       tc::mbar_wait(&bars[BAR_SFULL], n & 1, 5);
       tc::tc_fence_after();
-      // running log2 gate: inclusive scan over the chunk's 128 rows
+      // running log2 gate: inclusive scan over the chunk's 128 rows (first half)
+      if (h == 0) {
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float u = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += u;
+        for (int o = 1; o < 32; o <<= 1) {
+          const float u = __shfl_up_sync(0xffffffffu, x, o);
+          if (lane >= o) x += u;
+        }
+        if (lane == 31) sScan[quad] = x;
       }
-      if (lane == 31) sScan[quad] = x;
-      tc::named_bar_sync(1, 128);
-      float pre = 0.f;
+      tc::named_bar_sync(1, kGroup);
+      if (h == 0) {
+        float pre = 0.f;
 #pragma unroll
-      for (int qq = 0; qq < 4; ++qq)
-        if (qq < quad) pre += sScan[qq];
-      const float g2 = carry + pre + x;
-      sG[r] = g2;
-      // column factor relative to the last row of this row's 32-block (= lane 31)
-      sB[r] = tc::ex2(__shfl_sync(0xffffffffu, g2, 31) - g2);
-      const float start2 = carry;
-      if (r == 0) sGS[(n & 1) * 2] = start2;
-      if (r == nvalid - 1) sGS[(n & 1) * 2 + 1] = g2;
-      tc::named_bar_sync(1, 128);
+        for (int qq = 0; qq < 4; ++qq)
+          if (qq < quad) pre += sScan[qq];
+        const float g2 = carry + pre + x;
+        sG[r] = g2;
+        // column factor relative to the last row of this row's 32-block (= lane 31)
+        sB[r] = tc::ex2(__shfl_sync(0xffffffffu, g2, 31) - g2);
+        if (r == 0) sGS[(n & 1) * 2] = carry;
+        if (r == nvalid - 1) sGS[(n & 1) * 2 + 1] = g2;
+      }
+      tc::named_bar_sync(1, kGroup);
+      const float g2 = sG[r];
       const float end2 = sGS[(n & 1) * 2 + 1];
       carry = end2;
       tc::mbar_arrive(&bars[BAR_GATE]);
-      if (save && valid) g_out[(size_t)bh * L + r0 + r] = g2 * 0.6931471805599453f;
-      // a = bf16(s 2^(g2_r - g2_t)) for t <= r. Blocks left of the diagonal use
-      // 2^(g2_r - g2_ref) 2^(g2_ref - g2_t) with ref the block's last row (both
-      // factors <= 1); the diagonal block takes one ex2 per element; blocks to
-      // its right are zero. The row sums come from the MMA (a . 1).
+      if (save && valid && h == 0) g_out[(size_t)bh * L + r0 + r] = g2 * 0.6931471805599453f;
+      // a = bf16(s 2^(g2_r - g2_t)) for t <= r, this warp's 16 columns of every
+      // 32-column block. Blocks left of the diagonal use 2^(g2_r - g2_ref)
+      // 2^(g2_ref - g2_t) with ref the block's last row (both factors <= 1); the
+      // diagonal block takes one ex2 per element; blocks to its right are zero.
+      float den = 0.f;
 #pragma unroll 1
       for (int cb = 0; cb < 4; ++cb) {
-        uint32_t pk[16];
+        uint32_t pk[8];
+        const int c0 = 32 * cb + 16 * h;
         if (cb < quad) {
-          float s[32];
-          tc::tmem_ld32(trow + kTSA + 32 * cb, s);
+          float sc[16];
+          tc::tmem_ld16(trow + kTSA + c0, sc);
           const float ar = valid ? tc::ex2(g2 - sG[32 * cb + 31]) : 0.f;
-          const float4* bt = reinterpret_cast<const float4*>(sB + 32 * cb);
+          const float4* bt = reinterpret_cast<const float4*>(sB + c0);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
+          for (int j4 = 0; j4 < 4; ++j4) {
             const float4 f = bt[j4];
-            const uint32_t p0 = pack_bf16(s[4 * j4] * f.x * ar, s[4 * j4 + 1] * f.y * ar);
-            const uint32_t p1 = pack_bf16(s[4 * j4 + 2] * f.z * ar, s[4 * j4 + 3] * f.w * ar);
-            pk[2 * j4] = p0;
-            pk[2 * j4 + 1] = p1;
+            pk[2 * j4] = pack_bf16(sc[4 * j4] * f.x * ar, sc[4 * j4 + 1] * f.y * ar);
+            pk[2 * j4 + 1] = pack_bf16(sc[4 * j4 + 2] * f.z * ar, sc[4 * j4 + 3] * f.w * ar);
           }
         } else if (cb == quad) {
-          float s[32];
-          tc::tmem_ld32(trow + kTSA + 32 * cb, s);
-          const float4* gt = reinterpret_cast<const float4*>(sG + 32 * cb);
+          float sc[16];
+          tc::tmem_ld16(trow + kTSA + c0, sc);
+          const float4* gt = reinterpret_cast<const float4*>(sG + c0);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
+          for (int j4 = 0; j4 < 4; ++j4) {
             const float4 f = gt[j4];
-            const int t = 32 * cb + 4 * j4;
-            float w0 = s[4 * j4] * tc::ex2(g2 - f.x);
-            float w1 = s[4 * j4 + 1] * tc::ex2(g2 - f.y);
-            float w2 = s[4 * j4 + 2] * tc::ex2(g2 - f.z);
-            float w3 = s[4 * j4 + 3] * tc::ex2(g2 - f.w);
+            const int t = c0 + 4 * j4;
+            float w0 = sc[4 * j4] * tc::ex2(g2 - f.x);
+            float w1 = sc[4 * j4 + 1] * tc::ex2(g2 - f.y);
+            float w2 = sc[4 * j4 + 2] * tc::ex2(g2 - f.z);
+            float w3 = sc[4 * j4 + 3] * tc::ex2(g2 - f.w);
             w0 = (t <= r && valid) ? w0 : 0.f;
             w1 = (t + 1 <= r && valid) ? w1 : 0.f;
             w2 = (t + 2 <= r && valid) ? w2 : 0.f;
             w3 = (t + 3 <= r && valid) ? w3 : 0.f;
-            const uint32_t p0 = pack_bf16(w0, w1), p1 = pack_bf16(w2, w3);
-            pk[2 * j4] = p0;
-            pk[2 * j4 + 1] = p1;
+            pk[2 * j4] = pack_bf16(w0, w1);
+            pk[2 * j4 + 1] = pack_bf16(w2, w3);
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) pk[j] = 0u;
+          for (int j = 0; j < 8; ++j) pk[j] = 0u;
         }
-        tc::tmem_st16(trow + kTA + 16 * cb, pk);
-      }
-      // K~ = fk 2^(end - g2) in place. The causal mask gives the warp of rows
-      // 32q..32q+31 q+1 score blocks, so the K~ rows go to the lighter warps:
-      // quad 0 scales rows 0..63, quad 1 rows 64..95, quad 2 rows 96..127.
-      {
-        unsigned char* stage = base + (n & 1) * kStageBytes;
-        const int npass = quad == 0 ? 2 : (quad == 3 ? 0 : 1);
-        const int row0 = quad == 0 ? 0 : 32 + 32 * quad;
-#pragma unroll 1
-        for (int ps = 0; ps < npass; ++ps) {
-          const int t = row0 + 32 * ps + lane;
-          const float ks = t < nvalid ? tc::ex2(end2 - sG[t]) : 0.f;
-          uint4 w[16];
+        if (cb <= quad) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            w[i] = *reinterpret_cast<const uint4*>(stage + kOffK + (i >> 3) * 16384 + t * 128 +
-                                                   (((i & 7) ^ (t & 7)) * 16));
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            *reinterpret_cast<uint4*>(stage + kOffK + (i >> 3) * 16384 + t * 128 +
-                                      (((i & 7) ^ (t & 7)) * 16)) = scale8(w[i], ks);
+          for (int j = 0; j < 8; ++j) den += sum_bf16x2(pk[j]);
         }
+        tc::tmem_st8(trow + kTA + 16 * cb + 8 * h, pk);
       }
-      tc::fence_proxy_async_smem();
+      // this half's row sum of the bf16 weights, one column per (parity, half)
+      tc::tmem_st1(trow + kTDI + 2 * (n & 1) + h, __float_as_uint(den));
       tc::tmem_wait_st();
       tc::tc_fence_before();
       tc::mbar_arrive(&bars[BAR_AREADY]);
+      // K~ = fk 2^(end - g2) in place: thread et scales one 64-column half of row et / 2
+      {
+        unsigned char* stage = base + (n & 1) * kStageBytes;
+        const int t = et >> 1, hb = et & 1;
+        const float ks = t < nvalid ? tc::ex2(end2 - sG[t]) : 0.f;
+        unsigned char* row = stage + kOffK + hb * 16384 + t * 128;
+        uint4 w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          w[i] = *reinterpret_cast<const uint4*>(row + ((i ^ (t & 7)) * 16));
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          *reinterpret_cast<uint4*>(row + ((i ^ (t & 7)) * 16)) = scale8(w[i], ks);
+      }
+      tc::fence_proxy_async_smem();
+      tc::mbar_arrive(&bars[BAR_KREADY]);
     }
   } else {
     // ------------- output warps: y; S, z for the next chunk; Q~ in place
+    const int ow = warp - 10;            // 0..7
+    const int h = ow >> 2;               // column half
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // chunk row for o; state row f for S, z
+    const int r = quad * 32 + lane;      // chunk row for o; state row f for S, z
+    const int et = (ow << 5) | lane;     // 0..255 within the group
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
-    unsigned char* srow_base = base + kOffS + r * 128;
-    // z_hi / z_lo of state row r: row 1 / row 2 of operand block r / 64, column
-    // r % 64, in the 128-byte swizzled layout
-    unsigned char* zblk = misc + (r >> 6) * 1024;
-    const int zcol = ((((r & 63) >> 3) ^ 1) << 4) + (r & 7) * 2;
-    const int zcol2 = ((((r & 63) >> 3) ^ 2) << 4) + (r & 7) * 2;
+    unsigned char* srow = base + kOffS + h * 16384 + r * 128;  // this half of state row r
+    sDQ[h * 128 + r] = 0.f;              // no state enters chunk 0
     if (save) {  // the state entering chunk 0 is zero
-      uint4* p = reinterpret_cast<uint4*>(s_out + ((size_t)bh * NT * 128 + r) * 128);
+      uint4* p = reinterpret_cast<uint4*>(s_out + ((size_t)bh * NT * 128 + r) * 128 + 64 * h);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) p[i] = make_uint4(0u, 0u, 0u, 0u);
-      z_out[(size_t)bh * NT * 128 + r] = 0.f;
+      for (int i = 0; i < 8; ++i) p[i] = make_uint4(0u, 0u, 0u, 0u);
+      if (h == 0) z_out[(size_t)bh * NT * 128 + r] = 0.f;
     }
+    tc::named_bar_sync(4, kGroup);
     for (int n = 0; n < NT; ++n) {
       const int r0 = n * kC;
       const int nvalid = min(kC, L - r0);
       const bool valid = r < nvalid;
       tc::mbar_wait(&bars[BAR_OFULL], n & 1, 6);
       tc::tc_fence_after();
-      // y = o / max(den, FLT_MIN), den = a . 1 + Q~ . z_hi + Q~ . z_lo
-      float dv[32];
-      tc::tmem_ld32(trow + kTDI, dv);
+      // intra row sums (both halves) and this half of o; then o is free for the next a V
+      const float di0 = tc::tmem_ld1(trow + kTDI + 2 * (n & 1));
+      const float di1 = tc::tmem_ld1(trow + kTDI + 2 * (n & 1) + 1);
+      float o[64];
+      tc::tmem_ld64(trow + kTO + 64 * h, o);
+      // den = a . 1 + Q~ . z (the Q~ . z halves were formed with Q~)
+      const float dq = sDQ[r] + sDQ[128 + r];
       tc::tmem_wait_ld();
-      const float dtot = dv[0] + (n > 0 ? dv[17] + dv[18] : 0.f);
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars[BAR_OFREE]);
+      // y = o / max(den, FLT_MIN): this half of row r into the stage's fq block
+      // (every MMA reading it is done) in the 128-byte swizzled box layout; the
+      // TMA thread stores the tile
+      const float dtot = di0 + di1 + dq;
       const float inv = 1.f / fmaxf(dtot, kTiny);
       const size_t row = (size_t)bh * L + r0 + r;
-      // y rows go to the stage's fq block (free now: every MMA of this chunk is
-      // done) in the 128-byte swizzled box layout, then out with one TMA store
-      unsigned char* ystage = base + (n & 1) * kStageBytes + kOffQ;
-#pragma unroll 1
-      for (int hb = 0; hb < 2; ++hb) {
-        float o[64];
-        tc::tmem_ld64(trow + kTO + 64 * hb, o);
-        tc::tmem_wait_ld();
-        unsigned char* yrow = ystage + hb * 16384 + r * 128;
+      {
+        unsigned char* yrow = base + (n & 1) * kStageBytes + kOffQ + h * 16384 + r * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           uint4 w;
@@ -413,52 +454,70 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
           w.w = pack_bf16(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
           *reinterpret_cast<uint4*>(yrow + ((c ^ (r & 7)) * 16)) = w;
         }
-        if (save && valid) {
-          float4* d32 = reinterpret_cast<float4*>(y32 + row * 128 + 64 * hb);
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(&bars[BAR_YREADY0 + (n & 1)]);
+      }
+      if (valid) {
+        if (save) {
+          float4* d32 = reinterpret_cast<float4*>(y32 + row * 128 + 64 * h);
 #pragma unroll
           for (int q4 = 0; q4 < 16; ++q4)
             d32[q4] = make_float4(o[4 * q4] * inv, o[4 * q4 + 1] * inv, o[4 * q4 + 2] * inv,
                                   o[4 * q4 + 3] * inv);
+          if (h == 0) den_out[row] = dtot;
         }
       }
-      tc::fence_proxy_async_smem();
-      tc::named_bar_sync(2, 128);
-      if (r == 0) {
-        tc::tma_store_3d(&ty, ystage, 0, r0, bh);
-        tc::tma_store_3d(&ty, ystage + 16384, 64, r0, bh);
-        tc::bulk_commit();
-      }
-      if (save && valid) den_out[row] = dtot;
       if (n + 1 < NT) {
-        // prepare chunk n+1: bf16 S_{n+1}; S and z pre-scaled by its decay;
-        // Q~_{n+1} in place and its row sums against z_{n+1}
+        // prepare chunk n+1. Q~_{n+1} in place first: it needs only the gates
+        // and the finished scores of chunk n+1, so it overlaps this chunk's
+        // state MMAs; the scaled values stay in registers for Q~ . z.
         tc::mbar_wait(&bars[BAR_GATE], (n + 1) & 1, 10);
-        tc::mbar_wait(&bars[BAR_SFDONE], n & 1, 11);
-        tc::tc_fence_after();
+        tc::mbar_wait(&bars[BAR_SFULL], (n + 1) & 1, 15);
         const float start2 = sGS[((n + 1) & 1) * 2], end2 = sGS[((n + 1) & 1) * 2 + 1];
         const float decay = tc::ex2(end2 - start2);
-        const float g2r = sG[r];
-        const float zn = tc::tmem_ld1(trow + kTZ);
-        tc::tmem_wait_ld();
-        if (save) {
-          z_out[((size_t)bh * NT + n + 1) * 128 + r] = zn;
-          // the previous S store must have read the staging block
-          if (r == 0) tc::bulk_wait_read0();
-          tc::named_bar_sync(3, 128);
-        }
+        uint4 qv[8];
         {
-          const bf16 zh = __float2bfloat16_rn(zn);
-          *reinterpret_cast<bf16*>(zblk + 128 + zcol) = zh;
-          *reinterpret_cast<bf16*>(zblk + 256 + zcol2) =
-              __float2bfloat16_rn(zn - __bfloat162float(zh));
+          const bool nvld = r < min(kC, L - r0 - kC);
+          const float qs = nvld ? tc::ex2(sG[r] - start2) : 0.f;
+          unsigned char* nrow = base + ((n + 1) & 1) * kStageBytes + kOffQ + h * 16384 + r * 128;
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            qv[i] = scale8(*reinterpret_cast<const uint4*>(nrow + ((i ^ (r & 7)) * 16)), qs);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<uint4*>(nrow + ((i ^ (r & 7)) * 16)) = qv[i];
         }
-        tc::tmem_st1(trow + kTZ, __float_as_uint(zn * decay));
-#pragma unroll 1
-        for (int hb = 0; hb < 2; ++hb) {
-          float sv[64];
-          tc::tmem_ld64(trow + kTSF + 64 * hb, sv);
+        // then the state: the fp32 z entering chunk n+1, bf16 S_{n+1}; S and z
+        // pre-scaled by its decay
+        tc::mbar_wait(&bars[BAR_SFDONE], n & 1, 11);
+        tc::tc_fence_after();
+        if (h == 0) {
+          const float zn = tc::tmem_ld1(trow + kTZ);
           tc::tmem_wait_ld();
-          unsigned char* srow = srow_base + hb * 16384;
+          if (save) z_out[((size_t)bh * NT + n + 1) * 128 + r] = zn;
+          sZ[r] = zn;
+          tc::tmem_st1(trow + kTZ, __float_as_uint(zn * decay));
+        }
+        // the previous S store must have read the staging block (training);
+        // every z is in sZ, and every reader of the last Q~ . z halves is done
+        if (save && et == 0) tc::bulk_wait_read0();
+        tc::named_bar_sync(3, kGroup);
+        {
+          float sv[64];
+          tc::tmem_ld64(trow + kTSF + 64 * h, sv);
+          // Q~ . z over this half of row r while the state loads
+          const float4* z4 = reinterpret_cast<const float4*>(sZ + 64 * h);
+          float dqh = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint4 w = qv[i];
+            const float4 za = z4[2 * i], zb = z4[2 * i + 1];
+            dqh += bf16_lo(w.x) * za.x + bf16_hi(w.x) * za.y + bf16_lo(w.y) * za.z +
+                   bf16_hi(w.y) * za.w + bf16_lo(w.z) * zb.x + bf16_hi(w.z) * zb.y +
+                   bf16_lo(w.w) * zb.z + bf16_hi(w.w) * zb.w;
+          }
+          sDQ[h * 128 + r] = dqh;
+          tc::tmem_wait_ld();
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const float* v8 = &sv[8 * c];
@@ -471,47 +530,29 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
           }
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            uint32_t sc[16];
+            uint32_t scl[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) sc[j] = __float_as_uint(sv[16 * q + j] * decay);
-            tc::tmem_st16(trow + kTSF + 64 * hb + 16 * q, sc);
+            for (int j = 0; j < 16; ++j) scl[j] = __float_as_uint(sv[16 * q + j] * decay);
+            tc::tmem_st16(trow + kTSF + 64 * h + 16 * q, scl);
           }
         }
         if (save) {  // bf16 S_{n+1} to HBM for the backward, from the operand block
           tc::fence_proxy_async_smem();
-          tc::named_bar_sync(3, 128);
-          if (r == 0) {
+          tc::named_bar_sync(5, kGroup);
+          if (et == 0) {
             tc::tma_store_3d(&ts, base + kOffS, 0, (n + 1) * kC, bh);
             tc::tma_store_3d(&ts, base + kOffS + 16384, 64, (n + 1) * kC, bh);
             tc::bulk_commit();
           }
         }
-        {
-          const bool nvld = r < min(kC, L - r0 - kC);
-          const float qs = nvld ? tc::ex2(g2r - start2) : 0.f;
-          unsigned char* stage = base + ((n + 1) & 1) * kStageBytes;
-          uint4 w[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            w[i] = *reinterpret_cast<const uint4*>(stage + kOffQ + (i >> 3) * 16384 + r * 128 +
-                                                   (((i & 7) ^ (r & 7)) * 16));
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            *reinterpret_cast<uint4*>(stage + kOffQ + (i >> 3) * 16384 + r * 128 +
-                                      (((i & 7) ^ (r & 7)) * 16)) = scale8(w[i], qs);
-        }
       }
       tc::fence_proxy_async_smem();
       tc::tmem_wait_st();
       tc::tc_fence_before();
+      tc::named_bar_sync(4, kGroup);  // the Q~ . z halves of the next chunk are in sDQ
       tc::mbar_arrive(&bars[BAR_SREADY]);
-      if (r == 0) {  // the y staging block is read: hand the stage back to TMA
-        tc::bulk_wait_read0();
-        tc::mbar_arrive(&bars[BAR_EMPTY0 + (n & 1)]);
-      }
-      __syncwarp();
     }
-    if (r == 0) tc::bulk_wait0();  // output stores complete before the CTA exits
+    if (save && et == 0) tc::bulk_wait0();  // state stores complete before the CTA exits
   }
   tc::tc_fence_before();
   __syncthreads();

@@ -4,6 +4,7 @@ The shared library is built in-tree by lizard-reproduction_b200/csrc/build.py.
 There is no fallback: if the library is missing or its ABI revision differs,
 every call raises.
 """
+import contextlib
 import ctypes
 import threading
 from pathlib import Path
@@ -150,11 +151,20 @@ def set_schedule(name):
 
 
 def ptr(t):
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    """Device address of a tensor as a plain int (ctypes passes it as void*)."""
+    return None if t is None else t.data_ptr()
 
 
 def stream_of(t):
-    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def on_device(device):
+    """Make `device` current for a library call; a no-op when it already is,
+    which saves the device switch on every call of the common single-GPU case."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def require_cuda(*tensors):

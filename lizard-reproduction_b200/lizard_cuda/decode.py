@@ -41,7 +41,7 @@ def gla_state(fk, v, log_gamma):
                      dtype=torch.uint8)
     summary = torch.empty(lib.lz_gla_seg_summary_floats(B, Hs, F, D), device=fk.device,
                           dtype=torch.float32)
-    with torch.cuda.device(fk.device):
+    with _lib.on_device(fk.device):
         rc = lib.lz_gla_seg_fwd_begin(_lib.ptr(fk16), _lib.ptr(v16), _lib.ptr(lg), per_head,
                                       _lib.ptr(summary), _lib.ptr(ws), ws.numel(), B, Hs, L, F,
                                       D, _lib.stream_of(fk))

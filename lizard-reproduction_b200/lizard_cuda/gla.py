@@ -54,7 +54,7 @@ class _GLA(torch.autograd.Function):
         wbytes = lib.lz_gla_fwd_gqa_workspace_bytes(B, H, Hkv, L, F, D, chunk, per_head,
                                                     int(save))
         ws = torch.empty(wbytes, device=v.device, dtype=torch.uint8) if wbytes else None
-        with torch.cuda.device(v.device):
+        with _lib.on_device(v.device):
             rc = lib.lz_gla_fwd_gqa(_lib.ptr(fq), _lib.ptr(fk), _lib.ptr(v), _lib.ptr(lg),
                                     per_head, _lib.ptr(y), _lib.ptr(saved),
                                     0 if saved is None else saved.numel(), _lib.ptr(ws), wbytes,
@@ -80,7 +80,7 @@ class _GLA(torch.autograd.Function):
         dlg = torch.empty_like(lg)
         ws = torch.empty(lib.lz_gla_bwd_gqa_workspace_bytes(B, H, Hkv, L, F, D, chunk),
                          device=fq.device, dtype=torch.uint8)
-        with torch.cuda.device(fq.device):
+        with _lib.on_device(fq.device):
             rc = lib.lz_gla_bwd_gqa(_lib.ptr(fq), _lib.ptr(fk), _lib.ptr(v), _lib.ptr(lg),
                                     per_head, _lib.ptr(saved), saved.numel(), _lib.ptr(dy),
                                     _lib.ptr(dfq), _lib.ptr(dfk), _lib.ptr(dv), gdt,

@@ -32,7 +32,7 @@ class _Hedgehog(torch.autograd.Function):
         R = xc.numel() // Dh
         f = torch.empty(*x.shape[:-1], 2 * Fd, device=x.device, dtype=torch.bfloat16)
         xdt = _lib.LZ_DTYPE_BF16 if xc.dtype == torch.bfloat16 else _lib.LZ_DTYPE_F32
-        with torch.cuda.device(x.device):
+        with _lib.on_device(x.device):
             if strided:
                 B, H, L, _ = xc.shape
                 rc = lib.lz_hedgehog_fwd_strided(_lib.ptr(xc), xdt, xc.stride(0), xc.stride(1),
@@ -59,7 +59,7 @@ class _Hedgehog(torch.autograd.Function):
         dw = torch.empty(Fd, Dh, device=xc.device, dtype=torch.float32)
         nws = lib.lz_hedgehog_bwd_workspace_bytes(R, Dh, Fd)
         ws = torch.empty(nws, device=xc.device, dtype=torch.uint8)
-        with torch.cuda.device(xc.device):
+        with _lib.on_device(xc.device):
             if ctx.strided:
                 B, H, L, _ = xc.shape
                 rc = lib.lz_hedgehog_bwd_strided(_lib.ptr(xc), ctx.xdt, xc.stride(0),

@@ -20,6 +20,14 @@ upcast: every kernel converts its inputs to fp32 itself, so the values are the
 same, and the upcast copies are skipped. With autograd on, the upcast stays, so
 the gradients of q and k add in fp32 as in the reference. The projections and
 the gate are the same torch operations as the reference.
+
+Sequence parallelism: forward(..., seq_comm=comm) runs the layer on this
+rank's contiguous slice of every sequence (position_embeddings for the slice's
+own positions). The GLA branch hands its chunk state to the later ranks
+(seqpar.gla_seqpar) and the SWA branch takes the previous rank's last
+window - 1 keys and values as a halo (seqpar.swa_seqpar); everything else in
+the layer is per token. Parameter gradients are this rank's share, summed over
+the group by the caller as for any replicated parameter.
 """
 import torch
 import torch.nn as nn
@@ -30,6 +38,7 @@ from .decode import LayerCache, gla_decode, gla_state, swa_decode, swa_ring
 from .gla import gla
 from .hedgehog import hedgehog as fused_hedgehog
 from .rope import swa_rope
+from .seqpar import gla_seqpar, swa_seqpar
 
 BACKENDS = ("cuda",)
 
@@ -93,11 +102,16 @@ class LizardAttention(nn.Module):
         b, n, _ = x.shape
         return x.view(b, n, heads, self.head_dim).transpose(1, 2)
 
-    def forward(self, hidden_states, position_embeddings, lizard_cache=None, **kwargs):
+    def forward(self, hidden_states, position_embeddings, lizard_cache=None, seq_comm=None,
+                **kwargs):
         """(out, None) as the reference layer. With `lizard_cache` (a
         decode.LizardCache), a layer whose index is in the cache decodes its
         tokens one at a time against the stored state; otherwise it runs the
-        full forward and, given a cache, stores its state there."""
+        full forward and, given a cache, stores its state there. With
+        `seq_comm` (a seqpar.DistExchange, or any object with rank, size and
+        all_gather) hidden_states is this rank's slice of the sequence."""
+        if seq_comm is not None and lizard_cache is not None:
+            raise ValueError("a sequence-parallel forward does not fill a decode cache")
         if lizard_cache is not None and self.layer_idx in lizard_cache:
             return self.decode(hidden_states, position_embeddings,
                                lizard_cache[self.layer_idx]), None
@@ -116,8 +130,11 @@ class LizardAttention(nn.Module):
         alpha = self.param_as(self.alpha_blend, dtype)
         meta = self.param_as(self.meta_tokens, dtype)
         lg = F.logsigmoid(z)
-        y_gla = gla(fq, fk, v, lg)
-        y_swa = swa_rope(q, k, v, cos, sin, meta, self.window)
+        if seq_comm is not None:
+            y_gla, y_swa = self._seqpar_branches(q, k, v, fq, fk, lg, cos, sin, meta, seq_comm)
+        else:
+            y_gla = gla(fq, fk, v, lg)
+            y_swa = swa_rope(q, k, v, cos, sin, meta, self.window)
         if lizard_cache is not None:
             with torch.no_grad():
                 state, zstate = gla_state(fk, v, lg)  # Hkv states: the gate is per token
@@ -125,6 +142,26 @@ class LizardAttention(nn.Module):
                 pos = torch.full((x.shape[0],), x.shape[1], dtype=torch.int32, device=x.device)
                 lizard_cache[self.layer_idx] = LayerCache(state, zstate, k_ring, v_ring, pos)
         return self.o_proj(blend(y_gla, y_swa, alpha, x.dtype)), None
+
+    def _seqpar_branches(self, q, k, v, fq, fk, lg, cos, sin, meta, comm):
+        """Both attention branches on this rank's slice of the sequence. The
+        sequence-parallel GLA takes keys / values at the query head count, so
+        the grouped fk and v are repeated here, as the reference's caller does
+        (src/lizard_attention.py:73-76); q and k are rotated in fp32 with the
+        slice's own positions, as the reference's apply_rotary_pos_emb
+        (src/lizard_attention.py:87-88), and the SWA halo carries rotated keys."""
+        rep = self.heads // self.kv_heads
+        fk_r = fk.repeat_interleave(rep, dim=1) if rep > 1 else fk
+        v_r = v.repeat_interleave(rep, dim=1) if rep > 1 else v
+        y_gla = gla_seqpar(fq, fk_r, v_r, lg, comm=comm)
+        c, s_ = cos.float()[:, None], sin.float()[:, None]
+        half = self.head_dim // 2
+
+        def rot(x):
+            x = x.float()
+            return x * c + torch.cat([-x[..., half:], x[..., :half]], dim=-1) * s_
+        y_swa = swa_seqpar(rot(q), rot(k), v, meta, self.window, comm=comm)
+        return y_gla, y_swa
 
     @torch.no_grad()
     def decode(self, hidden_states, position_embeddings, cache):

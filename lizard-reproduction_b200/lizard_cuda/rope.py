@@ -148,7 +148,7 @@ class _SWARope(torch.autograd.Function):
                                 dtype=torch.uint8)
             rot = tuple(torch.empty(B, n, L, D, device=q.device, dtype=torch.bfloat16)
                         for n in (H, H, Hkv, Hkv))
-        with torch.cuda.device(q.device):
+        with _lib.on_device(q.device):
             if not _fused_forward(q, k, v, cos, sin, csb, csl, meta32, int(window), y, saved,
                                   rot):
                 rot = _two_pass_forward(q, k, v, cos, sin, csb, csl, meta32, int(window), y,
@@ -172,10 +172,10 @@ class _SWARope(torch.autograd.Function):
         dqr = torch.empty(B, H, L, D, device=dy.device, dtype=torch.float32)
         dkr = torch.empty(B, Hkv, L, D, device=dy.device, dtype=torch.float32)
         dv = torch.empty_like(dkr)
-        dmeta = torch.zeros(n_meta, device=dy.device, dtype=torch.float32)
+        dmeta = torch.empty(n_meta, device=dy.device, dtype=torch.float32)
         ws = torch.empty(lib.lz_swa_bwd_workspace_bytes(B, H, L, D, n_meta), device=dy.device,
                          dtype=torch.uint8)
-        with torch.cuda.device(dy.device):
+        with _lib.on_device(dy.device):
             rc = lib.lz_swa_bwd_gqa(_lib.ptr(q_hi), _lib.ptr(k_hi), _lib.ptr(v16),
                                     _lib.ptr(q_lo), _lib.ptr(k_lo),
                                     _lib.ptr(meta32) if n_meta else None, n_meta, ctx.window,

@@ -36,9 +36,12 @@ class DistExchange:
         self.size = dist.get_world_size(group)
 
     def all_gather(self, t):
-        parts = [torch.empty_like(t) for _ in range(self.size)]
-        self.dist.all_gather(parts, t.contiguous(), group=self.group)
-        return torch.stack(parts)
+        """[size, *t.shape]: every rank's t, gathered straight into one buffer
+        (no per-rank tensors and no stacking copy)."""
+        flat = t.contiguous().reshape(-1)
+        out = torch.empty(self.size * flat.numel(), dtype=t.dtype, device=t.device)
+        self.dist.all_gather_into_tensor(out, flat, group=self.group)
+        return out.view(self.size, *t.shape)
 
 
 class CudaSegmentOps:
@@ -54,7 +57,7 @@ class CudaSegmentOps:
         self.ws = torch.empty(nbytes, device=device, dtype=torch.uint8)
 
     def _call(self, name, *args):
-        with torch.cuda.device(self.device):
+        with _lib.on_device(self.device):
             rc = getattr(self.lib, name)(*args)
         _lib.check(rc, name)
 
@@ -184,3 +187,84 @@ def gla_seqpar(fq, fk, v, log_gamma, group=None, comm=None, ops=None):
         _lib.require_cuda(fq, fk, v, log_gamma)
         ops = CudaSegmentOps(B, H, L, F, D, per_head, fq.device)
     return _GLASeq.apply(fq, fk, v, log_gamma, comm, ops)
+
+
+class _SWASeq(torch.autograd.Function):
+    """Sliding-window attention of one sequence split over the ranks of `comm`.
+
+    A query sees the keys of the W - 1 positions before it (the reference's key
+    loop starts W - 1 rows before the query block, src/kernels/swa.py:40-41), so
+    rank r needs the last W - 1 rows of k and v of rank r - 1: its halo. Every
+    rank all-gathers its tail once (forward) and every halo gradient once
+    (backward), so all ranks make the same collective calls. The rank's own
+    slice runs as one plain call; its first W - 1 outputs, which lack the halo,
+    are replaced by a second call over [halo, first W - 1 rows] whose halo
+    positions carry zero queries and zero output gradients (they add nothing to
+    any gradient). The key/value gradient of the halo goes back to the rank that
+    sent it and is added to its last W - 1 rows.
+    """
+
+    @staticmethod
+    def forward(ctx, q, k, v, meta, window, comm, attn):
+        h = int(window) - 1
+        Ls = q.shape[2]
+        if h > Ls:
+            raise ValueError(f"swa_seqpar needs at least window - 1 = {h} positions per rank, "
+                             f"this rank has {Ls}")
+        rank = comm.rank
+        tails = comm.all_gather(torch.stack([k[:, :, Ls - h:], v[:, :, Ls - h:]])) if h else None
+        with torch.enable_grad():
+            leaves = [t.detach().requires_grad_(t.requires_grad or t.is_floating_point())
+                      for t in (q, k, v, meta)]
+            lq, lk, lv, lm = leaves
+            y = attn(lq, lk, lv, lm, window)
+            halo = None
+            if rank > 0 and h:
+                halo = tails[rank - 1].detach().requires_grad_()
+                zq = torch.zeros_like(lq[:, :, :h])
+                ys = attn(torch.cat([zq, lq[:, :, :h]], 2), torch.cat([halo[0], lk[:, :, :h]], 2),
+                          torch.cat([halo[1], lv[:, :, :h]], 2), lm, window)[:, :, h:]
+                y = torch.cat([ys, y[:, :, h:]], 2)
+        ctx.inner = (y, leaves, halo)
+        ctx.h, ctx.comm = h, comm
+        return y.detach()
+
+    @staticmethod
+    def backward(ctx, dy):
+        y, leaves, halo = ctx.inner
+        h, comm = ctx.h, ctx.comm
+        inputs = leaves + ([halo] if halo is not None else [])
+        grads = list(torch.autograd.grad(y, inputs, dy, allow_unused=True))
+        for i, t in enumerate(inputs):
+            if grads[i] is None:
+                grads[i] = torch.zeros_like(t)
+        if h:
+            dhalo = grads.pop() if halo is not None else None
+            k = leaves[1]
+            send = dhalo if dhalo is not None else torch.zeros(
+                (2,) + tuple(k.shape[:2]) + (h, k.shape[-1]), dtype=grads[1].dtype,
+                device=k.device)
+            back = comm.all_gather(send.to(grads[1].dtype))
+            if comm.rank + 1 < comm.size:  # the next rank's halo is this rank's tail
+                Ls = k.shape[2]
+                grads[1][:, :, Ls - h:] += back[comm.rank + 1][0].to(grads[1].dtype)
+                grads[2][:, :, Ls - h:] += back[comm.rank + 1][1].to(grads[2].dtype)
+        ctx.inner = None
+        return grads[0], grads[1], grads[2], grads[3], None, None, None
+
+
+def swa_seqpar(q, k, v, meta, window, group=None, comm=None, attn=None):
+    """swa() of one sequence split over the ranks of `group` (default: the world).
+
+    q [B, H, Ls, D], k, v [B, Hkv, Ls, D] (rotated, as swa() takes them) are this
+    rank's contiguous slice (rank order = sequence order, every slice at least
+    window - 1 long); meta [n_meta] is shared. Returns this rank's slice of y.
+    Gradients flow to q, k, v and meta; meta's gradient is this rank's share,
+    to be summed over the group like any replicated parameter's. `attn` is the
+    attention call (default lizard_cuda.swa); `comm` as in gla_seqpar.
+    """
+    if comm is None:
+        comm = DistExchange(group)
+    if attn is None:
+        from .swa import swa as attn
+    return _SWASeq.apply(q, k, v, meta, int(window), comm, attn)

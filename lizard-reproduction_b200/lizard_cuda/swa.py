@@ -54,7 +54,7 @@ class _SWA(torch.autograd.Function):
         if save:
             saved = torch.empty(lib.lz_swa_saved_bytes(B, H, L, D), device=q.device,
                                 dtype=torch.uint8)
-        with torch.cuda.device(q.device):
+        with _lib.on_device(q.device):
             rc = lib.lz_swa_fwd_gqa(_lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(q_lo),
                                     _lib.ptr(k_lo), _lib.ptr(meta) if n_meta else None,
                                     n_meta, int(window), _lib.ptr(y), _lib.ptr(saved),
@@ -80,10 +80,10 @@ class _SWA(torch.autograd.Function):
         dq = torch.empty(B, H, L, D, device=q.device, dtype=gtorch)
         dk = torch.empty(B, Hkv, L, D, device=q.device, dtype=gtorch)
         dv = torch.empty_like(dk)
-        dmeta = torch.zeros(n_meta, device=q.device, dtype=torch.float32)
+        dmeta = torch.empty(n_meta, device=q.device, dtype=torch.float32)
         ws = torch.empty(lib.lz_swa_bwd_workspace_bytes(B, H, L, D, n_meta), device=q.device,
                          dtype=torch.uint8)
-        with torch.cuda.device(q.device):
+        with _lib.on_device(q.device):
             rc = lib.lz_swa_bwd_gqa(_lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(q_lo),
                                     _lib.ptr(k_lo), _lib.ptr(meta) if n_meta else None,
                                     n_meta, ctx.window, _lib.ptr(saved), saved.numel(),

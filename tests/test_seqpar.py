@@ -96,3 +96,82 @@ def test_seqpar_matches_unsharded_oracle(bounds, per_head):
             p.kill()
             errs.append("a rank did not finish in 180 s")
     assert not errs and all(p.exitcode == 0 for p in procs), errs
+
+
+def _swa_worker(rank, world, port, bounds, window, heads, kv_heads, errq):
+    import sys
+    for p in (ROOT, ROOT / "lizard-reproduction_b200", ROOT / "oracle", ROOT / "tests"):
+        sys.path.insert(0, str(p))
+    try:
+        import torch.distributed as dist
+        import lizard_oracle as orc
+        from lizard_cuda import seqpar
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=__import__("datetime").timedelta(seconds=60))
+        B, D, L = 2, 8, bounds[-1]
+        g = torch.Generator().manual_seed(3)
+        q = torch.randn(B, heads, L, D, generator=g, dtype=torch.float64)
+        k = torch.randn(B, kv_heads, L, D, generator=g, dtype=torch.float64)
+        v = torch.randn(B, kv_heads, L, D, generator=g, dtype=torch.float64)
+        meta = torch.randn(3, generator=g, dtype=torch.float64)
+        dy = torch.randn(B, heads, L, D, generator=g, dtype=torch.float64)
+        rep = heads // kv_heads
+
+        def attn(q_, k_, v_, m_, w_):  # the float64 oracle with grouped keys / values
+            return orc.awa(q_, k_.repeat_interleave(rep, 1), v_.repeat_interleave(rep, 1), m_, w_)
+
+        a, b = bounds[rank], bounds[rank + 1]
+        leaves = [t[:, :, a:b].clone().requires_grad_() for t in (q, k, v)]
+        lm = meta.clone().requires_grad_()
+        y = seqpar.swa_seqpar(*leaves, lm, window, attn=attn)
+        y.backward(dy[:, :, a:b])
+        dist.all_reduce(lm.grad)  # meta is shared: its gradient is the sum over ranks
+        ref_leaves = [t.clone().requires_grad_() for t in (q, k, v, meta)]
+        ref = attn(*ref_leaves, window)
+        ref.backward(dy)
+        checks = [("y", y, ref.detach()[:, :, a:b])] + [
+            (n, lf.grad, r.grad[:, :, a:b]) for n, lf, r in zip(("dq", "dk", "dv"), leaves,
+                                                              ref_leaves)] + [
+            ("dmeta", lm.grad, ref_leaves[3].grad)]
+        for n, got, want in checks:
+            err = (got - want).abs().max().item() / want.abs().max().item()
+            if not err < 1e-10:
+                raise AssertionError(f"rank {rank}: {n} max rel err {err:.3e}")
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as e:  # report to the parent, then fail this process
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+@pytest.mark.parametrize("bounds,window,heads,kv_heads", [
+    ((0, 40, 80), 16, 2, 2),          # 2 ranks, halo of 15 rows
+    ((0, 30, 51, 90), 21, 4, 2),      # 3 ranks, unequal slices, a slice as long as the halo,
+                                      # grouped keys / values
+    ((0, 25, 50), 1, 2, 1),           # window 1: no halo
+])
+def test_swa_seqpar_halo_matches_unsharded_oracle(bounds, window, heads, kv_heads):
+    """Sliding-window attention with each rank holding a slice of the sequence:
+    the last window - 1 keys / values of the previous rank arrive as a halo
+    (and their gradients go back); every rank's slice of y and of dq, dk, dv,
+    and the summed dmeta equal the unsharded float64 oracle."""
+    world = len(bounds) - 1
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_swa_worker,
+                         args=(r, world, port, bounds, window, heads, kv_heads, errq))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            errs.append("a rank did not finish in 180 s")
+    assert not errs and all(p.exitcode == 0 for p in procs), errs
