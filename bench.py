@@ -293,13 +293,29 @@ def seqpar_measure(torch, lizard_cuda, device, dist, world, rank, steps=10, warm
     if world > 1:
         check = seqpar_check(torch, lizard_cuda, dist, world, rank,
                              (fq, fk, v, lg, dy), [t.grad for t in leaves])
+    # the same forward+backward replayed from one CUDA graph (the collectives
+    # inside it): the device time of the sharded step without the host's
+    # per-call work, captured and replayed by every rank in the same order
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    both_graph = timed(graph.replay)
+    del graph
     return {"workload": f"gla config 4 long sequence: B=1 L={SEQ_L} H={SEQ_H} F=D={SEQ_FD}, "
                         f"per-head gate, {world} rank(s) x {Ls} tokens",
             "check": check,
             "exchange": "none" if world == 1 else "one NCCL all_gather of the chunk-state "
                                                   "summaries per direction",
             "fwd_ms": fwd, "fwd_tokens_per_s": SEQ_L / (fwd / 1e3),
-            "fwd_bwd_ms": both, "fwd_bwd_tokens_per_s": SEQ_L / (both / 1e3)}
+            "fwd_bwd_ms": both, "fwd_bwd_tokens_per_s": SEQ_L / (both / 1e3),
+            "fwd_bwd_ms_graph": both_graph,
+            "fwd_bwd_tokens_per_s_graph": SEQ_L / (both_graph / 1e3)}
 
 
 SEQ_CHECK_HEADS = (0, 17)

@@ -63,6 +63,19 @@ uint64_t lz_launch_count(void);
  * (0 = no wait ever timed out). Synchronous. */
 int lz_device_timeout_flag(unsigned int* site);
 
+/* Clears that flag on the current device, after the caller has read and
+ * handled a timeout: until it is cleared, the waits of the affected kernels
+ * return at once. No counterpart in the reference (its Triton kernels have no
+ * bounded waits). Synchronous. */
+int lz_device_timeout_clear(void);
+
+/* Test switch for the bounded-wait path on the current device (no counterpart
+ * in the reference): with on != 0, lz_swa_decode arms the barrier of its
+ * ring-buffer copy but issues no copy, so the wait runs out after about 2 s,
+ * lz_device_timeout_flag reports the site, and the call writes nothing. Off by
+ * default; leave it off outside tests. */
+int lz_test_withhold_decode_ring_copy(int on);
+
 /* ------------------------------------------------------------------------ */
 /* GLA                                                                      */
 /* ------------------------------------------------------------------------ */

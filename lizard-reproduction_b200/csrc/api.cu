@@ -27,6 +27,13 @@ int hedgehog_timeout_flag(unsigned int* out);
 int swa_timeout_flag(unsigned int* out);
 int swa_tc_timeout_flag(unsigned int* out);
 int decode_timeout_flag(unsigned int* out);
+int gla_fwd_tc_timeout_clear();
+int gla_bwd_tc_timeout_clear();
+int gla_out_tc_timeout_clear();
+int hedgehog_timeout_clear();
+int swa_timeout_clear();
+int swa_tc_timeout_clear();
+int decode_timeout_clear();
 }  // namespace lz
 
 extern "C" int lz_device_timeout_flag(unsigned int* site) {
@@ -45,6 +52,19 @@ extern "C" int lz_device_timeout_flag(unsigned int* site) {
       *site = v;
       break;
     }
+  }
+  return LZ_OK;
+}
+
+extern "C" int lz_device_timeout_clear(void) {
+  lz::clear_error();
+  int (*const clearers[])() = {
+      lz::gla_fwd_tc_timeout_clear, lz::gla_bwd_tc_timeout_clear, lz::gla_out_tc_timeout_clear,
+      lz::hedgehog_timeout_clear,   lz::swa_timeout_clear,        lz::swa_tc_timeout_clear,
+      lz::decode_timeout_clear};
+  for (auto cl : clearers) {
+    const int rc = cl();
+    if (rc) return rc;
   }
   return LZ_OK;
 }

@@ -27,6 +27,13 @@
 namespace lz {
 namespace {
 
+// Test switch of the failure-detection path: when set, the SWA decode kernel
+// arms its ring-copy barrier but issues no copy, so its bounded wait runs out,
+// records its site in the timeout flag, and every CTA returns without writing
+// (no copy is in flight, nothing else waits on it). Off unless a test sets it
+// through lz_test_withhold_decode_ring_copy.
+static __device__ int g_withhold_ring_copy;
+
 constexpr int kT = 256;
 
 // One CTA per (batch row, state head). CG = D / 4 column groups of 4, RG = 256
@@ -190,8 +197,10 @@ swa_decode_kernel(const XT* __restrict__ q, long long q_sb, long long q_sh,
     if (tid == 0) {
       const uint32_t bytes = (uint32_t)W * D * 4;
       tc::mbar_expect_tx(bar, 2 * bytes);
-      tc::bulk_load(sKr, kring, bytes, bar);
-      tc::bulk_load(sVr, vring, bytes, bar);
+      if (!g_withhold_ring_copy) {
+        tc::bulk_load(sKr, kring, bytes, bar);
+        tc::bulk_load(sVr, vring, bytes, bar);
+      }
     }
   }
   // the group's rotated queries (while the copy is in flight)
@@ -370,8 +379,20 @@ int launch_swa_decode(const void* q, long long q_sb, long long q_sh, const void*
 
 }  // namespace
 int decode_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
+int decode_timeout_clear() { return tc::clear_timeout_flag_here(); }
 
 }  // namespace lz
+
+extern "C" int lz_test_withhold_decode_ring_copy(int on) {
+  lz::clear_error();
+  const int v = on ? 1 : 0;
+  cudaError_t e = cudaMemcpyToSymbol(lz::g_withhold_ring_copy, &v, sizeof(v));
+  if (e != cudaSuccess) {
+    lz::set_error(std::string("cudaMemcpyToSymbol: ") + cudaGetErrorString(e));
+    return LZ_ERR_CUDA;
+  }
+  return LZ_OK;
+}
 
 extern "C" int lz_gla_decode(const void* fq, const void* fk, const void* v,
                              const float* log_gamma, int gate_per_head, float* state,

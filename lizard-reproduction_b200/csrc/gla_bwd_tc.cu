@@ -767,5 +767,6 @@ int gla_bwd_tc_chunks(const bf16* fq, const bf16* fk, const bf16* v, const bf16*
 }
 
 int gla_bwd_tc_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
+int gla_bwd_tc_timeout_clear() { return tc::clear_timeout_flag_here(); }
 
 }  // namespace lz

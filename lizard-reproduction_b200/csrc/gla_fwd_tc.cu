@@ -628,5 +628,6 @@ int gla_fwd_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
 }
 
 int gla_fwd_tc_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
+int gla_fwd_tc_timeout_clear() { return tc::clear_timeout_flag_here(); }
 
 }  // namespace lz

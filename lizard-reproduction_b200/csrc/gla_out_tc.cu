@@ -1,7 +1,7 @@
 // Chunk outputs of the chunk-parallel GLA schedule on the 5th-generation
-// tensor cores (tcgen05 + TMEM + TMA), for F in {128, 256} with D = 64, and
-// F = D = 128. In training it also writes what the backward reads: y in fp32,
-// the row sums and the running log gate G.
+// tensor cores (tcgen05 + TMEM + TMA), for F in {128, 256} with D = 64,
+// F = D = 128 and F = D = 64 (config 3's shape). In training it also writes
+// what the backward reads: y in fp32, the row sums and the running log gate G.
 //
 // After the increments and the scan (gla_split.cu) every chunk's entering state
 // S_n (bf16) and normaliser z_n (fp32) are in HBM, so the chunks are
@@ -688,9 +688,13 @@ int gla_out_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
   if (F == 128 && D == 128)
     return launch_out_tc<128, 128>(fq, fk, v, lg, gph, B, H, Hkv, sgrp, L, NT64, s_in, z_in, y,
                                    sv, gs, st);
+  if (F == 64 && D == 64)
+    return launch_out_tc<64, 64>(fq, fk, v, lg, gph, B, H, Hkv, sgrp, L, NT64, s_in, z_in, y, sv,
+                                 gs, st);
   return LZ_ERR_UNSUPPORTED;
 }
 
 int gla_out_tc_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
+int gla_out_tc_timeout_clear() { return tc::clear_timeout_flag_here(); }
 
 }  // namespace lz

@@ -1085,6 +1085,7 @@ int hedgehog_bwd(const void* x, int x_dtype, const XRows& xm, const float* w, co
 }
 
 int hedgehog_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
+int hedgehog_timeout_clear() { return tc::clear_timeout_flag_here(); }
 
 }  // namespace lz
 

@@ -1084,5 +1084,6 @@ int swa_bwd(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const b
 }
 
 int swa_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
+int swa_timeout_clear() { return tc::clear_timeout_flag_here(); }
 
 }  // namespace lz

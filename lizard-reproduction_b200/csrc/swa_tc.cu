@@ -1752,6 +1752,7 @@ int swa_bwd_dq_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, c
 }
 
 int swa_tc_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
+int swa_tc_timeout_clear() { return tc::clear_timeout_flag_here(); }
 
 }  // namespace lz
 

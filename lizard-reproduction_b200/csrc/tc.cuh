@@ -40,6 +40,18 @@ static __device__ unsigned int g_timeout_flag;
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// Host side: clear this translation unit's copy of the flag, so its kernels
+// wait again after a timeout has been reported.
+static inline int clear_timeout_flag_here() {
+  const unsigned int zero = 0;
+  cudaError_t e = cudaMemcpyToSymbol(g_timeout_flag, &zero, sizeof(zero));
+  if (e != cudaSuccess) {
+    set_error(std::string("cudaMemcpyToSymbol: ") + cudaGetErrorString(e));
+    return LZ_ERR_CUDA;
+  }
+  return LZ_OK;
+}
+
 // Host side: this translation unit's copy of the flag (the flag is static, so
 // every unit that includes this header has its own; each unit exports a
 // reader lz::<unit>_timeout_flag and the C ABI reports the first one set).

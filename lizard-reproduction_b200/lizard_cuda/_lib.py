@@ -25,6 +25,8 @@ _SIGNATURES = {
     "lz_last_error_string": (ctypes.c_char_p, []),
     "lz_launch_count": (ctypes.c_uint64, []),
     "lz_device_timeout_flag": (_c_int, [ctypes.POINTER(ctypes.c_uint)]),
+    "lz_device_timeout_clear": (_c_int, []),
+    "lz_test_withhold_decode_ring_copy": (_c_int, [_c_int]),
     "lz_gla_saved_bytes": (_c_size, [_c_int] * 6),
     "lz_gla_bwd_workspace_bytes": (_c_size, [_c_int] * 6),
     "lz_gla_fwd_workspace_bytes": (_c_size, [_c_int] * 6),
@@ -137,6 +139,11 @@ def device_timeout_flag():
     out = ctypes.c_uint(0)
     check(load().lz_device_timeout_flag(ctypes.byref(out)), "timeout flag query")
     return int(out.value)
+
+
+def clear_device_timeout_flag():
+    """Clear the current device's timeout flag once a timeout has been handled."""
+    check(load().lz_device_timeout_clear(), "timeout flag clear")
 
 
 SCHEDULES = {"auto": 0, "walk": 1, "split": 2}
