@@ -674,6 +674,17 @@ int gla_bwd_tail(const bf16* fq, const bf16* fk, const bf16* v, int gph, const G
                  int ds_seeded, cudaStream_t stream) {
   const int BH = B * H, grp = H / Hkv;
   const int NT = (int)gla_nt(L);
+  // F = D = 64: per-chunk gradients on the tensor cores over 128-token chunks,
+  // reading the scan's 64-token states at stride two (gla_bwd_tc.cu)
+  if (F == 64 && D == 64 && gla_split_out_tc_enabled() && aligned16(fq) && aligned16(fk) &&
+      aligned16(v) && aligned16(dy) && aligned16(sv.s) && aligned16(wk.ds) &&
+      (gdt != LZ_DTYPE_BF16 || aligned16(dfq)) &&
+      (gdt_kv != LZ_DTYPE_BF16 || (aligned16(dfk) && aligned16(dv)))) {
+    int rc = gla_bwd_tc_chunks(fq, fk, v, dy, sv, wk, dfq, dfk, dv, gdt, gdt_kv, B, H, Hkv, L,
+                               s_seeded, ds_seeded, stream, true);
+    if (rc) return rc;
+    return launch_gate(wk.dg, wk.dgt, dlg, B, H, L, (L + 127) / 128, 128, gph, stream);
+  }
   const int vec_f = (F % 8 == 0) && aligned16(fq) && aligned16(fk);
   const int vec_d = (D % 8 == 0) && aligned16(v) && aligned16(dy) && aligned16(sv.s) &&
                     aligned16(wk.ds);

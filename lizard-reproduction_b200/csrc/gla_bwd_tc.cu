@@ -330,6 +330,16 @@ constexpr uint32_t kTS = 0, kTP = 128, kTDV = 256, kT5 = 384, kT2Cols = 512;
 enum { B2_FULL = 0, B2_SPFULL, B2_EWDONE, B2_P3DONE, B2_T12FREE, B2_DSFULL, B2_P4DONE, B2_DGA,
        B2_COUNT };
 
+// NARROW: F = D = 64 on the chunk-parallel schedule's 64-token states. The
+// 64-column tiles are read as the first box of a 128-wide tile whose second box
+// TMA fills with zeros (coordinates past the tensor's width), and the state and
+// its gradient as 64 x 64 boxes into the first box of a tile whose other rows
+// and columns the row threads zero: every product then runs on zero-padded
+// 128-wide operands, the padded features and values add nothing, and only the
+// first 64 columns of each gradient are written. The state entering 128-token
+// chunk n is the scan's state 2n, the gradient leaving it the scan's gradient
+// 2n + 1 (the last one for an odd tail), and the K-loops over F or D stop at 64.
+template <bool NARROW>
 __global__ void __launch_bounds__(kThreads, 1)
 gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv,
@@ -364,6 +374,15 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
   const int kvh = kv_head(bh, H, grp);  // head of fk and v (GQA)
   const int r0 = n * kC, nvalid = min(kC, L - r0);
   const size_t rowb = (size_t)bh * L, chunk = (size_t)bh * NT + n;
+  constexpr int kW = NARROW ? 64 : 128;   // columns of fq, fk, v, dy and the gradients
+  constexpr int kKs = NARROW ? 4 : 8;     // 16-wide K-steps over F or D
+  constexpr int kHB = NARROW ? 1 : 2;     // 64-column blocks holding data
+  // rows of the 64-token scan states (NARROW): entering = 2n, leaving = 2n + 1
+  const int NTs = (L + 63) / 64;
+  const int s_row = NARROW ? 2 * n * 64 : r0;
+  const int ds_row = NARROW ? min(2 * n + 1, NTs - 1) * 64 : r0;
+  const size_t zchunk = NARROW ? (size_t)bh * NTs + 2 * n : chunk;
+  const size_t dzchunk = NARROW ? (size_t)bh * NTs + min(2 * n + 1, NTs - 1) : chunk;
   const bool with_s = n > 0 || s_seeded;
   const bool with_ds = n + 1 < NT || ds_seeded;
   const bool bf16_out = gdt == LZ_DTYPE_BF16;    // dfq
@@ -399,7 +418,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
     // ---------------------------------------------------------------- TMA
     if (lane == 0) {
       uint64_t* full = &bars[B2_FULL];
-      tc::mbar_expect_tx(full, (with_s ? 5 : 4) * kTile);
+      tc::mbar_expect_tx(full, 4 * kTile + (with_s ? (NARROW ? 8192 : kTile) : 0));
       tc::tma_load_3d(base + kOQ, &tq, 0, r0, bh, full);
       tc::tma_load_3d(base + kOQ + 16384, &tq, 64, r0, bh, full);
       tc::tma_load_3d(base + kOK, &tk, 0, r0, kvh, full);
@@ -409,8 +428,8 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
       tc::tma_load_3d(base + kODY, &tdy, 0, r0, bh, full);
       tc::tma_load_3d(base + kODY + 16384, &tdy, 64, r0, bh, full);
       if (with_s) {
-        tc::tma_load_3d(base + kOX, &ts, 0, r0, bh, full);
-        tc::tma_load_3d(base + kOX + 16384, &ts, 64, r0, bh, full);
+        tc::tma_load_3d(base + kOX, &ts, 0, s_row, bh, full);
+        if (!NARROW) tc::tma_load_3d(base + kOX + 16384, &ts, 64, r0, bh, full);
       }
       bool ok = tc::mbar_wait(full, 0, 31);
       if (with_ds && ok) {
@@ -418,9 +437,9 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
         ok = tc::mbar_wait(&bars[B2_P3DONE], 0, 32);
         if (ok) {
           uint64_t* dsf = &bars[B2_DSFULL];
-          tc::mbar_expect_tx(dsf, kTile);
-          tc::tma_load_3d(base + kOX, &tds, 0, r0, bh, dsf);
-          tc::tma_load_3d(base + kOX + 16384, &tds, 64, r0, bh, dsf);
+          tc::mbar_expect_tx(dsf, NARROW ? 8192 : kTile);
+          tc::tma_load_3d(base + kOX, &tds, 0, ds_row, bh, dsf);
+          if (!NARROW) tc::tma_load_3d(base + kOX + 16384, &tds, 64, r0, bh, dsf);
           tc::mbar_wait(dsf, 0, 33);
         }
       }
@@ -438,13 +457,13 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
       bool ok = tc::mbar_wait(&bars[B2_FULL], 0, 34);
       if (ok) {
         tc::tc_fence_after();
-        // phase 1: s = fq fk^T, p = dy v^T
+        // phase 1: s = fq fk^T, p = dy v^T (K = F, D)
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < kKs; ++j)
           tc::mma_ss(tmem + kTS, tc::sdesc(q + ko_kmajor(j), 16, 1024),
                      tc::sdesc(k + ko_kmajor(j), 16, 1024), id_kk, j > 0);
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < kKs; ++j)
           tc::mma_ss(tmem + kTP, tc::sdesc(y + ko_kmajor(j), 16, 1024),
                      tc::sdesc(v + ko_kmajor(j), 16, 1024), id_kk, j > 0);
         tc::mma_commit(&bars[B2_SPFULL]);
@@ -461,9 +480,9 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
         for (int j = 0; j < 8; ++j)
           tc::mma_ss(tmem + kTS, tc::sdesc(dad + ko_kmajor(j), 16, 1024),
                      tc::sdesc(k + 2048 * j, 16384, 1024), id_km, j > 0);
-        if (with_s) {
+        if (with_s) {  // K = D
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
+          for (int j = 0; j < kKs; ++j)
             tc::mma_ss(tmem + kTP, tc::sdesc(y + ko_kmajor(j), 16, 1024),
                        tc::sdesc(x + ko_kmajor(j), 16, 1024), id_kk, j > 0);
         }
@@ -478,13 +497,13 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
         for (int j = 0; j < 8; ++j)
           tc::mma_ss(tmem + kTS, tc::sdesc(dad + 2048 * j, 16384, 1024),
                      tc::sdesc(q + 2048 * j, 16384, 1024), id_mm, j > 0);
-        if (with_ds) {
+        if (with_ds) {  // K = D, then K = F
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
+          for (int j = 0; j < kKs; ++j)
             tc::mma_ss(tmem + kTP, tc::sdesc(v + ko_kmajor(j), 16, 1024),
                        tc::sdesc(x + ko_kmajor(j), 16, 1024), id_kk, j > 0);
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
+          for (int j = 0; j < kKs; ++j)
             tc::mma_ss(tmem + kT5, tc::sdesc(k + ko_kmajor(j), 16, 1024),
                        tc::sdesc(x + 2048 * j, 16384, 1024), id_km, j > 0);
         }
@@ -505,8 +524,16 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
     const float dl = valid ? delta[rowb + r0 + i] : 0.f;
     if (grpA) {
       sG2[i] = g2i;
-      sZ[i] = with_s ? Z[chunk * 128 + i] : 0.f;
-      sDZ[i] = with_ds ? dZ[chunk * 128 + i] : 0.f;
+      sZ[i] = (with_s && i < kW) ? Z[zchunk * kW + i] : 0.f;
+      sDZ[i] = (with_ds && i < kW) ? dZ[dzchunk * kW + i] : 0.f;
+    }
+    if constexpr (NARROW) {
+      // the state / gradient tile holds a 64 x 64 box: zero its other rows
+      // (bytes [8192, 16384)) and its second box (bytes [16384, 32768))
+      const int e = (grpA ? 0 : 128) + i;  // 0..255
+      uint4* zt = reinterpret_cast<uint4*>(base + kOX + 8192);
+#pragma unroll
+      for (int u = 0; u < 6; ++u) zt[e + 256 * u] = make_uint4(0u, 0u, 0u, 0u);
     }
     tc::named_bar_sync(1, 256);
     const float g2end = sG2[nvalid - 1];
@@ -559,7 +586,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
       tc::mbar_wait(&bars[B2_P3DONE], 0, 42);
       tc::tc_fence_after();
 #pragma unroll 1
-      for (int hb = 0; hb < 2; ++hb) {
+      for (int hb = 0; hb < kHB; ++hb) {
         float t1[64], t2[64];
         tc::tmem_ld64(trow + kTS + 64 * hb, t1);
         if (with_s) tc::tmem_ld64(trow + kTP + 64 * hb, t2);
@@ -573,7 +600,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
         if (bf16_out) {
           tile_row_store64(base + kOADEN, i, hb, t1);
         } else if (valid) {
-          float4* o = reinterpret_cast<float4*>(static_cast<float*>(dfq) + (rowb + r0 + i) * 128 +
+          float4* o = reinterpret_cast<float4*>(static_cast<float*>(dfq) + (rowb + r0 + i) * kW +
                                                 64 * hb);
 #pragma unroll
           for (int c = 0; c < 16; ++c)
@@ -589,7 +616,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
         tc::named_bar_sync(2, 128);
         if (i == 0) {
           tc::tma_store_3d(&tdfq, base + kOADEN, 0, r0, bh);
-          tc::tma_store_3d(&tdfq, base + kOADEN + 16384, 64, r0, bh);
+          if (!NARROW) tc::tma_store_3d(&tdfq, base + kOADEN + 16384, 64, r0, bh);
           tc::bulk_commit();
         }
       }
@@ -597,7 +624,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
       tc::mbar_wait(&bars[B2_P4DONE], 0, 44);
       tc::tc_fence_after();
 #pragma unroll 1
-      for (int hb = 0; hb < 2; ++hb) {
+      for (int hb = 0; hb < kHB; ++hb) {
         float dvv[64], t5[64];
         tc::tmem_ld64(trow + kTDV + 64 * hb, dvv);
         if (with_ds) tc::tmem_ld64(trow + kT5 + 64 * hb, t5);
@@ -609,7 +636,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
         if (bf16_kv) {
           tile_row_store64(base + kOX, i, hb, dvv);
         } else if (valid) {
-          float4* o = reinterpret_cast<float4*>(static_cast<float*>(dv) + (rowb + r0 + i) * 128 +
+          float4* o = reinterpret_cast<float4*>(static_cast<float*>(dv) + (rowb + r0 + i) * kW +
                                                 64 * hb);
 #pragma unroll
           for (int c = 0; c < 16; ++c)
@@ -621,7 +648,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
         tc::named_bar_sync(2, 128);
         if (i == 0) {
           tc::tma_store_3d(&tdv, base + kOX, 0, r0, bh);
-          tc::tma_store_3d(&tdv, base + kOX + 16384, 64, r0, bh);
+          if (!NARROW) tc::tma_store_3d(&tdv, base + kOX + 16384, 64, r0, bh);
           tc::bulk_commit();
         }
       }
@@ -632,7 +659,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
       tc::mbar_wait(&bars[B2_P4DONE], 0, 46);
       tc::tc_fence_after();
 #pragma unroll 1
-      for (int hb = 0; hb < 2; ++hb) {
+      for (int hb = 0; hb < kHB; ++hb) {
         float t3[64], t4[64];
         tc::tmem_ld64(trow + kTS + 64 * hb, t3);
         if (with_ds) tc::tmem_ld64(trow + kTP + 64 * hb, t4);
@@ -646,7 +673,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
         if (bf16_kv) {
           tile_row_store64(base + kODAD, i, hb, t3);
         } else if (valid) {
-          float4* o = reinterpret_cast<float4*>(static_cast<float*>(dfk) + (rowb + r0 + i) * 128 +
+          float4* o = reinterpret_cast<float4*>(static_cast<float*>(dfk) + (rowb + r0 + i) * kW +
                                                 64 * hb);
 #pragma unroll
           for (int c = 0; c < 16; ++c)
@@ -658,7 +685,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
         tc::named_bar_sync(3, 128);
         if (i == 0) {
           tc::tma_store_3d(&tdfk, base + kODAD, 0, r0, bh);
-          tc::tma_store_3d(&tdfk, base + kODAD + 16384, 64, r0, bh);
+          if (!NARROW) tc::tma_store_3d(&tdfk, base + kODAD + 16384, 64, r0, bh);
           tc::bulk_commit();
         }
       }
@@ -688,13 +715,15 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
 
 // ------------------------------------------------------------ host helpers
 
-// [BH, rows, 128] bf16 as 3-D {128, rows, BH}, box {64, 128, 1}, 128-byte swizzle
-bool make_map(CUtensorMap* m, const void* ptr, int BH, int rows) {
+// [BH, rows, cols] bf16 as 3-D {cols, rows, BH}, box {64, box_rows, 1}, 128-byte
+// swizzle, zero fill outside (cols 64: a box at column 64 reads zeros)
+bool make_map(CUtensorMap* m, const void* ptr, int BH, int rows, int cols = 128,
+              int box_rows = 128) {
   tc::EncodeTiledFn fn = tc::encode_tiled_fn();
   if (!fn) return false;
-  cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)BH};
-  cuuint64_t strides[2] = {256, (cuuint64_t)rows * 256};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)rows * cols * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -741,27 +770,44 @@ int gla_bwd_tc_states(const bf16* fq, const bf16* dy, const GlaSaved& sv, const 
 int gla_bwd_tc_chunks(const bf16* fq, const bf16* fk, const bf16* v, const bf16* dy,
                       const GlaSaved& sv, const GlaWork& wk, void* dfq, void* dfk, void* dv,
                       int gdt, int gdt_kv, int B, int H, int Hkv, int L, int s_seeded,
-                      int ds_seeded, cudaStream_t stream) {
+                      int ds_seeded, cudaStream_t stream, bool narrow) {
   const int BH = B * H, NT = (L + kC - 1) / kC;
+  // narrow (F = D = 64): 64-column tensors, and the 64-token scan's states and
+  // state gradients [BH, NT64, 64, 64] read as 64 x 64 boxes
+  const int W = narrow ? 64 : 128;
+  const int srows = narrow ? ((L + 63) / 64) * 64 : NT * kC;
+  const int sbox = narrow ? 64 : 128;
   CUtensorMap mq, mk, mv, mdy, ms, mds, mdfq, mdfk, mdv;
-  bool ok = make_map(&mq, fq, BH, L) && make_map(&mk, fk, B * Hkv, L) &&
-            make_map(&mv, v, B * Hkv, L) && make_map(&mdy, dy, BH, L) &&
-            make_map(&ms, sv.s, BH, NT * kC) && make_map(&mds, wk.ds, BH, NT * kC);
+  bool ok = make_map(&mq, fq, BH, L, W) && make_map(&mk, fk, B * Hkv, L, W) &&
+            make_map(&mv, v, B * Hkv, L, W) && make_map(&mdy, dy, BH, L, W) &&
+            make_map(&ms, sv.s, BH, srows, W, sbox) && make_map(&mds, wk.ds, BH, srows, W, sbox);
   // fp32 gradients are stored directly; their maps are unused
   mdfq = mdfk = mdv = mq;
-  if (gdt == LZ_DTYPE_BF16) ok = ok && make_map(&mdfq, dfq, BH, L);
+  if (gdt == LZ_DTYPE_BF16) ok = ok && make_map(&mdfq, dfq, BH, L, W);
   if (gdt_kv == LZ_DTYPE_BF16)
-    ok = ok && make_map(&mdfk, dfk, BH, L) && make_map(&mdv, dv, BH, L);
+    ok = ok && make_map(&mdfk, dfk, BH, L, W) && make_map(&mdv, dv, BH, L, W);
   if (!ok) {
     set_error("gla_bwd: tensor map encoding failed");
     return LZ_ERR_CUDA;
   }
-  static bool done[64] = {false};
-  int rc = ensure_attr(reinterpret_cast<const void*>(gla_bwd_chunk_tc_kernel), kSmem2, done);
-  if (rc) return rc;
-  gla_bwd_chunk_tc_kernel<<<(unsigned)((long long)BH * NT), kThreads, kSmem2, stream>>>(
-      mq, mk, mv, mdy, ms, mds, mdfq, mdfk, mdv, sv.g, sv.den, wk.delta, sv.z, wk.dz, H, H / Hkv,
-      L, NT, gdt, gdt_kv, dfq, dfk, dv, wk.dg, wk.dgt, s_seeded, ds_seeded);
+  const unsigned grid = (unsigned)((long long)BH * NT);
+  if (narrow) {
+    static bool done[64] = {false};
+    int rc = ensure_attr(reinterpret_cast<const void*>(gla_bwd_chunk_tc_kernel<true>), kSmem2,
+                         done);
+    if (rc) return rc;
+    gla_bwd_chunk_tc_kernel<true><<<grid, kThreads, kSmem2, stream>>>(
+        mq, mk, mv, mdy, ms, mds, mdfq, mdfk, mdv, sv.g, sv.den, wk.delta, sv.z, wk.dz, H,
+        H / Hkv, L, NT, gdt, gdt_kv, dfq, dfk, dv, wk.dg, wk.dgt, s_seeded, ds_seeded);
+  } else {
+    static bool done[64] = {false};
+    int rc = ensure_attr(reinterpret_cast<const void*>(gla_bwd_chunk_tc_kernel<false>), kSmem2,
+                         done);
+    if (rc) return rc;
+    gla_bwd_chunk_tc_kernel<false><<<grid, kThreads, kSmem2, stream>>>(
+        mq, mk, mv, mdy, ms, mds, mdfq, mdfk, mdv, sv.g, sv.den, wk.delta, sv.z, wk.dz, H,
+        H / Hkv, L, NT, gdt, gdt_kv, dfq, dfk, dv, wk.dg, wk.dgt, s_seeded, ds_seeded);
+  }
   count_launches(1);
   return check_launch("gla_bwd_chunk_tc_kernel");
 }

@@ -233,7 +233,10 @@ int gla_bwd_tc_states(const bf16* fq, const bf16* dy, const GlaSaved& sv, const 
 int gla_bwd_tc_chunks(const bf16* fq, const bf16* fk, const bf16* v, const bf16* dy,
                       const GlaSaved& sv, const GlaWork& wk, void* dfq, void* dfk, void* dv,
                       int gdt, int gdt_kv, int B, int H, int Hkv, int L, int s_seeded,
-                      int ds_seeded, cudaStream_t stream);
+                      int ds_seeded, cudaStream_t stream, bool narrow = false);
+// The chunk-parallel schedule's tensor-core kernels (chunk outputs, and the
+// F = D = 64 chunk gradients) are on unless a test switched them off.
+bool gla_split_out_tc_enabled();
 
 // fk and v carry Hkv heads (H % Hkv == 0); dfk and dv are [B*Hkv, L, *], each
 // the sum over its group of query heads (wk.gk / wk.gv hold the per-head terms).

@@ -199,6 +199,38 @@ def test_gla_config4_top_length_forward_backward(L):
             assert_grad(got[sl], r, f"L={L} [{b},{h}] {n}")
 
 
+@pytest.mark.parametrize("tc_on", [True, False])
+@pytest.mark.parametrize("per_head,H,Hkv", [(False, 8, 8), (True, 4, 4), (False, 8, 2)])
+def test_gla_f64_d64_training_tensor_core_and_warp_mma(tc_on, per_head, H, Hkv):
+    """F = D = 64 (config 3's shape) with an odd tail of 76 tokens: with the
+    switch on the chunk outputs and the per-chunk gradients run on the tensor
+    cores over 128-token chunks (zero-padded 128-wide operands, the 64-token
+    states at stride two), with it off on the warp-MMA kernels; both against
+    the oracle, grouped keys / values included."""
+    import lizard_cuda
+    from lizard_cuda import _lib as binding
+    lib = binding.load()
+    fq, fk, v, lg, dy = baseline_inputs(2, H, 1100, 64, 64, per_head=per_head, seed=29)
+    grp = H // Hkv
+    fk_g, v_g = fk[:, ::grp].contiguous(), v[:, ::grp].contiguous()  # one key/value head a group
+    old = lib.lz_gla_set_split_out_tc(int(tc_on))
+    try:
+        leaves = [t.detach().clone().requires_grad_() for t in (fq, fk_g, v_g, lg)]
+        y = lizard_cuda.gla(*leaves)
+        y.backward(dy.to(y.dtype))
+        torch.cuda.synchronize()
+    finally:
+        lib.lz_gla_set_split_out_tc(old)
+    rep = lambda t: t.repeat_interleave(grp, 1)  # noqa: E731
+    ref, (rq, rk, rv, rl) = oracle_gla(fq, rep(fk_g), rep(v_g), lg, dy.bfloat16())
+    # the gradients of grouped keys / values are the sums over each group
+    rk = rk.view(2, Hkv, grp, 1100, 64).sum(2)
+    rv = rv.view(2, Hkv, grp, 1100, 64).sum(2)
+    assert_output(y, ref, f"F=D=64 tc={tc_on} y")
+    for got, r, n in zip([t.grad for t in leaves], (rq, rk, rv, rl), GRAD_NAMES):
+        assert_grad(got, r, f"F=D=64 tc={tc_on} {n}")
+
+
 def test_gla_model_feature_dim_256():
     """F = 2 * feature_dim = 256 (the 1B model), D = 64, fwd + bwd."""
     fq, fk, v, lg, dy = baseline_inputs(1, 4, 300, 256, 64, per_head=False, seed=5)
