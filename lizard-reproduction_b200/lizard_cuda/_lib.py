@@ -141,6 +141,22 @@ def device_timeout_flag():
     return int(out.value)
 
 
+_size_cache = {}
+
+
+def size_query(name, *args):
+    """The library's buffer-size query `name`(*args), remembered per argument
+    tuple: the sizes depend only on the shape and the GLA schedule switch, and
+    set_schedule clears what is remembered. (Every call still checks the sizes
+    it is given, so a wrong size raises instead of corrupting memory.)"""
+    key = (name,) + args
+    hit = _size_cache.get(key)
+    if hit is None:
+        hit = int(getattr(load(), name)(*args))
+        _size_cache[key] = hit
+    return hit
+
+
 def clear_device_timeout_flag():
     """Clear the current device's timeout flag once a timeout has been handled."""
     check(load().lz_device_timeout_clear(), "timeout flag clear")
@@ -151,6 +167,7 @@ SCHEDULES = {"auto": 0, "walk": 1, "split": 2}
 
 def set_schedule(name):
     """Process-wide GLA schedule ("auto", "walk" or "split"); returns the previous name."""
+    _size_cache.clear()
     prev = load().lz_gla_set_schedule(SCHEDULES[name])
     if prev < 0:
         check(-prev, "set schedule")

@@ -49,10 +49,10 @@ class _GLA(torch.autograd.Function):
         y = torch.empty(B, H, L, D, device=v.device, dtype=torch.bfloat16)
         saved = None
         if save:
-            nbytes = lib.lz_gla_saved_bytes(B, H, L, F, D, chunk)
+            nbytes = _lib.size_query("lz_gla_saved_bytes", B, H, L, F, D, chunk)
             saved = torch.empty(nbytes, device=v.device, dtype=torch.uint8)
-        wbytes = lib.lz_gla_fwd_gqa_workspace_bytes(B, H, Hkv, L, F, D, chunk, per_head,
-                                                    int(save))
+        wbytes = _lib.size_query("lz_gla_fwd_gqa_workspace_bytes", B, H, Hkv, L, F, D, chunk,
+                                 per_head, int(save))
         ws = torch.empty(wbytes, device=v.device, dtype=torch.uint8) if wbytes else None
         with _lib.on_device(v.device):
             rc = lib.lz_gla_fwd_gqa(_lib.ptr(fq), _lib.ptr(fk), _lib.ptr(v), _lib.ptr(lg),
@@ -78,8 +78,8 @@ class _GLA(torch.autograd.Function):
         dfk = torch.empty(B, Hkv, L, F, device=fq.device, dtype=gtorch)
         dv = torch.empty(B, Hkv, L, D, device=fq.device, dtype=gtorch)
         dlg = torch.empty_like(lg)
-        ws = torch.empty(lib.lz_gla_bwd_gqa_workspace_bytes(B, H, Hkv, L, F, D, chunk),
-                         device=fq.device, dtype=torch.uint8)
+        nws = _lib.size_query("lz_gla_bwd_gqa_workspace_bytes", B, H, Hkv, L, F, D, chunk)
+        ws = torch.empty(nws, device=fq.device, dtype=torch.uint8)
         with _lib.on_device(fq.device):
             rc = lib.lz_gla_bwd_gqa(_lib.ptr(fq), _lib.ptr(fk), _lib.ptr(v), _lib.ptr(lg),
                                     per_head, _lib.ptr(saved), saved.numel(), _lib.ptr(dy),

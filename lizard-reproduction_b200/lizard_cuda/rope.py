@@ -144,7 +144,7 @@ class _SWARope(torch.autograd.Function):
         save = any(ctx.needs_input_grad[:3]) or ctx.needs_input_grad[5]
         saved = rot = None
         if save:
-            saved = torch.empty(lib.lz_swa_saved_bytes(B, H, L, D), device=q.device,
+            saved = torch.empty(_lib.size_query("lz_swa_saved_bytes", B, H, L, D), device=q.device,
                                 dtype=torch.uint8)
             rot = tuple(torch.empty(B, n, L, D, device=q.device, dtype=torch.bfloat16)
                         for n in (H, H, Hkv, Hkv))
@@ -173,8 +173,8 @@ class _SWARope(torch.autograd.Function):
         dkr = torch.empty(B, Hkv, L, D, device=dy.device, dtype=torch.float32)
         dv = torch.empty_like(dkr)
         dmeta = torch.empty(n_meta, device=dy.device, dtype=torch.float32)
-        ws = torch.empty(lib.lz_swa_bwd_workspace_bytes(B, H, L, D, n_meta), device=dy.device,
-                         dtype=torch.uint8)
+        nws = _lib.size_query("lz_swa_bwd_workspace_bytes", B, H, L, D, n_meta)
+        ws = torch.empty(nws, device=dy.device, dtype=torch.uint8)
         with _lib.on_device(dy.device):
             rc = lib.lz_swa_bwd_gqa(_lib.ptr(q_hi), _lib.ptr(k_hi), _lib.ptr(v16),
                                     _lib.ptr(q_lo), _lib.ptr(k_lo),

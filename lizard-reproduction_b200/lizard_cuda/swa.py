@@ -52,7 +52,7 @@ class _SWA(torch.autograd.Function):
         save = any(ctx.needs_input_grad[:4])
         saved = None
         if save:
-            saved = torch.empty(lib.lz_swa_saved_bytes(B, H, L, D), device=q.device,
+            saved = torch.empty(_lib.size_query("lz_swa_saved_bytes", B, H, L, D), device=q.device,
                                 dtype=torch.uint8)
         with _lib.on_device(q.device):
             rc = lib.lz_swa_fwd_gqa(_lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(q_lo),
@@ -81,8 +81,8 @@ class _SWA(torch.autograd.Function):
         dk = torch.empty(B, Hkv, L, D, device=q.device, dtype=gtorch)
         dv = torch.empty_like(dk)
         dmeta = torch.empty(n_meta, device=q.device, dtype=torch.float32)
-        ws = torch.empty(lib.lz_swa_bwd_workspace_bytes(B, H, L, D, n_meta), device=q.device,
-                         dtype=torch.uint8)
+        nws = _lib.size_query("lz_swa_bwd_workspace_bytes", B, H, L, D, n_meta)
+        ws = torch.empty(nws, device=q.device, dtype=torch.uint8)
         with _lib.on_device(q.device):
             rc = lib.lz_swa_bwd_gqa(_lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(q_lo),
                                     _lib.ptr(k_lo), _lib.ptr(meta) if n_meta else None,
