@@ -112,6 +112,13 @@ int lz_gla_set_schedule(int schedule);
  * process-wide; y is the same with and without a saved buffer either way. */
 int lz_gla_set_split_out_tc(int on);
 
+/* Selects the walk schedule's tensor-core forward for F = D = 128: two
+ * sequences per SM with 64-token chunks (1, the default) or one sequence per
+ * SM with 128-token chunks (0). Both save the same 128-token chunk states for
+ * the backward. Returns the previous setting. A hook for tests and tuning,
+ * process-wide; do not change it between a forward and its backward. */
+int lz_gla_set_fwd_tc64(int on);
+
 /* Forward of gla(fq, fk, v, log_gamma, chunk).
  * Replaces gla() + _GLA.forward of the reference (src/kernels/gla.py:259-263
  * and 213-234): G = cumsum(log_gamma) is computed on the device, chunk by

@@ -21,6 +21,7 @@ int check_sizes(int B, int H, int L, int F, int D) {
 namespace lz {
 // Each unit whose kernels hold bounded waits has its own copy of the flag.
 int gla_fwd_tc_timeout_flag(unsigned int* out);
+int gla_fwd_tc64_timeout_flag(unsigned int* out);
 int gla_bwd_tc_timeout_flag(unsigned int* out);
 int gla_out_tc_timeout_flag(unsigned int* out);
 int hedgehog_timeout_flag(unsigned int* out);
@@ -28,6 +29,7 @@ int swa_timeout_flag(unsigned int* out);
 int swa_tc_timeout_flag(unsigned int* out);
 int decode_timeout_flag(unsigned int* out);
 int gla_fwd_tc_timeout_clear();
+int gla_fwd_tc64_timeout_clear();
 int gla_bwd_tc_timeout_clear();
 int gla_out_tc_timeout_clear();
 int hedgehog_timeout_clear();
@@ -40,9 +42,9 @@ extern "C" int lz_device_timeout_flag(unsigned int* site) {
   lz::clear_error();
   LZ_REQUIRE(site, LZ_ERR_INVALID_ARGUMENT, "null pointer");
   int (*const readers[])(unsigned int*) = {
-      lz::gla_fwd_tc_timeout_flag, lz::gla_bwd_tc_timeout_flag, lz::gla_out_tc_timeout_flag,
-      lz::hedgehog_timeout_flag,   lz::swa_timeout_flag,        lz::swa_tc_timeout_flag,
-      lz::decode_timeout_flag};
+      lz::gla_fwd_tc_timeout_flag, lz::gla_fwd_tc64_timeout_flag, lz::gla_bwd_tc_timeout_flag,
+      lz::gla_out_tc_timeout_flag, lz::hedgehog_timeout_flag,     lz::swa_timeout_flag,
+      lz::swa_tc_timeout_flag,     lz::decode_timeout_flag};
   *site = 0;
   for (auto rd : readers) {
     unsigned int v = 0;
@@ -59,9 +61,9 @@ extern "C" int lz_device_timeout_flag(unsigned int* site) {
 extern "C" int lz_device_timeout_clear(void) {
   lz::clear_error();
   int (*const clearers[])() = {
-      lz::gla_fwd_tc_timeout_clear, lz::gla_bwd_tc_timeout_clear, lz::gla_out_tc_timeout_clear,
-      lz::hedgehog_timeout_clear,   lz::swa_timeout_clear,        lz::swa_tc_timeout_clear,
-      lz::decode_timeout_clear};
+      lz::gla_fwd_tc_timeout_clear, lz::gla_fwd_tc64_timeout_clear, lz::gla_bwd_tc_timeout_clear,
+      lz::gla_out_tc_timeout_clear, lz::hedgehog_timeout_clear,     lz::swa_timeout_clear,
+      lz::swa_tc_timeout_clear,     lz::decode_timeout_clear};
   for (auto cl : clearers) {
     const int rc = cl();
     if (rc) return rc;
@@ -123,6 +125,12 @@ int gla_set_out_tc(int on);
 }
 
 extern "C" int lz_gla_set_split_out_tc(int on) { return lz::gla_set_out_tc(on); }
+
+namespace lz {
+int gla_set_fwd_tc64(int on);
+}
+
+extern "C" int lz_gla_set_fwd_tc64(int on) { return lz::gla_set_fwd_tc64(on); }
 
 extern "C" int lz_gla_fwd_gqa(const void* fq, const void* fk, const void* v,
                               const float* log_gamma, int gate_per_head, void* y, void* saved,

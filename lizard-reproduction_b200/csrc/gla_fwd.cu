@@ -15,6 +15,7 @@
 // The reference splits this into a state kernel that writes S for every
 // chunk to HBM and an output kernel that reads it back; here both live in
 // one pass.
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -258,6 +259,14 @@ int launch_fwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, i
 int gla_fwd_tc(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, bf16* y,
                const GlaSaved& sv, int B, int H, int Hkv, int L, int F, int D,
                cudaStream_t stream);
+int gla_fwd_tc64(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph,
+                 bf16* y, const GlaSaved& sv, int B, int H, int Hkv, int L, int F, int D,
+                 cudaStream_t stream);
+
+namespace {
+std::atomic<int> g_fwd_tc64{0};
+}  // namespace
+int gla_set_fwd_tc64(int on) { return g_fwd_tc64.exchange(on ? 1 : 0); }
 
 int gla_fwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int gph, bf16* y,
             const GlaSaved& sv, const GlaFwdWork& fw, int B, int H, int Hkv, int L, int F, int D,
@@ -266,7 +275,12 @@ int gla_fwd(const bf16* fq, const bf16* fk, const bf16* v, const float* lg, int 
     return gla_fwd_split_run(fq, fk, v, lg, gph, y, sv, fw, B, H, Hkv, L, F, D, stream);
   const int BH = B * H, grp = H / Hkv;
   if (gla_saved_chunk(B, H, L, F, D, fq, fk, v) == 128) {
-    // tensor-core kernel; in training it also saves the 128-token chunk states
+    // tensor-core kernels (two sequences per SM with 64-token chunks, or one
+    // with 128-token chunks); in training they also save the 128-token chunk states
+    if (g_fwd_tc64.load(std::memory_order_relaxed)) {
+      const int rc = gla_fwd_tc64(fq, fk, v, lg, gph, y, sv, B, H, Hkv, L, F, D, stream);
+      if (rc != LZ_ERR_UNSUPPORTED) return rc;
+    }
     const int rc = gla_fwd_tc(fq, fk, v, lg, gph, y, sv, B, H, Hkv, L, F, D, stream);
     if (rc != LZ_ERR_UNSUPPORTED) return rc;
     if (sv.y32) {

@@ -91,11 +91,18 @@ constexpr int kGroup = 256;  // threads of the decay group and of the output gro
 // every barrier, and the kernel ends. The TMA and MMA warps use no bar.sync and
 // stop at their first failed wait.
 
+// Eight bf16 values times one factor with packed bf16 multiplies: the product
+// of two bf16 values is exact in fp32, so each result is the bf16 rounding of
+// value * bf16(sc); the factor itself carries the bf16 rounding (2^-9 relative).
 __device__ __forceinline__ uint4 scale8(uint4 w, float sc) {
-  w.x = pack_bf16(bf16_lo(w.x) * sc, bf16_hi(w.x) * sc);
-  w.y = pack_bf16(bf16_lo(w.y) * sc, bf16_hi(w.y) * sc);
-  w.z = pack_bf16(bf16_lo(w.z) * sc, bf16_hi(w.z) * sc);
-  w.w = pack_bf16(bf16_lo(w.w) * sc, bf16_hi(w.w) * sc);
+  const __nv_bfloat162 s2 = __float2bfloat162_rn(sc);
+  uint32_t* p = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&p[i]);
+    x = __hmul2(x, s2);
+    p[i] = *reinterpret_cast<uint32_t*>(&x);
+  }
   return w;
 }
 
@@ -346,11 +353,16 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
           const float ar = valid ? tc::ex2(g2 - sG[32 * cb + 31]) : 0.f;
           const float4* bt = reinterpret_cast<const float4*>(sB + c0);
           tc::tmem_wait_ld();
+          const float2 ar2 = make_float2(ar, ar);
 #pragma unroll
-          for (int j4 = 0; j4 < 4; ++j4) {
+          for (int j4 = 0; j4 < 4; ++j4) {  // (s * f) * ar, two columns per packed multiply
             const float4 f = bt[j4];
-            pk[2 * j4] = pack_bf16(sc[4 * j4] * f.x * ar, sc[4 * j4 + 1] * f.y * ar);
-            pk[2 * j4 + 1] = pack_bf16(sc[4 * j4 + 2] * f.z * ar, sc[4 * j4 + 3] * f.w * ar);
+            const float2 p0 = __fmul2_rn(__fmul2_rn(make_float2(sc[4 * j4], sc[4 * j4 + 1]),
+                                                    make_float2(f.x, f.y)), ar2);
+            const float2 p1 = __fmul2_rn(__fmul2_rn(make_float2(sc[4 * j4 + 2], sc[4 * j4 + 3]),
+                                                    make_float2(f.z, f.w)), ar2);
+            pk[2 * j4] = pack_bf16(p0.x, p0.y);
+            pk[2 * j4 + 1] = pack_bf16(p1.x, p1.y);
           }
         } else if (cb == quad) {
           float sc[16];
@@ -445,13 +457,19 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       const size_t row = (size_t)bh * L + r0 + r;
       {
         unsigned char* yrow = base + (n & 1) * kStageBytes + kOffQ + h * 16384 + r * 128;
+        const float2 inv2 = make_float2(inv, inv);
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) {  // o * inv, two columns per packed multiply
+          const float2 q = __fmul2_rn(make_float2(o[i], o[i + 1]), inv2);
+          o[i] = q.x, o[i + 1] = q.y;
+        }
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           uint4 w;
-          w.x = pack_bf16(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
-          w.y = pack_bf16(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-          w.z = pack_bf16(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-          w.w = pack_bf16(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+          w.x = pack_bf16(o[8 * c + 0], o[8 * c + 1]);
+          w.y = pack_bf16(o[8 * c + 2], o[8 * c + 3]);
+          w.z = pack_bf16(o[8 * c + 4], o[8 * c + 5]);
+          w.w = pack_bf16(o[8 * c + 6], o[8 * c + 7]);
           *reinterpret_cast<uint4*>(yrow + ((c ^ (r & 7)) * 16)) = w;
         }
         tc::fence_proxy_async_smem();
@@ -461,9 +479,8 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         if (save) {
           float4* d32 = reinterpret_cast<float4*>(y32 + row * 128 + 64 * h);
 #pragma unroll
-          for (int q4 = 0; q4 < 16; ++q4)
-            d32[q4] = make_float4(o[4 * q4] * inv, o[4 * q4 + 1] * inv, o[4 * q4 + 2] * inv,
-                                  o[4 * q4 + 3] * inv);
+          for (int q4 = 0; q4 < 16; ++q4)  // o already holds o * inv
+            d32[q4] = make_float4(o[4 * q4], o[4 * q4 + 1], o[4 * q4 + 2], o[4 * q4 + 3]);
           if (h == 0) den_out[row] = dtot;
         }
       }
@@ -507,15 +524,17 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
           tc::tmem_ld64(trow + kTSF + 64 * h, sv);
           // Q~ . z over this half of row r while the state loads
           const float4* z4 = reinterpret_cast<const float4*>(sZ + 64 * h);
-          float dqh = 0.f;
+          float2 dq2 = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
+          for (int i = 0; i < 8; ++i) {  // two columns per packed FMA
             const uint4 w = qv[i];
             const float4 za = z4[2 * i], zb = z4[2 * i + 1];
-            dqh += bf16_lo(w.x) * za.x + bf16_hi(w.x) * za.y + bf16_lo(w.y) * za.z +
-                   bf16_hi(w.y) * za.w + bf16_lo(w.z) * zb.x + bf16_hi(w.z) * zb.y +
-                   bf16_lo(w.w) * zb.z + bf16_hi(w.w) * zb.w;
+            dq2 = __ffma2_rn(make_float2(bf16_lo(w.x), bf16_hi(w.x)), make_float2(za.x, za.y), dq2);
+            dq2 = __ffma2_rn(make_float2(bf16_lo(w.y), bf16_hi(w.y)), make_float2(za.z, za.w), dq2);
+            dq2 = __ffma2_rn(make_float2(bf16_lo(w.z), bf16_hi(w.z)), make_float2(zb.x, zb.y), dq2);
+            dq2 = __ffma2_rn(make_float2(bf16_lo(w.w), bf16_hi(w.w)), make_float2(zb.z, zb.w), dq2);
           }
+          const float dqh = dq2.x + dq2.y;
           sDQ[h * 128 + r] = dqh;
           tc::tmem_wait_ld();
 #pragma unroll
@@ -532,7 +551,12 @@ gla_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
           for (int q = 0; q < 4; ++q) {
             uint32_t scl[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) scl[j] = __float_as_uint(sv[16 * q + j] * decay);
+            for (int j = 0; j < 16; j += 2) {  // two columns per packed multiply
+              const float2 p = __fmul2_rn(make_float2(sv[16 * q + j], sv[16 * q + j + 1]),
+                                          make_float2(decay, decay));
+              scl[j] = __float_as_uint(p.x);
+              scl[j + 1] = __float_as_uint(p.y);
+            }
             tc::tmem_st16(trow + kTSF + 64 * h + 16 * q, scl);
           }
         }

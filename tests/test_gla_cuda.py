@@ -359,6 +359,45 @@ def test_gla_f128_training_many_chunks(per_head):
         assert_grad(got, r, f"F=D=128 L=1100 {n}")
 
 
+@pytest.mark.parametrize("tc64", [True, False])
+@pytest.mark.parametrize("per_head,H,Hkv,L", [(True, 4, 4, 1000), (False, 8, 2, 257),
+                                             (True, 2, 2, 63), (False, 2, 1, 64)])
+def test_gla_f128_both_tensor_core_forwards(schedule, tc64, per_head, H, Hkv, L):
+    """F = D = 128 under the walk schedule on either tensor-core forward (two
+    sequences per SM with 64-token chunks, or one with 128-token chunks), each
+    followed by the tensor-core backward on the states it saved: output and all
+    gradients against the oracle, grouped keys / values and ragged tails
+    included, and the output the same with and without a saved buffer."""
+    import lizard_cuda
+    from lizard_cuda import _lib as binding
+    if schedule != "walk":
+        pytest.skip("the walk schedule's forward kernels")
+    lib = binding.load()
+    prev = lib.lz_gla_set_fwd_tc64(int(tc64))
+    try:
+        fq, fk, v, lg, dy = baseline_inputs(2, H, L, 128, 128, per_head=per_head, seed=41)
+        grp = H // Hkv
+        fk, v = fk[:, ::grp].contiguous(), v[:, ::grp].contiguous()
+        y, grads = cuda_gla(fq, fk, v, lg, dy)
+        with torch.no_grad():
+            y_ng = lizard_cuda.gla(fq.to(DEV), fk.to(DEV), v.to(DEV), lg.to(DEV))
+        torch.cuda.synchronize()
+        assert torch.equal(y_ng, y.detach())
+        rep = lambda t: t.repeat_interleave(grp, dim=1).float().cpu().requires_grad_()
+        fkr, vr = rep(fk), rep(v)
+        leaves = [fq.float().cpu().requires_grad_(), fkr, vr, lg.float().cpu().requires_grad_()]
+        ref = orc.gla(leaves[0], fkr, vr, leaves[3])
+        ref.backward(dy.bfloat16().float().cpu())
+        dfk = fkr.grad.view(2, Hkv, grp, L, 128).sum(2)
+        dv = vr.grad.view(2, Hkv, grp, L, 128).sum(2)
+        kind = "64-token" if tc64 else "128-token"
+        assert_output(y, ref.detach(), f"{kind} forward y")
+        for got, r, n in zip(grads, [leaves[0].grad, dfk, dv, leaves[3].grad], GRAD_NAMES):
+            assert_grad(got, r, f"{kind} forward {n}")
+    finally:
+        lib.lz_gla_set_fwd_tc64(prev)
+
+
 def test_gla_f128_fp32_inputs_give_fp32_grads():
     """fp32 fq, fk, v at F = D = 128: fp32 gradients (stored without staging)."""
     fq, fk, v, lg, dy = baseline_inputs(1, 4, 520, 128, 128, per_head=True, seed=23)
