@@ -113,11 +113,18 @@ int lz_gla_set_schedule(int schedule);
 int lz_gla_set_split_out_tc(int on);
 
 /* Selects the walk schedule's tensor-core forward for F = D = 128: two
- * sequences per SM with 64-token chunks (1, the default) or one sequence per
- * SM with 128-token chunks (0). Both save the same 128-token chunk states for
- * the backward. Returns the previous setting. A hook for tests and tuning,
+ * sequences per SM with 64-token chunks (1) or one sequence per SM with
+ * 128-token chunks (0, the default). Both save the same 128-token chunk states
+ * for the backward. Returns the previous setting. A hook for tests and tuning,
  * process-wide; do not change it between a forward and its backward. */
 int lz_gla_set_fwd_tc64(int on);
+
+/* L2 prefetch in the tensor-core per-chunk gradient kernel (F = D = 128 and
+ * F = D = 64): each CTA sends the operands of the CTA one SM count further on
+ * to L2 while it computes (1, the default) or not (0). Results are identical
+ * either way. Returns the previous setting. A hook for tests and tuning,
+ * process-wide. No counterpart in the reference. */
+int lz_gla_set_bwd_prefetch(int on);
 
 /* Forward of gla(fq, fk, v, log_gamma, chunk).
  * Replaces gla() + _GLA.forward of the reference (src/kernels/gla.py:259-263

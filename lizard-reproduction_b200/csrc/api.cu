@@ -132,6 +132,12 @@ int gla_set_fwd_tc64(int on);
 
 extern "C" int lz_gla_set_fwd_tc64(int on) { return lz::gla_set_fwd_tc64(on); }
 
+namespace lz {
+int gla_set_bwd_prefetch(int on);
+}
+
+extern "C" int lz_gla_set_bwd_prefetch(int on) { return lz::gla_set_bwd_prefetch(on); }
+
 extern "C" int lz_gla_fwd_gqa(const void* fq, const void* fk, const void* v,
                               const float* log_gamma, int gate_per_head, void* y, void* saved,
                               size_t saved_bytes, void* workspace, size_t workspace_bytes, int B,

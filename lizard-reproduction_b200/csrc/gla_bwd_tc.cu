@@ -29,6 +29,7 @@
 // with bar.sync and never leave their code path early: a wait that gives up
 // sets the device flag, every later wait returns at once, and the groups run
 // on (writing in-bounds garbage) through every barrier to the end.
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -354,7 +355,7 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
                         int L, int NT, int gdt, int gdt_kv, void* __restrict__ dfq,
                         void* __restrict__ dfk,
                         void* __restrict__ dv, float* __restrict__ dG, float* __restrict__ dGt,
-                        int s_seeded, int ds_seeded) {
+                        int s_seeded, int ds_seeded, int pf_ahead) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   if (smem_u32(smem_raw) & 1023) {
     if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 97u);
@@ -430,6 +431,34 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
       if (with_s) {
         tc::tma_load_3d(base + kOX, &ts, 0, s_row, bh, full);
         if (!NARROW) tc::tma_load_3d(base + kOX + 16384, &ts, 64, r0, bh, full);
+      }
+      // One CTA per SM: the CTA that starts on an SM when this one ends is about
+      // pf_ahead blocks further on. Its tiles and row scalars go to L2 now, so
+      // their HBM reads overlap this CTA's MMA phases instead of following them.
+      if (pf_ahead > 0 && blockIdx.x + pf_ahead < gridDim.x) {
+        const int nb = blockIdx.x + pf_ahead;
+        const int pn = nb % NT, pbh = nb / NT, pkvh = kv_head(pbh, H, grp), pr0 = pn * kC;
+#pragma unroll
+        for (int hb = 0; hb < kHB; ++hb) {
+          tc::tma_prefetch_l2_3d(&tq, 64 * hb, pr0, pbh);
+          tc::tma_prefetch_l2_3d(&tk, 64 * hb, pr0, pkvh);
+          tc::tma_prefetch_l2_3d(&tv, 64 * hb, pr0, pkvh);
+          tc::tma_prefetch_l2_3d(&tdy, 64 * hb, pr0, pbh);
+        }
+        const int ps_row = NARROW ? 2 * pn * 64 : pr0;
+        const int pds_row = NARROW ? min(2 * pn + 1, NTs - 1) * 64 : pr0;
+        if (pn > 0 || s_seeded)
+          for (int hb = 0; hb < kHB; ++hb) tc::tma_prefetch_l2_3d(&ts, 64 * hb, ps_row, pbh);
+        if (pn + 1 < NT || ds_seeded)
+          for (int hb = 0; hb < kHB; ++hb) tc::tma_prefetch_l2_3d(&tds, 64 * hb, pds_row, pbh);
+        // G, den and delta rows of the chunk: whole 16-byte groups inside it
+        const size_t prow = (size_t)pbh * L + pr0;
+        const uint32_t pbytes = (uint32_t)(min(kC, L - pr0) / 4) * 16;
+        if ((prow & 3) == 0 && pbytes > 0) {
+          tc::bulk_prefetch_l2(G + prow, pbytes);
+          tc::bulk_prefetch_l2(den + prow, pbytes);
+          tc::bulk_prefetch_l2(delta + prow, pbytes);
+        }
       }
       bool ok = tc::mbar_wait(full, 0, 31);
       if (with_ds && ok) {
@@ -731,6 +760,22 @@ bool make_map(CUtensorMap* m, const void* ptr, int BH, int rows, int cols = 128,
 }
 
 std::mutex g_tc_mu;
+// L2 prefetch of the next CTA's operands in the per-chunk gradient kernel (on by
+// default; lz_gla_set_bwd_prefetch(0) turns it off to measure it)
+std::atomic<int> g_chunk_prefetch{1};
+
+int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && n[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev] = v > 0 ? v : 148;
+  }
+  return dev < 64 ? n[dev] : 148;
+}
+
 int ensure_attr(const void* fn, int bytes, bool* done) {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -791,6 +836,7 @@ int gla_bwd_tc_chunks(const bf16* fq, const bf16* fk, const bf16* v, const bf16*
     return LZ_ERR_CUDA;
   }
   const unsigned grid = (unsigned)((long long)BH * NT);
+  const int pf = g_chunk_prefetch.load() ? sm_count() : 0;
   if (narrow) {
     static bool done[64] = {false};
     int rc = ensure_attr(reinterpret_cast<const void*>(gla_bwd_chunk_tc_kernel<true>), kSmem2,
@@ -798,7 +844,7 @@ int gla_bwd_tc_chunks(const bf16* fq, const bf16* fk, const bf16* v, const bf16*
     if (rc) return rc;
     gla_bwd_chunk_tc_kernel<true><<<grid, kThreads, kSmem2, stream>>>(
         mq, mk, mv, mdy, ms, mds, mdfq, mdfk, mdv, sv.g, sv.den, wk.delta, sv.z, wk.dz, H,
-        H / Hkv, L, NT, gdt, gdt_kv, dfq, dfk, dv, wk.dg, wk.dgt, s_seeded, ds_seeded);
+        H / Hkv, L, NT, gdt, gdt_kv, dfq, dfk, dv, wk.dg, wk.dgt, s_seeded, ds_seeded, pf);
   } else {
     static bool done[64] = {false};
     int rc = ensure_attr(reinterpret_cast<const void*>(gla_bwd_chunk_tc_kernel<false>), kSmem2,
@@ -806,11 +852,13 @@ int gla_bwd_tc_chunks(const bf16* fq, const bf16* fk, const bf16* v, const bf16*
     if (rc) return rc;
     gla_bwd_chunk_tc_kernel<false><<<grid, kThreads, kSmem2, stream>>>(
         mq, mk, mv, mdy, ms, mds, mdfq, mdfk, mdv, sv.g, sv.den, wk.delta, sv.z, wk.dz, H,
-        H / Hkv, L, NT, gdt, gdt_kv, dfq, dfk, dv, wk.dg, wk.dgt, s_seeded, ds_seeded);
+        H / Hkv, L, NT, gdt, gdt_kv, dfq, dfk, dv, wk.dg, wk.dgt, s_seeded, ds_seeded, pf);
   }
   count_launches(1);
   return check_launch("gla_bwd_chunk_tc_kernel");
 }
+
+int gla_set_bwd_prefetch(int on) { return g_chunk_prefetch.exchange(on ? 1 : 0); }
 
 int gla_bwd_tc_timeout_flag(unsigned int* out) { return tc::read_timeout_flag_here(out); }
 int gla_bwd_tc_timeout_clear() { return tc::clear_timeout_flag_here(); }

@@ -3,7 +3,8 @@
 // shape (reference: src/lizard_attention.py:34-44 and the Triton kernels
 // src/kernels/swa.py:19-133): the forward (below), and the dq and dk / dv
 // kernels of the backward (further down; delta and the sink gradient stay in
-// swa.cu).
+// swa.cu). Windows of 65 to 128 keys (the reference's training configs use
+// 128) have their own wider forward, dq and dk / dv kernels near the end.
 //
 // One CTA of 8 warps takes 128 query rows [q0, q0 + 128) of one batch row and
 // one key/value head, and every query head of that head's group in turn:
@@ -1569,6 +1570,632 @@ swa_fwd_tc_persist_kernel(const __grid_constant__ CUtensorMap tq,
   }
 }
 
+// ============================================================ windows 65 ... 128
+// The same three products for 64 < W <= 128 (the reference's own training
+// configs use window 128). A 128-row tile then sees 128 keys to its left, so
+// the tiles are wider and each kernel runs one CTA per SM:
+//   forward : 128 query rows against the 256 keys [q0 - 128, q0 + 128) in one
+//             softmax pass, s [128 x 256] and o [128 x 64] in TMEM (512
+//             columns allocated); each row warp takes 80 of the 160 columns
+//             that hold its lane quadrant's windows
+//   dq      : the 256 keys in two halves of 128, ds of a half over its scores
+//   dk / dv : the 256 query rows [k0, k0 + 256) that can see a 128-key tile in
+//             two items of 128 rows per query head, dk and dv summed in TMEM
+//             over the items and the group's heads
+// In the backward kernels each row warp covers a fixed 64 of the 128 columns
+// of a half (masked outside the window), so every column of the bf16
+// operands is written. Precision as the kernels above: logits from the
+// hi / lo terms, p in bf16 hi + lo for P V, bf16 p and ds in the gradients.
+constexpr int kH2 = 128;            // keys left of a query tile (window <= 128)
+constexpr int kNK2 = kQ + kH2;      // 256 key rows per forward / dq tile
+constexpr int kW2Cols = 80;         // window columns per row warp in the forward
+struct Fwd128Smem {
+  static constexpr size_t KT = kNK2 * 128, QT = kQ * 128;
+  static constexpr size_t kh = 0, kl = kh + KT, v = kl + KT, qh = v + KT, ql = qh + QT,
+                          red = ql + QT, bars = red + 2048, slot = bars + 32, bytes = slot + 16;
+};
+// TMEM: s [0, 256); p hi / lo (bf16 pairs, 128 columns each) over s; o [256, 320)
+constexpr uint32_t kT2S = 0, kT2Ph = 0, kT2Pl = kNK2 / 2, kT2O = kNK2, kT2Cols = 512;
+
+template <bool SPLIT>
+__global__ void __launch_bounds__(kThreads, 1)
+swa_fwd_tc128_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                     const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tql,
+                     const __grid_constant__ CUtensorMap tkl, const float* __restrict__ meta,
+                     int n_meta, int W, float scale_log2, int H, int grp, int L, int nqb,
+                     bf16* __restrict__ y, float* __restrict__ lse, float* __restrict__ y32) {
+  using SM = Fwd128Smem;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 85u);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::bars);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + SM::slot);
+  float* red = reinterpret_cast<float*>(smem + SM::red);  // [max | sum][half][row]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qd = warp & 3, hf = warp >> 2;
+  const int qb = blockIdx.x % nqb, bk = blockIdx.x / nqb;
+  const int Hkv = H / grp, b = bk / Hkv, hk = bk - b * Hkv;
+  const int q0 = qb * kQ, k0 = q0 - kH2;
+  constexpr uint32_t kTileK = kNK2 * 128, kTileQ = kQ * 128;
+  constexpr int kCh = kW2Cols / 16;  // 16-column chunks per thread
+
+  if (tid == 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tc::mbar_init(&bars[j], 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tslot, kT2Cols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  auto issue_q = [&](int g) {
+    const int h = hk * grp + g;
+    tc::mbar_expect_tx(&bars[SB_Q], SPLIT ? 2 * kTileQ : kTileQ);
+    tc::tma_load_4d(smem + SM::qh, &tq, 0, q0, h, b, &bars[SB_Q]);
+    if (SPLIT) tc::tma_load_4d(smem + SM::ql, &tql, 0, q0, h, b, &bars[SB_Q]);
+  };
+  auto issue_s = [&]() {  // s = q k^T into TMEM columns [0, 256)
+    tc::tc_fence_after();
+    constexpr uint32_t id_s = tc::idesc_bf16(kQ, kNK2, 0, 0);
+    const uint32_t qh = smem_u32(smem + SM::qh), ql = smem_u32(smem + SM::ql),
+                   kh = smem_u32(smem + SM::kh), kl = smem_u32(smem + SM::kl);
+#pragma unroll
+    for (int j = 0; j < kDh / 16; ++j)
+      tc::mma_ss(tmem + kT2S, tc::sdesc(qh + 32 * j, 16, 1024), tc::sdesc(kh + 32 * j, 16, 1024),
+                 id_s, j > 0);
+    if (SPLIT) {
+#pragma unroll
+      for (int j = 0; j < kDh / 16; ++j)
+        tc::mma_ss(tmem + kT2S, tc::sdesc(qh + 32 * j, 16, 1024),
+                   tc::sdesc(kl + 32 * j, 16, 1024), id_s, 1u);
+#pragma unroll
+      for (int j = 0; j < kDh / 16; ++j)
+        tc::mma_ss(tmem + kT2S, tc::sdesc(ql + 32 * j, 16, 1024),
+                   tc::sdesc(kh + 32 * j, 16, 1024), id_s, 1u);
+    }
+    tc::mma_commit(&bars[SB_S]);
+  };
+  if (tid == 0) {
+    tc::mbar_expect_tx(&bars[SB_KV], SPLIT ? 3 * kTileK : 2 * kTileK);
+    tc::tma_load_4d(smem + SM::kh, &tk, 0, k0, hk, b, &bars[SB_KV]);
+    if (SPLIT) tc::tma_load_4d(smem + SM::kl, &tkl, 0, k0, hk, b, &bars[SB_KV]);
+    tc::tma_load_4d(smem + SM::v, &tv, 0, k0, hk, b, &bars[SB_KV]);
+    issue_q(0);
+  }
+
+  // sinks seed the max and the row sum (log2 domain)
+  float ms = -1e30f;
+  for (int j = 0; j < n_meta; ++j) ms = fmaxf(ms, meta[j] * kLog2e);
+  float ls = 0.f;
+  for (int j = 0; j < n_meta; ++j) ls += exp2f(meta[j] * kLog2e - ms);
+
+  tc::mbar_wait(&bars[SB_KV], 0, 110);
+  tc::mbar_wait(&bars[SB_Q], 0, 111);
+  tc::tc_fence_before();
+  __syncthreads();
+  if (tid == 0) issue_s();
+
+  const int r = 32 * qd + lane, i = q0 + r;
+  const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
+  // the window of row i is keys t in (i - W, i]: columns t - k0 in
+  // [32 qd + 1, 32 qd + 159] over the quadrant; this thread takes 80 of them
+  const int cw = 32 * qd + kW2Cols * hf;
+  for (int g = 0; g < grp; ++g) {
+    const uint32_t ph = (uint32_t)g & 1u;
+    const bool next = g + 1 < grp;
+    tc::mbar_wait(&bars[SB_S], ph, 112);
+    tc::tc_fence_after();
+    if (tid == 0 && next) issue_q(g + 1);  // the scores have read the query tiles
+
+    float s[kCh][16];
+#pragma unroll
+    for (int k = 0; k < kCh; ++k) tc::tmem_ld16(trow + kT2S + cw + 16 * k, s[k]);
+    tc::tmem_wait_ld();
+    float mx = ms;
+#pragma unroll
+    for (int k = 0; k < kCh; ++k)
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int t = k0 + cw + 16 * k + u;
+        const bool ok = t <= i && t > i - W && t >= 0;
+        const float x = ok ? s[k][u] * scale_log2 : -INFINITY;
+        s[k][u] = x;
+        mx = fmaxf(mx, x);
+      }
+    red[hf * kQ + r] = mx;
+    __syncthreads();
+    mx = fmaxf(mx, red[(1 - hf) * kQ + r]);
+    float l = 0.f;
+#pragma unroll
+    for (int k = 0; k < kCh; ++k) {
+      uint32_t phi[8], plo[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float p0 = tc::ex2(s[k][2 * j] - mx), p1 = tc::ex2(s[k][2 * j + 1] - mx);
+        l += p0 + p1;
+        const uint32_t hpk = pack_bf16(p0, p1);
+        phi[j] = hpk;
+        plo[j] = pack_bf16(p0 - bf16_lo(hpk), p1 - bf16_hi(hpk));
+      }
+      tc::tmem_st8(trow + kT2Ph + cw / 2 + 8 * k, phi);
+      tc::tmem_st8(trow + kT2Pl + cw / 2 + 8 * k, plo);
+    }
+    {  // p is zero outside the window: packed columns [0, 16 qd) and [16 qd + 80, 128)
+      uint32_t zero[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) zero[j] = 0u;
+      const int z0 = hf ? 16 * qd + kW2Cols : 0, z1 = hf ? kNK2 / 2 : 16 * qd;
+#pragma unroll 1
+      for (int c = z0; c < z1; c += 8) {
+        tc::tmem_st8(trow + kT2Ph + c, zero);
+        tc::tmem_st8(trow + kT2Pl + c, zero);
+      }
+    }
+    red[2 * kQ + hf * kQ + r] = l;
+    tc::tmem_wait_st();
+    tc::tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc::tc_fence_after();
+      constexpr uint32_t id_o = tc::idesc_bf16(kQ, kDh, 0, 1);  // p (TMEM) x V (MN-major)
+      const uint32_t va = smem_u32(smem + SM::v);
+#pragma unroll
+      for (int j = 0; j < kNK2 / 16; ++j)
+        tc::mma_ts(tmem + kT2O, tmem + kT2Ph + 8 * j, tc::sdesc(va + 2048 * j, kTileK, 1024), id_o,
+                   j > 0);
+#pragma unroll
+      for (int j = 0; j < kNK2 / 16; ++j)
+        tc::mma_ts(tmem + kT2O, tmem + kT2Pl + 8 * j, tc::sdesc(va + 2048 * j, kTileK, 1024), id_o,
+                   1u);
+      tc::mma_commit(&bars[SB_O]);
+    }
+    const float lrow = ls * exp2f(ms - mx) + red[2 * kQ + r] + red[3 * kQ + r];
+    if (next) tc::mbar_wait(&bars[SB_Q], ph ^ 1u, 111);
+    tc::mbar_wait(&bars[SB_O], ph, 113);
+    tc::tc_fence_after();
+    tc::tc_fence_before();
+    __syncthreads();  // P V done (s / p columns free), the next query tiles landed
+    if (tid == 0 && next) issue_s();
+
+    const float inv = 1.f / lrow;
+    const size_t row = ((size_t)b * H + hk * grp + g) * L + i;
+    float o[32];
+    tc::tmem_ld32(trow + kT2O + 32 * hf, o);
+    tc::tmem_wait_ld();
+    if (i < L) {
+      bf16* yr = y + row * kDh + 32 * hf;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint4 w;
+        w.x = pack_bf16(o[8 * q4] * inv, o[8 * q4 + 1] * inv);
+        w.y = pack_bf16(o[8 * q4 + 2] * inv, o[8 * q4 + 3] * inv);
+        w.z = pack_bf16(o[8 * q4 + 4] * inv, o[8 * q4 + 5] * inv);
+        w.w = pack_bf16(o[8 * q4 + 6] * inv, o[8 * q4 + 7] * inv);
+        reinterpret_cast<uint4*>(yr)[q4] = w;
+      }
+      if (y32) {
+        float4* d32 = reinterpret_cast<float4*>(y32 + row * kDh + 32 * hf);
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4)
+          d32[q4] = make_float4(o[4 * q4] * inv, o[4 * q4 + 1] * inv, o[4 * q4 + 2] * inv,
+                                o[4 * q4 + 3] * inv);
+      }
+      if (lse && hf == 0) lse[row] = mx * kLn2f + logf(lrow);
+    }
+    tc::tc_fence_before();
+    __syncthreads();  // o and the row-sum slots are free for the next head
+  }
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kT2Cols);
+  }
+}
+
+// dq for 64 < W <= 128: one CTA of 9 warps per 128 query rows and each query
+// head of the group; the keys [q0 - 128, q0 + 128) in four quarters of 64, so
+// the scores, dp and dq fit 256 TMEM columns and, with bf16 operands (96 KB
+// of shared memory, one query / dy stage), two CTAs share an SM.
+constexpr int kQK = 64;  // keys per quarter
+template <bool SPLIT>
+struct Dq128Smem {
+  static constexpr size_t KT = kNK2 * 128, QT = kQ * 128;
+  static constexpr size_t kh = 0, kl = kh + KT, v = kl + (SPLIT ? KT : 0), st = v + KT;
+  static constexpr size_t sq = 0, sql = QT, sdy = sql + (SPLIT ? QT : 0), sbytes = sdy + QT;
+  static constexpr size_t bars = st + sbytes, slot = bars + 64, bytes = slot + 16;
+};
+// TMEM: s of a quarter [0, 64) with ds (bf16 pairs) over it in [0, 16) and
+// [32, 48) (the first half of each row warp's 32 score columns); dp [64, 128);
+// dq [128, 192)
+constexpr uint32_t kU2S = 0, kU2Ds = 0, kU2Dp = 64, kU2Dq = 128, kU2Cols = 256;
+
+template <bool SPLIT>
+__global__ void __launch_bounds__(kCtaThreads, SPLIT ? 1 : 2)
+swa_bwd_dq_tc128_kernel(const __grid_constant__ CUtensorMap tq,
+                        const __grid_constant__ CUtensorMap tql,
+                        const __grid_constant__ CUtensorMap tdy,
+                        const __grid_constant__ CUtensorMap tk,
+                        const __grid_constant__ CUtensorMap tkl,
+                        const __grid_constant__ CUtensorMap tv, const float* __restrict__ lse,
+                        const float* __restrict__ delta, int W, float scale, int H, int grp, int L,
+                        int nqb, void* __restrict__ dq, int gdt) {
+  using SM = Dq128Smem<SPLIT>;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 84u);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::bars);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + SM::slot);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qb = blockIdx.x % nqb, bk = blockIdx.x / nqb;
+  const int Hkv = H / grp, b = bk / Hkv, hk = bk - b * Hkv;
+  const int q0 = qb * kQ, k0 = q0 - kH2;
+  constexpr uint32_t kTileK = kNK2 * 128, kTileQ = kQ * 128;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int j = 0; j < 6; ++j) tc::mbar_init(&bars[j], 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == 8) {
+    tc::tmem_alloc(tslot, kU2Cols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 8) {
+    const bool issuer = lane == 0;
+    auto load_stage = [&](int g) {  // query / dy rows of head hk * grp + g
+      const int h = hk * grp + g;
+      unsigned char* st = smem + SM::st;
+      uint64_t* bar = &bars[QB_Q0];
+      tc::mbar_expect_tx(bar, (SPLIT ? 3 : 2) * kTileQ);
+      tc::tma_load_4d(st + SM::sq, &tq, 0, q0, h, b, bar);
+      if (SPLIT) tc::tma_load_4d(st + SM::sql, &tql, 0, q0, h, b, bar);
+      tc::tma_load_4d(st + SM::sdy, &tdy, 0, q0, h, b, bar);
+    };
+    if (issuer) {
+      tc::mbar_expect_tx(&bars[QB_KV], (SPLIT ? 3 : 2) * kTileK);
+      tc::tma_load_4d(smem + SM::kh, &tk, 0, k0, hk, b, &bars[QB_KV]);
+      if (SPLIT) tc::tma_load_4d(smem + SM::kl, &tkl, 0, k0, hk, b, &bars[QB_KV]);
+      tc::tma_load_4d(smem + SM::v, &tv, 0, k0, hk, b, &bars[QB_KV]);
+      load_stage(0);
+      tc::mbar_wait(&bars[QB_KV], 0, 114);
+    }
+    __syncwarp();
+    const uint32_t kh = smem_u32(smem + SM::kh), kl = smem_u32(smem + SM::kl),
+                   va = smem_u32(smem + SM::v), qh = smem_u32(smem + SM::st + SM::sq),
+                   ql = smem_u32(smem + SM::st + SM::sql), dya = smem_u32(smem + SM::st + SM::sdy);
+    for (int g = 0; g < grp; ++g) {
+      for (int qv = 0; qv < 4; ++qv) {
+        const uint32_t ko = (uint32_t)(qv * kQK * 128);  // the quarter's first key row
+        if (issuer) {
+          // the previous quarter's ds has been read (one commit per quarter, four
+          // per head, so its parity is that of qv - 1; for qv = 0 the last quarter
+          // of head g - 1, waited here too so no later wait sees a stale phase)
+          if (qv > 0 || g > 0) tc::mbar_wait(&bars[QB_HALF], (uint32_t)(qv + 3) & 1u, 117);
+          // head g's tiles landed (loaded once head g - 1's MMAs were done)
+          if (qv == 0) tc::mbar_wait(&bars[QB_Q0], (uint32_t)g & 1u, 115);
+          tc::tc_fence_after();
+          constexpr uint32_t id_s = tc::idesc_bf16(kQ, kQK, 0, 0);  // K-major x K-major
+#pragma unroll
+          for (int j = 0; j < kDh / 16; ++j)
+            tc::mma_ss(tmem + kU2S, tc::sdesc(qh + 32 * j, 16, 1024),
+                       tc::sdesc(kh + ko + 32 * j, 16, 1024), id_s, j > 0);
+          if (SPLIT) {
+#pragma unroll
+            for (int j = 0; j < kDh / 16; ++j)
+              tc::mma_ss(tmem + kU2S, tc::sdesc(qh + 32 * j, 16, 1024),
+                         tc::sdesc(kl + ko + 32 * j, 16, 1024), id_s, 1u);
+#pragma unroll
+            for (int j = 0; j < kDh / 16; ++j)
+              tc::mma_ss(tmem + kU2S, tc::sdesc(ql + 32 * j, 16, 1024),
+                         tc::sdesc(kh + ko + 32 * j, 16, 1024), id_s, 1u);
+          }
+#pragma unroll
+          for (int j = 0; j < kDh / 16; ++j)
+            tc::mma_ss(tmem + kU2Dp, tc::sdesc(dya + 32 * j, 16, 1024),
+                       tc::sdesc(va + ko + 32 * j, 16, 1024), id_s, j > 0);
+          tc::mma_commit(&bars[QB_SD]);
+        }
+        __syncwarp();
+        tc::named_bar_sync(NB_PREADY, kCtaThreads);  // this quarter's ds in TMEM
+        if (issuer) {
+          tc::tc_fence_after();
+          constexpr uint32_t id_o = tc::idesc_bf16(kQ, kDh, 0, 1);  // TMEM x MN-major
+          // keys 16 j.. of the quarter: packed columns 32 (j / 2) + 8 (j % 2)
+#pragma unroll
+          for (int j = 0; j < kQK / 16; ++j)
+            tc::mma_ts(tmem + kU2Dq, tmem + kU2Ds + 32 * (j >> 1) + 8 * (j & 1),
+                       tc::sdesc(kh + ko + 2048 * j, kTileK, 1024), id_o,
+                       (qv > 0 || j > 0) ? 1u : 0u);
+          tc::mma_commit(&bars[QB_HALF]);
+          if (qv == 3) {
+            tc::mma_commit(&bars[QB_DQ]);
+            if (g + 1 < grp) {
+              tc::mbar_wait(&bars[QB_DQ], (uint32_t)g & 1u, 118);  // the stage's last reader
+              load_stage(g + 1);
+            }
+          }
+        }
+        __syncwarp();
+      }
+    }
+  } else {
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = 32 * qd + lane, i = q0 + r;  // this thread's query row
+    const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
+    for (int g = 0; g < grp; ++g) {
+      const uint32_t ph = (uint32_t)g & 1u;
+      const size_t row = ((size_t)b * H + hk * grp + g) * L + i;
+      const float lse_i = i < L ? lse[row] : 0.f, dl_i = i < L ? delta[row] : 0.f;
+      for (int qv = 0; qv < 4; ++qv) {
+        tc::mbar_wait(&bars[QB_SD], (uint32_t)qv & 1u, 119);  // four phases per head
+        tc::tc_fence_after();
+        // columns [32 hf, 32 hf + 32) of this quarter (keys t = k0 + 64 qv + c).
+        // The bf16 ds of 16-column chunk k goes to packed columns 32 hf + 8 k,
+        // inside the score columns this thread has already read (chunk 0), so no
+        // other warp's columns are touched and no barrier is needed.
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int c0 = 32 * hf + 16 * k;
+          float sv[16], dpv[16];
+          tc::tmem_ld16(trow + kU2S + c0, sv);
+          tc::tmem_ld16(trow + kU2Dp + c0, dpv);
+          tc::tmem_wait_ld();
+          uint32_t dk8[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float d2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int t = k0 + kQK * qv + c0 + 2 * j + e;
+              const bool ok = t <= i && t > i - W && t >= 0 && i < L;
+              const float p = ok ? __expf(sv[2 * j + e] * scale - lse_i) : 0.f;
+              d2[e] = p * (dpv[2 * j + e] - dl_i);
+            }
+            dk8[j] = pack_bf16(d2[0], d2[1]);
+          }
+          tc::tmem_st8(trow + kU2Ds + 32 * hf + 8 * k, dk8);
+        }
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        tc::named_bar_arrive(NB_PREADY, kCtaThreads);
+      }
+      tc::mbar_wait(&bars[QB_DQ], ph, 120);
+      tc::tc_fence_after();
+      float o[32];
+      tc::tmem_ld32(trow + kU2Dq + 32 * hf, o);  // this warp's 32 columns of dq
+      tc::tmem_wait_ld();
+      if (i < L) store_grad32(dq, row * kDh + 32 * hf, o, scale, gdt);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kU2Cols);
+  }
+}
+
+// dk / dv for 64 < W <= 128: one CTA of 9 warps per 128 key rows [k0, k0 + 128)
+// of one (batch row, key/value head). The query rows that see them,
+// [k0, k0 + 256), come as items of 64 rows, four per query head, each with its
+// q (q_lo) and dy tiles in one of two shared-memory stages:
+//   warp 8 : s^T = k q^T (hi / lo terms), dp^T = v dy^T -> TMEM [128 x 64]
+//            each; then dv += p^T dy and dk += ds^T q_hi with p^T, ds^T from
+//            TMEM, summed over the items and the group's heads
+//   8 warps: key row t = TMEM lane t, 32 of the item's 64 query columns each
+// 256 TMEM columns and at most 98 KB of shared memory: two CTAs per SM.
+constexpr int kIQ = 64;  // query rows per item
+template <bool SPLIT>
+struct Dkv128Smem {
+  static constexpr size_t KT = kBK * 128, QT = kIQ * 128;
+  static constexpr size_t kh = 0, kl = kh + KT, v = kl + (SPLIT ? KT : 0), st = v + KT;
+  static constexpr size_t sq = 0, sql = QT, sdy = sql + (SPLIT ? QT : 0), sbytes = sdy + QT;
+  static constexpr size_t rows = st + 2 * sbytes;  // [2 stages][lse | delta][64] fp32
+  static constexpr size_t bars = rows + 2 * 2 * kIQ * 4, slot = bars + 64, bytes = slot + 16;
+};
+// TMEM: s^T [0, 64) with p^T (bf16 pairs) over it in [0, 16) and [32, 48);
+// dp^T [64, 128) with ds^T over it in [64, 80) and [96, 112); dv [128, 192);
+// dk [192, 256)
+constexpr uint32_t kV2S = 0, kV2P = 0, kV2Ds = 64, kV2Dp = 64, kV2Dv = 128, kV2Dk = 192,
+                   kV2Cols = 256;
+
+template <bool SPLIT>
+__global__ void __launch_bounds__(kCtaThreads, 2)
+swa_bwd_dkv_tc128_kernel(const __grid_constant__ CUtensorMap tq,
+                         const __grid_constant__ CUtensorMap tql,
+                         const __grid_constant__ CUtensorMap tdy,
+                         const __grid_constant__ CUtensorMap tk,
+                         const __grid_constant__ CUtensorMap tkl,
+                         const __grid_constant__ CUtensorMap tv, const float* __restrict__ lse,
+                         const float* __restrict__ delta, int W, float scale, int H, int grp,
+                         int L, int nkt, void* __restrict__ dk, void* __restrict__ dv, int gdt) {
+  using SM = Dkv128Smem<SPLIT>;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 83u);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::bars);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + SM::slot);
+  float* rows = reinterpret_cast<float*>(smem + SM::rows);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kt = blockIdx.x % nkt, bk = blockIdx.x / nkt;
+  const int Hkv = H / grp, b = bk / Hkv, hk = bk - b * Hkv;
+  const int k0 = kt * kBK;
+  const int nit = 4 * grp;  // items: (head it / 4, query rows k0 + 64 (it % 4))
+  constexpr uint32_t kTileK = kBK * 128, kTileQ = kIQ * 128;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int j = 0; j < 5; ++j) tc::mbar_init(&bars[j], 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == 8) {
+    tc::tmem_alloc(tslot, kV2Cols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 8) {
+    const bool issuer = lane == 0;
+    auto load_stage = [&](int it) {  // item it's query / dy rows into stage it & 1
+      const int h = hk * grp + (it >> 2), qr = k0 + kIQ * (it & 3);
+      unsigned char* st = smem + SM::st + (it & 1) * SM::sbytes;
+      uint64_t* bar = &bars[DB_Q0 + (it & 1)];
+      tc::mbar_expect_tx(bar, (SPLIT ? 3 : 2) * kTileQ);
+      tc::tma_load_4d(st + SM::sq, &tq, 0, qr, h, b, bar);
+      if (SPLIT) tc::tma_load_4d(st + SM::sql, &tql, 0, qr, h, b, bar);
+      tc::tma_load_4d(st + SM::sdy, &tdy, 0, qr, h, b, bar);
+    };
+    if (issuer) {
+      tc::mbar_expect_tx(&bars[DB_KV], (SPLIT ? 3 : 2) * kTileK);
+      tc::tma_load_4d(smem + SM::kh, &tk, 0, k0, hk, b, &bars[DB_KV]);
+      if (SPLIT) tc::tma_load_4d(smem + SM::kl, &tkl, 0, k0, hk, b, &bars[DB_KV]);
+      tc::tma_load_4d(smem + SM::v, &tv, 0, k0, hk, b, &bars[DB_KV]);
+      load_stage(0);
+      load_stage(1);
+      tc::mbar_wait(&bars[DB_KV], 0, 121);
+    }
+    __syncwarp();
+    for (int it = 0; it < nit; ++it) {
+      const uint32_t ph = (uint32_t)it & 1u;
+      unsigned char* st = smem + SM::st + (it & 1) * SM::sbytes;
+      if (issuer) {
+        tc::mbar_wait(&bars[DB_Q0 + (it & 1)], (uint32_t)(it >> 1) & 1u, 122);
+        if (it > 0) tc::mbar_wait(&bars[DB_PD], ph ^ 1u, 123);  // p / ds of item it - 1 read
+        tc::tc_fence_after();
+        constexpr uint32_t id_s = tc::idesc_bf16(kBK, kIQ, 0, 0);  // K-major x K-major
+        const uint32_t kh = smem_u32(smem + SM::kh), kl = smem_u32(smem + SM::kl),
+                       va = smem_u32(smem + SM::v), qh = smem_u32(st + SM::sq),
+                       ql = smem_u32(st + SM::sql), dya = smem_u32(st + SM::sdy);
+#pragma unroll
+        for (int j = 0; j < kDh / 16; ++j)
+          tc::mma_ss(tmem + kV2S, tc::sdesc(kh + 32 * j, 16, 1024),
+                     tc::sdesc(qh + 32 * j, 16, 1024), id_s, j > 0);
+        if (SPLIT) {
+#pragma unroll
+          for (int j = 0; j < kDh / 16; ++j)
+            tc::mma_ss(tmem + kV2S, tc::sdesc(kh + 32 * j, 16, 1024),
+                       tc::sdesc(ql + 32 * j, 16, 1024), id_s, 1u);
+#pragma unroll
+          for (int j = 0; j < kDh / 16; ++j)
+            tc::mma_ss(tmem + kV2S, tc::sdesc(kl + 32 * j, 16, 1024),
+                       tc::sdesc(qh + 32 * j, 16, 1024), id_s, 1u);
+        }
+#pragma unroll
+        for (int j = 0; j < kDh / 16; ++j)
+          tc::mma_ss(tmem + kV2Dp, tc::sdesc(va + 32 * j, 16, 1024),
+                     tc::sdesc(dya + 32 * j, 16, 1024), id_s, j > 0);
+        tc::mma_commit(&bars[DB_SD]);
+      }
+      __syncwarp();
+      tc::named_bar_sync(NB_PREADY, kCtaThreads);  // p^T and ds^T in TMEM
+      if (issuer) {
+        tc::tc_fence_after();
+        constexpr uint32_t id_o = tc::idesc_bf16(kBK, kDh, 0, 1);  // TMEM x MN-major
+        const uint32_t qh = smem_u32(st + SM::sq), dya = smem_u32(st + SM::sdy);
+        // query rows 16 j.. of the item: packed columns 32 (j / 2) + 8 (j % 2)
+#pragma unroll
+        for (int j = 0; j < kIQ / 16; ++j)
+          tc::mma_ts(tmem + kV2Dv, tmem + kV2P + 32 * (j >> 1) + 8 * (j & 1),
+                     tc::sdesc(dya + 2048 * j, kTileQ, 1024), id_o, (it > 0 || j > 0) ? 1u : 0u);
+#pragma unroll
+        for (int j = 0; j < kIQ / 16; ++j)
+          tc::mma_ts(tmem + kV2Dk, tmem + kV2Ds + 32 * (j >> 1) + 8 * (j & 1),
+                     tc::sdesc(qh + 2048 * j, kTileQ, 1024), id_o, (it > 0 || j > 0) ? 1u : 0u);
+        tc::mma_commit(&bars[DB_PD]);
+        if (it + 2 < nit) {
+          tc::mbar_wait(&bars[DB_PD], ph, 124);  // stage it & 1 read by every MMA of item it
+          load_stage(it + 2);
+        }
+      }
+      __syncwarp();
+    }
+  } else {
+    const int qd = warp & 3, hf = warp >> 2;
+    const int r = 32 * qd + lane, t = k0 + r;  // this thread's key row
+    const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
+    for (int it = 0; it < nit; ++it) {
+      const uint32_t ph = (uint32_t)it & 1u;
+      const int g = it >> 2, qr = k0 + kIQ * (it & 3);
+      const size_t bh = (size_t)b * H + hk * grp + g;
+      float* rl = rows + (it & 1) * 2 * kIQ;  // lse, then delta, of query rows qr + c
+      for (int c = tid; c < kIQ; c += kThreads) {
+        const int i = qr + c;
+        rl[c] = i < L ? lse[bh * L + i] : 0.f;
+        rl[kIQ + c] = i < L ? delta[bh * L + i] : 0.f;
+      }
+      tc::named_bar_sync(NB_ROWS, kThreads);
+      tc::mbar_wait(&bars[DB_SD], ph, 125);
+      tc::tc_fence_after();
+      // p and ds of columns [32 hf, 32 hf + 32). Chunk k's bf16 p goes to packed
+      // columns 32 hf + 8 k over s^T and its ds to the same columns over dp^T,
+      // inside what this thread has already read (chunk 0): no other warp's
+      // columns are touched and no barrier is needed.
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        float sv[16], dpv[16];
+        tc::tmem_ld16(trow + kV2S + 32 * hf + 16 * k, sv);
+        tc::tmem_ld16(trow + kV2Dp + 32 * hf + 16 * k, dpv);
+        tc::tmem_wait_ld();
+        uint32_t pk[8], dk8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float p2[2], d2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int c = 32 * hf + 16 * k + 2 * j + e, i = qr + c;
+            const bool ok = i >= t && i < t + W && i < L && t < L;
+            const float p = ok ? __expf(sv[2 * j + e] * scale - rl[c]) : 0.f;
+            p2[e] = p;
+            d2[e] = p * (dpv[2 * j + e] - rl[kIQ + c]);
+          }
+          pk[j] = pack_bf16(p2[0], p2[1]);
+          dk8[j] = pack_bf16(d2[0], d2[1]);
+        }
+        tc::tmem_st8(trow + kV2P + 32 * hf + 8 * k, pk);
+        tc::tmem_st8(trow + kV2Ds + 32 * hf + 8 * k, dk8);
+      }
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      tc::named_bar_arrive(NB_PREADY, kCtaThreads);
+    }
+    // dv (warps of half 0) and dk (half 1) of this key row, summed over the items
+    tc::mbar_wait(&bars[DB_PD], (uint32_t)(nit - 1) & 1u, 126);
+    tc::tc_fence_after();
+    const size_t orow = ((size_t)bk * L + t) * kDh;
+#pragma unroll 1
+    for (int db = 0; db < 2; ++db) {
+      float o[32];
+      tc::tmem_ld32(trow + (hf ? kV2Dk : kV2Dv) + 32 * db, o);
+      tc::tmem_wait_ld();
+      if (t < L) store_grad32(hf ? dk : dv, orow + 32 * db, o, hf ? scale : 1.f, gdt);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kV2Cols);
+  }
+}
+
 // Tensor maps of the backward operands ([B, H or Hkv, L, 64] contiguous bf16);
 // false when one cannot be built.
 bool bwd_maps(const bf16* q, const bf16* ql, const bf16* dy, const bf16* k, const bf16* kl,
@@ -1601,6 +2228,72 @@ int ensure_tc_smem(Kern kern, size_t bytes, bool* done) {
     done[dev] = true;
   }
   return LZ_OK;
+}
+
+// The window 65 ... 128 forward allocates all 512 TMEM columns; it asks for at
+// least this much shared memory, so a second CTA never shares its SM and waits
+// inside the TMEM allocation.
+constexpr size_t kOnePerSm = 120 * 1024;
+
+int swa_fwd_tc128(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
+                  const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B,
+                  int H, int Hkv, int L, cudaStream_t st) {
+  const long long sl = kDh, sh = (long long)L * kDh;
+  const bool split = ql != nullptr;
+  CUtensorMap mq, mk, mv, mql, mkl;
+  if (!make_tc_map(&mq, q, L, H, B, H * sh, sh, sl, kQ) ||
+      !make_tc_map(&mk, k, L, Hkv, B, Hkv * sh, sh, sl, kNK2) ||
+      !make_tc_map(&mv, v, L, Hkv, B, Hkv * sh, sh, sl, kNK2))
+    return LZ_ERR_UNSUPPORTED;
+  if (split) {
+    if (!make_tc_map(&mql, ql, L, H, B, H * sh, sh, sl, kQ) ||
+        !make_tc_map(&mkl, kl, L, Hkv, B, Hkv * sh, sh, sl, kNK2))
+      return LZ_ERR_UNSUPPORTED;
+  } else {
+    mql = mq, mkl = mk;
+  }
+  auto kern = split ? swa_fwd_tc128_kernel<true> : swa_fwd_tc128_kernel<false>;
+  const size_t smem = std::max(Fwd128Smem::bytes, kOnePerSm);
+  static bool done[2][64] = {{false}};
+  const int rc = ensure_tc_smem(kern, smem, done[split]);
+  if (rc) return rc;
+  const int nqb = ceil_div(L, kQ);
+  kern<<<(unsigned)((long long)B * Hkv * nqb), kThreads, smem, st>>>(
+      mq, mk, mv, mql, mkl, meta, n_meta, W, kLog2e / sqrtf((float)kDh), H, H / Hkv, L, nqb, y,
+      sv.lse, sv.y32);
+  count_launches(1);
+  return check_launch("swa_fwd_tc128_kernel");
+}
+
+int swa_bwd_dq_tc128(const CUtensorMap* m, bool split, const float* lse, const float* delta,
+                     int W, void* dq, int gdt, int B, int H, int Hkv, int L, cudaStream_t st) {
+  auto kern = split ? swa_bwd_dq_tc128_kernel<true> : swa_bwd_dq_tc128_kernel<false>;
+  const size_t smem = split ? Dq128Smem<true>::bytes : Dq128Smem<false>::bytes;
+  static bool done[2][64] = {{false}};
+  const int rc = ensure_tc_smem(kern, smem, done[split]);
+  if (rc) return rc;
+  const int nqb = ceil_div(L, kQ);
+  kern<<<(unsigned)((long long)B * Hkv * nqb), kCtaThreads, smem, st>>>(
+      m[0], m[1], m[2], m[3], m[4], m[5], lse, delta, W, 1.f / sqrtf((float)kDh), H, H / Hkv, L,
+      nqb, dq, gdt);
+  count_launches(1);
+  return check_launch("swa_bwd_dq_tc128_kernel");
+}
+
+int swa_bwd_dkv_tc128(const CUtensorMap* m, bool split, const float* lse, const float* delta,
+                      int W, void* dk, void* dv, int gdt, int B, int H, int Hkv, int L,
+                      cudaStream_t st) {
+  auto kern = split ? swa_bwd_dkv_tc128_kernel<true> : swa_bwd_dkv_tc128_kernel<false>;
+  const size_t smem = split ? Dkv128Smem<true>::bytes : Dkv128Smem<false>::bytes;
+  static bool done[2][64] = {{false}};
+  const int rc = ensure_tc_smem(kern, smem, done[split]);
+  if (rc) return rc;
+  const int nkt = ceil_div(L, kBK);
+  kern<<<(unsigned)((long long)B * Hkv * nkt), kCtaThreads, smem, st>>>(
+      m[0], m[1], m[2], m[3], m[4], m[5], lse, delta, W, 1.f / sqrtf((float)kDh), H, H / Hkv, L,
+      nkt, dk, dv, gdt);
+  count_launches(1);
+  return check_launch("swa_bwd_dkv_tc128_kernel");
 }
 
 }  // namespace
@@ -1636,8 +2329,10 @@ int swa_rope_fwd_tc(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st) {
 int swa_fwd_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
                const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B, int H,
                int Hkv, int L, int D, cudaStream_t st) {
-  if (!swa_tc_enabled() || D != kDh || W < 1 || W > kNK - kQ) return LZ_ERR_UNSUPPORTED;
+  if (!swa_tc_enabled() || D != kDh || W < 1 || W > kH2) return LZ_ERR_UNSUPPORTED;
   if (!aligned16(y) || (sv.y32 && !aligned16(sv.y32))) return LZ_ERR_UNSUPPORTED;
+  if (W > kNK - kQ)
+    return swa_fwd_tc128(q, k, v, ql, kl, meta, n_meta, W, y, sv, B, H, Hkv, L, st);
   const long long sl = kDh, sh = (long long)L * kDh;
   CUtensorMap mq, mk, mv, mql, mkl;
   if (!make_tc_map(&mq, q, L, H, B, H * sh, sh, sl, kQ) ||
@@ -1680,9 +2375,13 @@ int swa_fwd_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, cons
 int swa_bwd_dkv_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
                    const bf16* dy, const float* lse, const float* delta, int W, void* dk,
                    void* dv, int gdt, int B, int H, int Hkv, int L, int D, cudaStream_t st) {
-  if (!swa_tc_enabled() || D != kDh || W < 1 || W > kBQ - kBK) return LZ_ERR_UNSUPPORTED;
+  if (!swa_tc_enabled() || D != kDh || W < 1 || W > kH2) return LZ_ERR_UNSUPPORTED;
   if (!aligned16(dk) || !aligned16(dv)) return LZ_ERR_UNSUPPORTED;
   CUtensorMap m[6];
+  if (W > kBQ - kBK) {
+    if (!bwd_maps(q, ql, dy, k, kl, v, B, H, Hkv, L, kIQ, kBK, m)) return LZ_ERR_UNSUPPORTED;
+    return swa_bwd_dkv_tc128(m, ql != nullptr, lse, delta, W, dk, dv, gdt, B, H, Hkv, L, st);
+  }
   if (!bwd_maps(q, ql, dy, k, kl, v, B, H, Hkv, L, kBQ, kBK, m)) return LZ_ERR_UNSUPPORTED;
   const bool split = ql != nullptr;
   const int nkt = ceil_div(L, kBK);
@@ -1716,9 +2415,13 @@ int swa_bwd_dkv_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, 
 int swa_bwd_dq_tc(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
                   const bf16* dy, const float* lse, const float* delta, int W, void* dq, int gdt,
                   int B, int H, int Hkv, int L, int D, cudaStream_t st) {
-  if (!swa_tc_enabled() || D != kDh || W < 1 || W > kNK - kQ) return LZ_ERR_UNSUPPORTED;
+  if (!swa_tc_enabled() || D != kDh || W < 1 || W > kH2) return LZ_ERR_UNSUPPORTED;
   if (!aligned16(dq)) return LZ_ERR_UNSUPPORTED;
   CUtensorMap m[6];
+  if (W > kNK - kQ) {
+    if (!bwd_maps(q, ql, dy, k, kl, v, B, H, Hkv, L, kQ, kNK2, m)) return LZ_ERR_UNSUPPORTED;
+    return swa_bwd_dq_tc128(m, ql != nullptr, lse, delta, W, dq, gdt, B, H, Hkv, L, st);
+  }
   if (!bwd_maps(q, ql, dy, k, kl, v, B, H, Hkv, L, kQ, kNK, m)) return LZ_ERR_UNSUPPORTED;
   const bool split = ql != nullptr;
   if (!split) {  // bf16 operands: the persistent kernel, one CTA per SM

@@ -176,6 +176,16 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
                "r"(bytes)
                : "memory");
 }
+// L2 prefetch of the 3-D tile box of `map` at (c0, c1, c2) (coordinates
+// innermost first, as the tile loads); no completion to wait for. Parts of the
+// box outside the tensor are skipped.
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c0, int c1,
+                                                   int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];\n" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

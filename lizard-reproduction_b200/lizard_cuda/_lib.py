@@ -33,6 +33,7 @@ _SIGNATURES = {
     "lz_gla_set_schedule": (_c_int, [_c_int]),
     "lz_gla_set_split_out_tc": (_c_int, [_c_int]),
     "lz_gla_set_fwd_tc64": (_c_int, [_c_int]),
+    "lz_gla_set_bwd_prefetch": (_c_int, [_c_int]),
     "lz_gla_fwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_size, _vp, _c_size]
                    + [_c_int] * 6 + [_vp]),
     "lz_gla_bwd": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _c_size, _vp, _vp, _vp, _vp, _c_int,

@@ -441,6 +441,29 @@ def test_gla_f128_backward_is_deterministic():
             assert_grad(got[sl], r, f"F=D=128 [{b_},{h}] {n}")
 
 
+@pytest.mark.parametrize("Fd,per_head,B,L", [(128, True, 4, 1100), (64, False, 8, 2048)])
+def test_gla_chunk_gradient_prefetch_changes_nothing(schedule, Fd, per_head, B, L):
+    """The per-chunk gradient kernel's L2 prefetch of the next CTA's operands
+    (one SM count ahead in the grid) moves data only: at shapes with several
+    waves of CTAs (a ragged last chunk at F = D = 128; F = D = 64 on the
+    64-token states) the output and every gradient are bit-identical with the
+    prefetch on and off."""
+    from lizard_cuda import _lib as binding
+    lib = binding.load()
+    fq, fk, v, lg, dy = baseline_inputs(B, 32, L, Fd, Fd, per_head=per_head, seed=57)
+    prev = lib.lz_gla_set_bwd_prefetch(1)
+    try:
+        y1, g1 = cuda_gla(fq, fk, v, lg, dy)
+        lib.lz_gla_set_bwd_prefetch(0)
+        y0, g0 = cuda_gla(fq, fk, v, lg, dy)
+        torch.cuda.synchronize()
+    finally:
+        lib.lz_gla_set_bwd_prefetch(prev)
+    assert torch.equal(y0, y1)
+    for n, a, b in zip(GRAD_NAMES, g0, g1):
+        assert torch.equal(a, b), f"{n} differs with the prefetch on and off"
+
+
 def test_no_kernel_wait_timed_out():
     """Every bounded wait inside the tensor-core kernels completed."""
     from lizard_cuda import _lib

@@ -1,5 +1,5 @@
-"""The tensor-core SWA forward (tcgen05 + TMEM + TMA; head dim 64, window
-<= 64) against the CPU oracle of the reference's attention
+"""The tensor-core SWA kernels (tcgen05 + TMEM + TMA; head dim 64, windows
+<= 64 and 65 ... 128) against the CPU oracle of the reference's attention
 (src/lizard_attention.py:34-44 on repeat_interleaved keys / values), through
 the public swa / swa_rope entry points, forward and backward; and against the
 64-row warp-MMA kernels it replaces at those shapes."""
@@ -156,3 +156,74 @@ def test_swa_rope_tc_reads_projections_in_place():
     assert_output(y, ref.float(), "swa_rope tc y")
     for t, r, n in zip(lv, rl, ("dq", "dk", "dv", "dmeta")):
         assert_grad(t.grad, r.grad.float(), f"swa_rope tc {n}")
+
+
+# windows 65 ... 128 (the reference's training configs use 128): the wider
+# tensor-core kernels (128 query rows against 256 keys; dq in two key halves;
+# dk / dv over two 128-row query items per head)
+@pytest.mark.parametrize("B,H,Hkv,L,W,n_meta,dtype", [
+    (1, 2, 2, 1, 128, 4, torch.bfloat16),     # one token
+    (2, 4, 2, 127, 128, 4, torch.bfloat16),   # one partial 128-row block
+    (1, 4, 1, 300, 128, 3, torch.float32),    # fp32: residual logits; grp 4
+    (2, 2, 2, 257, 65, 4, torch.bfloat16),    # the smallest wide window
+    (1, 8, 2, 300, 100, 0, torch.bfloat16),   # no sinks, even window, grp 4
+    (1, 2, 2, 1000, 127, 2, torch.float32),   # odd window, ragged tail
+    (1, 2, 2, 2048, 128, 4, torch.bfloat16),  # config-3 length
+])
+def test_swa_tc_wide_window_matches_oracle(B, H, Hkv, L, W, n_meta, dtype):
+    test_swa_tc_matches_oracle(B, H, Hkv, L, W, n_meta, dtype)
+
+
+def _cuda_kernel_names(fn):
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return {e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA}
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_swa_tc_wide_window_runs_tensor_core_kernels(dtype):
+    """Window 128: a training step runs the wide tensor-core forward, dq and
+    dk / dv kernels, and agrees with the 64-row warp-MMA kernels (switch off)
+    to bf16 rounding."""
+    import lizard_cuda
+    q, k, v, meta, dy = _inputs(2, 4, 2, 333, 128, 4, dtype, seed=6)
+    outs = []
+    for on in (1, 0):
+        old = _set_tc(on)
+        try:
+            lv = [t.detach().clone().requires_grad_() for t in (q, k, v, meta)]
+
+            def step():
+                y = lizard_cuda.swa(*lv, 128)
+                y.backward(dy)
+                outs.append((y.detach().float(), [t.grad.float() for t in lv]))
+            names = _cuda_kernel_names(step)
+            wide = {n for n in names if "tc128" in n}
+            if on:
+                assert len(wide) == 3, sorted(names)
+            else:
+                assert not wide, sorted(names)
+        finally:
+            _set_tc(old)
+    (y1, g1), (y2, g2) = outs
+    diff = (y1 - y2).abs().max().item()
+    assert diff <= 2 ** -7 * y2.abs().max().item(), diff
+    for a, b in zip(g1, g2):
+        assert (a - b).abs().max().item() <= 2e-2 * b.abs().max().item()
+
+
+def test_swa_tc_wide_window_is_deterministic():
+    """Two identical window-128 training steps give bit-identical outputs and
+    gradients (every sum in a fixed order) at several waves of CTAs."""
+    import lizard_cuda
+    q, k, v, meta, dy = _inputs(4, 32, 8, 2048, 128, 4, torch.bfloat16, seed=9)
+    res = []
+    for _ in range(2):
+        lv = [t.detach().clone().requires_grad_() for t in (q, k, v, meta)]
+        y = lizard_cuda.swa(*lv, 128)
+        y.backward(dy)
+        res.append([y.detach()] + [t.grad for t in lv])
+    for a, b, n in zip(res[0], res[1], ("y", "dq", "dk", "dv", "dmeta")):
+        assert torch.equal(a, b), f"{n} differs between two identical steps"
