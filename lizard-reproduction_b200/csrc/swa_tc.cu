@@ -1573,38 +1573,51 @@ swa_fwd_tc_persist_kernel(const __grid_constant__ CUtensorMap tq,
 // ============================================================ windows 65 ... 128
 // The same three products for 64 < W <= 128 (the reference's own training
 // configs use window 128). A 128-row tile then sees 128 keys to its left, so
-// the tiles are wider and each kernel runs one CTA per SM:
-//   forward : 128 query rows against the 256 keys [q0 - 128, q0 + 128) in one
-//             softmax pass, s [128 x 256] and o [128 x 64] in TMEM (512
-//             columns allocated); each row warp takes 80 of the 160 columns
-//             that hold its lane quadrant's windows
-//   dq      : the 256 keys in two halves of 128, ds of a half over its scores
+// each kernel splits the wider tile to stay within 256 TMEM columns:
+//   forward : 128 query rows against the 256 keys [q0 - 128, q0 + 128) in two
+//             halves of 128, each with its own softmax pass and P V
+//             accumulator, merged at the end by the two maxima
+//   dq      : the 256 keys in four quarters of 64, ds of a quarter over its
+//             scores
 //   dk / dv : the 256 query rows [k0, k0 + 256) that can see a 128-key tile in
-//             two items of 128 rows per query head, dk and dv summed in TMEM
+//             items of 64 rows, four per query head, dk and dv summed in TMEM
 //             over the items and the group's heads
-// In the backward kernels each row warp covers a fixed 64 of the 128 columns
-// of a half (masked outside the window), so every column of the bf16
-// operands is written. Precision as the kernels above: logits from the
-// hi / lo terms, p in bf16 hi + lo for P V, bf16 p and ds in the gradients.
+// With bf16 operands two CTAs share an SM. Each row warp covers a fixed half
+// of the columns of a half / quarter / item (masked outside the window), so
+// every column of the bf16 operands is written; in the backward kernels a warp
+// writes them over score columns it has itself already read, so no barrier
+// separates the reads from the writes. Precision as the kernels above: logits
+// from the hi / lo terms, p in bf16 hi + lo for P V, bf16 p and ds in the
+// gradients.
 constexpr int kH2 = 128;            // keys left of a query tile (window <= 128)
 constexpr int kNK2 = kQ + kH2;      // 256 key rows per forward / dq tile
-constexpr int kW2Cols = 80;         // window columns per row warp in the forward
+template <bool SPLIT>
 struct Fwd128Smem {
   static constexpr size_t KT = kNK2 * 128, QT = kQ * 128;
-  static constexpr size_t kh = 0, kl = kh + KT, v = kl + KT, qh = v + KT, ql = qh + QT,
-                          red = ql + QT, bars = red + 2048, slot = bars + 32, bytes = slot + 16;
+  static constexpr size_t kh = 0, kl = kh + KT, v = kl + (SPLIT ? KT : 0), qh = v + KT,
+                          ql = qh + QT, red = ql + (SPLIT ? QT : 0), bars = red + 2048,
+                          slot = bars + 32, bytes = slot + 16;
 };
-// TMEM: s [0, 256); p hi / lo (bf16 pairs, 128 columns each) over s; o [256, 320)
-constexpr uint32_t kT2S = 0, kT2Ph = 0, kT2Pl = kNK2 / 2, kT2O = kNK2, kT2Cols = 512;
+// TMEM: s of one key half [0, 128) with p hi / lo (bf16 pairs, 64 columns
+// each) over it; o of the left half [128, 192), of the right half [192, 256)
+constexpr uint32_t kT2S = 0, kT2Ph = 0, kT2Pl = 64, kT2OA = 128, kT2OB = 192, kT2Cols = 256;
 
+// The forward takes the 256 keys in two halves of 128, [q0 - 128, q0) and
+// [q0, q0 + 128), each with its own softmax pass and P V product into its own
+// accumulator: the left half's max m_A (seeded by the sinks), then the right
+// half's p relative to m = max(m_A, its own max), and at the end
+// o = o_A 2^(m_A - m) + o_B. 256 TMEM columns and, for bf16 operands, 82 KB of
+// shared memory: two CTAs per SM. Each row warp covers 64 of a half's 128
+// columns; 16-column chunks that no row of its lane quadrant can see are
+// skipped (no TMEM load, p = 0).
 template <bool SPLIT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, SPLIT ? 1 : 2)
 swa_fwd_tc128_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tql,
                      const __grid_constant__ CUtensorMap tkl, const float* __restrict__ meta,
                      int n_meta, int W, float scale_log2, int H, int grp, int L, int nqb,
                      bf16* __restrict__ y, float* __restrict__ lse, float* __restrict__ y32) {
-  using SM = Fwd128Smem;
+  using SM = Fwd128Smem<SPLIT>;
   extern __shared__ __align__(1024) unsigned char smem[];
   if (smem_u32(smem) & 1023) {
     if (threadIdx.x == 0) atomicExch(&tc::g_timeout_flag, 0x80000000u | 85u);
@@ -1619,7 +1632,6 @@ swa_fwd_tc128_kernel(const __grid_constant__ CUtensorMap tq, const __grid_consta
   const int Hkv = H / grp, b = bk / Hkv, hk = bk - b * Hkv;
   const int q0 = qb * kQ, k0 = q0 - kH2;
   constexpr uint32_t kTileK = kNK2 * 128, kTileQ = kQ * 128;
-  constexpr int kCh = kW2Cols / 16;  // 16-column chunks per thread
 
   if (tid == 0) {
 #pragma unroll
@@ -1641,11 +1653,12 @@ swa_fwd_tc128_kernel(const __grid_constant__ CUtensorMap tq, const __grid_consta
     tc::tma_load_4d(smem + SM::qh, &tq, 0, q0, h, b, &bars[SB_Q]);
     if (SPLIT) tc::tma_load_4d(smem + SM::ql, &tql, 0, q0, h, b, &bars[SB_Q]);
   };
-  auto issue_s = [&]() {  // s = q k^T into TMEM columns [0, 256)
+  auto issue_s = [&](int hv) {  // s = q k^T of key half hv into TMEM columns [0, 128)
     tc::tc_fence_after();
-    constexpr uint32_t id_s = tc::idesc_bf16(kQ, kNK2, 0, 0);
+    constexpr uint32_t id_s = tc::idesc_bf16(kQ, 128, 0, 0);
+    const uint32_t ko = (uint32_t)(hv * 128 * 128);
     const uint32_t qh = smem_u32(smem + SM::qh), ql = smem_u32(smem + SM::ql),
-                   kh = smem_u32(smem + SM::kh), kl = smem_u32(smem + SM::kl);
+                   kh = smem_u32(smem + SM::kh) + ko, kl = smem_u32(smem + SM::kl) + ko;
 #pragma unroll
     for (int j = 0; j < kDh / 16; ++j)
       tc::mma_ss(tmem + kT2S, tc::sdesc(qh + 32 * j, 16, 1024), tc::sdesc(kh + 32 * j, 16, 1024),
@@ -1680,117 +1693,130 @@ swa_fwd_tc128_kernel(const __grid_constant__ CUtensorMap tq, const __grid_consta
   tc::mbar_wait(&bars[SB_Q], 0, 111);
   tc::tc_fence_before();
   __syncthreads();
-  if (tid == 0) issue_s();
+  if (tid == 0) issue_s(0);
 
   const int r = 32 * qd + lane, i = q0 + r;
   const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
-  // the window of row i is keys t in (i - W, i]: columns t - k0 in
-  // [32 qd + 1, 32 qd + 159] over the quadrant; this thread takes 80 of them
-  const int cw = 32 * qd + kW2Cols * hf;
+  const int imin = q0 + 32 * qd, imax = imin + 31;  // the lane quadrant's query rows
   for (int g = 0; g < grp; ++g) {
-    const uint32_t ph = (uint32_t)g & 1u;
     const bool next = g + 1 < grp;
-    tc::mbar_wait(&bars[SB_S], ph, 112);
-    tc::tc_fence_after();
-    if (tid == 0 && next) issue_q(g + 1);  // the scores have read the query tiles
-
-    float s[kCh][16];
-#pragma unroll
-    for (int k = 0; k < kCh; ++k) tc::tmem_ld16(trow + kT2S + cw + 16 * k, s[k]);
-    tc::tmem_wait_ld();
-    float mx = ms;
-#pragma unroll
-    for (int k = 0; k < kCh; ++k)
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const int t = k0 + cw + 16 * k + u;
-        const bool ok = t <= i && t > i - W && t >= 0;
-        const float x = ok ? s[k][u] * scale_log2 : -INFINITY;
-        s[k][u] = x;
-        mx = fmaxf(mx, x);
-      }
-    red[hf * kQ + r] = mx;
-    __syncthreads();
-    mx = fmaxf(mx, red[(1 - hf) * kQ + r]);
-    float l = 0.f;
-#pragma unroll
-    for (int k = 0; k < kCh; ++k) {
-      uint32_t phi[8], plo[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float p0 = tc::ex2(s[k][2 * j] - mx), p1 = tc::ex2(s[k][2 * j + 1] - mx);
-        l += p0 + p1;
-        const uint32_t hpk = pack_bf16(p0, p1);
-        phi[j] = hpk;
-        plo[j] = pack_bf16(p0 - bf16_lo(hpk), p1 - bf16_hi(hpk));
-      }
-      tc::tmem_st8(trow + kT2Ph + cw / 2 + 8 * k, phi);
-      tc::tmem_st8(trow + kT2Pl + cw / 2 + 8 * k, plo);
-    }
-    {  // p is zero outside the window: packed columns [0, 16 qd) and [16 qd + 80, 128)
-      uint32_t zero[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) zero[j] = 0u;
-      const int z0 = hf ? 16 * qd + kW2Cols : 0, z1 = hf ? kNK2 / 2 : 16 * qd;
+    float mA = ms, lA = 0.f, mrow = ms, lB = 0.f;
 #pragma unroll 1
-      for (int c = z0; c < z1; c += 8) {
-        tc::tmem_st8(trow + kT2Ph + c, zero);
-        tc::tmem_st8(trow + kT2Pl + c, zero);
-      }
-    }
-    red[2 * kQ + hf * kQ + r] = l;
-    tc::tmem_wait_st();
-    tc::tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
+    for (int hv = 0; hv < 2; ++hv) {
+      tc::mbar_wait(&bars[SB_S], (uint32_t)hv, 112);  // two score commits per head
       tc::tc_fence_after();
-      constexpr uint32_t id_o = tc::idesc_bf16(kQ, kDh, 0, 1);  // p (TMEM) x V (MN-major)
-      const uint32_t va = smem_u32(smem + SM::v);
+      if (tid == 0 && hv == 1 && next) issue_q(g + 1);  // both halves' scores read q
+      // this warp's 64 columns of the half: keys t = k0 + 128 hv + 64 hf + c
+      const int tb = k0 + 128 * hv + 64 * hf;
+      float s[4][16];
+      bool live[4];
 #pragma unroll
-      for (int j = 0; j < kNK2 / 16; ++j)
-        tc::mma_ts(tmem + kT2O, tmem + kT2Ph + 8 * j, tc::sdesc(va + 2048 * j, kTileK, 1024), id_o,
-                   j > 0);
+      for (int k = 0; k < 4; ++k) {
+        const int t0 = tb + 16 * k;
+        live[k] = !(t0 > imax || t0 + 15 <= imin - W);  // some row of the quadrant sees it
+        if (live[k]) tc::tmem_ld16(trow + kT2S + 64 * hf + 16 * k, s[k]);
+      }
+      tc::tmem_wait_ld();
+      float mx = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < kNK2 / 16; ++j)
-        tc::mma_ts(tmem + kT2O, tmem + kT2Pl + 8 * j, tc::sdesc(va + 2048 * j, kTileK, 1024), id_o,
-                   1u);
-      tc::mma_commit(&bars[SB_O]);
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const int t = tb + 16 * k + u;
+          const bool ok = live[k] && t <= i && t > i - W && t >= 0;
+          const float x = ok ? s[k][u] * scale_log2 : -INFINITY;
+          s[k][u] = x;
+          mx = fmaxf(mx, x);
+        }
+      red[hf * kQ + r] = mx;
+      __syncthreads();  // every score column read; the partner's max in red
+      mx = fmaxf(mx, red[(1 - hf) * kQ + r]);
+      // reference of this half's p: m_A (with the sinks) on the left, then
+      // m = max(m_A, the right half's max)
+      const float mref = hv == 0 ? fmaxf(ms, mx) : fmaxf(mA, mx);
+      float l = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint32_t phi[8], plo[8];
+        if (live[k]) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float p0 = tc::ex2(s[k][2 * j] - mref), p1 = tc::ex2(s[k][2 * j + 1] - mref);
+            l += p0 + p1;
+            const uint32_t hpk = pack_bf16(p0, p1);
+            phi[j] = hpk;
+            plo[j] = pack_bf16(p0 - bf16_lo(hpk), p1 - bf16_hi(hpk));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) phi[j] = plo[j] = 0u;
+        }
+        tc::tmem_st8(trow + kT2Ph + 32 * hf + 8 * k, phi);
+        tc::tmem_st8(trow + kT2Pl + 32 * hf + 8 * k, plo);
+      }
+      red[2 * kQ + hf * kQ + r] = l;
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        tc::tc_fence_after();
+        constexpr uint32_t id_o = tc::idesc_bf16(kQ, kDh, 0, 1);  // p (TMEM) x V (MN-major)
+        const uint32_t va = smem_u32(smem + SM::v) + (uint32_t)(hv * 128 * 128);
+        const uint32_t od = tmem + (hv ? kT2OB : kT2OA);
+#pragma unroll
+        for (int j = 0; j < 128 / 16; ++j)
+          tc::mma_ts(od, tmem + kT2Ph + 8 * j, tc::sdesc(va + 2048 * j, kTileK, 1024), id_o,
+                     j > 0);
+#pragma unroll
+        for (int j = 0; j < 128 / 16; ++j)
+          tc::mma_ts(od, tmem + kT2Pl + 8 * j, tc::sdesc(va + 2048 * j, kTileK, 1024), id_o, 1u);
+        tc::mma_commit(&bars[SB_O]);
+      }
+      const float lh = red[2 * kQ + r] + red[3 * kQ + r];
+      if (hv == 0) {
+        mA = mref, lA = lh;
+      } else {
+        mrow = mref, lB = lh;
+      }
+      if (hv == 1 && next) tc::mbar_wait(&bars[SB_Q], (uint32_t)(g + 1) & 1u, 111);
+      tc::mbar_wait(&bars[SB_O], (uint32_t)hv, 113);  // two P V commits per head
+      tc::tc_fence_after();
+      tc::tc_fence_before();
+      __syncthreads();  // P V done (s / p columns and the row slots free)
+      if (tid == 0 && (hv == 0 || next)) issue_s(hv ^ 1);  // right half, or the next head's left
     }
-    const float lrow = ls * exp2f(ms - mx) + red[2 * kQ + r] + red[3 * kQ + r];
-    if (next) tc::mbar_wait(&bars[SB_Q], ph ^ 1u, 111);
-    tc::mbar_wait(&bars[SB_O], ph, 113);
-    tc::tc_fence_after();
-    tc::tc_fence_before();
-    __syncthreads();  // P V done (s / p columns free), the next query tiles landed
-    if (tid == 0 && next) issue_s();
-
+    const float fa = tc::ex2(mA - mrow);  // <= 1
+    const float lrow = ls * exp2f(ms - mrow) + lA * fa + lB;
     const float inv = 1.f / lrow;
     const size_t row = ((size_t)b * H + hk * grp + g) * L + i;
-    float o[32];
-    tc::tmem_ld32(trow + kT2O + 32 * hf, o);
-    tc::tmem_wait_ld();
-    if (i < L) {
-      bf16* yr = y + row * kDh + 32 * hf;
+#pragma unroll 1
+    for (int c16 = 0; c16 < 2; ++c16) {  // this warp's 32 output columns, 16 at a time
+      const int c0 = 32 * hf + 16 * c16;
+      float oa[16], ob[16];
+      tc::tmem_ld16(trow + kT2OA + c0, oa);
+      tc::tmem_ld16(trow + kT2OB + c0, ob);
+      tc::tmem_wait_ld();
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        uint4 w;
-        w.x = pack_bf16(o[8 * q4] * inv, o[8 * q4 + 1] * inv);
-        w.y = pack_bf16(o[8 * q4 + 2] * inv, o[8 * q4 + 3] * inv);
-        w.z = pack_bf16(o[8 * q4 + 4] * inv, o[8 * q4 + 5] * inv);
-        w.w = pack_bf16(o[8 * q4 + 6] * inv, o[8 * q4 + 7] * inv);
-        reinterpret_cast<uint4*>(yr)[q4] = w;
-      }
-      if (y32) {
-        float4* d32 = reinterpret_cast<float4*>(y32 + row * kDh + 32 * hf);
+      for (int u = 0; u < 16; ++u) oa[u] = (oa[u] * fa + ob[u]) * inv;
+      if (i < L) {
+        uint4* yr = reinterpret_cast<uint4*>(y + row * kDh + c0);
 #pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4)
-          d32[q4] = make_float4(o[4 * q4] * inv, o[4 * q4 + 1] * inv, o[4 * q4 + 2] * inv,
-                                o[4 * q4 + 3] * inv);
+        for (int q4 = 0; q4 < 2; ++q4)
+          yr[q4] = make_uint4(pack_bf16(oa[8 * q4], oa[8 * q4 + 1]),
+                              pack_bf16(oa[8 * q4 + 2], oa[8 * q4 + 3]),
+                              pack_bf16(oa[8 * q4 + 4], oa[8 * q4 + 5]),
+                              pack_bf16(oa[8 * q4 + 6], oa[8 * q4 + 7]));
+        if (y32) {
+          float4* d32 = reinterpret_cast<float4*>(y32 + row * kDh + c0);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            d32[q4] = make_float4(oa[4 * q4], oa[4 * q4 + 1], oa[4 * q4 + 2], oa[4 * q4 + 3]);
+        }
       }
-      if (lse && hf == 0) lse[row] = mx * kLn2f + logf(lrow);
     }
+    if (i < L && lse && hf == 0) lse[row] = mrow * kLn2f + logf(lrow);
     tc::tc_fence_before();
-    __syncthreads();  // o and the row-sum slots are free for the next head
+    __syncthreads();  // both o accumulators read before the next head's P V
   }
   if (warp == 0) {
     tc::tc_fence_after();
@@ -2230,11 +2256,6 @@ int ensure_tc_smem(Kern kern, size_t bytes, bool* done) {
   return LZ_OK;
 }
 
-// The window 65 ... 128 forward allocates all 512 TMEM columns; it asks for at
-// least this much shared memory, so a second CTA never shares its SM and waits
-// inside the TMEM allocation.
-constexpr size_t kOnePerSm = 120 * 1024;
-
 int swa_fwd_tc128(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
                   const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B,
                   int H, int Hkv, int L, cudaStream_t st) {
@@ -2253,7 +2274,7 @@ int swa_fwd_tc128(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, c
     mql = mq, mkl = mk;
   }
   auto kern = split ? swa_fwd_tc128_kernel<true> : swa_fwd_tc128_kernel<false>;
-  const size_t smem = std::max(Fwd128Smem::bytes, kOnePerSm);
+  const size_t smem = split ? Fwd128Smem<true>::bytes : Fwd128Smem<false>::bytes;
   static bool done[2][64] = {{false}};
   const int rc = ensure_tc_smem(kern, smem, done[split]);
   if (rc) return rc;
