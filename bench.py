@@ -85,6 +85,8 @@ def parse():
     ap.add_argument("--L", type=int, help="sequence length for --case (default: the config's)")
     ap.add_argument("--schedule", choices=("auto", "walk", "split"), default="auto",
                     help="GLA schedule for --case (default: chosen per shape)")
+    ap.add_argument("--window", type=int, default=64,
+                    help="SWA window for --case cfg3-swa-train (default 64)")
     return ap.parse_args()
 
 
@@ -644,7 +646,8 @@ def decode_measure(torch, model, cfg, ids, device, steps=8, warmup=2):
 
 def secondary(torch, lizard_cuda, device, steps=50, warmup=5):
     """Config 3 (B=1, L=2048, H=32, F=D=64): GLA fwd+bwd with a per-token gate
-    and SWA fwd+bwd (window 64, 4 sinks); device ms per step.
+    and SWA fwd+bwd (window 64, 4 sinks; also window 128, the reference's
+    training setting); device ms per step.
 
     "ms" is eager (one Python call per step, host launch overhead included);
     "ms_graph" replays the same step captured in a CUDA graph, which shows the
@@ -724,9 +727,13 @@ def secondary(torch, lizard_cuda, device, steps=50, warmup=5):
           (fq, fk, v, lg))
     timed("swa_fwd_bwd_cfg3", lambda: lizard_cuda.swa(q, k, v, meta, 64).backward(dy),
           (q, k, v, meta))
+    # the reference's training configs use window 128 (configs/lizard-1b*.yaml)
+    timed("swa_fwd_bwd_cfg3_w128", lambda: lizard_cuda.swa(q, k, v, meta, 128).backward(dy),
+          (q, k, v, meta))
     with torch.no_grad():
         timed("gla_fwd_cfg3", lambda: lizard_cuda.gla(fq, fk, v, lg), ())
         timed("swa_fwd_cfg3", lambda: lizard_cuda.swa(q, k, v, meta, 64), ())
+        timed("swa_fwd_cfg3_w128", lambda: lizard_cuda.swa(q, k, v, meta, 128), ())
     return out
 
 
@@ -876,6 +883,20 @@ def reference_gpu_measure(torch, lizard_cuda, device, budget_s=420.0):
             ref_kernels.swa(q, k, v, meta, 64)
     record("cfg3_swa_fwd", "swa fwd B=1 H=32 L=2048 D=64, window 64, 4 sinks",
            swa_fwd_ours, swa_fwd_ref)
+    # window 128, the reference's training configs (configs/lizard-1b*.yaml)
+    record("cfg3_swa_w128_fwd_bwd", "swa fwd+bwd B=1 H=32 L=2048 D=64, window 128, 4 sinks",
+           lambda: lizard_cuda.swa(*lo, 128).backward(dy),
+           lambda: ref_kernels.swa(*lr, 128).backward(dy), lo, lr)
+
+    def swa128_fwd_ours():
+        with torch.no_grad():
+            lizard_cuda.swa(q, k, v, meta, 128)
+
+    def swa128_fwd_ref():
+        with torch.no_grad():
+            ref_kernels.swa(q, k, v, meta, 128)
+    record("cfg3_swa_w128_fwd", "swa fwd B=1 H=32 L=2048 D=64, window 128, 4 sinks",
+           swa128_fwd_ours, swa128_fwd_ref)
     del q, k, v, meta, dy, lo, lr
     gla_case("cfg4_L2048_fwd_bwd", 16, 32, 2048, 128, True, True)
     gla_case("cfg4_L8192_fwd_bwd", 16, 32, 8192, 128, True, True)
@@ -1167,7 +1188,7 @@ def run_case(args, torch):
     else:
         args_in = [torch.randn(shape, generator=g, device=dev).bfloat16(),
                    torch.randn(shape, generator=g, device=dev).bfloat16(), v, meta]
-        call = lambda q, k, vv, m: lizard_cuda.swa(q, k, vv, m, 64)  # noqa: E731
+        call = lambda q, k, vv, m: lizard_cuda.swa(q, k, vv, m, args.window)  # noqa: E731
     leaves = [t.detach().requires_grad_() for t in args_in] if train else args_in
 
     def step():
