@@ -2256,6 +2256,8 @@ int ensure_tc_smem(Kern kern, size_t bytes, bool* done) {
   return LZ_OK;
 }
 
+constexpr size_t kTwoPerSm = 80 * 1024;
+
 int swa_fwd_tc128(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
                   const float* meta, int n_meta, int W, bf16* y, const SwaSaved& sv, int B,
                   int H, int Hkv, int L, cudaStream_t st) {
@@ -2305,7 +2307,10 @@ int swa_bwd_dkv_tc128(const CUtensorMap* m, bool split, const float* lse, const 
                       int W, void* dk, void* dv, int gdt, int B, int H, int Hkv, int L,
                       cudaStream_t st) {
   auto kern = split ? swa_bwd_dkv_tc128_kernel<true> : swa_bwd_dkv_tc128_kernel<false>;
-  const size_t smem = split ? Dkv128Smem<true>::bytes : Dkv128Smem<false>::bytes;
+  // 256 TMEM columns per CTA: at most two CTAs per SM, or a third would wait
+  // inside the TMEM allocation; the bf16 variant's 67 KB alone would let three in
+  const size_t smem =
+      std::max(split ? Dkv128Smem<true>::bytes : Dkv128Smem<false>::bytes, kTwoPerSm);
   static bool done[2][64] = {{false}};
   const int rc = ensure_tc_smem(kern, smem, done[split]);
   if (rc) return rc;
