@@ -426,8 +426,9 @@ int lz_swa_bwd_gqa(const void* q, const void* k, const void* v,
  * the rotated operands that lz_swa_bwd_gqa takes. Returns LZ_ERR_UNSUPPORTED
  * without launching when D is not 32, 64 or 128, a stride or base is not
  * 16-byte aligned, the tiles do not fit in shared memory (fp32 at D = 128), or
- * the projections are fp32 at the tensor-core shape; rotate first then (the
- * two passes reach the same forward kernel). The reference rotates with torch
+ * the projections are fp32 at the tensor-core shape, or (tensor cores on)
+ * D = 64 with a window of 65 to 128, whose tensor-core forward has no fused
+ * rotation; rotate first then (the two passes reach the same forward kernel). The reference rotates with torch
  * ops in its caller (src/lizard_attention.py:87-88). */
 int lz_swa_rope_fwd(const void* q, const void* k, const void* v, int x_dtype,
                     long long q_sb, long long q_sh, long long q_sl,

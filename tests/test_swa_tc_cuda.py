@@ -159,8 +159,8 @@ def test_swa_rope_tc_reads_projections_in_place():
 
 
 # windows 65 ... 128 (the reference's training configs use 128): the wider
-# tensor-core kernels (128 query rows against 256 keys; dq in two key halves;
-# dk / dv over two 128-row query items per head)
+# tensor-core kernels (128 query rows against 256 keys in two halves; dq in four
+# 64-key quarters; dk / dv over four 64-row query items per head)
 @pytest.mark.parametrize("B,H,Hkv,L,W,n_meta,dtype", [
     (1, 2, 2, 1, 128, 4, torch.bfloat16),     # one token
     (2, 4, 2, 127, 128, 4, torch.bfloat16),   # one partial 128-row block
@@ -227,3 +227,37 @@ def test_swa_tc_wide_window_is_deterministic():
         res.append([y.detach()] + [t.grad for t in lv])
     for a, b, n in zip(res[0], res[1], ("y", "dq", "dk", "dv", "dmeta")):
         assert torch.equal(a, b), f"{n} differs between two identical steps"
+
+
+def test_swa_rope_wide_window_matches_oracle():
+    """The layer's fused call at window 128 (the reference's training setting):
+    bf16 projections read as heads, RoPE inside, GQA 8 / 2, 4 sinks; forward
+    and backward against the oracle on the rotated inputs."""
+    import lizard_cuda
+    g = torch.Generator(device=DEV).manual_seed(12)
+    B, L, H, Hkv, D, W = 2, 400, 8, 2, 64, 128
+    qp = torch.randn(B, L, H * D, generator=g, device=DEV).bfloat16()
+    kp = torch.randn(B, L, Hkv * D, generator=g, device=DEV).bfloat16()
+    vp = torch.randn(B, L, Hkv * D, generator=g, device=DEV).bfloat16()
+    meta = torch.randn(4, generator=g, device=DEV)
+    dy = torch.randn(B, H, L, D, generator=g, device=DEV).bfloat16()
+    cos, sin = (t.to(DEV).expand(B, L, D) for t in orc.rotary_tables(L, D, 5e5))
+    lv = [t.detach().clone().requires_grad_() for t in (qp, kp, vp, meta)]
+    q = lv[0].view(B, L, H, D).transpose(1, 2)
+    k = lv[1].view(B, L, Hkv, D).transpose(1, 2)
+    v = lv[2].view(B, L, Hkv, D).transpose(1, 2)
+    y = lizard_cuda.swa_rope(q, k, v, cos, sin, lv[3], W)
+    y.backward(dy)
+    with torch.no_grad():
+        y_inf = lizard_cuda.swa_rope(q, k, v, cos, sin, lv[3], W)
+    assert torch.equal(y, y_inf)
+    c, s = cos.double().cpu(), sin.double().cpu()
+    rl = [t.detach().double().cpu().clone().requires_grad_() for t in (qp, kp, vp, meta)]
+    qr = orc.rope(rl[0].view(B, L, H, D).transpose(1, 2), c, s)
+    kr = orc.rope(rl[1].view(B, L, Hkv, D).transpose(1, 2), c, s)
+    vr = rl[2].view(B, L, Hkv, D).transpose(1, 2)
+    ref = orc.awa(qr, _rep(kr, H // Hkv), _rep(vr, H // Hkv), rl[3], W)
+    ref.backward(dy.double().cpu())
+    assert_output(y, ref.float(), "swa_rope window 128 y")
+    for t, r, n in zip(lv, rl, ("dq", "dk", "dv", "dmeta")):
+        assert_grad(t.grad, r.grad.float(), f"swa_rope window 128 {n}")
