@@ -264,6 +264,7 @@ def seqpar_measure(torch, lizard_cuda, device, dist, world, rank, steps=10, warm
     lg = F.logsigmoid(3 + 1.5 * torch.randn(1, SEQ_H, Ls, generator=g, device=device))
     dy = torch.randn(shape, generator=g, device=device).bfloat16()
     call = (lambda *a: lizard_cuda.gla(*a)) if world == 1 else seqpar.gla_seqpar
+    chain = lambda *a: seqpar.gla_seqpar(*a, exchange="chain")  # noqa: E731
 
     def timed(fn):
         for _ in range(warmup):
@@ -292,9 +293,31 @@ def seqpar_measure(torch, lizard_cuda, device, dist, world, rank, steps=10, warm
         call(*leaves).backward(dy)
     both = timed(step)
     check = None
+    chain_res = None
     if world > 1:
         check = seqpar_check(torch, lizard_cuda, dist, world, rank,
                              (fq, fk, v, lg, dy), [t.grad for t in leaves])
+        # the same step with the summaries passed rank to rank (NCCL send / recv,
+        # P - 1 dependent hops per direction) instead of one all_gather
+        ref = [leaves[0].grad.clone(), leaves[1].grad.clone(), leaves[2].grad.clone(),
+               leaves[3].grad.clone()]
+        with torch.no_grad():
+            y_ag = call(fq, fk, v, lg)
+            fwd_c = timed(lambda: chain(fq, fk, v, lg))
+            y_c = chain(fq, fk, v, lg)
+
+        def step_c():
+            for t in leaves:
+                t.grad = None
+            chain(*leaves).backward(dy)
+        both_c = timed(step_c)
+        diffs = [(a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-30)
+                 for a, b in zip([y_c] + [t.grad for t in leaves], [y_ag] + ref)]
+        dmax = torch.stack(diffs).double().max().reshape(1)
+        dist.all_reduce(dmax, op=dist.ReduceOp.MAX)
+        chain_res = {"exchange": "NCCL send / recv chain, P - 1 hops per direction",
+                     "fwd_ms": fwd_c, "fwd_bwd_ms": both_c,
+                     "max_rel_vs_all_gather": float(dmax.item())}
     # the same forward+backward replayed from one CUDA graph (the collectives
     # inside it): the device time of the sharded step without the host's
     # per-call work, captured and replayed by every rank in the same order
@@ -317,7 +340,8 @@ def seqpar_measure(torch, lizard_cuda, device, dist, world, rank, steps=10, warm
             "fwd_ms": fwd, "fwd_tokens_per_s": SEQ_L / (fwd / 1e3),
             "fwd_bwd_ms": both, "fwd_bwd_tokens_per_s": SEQ_L / (both / 1e3),
             "fwd_bwd_ms_graph": both_graph,
-            "fwd_bwd_tokens_per_s_graph": SEQ_L / (both_graph / 1e3)}
+            "fwd_bwd_tokens_per_s_graph": SEQ_L / (both_graph / 1e3),
+            "chain": chain_res}
 
 
 SEQ_CHECK_HEADS = (0, 17)

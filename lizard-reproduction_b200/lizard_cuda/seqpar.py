@@ -44,6 +44,57 @@ class DistExchange:
         return out.view(self.size, *t.shape)
 
 
+class ChainExchange(DistExchange):
+    """Rank-to-rank send / recv instead of all_gather (NCCL point-to-point over
+    NVLink on GPUs): the partial summary of the ranks before this one (forward)
+    or after it (backward) travels along the chain, and each rank folds its own
+    summary in with the same combine step before passing it on. P - 1 dependent
+    hops per direction instead of one collective; the arithmetic is the
+    all_gather path's step for step, so the states are the same."""
+
+    chain = True
+
+    def _peer(self, r):
+        return r if self.group is None else self.dist.get_global_rank(self.group, r)
+
+    def chain_seed(self, ops, summary, reverse):
+        """This rank's seed (None at the chain's start): the combined summary of
+        the ranks before it (forward) or after it (backward)."""
+        P, r = self.size, self.rank
+        src, dst = (r + 1, r - 1) if reverse else (r - 1, r + 1)
+        part = None
+        if 0 <= src < P:
+            part = torch.empty_like(summary)
+            self.dist.recv(part, self._peer(src), group=self.group)
+        if 0 <= dst < P:
+            if part is None:
+                out = summary
+            else:
+                # a three-entry buffer whose combine walks the received partial,
+                # then this rank (entries 0, 1 forward; 2, 1 backward)
+                buf = torch.zeros(3, summary.numel(), dtype=summary.dtype, device=summary.device)
+                if reverse:
+                    buf[1], buf[2] = summary, part
+                    folded = ops.combine(buf, 0, reverse=True)
+                else:
+                    buf[0], buf[1] = part, summary
+                    folded = ops.combine(buf, 2, reverse=False)
+                n = folded.numel()  # the state and normaliser; the total log decays add
+                out = torch.cat([folded.to(summary.dtype), part[n:] + summary[n:]])
+            self.dist.send(out.contiguous(), self._peer(dst), group=self.group)
+        return None if part is None else part[:ops.seed_floats()]
+
+    def chain_later_totals(self, own):
+        """Sum of the log-gate gradient totals of the ranks after this one."""
+        P, r = self.size, self.rank
+        later = torch.zeros_like(own)
+        if r + 1 < P:
+            self.dist.recv(later, self._peer(r + 1), group=self.group)
+        if r > 0:
+            self.dist.send((later + own).contiguous(), self._peer(r - 1), group=self.group)
+        return later
+
+
 class CudaSegmentOps:
     """The segment phases through the C ABI (lz_gla_seg_* in include/lizard_cuda.h)."""
 
@@ -63,6 +114,10 @@ class CudaSegmentOps:
 
     def _stream(self):
         return _lib.stream_of(self.ws)
+
+    def seed_floats(self):
+        B, H, L, F, D = self.dims
+        return B * H * F * (D + 1)
 
     def fwd_begin(self, fk, v, lg):
         B, H, L, F, D = self.dims
@@ -122,11 +177,21 @@ class CudaSegmentOps:
                    rank, rows, L, self._stream())
 
 
+def _seed(ops, comm, summary, reverse):
+    """The seed of this rank from every rank's summary: one all_gather and a
+    combine, or the send / recv chain of a ChainExchange. None for the first
+    rank (forward) or the last (backward)."""
+    if getattr(comm, "chain", False):
+        return comm.chain_seed(ops, summary, reverse)
+    summaries = comm.all_gather(summary)
+    edge = comm.size - 1 if reverse else 0
+    return None if comm.rank == edge else ops.combine(summaries, comm.rank, reverse)
+
+
 def forward_phases(ops, comm, fq, fk, v, lg, save):
     """One rank's forward: returns (y, saved, seeded)."""
     summary = ops.fwd_begin(fk, v, lg)
-    summaries = comm.all_gather(summary)
-    seed = ops.combine(summaries, comm.rank, reverse=False) if comm.rank > 0 else None
+    seed = _seed(ops, comm, summary, reverse=False)
     y, saved = ops.fwd_end(fq, fk, v, lg, seed, save)
     return y, saved, seed is not None
 
@@ -134,12 +199,14 @@ def forward_phases(ops, comm, fq, fk, v, lg, save):
 def backward_phases(ops, comm, fq, fk, v, saved, dy, seeded, grad_dtype):
     """One rank's backward: returns (dfq, dfk, dv, dlog_gamma) for its segment."""
     summary = ops.bwd_begin(fq, saved, dy)
-    summaries = comm.all_gather(summary)
-    last = comm.rank == comm.size - 1
-    dseed = None if last else ops.combine(summaries, comm.rank, reverse=True)
+    dseed = _seed(ops, comm, summary, reverse=True)
     dfq, dfk, dv, dlg = ops.bwd_end(fq, fk, v, saved, dy, dseed, seeded, grad_dtype)
-    totals = comm.all_gather(dlg[..., 0].contiguous().reshape(-1))
-    ops.gate_offset(dlg, totals, comm.rank)
+    own = dlg[..., 0].contiguous().reshape(-1)
+    if getattr(comm, "chain", False):
+        later = comm.chain_later_totals(own)
+        ops.gate_offset(dlg, torch.stack([torch.zeros_like(later), later]), 0)
+    else:
+        ops.gate_offset(dlg, comm.all_gather(own), comm.rank)
     return dfq, dfk, dv, dlg
 
 
@@ -167,7 +234,7 @@ class _GLASeq(torch.autograd.Function):
         return dfq, dfk, dv, dlg, None, None
 
 
-def gla_seqpar(fq, fk, v, log_gamma, group=None, comm=None, ops=None):
+def gla_seqpar(fq, fk, v, log_gamma, group=None, comm=None, ops=None, exchange="all_gather"):
     """gla() of one sequence split over the ranks of `group` (default: the world).
 
     fq, fk [B, H, Ls, F], v [B, H, Ls, D] and log_gamma [B, Ls] or [B, H, Ls] are
@@ -175,14 +242,19 @@ def gla_seqpar(fq, fk, v, log_gamma, group=None, comm=None, ops=None):
     the slices may differ in length). Returns this rank's slice of
     y (bf16); gradients flow to all four inputs as in gla(). `comm` (an object
     with rank, size and all_gather) and `ops` (the segment phases) default to
-    torch.distributed and the CUDA library.
+    torch.distributed and the CUDA library. `exchange` picks how the default
+    comm moves the chunk-state summaries: "all_gather" (one collective per
+    direction, the default) or "chain" (rank-to-rank send / recv, P - 1
+    dependent hops).
     """
     B, H, Hkv, L, F, D, per_head = _shapes(fq, fk, v, log_gamma)
     if Hkv != H:
         raise ValueError("gla_seqpar takes fk and v with the query head count; "
                          "repeat_interleave grouped keys / values first")
+    if exchange not in ("all_gather", "chain"):
+        raise ValueError(f"exchange must be 'all_gather' or 'chain', got {exchange!r}")
     if comm is None:
-        comm = DistExchange(group)
+        comm = ChainExchange(group) if exchange == "chain" else DistExchange(group)
     if ops is None:
         _lib.require_cuda(fq, fk, v, log_gamma)
         ops = CudaSegmentOps(B, H, L, F, D, per_head, fq.device)

@@ -60,6 +60,10 @@ class OracleSegmentOps:
         zE = torch.einsum("bhl,bhlf->bhf", w, fk)
         return torch.cat([E.flatten(), zE.flatten(), G[..., -1].flatten()])
 
+    def seed_floats(self):
+        B, H, F, D = self.dims
+        return B * H * F * (D + 1)
+
     def combine(self, summaries, rank, reverse):
         B, H, F, D = self.dims
         S, z, lam = self._split(summaries.double(), B * H, F, D)

@@ -34,7 +34,7 @@ def _inputs(B, H, L, F, D, per_head, seed=0):
     return fq, fk, v, lg, dy
 
 
-def _worker(rank, world, port, bounds, per_head, errq):
+def _worker(rank, world, port, bounds, per_head, errq, exchange="all_gather"):
     import sys
     for p in (ROOT, ROOT / "lizard-reproduction_b200", ROOT / "oracle", ROOT / "tests"):
         sys.path.insert(0, str(p))
@@ -52,7 +52,7 @@ def _worker(rank, world, port, bounds, per_head, errq):
         a, b = bounds[rank], bounds[rank + 1]
         sl = lambda t: t[..., a:b, :] if t.dim() == 4 else t[..., a:b]  # noqa: E731
         leaves = [sl(t).clone().requires_grad_() for t in (fq, fk, v, lg)]
-        y = seqpar.gla_seqpar(*leaves, ops=OracleSegmentOps(per_head, H))
+        y = seqpar.gla_seqpar(*leaves, ops=OracleSegmentOps(per_head, H), exchange=exchange)
         y.backward(sl(dy))
         # unsharded float64 oracle
         ref_leaves = [t.double().clone().requires_grad_() for t in (fq, fk, v, lg)]
@@ -72,17 +72,20 @@ def _worker(rank, world, port, bounds, per_head, errq):
         raise
 
 
+@pytest.mark.parametrize("exchange", ["all_gather", "chain"])
 @pytest.mark.parametrize("bounds,per_head", [
     ((0, 96, 192), False),        # 2 ranks, equal 96-token slices (chunk tails on both)
     ((0, 128, 200, 330), True),   # 3 ranks, unequal slices, per-head gates
     ((0, 64, 128, 130), False),   # 3 ranks, a 2-token last slice
 ])
-def test_seqpar_matches_unsharded_oracle(bounds, per_head):
+def test_seqpar_matches_unsharded_oracle(bounds, per_head, exchange):
+    """The chunk-state summaries moved by one all_gather per direction, or by
+    the rank-to-rank send / recv chain: every rank's slice matches."""
     world = len(bounds) - 1
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, bounds, per_head, errq))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, bounds, per_head, errq, exchange))
              for r in range(world)]
     for p in procs:
         p.start()

@@ -19,7 +19,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, errq):
+def _worker(rank, world, port, errq, exchange="all_gather"):
     import sys
     for p in (ROOT, ROOT / "lizard-reproduction_b200", ROOT / "oracle", ROOT / "tests",
               ROOT / "tests" / "golden"):
@@ -43,13 +43,14 @@ def _worker(rank, world, port, errq):
         a, b = rank * 256, (rank + 1) * 256
         leaves = [(t[..., a:b, :] if t.dim() == 4 else t[..., a:b]).detach().clone()
                   .requires_grad_() for t in (fq, fk, v, lg)]
-        y = seqpar.gla_seqpar(*leaves)
+        y = seqpar.gla_seqpar(*leaves, exchange=exchange)
         y.backward(dy[..., a:b, :].bfloat16())
         torch.cuda.synchronize()
         ref, rgrads = oracle_gla(fq, fk, v, lg, dy.bfloat16())
-        assert_output(y, ref[..., a:b, :], f"rank {rank} y")
+        assert_output(y, ref[..., a:b, :], f"rank {rank} {exchange} y")
         for got, r, n in zip([t.grad for t in leaves], rgrads, GRAD_NAMES):
-            assert_grad(got, r[..., a:b, :] if r.dim() == 4 else r[..., a:b], f"rank {rank} {n}")
+            assert_grad(got, r[..., a:b, :] if r.dim() == 4 else r[..., a:b],
+                        f"rank {rank} {exchange} {n}")
         dist.barrier()
         dist.destroy_process_group()
     except BaseException as e:
@@ -57,7 +58,11 @@ def _worker(rank, world, port, errq):
         raise
 
 
-def test_seqpar_over_nccl_matches_oracle():
+@pytest.mark.parametrize("exchange", ["all_gather", "chain"])
+def test_seqpar_over_nccl_matches_oracle(exchange):
+    """GLA sequence-parallel over NCCL (2 to 4 GPUs), the chunk-state summaries
+    moved by one all_gather per direction or by the send / recv chain: every
+    rank's slice of y and of the gradients against the oracle."""
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs 2 or more GPUs")
@@ -66,7 +71,8 @@ def test_seqpar_over_nccl_matches_oracle():
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, errq)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, errq, exchange))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
