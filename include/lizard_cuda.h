@@ -420,15 +420,14 @@ int lz_swa_bwd_gqa(const void* q, const void* k, const void* v,
  * with TMA, rotates q and k in fp32 and splits them into bf16 value + residual
  * tiles in shared memory, then runs the forward of lz_swa_fwd_gqa: y (and
  * saved) equal lz_rope_split + lz_swa_fwd_gqa bit for bit. With the tensor-core
- * forward on (lz_swa_set_tc) and D = 64, window <= 64 that is the tcgen05
+ * forward on (lz_swa_set_tc) and D = 64, window <= 128 that is a tcgen05
  * kernel (bf16 projections); otherwise the 64-row warp-MMA kernel. q_hi, q_lo
  * [B*H, L, D] and k_hi, k_lo [B*Hkv, L, D] (bf16, all null or all set) receive
  * the rotated operands that lz_swa_bwd_gqa takes. Returns LZ_ERR_UNSUPPORTED
  * without launching when D is not 32, 64 or 128, a stride or base is not
  * 16-byte aligned, the tiles do not fit in shared memory (fp32 at D = 128), or
- * the projections are fp32 at the tensor-core shape, or (tensor cores on)
- * D = 64 with a window of 65 to 128, whose tensor-core forward has no fused
- * rotation; rotate first then (the two passes reach the same forward kernel). The reference rotates with torch
+ * the projections are fp32 at the tensor-core shape; rotate first then (the
+ * two passes reach the same forward kernel). The reference rotates with torch
  * ops in its caller (src/lizard_attention.py:87-88). */
 int lz_swa_rope_fwd(const void* q, const void* k, const void* v, int x_dtype,
                     long long q_sb, long long q_sh, long long q_sl,

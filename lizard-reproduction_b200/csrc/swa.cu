@@ -1033,14 +1033,8 @@ int swa_rope_fwd(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st) {
   // At the tensor-core shape the fused forward is the tcgen05 kernel or
   // nothing: a decline (fp32 projections, strides its maps cannot take) sends
   // the caller to rotate first, and lz_swa_fwd_gqa then runs the same kernel.
-  if (swa_tc_enabled() && a.D == 64 && a.window >= 1 && a.window <= 64)
+  if (swa_tc_enabled() && a.D == 64 && a.window >= 1 && a.window <= 128)
     return swa_rope_fwd_tc(a, sv, st);
-  // Windows 65 ... 128 at head dim 64 have a tensor-core forward without the
-  // rotation inside: rotating first and running it beats this function's
-  // 64-row kernel (config-5 slice, window 128: 0.34 against 0.40 ms), so it
-  // declines and the caller takes the two passes.
-  if (swa_tc_enabled() && a.D == 64 && a.window > 64 && a.window <= 128)
-    return LZ_ERR_UNSUPPORTED;
   const bool f32 = a.x_dtype == LZ_DTYPE_F32, cf32 = a.cs_dtype == LZ_DTYPE_F32;
 #define LZ_ROPE(dp)                                                                          \
   if (a.D == dp) {                                                                           \

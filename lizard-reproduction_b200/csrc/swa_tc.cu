@@ -1610,13 +1610,22 @@ constexpr uint32_t kT2S = 0, kT2Ph = 0, kT2Pl = 64, kT2OA = 128, kT2OB = 192, kT
 // shared memory: two CTAs per SM. Each row warp covers 64 of a half's 128
 // columns; 16-column chunks that no row of its lane quadrant can see are
 // skipped (no TMEM load, p = 0).
-template <bool SPLIT>
-__global__ void __launch_bounds__(kThreads, SPLIT ? 1 : 2)
+// ROPE: q, k are the unrotated bf16 projections (maps tq, tk, raw rows landing
+// in the residual buffers), rotated and split into bf16 hi + lo in the CTA as
+// in the window <= 64 forward; the rotated operands go to qh_out ... kl_out
+// when given. Otherwise q, k are the rotated operands (SPLIT: with residuals).
+template <bool ROPE, bool SPLIT, typename CT>
+__global__ void __launch_bounds__(kThreads, (SPLIT || ROPE) ? 1 : 2)
 swa_fwd_tc128_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tql,
-                     const __grid_constant__ CUtensorMap tkl, const float* __restrict__ meta,
-                     int n_meta, int W, float scale_log2, int H, int grp, int L, int nqb,
-                     bf16* __restrict__ y, float* __restrict__ lse, float* __restrict__ y32) {
+                     const __grid_constant__ CUtensorMap tkl, const CT* __restrict__ cs,
+                     const CT* __restrict__ sn, long long cs_sb, long long cs_sl,
+                     const float* __restrict__ meta, int n_meta, int W, float scale_log2, int H,
+                     int grp, int L, int nqb, bf16* __restrict__ y, float* __restrict__ lse,
+                     float* __restrict__ y32, bf16* __restrict__ qh_out,
+                     bf16* __restrict__ ql_out, bf16* __restrict__ kh_out,
+                     bf16* __restrict__ kl_out) {
+  static_assert(SPLIT || !ROPE, "the rotation writes bf16 hi + lo operands");
   using SM = Fwd128Smem<SPLIT>;
   extern __shared__ __align__(1024) unsigned char smem[];
   if (smem_u32(smem) & 1023) {
@@ -1649,9 +1658,13 @@ swa_fwd_tc128_kernel(const __grid_constant__ CUtensorMap tq, const __grid_consta
 
   auto issue_q = [&](int g) {
     const int h = hk * grp + g;
-    tc::mbar_expect_tx(&bars[SB_Q], SPLIT ? 2 * kTileQ : kTileQ);
-    tc::tma_load_4d(smem + SM::qh, &tq, 0, q0, h, b, &bars[SB_Q]);
-    if (SPLIT) tc::tma_load_4d(smem + SM::ql, &tql, 0, q0, h, b, &bars[SB_Q]);
+    tc::mbar_expect_tx(&bars[SB_Q], (SPLIT && !ROPE) ? 2 * kTileQ : kTileQ);
+    if (ROPE) {
+      tc::tma_load_4d(smem + SM::ql, &tq, 0, q0, h, b, &bars[SB_Q]);  // raw rows land in lo
+    } else {
+      tc::tma_load_4d(smem + SM::qh, &tq, 0, q0, h, b, &bars[SB_Q]);
+      if (SPLIT) tc::tma_load_4d(smem + SM::ql, &tql, 0, q0, h, b, &bars[SB_Q]);
+    }
   };
   auto issue_s = [&](int hv) {  // s = q k^T of key half hv into TMEM columns [0, 128)
     tc::tc_fence_after();
@@ -1676,9 +1689,13 @@ swa_fwd_tc128_kernel(const __grid_constant__ CUtensorMap tq, const __grid_consta
     tc::mma_commit(&bars[SB_S]);
   };
   if (tid == 0) {
-    tc::mbar_expect_tx(&bars[SB_KV], SPLIT ? 3 * kTileK : 2 * kTileK);
-    tc::tma_load_4d(smem + SM::kh, &tk, 0, k0, hk, b, &bars[SB_KV]);
-    if (SPLIT) tc::tma_load_4d(smem + SM::kl, &tkl, 0, k0, hk, b, &bars[SB_KV]);
+    tc::mbar_expect_tx(&bars[SB_KV], (SPLIT && !ROPE) ? 3 * kTileK : 2 * kTileK);
+    if (ROPE) {
+      tc::tma_load_4d(smem + SM::kl, &tk, 0, k0, hk, b, &bars[SB_KV]);
+    } else {
+      tc::tma_load_4d(smem + SM::kh, &tk, 0, k0, hk, b, &bars[SB_KV]);
+      if (SPLIT) tc::tma_load_4d(smem + SM::kl, &tkl, 0, k0, hk, b, &bars[SB_KV]);
+    }
     tc::tma_load_4d(smem + SM::v, &tv, 0, k0, hk, b, &bars[SB_KV]);
     issue_q(0);
   }
@@ -1689,8 +1706,26 @@ swa_fwd_tc128_kernel(const __grid_constant__ CUtensorMap tq, const __grid_consta
   float ls = 0.f;
   for (int j = 0; j < n_meta; ++j) ls += exp2f(meta[j] * kLog2e - ms);
 
+  const CT* csb = ROPE ? cs + (size_t)b * cs_sb : nullptr;
+  const CT* snb = ROPE ? sn + (size_t)b * cs_sb : nullptr;
+  auto rotate_q = [&](int g) {
+    const size_t hrow = ((size_t)b * H + hk * grp + g) * L;
+    rotate_rows<0, kQ, CT>(smem + SM::qh, smem + SM::ql, q0, L, csb, snb, cs_sl, 0,
+                           qh_out ? qh_out + hrow * kDh : nullptr,
+                           qh_out ? ql_out + hrow * kDh : nullptr);
+  };
   tc::mbar_wait(&bars[SB_KV], 0, 110);
+  if (ROPE) {  // the 256 key rows once; this tile's own 128 rows go out for the backward
+    const size_t kvb = ((size_t)b * Hkv + hk) * L * kDh;
+    bf16* gh = kh_out ? kh_out + kvb : nullptr;
+    bf16* gl = kh_out ? kl_out + kvb : nullptr;
+    rotate_rows<0, 128, CT>(smem + SM::kh, smem + SM::kl, k0, L, csb, snb, cs_sl, kH2, gh, gl);
+    rotate_rows<128, 128, CT>(smem + SM::kh, smem + SM::kl, k0, L, csb, snb, cs_sl, kH2, gh,
+                              gl);
+  }
   tc::mbar_wait(&bars[SB_Q], 0, 111);
+  if (ROPE) rotate_q(0);
+  tc::fence_proxy_async_smem();
   tc::tc_fence_before();
   __syncthreads();
   if (tid == 0) issue_s(0);
@@ -1778,7 +1813,11 @@ swa_fwd_tc128_kernel(const __grid_constant__ CUtensorMap tq, const __grid_consta
       } else {
         mrow = mref, lB = lh;
       }
-      if (hv == 1 && next) tc::mbar_wait(&bars[SB_Q], (uint32_t)(g + 1) & 1u, 111);
+      if (hv == 1 && next) {  // the next head's query tiles, rotated while P V runs
+        tc::mbar_wait(&bars[SB_Q], (uint32_t)(g + 1) & 1u, 111);
+        if (ROPE) rotate_q(g + 1);
+        tc::fence_proxy_async_smem();
+      }
       tc::mbar_wait(&bars[SB_O], (uint32_t)hv, 113);  // two P V commits per head
       tc::tc_fence_after();
       tc::tc_fence_before();
@@ -2275,15 +2314,38 @@ int swa_fwd_tc128(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, c
   } else {
     mql = mq, mkl = mk;
   }
-  auto kern = split ? swa_fwd_tc128_kernel<true> : swa_fwd_tc128_kernel<false>;
+  auto kern = split ? swa_fwd_tc128_kernel<false, true, float>
+                    : swa_fwd_tc128_kernel<false, false, float>;
   const size_t smem = split ? Fwd128Smem<true>::bytes : Fwd128Smem<false>::bytes;
   static bool done[2][64] = {{false}};
   const int rc = ensure_tc_smem(kern, smem, done[split]);
   if (rc) return rc;
   const int nqb = ceil_div(L, kQ);
   kern<<<(unsigned)((long long)B * Hkv * nqb), kThreads, smem, st>>>(
-      mq, mk, mv, mql, mkl, meta, n_meta, W, kLog2e / sqrtf((float)kDh), H, H / Hkv, L, nqb, y,
-      sv.lse, sv.y32);
+      mq, mk, mv, mql, mkl, nullptr, nullptr, 0, 0, meta, n_meta, W,
+      kLog2e / sqrtf((float)kDh), H, H / Hkv, L, nqb, y, sv.lse, sv.y32, nullptr, nullptr,
+      nullptr, nullptr);
+  count_launches(1);
+  return check_launch("swa_fwd_tc128_kernel");
+}
+
+// The fused rotation for windows 65 ... 128 (bf16 projections read in place).
+template <typename CT>
+int swa_rope_fwd_tc128(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st) {
+  CUtensorMap mq, mk, mv;
+  if (!make_tc_map(&mq, a.q, a.L, a.H, a.B, a.q_sb, a.q_sh, a.q_sl, kQ) ||
+      !make_tc_map(&mk, a.k, a.L, a.Hkv, a.B, a.k_sb, a.k_sh, a.k_sl, kNK2) ||
+      !make_tc_map(&mv, a.v, a.L, a.Hkv, a.B, a.v_sb, a.v_sh, a.v_sl, kNK2))
+    return LZ_ERR_UNSUPPORTED;
+  auto kern = swa_fwd_tc128_kernel<true, true, CT>;
+  static bool done[64] = {false};
+  const int rc = ensure_tc_smem(kern, Fwd128Smem<true>::bytes, done);
+  if (rc) return rc;
+  const int nqb = ceil_div(a.L, kQ);
+  kern<<<(unsigned)((long long)a.B * a.Hkv * nqb), kThreads, Fwd128Smem<true>::bytes, st>>>(
+      mq, mk, mv, mq, mk, static_cast<const CT*>(a.cos), static_cast<const CT*>(a.sin), a.cs_sb,
+      a.cs_sl, a.meta, a.n_meta, a.window, kLog2e / sqrtf((float)kDh), a.H, a.H / a.Hkv, a.L,
+      nqb, a.y, sv.lse, sv.y32, a.q_hi, a.q_lo, a.k_hi, a.k_lo);
   count_launches(1);
   return check_launch("swa_fwd_tc128_kernel");
 }
@@ -2329,7 +2391,7 @@ int swa_set_tc(int on) { return g_swa_tc.exchange(on ? 1 : 0); }
 
 int swa_rope_fwd_tc(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st) {
   if (!swa_tc_enabled() || a.D != kDh || a.x_dtype != LZ_DTYPE_BF16 || a.window < 1 ||
-      a.window > kNK - kQ)
+      a.window > kH2)
     return LZ_ERR_UNSUPPORTED;
   const long long ces = a.cs_dtype == LZ_DTYPE_F32 ? 4 : 2;
   if (!aligned16(a.cos) || !aligned16(a.sin) || (a.cs_sl * ces) % 16 || (a.cs_sb * ces) % 16)
@@ -2338,6 +2400,9 @@ int swa_rope_fwd_tc(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st) {
                  !aligned16(a.k_lo)))
     return LZ_ERR_UNSUPPORTED;
   if (!aligned16(a.y) || (sv.y32 && !aligned16(sv.y32))) return LZ_ERR_UNSUPPORTED;
+  if (a.window > kNK - kQ)
+    return a.cs_dtype == LZ_DTYPE_F32 ? swa_rope_fwd_tc128<float>(a, sv, st)
+                                      : swa_rope_fwd_tc128<bf16>(a, sv, st);
   CUtensorMap mq, mk, mv;
   if (!make_tc_map(&mq, a.q, a.L, a.H, a.B, a.q_sb, a.q_sh, a.q_sl, kQ) ||
       !make_tc_map(&mk, a.k, a.L, a.Hkv, a.B, a.k_sb, a.k_sh, a.k_sl, kNK) ||
