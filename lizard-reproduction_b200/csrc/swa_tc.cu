@@ -2014,11 +2014,19 @@ swa_bwd_dq_tc128_kernel(const __grid_constant__ CUtensorMap tq,
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
           const int c0 = 32 * hf + 16 * k;
+          uint32_t dk8[8];
+          // keys that no row of this lane quadrant can see: ds = 0, no loads
+          const int t0 = k0 + kQK * qv + c0, i0 = q0 + 32 * qd;
+          if (t0 > i0 + 31 || t0 + 15 <= i0 - W) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dk8[j] = 0u;
+            tc::tmem_st8(trow + kU2Ds + 32 * hf + 8 * k, dk8);
+            continue;
+          }
           float sv[16], dpv[16];
           tc::tmem_ld16(trow + kU2S + c0, sv);
           tc::tmem_ld16(trow + kU2Dp + c0, dpv);
           tc::tmem_wait_ld();
-          uint32_t dk8[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             float d2[2];
@@ -2215,11 +2223,20 @@ swa_bwd_dkv_tc128_kernel(const __grid_constant__ CUtensorMap tq,
       // columns are touched and no barrier is needed.
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
+        uint32_t pk[8], dk8[8];
+        // query rows that see no key row of this lane quadrant: p = ds = 0, no loads
+        const int c0 = 32 * hf + 16 * k, tq0 = k0 + 32 * qd;
+        if (qr + c0 + 15 < tq0 || qr + c0 >= tq0 + 31 + W) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) pk[j] = dk8[j] = 0u;
+          tc::tmem_st8(trow + kV2P + 32 * hf + 8 * k, pk);
+          tc::tmem_st8(trow + kV2Ds + 32 * hf + 8 * k, dk8);
+          continue;
+        }
         float sv[16], dpv[16];
         tc::tmem_ld16(trow + kV2S + 32 * hf + 16 * k, sv);
         tc::tmem_ld16(trow + kV2Dp + 32 * hf + 16 * k, dpv);
         tc::tmem_wait_ld();
-        uint32_t pk[8], dk8[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           float p2[2], d2[2];
