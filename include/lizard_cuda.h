@@ -289,7 +289,7 @@ long long lz_hedgehog_set_rows_max(long long rows);
 
 /* SWA forwards (lz_swa_fwd_gqa and lz_swa_rope_fwd) and the dq and dk / dv
  * kernels of the backward on the tensor cores (1, the default: tcgen05
- * kernels for head dim 64, window <= 64, bf16 operands) or on the 64-row
+ * kernels for head dim 64 and windows up to 128) or on the 64-row
  * warp-MMA kernels (0). Returns the previous setting; a hook for tests and
  * tuning, process-wide. */
 int lz_swa_set_tc(int on);

@@ -66,8 +66,9 @@ struct SwaRopeArgs {
 // shape or strides.
 int swa_rope_fwd(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st);
 
-// The tensor-core forwards (swa_tc.cu): head dim 64, window <= 64, bf16
-// operands; LZ_ERR_UNSUPPORTED without launching for anything else or when
+// The tensor-core forwards (swa_tc.cu): head dim 64, windows up to 128 (the
+// fused rotation for bf16 projections); LZ_ERR_UNSUPPORTED without launching
+// for anything else or when
 // switched off (lz_swa_set_tc), and the callers then take the 64-row kernels.
 bool swa_tc_enabled();
 int swa_rope_fwd_tc(const SwaRopeArgs& a, const SwaSaved& sv, cudaStream_t st);
