@@ -31,6 +31,7 @@
 // on (writing in-bounds garbage) through every barrier to the end.
 #include <atomic>
 #include <mutex>
+#include <string>
 
 #include "common.cuh"
 #include "gla_layout.h"
@@ -746,17 +747,30 @@ gla_bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
 
 // [BH, rows, cols] bf16 as 3-D {cols, rows, BH}, box {64, box_rows, 1}, 128-byte
 // swizzle, zero fill outside (cols 64: a box at column 64 reads zeros)
+// The last encode failure of this thread (for the error message).
+thread_local int g_map_err = 0;
+
 bool make_map(CUtensorMap* m, const void* ptr, int BH, int rows, int cols = 128,
               int box_rows = 128) {
   tc::EncodeTiledFn fn = tc::encode_tiled_fn();
+  g_map_err = -1;
   if (!fn) return false;
   cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)BH};
   cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)rows * cols * 2};
   cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  const CUresult r =
+      fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  g_map_err = (int)r;
+  return r == CUDA_SUCCESS;
+}
+
+// "gla_bwd: tensor map encoding failed" with which map and the driver's code.
+void map_error(const char* which) {
+  set_error(std::string("gla_bwd: tensor map encoding failed (") + which + ", CUresult " +
+            std::to_string(g_map_err) + ")");
 }
 
 std::mutex g_tc_mu;
@@ -798,11 +812,9 @@ int gla_bwd_tc_states(const bf16* fq, const bf16* dy, const GlaSaved& sv, const 
                       int B, int H, int L, cudaStream_t stream) {
   const int BH = B * H, NT = (L + kC - 1) / kC;
   CUtensorMap mq, mdy, mds;
-  if (!make_map(&mq, fq, BH, L) || !make_map(&mdy, dy, BH, L) ||
-      !make_map(&mds, wk.ds, BH, NT * kC)) {
-    set_error("gla_bwd: tensor map encoding failed");
-    return LZ_ERR_CUDA;
-  }
+  if (!make_map(&mq, fq, BH, L)) return map_error("fq"), LZ_ERR_CUDA;
+  if (!make_map(&mdy, dy, BH, L)) return map_error("dy"), LZ_ERR_CUDA;
+  if (!make_map(&mds, wk.ds, BH, NT * kC)) return map_error("state gradients"), LZ_ERR_CUDA;
   static bool done[64] = {false};
   int rc = ensure_attr(reinterpret_cast<const void*>(gla_bwd_state_tc_kernel), kS1Smem, done);
   if (rc) return rc;
@@ -823,18 +835,19 @@ int gla_bwd_tc_chunks(const bf16* fq, const bf16* fk, const bf16* v, const bf16*
   const int srows = narrow ? ((L + 63) / 64) * 64 : NT * kC;
   const int sbox = narrow ? 64 : 128;
   CUtensorMap mq, mk, mv, mdy, ms, mds, mdfq, mdfk, mdv;
-  bool ok = make_map(&mq, fq, BH, L, W) && make_map(&mk, fk, B * Hkv, L, W) &&
-            make_map(&mv, v, B * Hkv, L, W) && make_map(&mdy, dy, BH, L, W) &&
-            make_map(&ms, sv.s, BH, srows, W, sbox) && make_map(&mds, wk.ds, BH, srows, W, sbox);
+  if (!make_map(&mq, fq, BH, L, W)) return map_error("fq"), LZ_ERR_CUDA;
+  if (!make_map(&mk, fk, B * Hkv, L, W)) return map_error("fk"), LZ_ERR_CUDA;
+  if (!make_map(&mv, v, B * Hkv, L, W)) return map_error("v"), LZ_ERR_CUDA;
+  if (!make_map(&mdy, dy, BH, L, W)) return map_error("dy"), LZ_ERR_CUDA;
+  if (!make_map(&ms, sv.s, BH, srows, W, sbox)) return map_error("saved states"), LZ_ERR_CUDA;
+  if (!make_map(&mds, wk.ds, BH, srows, W, sbox)) return map_error("state gradients"), LZ_ERR_CUDA;
   // fp32 gradients are stored directly; their maps are unused
   mdfq = mdfk = mdv = mq;
-  if (gdt == LZ_DTYPE_BF16) ok = ok && make_map(&mdfq, dfq, BH, L, W);
-  if (gdt_kv == LZ_DTYPE_BF16)
-    ok = ok && make_map(&mdfk, dfk, BH, L, W) && make_map(&mdv, dv, BH, L, W);
-  if (!ok) {
-    set_error("gla_bwd: tensor map encoding failed");
-    return LZ_ERR_CUDA;
-  }
+  if (gdt == LZ_DTYPE_BF16 && !make_map(&mdfq, dfq, BH, L, W))
+    return map_error("dfq"), LZ_ERR_CUDA;
+  if (gdt_kv == LZ_DTYPE_BF16 &&
+      (!make_map(&mdfk, dfk, BH, L, W) || !make_map(&mdv, dv, BH, L, W)))
+    return map_error("dfk / dv"), LZ_ERR_CUDA;
   const unsigned grid = (unsigned)((long long)BH * NT);
   const int pf = g_chunk_prefetch.load() ? sm_count() : 0;
   if (narrow) {

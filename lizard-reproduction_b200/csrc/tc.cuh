@@ -21,7 +21,19 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+// The encoder is a driver call and needs a current context on the calling
+// thread. A thread that has made no runtime call yet has none: PyTorch's
+// autograd worker running its first backward, for one, when every tensor it
+// allocates comes from the caching allocator's cache. cudaSetDevice makes the
+// device's primary context current; done once per thread and device.
+inline void ensure_current_context() {
+  thread_local int ready = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev == ready) return;
+  if (cudaSetDevice(dev) == cudaSuccess) ready = dev;
+}
 inline EncodeTiledFn encode_tiled_fn() {
+  ensure_current_context();
   static EncodeTiledFn fn = [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
