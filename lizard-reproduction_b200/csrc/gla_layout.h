@@ -52,13 +52,18 @@ struct GlaFwdWork {
 enum GlaSchedule { kScheduleAuto = 0, kScheduleWalk = 1, kScheduleSplit = 2 };
 int gla_schedule_override();  // process-wide, set by lz_gla_set_schedule
 
+constexpr long long kF128SplitHeads = 20;
+
 inline bool gla_fwd_split(int B, int H, int L, int F, int D) {
   const int o = gla_schedule_override();
   if (o == kScheduleWalk) return false;
   if (o == kScheduleSplit) return true;
   if (L <= 64) return false;  // a single chunk: both schedules are the same work
   const long long BH = (long long)B * H;
-  if (F == 128 && D == 128) return BH <= 40;  // tensor-core walk, one CTA per head
+  // F = D = 128: the tensor-core walk (one CTA per head) takes one chain's time
+  // whatever BH is, the chunk-parallel kernels time that grows with BH * L;
+  // they cross near 20 heads at L = 2048 ... 16384 (forward and backward)
+  if (F == 128 && D == 128) return BH <= kF128SplitHeads;
   // F = 256 (the model's feature map): the warp-MMA walk splits the value
   // columns and waits on every chunk's loads; the chunk-parallel kernels were
   // 1.6-3x faster at config-5 shapes, and equal without shared states at B=32
@@ -71,6 +76,7 @@ inline bool gla_bwd_split(int B, int H, int L, int F, int D) {
   if (o == kScheduleWalk) return false;
   if (o == kScheduleSplit) return true;
   if (L <= 64) return false;
+  if (F == 128 && D == 128) return (long long)B * H <= kF128SplitHeads;
   return (long long)B * H * ((F + 63) / 64) * ((D + 63) / 64) <= 148;
 }
 
