@@ -2312,6 +2312,9 @@ int ensure_tc_smem(Kern kern, size_t bytes, bool* done) {
   return LZ_OK;
 }
 
+// Shared memory a 256-TMEM-column kernel asks for at least: more than a third
+// of the SM's 227 KB, so at most two of its CTAs share an SM (a third would
+// wait inside the TMEM allocation).
 constexpr size_t kTwoPerSm = 80 * 1024;
 
 int swa_fwd_tc128(const bf16* q, const bf16* k, const bf16* v, const bf16* ql, const bf16* kl,
