@@ -165,6 +165,21 @@ def test_schedule_setting_and_forward_workspace(lib):
         lib.lz_gla_set_schedule(0)
 
 
+def test_f128_schedule_crossover(lib):
+    """At F = D = 128 the tensor-core walk runs one chain's time whatever the
+    head count; the chunk-parallel schedule (which needs a forward workspace and
+    a larger backward one) is planned only for 20 heads or fewer, the measured
+    crossover at L = 2048 ... 16384."""
+    for L in (2048, 16384):
+        assert lib.lz_gla_fwd_workspace_bytes(1, 20, L, 128, 128, 64) > 0
+        assert lib.lz_gla_fwd_workspace_bytes(1, 21, L, 128, 128, 64) == 0
+        assert lib.lz_gla_fwd_workspace_bytes(1, 32, L, 128, 128, 64) == 0
+        split_bwd = lib.lz_gla_bwd_workspace_bytes(1, 20, L, 128, 128, 64)
+        walk_bwd = lib.lz_gla_bwd_workspace_bytes(1, 21, L, 128, 128, 64)
+        # per head, the chunk-parallel backward also keeps the fp32 increments
+        assert split_bwd / 20 > walk_bwd / 21
+
+
 def test_gla_fwd_rejects_missing_workspace(lib):
     p = _fake(5)
     rc = lib.lz_gla_fwd(*p[:4], 0, p[4], None, 0, None, 0, 1, 32, 2048, 64, 64, 64, None)
